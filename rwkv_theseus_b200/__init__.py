@@ -1,0 +1,8 @@
+"""B200-native Parallel Layer Migration: distil every full-attention block of a
+frozen Qwen3.5-family hybrid teacher into an independent RWKV7 TimeMix student.
+
+Subpackages: ``models`` (teacher, student, runner, checkpoint IO), ``ops``
+(CUDA-kernel operators with PyTorch oracles), ``parallel`` (topology and the
+peer-memory gradient exchange), ``utils`` (profiling, build helpers).
+"""
+__version__ = "0.1.0"

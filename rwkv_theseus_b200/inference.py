@@ -1,0 +1,107 @@
+"""Self-contained export of the assembled model and its runtime.
+
+Export format 2 (reference ``theseus/inference.py:14-31``): HF-layout sharded
+safetensors (5 GB shards) in which every migrated block's TimeMix weights sit
+under ``model.layers.<i>.self_attn.core.*`` in bf16, ``config.json``, the
+tokenizer files of the base model, and ``theseus.json`` =
+``{format: 2, layers, head_size, backend, base_fingerprint, loader,
+state_layout: "B,H,value,key", migration_fingerprint}``.
+
+``load_export`` rebuilds the model on the meta device, installs the TimeMix
+blocks, loads the shards strictly and returns a ``Runner``. Format-1 exports
+(base model + delta) are also accepted. ``generate`` adds the greedy decode
+loop the reference leaves to the caller: one chunked prefill, then T=1 steps
+through the recurrent states (WKV7/GDN) and the KV cache.
+"""
+import json
+import os
+import shutil
+from pathlib import Path
+
+import torch
+from safetensors.torch import load_file
+
+from .checkpoint import model_fingerprint, split_delta
+from .data import digest_file
+from .models.hf_io import build_empty, finalize, load_model, save_model, shard_files
+from .models.qwen35 import HybridConfig
+from .models.runner import Runner, install
+
+TOKENIZER_PREFIXES = ("tokenizer", "vocab", "merges", "special_tokens", "chat_template")
+
+
+def save_export(model, path, cfg, order, base_id, checkpoint=None):
+    path = Path(path)
+    if path.exists():
+        raise FileExistsError(f"Refusing to overwrite export {path}")
+    temp = path.with_name("." + path.name + ".tmp")
+    if temp.exists():
+        shutil.rmtree(temp)
+    temp.mkdir(parents=True)
+    save_model(model, temp, max_shard_bytes=5 * 1000 ** 3)
+    for source in Path(cfg["model"]).iterdir():
+        if source.is_file() and source.name.startswith(TOKENIZER_PREFIXES):
+            shutil.copyfile(source, temp / source.name)
+    meta = {"format": 2, "layers": order, "head_size": cfg["head_size"], "backend": cfg["backend"],
+            "lora_rank": cfg.get("lora_rank"), "gate_lora_rank": cfg.get("gate_lora_rank"),
+            "base_fingerprint": base_id, "loader": "rwkv_theseus_b200.inference.load_export",
+            "state_layout": "B,H,value,key",
+            "migration_fingerprint": digest_file(Path(checkpoint) / "migrated.safetensors") if checkpoint else None}
+    (temp / "theseus.json").write_text(json.dumps(meta, indent=2))
+    os.replace(temp, path)
+
+
+def load_export(path, device="cuda", base_model=None):
+    path = Path(path)
+    meta = json.loads((path / "theseus.json").read_text())
+    if meta["format"] == 2:
+        cfg = HybridConfig.from_pretrained(path)
+        model = build_empty(cfg, "meta", torch.bfloat16)
+        for layer in meta["layers"]:
+            install(model, layer, meta)
+        expected = set(model.state_dict())
+        seen = set()
+        for shard in shard_files(path):
+            state = load_file(str(path / shard), device=str(device))
+            if seen.intersection(state) or set(state) - expected:
+                raise ValueError("Invalid converted checkpoint keys")
+            model.load_state_dict(state, strict=False, assign=True)
+            seen.update(state)
+        if cfg.tie_word_embeddings and "lm_head.weight" not in seen:
+            model.lm_head.weight = model.model.embed_tokens.weight
+            seen.add("lm_head.weight")
+        if expected != seen:
+            raise ValueError(f"Missing converted weights: {sorted(expected - seen)[:8]}")
+        finalize(model, device)
+        return Runner(model)
+    base = base_model or meta["base_model"]
+    if model_fingerprint(base) != meta["base_fingerprint"]:
+        raise ValueError("Export base fingerprint mismatch")
+    model = load_model(base, device)
+    delta = split_delta(load_file(str(path / "migrated.safetensors")))
+    for layer in meta["layers"]:
+        install(model, layer, meta, delta[layer])
+    return Runner(model)
+
+
+@torch.no_grad()
+def generate(runner, prompt, new_tokens, prefill_chunk=4096, on_token=None):
+    """Greedy decoding: chunked prefill of ``prompt`` [B, T], then ``new_tokens`` T=1 steps.
+
+    Returns the generated ids [B, new_tokens]. ``on_token(step, ids)`` is called
+    after each decode step (timing hooks, streaming).
+    """
+    runner.reset()
+    head = runner.model.lm_head.weight
+    hidden = None
+    for start in range(0, prompt.shape[1], prefill_chunk):
+        hidden = runner.forward(prompt[:, start:start + prefill_chunk])
+    token = (hidden[:, -1:].to(head.dtype) @ head.t()).argmax(-1)
+    out = [token]
+    for step in range(1, new_tokens):
+        hidden = runner.forward(token)
+        token = (hidden[:, -1:].to(head.dtype) @ head.t()).argmax(-1)
+        out.append(token)
+        if on_token is not None:
+            on_token(step, token)
+    return torch.cat(out, 1)

@@ -1,0 +1,37 @@
+"""Distillation statistics (reference ``theseus/losses.py:5-30``).
+
+``statistics`` returns the differentiable sums ``[sum NMSE, sum cosine, count]``
+over tokens, with per-token NMSE = mean((x-y)^2) / max(mean(y^2), eps). On CUDA
+the fused loss kernel computes the same three sums in one pass (and the NMSE
+gradient in the same kernel, see ``ops.loss``); this module is the
+device-agnostic definition used on CPU and as the test oracle.
+"""
+import torch
+from torch.nn import functional as F
+
+
+def statistics(prediction, target, epsilon=1e-6, mask=None):
+    x, y = prediction.float(), target.float()
+    nmse = (x - y).square().mean(-1) / y.square().mean(-1).clamp_min(epsilon)
+    cosine = F.cosine_similarity(x, y, dim=-1, eps=epsilon)
+    weight = torch.ones_like(nmse) if mask is None else mask.float()
+    return torch.stack([(nmse * weight).sum(), (cosine * weight).sum(), weight.sum()])
+
+
+def loss_sum(stats, cosine_weight):
+    return stats[0] + cosine_weight * (stats[2] - stats[1])
+
+
+def metrics(stats):
+    nmse, cosine, count = stats.double().cpu().tolist()
+    if count <= 0:
+        raise ValueError("No valid validation tokens")
+    mean = nmse / count
+    return {"nmse": mean, "rrms": mean ** .5, "cosine": cosine / count, "tokens": int(count)}
+
+
+def kl_sum(student_logits, teacher_logits):
+    """Sum over tokens of KL(teacher || student) on the full vocabulary."""
+    teacher = F.log_softmax(teacher_logits.float(), dim=-1)
+    student = F.log_softmax(student_logits.float(), dim=-1)
+    return (teacher.exp() * (teacher - student)).sum()
