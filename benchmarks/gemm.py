@@ -1,0 +1,84 @@
+#!/usr/bin/env python3
+"""tcgen05 GEMM vs cuBLAS (torch.matmul) on the projection shapes of the 27B
+migration step (1024 tokens): teacher MLP/GDN/attention projections and the
+student C x C GEMMs in forward, input-gradient (MN-major B) and
+weight-gradient (MN-major A and B) form. Device time with CUDA events,
+median of --iters after --warmup; operands rotate over buffers larger than L2.
+"""
+import argparse
+import json
+import os
+import sys
+
+import torch
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+from rwkv_theseus_b200.ops import native  # noqa: E402
+
+SHAPES = [  # (name, M, N, K, a_t, b_t)
+    ("mlp_gate_up", 1024, 17408, 5120, False, False),
+    ("mlp_down", 1024, 5120, 17408, False, False),
+    ("gdn_in_qkv", 1024, 10240, 5120, False, False),
+    ("gdn_out", 1024, 5120, 6144, False, False),
+    ("attn_q", 1024, 12288, 5120, False, False),
+    ("student_fwd", 1024, 5120, 5120, False, False),
+    ("student_dx", 1024, 5120, 5120, False, True),
+    ("student_dw", 5120, 5120, 1024, True, True),
+    ("big_square", 8192, 8192, 8192, False, False),
+]
+
+
+def timed(fn, warmup, iters):
+    for _ in range(warmup):
+        fn(0)
+    torch.cuda.synchronize()
+    times = []
+    for i in range(iters):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn(i + 1)
+        e.record()
+        torch.cuda.synchronize()
+        times.append(s.elapsed_time(e))
+    return sorted(times)[len(times) // 2]
+
+
+def main():
+    p = argparse.ArgumentParser()
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--iters", type=int, default=20)
+    p.add_argument("--only", default=None)
+    args = p.parse_args()
+    results = []
+    for name, M, N, K, a_t, b_t in SHAPES:
+        if args.only and args.only not in name:
+            continue
+        bytes_per_set = (M * K + N * K) * 2
+        sets = max(1, min(8, (256 << 20) // bytes_per_set + 1))
+        As = [torch.randn((K, M) if a_t else (M, K), device="cuda").to(torch.bfloat16) for _ in range(sets)]
+        Bs = [torch.randn((K, N) if b_t else (N, K), device="cuda").to(torch.bfloat16) for _ in range(sets)]
+        out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+
+        def ours(i):
+            native().gemm(As[i % sets], a_t, Bs[i % sets], b_t, 0, 1.0, out)
+
+        def cublas(i):
+            a = As[i % sets].t() if a_t else As[i % sets]
+            b = Bs[i % sets] if b_t else Bs[i % sets].t()
+            torch.matmul(a, b, out=out)
+
+        flops = 2.0 * M * N * K
+        t_ours = timed(ours, args.warmup, args.iters)
+        t_cub = timed(cublas, args.warmup, args.iters)
+        ref = torch.matmul(As[0].t() if a_t else As[0], Bs[0] if b_t else Bs[0].t()).float()
+        native().gemm(As[0], a_t, Bs[0], b_t, 0, 1.0, out)
+        rel = ((out.float() - ref).abs().max() / ref.abs().max()).item()
+        row = {"shape": name, "M": M, "N": N, "K": K, "ours_ms": t_ours, "cublas_ms": t_cub,
+               "ours_tflops": flops / t_ours / 1e9, "cublas_tflops": flops / t_cub / 1e9,
+               "ratio": t_cub / t_ours, "max_rel_err": rel}
+        results.append(row)
+        print(json.dumps(row), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,377 @@
+// Persistent warp-specialised tcgen05 GEMM for sm_100a: C = epilogue(A · B^T).
+//
+//   A: [M, K] bf16, K-major (row-major activations) or MN-major (A = X^T of a
+//      row-major X[K, M], used for weight gradients dY^T · X).
+//   B: [N, K] bf16, K-major (nn.Linear weights [out, in]) or MN-major
+//      (B = W^T of a row-major W[K, N], used for input gradients dY · W).
+//   Accumulation in fp32 in tensor memory (TMEM).
+//
+// Roles (192 threads): warp 0 issues TMA tile loads (128-byte swizzle, no
+// multicast) into a STAGES-deep shared-memory ring; warp 1 issues
+// tcgen05.mma (M=128, N=BN, K=16) from one elected thread and commits each
+// stage back to the producer; warps 2-5 drain the double-buffered TMEM
+// accumulator (tcgen05.ld 32x32b) and run the epilogue while the next tile
+// accumulates. One CTA per SM walks tiles M-fastest so the CTAs running at
+// the same time share B tiles through L2.
+//
+// Epilogues: bf16 store, fp32 store, fp32 accumulate (C += alpha * acc, for
+// gradient accumulation into the flat fp32 buffers), and SwiGLU with two B
+// operands (out = silu(A·Bg^T) * (A·Bu^T), bf16).
+//
+// All waits are bounded (sm100.cuh); on timeout the kernel records status 1
+// in *status and unwinds, freeing its TMEM.
+#include <cuda.h>
+#include "../common/common.cuh"
+#include "../common/sm100.cuh"
+
+namespace {
+
+enum Epi : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_F32_ACCUM = 2, EPI_SWIGLU = 3 };
+
+constexpr int BM = 128, BK = 64, STAGES = 4, THREADS = 192;
+constexpr int MN_CHUNK_BYTES = 64 * BK * 2;  // one 64-wide MN-major chunk: BK rows x 128 B
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
+struct Cfg {
+  static constexpr int NB = EPI == EPI_SWIGLU ? 2 : 1;
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + NB * B_BYTES;
+  static constexpr int ACC_COLS = NB * BN;
+  static constexpr int TMEM_COLS = 2 * ACC_COLS;
+  static constexpr uint32_t IDESC = sm100::idesc_bf16(BM, BN, A_MN, B_MN);
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+  static_assert(TMEM_COLS == 128 || TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM columns must be a power of 2");
+};
+
+struct GemmArgs {
+  int M, N, K;
+  void* C;
+  long ldc;
+  int tiles_m, tiles_n;
+  float alpha;
+  int* status;
+};
+
+__device__ __forceinline__ void store_row(float (&v)[32], int epi, void* C, long ldc, int row, int col, int N,
+                                          float alpha) {
+  if (epi == EPI_BF16 || epi == EPI_SWIGLU) {
+    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(C) + (long)row * ldc + col;
+    if (col + 32 <= N && ((reinterpret_cast<uintptr_t>(out) & 15) == 0)) {
+      uint4* dst = reinterpret_cast<uint4*>(out);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        __nv_bfloat162 p0 = __floats2bfloat162_rn(v[8 * q + 0], v[8 * q + 1]);
+        __nv_bfloat162 p1 = __floats2bfloat162_rn(v[8 * q + 2], v[8 * q + 3]);
+        __nv_bfloat162 p2 = __floats2bfloat162_rn(v[8 * q + 4], v[8 * q + 5]);
+        __nv_bfloat162 p3 = __floats2bfloat162_rn(v[8 * q + 6], v[8 * q + 7]);
+        uint4 pk;
+        pk.x = *reinterpret_cast<uint32_t*>(&p0);
+        pk.y = *reinterpret_cast<uint32_t*>(&p1);
+        pk.z = *reinterpret_cast<uint32_t*>(&p2);
+        pk.w = *reinterpret_cast<uint32_t*>(&p3);
+        dst[q] = pk;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (col + i < N) out[i] = __float2bfloat16_rn(v[i]);
+    }
+    return;
+  }
+  float* out = reinterpret_cast<float*>(C) + (long)row * ldc + col;
+  const bool vec = col + 32 <= N && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
+  if (epi == EPI_F32) {
+    if (vec) {
+      float4* dst = reinterpret_cast<float4*>(out);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (col + i < N) out[i] = v[i];
+    }
+  } else {  // EPI_F32_ACCUM
+    if (vec) {
+      float4* dst = reinterpret_cast<float4*>(out);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        float4 o = dst[q];
+        o.x += alpha * v[4 * q]; o.y += alpha * v[4 * q + 1]; o.z += alpha * v[4 * q + 2]; o.w += alpha * v[4 * q + 3];
+        dst[q] = o;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (col + i < N) out[i] += alpha * v[i];
+    }
+  }
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(THREADS, 1)
+gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb0,
+            const __grid_constant__ CUtensorMap tb1, const GemmArgs args) {
+  using C_ = Cfg<BN, A_MN, B_MN, EPI>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * C_::STAGE_BYTES);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* tfull = bars + 2 * STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int total = args.tiles_m * args.tiles_n;
+  const int kblocks = (args.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      sm100::mbar_init(&full[s], 1);
+      sm100::mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      sm100::mbar_init(&tfull[a], 1);
+      sm100::mbar_init(&tempty[a], 128);
+    }
+    sm100::mbar_init(drain, 1);
+    *abort = 0;
+    sm100::fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    sm100::prefetch_tmap(&ta);
+    sm100::prefetch_tmap(&tb0);
+    if (C_::NB == 2) sm100::prefetch_tmap(&tb1);
+  }
+  if (warp == 1) {
+    sm100::tmem_alloc(tmem_slot, C_::TMEM_COLS);
+    sm100::tmem_relinquish();
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    if (sm100::elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      for (int tile = blockIdx.x; tile < total && !*abort; tile += gridDim.x) {
+        const int tm = tile % args.tiles_m, tn = tile / args.tiles_m;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!sm100::mbar_wait(&empty[stage], phase ^ 1, abort)) break;
+          uint8_t* a_dst = smem + stage * C_::STAGE_BYTES;
+          sm100::mbar_expect_tx(&full[stage], C_::STAGE_BYTES);
+          if (!A_MN) {
+            sm100::tma_load_2d(a_dst, &ta, &full[stage], kb * BK, tm * BM);
+          } else {
+            sm100::tma_load_2d(a_dst, &ta, &full[stage], tm * BM, kb * BK);
+            sm100::tma_load_2d(a_dst + MN_CHUNK_BYTES, &ta, &full[stage], tm * BM + 64, kb * BK);
+          }
+#pragma unroll
+          for (int j = 0; j < C_::NB; ++j) {
+            uint8_t* b_dst = a_dst + C_::A_BYTES + j * C_::B_BYTES;
+            const CUtensorMap* tb = j == 0 ? &tb0 : &tb1;
+            if (!B_MN) {
+              sm100::tma_load_2d(b_dst, tb, &full[stage], kb * BK, tn * BN);
+            } else {
+#pragma unroll
+              for (int c = 0; c < BN / 64; ++c)
+                sm100::tma_load_2d(b_dst + c * MN_CHUNK_BYTES, tb, &full[stage], tn * BN + c * 64, kb * BK);
+            }
+          }
+          ++issued;
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      // Drain: every issued stage must have been consumed before shared memory goes away.
+      (void)issued;
+      for (int s = 0; s < STAGES; ++s) {
+        if (!sm100::mbar_wait_bounded(&empty[stage], phase ^ 1)) break;
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (sm100::elect_one()) {
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      for (int tile = blockIdx.x; tile < total && !*abort; tile += gridDim.x) {
+        if (!sm100::mbar_wait(&tempty[acc], acc_phase ^ 1, abort)) break;
+        sm100::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * C_::ACC_COLS;
+        bool ok = true;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!sm100::mbar_wait(&full[stage], phase, abort)) { ok = false; break; }
+          sm100::tc_fence_after();
+          const uint32_t a_base = sm100::smem_u32(smem + stage * C_::STAGE_BYTES);
+#pragma unroll
+          for (int ks = 0; ks < BK / 16; ++ks) {
+            const uint64_t adesc = A_MN ? sm100::smem_desc(a_base + ks * 2048, MN_CHUNK_BYTES, 1024)
+                                        : sm100::smem_desc(a_base + ks * 32, 16, 1024);
+#pragma unroll
+            for (int j = 0; j < C_::NB; ++j) {
+              const uint32_t b_base = a_base + C_::A_BYTES + j * C_::B_BYTES;
+              const uint64_t bdesc = B_MN ? sm100::smem_desc(b_base + ks * 2048, MN_CHUNK_BYTES, 1024)
+                                          : sm100::smem_desc(b_base + ks * 32, 16, 1024);
+              sm100::mma_bf16(d_tmem + j * BN, adesc, bdesc, C_::IDESC, (kb | ks) != 0);
+            }
+          }
+          sm100::mma_commit(&empty[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        sm100::mma_commit(&tfull[acc]);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      }
+      sm100::mma_commit(drain);
+      sm100::mbar_wait_bounded(drain, 0);
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue (warps 2..5)
+    const int quarter = warp & 3;
+    const int row_in_tile = quarter * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < total && !*abort; tile += gridDim.x) {
+      const int tm = tile % args.tiles_m, tn = tile / args.tiles_m;
+      if (!sm100::mbar_wait(&tfull[acc], acc_phase, abort)) break;
+      sm100::tc_fence_after();
+      const int row = tm * BM + row_in_tile;
+      const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * C_::ACC_COLS;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        float v[32];
+        sm100::tmem_ld32(t_row + c * 32, v);
+        if (EPI == EPI_SWIGLU) {
+          float u[32];
+          sm100::tmem_ld32(t_row + BN + c * 32, u);
+          sm100::tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = rt::siluf_(v[i]) * u[i];
+        } else {
+          sm100::tmem_wait_ld();
+        }
+        if (row < args.M) store_row(v, EPI, args.C, args.ldc, row, tn * BN + c * 32, args.N, args.alpha);
+      }
+      sm100::tc_fence_before();
+      sm100::mbar_arrive(&tempty[acc]);
+      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+    }
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem_base, C_::TMEM_COLS);
+  }
+  if (threadIdx.x == 0 && *abort && args.status) atomicExch(args.status, 1);
+}
+
+bool make_tmap(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+               uint32_t box_inner, uint32_t box_outer) {
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = cuTensorMapEncodeTiled(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides,
+                                      box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+int num_sms_cached() {
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return sms;
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
+cudaError_t launch(const void* A, long lda, const void* B0, const void* B1, long ldb, void* C, long ldc, int M,
+                   int N, int K, float alpha, int* status, cudaStream_t stream) {
+  using C_ = Cfg<BN, A_MN, B_MN, EPI>;
+  CUtensorMap ta, tb0, tb1;
+  bool ok = A_MN ? make_tmap(&ta, A, M, K, lda * 2, 64, BK) : make_tmap(&ta, A, K, M, lda * 2, BK, BM);
+  ok = ok && (B_MN ? make_tmap(&tb0, B0, N, K, ldb * 2, 64, BK) : make_tmap(&tb0, B0, K, N, ldb * 2, BK, BN));
+  if (C_::NB == 2)
+    ok = ok && (B_MN ? make_tmap(&tb1, B1, N, K, ldb * 2, 64, BK) : make_tmap(&tb1, B1, K, N, ldb * 2, BK, BN));
+  else
+    tb1 = tb0;
+  if (!ok) return cudaErrorInvalidValue;
+  GemmArgs args;
+  args.M = M; args.N = N; args.K = K; args.C = C; args.ldc = ldc; args.alpha = alpha; args.status = status;
+  args.tiles_m = (M + BM - 1) / BM;
+  args.tiles_n = (N + BN - 1) / BN;
+  const int total = args.tiles_m * args.tiles_n;
+  auto kern = gemm_kernel<BN, A_MN, B_MN, EPI>;
+  RT_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C_::SMEM_BYTES));
+  const int grid = total < num_sms_cached() ? total : num_sms_cached();
+  kern<<<grid, THREADS, C_::SMEM_BYTES, stream>>>(ta, tb0, tb1, args);
+  return cudaGetLastError();
+}
+
+// Tile width: the smallest number of "waves x tile width" over the SMs.
+int pick_bn(int M, int N, bool swiglu) {
+  if (swiglu) return 128;
+  const int sms = num_sms_cached();
+  const int tm = (M + BM - 1) / BM;
+  int best = 256;
+  long best_cost = -1;
+  for (int bn : {256, 128, 64}) {
+    const long tiles = (long)tm * ((N + bn - 1) / bn);
+    const long waves = (tiles + sms - 1) / sms;
+    const long cost = waves * bn + (bn == 64 ? 16 : 0);
+    if (best_cost < 0 || cost < best_cost) { best_cost = cost; best = bn; }
+  }
+  return best;
+}
+
+template <bool A_MN, bool B_MN, int EPI>
+cudaError_t dispatch_bn(int bn, const void* A, long lda, const void* B0, const void* B1, long ldb, void* C, long ldc,
+                        int M, int N, int K, float alpha, int* status, cudaStream_t s) {
+  if (bn == 256) return launch<256, A_MN, B_MN, EPI>(A, lda, B0, B1, ldb, C, ldc, M, N, K, alpha, status, s);
+  if (bn == 128) return launch<128, A_MN, B_MN, EPI>(A, lda, B0, B1, ldb, C, ldc, M, N, K, alpha, status, s);
+  return launch<64, A_MN, B_MN, EPI>(A, lda, B0, B1, ldb, C, ldc, M, N, K, alpha, status, s);
+}
+
+}  // namespace
+
+// C[M,N] (ldc) = epi(A · B^T); A K-major [M,K] (lda) or MN-major [K,M] (lda); B K-major [N,K] (ldb) or
+// MN-major [K,N] (ldb). bf16 operands; lda/ldb/ldc multiples of 8 elements, 16-byte aligned bases.
+extern "C" cudaError_t rt_gemm_bf16(const void* A, long lda, int a_mn, const void* B, long ldb, int b_mn, void* C,
+                                    long ldc, int M, int N, int K, int epi, float alpha, int* status,
+                                    cudaStream_t stream) {
+  if (M <= 0 || N <= 0 || K <= 0) return cudaSuccess;
+  if ((lda & 7) || (ldb & 7) || (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15))
+    return cudaErrorInvalidValue;
+  const int bn = pick_bn(M, N, false);
+#define RT_G(AM, BMN)                                                                                         \
+  switch (epi) {                                                                                              \
+    case EPI_BF16: return dispatch_bn<AM, BMN, EPI_BF16>(bn, A, lda, B, B, ldb, C, ldc, M, N, K, alpha, status, stream); \
+    case EPI_F32: return dispatch_bn<AM, BMN, EPI_F32>(bn, A, lda, B, B, ldb, C, ldc, M, N, K, alpha, status, stream);   \
+    default: return dispatch_bn<AM, BMN, EPI_F32_ACCUM>(bn, A, lda, B, B, ldb, C, ldc, M, N, K, alpha, status, stream);  \
+  }
+  if (!a_mn && !b_mn) { RT_G(false, false) }
+  if (!a_mn && b_mn) { RT_G(false, true) }
+  if (a_mn && !b_mn) { RT_G(true, false) }
+  RT_G(true, true)
+#undef RT_G
+}
+
+// out[M,N] bf16 = silu(A · Bg^T) * (A · Bu^T); A, Bg, Bu K-major.
+extern "C" cudaError_t rt_gemm_swiglu_bf16(const void* A, long lda, const void* Bg, const void* Bu, long ldb, void* C,
+                                           long ldc, int M, int N, int K, int* status, cudaStream_t stream) {
+  if (M <= 0 || N <= 0 || K <= 0) return cudaSuccess;
+  if ((lda & 7) || (ldb & 7)) return cudaErrorInvalidValue;
+  return launch<128, false, false, EPI_SWIGLU>(A, lda, Bg, Bu, ldb, C, ldc, M, N, K, 1.f, status, stream);
+}

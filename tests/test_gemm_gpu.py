@@ -1,0 +1,65 @@
+"""tcgen05 GEMM against an fp32 PyTorch matmul of the same bf16 operands."""
+import pytest
+import torch
+
+from rwkv_theseus_b200.ops import native
+
+pytestmark = pytest.mark.gpu
+cuda = pytest.mark.skipif(not torch.cuda.is_available(), reason="CUDA unavailable")
+
+
+def _bf(*shape, seed=0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    return (torch.randn(*shape, device="cuda", generator=g) * 0.5).to(torch.bfloat16)
+
+
+def _check(out, ref, tol=2e-2):
+    err = (out.float() - ref).abs().max().item()
+    scale = ref.abs().max().item() + 1e-6
+    assert err <= tol * scale, (err, scale)
+
+
+@cuda
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 512), (1024, 5120, 5120), (37, 48, 5120),
+                                   (1, 192, 5120), (130, 352, 192), (1000, 200, 352), (64, 64, 8)])
+@pytest.mark.parametrize("a_t,b_t", [(False, False), (False, True), (True, False), (True, True)])
+def test_layouts_and_tails(M, N, K, a_t, b_t):
+    if (a_t and M % 8) or (b_t and N % 8):
+        pytest.skip("MN-major operands need a row stride that is a multiple of 8")
+    A = _bf(K, M, seed=1) if a_t else _bf(M, K, seed=1)
+    B = _bf(K, N, seed=2) if b_t else _bf(N, K, seed=2)
+    ref = (A.float().t() if a_t else A.float()) @ (B.float() if b_t else B.float().t())
+    out = native().gemm(A, a_t, B, b_t, 0, 1.0, None)
+    _check(out, ref)
+    out32 = native().gemm(A, a_t, B, b_t, 1, 1.0, None)
+    _check(out32, ref, 1e-3)
+
+
+@cuda
+def test_accumulate_epilogue():
+    dy, x = _bf(300, 256, seed=3), _bf(300, 192, seed=4)
+    grad = torch.randn(256, 192, device="cuda")
+    expected = grad + 0.5 * dy.float().t() @ x.float()
+    native().gemm(dy, True, x, True, 2, 0.5, grad)
+    _check(grad, expected, 1e-3)
+
+
+@cuda
+def test_swiglu_epilogue():
+    x, wg, wu = _bf(257, 512, seed=5), _bf(384, 512, seed=6), _bf(384, 512, seed=7)
+    ref = torch.nn.functional.silu(x.float() @ wg.float().t()) * (x.float() @ wu.float().t())
+    _check(native().gemm_swiglu(x, wg, wu), ref)
+
+
+@cuda
+def test_strided_rows_and_current_stream():
+    big = _bf(512, 1024, seed=8)
+    A = big[:, 256:768]                 # row stride 1024, unit inner stride
+    B = _bf(640, 512, seed=9)
+    ref = A.float() @ B.float().t()
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        out = native().gemm(A, False, B, False, 0, 1.0, None)
+    torch.cuda.current_stream().wait_stream(stream)
+    _check(out, ref)
