@@ -24,6 +24,53 @@ cudaError_t rt_gemm_bf16(const void* A, long lda, int a_mn, const void* B, long 
 cudaError_t rt_gemm_swiglu_bf16(const void* A, long lda, const void* Bg, const void* Bu, long ldb, void* C, long ldc,
                                 int M, int N, int K, int* status, cudaStream_t stream);
 
+// Teacher-block kernels (bf16 activations, fp32 parameters).
+cudaError_t rt_rmsnorm_1p(const void* x, const void* h, const float* w, void* sum_out, void* out, long rows, int C,
+                          float eps, cudaStream_t stream);
+cudaError_t rt_conv1d_silu(const void* x, const void* state, const float* weight, void* y, void* new_state, int B,
+                           int T, int C, int K, cudaStream_t stream);
+cudaError_t rt_gated_rmsnorm(const void* x, const void* z, const float* w, void* out, long rows, int D, float eps,
+                             cudaStream_t stream);
+cudaError_t rt_norm_rope(const void* src, long src_stride, const float* w, const float* inv_freq, void* dst, int B,
+                         int T, int heads, long dst_batch_stride, int pos0, int D, int rot, float eps,
+                         cudaStream_t stream);
+cudaError_t rt_copy_rows(const void* src, long src_stride, void* dst, int B, int T, long dst_batch_stride, int width,
+                         cudaStream_t stream);
+long rt_gdn_workspace_floats(int B, int T, int Hk, int D);
+cudaError_t rt_gdn_forward(const void* qkv, long row_stride, const void* a, const void* b, long ab_stride,
+                           const float* A_log, const float* dt_bias, float* state, void* out, float* work, int B,
+                           int T, int Hk, int Hv, int D, cudaStream_t stream);
+
+// TimeMix student stages and the flat optimizer (student_ops.cu).
+cudaError_t rt_tm_mix(const void* x, const void* shift, const float* coef, void* out, int B, int T, int C,
+                      cudaStream_t s);
+cudaError_t rt_tm_mix_bwd(const void* x, const void* shift, const void* dmix, float* dcoef, int B, int T, int C,
+                          cudaStream_t s);
+cudaError_t rt_tm_pre_wkv(const void* k, const void* lw, const void* la, const float* w0, const float* a0,
+                          const float* k_k, const float* k_a, void* w_in, void* k_in, void* a_in, void* b_in,
+                          long rows, int H, int N, cudaStream_t s);
+cudaError_t rt_tm_post_wkv(const void* y, const void* r, const void* kp, const void* v, const void* g,
+                           const float* ln_w, const float* ln_b, const float* r_k, void* out, float* stats, long rows,
+                           int H, int N, cudaStream_t s);
+cudaError_t rt_tm_post_wkv_bwd(const void* dout, const void* y, const void* r, const void* kp, const void* v,
+                               const void* g, const float* ln_w, const float* ln_b, const float* r_k,
+                               const float* stats, void* dy, void* dg, float* dr, float* dk, float* dv, float* dln_w,
+                               float* dln_b, float* dr_k, long rows, int H, int N, cudaStream_t s);
+cudaError_t rt_tm_pre_wkv_bwd(const float* g_r, const float* g_w, const float* g_kp, const float* g_v,
+                              const float* g_a, const float* g_b, const float* b_r, const float* b_kp,
+                              const float* b_v, const void* k, const void* la, const float* w0, const float* a0,
+                              const float* k_k, const float* k_a, void* dr, void* dk, void* dv, void* dlw, void* dla,
+                              float* dw0, float* da0, float* dk_k, float* dk_a, long rows, int H, int N,
+                              cudaStream_t s);
+cudaError_t rt_act(void* x, long n, int mode, cudaStream_t s);
+cudaError_t rt_act_bwd(const void* h, void* dh, long n, int mode, cudaStream_t s);
+cudaError_t rt_nmse_loss(const void* pred, const void* target, float* stats, void* dpred, long rows, int C, float eps,
+                         cudaStream_t s);
+cudaError_t rt_flat_adamw(float* p, float* g, float* m, float* v, void* shadow, long n, long decay_numel,
+                          const float* stats, float* norm2, float* report, float lr, float beta1, float beta2,
+                          float eps, float weight_decay, float clip, int step, cudaStream_t s);
+cudaError_t rt_to_bf16(const float* src, void* dst, long n, cudaStream_t s);
+
 #ifdef __cplusplus
 }
 #endif

@@ -137,6 +137,208 @@ at::Tensor gemm_swiglu(at::Tensor A, at::Tensor Bg, at::Tensor Bu) {
   return C;
 }
 
+void check_bf16(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.is_contiguous(), name,
+              " must be a contiguous CUDA bf16 tensor");
+}
+
+at::Tensor f32(const at::Tensor& w) { return w.to(at::kFloat).contiguous(); }
+
+at::Tensor rmsnorm_1p(at::Tensor x, at::Tensor w, double eps) {
+  check_bf16(x, "x");
+  c10::cuda::CUDAGuard guard(x.device());
+  const long C = x.size(-1), rows = x.numel() / C;
+  auto wf = f32(w);
+  auto out = at::empty_like(x);
+  check_cuda(rt_rmsnorm_1p(x.data_ptr(), nullptr, wf.data_ptr<float>(), nullptr, out.data_ptr(), rows, C, eps,
+                           stream_of(x)),
+             "rmsnorm_1p");
+  return out;
+}
+
+std::vector<at::Tensor> add_rmsnorm_1p(at::Tensor x, at::Tensor h, at::Tensor w, double eps) {
+  check_bf16(x, "x");
+  check_bf16(h, "h");
+  TORCH_CHECK(x.sizes() == h.sizes(), "residual shapes differ");
+  c10::cuda::CUDAGuard guard(x.device());
+  const long C = x.size(-1), rows = x.numel() / C;
+  auto wf = f32(w);
+  auto sum = at::empty_like(x), out = at::empty_like(x);
+  check_cuda(rt_rmsnorm_1p(x.data_ptr(), h.data_ptr(), wf.data_ptr<float>(), sum.data_ptr(), out.data_ptr(), rows, C,
+                           eps, stream_of(x)),
+             "add_rmsnorm_1p");
+  return {sum, out};
+}
+
+std::vector<at::Tensor> conv1d_silu(at::Tensor x, at::Tensor state, at::Tensor weight) {
+  check_bf16(x, "x");
+  check_bf16(state, "state");
+  c10::cuda::CUDAGuard guard(x.device());
+  const int B = x.size(0), T = x.size(1), C = x.size(2), K = weight.size(-1);
+  TORCH_CHECK(state.size(0) == B && state.size(1) == K - 1 && state.size(2) == C, "conv state must be [B, K-1, C]");
+  auto wf = f32(weight.reshape({C, K}));
+  auto y = at::empty_like(x), ns = at::empty_like(state);
+  check_cuda(rt_conv1d_silu(x.data_ptr(), state.data_ptr(), wf.data_ptr<float>(), y.data_ptr(), ns.data_ptr(), B, T, C,
+                            K, stream_of(x)),
+             "conv1d_silu");
+  return {y, ns};
+}
+
+at::Tensor gated_rmsnorm(at::Tensor x, at::Tensor z, at::Tensor w, double eps) {
+  check_bf16(x, "x");
+  check_bf16(z, "z");
+  c10::cuda::CUDAGuard guard(x.device());
+  const long D = w.numel(), rows = x.numel() / D;
+  auto wf = f32(w);
+  auto out = at::empty_like(x);
+  check_cuda(rt_gated_rmsnorm(x.data_ptr(), z.data_ptr(), wf.data_ptr<float>(), out.data_ptr(), rows, D, eps,
+                              stream_of(x)),
+             "gated_rmsnorm");
+  return out;
+}
+
+// src: [B*T, row] bf16 rows whose head h starts at h * (row_stride / heads); writes RMSNorm(1+w) + RoPE
+// (angle position rope_pos0 + t) into dst[b, dst_pos0 + t, head, :] of dst [B, cap, heads, D].
+void norm_rope_(at::Tensor src, int64_t heads, at::Tensor w, at::Tensor inv_freq, at::Tensor dst, int64_t rope_pos0,
+                int64_t dst_pos0, int64_t rot, double eps) {
+  TORCH_CHECK(src.is_cuda() && src.scalar_type() == at::kBFloat16 && src.dim() == 2 && src.stride(-1) == 1,
+              "src must be 2-D bf16 rows");
+  check_bf16(dst, "dst");
+  TORCH_CHECK(dst.dim() == 4 && dst.size(2) == heads, "dst must be [B, cap, heads, D]");
+  c10::cuda::CUDAGuard guard(src.device());
+  const int B = dst.size(0), D = dst.size(3);
+  const int T = src.size(0) / B;
+  TORCH_CHECK(dst_pos0 + T <= dst.size(1), "cache too small");
+  auto wf = f32(w), fq = f32(inv_freq);
+  check_cuda(rt_norm_rope(src.data_ptr(), src.stride(0), wf.data_ptr<float>(), fq.data_ptr<float>(),
+                          dst.data_ptr<at::BFloat16>() + dst_pos0 * heads * D, B, T, heads, dst.stride(0),
+                          (int)rope_pos0, D, rot, eps, stream_of(src)),
+             "norm_rope");
+}
+
+void copy_rows_(at::Tensor src, at::Tensor dst, int64_t pos0) {
+  TORCH_CHECK(src.is_cuda() && src.scalar_type() == at::kBFloat16 && src.dim() == 2 && src.stride(-1) == 1,
+              "src must be 2-D bf16 rows");
+  check_bf16(dst, "dst");
+  c10::cuda::CUDAGuard guard(src.device());
+  const int B = dst.size(0);
+  const int width = dst.size(2) * dst.size(3);
+  const int T = src.size(0) / B;
+  TORCH_CHECK(pos0 + T <= dst.size(1) && src.size(1) >= width, "cache too small or rows too narrow");
+  const long src_stride = src.stride(0);
+  check_cuda(rt_copy_rows(src.data_ptr(), src_stride, dst.data_ptr<at::BFloat16>() + pos0 * width, B, T, dst.stride(0),
+                          width, stream_of(src)),
+             "copy_rows");
+}
+
+// GDN forward on the conv output `qkv` [B, T, 2*Hk*D + Hv*D]; a, b: [B, T, Hv]; state [B, Hv, D, D] fp32
+// (updated in place). Returns o [B, T, Hv, D] bf16.
+at::Tensor gdn_forward(at::Tensor qkv, at::Tensor a, at::Tensor b, at::Tensor A_log, at::Tensor dt_bias,
+                       at::Tensor state, int64_t Hk, int64_t Hv, int64_t D) {
+  check_bf16(qkv, "qkv");
+  TORCH_CHECK(a.is_cuda() && a.scalar_type() == at::kBFloat16 && a.stride(-1) == 1, "a must be bf16");
+  TORCH_CHECK(b.is_cuda() && b.scalar_type() == at::kBFloat16 && b.stride(-1) == 1 && a.stride(-2) == b.stride(-2),
+              "b must be bf16 with the stride of a");
+  TORCH_CHECK(state.is_cuda() && state.scalar_type() == at::kFloat && state.is_contiguous(), "state must be fp32");
+  c10::cuda::CUDAGuard guard(qkv.device());
+  const int B = qkv.size(0), T = qkv.size(1);
+  TORCH_CHECK(qkv.size(2) == 2 * Hk * D + Hv * D, "qkv width mismatch");
+  auto work = at::empty({rt_gdn_workspace_floats(B, T, Hk, D)}, state.options());
+  auto out = at::empty({B, T, Hv, D}, qkv.options());
+  auto al = f32(A_log), dt = f32(dt_bias);
+  check_cuda(rt_gdn_forward(qkv.data_ptr(), qkv.size(2), a.data_ptr(), b.data_ptr(), a.stride(-2), al.data_ptr<float>(),
+                            dt.data_ptr<float>(), state.data_ptr<float>(), out.data_ptr(), work.data_ptr<float>(), B, T,
+                            Hk, Hv, D, stream_of(qkv)),
+             "gdn_forward");
+  return out;
+}
+
+// ------------------------------------------------------------------ TimeMix student stages
+// Raw-pointer bindings: the Python layer (models/student_fused.py) owns shapes and buffers.
+#define PTR(t) ((t).data_ptr())
+#define FPTR(t) ((t).data_ptr<float>())
+void need(bool ok, const char* msg) { TORCH_CHECK(ok, msg); }
+
+void tm_mix(at::Tensor x, at::Tensor shift, at::Tensor coef, at::Tensor out) {
+  need(x.is_contiguous() && shift.is_contiguous() && out.is_contiguous() && coef.is_contiguous(), "tm_mix layout");
+  c10::cuda::CUDAGuard guard(x.device());
+  check_cuda(rt_tm_mix(PTR(x), PTR(shift), FPTR(coef), PTR(out), x.size(0), x.size(1), x.size(2), stream_of(x)),
+             "tm_mix");
+}
+void tm_mix_bwd(at::Tensor x, at::Tensor shift, at::Tensor dmix, at::Tensor dcoef) {
+  c10::cuda::CUDAGuard guard(x.device());
+  check_cuda(rt_tm_mix_bwd(PTR(x), PTR(shift), PTR(dmix), FPTR(dcoef), x.size(0), x.size(1), x.size(2), stream_of(x)),
+             "tm_mix_bwd");
+}
+void tm_pre_wkv(at::Tensor k, at::Tensor lw, at::Tensor la, at::Tensor w0, at::Tensor a0, at::Tensor k_k,
+                at::Tensor k_a, at::Tensor w_in, at::Tensor k_in, at::Tensor a_in, at::Tensor b_in, int64_t H,
+                int64_t N) {
+  c10::cuda::CUDAGuard guard(k.device());
+  check_cuda(rt_tm_pre_wkv(PTR(k), PTR(lw), PTR(la), FPTR(w0), FPTR(a0), FPTR(k_k), FPTR(k_a), PTR(w_in), PTR(k_in),
+                           PTR(a_in), PTR(b_in), k.numel() / (H * N), H, N, stream_of(k)),
+             "tm_pre_wkv");
+}
+void tm_post_wkv(at::Tensor y, at::Tensor r, at::Tensor kp, at::Tensor v, at::Tensor g, at::Tensor ln_w,
+                 at::Tensor ln_b, at::Tensor r_k, at::Tensor out, at::Tensor stats, int64_t H, int64_t N) {
+  c10::cuda::CUDAGuard guard(y.device());
+  check_cuda(rt_tm_post_wkv(PTR(y), PTR(r), PTR(kp), PTR(v), PTR(g), FPTR(ln_w), FPTR(ln_b), FPTR(r_k), PTR(out),
+                            FPTR(stats), y.numel() / (H * N), H, N, stream_of(y)),
+             "tm_post_wkv");
+}
+void tm_post_wkv_bwd(at::Tensor dout, at::Tensor y, at::Tensor r, at::Tensor kp, at::Tensor v, at::Tensor g,
+                     at::Tensor ln_w, at::Tensor ln_b, at::Tensor r_k, at::Tensor stats, at::Tensor dy, at::Tensor dg,
+                     at::Tensor dr, at::Tensor dk, at::Tensor dv, at::Tensor dln_w, at::Tensor dln_b,
+                     at::Tensor dr_k, int64_t H, int64_t N) {
+  c10::cuda::CUDAGuard guard(y.device());
+  check_cuda(rt_tm_post_wkv_bwd(PTR(dout), PTR(y), PTR(r), PTR(kp), PTR(v), PTR(g), FPTR(ln_w), FPTR(ln_b), FPTR(r_k),
+                                FPTR(stats), PTR(dy), PTR(dg), FPTR(dr), FPTR(dk), FPTR(dv), FPTR(dln_w), FPTR(dln_b),
+                                FPTR(dr_k), y.numel() / (H * N), H, N, stream_of(y)),
+             "tm_post_wkv_bwd");
+}
+void tm_pre_wkv_bwd(std::vector<at::Tensor> gw, std::vector<at::Tensor> bonus, at::Tensor k, at::Tensor la,
+                    at::Tensor w0, at::Tensor a0, at::Tensor k_k, at::Tensor k_a, std::vector<at::Tensor> outs,
+                    std::vector<at::Tensor> pgrads, int64_t H, int64_t N) {
+  need(gw.size() == 6 && bonus.size() == 3 && outs.size() == 5 && pgrads.size() == 4, "tm_pre_wkv_bwd arity");
+  c10::cuda::CUDAGuard guard(k.device());
+  check_cuda(rt_tm_pre_wkv_bwd(FPTR(gw[0]), FPTR(gw[1]), FPTR(gw[2]), FPTR(gw[3]), FPTR(gw[4]), FPTR(gw[5]),
+                               FPTR(bonus[0]), FPTR(bonus[1]), FPTR(bonus[2]), PTR(k), PTR(la), FPTR(w0), FPTR(a0),
+                               FPTR(k_k), FPTR(k_a), PTR(outs[0]), PTR(outs[1]), PTR(outs[2]), PTR(outs[3]),
+                               PTR(outs[4]), FPTR(pgrads[0]), FPTR(pgrads[1]), FPTR(pgrads[2]), FPTR(pgrads[3]),
+                               k.numel() / (H * N), H, N, stream_of(k)),
+             "tm_pre_wkv_bwd");
+}
+void act_(at::Tensor x, int64_t mode) {
+  c10::cuda::CUDAGuard guard(x.device());
+  check_cuda(rt_act(PTR(x), x.numel(), mode, stream_of(x)), "act");
+}
+void act_bwd_(at::Tensor h, at::Tensor dh, int64_t mode) {
+  c10::cuda::CUDAGuard guard(h.device());
+  check_cuda(rt_act_bwd(PTR(h), PTR(dh), h.numel(), mode, stream_of(h)), "act_bwd");
+}
+void nmse_loss(at::Tensor pred, at::Tensor target, at::Tensor stats, c10::optional<at::Tensor> dpred, double eps) {
+  need(pred.is_contiguous() && target.is_contiguous() && pred.sizes() == target.sizes(), "loss operands");
+  c10::cuda::CUDAGuard guard(pred.device());
+  const long C = pred.size(-1);
+  check_cuda(rt_nmse_loss(PTR(pred), PTR(target), FPTR(stats), dpred ? PTR(*dpred) : nullptr, pred.numel() / C, C,
+                          eps, stream_of(pred)),
+             "nmse_loss");
+}
+void flat_adamw(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, c10::optional<at::Tensor> shadow,
+                int64_t decay_numel, at::Tensor stats, at::Tensor norm2, at::Tensor report, double lr, double beta1,
+                double beta2, double eps, double wd, double clip, int64_t step) {
+  need(p.numel() == g.numel() && p.numel() == m.numel() && p.numel() == v.numel(), "flat buffer sizes");
+  c10::cuda::CUDAGuard guard(p.device());
+  check_cuda(rt_flat_adamw(FPTR(p), FPTR(g), FPTR(m), FPTR(v), shadow ? PTR(*shadow) : nullptr, p.numel(), decay_numel,
+                           FPTR(stats), FPTR(norm2), FPTR(report), lr, beta1, beta2, eps, wd, clip, step,
+                           stream_of(p)),
+             "flat_adamw");
+}
+void to_bf16_(at::Tensor src, at::Tensor dst) {
+  need(src.numel() == dst.numel(), "to_bf16 sizes");
+  c10::cuda::CUDAGuard guard(src.device());
+  check_cuda(rt_to_bf16(FPTR(src), PTR(dst), src.numel(), stream_of(src)), "to_bf16");
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -147,5 +349,24 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("A"), py::arg("a_t"), py::arg("B"), py::arg("b_t"), py::arg("epi") = 0, py::arg("alpha") = 1.0,
         py::arg("out") = py::none());
   m.def("gemm_swiglu", &gemm_swiglu, "silu(A . Bg^T) * (A . Bu^T) in one tcgen05 GEMM");
+  m.def("rmsnorm_1p", &rmsnorm_1p);
+  m.def("add_rmsnorm_1p", &add_rmsnorm_1p);
+  m.def("conv1d_silu", &conv1d_silu);
+  m.def("gated_rmsnorm", &gated_rmsnorm);
+  m.def("norm_rope_", &norm_rope_);
+  m.def("copy_rows_", &copy_rows_);
+  m.def("gdn_forward", &gdn_forward);
+  m.def("tm_mix", &tm_mix);
+  m.def("tm_mix_bwd", &tm_mix_bwd);
+  m.def("tm_pre_wkv", &tm_pre_wkv);
+  m.def("tm_post_wkv", &tm_post_wkv);
+  m.def("tm_post_wkv_bwd", &tm_post_wkv_bwd);
+  m.def("tm_pre_wkv_bwd", &tm_pre_wkv_bwd);
+  m.def("act_", &act_);
+  m.def("act_bwd_", &act_bwd_);
+  m.def("nmse_loss", &nmse_loss, py::arg("pred"), py::arg("target"), py::arg("stats"), py::arg("dpred"),
+        py::arg("eps"));
+  m.def("flat_adamw", &flat_adamw);
+  m.def("to_bf16_", &to_bf16_);
   m.def("wkv7_chunk_len", []() { return rt_wkv7_chunk_len(); });
 }

@@ -221,9 +221,11 @@ class TextModel(nn.Module):
         inv_freq = 1.0 / (cfg.rope_theta ** (torch.arange(0, dim, 2, dtype=torch.int64).float() / dim))
         self.register_buffer("inv_freq", inv_freq, persistent=False)
 
-    def forward(self, ids, positions, cache, stop_hook=None):
+    def forward(self, ids, positions, cache):
+        """``positions``: first absolute position (int) or a tensor of consecutive positions."""
+        start = int(positions[0]) if torch.is_tensor(positions) else int(positions)
         x = self.embed_tokens(ids)
-        rope = T.rope_tables(self.inv_freq, positions, x.dtype)
+        rope = T.rope_tables(self.inv_freq, start, ids.shape[1], x.device, x.dtype)
         for layer in self.layers:
             x = layer(x, rope, cache)
         return self.norm(x)

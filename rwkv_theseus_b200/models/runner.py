@@ -129,7 +129,6 @@ class Runner:
         """Cached forward of one chunk; returns final hidden states, or the
         attention output of ``through_layer`` (stopping there)."""
         T = ids.shape[1]
-        positions = torch.arange(self.cache.cursor, self.cache.cursor + T, device=ids.device)
         hook = None
         found = []
         if through_layer is not None:
@@ -146,7 +145,7 @@ class Runner:
         try:
             with cast:
                 try:
-                    hidden = self.model.model(ids, positions, self.cache)
+                    hidden = self.model.model(ids, self.cache.cursor, self.cache)
                 except _Boundary:
                     hidden = found.pop()
         finally:

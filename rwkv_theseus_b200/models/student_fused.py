@@ -1,0 +1,186 @@
+"""TimeMix student on CUDA: fused kernels with a hand-written backward.
+
+Same math as ``models.timemix.TimeMix.forward`` under bf16 autocast (the
+reference path, ``theseus/timemix.py:66-89``) but scheduled as:
+
+forward
+    mix (token shift, 6 lerps)                       1 kernel
+    r, k, v projections; LoRA down/up for w, a, g    9 tcgen05 GEMMs (+ tanh / sigmoid)
+    pre-WKV (decay, ICL rate, kk, k', a/b inputs)   1 kernel
+    chunked WKV7 (chunk checkpoints kept)            1 kernel
+    post-WKV (GroupNorm, bonus, output gate)         1 kernel
+    output projection                                1 GEMM
+    NMSE/cosine sums + d loss / d prediction         1 kernel
+backward
+    output projection dX / dW                        2 GEMMs (dW accumulates into the fp32 flat buffer)
+    post-WKV backward (+ ln_x, r_k partial sums)     1 kernel
+    WKV7 backward (no history, no atomics)           1 kernel
+    pre-WKV backward (+ w0, a0, k_k, k_a)            1 kernel
+    projection and LoRA dX / dW                      15 GEMMs (+ 2 activation backwards)
+    mix backward (x_* partial sums)                  1 kernel
+
+Weight operands come from a bf16 copy of the flat fp32 parameters that the
+optimizer kernel refreshes after every update (the value autocast would use);
+transposed operands are read MN-major by the GEMM, never materialised.
+"""
+import torch
+
+from ..ops import native
+
+_MIX = ("x_r", "x_w", "x_k", "x_v", "x_a", "x_g")
+
+
+class FusedStudent:
+    def __init__(self, student):
+        self.student = student
+        core, flat = student.core, student.flat
+        self.C, self.H, self.N = core.width, core.heads, core.head_size
+        self.device = flat.param.device
+        self.shadow = torch.empty(flat.numel, device=self.device, dtype=torch.bfloat16)
+        self.norm2 = torch.zeros(1, device=self.device)
+        start = flat.offsets[flat.names.index("x_r")]
+        if [flat.names[flat.names.index("x_r") + i] for i in range(6)] != list(_MIX):
+            raise RuntimeError("unexpected flat parameter order")
+        self.coef = flat.param[start:start + 6 * self.C]
+        self.dcoef = flat.grad[start:start + 6 * self.C]
+        self.refresh_weights()
+
+    # ------------------------------------------------------------------ helpers
+    def refresh_weights(self):
+        native().to_bf16_(self.student.flat.param, self.shadow)
+
+    def w(self, name):
+        """bf16 copy of a weight matrix."""
+        return self.student.flat.view(self.shadow, name)
+
+    def p(self, name):
+        return self.student.flat.view(self.student.flat.param, name).reshape(-1)
+
+    def g(self, name):
+        return self.student.flat.view(self.student.flat.grad, name)
+
+    @staticmethod
+    def mm(a, a_t, b, b_t):
+        return native().gemm(a, a_t, b, b_t, 0, 1.0, None)
+
+    @staticmethod
+    def mm_acc(grad, a, a_t, b, b_t):
+        native().gemm(a, a_t, b, b_t, 2, 1.0, grad)
+
+    def _state(self, x, state):
+        B = x.shape[0]
+        if state is None:
+            return (torch.zeros(B, self.C, device=x.device, dtype=torch.bfloat16),
+                    torch.zeros(B, self.H, self.N, self.N, device=x.device, dtype=torch.float32))
+        return state["shift"].to(torch.bfloat16).contiguous(), state["wkv"].float().contiguous()
+
+    # ------------------------------------------------------------------ forward
+    def _forward(self, x, state, keep):
+        B, T, C = x.shape
+        M, H, N = B * T, self.H, self.N
+        x = x.to(torch.bfloat16).contiguous()
+        shift, wkv0 = self._state(x, state)
+        ext = native()
+        mix = torch.empty(6, M, C, device=x.device, dtype=torch.bfloat16)
+        ext.tm_mix(x, shift, self.coef, mix)
+        xr, xw, xk, xv, xa, xg = mix.unbind(0)
+        r = self.mm(xr, False, self.w("receptance.weight"), False)
+        k = self.mm(xk, False, self.w("key.weight"), False)
+        v = self.mm(xv, False, self.w("value.weight"), False)
+        hw = self.mm(xw, False, self.w("w1"), True)
+        ext.act_(hw, 0)
+        lw = self.mm(hw, False, self.w("w2"), True)
+        ha = self.mm(xa, False, self.w("a1"), True)
+        la = self.mm(ha, False, self.w("a2"), True)
+        hg = self.mm(xg, False, self.w("g1"), True)
+        ext.act_(hg, 1)
+        g = self.mm(hg, False, self.w("g2"), True)
+        w_in, k_in, a_in, b_in = (torch.empty_like(r) for _ in range(4))
+        ext.tm_pre_wkv(k, lw, la, self.p("w0"), self.p("a0"), self.p("k_k"), self.p("k_a"),
+                       w_in, k_in, a_in, b_in, H, N)
+        shape = (B, T, H, N)
+        wkv_in = [t.view(shape) for t in (r, w_in, k_in, v, a_in, b_in)]
+        y, end, ckpt = ext.wkv7_forward(*wkv_in, wkv0, keep)
+        yg = torch.empty_like(r)
+        gn = torch.empty(M * H * 3, device=x.device)
+        ext.tm_post_wkv(y, r, k_in, v, g, self.p("ln_x.weight"), self.p("ln_x.bias"), self.p("r_k"), yg, gn, H, N)
+        pred = self.mm(yg, False, self.w("output.weight"), False)
+        new_state = {"shift": x[:, -1].clone(), "wkv": end}
+        saved = None
+        if keep:
+            saved = dict(x=x, shift=shift, mix=mix, r=r, k=k, v=v, hw=hw, ha=ha, hg=hg, lw=lw, la=la, g=g,
+                         w_in=w_in, k_in=k_in, a_in=a_in, b_in=b_in, y=y, ckpt=ckpt, yg=yg, gn=gn)
+        return pred, new_state, saved
+
+    @torch.no_grad()
+    def forward(self, x, state):
+        pred, new_state, _ = self._forward(x, state, False)
+        return pred.view(x.shape), new_state
+
+    # ------------------------------------------------------------------ training micro-step
+    @torch.no_grad()
+    def forward_backward(self, x, target, state, eps):
+        B, T, C = x.shape
+        M, H, N = B * T, self.H, self.N
+        ext = native()
+        pred, new_state, s = self._forward(x, state, True)
+        stats = torch.zeros(3, device=x.device)
+        dpred = torch.empty_like(pred)
+        ext.nmse_loss(pred, target.reshape(M, C).to(torch.bfloat16).contiguous(), stats, dpred, float(eps))
+        # output projection
+        dyg = self.mm(dpred, False, self.w("output.weight"), True)
+        self.mm_acc(self.g("output.weight"), dpred, True, s["yg"], True)
+        # post-WKV backward
+        dy = torch.empty_like(pred)
+        dg = torch.empty_like(pred)
+        bonus = [torch.empty(M, C, device=x.device) for _ in range(3)]
+        ext.tm_post_wkv_bwd(dyg, s["y"], s["r"], s["k_in"], s["v"], s["g"], self.p("ln_x.weight"),
+                            self.p("ln_x.bias"), self.p("r_k"), s["gn"], dy, dg, bonus[0], bonus[1], bonus[2],
+                            self.g("ln_x.weight"), self.g("ln_x.bias"), self.g("r_k"), H, N)
+        shape = (B, T, H, N)
+        wkv_in = [s[n].view(shape) for n in ("r", "w_in", "k_in", "v", "a_in", "b_in")]
+        dend = torch.zeros(B, H, N, N, device=x.device)
+        gw = ext.wkv7_backward(*wkv_in, s["ckpt"], dy.view(shape), dend)
+        dr, dk, dv, dlw, dla = (torch.empty_like(pred) for _ in range(5))
+        ext.tm_pre_wkv_bwd(list(gw[:6]), bonus, s["k"], s["la"], self.p("w0"), self.p("a0"), self.p("k_k"),
+                           self.p("k_a"), [dr, dk, dv, dlw, dla],
+                           [self.g("w0").reshape(-1), self.g("a0").reshape(-1), self.g("k_k").reshape(-1),
+                            self.g("k_a").reshape(-1)], H, N)
+        del gw, bonus
+        mix = s["mix"]
+        dmix = torch.empty_like(mix)
+        xr, xw, xk, xv, xa, xg = mix.unbind(0)
+        # r, k, v projections
+        for grad_out, inp, name, slot in ((dr, xr, "receptance.weight", 0), (dk, xk, "key.weight", 2),
+                                          (dv, xv, "value.weight", 3)):
+            ext.gemm(grad_out, False, self.w(name), True, 0, 1.0, dmix[slot])
+            self.mm_acc(self.g(name), grad_out, True, inp, True)
+        # decay LoRA: lw = tanh(xw w1) w2
+        self.mm_acc(self.g("w2"), s["hw"], True, dlw, True)
+        dhw = self.mm(dlw, False, self.w("w2"), False)
+        ext.act_bwd_(s["hw"], dhw, 0)
+        self.mm_acc(self.g("w1"), xw, True, dhw, True)
+        ext.gemm(dhw, False, self.w("w1"), False, 0, 1.0, dmix[1])
+        # ICL-rate LoRA: la = (xa a1) a2
+        self.mm_acc(self.g("a2"), s["ha"], True, dla, True)
+        dha = self.mm(dla, False, self.w("a2"), False)
+        self.mm_acc(self.g("a1"), xa, True, dha, True)
+        ext.gemm(dha, False, self.w("a1"), False, 0, 1.0, dmix[4])
+        # gate LoRA: g = sigmoid(xg g1) g2
+        self.mm_acc(self.g("g2"), s["hg"], True, dg, True)
+        dhg = self.mm(dg, False, self.w("g2"), False)
+        ext.act_bwd_(s["hg"], dhg, 1)
+        self.mm_acc(self.g("g1"), xg, True, dhg, True)
+        ext.gemm(dhg, False, self.w("g1"), False, 0, 1.0, dmix[5])
+        ext.tm_mix_bwd(s["x"], s["shift"], dmix, self.dcoef)
+        return stats, new_state
+
+    # ------------------------------------------------------------------ update
+    @torch.no_grad()
+    def update(self, lr, step):
+        st = self.student
+        cfg, flat = st.cfg, st.flat
+        beta1, beta2 = cfg["betas"]
+        native().flat_adamw(flat.param, flat.grad, flat.exp_avg, flat.exp_avg_sq, self.shadow, st.decay_numel,
+                            st.stats, self.norm2, st.report, float(lr), float(beta1), float(beta2),
+                            float(cfg["adam_eps"]), float(cfg["weight_decay"]), float(cfg["clip_norm"]), int(step))

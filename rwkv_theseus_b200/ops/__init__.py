@@ -14,6 +14,7 @@ def native():
     """Return the compiled extension module, raising if it cannot be imported."""
     global _NATIVE, _ERROR
     if _NATIVE is None:
+        import torch  # noqa: F401  (loads libc10/libtorch before the extension)
         try:
             _NATIVE = importlib.import_module("rwkv_theseus_b200._C")
         except ImportError as exc:  # pragma: no cover - depends on the build

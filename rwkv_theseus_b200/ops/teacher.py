@@ -43,8 +43,14 @@ def residual_add(x, y):
     return x + y
 
 
-def rope_tables(inv_freq, positions, dtype):
-    return R.rope_tables(inv_freq, positions, dtype)
+def rope_tables(inv_freq, start, length, device, dtype):
+    """(cos, sin, inv_freq, start) for positions start..start+length-1; on CUDA the
+    kernels compute the angles themselves and cos/sin are not materialised."""
+    if device.type == "cuda":
+        return None, None, inv_freq, start
+    positions = torch.arange(start, start + length, device=device)
+    cos, sin = R.rope_tables(inv_freq, positions, dtype)
+    return cos, sin, inv_freq, start
 
 
 def swiglu_mlp(x, w_gate, w_up, w_down):
@@ -122,10 +128,10 @@ def gated_attention(module, x, rope, state):
     cfg = module.cfg
     B, T, _ = x.shape
     Hq, Hkv, D = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
-    cos, sin = rope
     if _cuda(x):
         from .attention import attention_block
-        return attention_block(module, x, cos, sin, state)
+        return attention_block(module, x, rope, state)
+    cos, sin = rope[0], rope[1]
     qg = linear(x, module.q_proj.weight).view(B, T, Hq, 2 * D)
     q, gate = qg[..., :D], qg[..., D:]
     gate = gate.reshape(B, T, Hq * D)

@@ -82,7 +82,7 @@ class Student:
         self.stats = torch.zeros(3, device=device)      # [sum nmse, sum cos, count] of the current update
         self.report = torch.zeros(5, device=device)     # [nmse, cos, count, grad_norm, error] of last update
         self.fused = None
-        if device.type == "cuda":
+        if device.type == "cuda" and cfg.get("fused_optimizer", True):
             from .models.student_fused import FusedStudent
             self.fused = FusedStudent(self)
 

@@ -31,7 +31,6 @@ setup(
         sources=sources(),
         include_dirs=[os.path.join(ROOT, "csrc")],
         extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": CUDA_FLAGS},
-        libraries=["cuda"],
     )],
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
 )
