@@ -1,0 +1,383 @@
+#!/usr/bin/env python3
+"""Headline benchmark: Parallel Layer Migration training tokens/s on the 27B hybrid.
+
+Config: Qwen3.5-style hybrid teacher, bf16, random init
+(vocab 248077, hidden 5120, 64 blocks, every 4th full attention with 24/4
+heads x 256, GDN 16/48 heads x 128, conv 4, SwiGLU 17408) and sixteen RWKV7
+TimeMix students (head size 64) trained with AdamW; synthetic documents with
+log-uniform lengths in [256, 16384] and uniform token ids; context 4096,
+chunk 1024, micro-batch 1; one process per GPU, each rank on its own data
+shard (weak scaling).
+
+A step is one optimizer update of all sixteen layers on one chunk: one
+teacher forward, sixteen student forward/backward passes, sixteen gradient
+reductions (world > 1) and sixteen clip+AdamW updates.
+
+Timing: W untimed warm-up steps, then K steps bracketed by a barrier and
+device synchronisation, timed with CUDA events; the reported number is the
+total token count over all ranks divided by the slowest rank's time. The
+working set (54 GB of teacher weights per step) exceeds L2, so no flush is
+needed between steps. ``e2e`` repeats K steps through the public step API
+with the per-step host-to-device copy of token ids from pinned memory and the
+device-to-host read of the step's loss metrics inside the timed region.
+
+--impl reference runs the unmodified reference package (installed under
+baseline/_ref) through its own API on the same synthetic data.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+BASELINE_TOKENS_PER_S = None  # the reference publishes no throughput
+
+MODEL_27B = dict(vocab_size=248077, hidden_size=5120, intermediate_size=17408, num_hidden_layers=64,
+                 num_attention_heads=24, num_key_value_heads=4, head_dim=256, linear_num_key_heads=16,
+                 linear_num_value_heads=48, linear_key_head_dim=128, linear_value_head_dim=128,
+                 linear_conv_kernel_dim=4, rms_norm_eps=1e-6, rope_theta=10000000.0, partial_rotary_factor=0.25)
+MODEL_SMALL = dict(vocab_size=4096, hidden_size=1024, intermediate_size=2048, num_hidden_layers=8,
+                   num_attention_heads=8, num_key_value_heads=2, head_dim=128, linear_num_key_heads=4,
+                   linear_num_value_heads=8, linear_key_head_dim=128, linear_value_head_dim=128,
+                   linear_conv_kernel_dim=4, rms_norm_eps=1e-6, rope_theta=10000000.0, partial_rotary_factor=0.25)
+
+
+def layer_types(n):
+    return ["full_attention" if (i + 1) % 4 == 0 else "linear_attention" for i in range(n)]
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=8)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--model", choices=("27b", "small"), default="27b")
+    p.add_argument("--chunk", type=int, default=1024)
+    p.add_argument("--context", type=int, default=4096)
+    p.add_argument("--micro-batch", type=int, default=1)
+    p.add_argument("--no-e2e", action="store_true")
+    return p.parse_args()
+
+
+# ---------------------------------------------------------------------------- environment
+def init_env(args):
+    os.environ.setdefault("RANK", "0")
+    os.environ.setdefault("WORLD_SIZE", str(max(1, args.gpus if "LOCAL_RANK" in os.environ else 1)))
+    os.environ.setdefault("LOCAL_RANK", "0")
+    os.environ.setdefault("LOCAL_WORLD_SIZE", os.environ["WORLD_SIZE"])
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    os.environ.setdefault("MASTER_PORT", str(29500 + os.getpid() % 1000))
+    os.environ.setdefault("TQDM_DISABLE", "1")
+
+
+def write_dataset(root, vocab, tokens_needed, seed):
+    """Synthetic manifest v1: documents with log-uniform lengths in [256, 16384]."""
+    import numpy as np
+    from rwkv_theseus_b200.data import digest_file
+    rng = np.random.default_rng(seed)
+    lengths, total = [], 0
+    while total < tokens_needed:
+        n = int(np.exp(rng.uniform(np.log(256), np.log(16384))))
+        lengths.append(n)
+        total += n
+    root.mkdir(parents=True, exist_ok=True)
+    rng.integers(0, vocab, size=total, dtype=np.uint32).astype("<u4").tofile(root / "tokens.bin")
+    np.save(root / "offsets.npy", np.concatenate([[0], np.cumsum(lengths)]).astype(np.int64))
+    manifest = {"format": 1, "vocab_size": vocab, "sources": [{
+        "tokens": "tokens.bin", "offsets": "offsets.npy", "weight": 1.0,
+        "tokens_sha256": digest_file(root / "tokens.bin"), "offsets_sha256": digest_file(root / "offsets.npy")}]}
+    (root / "manifest.json").write_text(json.dumps(manifest))
+    return root / "manifest.json"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons of this rank's GPU during the timed region."""
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, uuid):
+        self.proc = None
+        self.path = Path(tempfile.mkstemp(suffix=".csv")[1])
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", uuid, f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.path.open("w"), stderr=subprocess.DEVNULL)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for name, flag in zip(self.NAMES, parts[3:7]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------- our implementation
+def build_ours(args, topo, manifest, model_spec):
+    import torch
+    from rwkv_theseus_b200.config import make_config
+    from rwkv_theseus_b200.data import reader_for
+    from rwkv_theseus_b200.models.hf_io import random_model
+    from rwkv_theseus_b200.models.qwen35 import HybridConfig
+    from rwkv_theseus_b200.models.runner import Capture, Runner, migration_order
+    from rwkv_theseus_b200.stage import Student
+    from rwkv_theseus_b200.trainer import StepEngine
+    mcfg = HybridConfig(**model_spec, layer_types=layer_types(model_spec["num_hidden_layers"]))
+    model = random_model(mcfg, topo.device, seed=0)
+    order = migration_order(model, len([t for t in mcfg.layer_types if t == "full_attention"]))
+    cfg = make_config({"train_manifest": str(manifest), "validation_manifest": str(manifest),
+                       "output": str(Path(tempfile.gettempdir()) / "bench_out"), "model": str(ROOT),
+                       "chunk_tokens": args.chunk, "context_tokens": args.context,
+                       "micro_batch_size": args.micro_batch, "training_mode": "epoch", "head_size": 64,
+                       "backend": "cuda", "distributed_backend": "nccl"})
+    runner = Runner(model)
+    students, captures = {}, {}
+    for i, layer in enumerate(order):
+        torch.manual_seed(cfg["seed"] + i)
+        students[layer] = Student(mcfg, layer, cfg, topo, total_steps=10 ** 6)
+        captures[layer] = Capture(model.model.layers[layer].self_attn)
+    engine = StepEngine(cfg, topo, runner, order, students, captures)
+    reader = reader_for(cfg, topo)
+
+    def step(read):
+        before = reader.consumed_tokens
+        reports = engine.step(reader)
+        if read:
+            engine.read_metrics(reports)
+        return reader.consumed_tokens - before
+    return step
+
+
+# ---------------------------------------------------------------------------- reference implementation
+def build_reference(args, topo_unused, manifest, model_spec):
+    sys.path.insert(0, str(ROOT / "baseline" / "_ref"))
+    import torch
+    from transformers import Qwen3_5TextConfig, Qwen3_5ForCausalLM
+    from theseus.config import DEFAULTS
+    from theseus.distributed import Topology
+    from theseus.hf_model import Capture, Runner, migration_order
+    from theseus.losses import statistics, metrics
+    from theseus.stage import prepare_student
+    from theseus.timemix import detach_state
+    from theseus.validation import reader_for
+    spec = dict(model_spec)
+    theta, partial = spec.pop("rope_theta"), spec.pop("partial_rotary_factor")
+    tcfg = Qwen3_5TextConfig(**spec, layer_types=layer_types(spec["num_hidden_layers"]),
+                             rope_parameters={"rope_type": "default", "rope_theta": theta,
+                                              "partial_rotary_factor": partial, "mrope_section": [11, 11, 10]})
+    tcfg._attn_implementation = "sdpa"
+    topo = Topology("nccl", 30)
+    torch.set_default_dtype(torch.bfloat16)
+    with torch.device(topo.device):
+        model = Qwen3_5ForCausalLM(tcfg)
+    torch.set_default_dtype(torch.float32)
+    model.requires_grad_(False).eval()
+    order = migration_order(model, len([t for t in tcfg.layer_types if t == "full_attention"]))
+    cfg = DEFAULTS | {"train_manifest": str(manifest), "validation_manifest": str(manifest), "head_size": 64,
+                      "chunk_tokens": args.chunk, "context_tokens": args.context,
+                      "micro_batch_size": args.micro_batch, "training_mode": "epoch", "backend": "cuda",
+                      "distributed_backend": "nccl"}
+    runner = Runner(model)
+    reader = reader_for(cfg, topo)
+    students, captures = {}, {}
+    for index, layer in enumerate(order):
+        torch.manual_seed(cfg["seed"] + index)
+        students[layer] = prepare_student(model, layer, cfg, topo, None, total_steps=10 ** 6, detached=True)
+        captures[layer] = Capture(model.model.layers[layer].self_attn)
+
+    def step(read):
+        # The body of the reference train.py step loop (train.py:153-211) with grad_accum_steps = 1.
+        accum = {layer: torch.zeros(3, device=topo.device) for layer in order}
+        for _, _, optimizer, _ in students.values():
+            optimizer.zero_grad(set_to_none=True)
+        batch = reader.next()
+        if batch["reset"]:
+            runner.reset()
+            for adapter, *_ in students.values():
+                adapter.state = None
+        runner.forward(batch["ids"].to(topo.device))
+        for layer in order:
+            adapter, ddp, optimizer, scheduler = students[layer]
+            capture = captures[layer]
+            x, target = capture.x, capture.y
+            with torch.autocast(topo.device.type, dtype=torch.bfloat16):
+                prediction, state = ddp(x, adapter.state)
+            adapter.state = detach_state(state)
+            stats = statistics(prediction, target, cfg["loss_epsilon"])
+            accum[layer] += stats.detach()
+            stats[0].backward()
+            del prediction, state, stats, x, target
+            capture.x = capture.y = None
+            topo.student_sum(accum[layer])
+            count = accum[layer][2]
+            if count.item() <= 0:
+                raise RuntimeError("No training tokens in update")
+            for p in adapter.core.parameters():
+                if p.grad is not None:
+                    p.grad.mul_(topo.world / count)
+            norm = torch.nn.utils.clip_grad_norm_(adapter.core.parameters(), cfg["clip_norm"],
+                                                  error_if_nonfinite=True)
+            optimizer.step()
+            scheduler.step()
+            optimizer.zero_grad(set_to_none=True)
+            if read:
+                metrics(accum[layer]) | {"grad_norm": norm.item()}
+        return int(batch["ids"].numel())
+    return step, topo
+
+
+# ---------------------------------------------------------------------------- driver
+def count_launches(step_fn):
+    """Kernels launched by one step, split into this package's kernels and others (profiled, untimed)."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+    mine = ("wkv7_", "gemm_kernel", "rmsnorm_kernel", "conv1d_silu", "gdn_", "mix_kernel", "mix_bwd", "pre_wkv",
+            "post_wkv", "nmse_loss", "adamw_kernel", "scale_norm", "act_kernel", "act_bwd", "norm_rope",
+            "copy_rows", "to_bf16", "report_kernel", "gated_rmsnorm", "flash_attn", "peer_")
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        step_fn(False)
+        torch.cuda.synchronize()
+    ours = other = 0
+    names = {}
+    for evt in prof.events():
+        if evt.device_type != torch.autograd.DeviceType.CUDA:
+            continue
+        if any(key in evt.name for key in mine):
+            ours += 1
+        else:
+            other += 1
+            names[evt.name[:60]] = names.get(evt.name[:60], 0) + 1
+    return ours, other, names
+
+
+def main():
+    args = parse()
+    init_env(args)
+    sys.path.insert(0, str(ROOT))
+    import torch
+    import torch.distributed as dist
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    if args.impl == "reference" and not (ROOT / "baseline" / "_ref" / "theseus").exists():
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "baseline/_ref is not installed"}))
+        return
+    model_spec = MODEL_27B if args.model == "27b" else MODEL_SMALL
+    needed = (args.warmup + 2 * args.steps + 16) * args.chunk * args.micro_batch * 2
+    data_root = Path(tempfile.gettempdir()) / f"theseus_bench_{os.environ.get('MASTER_PORT')}_{rank}"
+    topo = None
+    if args.impl == "ours":
+        from rwkv_theseus_b200.parallel.topology import Topology
+        topo = Topology("nccl", 30)
+        manifest = write_dataset(data_root, model_spec["vocab_size"], needed * world, seed=1234)
+        step = build_ours(args, topo, manifest, model_spec)
+        device = topo.device
+    else:
+        manifest = write_dataset(data_root, model_spec["vocab_size"], needed * world, seed=1234)
+        step, topo = build_reference(args, None, manifest, model_spec)
+        device = topo.device
+
+    def barrier():
+        torch.cuda.synchronize(device)
+        if world > 1:
+            dist.barrier()
+
+    # Start the clock sampler before warm-up: nvidia-smi's start-up briefly stalls CUDA calls.
+    uuid = str(torch.cuda.get_device_properties(device).uuid)
+    uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+    sampler = ClockSampler(uuid)
+    time.sleep(2.0)
+    for _ in range(args.warmup):
+        step(False)
+    barrier()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    start.record()
+    tokens = 0
+    for _ in range(args.steps):
+        tokens += step(False)
+    stop.record()
+    barrier()
+    clocks = sampler.stop()
+    ms = start.elapsed_time(stop)
+    e2e_ms = None
+    e2e_tokens = 0
+    if not args.no_e2e:
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            e2e_tokens += step(True)
+        barrier()
+        e2e_ms = (time.perf_counter() - t0) * 1000
+    stats = torch.tensor([ms, float(tokens), e2e_ms or 0.0, float(e2e_tokens)], device=device, dtype=torch.float64)
+    if world > 1:
+        gathered = [torch.zeros_like(stats) for _ in range(world)]
+        dist.all_gather(gathered, stats)
+    else:
+        gathered = [stats]
+    ms_max = max(g[0].item() for g in gathered)
+    total_tokens = sum(g[1].item() for g in gathered)
+    e2e_max = max(g[2].item() for g in gathered)
+    e2e_total = sum(g[3].item() for g in gathered)
+    ours_launches, other_launches, other_names = count_launches(step) if args.impl == "ours" else (0, 0, {})
+    value = total_tokens / (ms_max / 1000)
+    if rank == 0:
+        line = {
+            "metric": "train tokens/s (27B hybrid parallel layer migration, 16 TimeMix students)",
+            "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": (value / BASELINE_TOKENS_PER_S) if BASELINE_TOKENS_PER_S else None,
+            "dtype": "bf16", "data": "synthetic (log-uniform docs 256..16384, uniform ids; random-init weights)",
+            "config": {"model": f"qwen3.5-hybrid-{args.model} + 16 RWKV7 TimeMix students", "global_batch":
+                       args.micro_batch * world, "seq_len": args.chunk, "context": args.context,
+                       "parallelism": f"dp{world}", "tokens_timed": total_tokens,
+                       "l2": "no flush: 54 GB of teacher weights streamed per step (> L2)"},
+            "clocks": clocks,
+            "e2e": None if args.no_e2e else {
+                "value": e2e_total / (e2e_max / 1000), "unit": "tokens/s",
+                "h2d_bytes_per_step": 8 * args.chunk * args.micro_batch,
+                "d2h_bytes_per_step": 4 * 5 * 16 if args.impl == "ours" else 4 * 3 * 16},
+            "gpu_launches": ours_launches * args.steps,
+            "other_launches_per_step": other_launches,
+        }
+        if args.impl == "reference":
+            line["impl"] = "reference"
+        else:
+            line["other_kernels"] = dict(sorted(other_names.items(), key=lambda kv: -kv[1])[:8])
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+    if topo is not None and hasattr(topo, "close"):
+        try:
+            topo.close()
+        except Exception:
+            pass
+
+
+if __name__ == "__main__":
+    main()
