@@ -1,0 +1,47 @@
+// Allocation-free Gated DeltaNet forward: rt_gdn_forward with its scratch in
+// a file-scope device array. See gdn_noalloc.h for who needs it, the size
+// limit and the sharing rules. This entry point has no counterpart in the
+// reference project.
+#include "gdn_noalloc.h"
+#include "../api.h"
+
+namespace {
+
+// The scratch itself. In host code this name is only a stand-in for the
+// device symbol: its device address comes from cudaGetSymbolAddress below.
+static __device__ __align__(256) float g_gdn_scratch[RT_GDN_NOALLOC_MAX_FLOATS];
+
+constexpr int kMaxDevices = 64;
+float* g_scratch_ptr[kMaxDevices] = {nullptr};
+
+// Resolves (once per device, with that device current) the scratch's device address.
+cudaError_t scratch_for_current_device(float** out) {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  if (!g_scratch_ptr[dev]) {
+    void* ptr = nullptr;
+    err = cudaGetSymbolAddress(&ptr, g_gdn_scratch);
+    if (err != cudaSuccess) return err;
+    g_scratch_ptr[dev] = static_cast<float*>(ptr);
+  }
+  *out = g_scratch_ptr[dev];
+  return cudaSuccess;
+}
+
+}  // namespace
+
+extern "C" long rt_gdn_noalloc_capacity_floats() { return RT_GDN_NOALLOC_MAX_FLOATS; }
+
+extern "C" cudaError_t rt_gdn_forward_noalloc(const void* qkv, long row_stride, const void* a, const void* b,
+                                              long ab_stride, const float* A_log, const float* dt_bias,
+                                              float* state, void* out, int B, int T, int Hk, int Hv, int D,
+                                              cudaStream_t stream) {
+  if (B <= 0 || T <= 0 || Hk <= 0 || Hv <= 0 || D <= 0) return cudaErrorInvalidValue;
+  if (rt_gdn_workspace_floats(B, T, Hk, D) > RT_GDN_NOALLOC_MAX_FLOATS) return cudaErrorInvalidValue;
+  float* work = nullptr;
+  cudaError_t err = scratch_for_current_device(&work);
+  if (err != cudaSuccess) return err;
+  return rt_gdn_forward(qkv, row_stride, a, b, ab_stride, A_log, dt_bias, state, out, work, B, T, Hk, Hv, D, stream);
+}
