@@ -61,6 +61,7 @@ def parse():
     p.add_argument("--context", type=int, default=4096)
     p.add_argument("--micro-batch", type=int, default=1)
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--profile", action="store_true", help="print a per-kernel breakdown of one step and exit")
     return p.parse_args()
 
 
@@ -276,6 +277,37 @@ def count_launches(step_fn):
     return ours, other, names
 
 
+def print_breakdown(step_fn, rank):
+    """Per-kernel device time of one step, grouped by kernel name (profiled; not a benchmark number)."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        step_fn(False)
+        torch.cuda.synchronize()
+    groups = {}
+    total = 0.0
+    for evt in prof.events():
+        if evt.device_type != torch.autograd.DeviceType.CUDA:
+            continue
+        name = evt.name
+        for key in ("gemm_kernel<256", "gemm_kernel<128", "gemm_kernel<64", "wkv7_forward", "wkv7_backward",
+                    "gdn_chunk", "gdn_prep", "fmha", "sdpa", "flash", "efficient_attention", "adamw", "scale_norm",
+                    "rmsnorm", "conv1d", "post_wkv_bwd", "pre_wkv_bwd", "post_wkv", "pre_wkv", "mix_bwd",
+                    "mix_kernel", "nmse", "gated_rmsnorm", "norm_rope", "elementwise", "Memcpy", "Memset"):
+            if key in name:
+                name = key
+                break
+        dur = evt.device_time_total if hasattr(evt, "device_time_total") else evt.cuda_time_total
+        groups[name] = groups.get(name, [0.0, 0])
+        groups[name][0] += dur
+        groups[name][1] += 1
+        total += dur
+    if rank == 0:
+        for name, (us, n) in sorted(groups.items(), key=lambda kv: -kv[1][0])[:30]:
+            print(f"{us / 1000:9.3f} ms {100 * us / total:5.1f}% {n:6d}  {name[:90]}")
+        print(f"{total / 1000:9.3f} ms total kernel time")
+
+
 def main():
     args = parse()
     init_env(args)
@@ -307,6 +339,12 @@ def main():
         if world > 1:
             dist.barrier()
 
+    if args.profile:
+        for _ in range(args.warmup):
+            step(False)
+        barrier()
+        print_breakdown(step, rank)
+        return
     # Start the clock sampler before warm-up: nvidia-smi's start-up briefly stalls CUDA calls.
     uuid = str(torch.cuda.get_device_properties(device).uuid)
     uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid

@@ -12,10 +12,11 @@ int rt_wkv7_chunk_len();
 cudaError_t rt_wkv7_forward(int dtype, int B, int T, int H, int N, const void* r, const void* w, const void* k,
                             const void* v, const void* a, const void* b, const float* s0, void* y, float* s_end,
                             float* checkpoints, cudaStream_t stream);
+long rt_wkv7_backward_workspace_floats(int B, int T, int H, int N);
 cudaError_t rt_wkv7_backward(int dtype, int B, int T, int H, int N, const void* r, const void* w, const void* k,
                              const void* v, const void* a, const void* b, const float* checkpoints, const void* dy,
                              const float* dend, float* dr, float* dw, float* dk, float* dv, float* da, float* db,
-                             float* ds0, cudaStream_t stream);
+                             float* ds0, float* work, cudaStream_t stream);
 
 // GEMM: C = epi(A . B^T). a_mn / b_mn select MN-major operands (see gemm.cu).
 // epi: 0 bf16 store, 1 fp32 store, 2 fp32 accumulate (C += alpha * A.B^T).

@@ -68,11 +68,12 @@ std::vector<at::Tensor> wkv7_backward(at::Tensor r, at::Tensor w, at::Tensor k, 
   std::vector<at::Tensor> g;
   for (int i = 0; i < 6; ++i) g.push_back(at::empty(r.sizes(), opts));
   g.push_back(at::empty({B, H, N, N}, opts));
+  auto work = at::empty({rt_wkv7_backward_workspace_floats(B, T, H, N)}, opts);
   check_cuda(rt_wkv7_backward(dtype_code(r), B, T, H, N, r.data_ptr(), w.data_ptr(), k.data_ptr(), v.data_ptr(),
                               a.data_ptr(), b.data_ptr(), ckpt.data_ptr<float>(), dy.data_ptr(),
                               dend.data_ptr<float>(), g[0].data_ptr<float>(), g[1].data_ptr<float>(),
                               g[2].data_ptr<float>(), g[3].data_ptr<float>(), g[4].data_ptr<float>(),
-                              g[5].data_ptr<float>(), g[6].data_ptr<float>(), stream_of(r)),
+                              g[5].data_ptr<float>(), g[6].data_ptr<float>(), work.data_ptr<float>(), stream_of(r)),
              "wkv7_backward");
   return g;
 }

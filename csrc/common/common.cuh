@@ -44,6 +44,16 @@ RT_DEVICE float block_sum(float v, float* scratch) {
   return v;
 }
 
+// Asynchronous 16-byte global->shared copy (zero-filled when !pred; gmem must still be a valid address).
+RT_DEVICE void cp_async16(void* smem, const void* gmem, bool pred) {
+  const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+  const int n = pred ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(s), "l"(gmem), "r"(n) : "memory");
+}
+RT_DEVICE void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+RT_DEVICE void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 }  // namespace rt
 
 // Host-side status helpers.

@@ -89,7 +89,43 @@ gdn_prep_kernel(const bf16* __restrict__ qkv, long row_stride, int T, int Hk, fl
 }
 
 // ---------------------------------------------------------------- recurrent chunk kernel
-// grid (D/R, Hv, B). Value columns [col0, col0+R) of value head h.
+// grid (D/R, Hv, B). Value columns [col0, col0+R) of value head h. The next chunk's q, k, Gram matrices
+// and v columns are copied asynchronously (cp.async, double buffered) while the current chunk computes;
+// the per-step gates of the next chunk are prefetched into registers.
+template <int D>
+struct GdnSmem {
+  static constexpr int SP = D + 4;
+  static constexpr int STAGE = 2 * L * SP + 2 * L * L + L * R / 2;  // q, k, gram (fp32) + v (bf16) in floats
+  static constexpr int FLOATS = 2 * STAGE + D * (R + 1) + 4 * L * R + 4 * L * (L + 1) + 6 * L;
+};
+
+template <int D>
+RT_DEVICE void gdn_issue(float* stage, const float* qn, const float* kn, const float* gram, const bf16* qkv,
+                         long row_stride, long vbase, int b, int T, int Hk, int kh, int ch, int chunks) {
+  using G = GdnSmem<D>;
+  float* sq = stage;
+  float* sk = sq + L * G::SP;
+  float* sg = sk + L * G::SP;
+  bf16* sv = reinterpret_cast<bf16*>(sg + 2 * L * L);
+  constexpr int QV = D / 4;
+  for (int e = threadIdx.x; e < 2 * L * QV; e += THREADS) {
+    const int which = e / (L * QV), rem = e % (L * QV), tt = rem / QV, c = (rem % QV) * 4, t = ch * L + tt;
+    const bool ok = t < T;
+    const float* base = which ? kn : qn;
+    const float* src = base + (ok ? (((long)b * T + t) * Hk + kh) * D + c : 0);
+    rt::cp_async16((which ? sk : sq) + tt * G::SP + c, src, ok);
+  }
+  const float* gsrc = gram + (((long)b * Hk + kh) * chunks + ch) * 2 * L * L;
+  for (int e = threadIdx.x; e < 2 * L * L / 4; e += THREADS) rt::cp_async16(sg + 4 * e, gsrc + 4 * e, true);
+  for (int e = threadIdx.x; e < L * (R / 8); e += THREADS) {
+    const int tt = e / (R / 8), i = (e % (R / 8)) * 8, t = ch * L + tt;
+    const bool ok = t < T;
+    const bf16* src = qkv + (ok ? ((long)b * T + t) * row_stride + vbase + i : 0);
+    rt::cp_async16(sv + tt * R + i, src, ok);
+  }
+  rt::cp_async_commit();
+}
+
 template <int D>
 __global__ void __launch_bounds__(THREADS)
 gdn_chunk_kernel(const float* __restrict__ qn, const float* __restrict__ kn, const float* __restrict__ gram,
@@ -97,11 +133,11 @@ gdn_chunk_kernel(const float* __restrict__ qn, const float* __restrict__ kn, con
                  const bf16* __restrict__ pb, long ab_stride, const float* __restrict__ A_log,
                  const float* __restrict__ dt_bias, float* __restrict__ state, bf16* __restrict__ out, int T, int Hk,
                  int Hv) {
-  constexpr int SP = D + 4;
+  using G = GdnSmem<D>;
+  constexpr int SP = G::SP;
   extern __shared__ __align__(16) float sm[];
-  float* sq = sm;                 // [L][SP] normalised, scaled q
-  float* sk = sq + L * SP;        // [L][SP] normalised k
-  float* S = sk + L * SP;         // [D][R+1] state block (key j, value column i)
+  float* stage[2] = {sm, sm + G::STAGE};
+  float* S = sm + 2 * G::STAGE;   // [D][R+1] state block (key j, value column i)
   float* V = S + D * (R + 1);     // [L][R]  beta * v
   float* Z = V + L * R;           // [L][R]
   float* U = Z + L * R;           // [L][R]
@@ -122,38 +158,50 @@ gdn_chunk_kernel(const float* __restrict__ qn, const float* __restrict__ kn, con
   const int chunks = (T + L - 1) / L;
   const long vbase = 2L * Hk * D + (long)h * D + col0;  // v column offset inside a qkv row
   float* st = state + ((long)b * Hv + h) * D * D;       // [D key][D value]
+  gdn_issue<D>(stage[0], qn, kn, gram, qkv, row_stride, vbase, b, T, Hk, kh, 0, chunks);
   for (int e = threadIdx.x; e < D * R; e += THREADS) {
     const int j = e / R, i = e % R;
     S[j * (R + 1) + i] = st[(long)j * D + col0 + i];
   }
   const float neg_a = -expf(A_log[h]);
   const float dtb = dt_bias[h];
+  // Gate inputs of the current chunk held in registers by threads < L.
+  float ga = 0.f, gb = 0.f;
+  if (threadIdx.x < L && threadIdx.x < T) {
+    ga = rt::to_f(pa[((long)b * T + threadIdx.x) * ab_stride + h]);
+    gb = rt::to_f(pb[((long)b * T + threadIdx.x) * ab_stride + h]);
+  }
   for (int ch = 0; ch < chunks; ++ch) {
     const int t0 = ch * L;
-    __syncthreads();
-    for (int e = threadIdx.x; e < L * D; e += THREADS) {
-      const int tt = e / D, c = e % D, t = t0 + tt;
-      const bool ok = t < T;
-      sq[tt * SP + c] = ok ? qn[(((long)b * T + t) * Hk + kh) * D + c] : 0.f;
-      sk[tt * SP + c] = ok ? kn[(((long)b * T + t) * Hk + kh) * D + c] : 0.f;
+    if (ch + 1 < chunks) {
+      gdn_issue<D>(stage[(ch + 1) & 1], qn, kn, gram, qkv, row_stride, vbase, b, T, Hk, kh, ch + 1, chunks);
+      rt::cp_async_wait<1>();
+    } else {
+      rt::cp_async_wait<0>();
     }
+    float na = 0.f, nb = 0.f;  // next chunk's gates (prefetched into registers)
     if (threadIdx.x < L) {
+      const int tn = t0 + L + threadIdx.x;
+      if (tn < T) {
+        na = rt::to_f(pa[((long)b * T + tn) * ab_stride + h]);
+        nb = rt::to_f(pb[((long)b * T + tn) * ab_stride + h]);
+      }
       const int tt = threadIdx.x, t = t0 + tt;
       float g = 0.f, bt = 0.f;
       if (t < T) {
-        const float av = rt::to_f(pa[((long)b * T + t) * ab_stride + h]) + dtb;
+        const float av = ga + dtb;
         const float sp = av > 20.f ? av : log1pf(expf(av));
         g = neg_a * sp;
-        bt = __bfloat162float(__float2bfloat16_rn(rt::sigmoidf_(rt::to_f(pb[((long)b * T + t) * ab_stride + h]))));
+        bt = __bfloat162float(__float2bfloat16_rn(rt::sigmoidf_(gb)));
       }
       lam[tt] = g;
       beta[tt] = bt;
     }
-    for (int e = threadIdx.x; e < L * R; e += THREADS) {
-      const int tt = e / R, i = e % R, t = t0 + tt;
-      V[e] = t < T ? rt::to_f(qkv[((long)b * T + t) * row_stride + vbase + i]) : 0.f;
-    }
     __syncthreads();
+    const float* sq = stage[ch & 1];
+    const float* sk = sq + L * SP;
+    const float* gr = sk + L * SP;
+    const bf16* sv = reinterpret_cast<const bf16*>(gr + 2 * L * L);
     if (threadIdx.x == 0) {
       float run = 0.f;
       for (int tt = 0; tt < L; ++tt) { run += lam[tt]; lam[tt] = run; }
@@ -167,9 +215,8 @@ gdn_chunk_kernel(const float* __restrict__ qn, const float* __restrict__ kn, con
       c_u[tt] = -beta[tt] * expf(lL - prev);
       c_v[tt] = expf(lL - lam[tt]);
     }
-    for (int e = threadIdx.x; e < L * R; e += THREADS) V[e] *= beta[e / R];
+    for (int e = threadIdx.x; e < L * R; e += THREADS) V[e] = rt::to_f(sv[e]) * beta[e / R];
     // Chunk matrices from the Gram matrices (all exponents <= 0).
-    const float* gr = gram + (((long)b * Hk + kh) * chunks + ch) * 2 * L * L;
     for (int e = threadIdx.x; e < L * L; e += THREADS) {
       const int t = e / L, s = e % L;
       const float kk = gr[e], qk = gr[L * L + e];
@@ -186,9 +233,9 @@ gdn_chunk_kernel(const float* __restrict__ qn, const float* __restrict__ kn, con
       float zk = 0.f, yq = 0.f;
 #pragma unroll 8
       for (int j = 0; j < D; ++j) {
-        const float sv = S[j * (R + 1) + i];
-        zk += sk[t * SP + j] * sv;
-        yq += sq[t * SP + j] * sv;
+        const float sv2 = S[j * (R + 1) + i];
+        zk += sk[t * SP + j] * sv2;
+        yq += sq[t * SP + j] * sv2;
       }
       float z = zk * e_prev[t], y = yq * e_cur[t];
       for (int s = 0; s < t; ++s) z += Mak[t * (L + 1) + s] * V[s * R + i];
@@ -223,8 +270,10 @@ gdn_chunk_kernel(const float* __restrict__ qn, const float* __restrict__ kn, con
       for (int s = 0; s < L; ++s) acc += sk[s * SP + j] * (U[s * R + i] * c_u[s] + V[s * R + i] * c_v[s]);
       S[j * (R + 1) + i] = acc;
     }
+    ga = na;
+    gb = nb;
+    __syncthreads();
   }
-  __syncthreads();
   for (int e = threadIdx.x; e < D * R; e += THREADS) {
     const int j = e / R, i = e % R;
     st[(long)j * D + col0 + i] = S[j * (R + 1) + i];
@@ -241,7 +290,7 @@ cudaError_t launch(const void* qkv, long row_stride, const void* a, const void* 
   float* gram = kn + (long)B * T * Hk * D;
   gdn_prep_kernel<D><<<dim3(chunks, Hk, B), THREADS, 0, stream>>>((const bf16*)qkv, row_stride, T, Hk, qn, kn, gram);
   RT_CUDA_CHECK(cudaGetLastError());
-  const size_t smem = (2 * L * (D + 4) + D * (R + 1) + 4 * L * R + 4 * L * (L + 1) + 6 * L) * sizeof(float);
+  const size_t smem = GdnSmem<D>::FLOATS * sizeof(float);
   RT_CUDA_CHECK(cudaFuncSetAttribute(gdn_chunk_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   gdn_chunk_kernel<D><<<dim3(D / R, Hv, B), THREADS, smem, stream>>>(
       qn, kn, gram, (const bf16*)qkv, row_stride, (const bf16*)a, (const bf16*)b, ab_stride, A_log, dt_bias, state,

@@ -340,20 +340,17 @@ cudaError_t launch(const void* A, long lda, const void* B0, const void* B1, long
   return cudaGetLastError();
 }
 
-// Tile width: the smallest number of "waves x tile width" over the SMs.
+// Tile width: the widest tile (least L2 traffic per FLOP, most work per pipeline stage) whose tile count
+// still covers three quarters of the SMs; otherwise the narrowest (most tiles).
 int pick_bn(int M, int N, bool swiglu) {
   if (swiglu) return 128;
   const int sms = num_sms_cached();
-  const int tm = (M + BM - 1) / BM;
-  int best = 256;
-  long best_cost = -1;
-  for (int bn : {256, 128, 64}) {
-    const long tiles = (long)tm * ((N + bn - 1) / bn);
-    const long waves = (tiles + sms - 1) / sms;
-    const long cost = waves * bn + (bn == 64 ? 16 : 0);
-    if (best_cost < 0 || cost < best_cost) { best_cost = cost; best = bn; }
+  const long tm = (M + BM - 1) / BM;
+  for (int bn : {256, 128}) {
+    if (N < bn / 2) continue;
+    if (tm * ((N + bn - 1) / bn) * 4 >= 3L * sms) return bn;
   }
-  return best;
+  return 64;
 }
 
 template <bool A_MN, bool B_MN, int EPI>

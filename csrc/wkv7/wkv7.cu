@@ -6,7 +6,8 @@
 //   y_t = S_t r_t,
 // with an explicit initial state s0 and final state output.
 //
-// Algorithm (own design): the sequence is cut into chunks of L = 16 steps.
+// Algorithm (own design; this file holds the forward, wkv7_bwd.cu the backward):
+// the sequence is cut into chunks of L = 16 steps.
 // With Lambda_t the cumulative log decay inside a chunk and
 //   a~_t = a_t e^{Lambda_{t-1}}, r~_t = r_t e^{Lambda_t}, b~_s = b_s e^{-Lambda_s}, k~_s = k_s e^{-Lambda_s},
 // the per-chunk update of every value row is
@@ -15,18 +16,14 @@
 //   S_L = S0 diag(D_L) + U^T (B~ D_L) + V^T (K~ D_L)
 // where Mxy[t][s] = x~_t . y~_s (strictly lower for a-rows, inclusive for
 // r-rows). Value rows are independent, so each CTA owns R = 16 rows of one
-// head and the head's rows are spread over NSPLIT CTAs. The forward pass keeps
-// S in shared memory and stores only chunk-start states ("checkpoints") when
-// a backward is needed. The backward walks chunks in reverse, recomputes U
-// from the checkpoint, propagates dS row-locally and forms the key-side
-// gradients (dr, dw, dk, da, db), which sum over all value rows: the NSPLIT
-// CTAs of a head form a thread-block cluster and add their partial sums
-// through distributed shared memory in a fixed order (deterministic, no
-// atomics). Padded tail steps use zero inputs and zero log-decay.
-#include <cooperative_groups.h>
+// head and the head's rows are spread over N/16 CTAs. The forward pass keeps
+// S in shared memory, prefetches the next chunk's inputs with cp.async while
+// the current chunk computes, and stores only chunk-start states
+// ("checkpoints") when a backward is needed. Padded tail steps use zero
+// inputs and zero log-decay.
+#include <initializer_list>
 #include "../common/common.cuh"
 
-namespace cg = cooperative_groups;
 
 namespace {
 
@@ -46,11 +43,57 @@ struct Smem {
   static constexpr int PART = 4 * MAT + 4 * KEY + NP;
 };
 
-template <typename T>
-RT_DEVICE float load_or_zero(const T* p, bool ok) { return ok ? rt::to_f<T>(*p) : 0.f; }
+// Raw (input dtype) staging of one chunk: r, w, k, a, b [L][NP], v and dy [L][R] (dy in backward),
+// filled by 16-byte cp.async copies (zero-filled outside the sequence / head) one chunk ahead.
+template <typename T, int NP>
+struct Raw {
+  static constexpr int VEC = 16 / sizeof(T);
+  static constexpr int KEYV = L * NP;
+  static constexpr int ELEMS = 5 * KEYV + 2 * L * R;
+  static constexpr int FLOATS = (ELEMS * (int)sizeof(T) + 15) / 16 * 4;  // size in floats, 16-byte multiple
+};
 
-// Shared per-chunk preparation: load r,w,k,a,b (key side) and v (my rows),
-// cumulative log decay, decayed vectors, D_L and the four chunk matrices.
+// Issues the copies of chunk t0 into `raw` (one commit group per call).
+template <typename T, int NP, bool ASYNC>
+RT_DEVICE void issue_chunk(T* raw, const T* pr, const T* pw, const T* pk, const T* pa, const T* pb, const T* pv,
+                           const T* pdy, int T_, int H, int N, int batch, int head, int t0, int row0) {
+  using RW = Raw<T, NP>;
+  constexpr int VEC = RW::VEC, QV = NP / VEC;
+  for (int e = threadIdx.x; e < 5 * L * QV; e += THREADS) {
+    const int tensor = e / (L * QV), rem = e % (L * QV), tt = rem / QV, j = (rem % QV) * VEC;
+    const int t = t0 + tt;
+    const bool ok = (t < T_) && (j < N);
+    const T* base = tensor == 0 ? pr : tensor == 1 ? pw : tensor == 2 ? pk : tensor == 3 ? pa : pb;
+    const T* src = base + (ok ? ((long)(batch * T_ + t) * H + head) * N + j : 0);
+    T* dst = raw + tensor * RW::KEYV + tt * NP + j;
+    if (ASYNC) {
+      rt::cp_async16(dst, src, ok);
+    } else {
+#pragma unroll
+      for (int u = 0; u < VEC; ++u) dst[u] = (ok && j + u < N) ? src[u] : rt::from_f<T>(0.f);
+    }
+  }
+  constexpr int RV = R / VEC;
+  const int rows_arrays = pdy ? 2 : 1;
+  for (int e = threadIdx.x; e < rows_arrays * L * RV; e += THREADS) {
+    const int which = e / (L * RV), rem = e % (L * RV), tt = rem / RV, i = (rem % RV) * VEC;
+    const int t = t0 + tt, row = row0 + i;
+    const bool ok = (t < T_) && (row < N);
+    const T* base = which ? pdy : pv;
+    const T* src = base + (ok ? ((long)(batch * T_ + t) * H + head) * N + row : 0);
+    T* dst = raw + 5 * RW::KEYV + which * L * R + tt * R + i;
+    if (ASYNC) {
+      rt::cp_async16(dst, src, ok);
+    } else {
+#pragma unroll
+      for (int u = 0; u < VEC; ++u) dst[u] = (ok && row + u < N) ? src[u] : rt::from_f<T>(0.f);
+    }
+  }
+  if (ASYNC) rt::cp_async_commit();
+}
+
+// Per-chunk preparation from the raw staging: cumulative log decay, decayed vectors, D_L and the four
+// chunk matrices (fp32 in shared memory).
 template <typename T, int NP>
 struct Chunk {
   using S = Smem<NP>;
@@ -62,26 +105,25 @@ struct Chunk {
   }
   static constexpr int FLOATS = 6 * S::KEY + NP + S::ROWS + 4 * S::MAT;
 
-  RT_DEVICE void load(const T* pr, const T* pw, const T* pk, const T* pv, const T* pa, const T* pb,
-                      int T_, int H, int N, int batch, int head, int t0, int row0) {
+  // dy_out (optional): receives the chunk's output gradient rows as fp32 [L][R].
+  RT_DEVICE void prepare(const T* raw, int T_, int N, int t0, float* dy_out) {
+    using RW = Raw<T, NP>;
     const int tid = threadIdx.x;
     for (int e = tid; e < L * NP; e += THREADS) {
-      const int tt = e / NP, j = e % NP, t = t0 + tt;
-      const bool ok = (t < T_) && (j < N);
-      const long idx = ((long)(batch * T_ + t) * H + head) * N + j;
+      const int tt = e / NP, j = e % NP;
+      const bool ok = (t0 + tt < T_) && (j < N);
       const int o = tt * S::SP + j;
-      r[o] = load_or_zero(pr + idx, ok);
-      k[o] = load_or_zero(pk + idx, ok);
-      a[o] = load_or_zero(pa + idx, ok);
-      b[o] = load_or_zero(pb + idx, ok);
-      const float sg = ok ? rt::sigmoidf_(rt::to_f<T>(pw[idx])) : 0.f;
+      r[o] = rt::to_f<T>(raw[0 * RW::KEYV + e]);
+      k[o] = rt::to_f<T>(raw[2 * RW::KEYV + e]);
+      a[o] = rt::to_f<T>(raw[3 * RW::KEYV + e]);
+      b[o] = rt::to_f<T>(raw[4 * RW::KEYV + e]);
+      const float sg = ok ? rt::sigmoidf_(rt::to_f<T>(raw[1 * RW::KEYV + e])) : 0.f;
       sig[o] = sg;
       lam[o] = -DECAY_SCALE * sg;
     }
     for (int e = tid; e < L * R; e += THREADS) {
-      const int tt = e / R, i = e % R, t = t0 + tt, row = row0 + i;
-      const bool ok = (t < T_) && (row < N);
-      v[e] = load_or_zero(pv + ((long)(batch * T_ + t) * H + head) * N + row, ok);
+      v[e] = rt::to_f<T>(raw[5 * RW::KEYV + e]);
+      if (dy_out) dy_out[e] = rt::to_f<T>(raw[5 * RW::KEYV + L * R + e]);
     }
     __syncthreads();
     if (tid < NP) {
@@ -143,6 +185,24 @@ struct Chunk {
   RT_DEVICE float m(int which, int t, int s) const { return M[which * S::MAT + t * (L + 1) + s]; }
 };
 
+// Issues the copy of the fp32 chunk-start state rows [R][NP] of this CTA (backward).
+template <int NP, bool ASYNC>
+RT_DEVICE void issue_state(float* dst, const float* src_state, int N, int row0) {
+  constexpr int QV = NP / 4;
+  for (int e = threadIdx.x; e < R * QV; e += THREADS) {
+    const int i = e / QV, j = (e % QV) * 4, row = row0 + i;
+    const bool ok = row < N && j < N;
+    const float* src = src_state + (ok ? (long)row * N + j : 0);
+    if (ASYNC) {
+      rt::cp_async16(dst + i * NP + j, src, ok);
+    } else {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) dst[i * NP + j + u] = (ok && j + u < N) ? src[u] : 0.f;
+    }
+  }
+  if (ASYNC) rt::cp_async_commit();
+}
+
 // Z[t][i] = a~_t . S0_i + sum_{s<t} Mak[t][s] v[s][i]; Yp = r~_t . S0_i + sum_{s<=t} Mrk[t][s] v[s][i];
 // then U by forward substitution. Leaves Z, U (and Yp if requested) in shared memory.
 template <typename T, int NP>
@@ -177,23 +237,27 @@ RT_DEVICE void solve_u(const Chunk<T, NP>& c, const float* S0, float* Z, float* 
   __syncthreads();
 }
 
-template <typename T, int NP>
+template <typename T, int NP, bool ASYNC>
 __global__ void __launch_bounds__(THREADS)
 wkv7_forward_kernel(int T_, int H, int N, const T* __restrict__ pr, const T* __restrict__ pw,
                     const T* __restrict__ pk, const T* __restrict__ pv, const T* __restrict__ pa,
                     const T* __restrict__ pb, const float* __restrict__ s0, T* __restrict__ py,
                     float* __restrict__ s_end, float* __restrict__ checkpoints) {
   using S = Smem<NP>;
+  using RW = Raw<T, NP>;
   extern __shared__ __align__(16) float smem[];
+  constexpr int ST = ASYNC ? 2 : 1;
+  T* raw[2] = {reinterpret_cast<T*>(smem), reinterpret_cast<T*>(smem + (ST - 1) * RW::FLOATS)};
   Chunk<T, NP> c;
-  c.bind(smem);
-  float* St = smem + Chunk<T, NP>::FLOATS;
+  c.bind(smem + ST * RW::FLOATS);
+  float* St = smem + ST * RW::FLOATS + Chunk<T, NP>::FLOATS;
   float* Z = St + S::STATE;
   float* U = Z + S::ROWS;
   float* Y = U + S::ROWS;
   const int rb = blockIdx.x, bh = blockIdx.y, batch = bh / H, head = bh % H, row0 = rb * R;
   const int chunks = (T_ + L - 1) / L;
   const long NN = (long)N * N;
+  if (ASYNC) issue_chunk<T, NP, ASYNC>(raw[0], pr, pw, pk, pa, pb, pv, nullptr, T_, H, N, batch, head, 0, row0);
   for (int e = threadIdx.x; e < R * NP; e += THREADS) {
     const int i = e / NP, j = e % NP, row = row0 + i;
     St[i * S::SP + j] = (row < N && j < N) ? s0[bh * NN + (long)row * N + j] : 0.f;
@@ -207,7 +271,19 @@ wkv7_forward_kernel(int T_, int H, int N, const T* __restrict__ pr, const T* __r
         if (row < N && j < N) dst[(long)row * N + j] = St[i * S::SP + j];
       }
     }
-    c.load(pr, pw, pk, pv, pa, pb, T_, H, N, batch, head, t0, row0);
+    if constexpr (ASYNC) {
+      if (ch + 1 < chunks) {
+        issue_chunk<T, NP, ASYNC>(raw[(ch + 1) & 1], pr, pw, pk, pa, pb, pv, nullptr, T_, H, N, batch, head,
+                                  t0 + L, row0);
+        rt::cp_async_wait<1>();
+      } else {
+        rt::cp_async_wait<0>();
+      }
+    } else {
+      issue_chunk<T, NP, ASYNC>(raw[0], pr, pw, pk, pa, pb, pv, nullptr, T_, H, N, batch, head, t0, row0);
+    }
+    __syncthreads();
+    c.prepare(raw[ASYNC ? (ch & 1) : 0], T_, N, t0, nullptr);
     solve_u<T, NP>(c, St, Z, U, Y);
     for (int e = threadIdx.x; e < L * R; e += THREADS) {
       const int t = e / R, i = e % R;
@@ -237,265 +313,26 @@ wkv7_forward_kernel(int T_, int H, int N, const T* __restrict__ pr, const T* __r
   }
 }
 
-template <typename T, int NP>
-struct BwdLayout {
-  using S = Smem<NP>;
-  static constexpr int ROW_ARRAYS = 6;  // Z, U, dY, dU, dZ, dLam-work
-  static constexpr int FLOATS = Chunk<T, NP>::FLOATS + 2 * S::STATE + ROW_ARRAYS * S::ROWS +
-                                4 * S::MAT + S::KEY + 2 * S::PART;
-};
-
-template <typename T, int NP, int NSPLIT>
-__global__ void __launch_bounds__(THREADS)
-wkv7_backward_kernel(int T_, int H, int N, const T* __restrict__ pr, const T* __restrict__ pw,
-                     const T* __restrict__ pk, const T* __restrict__ pv, const T* __restrict__ pa,
-                     const T* __restrict__ pb, const float* __restrict__ checkpoints,
-                     const T* __restrict__ pdy, const float* __restrict__ dend,
-                     float* __restrict__ dr, float* __restrict__ dw, float* __restrict__ dk,
-                     float* __restrict__ dv, float* __restrict__ da, float* __restrict__ db,
-                     float* __restrict__ ds0) {
-  using S = Smem<NP>;
-  constexpr int JQ = NP / NSPLIT;  // key columns whose gradients this CTA finalises
-  extern __shared__ __align__(16) float smem[];
-  Chunk<T, NP> c;
-  c.bind(smem);
-  float* S0 = smem + Chunk<T, NP>::FLOATS;
-  float* dS = S0 + S::STATE;
-  float* Z = dS + S::STATE;
-  float* U = Z + S::ROWS;
-  float* dY = U + S::ROWS;
-  float* dU = dY + S::ROWS;
-  float* dZ = dU + S::ROWS;
-  float* dM = dZ + 2 * S::ROWS;           // reduced dM (4 matrices)
-  float* dLam = dM + 4 * S::MAT;          // [L][SP] work for the column chain
-  float* part0 = dLam + S::KEY;           // two partial-sum buffers (double buffered)
-
-  cg::cluster_group cluster = cg::this_cluster();
-  const int rb = (NSPLIT > 1) ? (int)cluster.block_rank() : 0;
-  const int bh = blockIdx.y, batch = bh / H, head = bh % H, row0 = rb * R;
-  const int chunks = (T_ + L - 1) / L;
-  const long NN = (long)N * N;
-  for (int e = threadIdx.x; e < R * NP; e += THREADS) {
-    const int i = e / NP, j = e % NP, row = row0 + i;
-    dS[i * S::SP + j] = (row < N && j < N) ? dend[bh * NN + (long)row * N + j] : 0.f;
-  }
-  for (int ch = chunks - 1; ch >= 0; --ch) {
-    const int t0 = ch * L;
-    float* P = part0 + (ch & 1) * S::PART;
-    float* PdM = P;                       // 4 * MAT
-    float* PdR = P + 4 * S::MAT;          // [L][SP] dR~ direct
-    float* PdA = PdR + S::KEY;            // [L][SP] dA~ direct
-    float* PdB = PdA + S::KEY;            // [L][SP] dB^
-    float* PdK = PdB + S::KEY;            // [L][SP] dK^
-    float* PdD = PdK + S::KEY;            // [NP]    dD_L
-    const float* src = checkpoints + ((long)bh * (chunks + 1) + ch) * NN;
-    for (int e = threadIdx.x; e < R * NP; e += THREADS) {
-      const int i = e / NP, j = e % NP, row = row0 + i;
-      S0[i * S::SP + j] = (row < N && j < N) ? src[(long)row * N + j] : 0.f;
-    }
-    for (int e = threadIdx.x; e < L * R; e += THREADS) {
-      const int tt = e / R, i = e % R, t = t0 + tt, row = row0 + i;
-      dY[e] = load_or_zero(pdy + ((long)(batch * T_ + t) * H + head) * N + row, t < T_ && row < N);
-    }
-    c.load(pr, pw, pk, pv, pa, pb, T_, H, N, batch, head, t0, row0);
-    solve_u<T, NP>(c, S0, Z, U, nullptr);
-    // dU[s][i] = sum_{t>=s} Mrb[t][s] dY[t][i] + sum_j b~[s][j] D_L[j] dS[i][j];
-    // the K-side analogue (for dV) is computed in the same pass.
-    float* dVk = Z;  // Z is no longer needed: reuse it for the k^-part of dV
-    for (int e = threadIdx.x; e < L * R; e += THREADS) {
-      const int s = e / R, i = e % R;
-      float u = 0.f, w = 0.f;
-      const float* bs = c.b + s * S::SP;
-      const float* ks = c.k + s * S::SP;
-      const float* di = dS + i * S::SP;
-#pragma unroll 4
-      for (int j = 0; j < NP; ++j) {
-        const float g = di[j] * c.dl[j];
-        u += bs[j] * g;
-        w += ks[j] * g;
-      }
-      for (int t = s; t < L; ++t) u += c.m(2, t, s) * dY[t * R + i];
-      dU[e] = u;
-      dVk[e] = w;
-    }
-    __syncthreads();
-    if (threadIdx.x < R) {
-      const int i = threadIdx.x;
-      for (int s = L - 1; s >= 0; --s) {
-        float z = dU[s * R + i];
-        for (int t = s + 1; t < L; ++t) z += c.m(0, t, s) * dZ[t * R + i];
-        dZ[s * R + i] = z;
-      }
-    }
-    __syncthreads();
-    // dV (row-local, final) and the row partial sums of the key-side gradients.
-    for (int e = threadIdx.x; e < L * R; e += THREADS) {
-      const int s = e / R, i = e % R;
-      float g = dVk[e];
-      for (int t = s; t < L; ++t) g += c.m(3, t, s) * dY[t * R + i];
-      for (int t = s + 1; t < L; ++t) g += c.m(1, t, s) * dZ[t * R + i];
-      const int tg = t0 + s, row = row0 + i;
-      if (tg < T_ && row < N) dv[((long)(batch * T_ + tg) * H + head) * N + row] = g;
-    }
-    for (int e = threadIdx.x; e < L * L; e += THREADS) {
-      const int t = e / L, s = e % L;
-      float zab = 0, zak = 0, yrb = 0, yrk = 0;
-#pragma unroll
-      for (int i = 0; i < R; ++i) {
-        const float zt = dZ[t * R + i], yt = dY[t * R + i], us = U[s * R + i], vs = c.v[s * R + i];
-        zab += zt * us; zak += zt * vs; yrb += yt * us; yrk += yt * vs;
-      }
-      const int o = t * (L + 1) + s;
-      PdM[0 * S::MAT + o] = s < t ? zab : 0.f;
-      PdM[1 * S::MAT + o] = s < t ? zak : 0.f;
-      PdM[2 * S::MAT + o] = s <= t ? yrb : 0.f;
-      PdM[3 * S::MAT + o] = s <= t ? yrk : 0.f;
-    }
-    for (int e = threadIdx.x; e < L * NP; e += THREADS) {
-      const int t = e / NP, j = e % NP;
-      float rd = 0, ad = 0, bh_ = 0, kh = 0;
-#pragma unroll
-      for (int i = 0; i < R; ++i) {
-        const float s0v = S0[i * S::SP + j], dsv = dS[i * S::SP + j];
-        rd += dY[t * R + i] * s0v;
-        ad += dZ[t * R + i] * s0v;
-        bh_ += U[t * R + i] * dsv;
-        kh += c.v[t * R + i] * dsv;
-      }
-      const int o = t * S::SP + j;
-      PdR[o] = rd; PdA[o] = ad; PdB[o] = bh_; PdK[o] = kh;
-    }
-    if (threadIdx.x < NP) {
-      const int j = threadIdx.x;
-      float acc = 0.f;
-#pragma unroll
-      for (int i = 0; i < R; ++i) acc += S0[i * S::SP + j] * dS[i * S::SP + j];
-      PdD[j] = acc;
-    }
-    __syncthreads();
-    // dS for the previous chunk: dY^T R~ + dZ^T A~ + dS diag(D_L).
-    for (int e = threadIdx.x; e < R * NP; e += THREADS) {
-      const int i = e / NP, j = e % NP;
-      float acc = dS[i * S::SP + j] * c.dl[j];
-#pragma unroll
-      for (int t = 0; t < L; ++t) acc += dY[t * R + i] * c.r[t * S::SP + j] + dZ[t * R + i] * c.a[t * S::SP + j];
-      dS[i * S::SP + j] = acc;
-    }
-    // Cluster-wide reduction of the partials (fixed rank order => deterministic).
-    if constexpr (NSPLIT > 1) cluster.sync(); else __syncthreads();
-    for (int e = threadIdx.x; e < 4 * S::MAT; e += THREADS) {
-      float acc = 0.f;
-#pragma unroll
-      for (int q = 0; q < NSPLIT; ++q) {
-        const float* rp = (NSPLIT > 1) ? cluster.map_shared_rank(PdM, q) : PdM;
-        acc += rp[e];
-      }
-      dM[e] = acc;
-    }
-    const int j0 = rb * JQ;
-    // Reduced column slice: dR~d, dA~d, dB^, dK^ for columns [j0, j0+JQ), stored into dLam
-    // scratch rows via registers below; first gather them.
-    __syncthreads();
-    for (int e = threadIdx.x; e < L * JQ; e += THREADS) {
-      const int t = e / JQ, jj = e % JQ, j = j0 + jj, o = t * S::SP + j;
-      float rd = 0, ad = 0, bhat = 0, khat = 0;
-#pragma unroll
-      for (int q = 0; q < NSPLIT; ++q) {
-        const float* rp = (NSPLIT > 1) ? cluster.map_shared_rank(P, q) : P;
-        rd += rp[4 * S::MAT + o];
-        ad += rp[4 * S::MAT + S::KEY + o];
-        bhat += rp[4 * S::MAT + 2 * S::KEY + o];
-        khat += rp[4 * S::MAT + 3 * S::KEY + o];
-      }
-      // Chain through the chunk matrices for column j.
-      float dat = ad, drt = rd, dbt = bhat * c.dl[j], dkt = khat * c.dl[j];
-#pragma unroll
-      for (int s = 0; s < L; ++s) {
-        dat += dM[0 * S::MAT + t * (L + 1) + s] * c.b[s * S::SP + j] + dM[1 * S::MAT + t * (L + 1) + s] * c.k[s * S::SP + j];
-        drt += dM[2 * S::MAT + t * (L + 1) + s] * c.b[s * S::SP + j] + dM[3 * S::MAT + t * (L + 1) + s] * c.k[s * S::SP + j];
-        dbt += dM[0 * S::MAT + s * (L + 1) + t] * c.a[s * S::SP + j] + dM[2 * S::MAT + s * (L + 1) + t] * c.r[s * S::SP + j];
-        dkt += dM[1 * S::MAT + s * (L + 1) + t] * c.a[s * S::SP + j] + dM[3 * S::MAT + s * (L + 1) + t] * c.r[s * S::SP + j];
-      }
-      const float lam_t = c.lam[o];
-      const float lam_p = t ? c.lam[o - S::SP] : 0.f;
-      const float e_t = expf(lam_t), e_p = expf(lam_p), inv_t = 1.f / e_t;
-      // Raw-input gradients.
-      const int tg = t0 + t;
-      if (tg < T_ && j < N) {
-        const long idx = ((long)(batch * T_ + tg) * H + head) * N + j;
-        dr[idx] = drt * e_t;
-        da[idx] = dat * e_p;
-        db[idx] = dbt * inv_t;
-        dk[idx] = dkt * inv_t;
-      }
-      // d Lambda_t contributions that live at index t; the a~ term belongs to t-1.
-      dLam[o] = drt * c.r[o] - dbt * c.b[o] - dkt * c.k[o];
-      // Stash dA~ * a~ for the (t-1) term in dU's slot (free now): one float per (t, jj).
-      dU[t * JQ + jj] = dat * c.a[o];
-      if (t == L - 1) {
-        // D_L = e^{Lambda_{L-1}} : collect dD_L (direct + through b^, k^).
-        float ddl = 0.f;
-#pragma unroll
-        for (int q = 0; q < NSPLIT; ++q) {
-          const float* rp = (NSPLIT > 1) ? cluster.map_shared_rank(P, q) : P;
-          ddl += rp[4 * S::MAT + 4 * S::KEY + j];
-        }
-        dZ[jj] = ddl;  // dZ is free now: stash the reduced direct dD_L
-      }
-    }
-    __syncthreads();
-    // Column-wise: add the b^/k^ terms of dD_L, the shifted a~ term, then reverse cumsum -> dw.
-    if (threadIdx.x < JQ) {
-      const int jj = threadIdx.x, j = j0 + jj;
-      float ddl = dZ[jj];
-      // dD_L also receives sum_s dB^[s] b~[s] + dK^[s] k~[s] (b^ = b~ D_L).
-#pragma unroll
-      for (int s = 0; s < L; ++s) {
-        float bhat = 0, khat = 0;
-#pragma unroll
-        for (int q = 0; q < NSPLIT; ++q) {
-          const float* rp = (NSPLIT > 1) ? cluster.map_shared_rank(P, q) : P;
-          bhat += rp[4 * S::MAT + 2 * S::KEY + s * S::SP + j];
-          khat += rp[4 * S::MAT + 3 * S::KEY + s * S::SP + j];
-        }
-        ddl += bhat * c.b[s * S::SP + j] + khat * c.k[s * S::SP + j];
-      }
-      float run = 0.f;
-      for (int t = L - 1; t >= 0; --t) {
-        float g = dLam[t * S::SP + j];
-        if (t + 1 < L) g += dU[(t + 1) * JQ + jj];
-        if (t == L - 1) g += ddl * c.dl[j];
-        run += g;
-        const int tg = t0 + t;
-        if (tg < T_ && j < N) {
-          const float sg = c.sig[t * S::SP + j];
-          dw[((long)(batch * T_ + tg) * H + head) * N + j] = run * (-DECAY_SCALE) * sg * (1.f - sg);
-        }
-      }
-    }
-    // Remote partial buffers of this chunk may be read until every CTA passes the next
-    // cluster barrier; the double buffer keeps the next chunk's writes off them.
-    __syncthreads();
-  }
-  if constexpr (NSPLIT > 1) cluster.sync();
-  for (int e = threadIdx.x; e < R * NP; e += THREADS) {
-    const int i = e / NP, j = e % NP, row = row0 + i;
-    if (row < N && j < N) ds0[bh * NN + (long)row * N + j] = dS[i * S::SP + j];
-  }
-}
-
 template <int NP>
 constexpr int padded_np() { return NP; }
 
 int pick_np(int N) { return N <= 16 ? 16 : N <= 32 ? 32 : N <= 64 ? 64 : 128; }
 
-template <typename T, int NP>
-cudaError_t launch_fwd(int B, int T_, int H, int N, const void* r, const void* w, const void* k, const void* v,
-                       const void* a, const void* b, const float* s0, void* y, float* s_end, float* ckpt,
-                       cudaStream_t stream) {
+bool async_ok(int N, int elem, std::initializer_list<const void*> ptrs) {
+  if ((N * elem) % 16 || (N % 4)) return false;
+  for (const void* p : ptrs)
+    if (reinterpret_cast<uintptr_t>(p) & 15) return false;
+  return true;
+}
+
+template <typename T, int NP, bool ASYNC>
+cudaError_t launch_fwd_impl(int B, int T_, int H, int N, const void* r, const void* w, const void* k, const void* v,
+                            const void* a, const void* b, const float* s0, void* y, float* s_end, float* ckpt,
+                            cudaStream_t stream) {
   using S = Smem<NP>;
-  const size_t bytes = (Chunk<T, NP>::FLOATS + S::STATE + 3 * S::ROWS) * sizeof(float);
-  auto kern = wkv7_forward_kernel<T, NP>;
+  constexpr int ST = ASYNC ? 2 : 1;
+  const size_t bytes = (ST * Raw<T, NP>::FLOATS + Chunk<T, NP>::FLOATS + S::STATE + 3 * S::ROWS) * sizeof(float);
+  auto kern = wkv7_forward_kernel<T, NP, ASYNC>;
   RT_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
   dim3 grid(NP / R, B * H);
   kern<<<grid, THREADS, bytes, stream>>>(T_, H, N, (const T*)r, (const T*)w, (const T*)k, (const T*)v,
@@ -504,28 +341,12 @@ cudaError_t launch_fwd(int B, int T_, int H, int N, const void* r, const void* w
 }
 
 template <typename T, int NP>
-cudaError_t launch_bwd(int B, int T_, int H, int N, const void* r, const void* w, const void* k, const void* v,
-                       const void* a, const void* b, const float* ckpt, const void* dy, const float* dend,
-                       float* dr, float* dw, float* dk, float* dv, float* da, float* db, float* ds0,
+cudaError_t launch_fwd(int B, int T_, int H, int N, const void* r, const void* w, const void* k, const void* v,
+                       const void* a, const void* b, const float* s0, void* y, float* s_end, float* ckpt,
                        cudaStream_t stream) {
-  constexpr int NSPLIT = NP / R;
-  const size_t bytes = BwdLayout<T, NP>::FLOATS * sizeof(float);
-  auto kern = wkv7_backward_kernel<T, NP, NSPLIT>;
-  RT_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(NSPLIT, B * H);
-  cfg.blockDim = dim3(THREADS);
-  cfg.dynamicSmemBytes = bytes;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = NSPLIT;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, T_, H, N, (const T*)r, (const T*)w, (const T*)k, (const T*)v,
-                            (const T*)a, (const T*)b, ckpt, (const T*)dy, dend, dr, dw, dk, dv, da, db, ds0);
+  if (async_ok(N, sizeof(T), {r, w, k, v, a, b}))
+    return launch_fwd_impl<T, NP, true>(B, T_, H, N, r, w, k, v, a, b, s0, y, s_end, ckpt, stream);
+  return launch_fwd_impl<T, NP, false>(B, T_, H, N, r, w, k, v, a, b, s0, y, s_end, ckpt, stream);
 }
 
 }  // namespace
@@ -551,22 +372,3 @@ extern "C" cudaError_t rt_wkv7_forward(int dtype, int B, int T_, int H, int N, c
 #undef RT_FWD
 }
 
-extern "C" cudaError_t rt_wkv7_backward(int dtype, int B, int T_, int H, int N, const void* r, const void* w,
-                                        const void* k, const void* v, const void* a, const void* b,
-                                        const float* checkpoints, const void* dy, const float* dend,
-                                        float* dr, float* dw, float* dk, float* dv, float* da, float* db,
-                                        float* ds0, cudaStream_t stream) {
-  const int np = pick_np(N);
-#define RT_BWD(TYPE, NPV) \
-  return launch_bwd<TYPE, NPV>(B, T_, H, N, r, w, k, v, a, b, checkpoints, dy, dend, dr, dw, dk, dv, da, db, ds0, stream)
-#define RT_BWD_NP(TYPE)                                   \
-  switch (np) {                                           \
-    case 16: RT_BWD(TYPE, 16);                            \
-    case 32: RT_BWD(TYPE, 32);                            \
-    case 64: RT_BWD(TYPE, 64);                            \
-    default: RT_BWD(TYPE, 128);                           \
-  }
-  if (dtype == (int)rt::DType::BF16) { RT_BWD_NP(__nv_bfloat16) } else { RT_BWD_NP(float) }
-#undef RT_BWD_NP
-#undef RT_BWD
-}
