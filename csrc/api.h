@@ -72,6 +72,11 @@ cudaError_t rt_flat_adamw(float* p, float* g, float* m, float* v, void* shadow, 
                           float eps, float weight_decay, float clip, int step, cudaStream_t s);
 cudaError_t rt_to_bf16(const float* src, void* dst, long n, cudaStream_t s);
 
+// Flash attention forward (head_dim 256, GQA, causal with cache offset, fused sigmoid gate).
+cudaError_t rt_flash_attention_fwd(const void* q, const void* keys, const void* values, const void* gate,
+                                   long gate_row, long gate_head, void* out, int B, int T, int Hq, int Hkv, int offset,
+                                   int cap, int* status, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -340,6 +340,26 @@ void to_bf16_(at::Tensor src, at::Tensor dst) {
   check_cuda(rt_to_bf16(FPTR(src), PTR(dst), src.numel(), stream_of(src)), "to_bf16");
 }
 
+// q [B,T,Hq,256]; keys/values [B,cap,Hkv,256]; gate rows: qg [B*T, Hq*512] with the gate in the second half of
+// every head's 512 values. Returns [B,T,Hq,256] bf16.
+at::Tensor flash_attention(at::Tensor q, at::Tensor keys, at::Tensor values, at::Tensor qg, int64_t offset) {
+  check_bf16(q, "q");
+  check_bf16(keys, "keys");
+  check_bf16(values, "values");
+  TORCH_CHECK(q.dim() == 4 && q.size(3) == 256 && keys.dim() == 4 && keys.size(3) == 256 && keys.sizes() == values.sizes(),
+              "flash_attention expects head_dim 256");
+  TORCH_CHECK(qg.is_cuda() && qg.scalar_type() == at::kBFloat16 && qg.stride(-1) == 1, "gate must be bf16 rows");
+  c10::cuda::CUDAGuard guard(q.device());
+  const int B = q.size(0), T = q.size(1), Hq = q.size(2), Hkv = keys.size(2), cap = keys.size(1);
+  TORCH_CHECK(qg.numel() == (long)B * T * Hq * 512, "gate buffer must be [B*T, Hq*512]");
+  auto out = at::empty_like(q);
+  check_cuda(rt_flash_attention_fwd(q.data_ptr(), keys.data_ptr(), values.data_ptr(),
+                                    static_cast<const at::BFloat16*>(qg.data_ptr()) + 256, (long)Hq * 512, 512,
+                                    out.data_ptr(), B, T, Hq, Hkv, (int)offset, cap, nullptr, stream_of(q)),
+             "flash_attention");
+  return out;
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -369,5 +389,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("eps"));
   m.def("flat_adamw", &flat_adamw);
   m.def("to_bf16_", &to_bf16_);
+  m.def("flash_attention", &flash_attention);
   m.def("wkv7_chunk_len", []() { return rt_wkv7_chunk_len(); });
 }

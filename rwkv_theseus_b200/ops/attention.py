@@ -21,8 +21,9 @@ def _ensure_cache(state, B, T, Hkv, D, device):
     need = length + T
     if keys is None or keys.shape[1] < need:
         cap = max(need, 2 * (keys.shape[1] if keys is not None else 0), 1024)
-        new_k = torch.empty(B, cap, Hkv, D, device=device, dtype=torch.bfloat16)
-        new_v = torch.empty_like(new_k)
+        # Zero-filled: attention tiles read whole key blocks, and masked keys must hold finite values.
+        new_k = torch.zeros(B, cap, Hkv, D, device=device, dtype=torch.bfloat16)
+        new_v = torch.zeros_like(new_k)
         if keys is not None and length:
             new_k[:, :length].copy_(keys[:, :length])
             new_v[:, :length].copy_(state["values"][:, :length])
@@ -31,7 +32,7 @@ def _ensure_cache(state, B, T, Hkv, D, device):
 
 
 def core_attention(q, k_all, v_all, offset):
-    """Causal GQA attention; q [B,T,Hq,D], caches [B,L,Hkv,D]; query t at absolute offset+t."""
+    """Causal GQA attention for head sizes the tcgen05 kernel does not cover (PyTorch SDPA)."""
     B, T, Hq, D = q.shape
     L = k_all.shape[1]
     rows = torch.arange(T, device=q.device)[:, None] + offset
@@ -59,7 +60,10 @@ def attention_block(module, x, rope, state):
     native().norm_rope_(k, Hkv, module.k_norm.weight, inv_freq, state["keys"], pos0, length, rot, module.k_norm.eps)
     native().copy_rows_(v, state["values"], length)
     state["length"] = length + T
-    out = core_attention(q, state["keys"][:, :length + T], state["values"][:, :length + T], length)
-    gate = qg.view(B, T, Hq, 2 * D)[..., D:]
-    out = (out * torch.sigmoid(gate)).reshape(B * T, Hq * D)
+    if D == 256:
+        out = native().flash_attention(q, state["keys"], state["values"], qg, length).view(B * T, Hq * D)
+    else:
+        out = core_attention(q, state["keys"][:, :length + T], state["values"][:, :length + T], length)
+        gate = qg.view(B, T, Hq, 2 * D)[..., D:]
+        out = (out * torch.sigmoid(gate)).reshape(B * T, Hq * D)
     return linear(out, module.o_proj.weight).view(B, T, C)
