@@ -89,14 +89,17 @@ gdn_prep_kernel(const bf16* __restrict__ qkv, long row_stride, int T, int Hk, fl
 }
 
 // ---------------------------------------------------------------- recurrent chunk kernel
-// grid (D/R, Hv, B). Value columns [col0, col0+R) of value head h. The next chunk's q, k, Gram matrices
-// and v columns are copied asynchronously (cp.async, double buffered) while the current chunk computes;
-// the per-step gates of the next chunk are prefetched into registers.
+// grid (D/R, Hv, B), 256 threads. Value columns [col0, col0+R) of value head h; the state block is held
+// value-major (S[i][j], i value column, j key) so every inner product over keys uses 128-bit shared loads.
+// The next chunk's q, k, Gram matrices and v columns are copied asynchronously (cp.async, double buffered)
+// while the current chunk computes; the per-step gates of the next chunk are prefetched into registers.
+constexpr int CT = 256;
+
 template <int D>
 struct GdnSmem {
   static constexpr int SP = D + 4;
   static constexpr int STAGE = 2 * L * SP + 2 * L * L + L * R / 2;  // q, k, gram (fp32) + v (bf16) in floats
-  static constexpr int FLOATS = 2 * STAGE + D * (R + 1) + 4 * L * R + 4 * L * (L + 1) + 6 * L;
+  static constexpr int FLOATS = 2 * STAGE + R * SP + 5 * L * R + 4 * L * (L + 1) + 6 * L;
 };
 
 template <int D>
@@ -108,7 +111,7 @@ RT_DEVICE void gdn_issue(float* stage, const float* qn, const float* kn, const f
   float* sg = sk + L * G::SP;
   bf16* sv = reinterpret_cast<bf16*>(sg + 2 * L * L);
   constexpr int QV = D / 4;
-  for (int e = threadIdx.x; e < 2 * L * QV; e += THREADS) {
+  for (int e = threadIdx.x; e < 2 * L * QV; e += CT) {
     const int which = e / (L * QV), rem = e % (L * QV), tt = rem / QV, c = (rem % QV) * 4, t = ch * L + tt;
     const bool ok = t < T;
     const float* base = which ? kn : qn;
@@ -116,8 +119,8 @@ RT_DEVICE void gdn_issue(float* stage, const float* qn, const float* kn, const f
     rt::cp_async16((which ? sk : sq) + tt * G::SP + c, src, ok);
   }
   const float* gsrc = gram + (((long)b * Hk + kh) * chunks + ch) * 2 * L * L;
-  for (int e = threadIdx.x; e < 2 * L * L / 4; e += THREADS) rt::cp_async16(sg + 4 * e, gsrc + 4 * e, true);
-  for (int e = threadIdx.x; e < L * (R / 8); e += THREADS) {
+  for (int e = threadIdx.x; e < 2 * L * L / 4; e += CT) rt::cp_async16(sg + 4 * e, gsrc + 4 * e, true);
+  for (int e = threadIdx.x; e < L * (R / 8); e += CT) {
     const int tt = e / (R / 8), i = (e % (R / 8)) * 8, t = ch * L + tt;
     const bool ok = t < T;
     const bf16* src = qkv + (ok ? ((long)b * T + t) * row_stride + vbase + i : 0);
@@ -127,7 +130,7 @@ RT_DEVICE void gdn_issue(float* stage, const float* qn, const float* kn, const f
 }
 
 template <int D>
-__global__ void __launch_bounds__(THREADS)
+__global__ void __launch_bounds__(CT)
 gdn_chunk_kernel(const float* __restrict__ qn, const float* __restrict__ kn, const float* __restrict__ gram,
                  const bf16* __restrict__ qkv, long row_stride, const bf16* __restrict__ pa,
                  const bf16* __restrict__ pb, long ab_stride, const float* __restrict__ A_log,
@@ -137,12 +140,13 @@ gdn_chunk_kernel(const float* __restrict__ qn, const float* __restrict__ kn, con
   constexpr int SP = G::SP;
   extern __shared__ __align__(16) float sm[];
   float* stage[2] = {sm, sm + G::STAGE};
-  float* S = sm + 2 * G::STAGE;   // [D][R+1] state block (key j, value column i)
-  float* V = S + D * (R + 1);     // [L][R]  beta * v
+  float* S = sm + 2 * G::STAGE;   // [R][SP] state block, value-major
+  float* V = S + R * SP;          // [L][R]  beta * v
   float* Z = V + L * R;           // [L][R]
   float* U = Z + L * R;           // [L][R]
   float* Y = U + L * R;           // [L][R]
-  float* Mab = Y + L * R;         // [L][L+1]
+  float* Q = Y + L * R;           // [L][R]  per-step state-update coefficients
+  float* Mab = Q + L * R;         // [L][L+1]
   float* Mak = Mab + L * (L + 1);
   float* Mrb = Mak + L * (L + 1);
   float* Mrk = Mrb + L * (L + 1);
@@ -159,18 +163,18 @@ gdn_chunk_kernel(const float* __restrict__ qn, const float* __restrict__ kn, con
   const long vbase = 2L * Hk * D + (long)h * D + col0;  // v column offset inside a qkv row
   float* st = state + ((long)b * Hv + h) * D * D;       // [D key][D value]
   gdn_issue<D>(stage[0], qn, kn, gram, qkv, row_stride, vbase, b, T, Hk, kh, 0, chunks);
-  for (int e = threadIdx.x; e < D * R; e += THREADS) {
+  for (int e = threadIdx.x; e < D * R; e += CT) {
     const int j = e / R, i = e % R;
-    S[j * (R + 1) + i] = st[(long)j * D + col0 + i];
+    S[i * SP + j] = st[(long)j * D + col0 + i];
   }
   const float neg_a = -expf(A_log[h]);
   const float dtb = dt_bias[h];
-  // Gate inputs of the current chunk held in registers by threads < L.
-  float ga = 0.f, gb = 0.f;
+  float ga = 0.f, gb = 0.f;  // gate inputs of the current chunk (threads < L)
   if (threadIdx.x < L && threadIdx.x < T) {
     ga = rt::to_f(pa[((long)b * T + threadIdx.x) * ab_stride + h]);
     gb = rt::to_f(pb[((long)b * T + threadIdx.x) * ab_stride + h]);
   }
+  const int ti = threadIdx.x >> 4, ii = threadIdx.x & 15;  // (t, i) owned in the L x R loops
   for (int ch = 0; ch < chunks; ++ch) {
     const int t0 = ch * L;
     if (ch + 1 < chunks) {
@@ -179,104 +183,114 @@ gdn_chunk_kernel(const float* __restrict__ qn, const float* __restrict__ kn, con
     } else {
       rt::cp_async_wait<0>();
     }
-    float na = 0.f, nb = 0.f;  // next chunk's gates (prefetched into registers)
+    float na = 0.f, nb = 0.f;
     if (threadIdx.x < L) {
       const int tn = t0 + L + threadIdx.x;
       if (tn < T) {
         na = rt::to_f(pa[((long)b * T + tn) * ab_stride + h]);
         nb = rt::to_f(pb[((long)b * T + tn) * ab_stride + h]);
       }
-      const int tt = threadIdx.x, t = t0 + tt;
       float g = 0.f, bt = 0.f;
-      if (t < T) {
+      if (t0 + threadIdx.x < T) {
         const float av = ga + dtb;
-        const float sp = av > 20.f ? av : log1pf(expf(av));
-        g = neg_a * sp;
+        g = neg_a * (av > 20.f ? av : log1pf(expf(av)));
         bt = __bfloat162float(__float2bfloat16_rn(rt::sigmoidf_(gb)));
       }
-      lam[tt] = g;
-      beta[tt] = bt;
+      lam[threadIdx.x] = g;
+      beta[threadIdx.x] = bt;
     }
     __syncthreads();
     const float* sq = stage[ch & 1];
     const float* sk = sq + L * SP;
     const float* gr = sk + L * SP;
     const bf16* sv = reinterpret_cast<const bf16*>(gr + 2 * L * L);
-    if (threadIdx.x == 0) {
-      float run = 0.f;
-      for (int tt = 0; tt < L; ++tt) { run += lam[tt]; lam[tt] = run; }
+    if (threadIdx.x < 32) {  // inclusive scan of the 16 log-gates in one warp
+      float x = threadIdx.x < L ? lam[threadIdx.x] : 0.f;
+#pragma unroll
+      for (int o = 1; o < L; o <<= 1) {
+        const float y = __shfl_up_sync(0xffffffffu, x, o);
+        if (threadIdx.x >= o) x += y;
+      }
+      const float lL = __shfl_sync(0xffffffffu, x, L - 1);
+      const float prev = __shfl_up_sync(0xffffffffu, x, 1);
+      if (threadIdx.x < L) {
+        const float pv = threadIdx.x ? prev : 0.f;
+        lam[threadIdx.x] = x;
+        e_prev[threadIdx.x] = expf(pv);
+        e_cur[threadIdx.x] = expf(x);
+        c_u[threadIdx.x] = -beta[threadIdx.x] * expf(lL - pv);
+        c_v[threadIdx.x] = expf(lL - x);
+      }
+    }
+    V[threadIdx.x] = rt::to_f(sv[threadIdx.x]);  // L * R == CT
+    __syncthreads();
+    {  // chunk matrices from the Gram matrices (all exponents <= 0); beta-scaled V
+      const int t = ti, s2 = ii;
+      const float kk = gr[t * L + s2], qk = gr[L * L + t * L + s2];
+      const float lt = lam[t], lt1 = t ? lam[t - 1] : 0.f, ls = lam[s2], ls1 = s2 ? lam[s2 - 1] : 0.f;
+      Mab[t * (L + 1) + s2] = s2 < t ? -beta[s2] * kk * expf(lt1 - ls1) : 0.f;
+      Mak[t * (L + 1) + s2] = s2 < t ? kk * expf(lt1 - ls) : 0.f;
+      Mrb[t * (L + 1) + s2] = s2 <= t ? -beta[s2] * qk * expf(lt - ls1) : 0.f;
+      Mrk[t * (L + 1) + s2] = s2 <= t ? qk * expf(lt - ls) : 0.f;
+      V[threadIdx.x] *= beta[ti];
     }
     __syncthreads();
-    if (threadIdx.x < L) {
-      const int tt = threadIdx.x;
-      const float prev = tt ? lam[tt - 1] : 0.f, lL = lam[L - 1];
-      e_prev[tt] = expf(prev);
-      e_cur[tt] = expf(lam[tt]);
-      c_u[tt] = -beta[tt] * expf(lL - prev);
-      c_v[tt] = expf(lL - lam[tt]);
-    }
-    for (int e = threadIdx.x; e < L * R; e += THREADS) V[e] = rt::to_f(sv[e]) * beta[e / R];
-    // Chunk matrices from the Gram matrices (all exponents <= 0).
-    for (int e = threadIdx.x; e < L * L; e += THREADS) {
-      const int t = e / L, s = e % L;
-      const float kk = gr[e], qk = gr[L * L + e];
-      const float lt = lam[t], lt1 = t ? lam[t - 1] : 0.f, ls = lam[s], ls1 = s ? lam[s - 1] : 0.f;
-      Mab[t * (L + 1) + s] = s < t ? -beta[s] * kk * expf(lt1 - ls1) : 0.f;
-      Mak[t * (L + 1) + s] = s < t ? kk * expf(lt1 - ls) : 0.f;
-      Mrb[t * (L + 1) + s] = s <= t ? -beta[s] * qk * expf(lt - ls1) : 0.f;
-      Mrk[t * (L + 1) + s] = s <= t ? qk * expf(lt - ls) : 0.f;
-    }
-    __syncthreads();
-    // Z = e^{Lambda_{t-1}} S0^T k_t + Mak V ;  Yp = e^{Lambda_t} S0^T q_t + Mrk V
-    for (int e = threadIdx.x; e < L * R; e += THREADS) {
-      const int t = e / R, i = e % R;
+    {  // Z = e^{Lambda_{t-1}} S0 k_t + Mak V ;  Yp = e^{Lambda_t} S0 q_t + Mrk V
+      const float4* kt = reinterpret_cast<const float4*>(sk + ti * SP);
+      const float4* qt = reinterpret_cast<const float4*>(sq + ti * SP);
+      const float4* si = reinterpret_cast<const float4*>(S + ii * SP);
       float zk = 0.f, yq = 0.f;
 #pragma unroll 8
-      for (int j = 0; j < D; ++j) {
-        const float sv2 = S[j * (R + 1) + i];
-        zk += sk[t * SP + j] * sv2;
-        yq += sq[t * SP + j] * sv2;
+      for (int u = 0; u < D / 4; ++u) {
+        const float4 s4 = si[u], k4 = kt[u], q4 = qt[u];
+        zk += k4.x * s4.x + k4.y * s4.y + k4.z * s4.z + k4.w * s4.w;
+        yq += q4.x * s4.x + q4.y * s4.y + q4.z * s4.z + q4.w * s4.w;
       }
-      float z = zk * e_prev[t], y = yq * e_cur[t];
-      for (int s = 0; s < t; ++s) z += Mak[t * (L + 1) + s] * V[s * R + i];
-      for (int s = 0; s <= t; ++s) y += Mrk[t * (L + 1) + s] * V[s * R + i];
-      Z[e] = z;
-      Y[e] = y;
+      float z = zk * e_prev[ti], y = yq * e_cur[ti];
+      for (int s2 = 0; s2 < ti; ++s2) z += Mak[ti * (L + 1) + s2] * V[s2 * R + ii];
+      for (int s2 = 0; s2 <= ti; ++s2) y += Mrk[ti * (L + 1) + s2] * V[s2 * R + ii];
+      Z[threadIdx.x] = z;
+      Y[threadIdx.x] = y;
     }
     __syncthreads();
     if (threadIdx.x < R) {
       const int i = threadIdx.x;
       for (int t = 0; t < L; ++t) {
         float u = Z[t * R + i];
-        for (int s = 0; s < t; ++s) u += Mab[t * (L + 1) + s] * U[s * R + i];
+        for (int s2 = 0; s2 < t; ++s2) u += Mab[t * (L + 1) + s2] * U[s2 * R + i];
         U[t * R + i] = u;
       }
     }
     __syncthreads();
-    for (int e = threadIdx.x; e < L * R; e += THREADS) {
-      const int t = e / R, i = e % R;
-      float y = Y[e];
-      for (int s = 0; s <= t; ++s) y += Mrb[t * (L + 1) + s] * U[s * R + i];
-      const int tg = t0 + t;
-      if (tg < T) out[(((long)b * T + tg) * Hv + h) * D + col0 + i] = __float2bfloat16_rn(y);
+    {
+      float y = Y[threadIdx.x];
+      for (int s2 = 0; s2 <= ti; ++s2) y += Mrb[ti * (L + 1) + s2] * U[s2 * R + ii];
+      const int tg = t0 + ti;
+      if (tg < T) out[(((long)b * T + tg) * Hv + h) * D + col0 + ii] = __float2bfloat16_rn(y);
+      Q[threadIdx.x] = U[threadIdx.x] * c_u[ti] + V[threadIdx.x] * c_v[ti];
     }
-    // S_L = e^{Lambda_L} S0 + sum_s k_s (U_s c_s + V_s d_s), c_s = -beta_s e^{Lambda_L - Lambda_{s-1}},
-    // d_s = e^{Lambda_L - Lambda_s}.
+    __syncthreads();
+    // S_L[i][j] = e^{Lambda_L} S0[i][j] + sum_s Q[s][i] k_s[j]
     const float eL = e_cur[L - 1];
-    for (int e = threadIdx.x; e < D * R; e += THREADS) {
-      const int j = e / R, i = e % R;
-      float acc = S[j * (R + 1) + i] * eL;
+    for (int e = threadIdx.x; e < R * (D / 4); e += CT) {
+      const int i = e / (D / 4), j = (e % (D / 4)) * 4;
+      float4 acc = *reinterpret_cast<float4*>(S + i * SP + j);
+      acc.x *= eL; acc.y *= eL; acc.z *= eL; acc.w *= eL;
 #pragma unroll
-      for (int s = 0; s < L; ++s) acc += sk[s * SP + j] * (U[s * R + i] * c_u[s] + V[s * R + i] * c_v[s]);
-      S[j * (R + 1) + i] = acc;
+      for (int s2 = 0; s2 < L; ++s2) {
+        const float qv = Q[s2 * R + i];
+        const float4 k4 = *reinterpret_cast<const float4*>(sk + s2 * SP + j);
+        acc.x += qv * k4.x; acc.y += qv * k4.y; acc.z += qv * k4.z; acc.w += qv * k4.w;
+      }
+      *reinterpret_cast<float4*>(S + i * SP + j) = acc;
     }
     ga = na;
     gb = nb;
     __syncthreads();
   }
-  for (int e = threadIdx.x; e < D * R; e += THREADS) {
+  for (int e = threadIdx.x; e < D * R; e += CT) {
     const int j = e / R, i = e % R;
-    st[(long)j * D + col0 + i] = S[j * (R + 1) + i];
+    st[(long)j * D + col0 + i] = S[i * SP + j];
   }
 }
 
@@ -292,7 +306,7 @@ cudaError_t launch(const void* qkv, long row_stride, const void* a, const void* 
   RT_CUDA_CHECK(cudaGetLastError());
   const size_t smem = GdnSmem<D>::FLOATS * sizeof(float);
   RT_CUDA_CHECK(cudaFuncSetAttribute(gdn_chunk_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  gdn_chunk_kernel<D><<<dim3(D / R, Hv, B), THREADS, smem, stream>>>(
+  gdn_chunk_kernel<D><<<dim3(D / R, Hv, B), CT, smem, stream>>>(
       qn, kn, gram, (const bf16*)qkv, row_stride, (const bf16*)a, (const bf16*)b, ab_stride, A_log, dt_bias, state,
       (bf16*)out, T, Hk, Hv);
   return cudaGetLastError();
