@@ -260,7 +260,7 @@ def count_launches(step_fn):
     from torch.profiler import ProfilerActivity, profile
     mine = ("wkv7_", "gemm_kernel", "rmsnorm_kernel", "conv1d_silu", "gdn_", "mix_kernel", "mix_bwd", "pre_wkv",
             "post_wkv", "nmse_loss", "adamw_kernel", "scale_norm", "act_kernel", "act_bwd", "norm_rope",
-            "copy_rows", "to_bf16", "report_kernel", "gated_rmsnorm", "flash_attn", "peer_")
+            "copy_rows", "to_bf16", "report_kernel", "gated_rmsnorm", "flash_attn", "exchange_")
     with profile(activities=[ProfilerActivity.CUDA]) as prof:
         step_fn(False)
         torch.cuda.synchronize()

@@ -77,6 +77,18 @@ cudaError_t rt_flash_attention_fwd(const void* q, const void* keys, const void* 
                                    long gate_row, long gate_head, void* out, int B, int T, int Hq, int Hkv, int offset,
                                    int cap, int* status, cudaStream_t stream);
 
+// ---- peer-memory gradient exchange (csrc/parallel/peer_exchange.cu)
+int rt_exchange_signal_words();
+cudaError_t rt_exchange_update(float* const* grads, float* const* params, void* const* shadows, unsigned* const* sigs,
+                               int rank, int world, long n, float* m, float* v, float* stats, float* report, float lr,
+                               float beta1, float beta2, float eps, float weight_decay, float clip, int step,
+                               long decay_numel, unsigned epoch, double limit_s, int blocks, cudaStream_t s);
+void rt_exchange_shard(long n, int rank, int world, long* out4);
+cudaError_t rt_ipc_export(const void* ptr, void* handle64, long* offset);
+cudaError_t rt_ipc_open(const void* handle64, void** base);
+cudaError_t rt_ipc_close(void* base);
+
 #ifdef __cplusplus
 }
 #endif
+

@@ -340,6 +340,56 @@ void to_bf16_(at::Tensor src, at::Tensor dst) {
   check_cuda(rt_to_bf16(FPTR(src), PTR(dst), src.numel(), stream_of(src)), "to_bf16");
 }
 
+// ---- peer-memory gradient exchange. Pointer lists hold one device address per rank (int64), peers' addresses
+// already mapped into this process by ipc_open.
+void exchange_update(std::vector<int64_t> grads, std::vector<int64_t> params, std::vector<int64_t> shadows,
+                     std::vector<int64_t> sigs, int64_t rank, int64_t world, int64_t n, at::Tensor m, at::Tensor v,
+                     at::Tensor stats, at::Tensor report, double lr, double beta1, double beta2, double eps, double wd,
+                     double clip, int64_t step, int64_t decay_numel, int64_t epoch, double limit_s, int64_t blocks) {
+  need((int64_t)grads.size() == world && (int64_t)params.size() == world && (int64_t)shadows.size() == world &&
+           (int64_t)sigs.size() == world, "one pointer per rank");
+  need(m.numel() == n && v.numel() == n && m.is_cuda() && m.scalar_type() == at::kFloat, "moment buffers");
+  std::vector<float*> g(world), p(world);
+  std::vector<void*> sh(world);
+  std::vector<unsigned*> sg(world);
+  for (int q = 0; q < world; ++q) {
+    g[q] = reinterpret_cast<float*>(grads[q]);
+    p[q] = reinterpret_cast<float*>(params[q]);
+    sh[q] = reinterpret_cast<void*>(shadows[q]);
+    sg[q] = reinterpret_cast<unsigned*>(sigs[q]);
+  }
+  c10::cuda::CUDAGuard guard(m.device());
+  check_cuda(rt_exchange_update(g.data(), p.data(), sh.data(), sg.data(), (int)rank, (int)world, n, FPTR(m), FPTR(v),
+                                FPTR(stats), FPTR(report), lr, beta1, beta2, eps, wd, clip, (int)step, decay_numel,
+                                (unsigned)epoch, limit_s, (int)blocks, stream_of(m)),
+             "exchange_update");
+}
+py::tuple ipc_export(at::Tensor t) {
+  need(t.is_cuda(), "ipc_export needs a CUDA tensor");
+  c10::cuda::CUDAGuard guard(t.device());
+  char handle[64];
+  long offset = 0;
+  check_cuda(rt_ipc_export(t.data_ptr(), handle, &offset), "ipc_export");
+  return py::make_tuple(py::bytes(handle, 64), (int64_t)offset);
+}
+int64_t ipc_open(py::bytes handle, int64_t device) {
+  std::string h = handle;
+  need(h.size() == 64, "IPC handle size");
+  c10::cuda::CUDAGuard guard((c10::DeviceIndex)device);
+  void* base = nullptr;
+  check_cuda(rt_ipc_open(h.data(), &base), "ipc_open");
+  return reinterpret_cast<int64_t>(base);
+}
+void ipc_close(int64_t base, int64_t device) {
+  c10::cuda::CUDAGuard guard((c10::DeviceIndex)device);
+  check_cuda(rt_ipc_close(reinterpret_cast<void*>(base)), "ipc_close");
+}
+std::vector<int64_t> exchange_shard(int64_t n, int64_t rank, int64_t world) {
+  long out[4];
+  rt_exchange_shard(n, (int)rank, (int)world, out);
+  return {out[0], out[1], out[2], out[3]};
+}
+
 // q [B,T,Hq,256]; keys/values [B,cap,Hkv,256]; gate rows: qg [B*T, Hq*512] with the gate in the second half of
 // every head's 512 values. Returns [B,T,Hq,256] bf16.
 at::Tensor flash_attention(at::Tensor q, at::Tensor keys, at::Tensor values, at::Tensor qg, int64_t offset) {
@@ -390,5 +440,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flat_adamw", &flat_adamw);
   m.def("to_bf16_", &to_bf16_);
   m.def("flash_attention", &flash_attention);
+  m.def("exchange_update", &exchange_update, "peer-memory reduce-scatter + clip + AdamW + all-gather of one layer");
+  m.def("exchange_shard", &exchange_shard);
+  m.def("exchange_signal_words", []() { return rt_exchange_signal_words(); });
+  m.def("ipc_export", &ipc_export);
+  m.def("ipc_open", &ipc_open);
+  m.def("ipc_close", &ipc_close);
   m.def("wkv7_chunk_len", []() { return rt_wkv7_chunk_len(); });
 }

@@ -30,7 +30,7 @@ from safetensors.torch import load_file, save_file
 from .data import digest_file
 
 MUTABLE_KEYS = {"output", "log_interval", "checkpoint_interval", "validation_interval", "timeout_minutes",
-                "lr", "warmup_steps", "constant_steps", "min_lr", "fused_optimizer"}
+                "lr", "warmup_steps", "constant_steps", "min_lr", "fused_optimizer", "grad_sync"}
 
 
 def cpu_tree(obj):
@@ -106,6 +106,9 @@ def save_checkpoint(topo, cfg, step, complete, order, runner, reader, base_id, s
             shutil.rmtree(temp)
         (temp / "ranks").mkdir(parents=True)
     topo.barrier()
+    topo.join_grad_sync()
+    for s in students.values():
+        s.sync_state()
     local = {"runner": runner.state_dict(), "reader": reader.state_dict() if reader else None, "rng": rng_state(),
              "students": {layer: s.state for layer, s in students.items()}}
     torch.save(cpu_tree(local), temp / "ranks" / f"rank_{topo.rank:05d}.pt")

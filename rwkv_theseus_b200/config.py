@@ -12,6 +12,10 @@ Two optional keys are added on top of the reference schema (both default to
   Small fixtures (rank 8) need them.
 * ``fused_optimizer`` selects the flat-buffer fused clip+AdamW kernels on CUDA
   (default ``True``); ``False`` uses ``torch.optim.AdamW(fused=True)``.
+* ``grad_sync`` picks the multi-GPU gradient path of the fused optimizer:
+  ``"peer"`` (default; one-node NVLink peer-memory exchange with sharded
+  AdamW, ``parallel/grad_sync.py``) or ``"nccl"`` (all-reduce, then the
+  full update on every rank, as the reference does).
 """
 import json
 from pathlib import Path
@@ -32,6 +36,7 @@ DEFAULTS = {
     "distributed_backend": "nccl", "timeout_minutes": 60,
     # Extensions (not in the reference schema; defaults keep reference behaviour).
     "lora_rank": None, "gate_lora_rank": None, "fused_optimizer": True,
+    "grad_sync": "peer",
 }
 
 _POSITIVE_INTS = ("chunk_tokens", "context_tokens", "grad_accum_steps", "micro_batch_size",
@@ -85,6 +90,8 @@ def _check(cfg):
             raise ValueError(f"{name} must be null or a positive integer")
     if not isinstance(cfg["fused_optimizer"], bool):
         raise ValueError("fused_optimizer must be a boolean")
+    if cfg["grad_sync"] not in ("peer", "nccl"):
+        raise ValueError("grad_sync must be peer or nccl")
 
 
 def load_config(path):

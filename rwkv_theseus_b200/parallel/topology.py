@@ -137,6 +137,15 @@ class Topology:
         self.assert_same(digest.hexdigest(), "promoted weights")
         return result
 
+    def join_grad_sync(self):
+        """Make the current stream wait for any in-flight peer exchange."""
+        if self._grad_sync is not None:
+            self._grad_sync.wait()
+
+    def check_grad_sync(self):
+        if self._grad_sync is not None:
+            self._grad_sync.check()
+
     def grad_sync(self):
         """Lazily created peer-memory gradient exchange (NCCL, one node, world > 1)."""
         if self._grad_sync is None and self.world > 1 and self.backend == "nccl" and self.single_node:

@@ -114,14 +114,18 @@ class Student:
     def current_lr(self):
         return self.cfg["lr"] * lr_factor(self.steps_done, self.cfg, self.total_steps)
 
+    def _exchange(self):
+        """The peer-memory exchange when it applies (CUDA, fused optimizer, one node, world > 1)."""
+        if self.topo.world == 1 or self.fused is None or self.cfg.get("grad_sync", "peer") != "peer":
+            return None
+        return self.topo.grad_sync()
+
     def reduce(self):
-        """Sum gradients and loss statistics over ranks (one bucket per layer)."""
+        """Sum gradients and loss statistics over ranks (one bucket per layer).
+
+        With the peer-memory exchange the reduction is part of ``update``."""
         topo = self.topo
-        if topo.world == 1:
-            return
-        sync = topo.grad_sync()
-        if sync is not None:
-            sync.all_reduce_(self.flat.grad, self.stats)
+        if topo.world == 1 or self._exchange() is not None:
             return
         import torch.distributed as dist
         dist.all_reduce(self.flat.grad, group=topo.student_group)
@@ -132,13 +136,23 @@ class Student:
         """Scale by 1/count, clip, AdamW, clear gradients; stats go to ``report``."""
         lr = self.current_lr()
         self.steps_done += 1
-        cfg = self.cfg
+        exchange = self._exchange()
+        if exchange is not None:
+            # Reduce-scatter, clip, AdamW on this rank's shard, all-gather; clears grad and stats on its stream.
+            exchange.update(self, lr, self.steps_done)
+            return lr
         if self.fused is not None:
             self.fused.update(lr, self.steps_done)
         else:
             self._update_reference(lr, self.steps_done)
         self.stats.zero_()
         return lr
+
+    def sync_state(self):
+        """Collective before a checkpoint: complete Adam moments on every rank."""
+        exchange = self._exchange()
+        if exchange is not None:
+            exchange.gather_moments(self)
 
     def _update_reference(self, lr, step):
         cfg, flat = self.cfg, self.flat

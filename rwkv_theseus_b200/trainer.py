@@ -92,11 +92,13 @@ class StepEngine:
                 if last:
                     student.reduce()
                     student.update()
+        self.topo.join_grad_sync()
         return {layer: s.report for layer, s in self.students.items()}
 
     def read_metrics(self, reports):
         """One device-to-host copy of all layer reports; raises on update errors."""
         rows = torch.stack([reports[layer] for layer in self.order]).double().cpu().tolist()
+        self.topo.check_grad_sync()
         layer_metrics = {}
         for layer, (nmse, cos, count, norm, bad) in zip(self.order, rows):
             if count <= 0:
