@@ -11,14 +11,18 @@
 //      (per-block partials summed in a fixed order by the last block, which
 //      publishes the rank's partial norm and loss statistics into every
 //      rank's slot array and raises its flag there);
-//   B  update + all-gather: after every rank's norm is published, each rank
-//      forms the same global norm (fixed summation order), clips, applies
-//      AdamW to its shard, and stores the new fp32 parameters and their bf16
-//      copy into every rank's buffers (peer stores); it then clears its whole
-//      local gradient (all peers have finished reading it) and its loss
-//      statistics, writes the report and raises its "done" flag everywhere;
-//   C  one warp waits until every rank is done, so later work on the stream
-//      sees the complete parameters.
+//   B  update: after every rank's norm is published, each rank forms the
+//      same global norm (fixed summation order), clips, applies AdamW to its
+//      shard (fp32 master, moments, bf16 weight copy; local memory only),
+//      clears its whole local gradient (all peers have finished reading it)
+//      and its loss statistics, writes the report and raises its "shard
+//      updated" flag everywhere;
+//   C  all-gather: after every rank's flag, each rank pulls the other shards
+//      of the bf16 weight copy and of the fp32 non-decay parameters (read in
+//      fp32 by the forward) with peer loads. The fp32 masters of the four
+//      decay matrices stay sharded (only the bf16 copy is used for compute)
+//      and are gathered for checkpoints. NVLink bytes per rank and direction:
+//      (N-1)/N * (4 + 2) bytes per parameter.
 //
 // Flags are epoch numbers (monotonic per exchange, no reset). Every wait is
 // bounded by %globaltimer; on expiry the kernel records a status word that
@@ -31,12 +35,13 @@ namespace {
 using bf16 = __nv_bfloat16;
 constexpr int MAXR = 8;
 constexpr int THREADS = 512;
+constexpr int THREADS_B = 256;  // update kernel: 4x the grid of the copy kernels
 
 // Signal-buffer layout (32-bit words) of every rank.
 constexpr int ARRIVE = 0;      // [MAXR] epoch of rank q's "gradients ready"
 constexpr int NORMF = 8;       // [MAXR] epoch of rank q's published partial norm
-constexpr int DONE = 16;       // [MAXR] epoch of rank q's finished parameter stores
-constexpr int STATUS = 24;     // nonzero after a timed-out wait: 1 = arrive, 2 = norm, 3 = done
+constexpr int DONE = 16;       // [MAXR] epoch of rank q's updated shard
+constexpr int STATUS = 24;     // nonzero after a timed-out wait: 1 = arrive, 2 = norm, 3 = updated shard
 constexpr int COUNT_A = 25;    // block completion counters (local)
 constexpr int COUNT_B = 26;
 constexpr int WAITED = 27;     // rank whose flag was missing at the timeout
@@ -91,9 +96,12 @@ RT_DEVICE bool wait_all(unsigned* sig, int base, int world, unsigned epoch, unsi
 RT_DEVICE float block_sum(float v, float* scratch) { return rt::block_sum(v, scratch); }
 
 // ---------------------------------------------------------------- A: reduce-scatter + norm
+template <int W>
 __global__ void __launch_bounds__(THREADS)
-exchange_reduce_kernel(Peers peers, int rank, int world, long lo4, long hi4, long tail_lo, long tail_hi,
+exchange_reduce_kernel(Peers peers, int rank, long lo4, long hi4, long tail_lo, long tail_hi,
                        const float* __restrict__ stats, unsigned epoch, unsigned long long limit_ns) {
+  constexpr int world = W;
+  constexpr int UNROLL = W <= 2 ? 8 : (W <= 4 ? 4 : 2);
   __shared__ float scratch[32];
   __shared__ int ok;
   unsigned* sig = peers.sig[rank];
@@ -103,17 +111,28 @@ exchange_reduce_kernel(Peers peers, int rank, int world, long lo4, long hi4, lon
   if (!ok) return;
   float acc = 0.f;
   float4* mine = reinterpret_cast<float4*>(peers.grad[rank]);
-  for (long i = lo4 + (long)blockIdx.x * THREADS + threadIdx.x; i < hi4; i += (long)gridDim.x * THREADS) {
-    float4 v[MAXR];
+  // UNROLL independent float4 per thread and rank in flight: NVLink loads need ~1-2 us of latency hidden.
+  const long stride = (long)gridDim.x * THREADS;
+  for (long i0 = lo4 + (long)blockIdx.x * THREADS + threadIdx.x; i0 < hi4; i0 += UNROLL * stride) {
+    float4 v[UNROLL][W];
 #pragma unroll
-    for (int q = 0; q < MAXR; ++q)
-      if (q < world) v[q] = reinterpret_cast<const float4*>(peers.grad[q])[i];
-    float4 s = v[0];
+    for (int u = 0; u < UNROLL; ++u) {
+      const long i = i0 + u * stride;
 #pragma unroll
-    for (int q = 1; q < MAXR; ++q)
-      if (q < world) { s.x += v[q].x; s.y += v[q].y; s.z += v[q].z; s.w += v[q].w; }
-    mine[i] = s;
-    acc += s.x * s.x + s.y * s.y + s.z * s.z + s.w * s.w;
+      for (int q = 0; q < W; ++q)
+        if (i < hi4) v[u][q] = __ldcg(reinterpret_cast<const float4*>(peers.grad[q]) + i);
+    }
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) {
+      const long i = i0 + u * stride;
+      if (i < hi4) {
+        float4 s = v[u][0];
+#pragma unroll
+        for (int q = 1; q < W; ++q) { s.x += v[u][q].x; s.y += v[u][q].y; s.z += v[u][q].z; s.w += v[u][q].w; }
+        mine[i] = s;
+        acc += s.x * s.x + s.y * s.y + s.z * s.z + s.w * s.w;
+      }
+    }
   }
   for (long i = tail_lo + (long)blockIdx.x * THREADS + threadIdx.x; i < tail_hi; i += (long)gridDim.x * THREADS) {
     float s = 0.f;
@@ -155,10 +174,13 @@ RT_DEVICE float adam_one(float g, float& p, float& m, float& v, long i, const Ad
   return p;
 }
 
-__global__ void __launch_bounds__(THREADS)
-exchange_update_kernel(Peers peers, int rank, int world, long n, long lo4, long hi4, long tail_lo, long tail_hi,
+template <int W>
+__global__ void __launch_bounds__(THREADS_B)
+exchange_update_kernel(Peers peers, int rank, long n, long lo4, long hi4, long tail_lo, long tail_hi,
                        float* __restrict__ m, float* __restrict__ v, float* __restrict__ stats,
                        float* __restrict__ report, Adam a, unsigned epoch, unsigned long long limit_ns) {
+  constexpr int world = W;
+  constexpr int UNROLL = 2;  // 8 independent 16-byte loads in flight per thread
   __shared__ int ok;
   unsigned* sig = peers.sig[rank];
   if (threadIdx.x == 0) ok = wait_all(sig, NORMF, world, epoch, limit_ns, 2);
@@ -176,49 +198,63 @@ exchange_update_kernel(Peers peers, int rank, int world, long n, long lo4, long 
   const float norm = sqrtf(norm2) * inv;
   const float gscale = inv * fminf(1.f, a.clip / (norm + 1e-6f));
   const float step = a.lr / a.bias1;
-  float* p = peers.param[rank];
-  float* g = peers.grad[rank];
-  for (long i = lo4 + (long)blockIdx.x * THREADS + threadIdx.x; i < hi4; i += (long)gridDim.x * THREADS) {
-    const float4 g4 = reinterpret_cast<const float4*>(g)[i];
-    reinterpret_cast<float4*>(g)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    float4 p4 = reinterpret_cast<const float4*>(p)[i];
-    float4 m4 = reinterpret_cast<const float4*>(m)[i];
-    float4 v4 = reinterpret_cast<const float4*>(v)[i];
-    const long e = 4 * i;
-    adam_one(g4.x * gscale, p4.x, m4.x, v4.x, e + 0, a, step);
-    adam_one(g4.y * gscale, p4.y, m4.y, v4.y, e + 1, a, step);
-    adam_one(g4.z * gscale, p4.z, m4.z, v4.z, e + 2, a, step);
-    adam_one(g4.w * gscale, p4.w, m4.w, v4.w, e + 3, a, step);
-    reinterpret_cast<float4*>(m)[i] = m4;
-    reinterpret_cast<float4*>(v)[i] = v4;
-    __nv_bfloat162 lo = __floats2bfloat162_rn(p4.x, p4.y), hi = __floats2bfloat162_rn(p4.z, p4.w);
-    uint2 packed;
-    packed.x = *reinterpret_cast<unsigned*>(&lo);
-    packed.y = *reinterpret_cast<unsigned*>(&hi);
+  float4* __restrict__ p4s = reinterpret_cast<float4*>(peers.param[rank]);
+  float4* __restrict__ g4s = reinterpret_cast<float4*>(peers.grad[rank]);
+  float4* __restrict__ m4s = reinterpret_cast<float4*>(m);
+  float4* __restrict__ v4s = reinterpret_cast<float4*>(v);
+  uint2* __restrict__ sh2 = reinterpret_cast<uint2*>(peers.shadow[rank]);
+  const long stride = (long)gridDim.x * THREADS_B;
+  for (long i0 = lo4 + (long)blockIdx.x * THREADS_B + threadIdx.x; i0 < hi4; i0 += UNROLL * stride) {
+    float4 g4[UNROLL], p4[UNROLL], m4[UNROLL], v4[UNROLL];
 #pragma unroll
-    for (int q = 0; q < MAXR; ++q) {
-      if (q < world) {
-        reinterpret_cast<float4*>(peers.param[q])[i] = p4;
-        reinterpret_cast<uint2*>(peers.shadow[q])[i] = packed;
+    for (int u = 0; u < UNROLL; ++u) {
+      const long i = i0 + u * stride;
+      if (i < hi4) {
+        g4[u] = __ldcs(g4s + i);
+        p4[u] = p4s[i];
+        m4[u] = __ldcs(m4s + i);
+        v4[u] = __ldcs(v4s + i);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) {
+      const long i = i0 + u * stride;
+      if (i < hi4) {
+        const long e = 4 * i;
+        adam_one(g4[u].x * gscale, p4[u].x, m4[u].x, v4[u].x, e + 0, a, step);
+        adam_one(g4[u].y * gscale, p4[u].y, m4[u].y, v4[u].y, e + 1, a, step);
+        adam_one(g4[u].z * gscale, p4[u].z, m4[u].z, v4[u].z, e + 2, a, step);
+        adam_one(g4[u].w * gscale, p4[u].w, m4[u].w, v4[u].w, e + 3, a, step);
+        __stcs(g4s + i, make_float4(0.f, 0.f, 0.f, 0.f));
+        __stcs(m4s + i, m4[u]);
+        __stcs(v4s + i, v4[u]);
+        p4s[i] = p4[u];
+        __nv_bfloat162 lo = __floats2bfloat162_rn(p4[u].x, p4[u].y), hi = __floats2bfloat162_rn(p4[u].z, p4[u].w);
+        uint2 packed;
+        packed.x = *reinterpret_cast<unsigned*>(&lo);
+        packed.y = *reinterpret_cast<unsigned*>(&hi);
+        sh2[i] = packed;
       }
     }
   }
-  for (long i = tail_lo + (long)blockIdx.x * THREADS + threadIdx.x; i < tail_hi; i += (long)gridDim.x * THREADS) {
+  float* p = peers.param[rank];
+  float* g = peers.grad[rank];
+  bf16* sh = peers.shadow[rank];
+  for (long i = tail_lo + (long)blockIdx.x * THREADS_B + threadIdx.x; i < tail_hi; i += stride) {
     float pv = p[i], mv = m[i], vv = v[i];
     adam_one(g[i] * gscale, pv, mv, vv, i, a, step);
     g[i] = 0.f;
     m[i] = mv;
     v[i] = vv;
-    for (int q = 0; q < world; ++q) {
-      peers.param[q][i] = pv;
-      peers.shadow[q][i] = __float2bfloat16_rn(pv);
-    }
+    p[i] = pv;
+    sh[i] = __float2bfloat16_rn(pv);
   }
   // Clear the rest of the local gradient: every peer has finished reading it (their norms are published).
-  for (long i = (long)blockIdx.x * THREADS + threadIdx.x; i < n / 4; i += (long)gridDim.x * THREADS)
-    if (i < lo4 || i >= hi4) reinterpret_cast<float4*>(g)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (long i = (n / 4) * 4 + (long)blockIdx.x * THREADS + threadIdx.x; i < tail_lo; i += (long)gridDim.x * THREADS)
-    g[i] = 0.f;
+  for (long i = (long)blockIdx.x * THREADS_B + threadIdx.x; i < lo4; i += stride)
+    __stcs(g4s + i, make_float4(0.f, 0.f, 0.f, 0.f));
+  for (long i = hi4 + (long)blockIdx.x * THREADS_B + threadIdx.x; i < n / 4; i += stride)
+    __stcs(g4s + i, make_float4(0.f, 0.f, 0.f, 0.f));
+  for (long i = (n / 4) * 4 + (long)blockIdx.x * THREADS_B + threadIdx.x; i < tail_lo; i += stride) g[i] = 0.f;
   if (blockIdx.x == 0 && threadIdx.x == 0) {
     report[0] = s0;
     report[1] = s1;
@@ -227,11 +263,11 @@ exchange_update_kernel(Peers peers, int rank, int world, long n, long lo4, long 
     report[4] = (!isfinite(norm) || count <= 0.f) ? 1.f : 0.f;
     stats[0] = stats[1] = stats[2] = 0.f;
   }
-  __threadfence_system();
+  __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
     const unsigned done = atomicAdd(sig + COUNT_B, 1u);
-    if (done == gridDim.x - 1) {
+    if (done == gridDim.x - 1) {  // last block: this rank's shard is final; peers may pull it
       __threadfence_system();
       for (int q = 0; q < world; ++q) st_release_sys(peers.sig[q] + DONE + rank, epoch);
       sig[COUNT_B] = 0;
@@ -239,17 +275,67 @@ exchange_update_kernel(Peers peers, int rank, int world, long n, long lo4, long 
   }
 }
 
-// ---------------------------------------------------------------- C: wait for every rank's stores
-__global__ void exchange_wait_kernel(unsigned* sig, int world, unsigned epoch, unsigned long long limit_ns) {
-  if (threadIdx.x == 0) wait_all(sig, DONE, world, epoch, limit_ns, 3);
+// ---------------------------------------------------------------- C: all-gather by pulling peers' shards
+// Pulls every other rank's updated shard of the bf16 weight copy (16-byte loads, UNROLL in flight per thread)
+// and the fp32 parameters of the non-decay range [decay4 * 4, n) (small vectors and LoRA factors read in fp32 by
+// the forward). The decay-group fp32 masters stay sharded until gather_state. No completion flags are needed:
+// a peer changes its shard again only in its next update of this layer, which waits for this rank's next norm.
+template <int W>
+__global__ void __launch_bounds__(THREADS)
+exchange_gather_kernel(Peers peers, int rank, long n, long n8, long decay4, unsigned epoch,
+                       unsigned long long limit_ns) {
+  constexpr int UNROLL = 8;
+  __shared__ int ok;
+  unsigned* sig = peers.sig[rank];
+  if (threadIdx.x == 0) ok = wait_all(sig, DONE, W, epoch, limit_ns, 3);
+  __syncthreads();
+  if (!ok) return;
+  const long stride = (long)gridDim.x * THREADS;
+  const long t0 = (long)blockIdx.x * THREADS + threadIdx.x;
+  // bf16 copy: concatenated index space over the W-1 peer shards (units of 8 elements)
+#pragma unroll 1
+  for (int k = 1; k < W; ++k) {
+    const int q = (rank + k) % W;
+    const long lo = n8 * q / W, hi = n8 * (q + 1) / W;
+    const uint4* src = reinterpret_cast<const uint4*>(peers.shadow[q]);
+    uint4* dst = reinterpret_cast<uint4*>(peers.shadow[rank]);
+    for (long i0 = lo + t0; i0 < hi; i0 += UNROLL * stride) {
+      uint4 r[UNROLL];
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u)
+        if (i0 + u * stride < hi) r[u] = __ldcg(src + i0 + u * stride);
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u)
+        if (i0 + u * stride < hi) dst[i0 + u * stride] = r[u];
+    }
+    // fp32 parameters of the non-decay range inside shard q (units of 4 elements)
+    const long flo = lo * 2 > decay4 ? lo * 2 : decay4, fhi = hi * 2;
+    const float4* fsrc = reinterpret_cast<const float4*>(peers.param[q]);
+    float4* fdst = reinterpret_cast<float4*>(peers.param[rank]);
+    for (long i0 = flo + t0; i0 < fhi; i0 += UNROLL * stride) {
+      float4 r[UNROLL];
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u)
+        if (i0 + u * stride < fhi) r[u] = __ldcg(fsrc + i0 + u * stride);
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u)
+        if (i0 + u * stride < fhi) fdst[i0 + u * stride] = r[u];
+    }
+  }
+  if (rank != W - 1) {  // scalar tail [8 * n8, n), owned by the last rank
+    for (long i = 8 * n8 + t0; i < n; i += stride) {
+      peers.shadow[rank][i] = peers.shadow[W - 1][i];
+      peers.param[rank][i] = peers.param[W - 1][i];
+    }
+  }
 }
 
-// Shard of rank r in float4 units plus the scalar tail (owned by the last rank).
+// Shard of rank r: float4 body [lo4, hi4) in units of 8 elements, plus the scalar tail (owned by the last rank).
 void shard(long n, int rank, int world, long& lo4, long& hi4, long& tail_lo, long& tail_hi) {
-  const long n4 = n / 4;
-  lo4 = n4 * rank / world;
-  hi4 = n4 * (rank + 1) / world;
-  tail_lo = rank == world - 1 ? n4 * 4 : n;
+  const long n8 = n / 8;
+  lo4 = 2 * (n8 * rank / world);
+  hi4 = 2 * (n8 * (rank + 1) / world);
+  tail_lo = rank == world - 1 ? n8 * 8 : n;
   tail_hi = n;
 }
 
@@ -274,24 +360,39 @@ extern "C" cudaError_t rt_exchange_update(float* const* grads, float* const* par
     peers.shadow[q] = reinterpret_cast<bf16*>(shadows[q]);
     peers.sig[q] = sigs[q];
     if ((reinterpret_cast<uintptr_t>(grads[q]) | reinterpret_cast<uintptr_t>(params[q])) & 15 ||
-        reinterpret_cast<uintptr_t>(shadows[q]) & 7)
+        reinterpret_cast<uintptr_t>(shadows[q]) & 15)
       return cudaErrorMisalignedAddress;
   }
   long lo4, hi4, tail_lo, tail_hi;
   shard(n, rank, world, lo4, hi4, tail_lo, tail_hi);
   const unsigned long long limit_ns = (unsigned long long)(limit_s * 1e9);
-  exchange_reduce_kernel<<<blocks, THREADS, 0, s>>>(peers, rank, world, lo4, hi4, tail_lo, tail_hi, stats, epoch,
-                                                     limit_ns);
-  RT_CUDA_CHECK(cudaGetLastError());
   Adam a;
   a.lr = lr; a.beta1 = beta1; a.beta2 = beta2; a.eps = eps; a.weight_decay = weight_decay; a.clip = clip;
   a.bias1 = (float)(1.0 - pow((double)beta1, (double)step));
   a.bias2_sqrt = (float)sqrt(1.0 - pow((double)beta2, (double)step));
   a.decay_numel = decay_numel;
-  exchange_update_kernel<<<blocks, THREADS, 0, s>>>(peers, rank, world, n, lo4, hi4, tail_lo, tail_hi, m, v, stats,
-                                                     report, a, epoch, limit_ns);
-  RT_CUDA_CHECK(cudaGetLastError());
-  exchange_wait_kernel<<<1, 32, 0, s>>>(sigs[rank], world, epoch, limit_ns);
+  const long n8 = n / 8, decay4 = decay_numel / 4;
+  switch (world) {
+#define RT_EXCHANGE_CASE(W)                                                                                        \
+  case W:                                                                                                          \
+    exchange_reduce_kernel<W><<<blocks, THREADS, 0, s>>>(peers, rank, lo4, hi4, tail_lo, tail_hi, stats, epoch,   \
+                                                         limit_ns);                                                \
+    RT_CUDA_CHECK(cudaGetLastError());                                                                             \
+    exchange_update_kernel<W><<<4 * blocks, THREADS_B, 0, s>>>(peers, rank, n, lo4, hi4, tail_lo, tail_hi, m, v, stats, \
+                                                         report, a, epoch, limit_ns);                              \
+    RT_CUDA_CHECK(cudaGetLastError());                                                                             \
+    exchange_gather_kernel<W><<<blocks, THREADS, 0, s>>>(peers, rank, n, n8, decay4, epoch, limit_ns);             \
+    break;
+    RT_EXCHANGE_CASE(1)
+    RT_EXCHANGE_CASE(2)
+    RT_EXCHANGE_CASE(3)
+    RT_EXCHANGE_CASE(4)
+    RT_EXCHANGE_CASE(5)
+    RT_EXCHANGE_CASE(6)
+    RT_EXCHANGE_CASE(7)
+    RT_EXCHANGE_CASE(8)
+#undef RT_EXCHANGE_CASE
+  }
   return cudaGetLastError();
 }
 

@@ -6,17 +6,18 @@ clips and steps torch AdamW over the whole layer on every rank
 layer (fp32 gradient, fp32 parameters, bf16 weight copy) and one small signal
 buffer per rank are mapped into every other rank's address space with CUDA
 IPC, and ``exchange_update`` (``csrc/parallel/peer_exchange.cu``) runs the
-whole update as three kernels: reduce-scatter with the squared norm, then
-clip + AdamW on this rank's 1/N shard with the new parameters stored straight
-into every rank's buffers, then a bounded wait for all ranks. The global norm
-and loss statistics are summed in rank order on every rank, so all ranks
-apply the identical clip coefficient.
+whole update as three kernels: reduce-scatter with the squared norm (peer
+loads), then clip + AdamW on this rank's 1/N shard (local), then an
+all-gather that pulls the other shards of the bf16 weight copy and of the
+fp32 non-decay parameters. The global norm and loss statistics are summed in
+rank order on every rank, so all ranks apply the identical clip coefficient.
 
 The kernels run on a side stream: the main stream continues with the next
 layer's student while the exchange of this one moves over NVLink, and
 ``wait`` joins the streams before the parameters are used again (the next
-step). Adam moments are sharded (each rank updates only its own range);
-``gather_moments`` assembles the full moments for a checkpoint.
+step). The fp32 masters of the four decay matrices and the Adam moments are
+sharded (each rank updates only its own range; compute reads the bf16 copy);
+``gather_state`` assembles them on every rank for a checkpoint or export.
 
 Every device wait is bounded (``limit_s``); an expired wait records a status
 that ``check`` turns into an exception on the host.
@@ -27,7 +28,7 @@ import torch.distributed as dist
 from ..ops import native
 
 STATUS_WORD, WAITED_WORD = 24, 27
-_WHAT = {1: "gradients ready", 2: "partial norm", 3: "parameter stores"}
+_WHAT = {1: "gradients ready", 2: "partial norm", 3: "updated shard"}
 
 
 class PeerGradExchange:
@@ -44,7 +45,6 @@ class PeerGradExchange:
         self.stream = torch.cuda.Stream(self.device)
         self.epoch = 0
         self._opened = {}   # (rank, peer allocation base) -> mapped base address
-        self._layers = {}   # id(student) -> (grads, params, shadows)
         self.sig_ptrs = self.share(self.sig)
         self.pending = False
 
@@ -66,16 +66,21 @@ class PeerGradExchange:
         return out
 
     def register(self, student):
-        key = id(student)
-        if key not in self._layers:
-            flat = student.flat
-            self._layers[key] = (self.share(flat.grad), self.share(flat.param), self.share(student.fused.shadow))
-        return self._layers[key]
+        """Collective (same students in the same order on every rank): map the student's buffers.
+
+        The address tables are kept on the student object, so an exchange never runs on the addresses of
+        another (possibly freed) student's buffers."""
+        flat = student.flat
+        student.peer_tables = (self.share(flat.grad), self.share(flat.param), self.share(student.fused.shadow))
+        return student.peer_tables
 
     # ---------------------------------------------------------------- update
     def update(self, student, lr, step):
         """Reduce, clip, AdamW and all-gather one layer on the side stream."""
-        grads, params, shadows = self.register(student)
+        tables = getattr(student, "peer_tables", None)
+        if tables is None:
+            raise RuntimeError("student buffers are not registered with the peer exchange")
+        grads, params, shadows = tables
         cfg, flat = student.cfg, student.flat
         beta1, beta2 = cfg["betas"]
         self.epoch += 1
@@ -106,20 +111,18 @@ class PeerGradExchange:
         lo, hi, tail_lo, tail_hi = native().exchange_shard(n, rank, self.world)
         return [(lo, hi), (tail_lo, tail_hi)]
 
-    def gather_moments(self, student):
-        """Collective: full Adam moments on every rank (each rank owns one shard)."""
+    def gather_state(self, student):
+        """Collective: full fp32 parameters and Adam moments on every rank (each rank owns one shard)."""
         self.wait()
         flat = student.flat
         for q in range(self.world):
             for lo, hi in self.shard(flat.numel, q):
                 if hi > lo:
-                    for buf in (flat.exp_avg, flat.exp_avg_sq):
-                        piece = buf[lo:hi]
-                        dist.broadcast(piece, src=q, group=self.topo.student_group)
+                    for buf in (flat.param, flat.exp_avg, flat.exp_avg_sq):
+                        dist.broadcast(buf[lo:hi], src=q, group=self.topo.student_group)
 
     def close(self):
         torch.cuda.synchronize(self.device)
         for base in self._opened.values():
             native().ipc_close(base, self.device.index)
         self._opened.clear()
-        self._layers.clear()

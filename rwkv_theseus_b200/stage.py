@@ -82,9 +82,13 @@ class Student:
         self.stats = torch.zeros(3, device=device)      # [sum nmse, sum cos, count] of the current update
         self.report = torch.zeros(5, device=device)     # [nmse, cos, count, grad_norm, error] of last update
         self.fused = None
+        self.sharded = False           # fp32 masters / moments hold only this rank's shard (peer exchange)
         if device.type == "cuda" and cfg.get("fused_optimizer", True):
             from .models.student_fused import FusedStudent
             self.fused = FusedStudent(self)
+        exchange = self._exchange()
+        if exchange is not None:  # collective: every rank builds the same students in the same order
+            exchange.register(self)
 
     # ---------------------------------------------------------------- forward/backward
     def micro_step(self, x, target):
@@ -140,6 +144,7 @@ class Student:
         if exchange is not None:
             # Reduce-scatter, clip, AdamW on this rank's shard, all-gather; clears grad and stats on its stream.
             exchange.update(self, lr, self.steps_done)
+            self.sharded = True
             return lr
         if self.fused is not None:
             self.fused.update(lr, self.steps_done)
@@ -149,10 +154,14 @@ class Student:
         return lr
 
     def sync_state(self):
-        """Collective before a checkpoint: complete Adam moments on every rank."""
+        """Collective before a checkpoint or export: complete fp32 parameters and Adam moments on every rank.
+
+        With the peer exchange each rank updates only its shard of the fp32 masters of the decay matrices and
+        of the moments (compute reads the all-gathered bf16 copy)."""
         exchange = self._exchange()
-        if exchange is not None:
-            exchange.gather_moments(self)
+        if exchange is not None and self.sharded:
+            exchange.gather_state(self)
+            self.sharded = False
 
     def _update_reference(self, lr, step):
         cfg, flat = self.cfg, self.flat
@@ -175,10 +184,14 @@ class Student:
 
     # ---------------------------------------------------------------- state/IO
     def weights(self):
+        if self.sharded:
+            raise RuntimeError("fp32 parameters are sharded across ranks; call sync_state() on every rank first")
         return {name: t.detach() for name, t in self.core.state_dict().items()}
 
     def optimizer_state_dict(self):
         """torch.optim.AdamW-compatible state_dict (same indices and groups)."""
+        if self.sharded:
+            raise RuntimeError("Adam moments are sharded across ranks; call sync_state() on every rank first")
         flat, cfg = self.flat, self.cfg
         state = {}
         if self.steps_done:

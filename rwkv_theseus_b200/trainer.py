@@ -241,6 +241,9 @@ def _run(cfg, resume, stop_after, tracker):
     progress.close()
     for capture in captures.values():
         capture.close()
+    topo.join_grad_sync()
+    for s in students.values():
+        s.sync_state()
     weights = {layer: cpu_tree(s.weights()) for layer, s in students.items()}
     students.clear()
     del runner, model, engine

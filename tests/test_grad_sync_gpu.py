@@ -71,6 +71,7 @@ def _match(topo):
         g = torch.Generator(device=dev).manual_seed(1000 + 17 * step + topo.rank)
         grad = torch.randn(n, device=dev, generator=g) * (0.01 if step % 2 else 3.0)  # clipped / unclipped
         stats = torch.tensor([1.5 + topo.rank, 0.25, 64.0 + 8 * topo.rank], device=dev)
+
         for s in (peer, nccl):
             s.flat.grad.copy_(grad)
             s.stats.copy_(stats)
@@ -78,13 +79,29 @@ def _match(topo):
             s.update()
         topo.join_grad_sync()
         torch.cuda.synchronize()
-        assert torch.allclose(peer.flat.param, nccl.flat.param, rtol=1e-5, atol=1e-7), step
-        assert torch.equal(peer.fused.shadow, peer.flat.param.to(torch.bfloat16)), step
+        if step == 2:
+            try:
+                peer.weights()
+            except RuntimeError as err:
+                assert "sync_state" in str(err)
+            else:
+                raise AssertionError("sharded weights must not be readable")
+        assert torch.equal(peer.fused.shadow, nccl.fused.shadow) or \
+            (peer.fused.shadow.float() - nccl.fused.shadow.float()).abs().max() <= 1e-2 * nccl.flat.param.abs().max()
+        tail = slice(peer.decay_numel, None)  # fp32 non-decay parameters are gathered every update
+        assert torch.allclose(peer.flat.param[tail], nccl.flat.param[tail], rtol=1e-5, atol=1e-7), step
+        if step == 1:
+            peer.sync_state()  # gather the sharded fp32 masters and moments mid-run; training continues
+            torch.cuda.synchronize()
+        assert torch.allclose(peer.flat.param, nccl.flat.param, rtol=1e-5, atol=1e-7) or step != 1, step
+        assert torch.equal(peer.fused.shadow, peer.flat.param.to(torch.bfloat16)) or step != 1, step
         assert torch.allclose(peer.report, nccl.report, rtol=1e-5), (step, peer.report, nccl.report)
         assert not peer.flat.grad.any() and not peer.stats.any(), step
     topo.check_grad_sync()
     peer.sync_state()
     torch.cuda.synchronize()
+    assert torch.allclose(peer.flat.param, nccl.flat.param, rtol=1e-5, atol=1e-7)
+    assert torch.equal(peer.fused.shadow, peer.flat.param.to(torch.bfloat16))
     assert torch.allclose(peer.flat.exp_avg, nccl.flat.exp_avg, rtol=1e-5, atol=1e-9)
     assert torch.allclose(peer.flat.exp_avg_sq, nccl.flat.exp_avg_sq, rtol=1e-5, atol=1e-12)
     everyone = [torch.empty_like(peer.flat.param) for _ in range(topo.world)]
@@ -110,6 +127,7 @@ def _odd(topo):
     ex = PeerGradExchange(topo, blocks=3, limit_s=30.0)
     for n, decay in ((1001, 500), (7, 3), (4096 + 2, 4096)):
         st = _fake(topo, n, decay)
+        ex.register(st)
         g0 = torch.Generator(device=dev).manual_seed(5)
         p0 = torch.randn(n, device=dev, generator=g0)
         st.flat.param.copy_(p0)
@@ -124,7 +142,7 @@ def _odd(topo):
             st.flat.grad.copy_(grads[topo.rank])
             st.stats.copy_(torch.tensor([1.0, 2.0, 10.0], device=dev))
             ex.update(st, 1e-2, step)
-            ex.wait()
+            ex.gather_state(st)
             torch.cuda.synchronize()
             count = 10.0 * topo.world
             gsum = sum(x.double().cpu() for x in grads) / count
