@@ -28,12 +28,30 @@ def timed(fn, warmup, iters):
     return sorted(out)[len(out) // 2]
 
 
+def kernel_times(fn, reps=3):
+    """Per-kernel device time (us per call) from a profiled run; not a benchmark number."""
+    from torch.profiler import ProfilerActivity, profile
+    fn()
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(reps):
+            fn()
+        torch.cuda.synchronize()
+    rows = {}
+    for evt in prof.events():
+        if evt.device_type == torch.autograd.DeviceType.CUDA:
+            rows[evt.name[:60]] = rows.get(evt.name[:60], 0.0) + evt.device_time / reps
+    for name, us in sorted(rows.items(), key=lambda kv: -kv[1]):
+        print(json.dumps({"kernel": name, "us_per_call": round(us, 1)}), flush=True)
+
+
 def main():
     p = argparse.ArgumentParser()
     p.add_argument("--T", type=int, default=1024)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--iters", type=int, default=10)
     p.add_argument("--only", default=None)
+    p.add_argument("--profile", action="store_true", help="also print per-kernel device times (profiled run)")
     a = p.parse_args()
     ext = native()
     T = a.T
@@ -43,8 +61,11 @@ def main():
         ab = torch.randn(T, 2 * Hv, device="cuda").to(torch.bfloat16)
         A_log, dt = torch.rand(Hv, device="cuda") * 3, torch.randn(Hv, device="cuda")
         state = torch.zeros(1, Hv, D, D, device="cuda")
-        ms = timed(lambda: ext.gdn_forward(qkv, ab[:, :Hv], ab[:, Hv:], A_log, dt, state, Hk, Hv, D), a.warmup, a.iters)
+        fn = lambda: ext.gdn_forward(qkv, ab[:, :Hv], ab[:, Hv:], A_log, dt, state, Hk, Hv, D)  # noqa: E731
+        ms = timed(fn, a.warmup, a.iters)
         print(json.dumps({"kernel": "gdn_forward", "T": T, "ms": ms}), flush=True)
+        if a.profile:
+            kernel_times(fn)
     if a.only in (None, "wkv"):
         B, H, N = 1, 80, 64
         xs = [torch.randn(B, T, H, N, device="cuda").to(torch.bfloat16) for _ in range(6)]

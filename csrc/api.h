@@ -37,7 +37,11 @@ cudaError_t rt_norm_rope(const void* src, long src_stride, const float* w, const
                          cudaStream_t stream);
 cudaError_t rt_copy_rows(const void* src, long src_stride, void* dst, int B, int T, long dst_batch_stride, int width,
                          cudaStream_t stream);
-long rt_gdn_workspace_floats(int B, int T, int Hk, int D);
+long rt_gdn_workspace_floats(int B, int T, int Hk, int Hv, int D, long row_stride);
+long rt_gdn_serial_workspace_floats(int B, int T, int Hk, int D);
+cudaError_t rt_gdn_forward_serial(const void* qkv, long row_stride, const void* a, const void* b, long ab_stride,
+                                  const float* A_log, const float* dt_bias, float* state, void* out, float* work,
+                                  int B, int T, int Hk, int Hv, int D, cudaStream_t stream);
 cudaError_t rt_gdn_forward(const void* qkv, long row_stride, const void* a, const void* b, long ab_stride,
                            const float* A_log, const float* dt_bias, float* state, void* out, float* work, int B,
                            int T, int Hk, int Hv, int D, cudaStream_t stream);

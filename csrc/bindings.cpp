@@ -244,7 +244,7 @@ at::Tensor gdn_forward(at::Tensor qkv, at::Tensor a, at::Tensor b, at::Tensor A_
   c10::cuda::CUDAGuard guard(qkv.device());
   const int B = qkv.size(0), T = qkv.size(1);
   TORCH_CHECK(qkv.size(2) == 2 * Hk * D + Hv * D, "qkv width mismatch");
-  auto work = at::empty({rt_gdn_workspace_floats(B, T, Hk, D)}, state.options());
+  auto work = at::empty({rt_gdn_workspace_floats(B, T, Hk, Hv, D, qkv.size(2))}, state.options());
   auto out = at::empty({B, T, Hv, D}, qkv.options());
   auto al = f32(A_log), dt = f32(dt_bias);
   check_cuda(rt_gdn_forward(qkv.data_ptr(), qkv.size(2), a.data_ptr(), b.data_ptr(), a.stride(-2), al.data_ptr<float>(),

@@ -314,10 +314,42 @@ cudaError_t launch(const void* qkv, long row_stride, const void* a, const void* 
 
 }  // namespace
 
-// Scratch floats needed by rt_gdn_forward: normalised q and k plus the Gram matrices.
-extern "C" long rt_gdn_workspace_floats(int B, int T, int Hk, int D) {
+// Long prefills take the WY path (csrc/gdn/gdn_wy.cu: state-free chunk algebra in parallel, a light serial state
+// pass); short calls (decode steps, small chunks) the serial 16-step kernel above.
+long rt_gdn_wy_workspace_floats(int B, int T, int Hk, int Hv, int D);
+cudaError_t rt_gdn_wy_forward(const void* qkv, long row_stride, const void* a, const void* b, long ab_stride,
+                              const float* A_log, const float* dt_bias, float* state, void* out, float* work, int B,
+                              int T, int Hk, int Hv, int D, cudaStream_t stream);
+
+namespace {
+constexpr int WY_MIN_T = 128;
+bool use_wy(int T, long row_stride, int D) { return T >= WY_MIN_T && (D == 64 || D == 128) && row_stride % 8 == 0; }
+}  // namespace
+
+// Scratch floats of the serial 16-step path alone.
+extern "C" long rt_gdn_serial_workspace_floats(int B, int T, int Hk, int D) {
   const long chunks = (T + L - 1) / L;
   return 2L * B * T * Hk * D + (long)B * Hk * chunks * 2 * L * L;
+}
+
+// Scratch floats needed by rt_gdn_forward for these sizes (row_stride decides the path only through alignment).
+extern "C" long rt_gdn_workspace_floats(int B, int T, int Hk, int Hv, int D, long row_stride) {
+  if (use_wy(T, row_stride, D)) return rt_gdn_wy_workspace_floats(B, T, Hk, Hv, D);
+  return rt_gdn_serial_workspace_floats(B, T, Hk, D);
+}
+
+// The serial 16-step path for any T (its scratch is rt_gdn_serial_workspace_floats).
+extern "C" cudaError_t rt_gdn_forward_serial(const void* qkv, long row_stride, const void* a, const void* b,
+                                             long ab_stride, const float* A_log, const float* dt_bias, float* state,
+                                             void* out, float* work, int B, int T, int Hk, int Hv, int D,
+                                             cudaStream_t stream) {
+  if (Hv % Hk) return cudaErrorInvalidValue;
+  switch (D) {
+    case 128: return launch<128>(qkv, row_stride, a, b, ab_stride, A_log, dt_bias, state, out, work, B, T, Hk, Hv, stream);
+    case 64: return launch<64>(qkv, row_stride, a, b, ab_stride, A_log, dt_bias, state, out, work, B, T, Hk, Hv, stream);
+    case 32: return launch<32>(qkv, row_stride, a, b, ab_stride, A_log, dt_bias, state, out, work, B, T, Hk, Hv, stream);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 // qkv: conv+SiLU output rows [B*T, row_stride] bf16 (q | k | v); a, b: [B*T, ab_stride] bf16 gate inputs;
@@ -326,10 +358,9 @@ extern "C" cudaError_t rt_gdn_forward(const void* qkv, long row_stride, const vo
                                       const float* A_log, const float* dt_bias, float* state, void* out, float* work,
                                       int B, int T, int Hk, int Hv, int D, cudaStream_t stream) {
   if (Hv % Hk) return cudaErrorInvalidValue;
-  switch (D) {
-    case 128: return launch<128>(qkv, row_stride, a, b, ab_stride, A_log, dt_bias, state, out, work, B, T, Hk, Hv, stream);
-    case 64: return launch<64>(qkv, row_stride, a, b, ab_stride, A_log, dt_bias, state, out, work, B, T, Hk, Hv, stream);
-    case 32: return launch<32>(qkv, row_stride, a, b, ab_stride, A_log, dt_bias, state, out, work, B, T, Hk, Hv, stream);
-    default: return cudaErrorInvalidValue;
-  }
+  if (use_wy(T, row_stride, D))
+    return rt_gdn_wy_forward(qkv, row_stride, a, b, ab_stride, A_log, dt_bias, state, out, work, B, T, Hk, Hv, D,
+                             stream);
+  return rt_gdn_forward_serial(qkv, row_stride, a, b, ab_stride, A_log, dt_bias, state, out, work, B, T, Hk, Hv, D,
+                               stream);
 }

@@ -1,4 +1,5 @@
-// Allocation-free Gated DeltaNet forward: rt_gdn_forward with its scratch in
+// Allocation-free Gated DeltaNet forward: the serial path of rt_gdn_forward
+// (rt_gdn_forward_serial, the one with the smallest scratch) with its scratch in
 // a file-scope device array. See gdn_noalloc.h for who needs it, the size
 // limit and the sharing rules. This entry point has no counterpart in the
 // reference project.
@@ -39,9 +40,10 @@ extern "C" cudaError_t rt_gdn_forward_noalloc(const void* qkv, long row_stride, 
                                               float* state, void* out, int B, int T, int Hk, int Hv, int D,
                                               cudaStream_t stream) {
   if (B <= 0 || T <= 0 || Hk <= 0 || Hv <= 0 || D <= 0) return cudaErrorInvalidValue;
-  if (rt_gdn_workspace_floats(B, T, Hk, D) > RT_GDN_NOALLOC_MAX_FLOATS) return cudaErrorInvalidValue;
+  if (rt_gdn_serial_workspace_floats(B, T, Hk, D) > RT_GDN_NOALLOC_MAX_FLOATS) return cudaErrorInvalidValue;
   float* work = nullptr;
   cudaError_t err = scratch_for_current_device(&work);
   if (err != cudaSuccess) return err;
-  return rt_gdn_forward(qkv, row_stride, a, b, ab_stride, A_log, dt_bias, state, out, work, B, T, Hk, Hv, D, stream);
+  return rt_gdn_forward_serial(qkv, row_stride, a, b, ab_stride, A_log, dt_bias, state, out, work, B, T, Hk, Hv, D,
+                               stream);
 }

@@ -15,7 +15,7 @@
 //
 // Limits and behaviour:
 //   * the scratch holds RT_GDN_NOALLOC_MAX_FLOATS floats (4 MiB); calls whose
-//     workspace (rt_gdn_workspace_floats(B, T, Hk, D)) exceeds it return
+//     workspace (rt_gdn_serial_workspace_floats(B, T, Hk, D)) exceeds it return
 //     cudaErrorInvalidValue before launching anything. For the 27B geometry
 //     (Hk = 16, D = 128) and B = 1 that allows T <= 226 tokens per call;
 //   * every GPU that loads this library keeps the 4 MiB array until the

@@ -1,0 +1,559 @@
+// Gated DeltaNet forward for long prefills, sm_100a: WY form with 64-token chunks.
+//
+// Recurrence (per value head, state S[key j][value i], chunk-local cumulative log-decay Lambda_t with
+// Lambda_{-1} = 0, normalised q (scaled by D^-1/2) and k):
+//   S_t = e^{g_t} S_{t-1} + k_t Vt_t^T,   Vt_t = beta_t (v_t - e^{g_t} S_{t-1}^T k_t),   o_t = S_t^T q_t.
+// Unrolling S_{t-1} inside a chunk from its start state S0 gives, with A[t][s] = beta_t e^{Lambda_t -
+// Lambda_s} (k_t . k_s) for s < t and T = (I + A)^{-1} (unit lower triangular):
+//   Vt  = U0 + W S0,            U0 = T (beta o v),   W = -T diag(beta_t e^{Lambda_t}) K        (state-free)
+//   S_L = e^{Lambda_{L-1}} S0 + sum_s e^{Lambda_{L-1} - Lambda_s} k_s Vt_s^T
+//   o_t = e^{Lambda_t} S0^T q_t + sum_{s<=t} e^{Lambda_t - Lambda_s} (q_t . k_s) Vt_s
+// Every exponent is <= 0, so large negative gates are safe. Three kernels:
+//   1 (parallel over chunks and heads)  T by blocked 16x16 inversion, U0 and W;
+//   2 (serial over chunks, parallel over heads and 32-column value blocks)  Vt = U0 + W S0, the chunk-start
+//     state is stored, S advanced -- the only sequential work is two 64x128x32 products per chunk;
+//   3 (parallel)  outputs from the stored chunk-start states and Vt.
+// Padded steps past T get beta = 0 and g = 0, so they add nothing.
+// Reference semantics: HF Qwen3_5GatedDeltaNet chunk rule (torch_chunk_gated_delta_rule), as invoked from the
+// reference's teacher adapter (theseus/hf_model.py:38-52).
+#include "../common/common.cuh"
+
+namespace rt_gdn_wy {
+
+using bf16 = __nv_bfloat16;
+constexpr int LC = 64;       // chunk length
+constexpr int NT = 256;      // threads per CTA
+constexpr int VB = 32;       // value columns per CTA in the serial kernel
+constexpr int OB = 64;       // value columns per CTA in the output kernel
+
+template <int D>
+struct Dims {
+  static constexpr int SP = D + 4;   // padded fp32 row (16-byte aligned, conflict-free float4 columns)
+};
+
+RT_DEVICE float gate_g(float a, float dtb, float neg_a) {
+  const float av = a + dtb;
+  return neg_a * (av > 20.f ? av : log1pf(expf(av)));
+}
+
+// Inclusive scan of x over 64 threads (threads 0..63 hold the values; returns the scan for those threads).
+RT_DEVICE float scan64(float x, float* tmp) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (warp == 0 && lane == 31) tmp[0] = x;
+  __syncthreads();
+  if (warp == 1) x += tmp[0];
+  return x;
+}
+
+// ---------------------------------------------------------------- 1: T, U0, W per (chunk, value head)
+// grid (chunks, Hv, B). qn/kn: [B, T, Hk, D] fp32 normalised. Writes W, U0: [B, Hv, Tp, D] fp32 and
+// lam: [B, Hv, Tp] (chunk-local cumulative log decay).
+template <int D>
+struct WySmem {
+  static constexpr int SP = Dims<D>::SP;
+  static constexpr int FLOATS = 2 * LC * SP + 2 * LC * (LC + 1) + 3 * 16 * 17 + 4 * LC + 32;
+};
+
+template <int D>
+__global__ void __launch_bounds__(NT)
+gdn_wy_kernel(const float* __restrict__ kn, const bf16* __restrict__ qkv, long row_stride, const bf16* __restrict__ pa,
+              const bf16* __restrict__ pb, long ab_stride, const float* __restrict__ A_log,
+              const float* __restrict__ dt_bias, float* __restrict__ Wout, float* __restrict__ Uout,
+              float* __restrict__ lam_out, int T, int Tp, int Hk, int Hv) {
+  constexpr int SP = Dims<D>::SP;
+  constexpr int MP = LC + 1;
+  extern __shared__ __align__(16) float sm[];
+  float* K = sm;                 // [LC][SP]  k, later diag(beta e^Lambda) k
+  float* V = K + LC * SP;        // [LC][SP]  beta v
+  float* A = V + LC * SP;        // [LC][MP]
+  float* Ti = A + LC * MP;       // [LC][MP]  (I + A)^{-1}
+  float* P = Ti + LC * MP;       // [3][16][17]  scratch blocks of the blocked inversion
+  float* lam = P + 3 * 16 * 17;  // [LC]
+  float* beta = lam + LC;        // [LC]
+  float* elam = beta + LC;       // [LC]  e^{Lambda_t}
+  float* tmp = elam + LC;
+  const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int kh = h / (Hv / Hk);
+  const int t0 = c * LC;
+  const long vcol = 2L * Hk * D + (long)h * D;
+  // k rows (fp32, cp.async) and v rows (bf16 -> fp32)
+  for (int e = threadIdx.x; e < LC * (D / 4); e += NT) {
+    const int tt = e / (D / 4), j = (e % (D / 4)) * 4, t = t0 + tt;
+    const bool ok = t < T;
+    rt::cp_async16(K + tt * SP + j, kn + (ok ? (((long)b * T + t) * Hk + kh) * D + j : 0), ok);
+  }
+  rt::cp_async_commit();
+  float g = 0.f, bt = 0.f;
+  if (threadIdx.x < LC) {
+    const int t = t0 + threadIdx.x;
+    if (t < T) {
+      g = gate_g(rt::to_f(pa[((long)b * T + t) * ab_stride + h]), dt_bias[h], -expf(A_log[h]));
+      bt = __bfloat162float(__float2bfloat16_rn(rt::sigmoidf_(rt::to_f(pb[((long)b * T + t) * ab_stride + h]))));
+    }
+  }
+  const float lt = scan64(threadIdx.x < LC ? g : 0.f, tmp);
+  if (threadIdx.x < LC) {
+    lam[threadIdx.x] = lt;
+    beta[threadIdx.x] = bt;
+    elam[threadIdx.x] = expf(lt);
+    lam_out[((long)b * Hv + h) * Tp + t0 + threadIdx.x] = lt;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < LC * (D / 8); e += NT) {
+    const int tt = e / (D / 8), i = (e % (D / 8)) * 8, t = t0 + tt;
+    float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (t < T) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(qkv + ((long)b * T + t) * row_stride + vcol + i);
+      const bf16* hv = reinterpret_cast<const bf16*>(&raw);
+      const float bv = beta[tt];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) f[u] = __bfloat162float(hv[u]) * bv;
+    }
+    *reinterpret_cast<float4*>(V + tt * SP + i) = make_float4(f[0], f[1], f[2], f[3]);
+    *reinterpret_cast<float4*>(V + tt * SP + i + 4) = make_float4(f[4], f[5], f[6], f[7]);
+  }
+  rt::cp_async_wait<0>();
+  __syncthreads();
+  // A[t][s] = beta_t e^{Lambda_t - Lambda_s} (k_t . k_s), s < t. Thread: rows t = 4*ty..+3, cols s = tx + 16*u.
+  {
+    const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
+    float acc[4][4] = {};
+    for (int j = 0; j < D; j += 4) {
+      float4 kt[4], ks[4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) kt[r] = *reinterpret_cast<const float4*>(K + (4 * ty + r) * SP + j);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) ks[u] = *reinterpret_cast<const float4*>(K + (tx + 16 * u) * SP + j);
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          acc[r][u] += kt[r].x * ks[u].x + kt[r].y * ks[u].y + kt[r].z * ks[u].z + kt[r].w * ks[u].w;
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int t = 4 * ty + r, s = tx + 16 * u;
+        A[t * MP + s] = s < t ? beta[t] * expf(lam[t] - lam[s]) * acc[r][u] : 0.f;
+      }
+  }
+  __syncthreads();
+  // Blocked inverse of the unit lower-triangular (I + A), 16x16 blocks. Diagonal blocks by forward substitution
+  // (one thread per column of each block); then block diagonals d = 1..3: T_ij = -T_ii sum_{k=j}^{i-1} A_ik T_kj.
+  if (threadIdx.x < LC) {
+    const int blk = threadIdx.x >> 4, col = threadIdx.x & 15, o = 16 * blk, s = o + col;
+    for (int t = o; t < o + 16; ++t) {
+      float v = t == s ? 1.f : 0.f;
+      if (t > s)
+        for (int r = s; r < t; ++r) v -= A[t * MP + r] * Ti[r * MP + s];
+      Ti[t * MP + s] = v;
+    }
+  }
+  // zero the strictly upper blocks
+  for (int e = threadIdx.x; e < LC * LC; e += NT) {
+    const int t = e / LC, s = e % LC;
+    if ((t >> 4) < (s >> 4)) Ti[t * MP + s] = 0.f;
+  }
+  __syncthreads();
+  for (int d = 1; d < 4; ++d) {
+    // P_ij = sum_{k=j}^{i-1} A_ik T_kj for the 4-d blocks (i, j = i-d)
+    for (int e = threadIdx.x; e < (4 - d) * 256; e += NT) {
+      const int bi = e / 256 + d, bj = bi - d, r = (e % 256) / 16, cc = e % 16;
+      const int t = 16 * bi + r, s = 16 * bj + cc;
+      float v = 0.f;
+      for (int k = 16 * bj; k < 16 * bi; ++k) v += A[t * MP + k] * Ti[k * MP + s];
+      P[(bi - d) * 272 + r * 17 + cc] = v;
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < (4 - d) * 256; e += NT) {
+      const int bi = e / 256 + d, bj = bi - d, r = (e % 256) / 16, cc = e % 16;
+      const int t = 16 * bi + r, s = 16 * bj + cc;
+      float v = 0.f;
+      for (int k = 16 * bi; k <= t; ++k) v -= Ti[t * MP + k] * P[(bi - d) * 272 + (k - 16 * bi) * 17 + cc];
+      Ti[t * MP + s] = v;
+    }
+    __syncthreads();
+  }
+  // K <- diag(beta e^Lambda) K
+  for (int e = threadIdx.x; e < LC * (D / 4); e += NT) {
+    const int tt = e / (D / 4), j = (e % (D / 4)) * 4;
+    const float f = beta[tt] * elam[tt];
+    float4 k4 = *reinterpret_cast<float4*>(K + tt * SP + j);
+    k4.x *= f; k4.y *= f; k4.z *= f; k4.w *= f;
+    *reinterpret_cast<float4*>(K + tt * SP + j) = k4;
+  }
+  __syncthreads();
+  // W = -T K', U0 = T V'. Thread: rows t = 4*ty..+3 (ty < 16), columns j = 4*tx.. (tx < 16), D / 64 passes.
+  {
+    const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
+    const long rowbase = ((long)b * Hv + h) * Tp + t0;
+    for (int jb = 0; jb < D; jb += 64) {
+      const int j = jb + 4 * tx;
+      float4 w[4], u[4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) w[r] = u[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+      const int tmax = 4 * ty + 3;
+      for (int s = 0; s <= tmax; ++s) {
+        const float4 k4 = *reinterpret_cast<const float4*>(K + s * SP + j);
+        const float4 v4 = *reinterpret_cast<const float4*>(V + s * SP + j);
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const float tv = Ti[(4 * ty + r) * MP + s];
+          w[r].x += tv * k4.x; w[r].y += tv * k4.y; w[r].z += tv * k4.z; w[r].w += tv * k4.w;
+          u[r].x += tv * v4.x; u[r].y += tv * v4.y; u[r].z += tv * v4.z; u[r].w += tv * v4.w;
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const long row = rowbase + 4 * ty + r;
+        w[r].x = -w[r].x; w[r].y = -w[r].y; w[r].z = -w[r].z; w[r].w = -w[r].w;
+        *reinterpret_cast<float4*>(Wout + row * D + j) = w[r];
+        *reinterpret_cast<float4*>(Uout + row * D + j) = u[r];
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------- 2: serial state pass
+// grid (D / VB, Hv, B). Per chunk: Vt = U0 + W S (stored over U0), chunk-start S stored to S0 [B,Hv,C,D(i),D(j)],
+// S <- e^{Lambda_{L-1}} S + sum_s e^{Lambda_{L-1} - Lambda_s} k_s Vt_s^T. The state block is value-major
+// (S[i][j]) so products over keys use float4 rows.
+template <int D>
+struct StSmem {
+  static constexpr int SP = Dims<D>::SP;
+  static constexpr int FLOATS = VB * SP + 2 * LC * SP + 2 * LC * VB + 2 * LC;
+};
+
+template <int D>
+__global__ void __launch_bounds__(NT)
+gdn_state_kernel(const float* __restrict__ kn, const float* __restrict__ W, float* __restrict__ U,
+                 const float* __restrict__ lam_in, float* __restrict__ state, float* __restrict__ S0out, int T, int Tp,
+                 int Hk, int Hv) {
+  constexpr int SP = Dims<D>::SP;
+  extern __shared__ __align__(16) float sm[];
+  float* S = sm;                  // [VB][SP]
+  float* Ws = S + VB * SP;        // [LC][SP]
+  float* Ks = Ws + LC * SP;       // [LC][SP]
+  float* Us = Ks + LC * SP;       // [LC][VB]  U0 block, then Vt
+  float* Vh = Us + LC * VB;       // [LC][VB]  e^{Lambda_L - Lambda_s} Vt
+  float* lam = Vh + LC * VB;      // [LC]
+  float* fac = lam + LC;          // [LC]
+  const int vb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int kh = h / (Hv / Hk);
+  const int col0 = vb * VB;
+  const int chunks = Tp / LC;
+  float* st = state + ((long)b * Hv + h) * D * D;  // [j][i]
+  const long rowbase = ((long)b * Hv + h) * Tp;
+  // Two cp.async groups per chunk: {W, U0 block, lam} (needed first) and {K} (needed by the state update), so
+  // K of chunk c+1 streams in during the Vt product of chunk c+1 and W of chunk c+1 during the update of chunk c.
+  auto load_w = [&](int c) {
+    for (int e = threadIdx.x; e < LC * (D / 4); e += NT) {
+      const int tt = e / (D / 4), j = (e % (D / 4)) * 4;
+      rt::cp_async16(Ws + tt * SP + j, W + (rowbase + c * LC + tt) * D + j, true);
+    }
+    for (int e = threadIdx.x; e < LC * (VB / 4); e += NT) {
+      const int tt = e / (VB / 4), i = (e % (VB / 4)) * 4;
+      rt::cp_async16(Us + tt * VB + i, U + (rowbase + c * LC + tt) * D + col0 + i, true);
+    }
+    if (threadIdx.x < LC / 4) rt::cp_async16(lam + 4 * threadIdx.x, lam_in + rowbase + c * LC + 4 * threadIdx.x, true);
+    rt::cp_async_commit();
+  };
+  auto load_k = [&](int c) {
+    for (int e = threadIdx.x; e < LC * (D / 4); e += NT) {
+      const int tt = e / (D / 4), j = (e % (D / 4)) * 4, t = c * LC + tt;
+      const bool ok = t < T;
+      rt::cp_async16(Ks + tt * SP + j, kn + (ok ? (((long)b * T + t) * Hk + kh) * D + j : 0), ok);
+    }
+    rt::cp_async_commit();
+  };
+  load_w(0);
+  load_k(0);
+  for (int e = threadIdx.x; e < D * VB; e += NT) {
+    const int j = e / VB, i = e % VB;
+    S[i * SP + j] = st[(long)j * D + col0 + i];
+  }
+  for (int c = 0; c < chunks; ++c) {
+    rt::cp_async_wait<1>();  // W, U0, lam of chunk c (K of chunk c may still be in flight)
+    __syncthreads();
+    // chunk-start state to S0 (value-major rows)
+    float* s0 = S0out + (((long)b * Hv + h) * chunks + c) * D * D;
+    for (int e = threadIdx.x; e < VB * (D / 4); e += NT) {
+      const int i = e / (D / 4), j = (e % (D / 4)) * 4;
+      *reinterpret_cast<float4*>(s0 + (long)(col0 + i) * D + j) = *reinterpret_cast<const float4*>(S + i * SP + j);
+    }
+    if (threadIdx.x < LC) fac[threadIdx.x] = expf(lam[LC - 1] - lam[threadIdx.x]);
+    const float eL = expf(lam[LC - 1]);  // read before lam is refilled for the next chunk
+    // Vt = U0 + W S: thread rows t = 4*ty..+3 (ty < 16), columns i = tx, tx + 16 (tx < 16)
+    {
+      const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
+      float acc[4][2] = {};
+      const float4* s_a = reinterpret_cast<const float4*>(S + tx * SP);
+      const float4* s_b = reinterpret_cast<const float4*>(S + (tx + 16) * SP);
+#pragma unroll 4
+      for (int q = 0; q < D / 4; ++q) {
+        const float4 a4 = s_a[q], b4 = s_b[q];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const float4 w4 = reinterpret_cast<const float4*>(Ws + (4 * ty + r) * SP)[q];
+          acc[r][0] += w4.x * a4.x + w4.y * a4.y + w4.z * a4.z + w4.w * a4.w;
+          acc[r][1] += w4.x * b4.x + w4.y * b4.y + w4.z * b4.z + w4.w * b4.w;
+        }
+      }
+      __syncthreads();  // fac visible; every thread done reading Ws
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int t = 4 * ty + r;
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          const int i = tx + 16 * k;
+          const float v = Us[t * VB + i] + acc[r][k];
+          Us[t * VB + i] = v;
+          Vh[t * VB + i] = v * fac[t];
+          U[(rowbase + c * LC + t) * D + col0 + i] = v;
+        }
+      }
+    }
+    if (c + 1 < chunks) {
+      load_w(c + 1);
+      rt::cp_async_wait<1>();  // K of chunk c
+    } else {
+      rt::cp_async_wait<0>();
+    }
+    __syncthreads();
+    // S[i][j] = e^{Lambda_L} S[i][j] + sum_t Vh[t][i] K[t][j]; thread: IPT rows i = IPT*iy.., 4 columns j = 4*jx
+    {
+      constexpr int JT = D / 4, IT = NT / JT, IPT = VB / IT;
+      const int iy = threadIdx.x / JT, jx = threadIdx.x % JT, j = 4 * jx;
+      float4 acc[IPT];
+#pragma unroll
+      for (int r = 0; r < IPT; ++r) {
+        acc[r] = *reinterpret_cast<const float4*>(S + (IPT * iy + r) * SP + j);
+        acc[r].x *= eL; acc[r].y *= eL; acc[r].z *= eL; acc[r].w *= eL;
+      }
+#pragma unroll 4
+      for (int t = 0; t < LC; ++t) {
+        const float4 k4 = *reinterpret_cast<const float4*>(Ks + t * SP + j);
+#pragma unroll
+        for (int r = 0; r < IPT; ++r) {
+          const float vv = Vh[t * VB + IPT * iy + r];
+          acc[r].x += vv * k4.x; acc[r].y += vv * k4.y; acc[r].z += vv * k4.z; acc[r].w += vv * k4.w;
+        }
+      }
+      __syncthreads();  // all reads of S and Ks done
+#pragma unroll
+      for (int r = 0; r < IPT; ++r) *reinterpret_cast<float4*>(S + (IPT * iy + r) * SP + j) = acc[r];
+    }
+    if (c + 1 < chunks) load_k(c + 1);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < D * VB; e += NT) {
+    const int j = e / VB, i = e % VB;
+    st[(long)j * D + col0 + i] = S[i * SP + j];
+  }
+}
+
+// ---------------------------------------------------------------- 3: outputs
+// grid (chunks, Hv, B * D / OB). o_t[i] = e^{Lambda_t} sum_j q_t[j] S0[i][j] + sum_{s<=t} M[t][s] Vt_s[i],
+// M[t][s] = e^{Lambda_t - Lambda_s} (q_t . k_s).
+template <int D>
+struct OutSmem {
+  static constexpr int SP = Dims<D>::SP;
+  static constexpr int OP = OB + 4;
+  static constexpr int FLOATS = 2 * LC * SP + LC * OP + LC * (LC + 1) + LC;
+};
+
+template <int D>
+__global__ void __launch_bounds__(NT)
+gdn_out_kernel(const float* __restrict__ qn, const float* __restrict__ kn, const float* __restrict__ U,
+               const float* __restrict__ lam_in, const float* __restrict__ S0, bf16* __restrict__ out, int T, int Tp,
+               int Hk, int Hv) {
+  constexpr int SP = Dims<D>::SP;
+  constexpr int OP = OutSmem<D>::OP;
+  constexpr int MP = LC + 1;
+  extern __shared__ __align__(16) float sm[];
+  float* Q = sm;                 // [LC][SP]
+  float* KS = Q + LC * SP;       // [LC][SP]  k rows, then the S0 value block (OB rows of D)
+  float* Vt = KS + LC * SP;      // [LC][OP]
+  float* M = Vt + LC * OP;       // [LC][MP]
+  float* lam = M + LC * MP;      // [LC]
+  const int c = blockIdx.x, h = blockIdx.y;
+  const int b = blockIdx.z / (D / OB), ob = blockIdx.z % (D / OB);
+  const int kh = h / (Hv / Hk);
+  const int chunks = Tp / LC;
+  const int col0 = ob * OB;
+  const long rowbase = ((long)b * Hv + h) * Tp + c * LC;
+  for (int e = threadIdx.x; e < LC * (D / 4); e += NT) {
+    const int tt = e / (D / 4), j = (e % (D / 4)) * 4, t = c * LC + tt;
+    const bool ok = t < T;
+    const long src = ok ? (((long)b * T + t) * Hk + kh) * D + j : 0;
+    rt::cp_async16(Q + tt * SP + j, qn + src, ok);
+    rt::cp_async16(KS + tt * SP + j, kn + src, ok);
+  }
+  for (int e = threadIdx.x; e < LC * (OB / 4); e += NT) {
+    const int tt = e / (OB / 4), i = (e % (OB / 4)) * 4;
+    rt::cp_async16(Vt + tt * OP + i, U + (rowbase + tt) * D + col0 + i, true);
+  }
+  if (threadIdx.x < LC / 4) rt::cp_async16(lam + 4 * threadIdx.x, lam_in + rowbase + 4 * threadIdx.x, true);
+  rt::cp_async_commit();
+  rt::cp_async_wait<0>();
+  __syncthreads();
+  {  // M, rows t = 4*ty..+3, cols s = tx + 16u
+    const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
+    float acc[4][4] = {};
+    for (int j = 0; j < D; j += 4) {
+      float4 qt[4], ks[4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) qt[r] = *reinterpret_cast<const float4*>(Q + (4 * ty + r) * SP + j);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) ks[u] = *reinterpret_cast<const float4*>(KS + (tx + 16 * u) * SP + j);
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          acc[r][u] += qt[r].x * ks[u].x + qt[r].y * ks[u].y + qt[r].z * ks[u].z + qt[r].w * ks[u].w;
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int t = 4 * ty + r, s = tx + 16 * u;
+        M[t * MP + s] = s <= t ? expf(lam[t] - lam[s]) * acc[r][u] : 0.f;
+      }
+  }
+  __syncthreads();
+  {  // S0 value block -> KS rows (value-major)
+    const float* s0 = S0 + (((long)b * Hv + h) * chunks + c) * D * D + (long)col0 * D;
+    for (int e = threadIdx.x; e < OB * (D / 4); e += NT) {
+      const int i = e / (D / 4), j = (e % (D / 4)) * 4;
+      rt::cp_async16(KS + i * SP + j, s0 + (long)i * D + j, true);
+    }
+    rt::cp_async_commit();
+    rt::cp_async_wait<0>();
+  }
+  __syncthreads();
+  {  // thread: rows t = 4*ty..+3 (ty < 16), columns i = tx + 16u (tx < 16, u < 4)
+    const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
+    float acc[4][4] = {};
+    for (int j = 0; j < D; j += 4) {
+      float4 qt[4], sv[4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) qt[r] = *reinterpret_cast<const float4*>(Q + (4 * ty + r) * SP + j);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) sv[u] = *reinterpret_cast<const float4*>(KS + (tx + 16 * u) * SP + j);
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          acc[r][u] += qt[r].x * sv[u].x + qt[r].y * sv[u].y + qt[r].z * sv[u].z + qt[r].w * sv[u].w;
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int t = 4 * ty + r;
+      const float el = expf(lam[t]);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) acc[r][u] *= el;
+      for (int s = 0; s <= t; ++s) {
+        const float m = M[t * MP + s];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) acc[r][u] += m * Vt[s * OP + tx + 16 * u];
+      }
+      const int tg = c * LC + t;
+      if (tg < T) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          out[(((long)b * T + tg) * Hv + h) * D + col0 + tx + 16 * u] = __float2bfloat16_rn(acc[r][u]);
+      }
+    }
+  }
+}
+
+// q/k normalisation: qn = q / |q| * D^-1/2, kn = k / |k| (eps 1e-6), fp32 rows [B, T, Hk, D]. grid (T, B).
+template <int D>
+__global__ void __launch_bounds__(128) gdn_norm_kernel(const bf16* __restrict__ qkv, long row_stride, int T, int Hk,
+                                                       float* __restrict__ qn, float* __restrict__ kn) {
+  const int t = blockIdx.x, b = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float scale = rsqrtf((float)D);
+  const bf16* row = qkv + ((long)b * T + t) * row_stride;
+  for (int hh = warp; hh < 2 * Hk; hh += 4) {
+    const bool is_k = hh >= Hk;
+    const int kh = is_k ? hh - Hk : hh;
+    float x[D / 32];
+    float ss = 0.f;
+#pragma unroll
+    for (int u = 0; u < D / 32; ++u) {
+      x[u] = rt::to_f(row[(long)hh * D + lane + 32 * u]);
+      ss += x[u] * x[u];
+    }
+    ss = rt::warp_sum(ss);
+    const float f = rsqrtf(ss + 1e-6f) * (is_k ? 1.f : scale);
+    float* dst = (is_k ? kn : qn) + (((long)b * T + t) * Hk + kh) * D;
+#pragma unroll
+    for (int u = 0; u < D / 32; ++u) dst[lane + 32 * u] = x[u] * f;
+  }
+}
+
+template <int D>
+long workspace(int B, int T, int Hk, int Hv) {
+  const long Tp = (T + LC - 1) / LC * LC, chunks = Tp / LC;
+  return 2L * B * T * Hk * D            // qn, kn
+         + 2L * B * Hv * Tp * D         // W, U0 / Vt
+         + (long)B * Hv * Tp            // lam
+         + (long)B * Hv * chunks * D * D;  // chunk-start states
+}
+
+template <int D>
+cudaError_t launch(const void* qkv, long row_stride, const void* a, const void* bb, long ab_stride,
+                   const float* A_log, const float* dt_bias, float* state, void* out, float* work, int B, int T,
+                   int Hk, int Hv, cudaStream_t stream) {
+  const int Tp = (T + LC - 1) / LC * LC, chunks = Tp / LC;
+  float* qn = work;
+  float* kn = qn + (long)B * T * Hk * D;
+  float* W = kn + (long)B * T * Hk * D;
+  float* U = W + (long)B * Hv * Tp * D;
+  float* lam = U + (long)B * Hv * Tp * D;
+  float* S0 = lam + (long)B * Hv * Tp;
+  gdn_norm_kernel<D><<<dim3(T, B), 128, 0, stream>>>((const bf16*)qkv, row_stride, T, Hk, qn, kn);
+  RT_CUDA_CHECK(cudaGetLastError());
+  const int s1 = WySmem<D>::FLOATS * 4, s2 = StSmem<D>::FLOATS * 4, s3 = OutSmem<D>::FLOATS * 4;
+  RT_CUDA_CHECK(cudaFuncSetAttribute(gdn_wy_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, s1));
+  RT_CUDA_CHECK(cudaFuncSetAttribute(gdn_state_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, s2));
+  RT_CUDA_CHECK(cudaFuncSetAttribute(gdn_out_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, s3));
+  gdn_wy_kernel<D><<<dim3(chunks, Hv, B), NT, s1, stream>>>(kn, (const bf16*)qkv, row_stride, (const bf16*)a,
+                                                             (const bf16*)bb, ab_stride, A_log, dt_bias, W, U, lam, T,
+                                                             Tp, Hk, Hv);
+  RT_CUDA_CHECK(cudaGetLastError());
+  gdn_state_kernel<D><<<dim3(D / VB, Hv, B), NT, s2, stream>>>(kn, W, U, lam, state, S0, T, Tp, Hk, Hv);
+  RT_CUDA_CHECK(cudaGetLastError());
+  gdn_out_kernel<D><<<dim3(chunks, Hv, B * (D / OB)), NT, s3, stream>>>(qn, kn, U, lam, S0, (bf16*)out, T, Tp, Hk,
+                                                                        Hv);
+  return cudaGetLastError();
+}
+
+}  // namespace rt_gdn_wy
+
+// Workspace floats of the WY path (D = 64 or 128).
+long rt_gdn_wy_workspace_floats(int B, int T, int Hk, int Hv, int D) {
+  return D == 128 ? rt_gdn_wy::workspace<128>(B, T, Hk, Hv) : rt_gdn_wy::workspace<64>(B, T, Hk, Hv);
+}
+
+cudaError_t rt_gdn_wy_forward(const void* qkv, long row_stride, const void* a, const void* b, long ab_stride,
+                              const float* A_log, const float* dt_bias, float* state, void* out, float* work, int B,
+                              int T, int Hk, int Hv, int D, cudaStream_t stream) {
+  switch (D) {
+    case 128:
+      return rt_gdn_wy::launch<128>(qkv, row_stride, a, b, ab_stride, A_log, dt_bias, state, out, work, B, T, Hk, Hv,
+                                    stream);
+    case 64:
+      return rt_gdn_wy::launch<64>(qkv, row_stride, a, b, ab_stride, A_log, dt_bias, state, out, work, B, T, Hk, Hv,
+                                   stream);
+    default:
+      return cudaErrorInvalidValue;
+  }
+}

@@ -43,9 +43,12 @@ def test_chunked_forward_matches_fp32_reference(D):
 
 
 @cuda
-def test_gdn_kernel_matches_reference_recurrence():
+@pytest.mark.parametrize("B,T,Hk,Hv,D", [(2, 45, 2, 6, 64),       # serial 16-step path
+                                         (2, 200, 2, 6, 64),      # WY path, partial last chunk
+                                         (1, 128, 2, 4, 128),     # WY path, exact chunks
+                                         (1, 333, 4, 12, 128)])   # WY path, 6 chunks, GQA 3
+def test_gdn_kernel_matches_reference_recurrence(B, T, Hk, Hv, D):
     torch.manual_seed(1)
-    B, T, Hk, Hv, D = 2, 45, 2, 6, 64
     qkv = (torch.randn(B, T, 2 * Hk * D + Hv * D, device="cuda") * 0.5).to(torch.bfloat16)
     ab = (torch.randn(B * T, 2 * Hv, device="cuda")).to(torch.bfloat16)
     A_log = torch.rand(Hv, device="cuda") * 3
