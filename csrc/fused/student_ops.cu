@@ -403,18 +403,19 @@ __global__ void nmse_loss_kernel(const bf16* __restrict__ pred, const bf16* __re
 }
 
 // ---------------------------------------------------------------- optimizer
-// norm2 += sum (g / count)^2 ; also scales g in place by 1/count.
-__global__ void scale_norm_kernel(float* __restrict__ g, long n, const float* __restrict__ stats,
-                                  float* __restrict__ norm2) {
+// The gradient buffer is read, never written: the next micro-step's GEMMs store the four big matrices' gradients
+// and the rest of the buffer is cleared when that micro-step starts (models/student_fused.py).
+// norm2 += sum g^2 (raw sums; the 1/count scale is applied in adamw_kernel).
+__global__ void norm2_kernel(const float4* __restrict__ g, long n4, const float* __restrict__ g_tail, long tail,
+                             float* __restrict__ norm2) {
   __shared__ float scratch[32];
-  const float count = stats[2];
-  const float inv = count > 0.f ? 1.f / count : 0.f;
   float acc = 0.f;
-  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
-    const float v = g[i] * inv;
-    g[i] = v;
-    acc += v * v;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (long)gridDim.x * blockDim.x) {
+    const float4 v = __ldcs(g + i);
+    acc += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
   }
+  if (blockIdx.x == 0)
+    for (long i = threadIdx.x; i < tail; i += blockDim.x) acc += g_tail[i] * g_tail[i];
   acc = rt::block_sum(acc, scratch);
   if (threadIdx.x == 0) atomicAdd(norm2, acc);
 }
@@ -424,35 +425,66 @@ struct AdamArgs {
   long decay_numel;
 };
 
-__global__ void adamw_kernel(float* __restrict__ p, float* __restrict__ g, float* __restrict__ m,
+RT_DEVICE void adam_elem(float g, float& p, float& m, float& v, long i, const AdamArgs& a, float step) {
+  if (i < a.decay_numel) p *= 1.f - a.lr * a.weight_decay;
+  m = m + (1.f - a.beta1) * (g - m);
+  v = a.beta2 * v + (1.f - a.beta2) * g * g;
+  p -= step * m / (sqrtf(v) / a.bias2_sqrt + a.eps);
+}
+
+// g is scaled by (1/count) * min(1, clip / (|g| / count + 1e-6)): the reference's division by the token count
+// followed by clip_grad_norm_ on the divided gradients.
+__global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
                              float* __restrict__ v, bf16* __restrict__ shadow, long n, const float* __restrict__ norm2,
-                             AdamArgs a) {
-  const float norm = sqrtf(*norm2);
-  const float coef = fminf(1.f, a.clip / (norm + 1e-6f));
+                             const float* __restrict__ stats, AdamArgs a) {
+  const float count = stats[2];
+  const float inv = count > 0.f ? 1.f / count : 0.f;
+  const float norm = sqrtf(*norm2) * inv;
+  const float gscale = inv * fminf(1.f, a.clip / (norm + 1e-6f));
   const float step = a.lr / a.bias1;
-  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
-    const float gv = g[i] * coef;
-    float pv = p[i];
-    if (i < a.decay_numel) pv *= 1.f - a.lr * a.weight_decay;
-    const float mv = m[i] + (1.f - a.beta1) * (gv - m[i]);
-    const float vv = a.beta2 * v[i] + (1.f - a.beta2) * gv * gv;
-    pv -= step * mv / (sqrtf(vv) / a.bias2_sqrt + a.eps);
-    p[i] = pv;
-    m[i] = mv;
-    v[i] = vv;
-    g[i] = 0.f;
-    if (shadow) shadow[i] = __float2bfloat16_rn(pv);
+  const long n4 = n / 4;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (long)gridDim.x * blockDim.x) {
+    const float4 g4 = __ldcs(reinterpret_cast<const float4*>(g) + i);
+    float4 p4 = reinterpret_cast<const float4*>(p)[i];
+    float4 m4 = __ldcs(reinterpret_cast<const float4*>(m) + i);
+    float4 v4 = __ldcs(reinterpret_cast<const float4*>(v) + i);
+    const long e = 4 * i;
+    adam_elem(g4.x * gscale, p4.x, m4.x, v4.x, e + 0, a, step);
+    adam_elem(g4.y * gscale, p4.y, m4.y, v4.y, e + 1, a, step);
+    adam_elem(g4.z * gscale, p4.z, m4.z, v4.z, e + 2, a, step);
+    adam_elem(g4.w * gscale, p4.w, m4.w, v4.w, e + 3, a, step);
+    reinterpret_cast<float4*>(p)[i] = p4;
+    __stcs(reinterpret_cast<float4*>(m) + i, m4);
+    __stcs(reinterpret_cast<float4*>(v) + i, v4);
+    if (shadow) {
+      __nv_bfloat162 lo = __floats2bfloat162_rn(p4.x, p4.y), hi = __floats2bfloat162_rn(p4.z, p4.w);
+      uint2 packed;
+      packed.x = *reinterpret_cast<unsigned*>(&lo);
+      packed.y = *reinterpret_cast<unsigned*>(&hi);
+      reinterpret_cast<uint2*>(shadow)[i] = packed;
+    }
+  }
+  if (blockIdx.x == 0) {
+    for (long i = 4 * n4 + threadIdx.x; i < n; i += blockDim.x) {
+      float pv = p[i], mv = m[i], vv = v[i];
+      adam_elem(g[i] * gscale, pv, mv, vv, i, a, step);
+      p[i] = pv;
+      m[i] = mv;
+      v[i] = vv;
+      if (shadow) shadow[i] = __float2bfloat16_rn(pv);
+    }
   }
 }
 
 __global__ void report_kernel(const float* __restrict__ stats, const float* __restrict__ norm2,
                               float* __restrict__ report) {
-  const float norm = sqrtf(*norm2);
+  const float count = stats[2];
+  const float norm = sqrtf(*norm2) * (count > 0.f ? 1.f / count : 0.f);
   report[0] = stats[0];
   report[1] = stats[1];
-  report[2] = stats[2];
+  report[2] = count;
   report[3] = norm;
-  report[4] = (!isfinite(norm) || stats[2] <= 0.f) ? 1.f : 0.f;
+  report[4] = (!isfinite(norm) || count <= 0.f) ? 1.f : 0.f;
 }
 
 __global__ void to_bf16_kernel(const float* __restrict__ src, bf16* __restrict__ dst, long n) {
@@ -551,14 +583,20 @@ extern "C" cudaError_t rt_nmse_loss(const void* pred, const void* target, float*
   return cudaGetLastError();
 }
 
-// Scales the flat gradient by 1/count, reduces its norm, clips, applies AdamW, refreshes the bf16 shadow,
-// clears the gradient and writes the report. `norm2` is one float of scratch (zeroed here).
+// Reduces the flat gradient's norm, scales by 1/count, clips, applies AdamW, refreshes the bf16 shadow and
+// writes the report; the gradient itself is left untouched. `norm2` is one float of scratch (zeroed here).
+// p, g, m, v and shadow must be 16-byte aligned (flat buffers from the caching allocator are).
 extern "C" cudaError_t rt_flat_adamw(float* p, float* g, float* m, float* v, void* shadow, long n, long decay_numel,
                                      const float* stats, float* norm2, float* report, float lr, float beta1,
                                      float beta2, float eps, float weight_decay, float clip, int step,
                                      cudaStream_t s) {
+  if ((reinterpret_cast<uintptr_t>(p) | reinterpret_cast<uintptr_t>(g) | reinterpret_cast<uintptr_t>(m) |
+       reinterpret_cast<uintptr_t>(v)) & 15 || reinterpret_cast<uintptr_t>(shadow) & 7)
+    return cudaErrorMisalignedAddress;
   RT_CUDA_CHECK(cudaMemsetAsync(norm2, 0, sizeof(float), s));
-  scale_norm_kernel<<<grid_for(n, 512), 512, 0, s>>>(g, n, stats, norm2);
+  const long n4 = n / 4;
+  norm2_kernel<<<grid_for(n4, 512), 512, 0, s>>>(reinterpret_cast<const float4*>(g), n4, g + 4 * n4, n - 4 * n4,
+                                                 norm2);
   RT_CUDA_CHECK(cudaGetLastError());
   report_kernel<<<1, 1, 0, s>>>(stats, norm2, report);
   RT_CUDA_CHECK(cudaGetLastError());
@@ -567,7 +605,7 @@ extern "C" cudaError_t rt_flat_adamw(float* p, float* g, float* m, float* v, voi
   a.bias1 = (float)(1.0 - pow((double)beta1, (double)step));
   a.bias2_sqrt = (float)sqrt(1.0 - pow((double)beta2, (double)step));
   a.decay_numel = decay_numel;
-  adamw_kernel<<<grid_for(n, 512), 512, 0, s>>>(p, g, m, v, (bf16*)shadow, n, norm2, a);
+  adamw_kernel<<<grid_for(n4, 256, 148 * 12), 256, 0, s>>>(p, g, m, v, (bf16*)shadow, n, norm2, stats, a);
   return cudaGetLastError();
 }
 

@@ -14,9 +14,9 @@
 //   B  update: after every rank's norm is published, each rank forms the
 //      same global norm (fixed summation order), clips, applies AdamW to its
 //      shard (fp32 master, moments, bf16 weight copy; local memory only),
-//      clears its whole local gradient (all peers have finished reading it)
-//      and its loss statistics, writes the report and raises its "shard
-//      updated" flag everywhere;
+//      clears its loss statistics, writes the report and raises its "shard
+//      updated" flag everywhere (the gradient buffer is not cleared: the next
+//      micro-step overwrites it);
 //   C  all-gather: after every rank's flag, each rank pulls the other shards
 //      of the bf16 weight copy and of the fp32 non-decay parameters (read in
 //      fp32 by the forward) with peer loads. The fp32 masters of the four
@@ -225,7 +225,6 @@ exchange_update_kernel(Peers peers, int rank, long n, long lo4, long hi4, long t
         adam_one(g4[u].y * gscale, p4[u].y, m4[u].y, v4[u].y, e + 1, a, step);
         adam_one(g4[u].z * gscale, p4[u].z, m4[u].z, v4[u].z, e + 2, a, step);
         adam_one(g4[u].w * gscale, p4[u].w, m4[u].w, v4[u].w, e + 3, a, step);
-        __stcs(g4s + i, make_float4(0.f, 0.f, 0.f, 0.f));
         __stcs(m4s + i, m4[u]);
         __stcs(v4s + i, v4[u]);
         p4s[i] = p4[u];
@@ -243,18 +242,11 @@ exchange_update_kernel(Peers peers, int rank, long n, long lo4, long hi4, long t
   for (long i = tail_lo + (long)blockIdx.x * THREADS_B + threadIdx.x; i < tail_hi; i += stride) {
     float pv = p[i], mv = m[i], vv = v[i];
     adam_one(g[i] * gscale, pv, mv, vv, i, a, step);
-    g[i] = 0.f;
     m[i] = mv;
     v[i] = vv;
     p[i] = pv;
     sh[i] = __float2bfloat16_rn(pv);
   }
-  // Clear the rest of the local gradient: every peer has finished reading it (their norms are published).
-  for (long i = (long)blockIdx.x * THREADS_B + threadIdx.x; i < lo4; i += stride)
-    __stcs(g4s + i, make_float4(0.f, 0.f, 0.f, 0.f));
-  for (long i = hi4 + (long)blockIdx.x * THREADS_B + threadIdx.x; i < n / 4; i += stride)
-    __stcs(g4s + i, make_float4(0.f, 0.f, 0.f, 0.f));
-  for (long i = (n / 4) * 4 + (long)blockIdx.x * THREADS_B + threadIdx.x; i < tail_lo; i += stride) g[i] = 0.f;
   if (blockIdx.x == 0 && threadIdx.x == 0) {
     report[0] = s0;
     report[1] = s1;

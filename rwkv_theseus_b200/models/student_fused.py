@@ -67,6 +67,10 @@ class FusedStudent:
     def mm_acc(grad, a, a_t, b, b_t):
         native().gemm(a, a_t, b, b_t, 2, 1.0, grad)
 
+    def mm_grad(self, name, first, a, a_t, b, b_t):
+        """Weight gradient of a big matrix: stored on the first micro-step of an update, accumulated after."""
+        native().gemm(a, a_t, b, b_t, 1 if first else 2, 1.0, self.g(name))
+
     def _state(self, x, state):
         B = x.shape[0]
         if state is None:
@@ -119,17 +123,21 @@ class FusedStudent:
 
     # ------------------------------------------------------------------ training micro-step
     @torch.no_grad()
-    def forward_backward(self, x, target, state, eps):
+    def forward_backward(self, x, target, state, eps, first=False):
+        """One micro-step. ``first``: the gradient buffer holds a finished update's values; the four big
+        matrices' gradients are then stored (not accumulated) and the rest of the buffer is cleared."""
         B, T, C = x.shape
         M, H, N = B * T, self.H, self.N
         ext = native()
+        if first:
+            self.student.flat.grad[self.student.decay_numel:].zero_()
         pred, new_state, s = self._forward(x, state, True)
         stats = torch.zeros(3, device=x.device)
         dpred = torch.empty_like(pred)
         ext.nmse_loss(pred, target.reshape(M, C).to(torch.bfloat16).contiguous(), stats, dpred, float(eps))
         # output projection
         dyg = self.mm(dpred, False, self.w("output.weight"), True)
-        self.mm_acc(self.g("output.weight"), dpred, True, s["yg"], True)
+        self.mm_grad("output.weight", first, dpred, True, s["yg"], True)
         # post-WKV backward
         dy = torch.empty_like(pred)
         dg = torch.empty_like(pred)
@@ -154,7 +162,7 @@ class FusedStudent:
         for grad_out, inp, name, slot in ((dr, xr, "receptance.weight", 0), (dk, xk, "key.weight", 2),
                                           (dv, xv, "value.weight", 3)):
             ext.gemm(grad_out, False, self.w(name), True, 0, 1.0, dmix[slot])
-            self.mm_acc(self.g(name), grad_out, True, inp, True)
+            self.mm_grad(name, first, grad_out, True, inp, True)
         # decay LoRA: lw = tanh(xw w1) w2
         self.mm_acc(self.g("w2"), s["hw"], True, dlw, True)
         dhw = self.mm(dlw, False, self.w("w2"), False)

@@ -83,6 +83,7 @@ class Student:
         self.report = torch.zeros(5, device=device)     # [nmse, cos, count, grad_norm, error] of last update
         self.fused = None
         self.sharded = False           # fp32 masters / moments hold only this rank's shard (peer exchange)
+        self.grads_live = False        # the flat gradient holds this update's micro-steps (fused path)
         if device.type == "cuda" and cfg.get("fused_optimizer", True):
             from .models.student_fused import FusedStudent
             self.fused = FusedStudent(self)
@@ -95,7 +96,8 @@ class Student:
         """Forward + backward on one chunk; gradients accumulate into the flat buffer."""
         eps = self.cfg["loss_epsilon"]
         if self.fused is not None:
-            stats, self.state = self.fused.forward_backward(x, target, self.state, eps)
+            stats, self.state = self.fused.forward_backward(x, target, self.state, eps, first=not self.grads_live)
+            self.grads_live = True
             self.stats += stats
             return
         from .losses import statistics
@@ -128,6 +130,9 @@ class Student:
         """Sum gradients and loss statistics over ranks (one bucket per layer).
 
         With the peer-memory exchange the reduction is part of ``update``."""
+        if self.fused is not None and not self.grads_live:
+            self.flat.grad.zero_()  # no micro-step this update (exhausted rank): contribute zeros
+            self.grads_live = True
         topo = self.topo
         if topo.world == 1 or self._exchange() is not None:
             return
@@ -145,9 +150,13 @@ class Student:
             # Reduce-scatter, clip, AdamW on this rank's shard, all-gather; clears grad and stats on its stream.
             exchange.update(self, lr, self.steps_done)
             self.sharded = True
+            self.grads_live = False
             return lr
         if self.fused is not None:
+            if not self.grads_live:
+                self.flat.grad.zero_()
             self.fused.update(lr, self.steps_done)
+            self.grads_live = False
         else:
             self._update_reference(lr, self.steps_done)
         self.stats.zero_()

@@ -79,11 +79,13 @@ def test_fused_update_matches_reference_update():
     grad = torch.randn(ref.flat.numel, device="cuda", generator=g)
     for s in (ref, fused):
         s.flat.grad.copy_(grad)
+        s.grads_live = True  # gradients injected directly stand for this update's micro-steps
         s.stats.copy_(torch.tensor([3.0, 1.0, 7.0], device="cuda"))
     for step in range(3):
         for s in (ref, fused):
             if step:
                 s.flat.grad.copy_(grad * (step + 1))
+                s.grads_live = True
                 s.stats.copy_(torch.tensor([3.0, 1.0, 7.0], device="cuda"))
             s.update()
         torch.testing.assert_close(fused.flat.param, ref.flat.param, rtol=1e-5, atol=1e-6)
@@ -105,3 +107,40 @@ def test_fused_student_learns():
         s.update()
         losses.append(s.report[0].item() / s.report[2].item())
     assert losses[-1] < losses[0]
+
+
+@cuda
+def test_fused_gradients_accumulate_then_restart_after_update():
+    """First micro-step of an update stores the gradient, later ones accumulate, an update starts over."""
+    s = make(True)
+    g = torch.Generator(device="cuda").manual_seed(4)
+    x = torch.randn(1, 40, 256, device="cuda", generator=g).to(torch.bfloat16)
+    target = torch.randn(1, 40, 256, device="cuda", generator=g).to(torch.bfloat16)
+    s.state = None
+    s.micro_step(x, target)
+    once = s.flat.grad.clone()
+    s.state = None
+    s.micro_step(x, target)
+    torch.testing.assert_close(s.flat.grad, 2 * once, rtol=1e-5, atol=1e-6)
+    s.cfg = dict(s.cfg, lr=0.0)  # an update that leaves the weights as they are
+    s.update()
+    s.state = None
+    s.micro_step(x, target)
+    assert s.grads_live
+    # after an update the buffer restarts: no trace of the two accumulated micro-steps
+    torch.testing.assert_close(s.flat.grad, once, rtol=1e-5, atol=1e-6)
+
+
+@cuda
+def test_exhausted_update_uses_zero_gradients():
+    """An update with no micro-step (a rank out of data) applies zero gradients, not the last ones."""
+    s = make(True)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    x = torch.randn(1, 24, 256, device="cuda", generator=g).to(torch.bfloat16)
+    s.micro_step(x, x)
+    s.update()
+    moments = s.flat.exp_avg.clone()
+    s.stats.copy_(torch.tensor([0.0, 0.0, 1.0], device="cuda"))
+    s.reduce()
+    s.update()
+    torch.testing.assert_close(s.flat.exp_avg, 0.9 * moments)  # beta1 decay only: the gradient was zero
