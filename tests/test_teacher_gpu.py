@@ -94,3 +94,34 @@ def test_smoke_step():
     from rwkv_theseus_b200.smoke import run_smoke
     reports = run_smoke(torch.device("cuda", 0))
     assert reports.shape == (2, 5)
+
+
+@cuda
+@pytest.mark.parametrize("B", [1, 2])
+def test_gdn_state_carry_across_mixed_call_lengths(B):
+    """Calls of 512, 257, 511, 1, 383, 17 and 63 tokens (both kernel paths, decode-sized steps) carry the
+    recurrent state exactly like one pass of the reference recurrence."""
+    torch.manual_seed(3)
+    Hk, Hv, D = 2, 4, 128
+    lengths = [512, 257, 511, 1, 383, 17, 63]
+    T = sum(lengths)
+    qkv = (torch.randn(B, T, 2 * Hk * D + Hv * D, device="cuda") * 0.5).to(torch.bfloat16)
+    ab = torch.randn(B, T, 2 * Hv, device="cuda").to(torch.bfloat16)
+    A_log = torch.rand(Hv, device="cuda") * 2
+    dt_bias = torch.randn(Hv, device="cuda")
+    state = torch.zeros(B, Hv, D, D, device="cuda")
+    outs, t0 = [], 0
+    for n in lengths:
+        piece = qkv[:, t0:t0 + n].contiguous()
+        gates = ab[:, t0:t0 + n].reshape(B * n, 2 * Hv)
+        outs.append(native().gdn_forward(piece, gates[:, :Hv], gates[:, Hv:], A_log, dt_bias, state, Hk, Hv, D))
+        t0 += n
+    out = torch.cat(outs, 1)
+    q, k, v = torch.split(qkv.float(), [Hk * D, Hk * D, Hv * D], -1)
+    a, b = ab[..., :Hv].float(), ab[..., Hv:]
+    g = -A_log.exp() * torch.nn.functional.softplus(a + dt_bias)
+    beta = torch.sigmoid(b).float()
+    ro, rs = R.gated_delta_rule(q.view(B, T, Hk, D), k.view(B, T, Hk, D), v.view(B, T, Hv, D), g, beta,
+                                torch.zeros(B, Hv, D, D, device="cuda"))
+    torch.testing.assert_close(out.float(), ro.float(), atol=2e-2, rtol=2e-2)
+    torch.testing.assert_close(state, rs, atol=3e-3, rtol=3e-3)
