@@ -104,6 +104,14 @@ at::Tensor gemm(at::Tensor A, bool a_t, at::Tensor B, bool b_t, int64_t epi, dou
   const long M = a_t ? A.size(1) : A.size(0), K = a_t ? A.size(0) : A.size(1);
   const long N = b_t ? B.size(1) : B.size(0), KB = b_t ? B.size(0) : B.size(1);
   TORCH_CHECK(K == KB, "GEMM inner dimensions differ: ", K, " vs ", KB);
+  if (epi == 0 && M <= 32 && !a_t && !b_t && !out.has_value()) {  // decode-sized: split-K weight streaming
+    auto C = at::empty({M, N}, A.options().dtype(at::kBFloat16));
+    auto ws = at::empty({M, N}, A.options().dtype(at::kFloat));
+    check_cuda(rt_gemm_skinny_bf16(a.ptr, a.ld, b.ptr, nullptr, b.ld, ws.data_ptr<float>(), C.data_ptr(), N, M, N,
+                                   K, nullptr, stream_of(A)),
+               "gemm (skinny)");
+    return C;
+  }
   at::Tensor C;
   if (epi == 2) {
     TORCH_CHECK(out.has_value(), "accumulate epilogue needs `out`");
@@ -133,6 +141,13 @@ at::Tensor gemm_swiglu(at::Tensor A, at::Tensor Bg, at::Tensor Bu) {
   const long M = A.size(0), K = A.size(1), N = Bg.size(0);
   TORCH_CHECK(Bg.size(1) == K, "SwiGLU inner dimension mismatch");
   auto C = at::empty({M, N}, A.options());
+  if (M <= 32) {  // decode-sized: split-K weight streaming of both operands, fused silu * up
+    auto ws = at::empty({2 * M, N}, A.options().dtype(at::kFloat));
+    check_cuda(rt_gemm_skinny_bf16(a.ptr, a.ld, g.ptr, u.ptr, g.ld, ws.data_ptr<float>(), C.data_ptr(), N, M, N, K,
+                                   nullptr, stream_of(A)),
+               "gemm_swiglu (skinny)");
+    return C;
+  }
   check_cuda(rt_gemm_swiglu_bf16(a.ptr, a.ld, g.ptr, u.ptr, g.ld, C.data_ptr(), N, M, N, K, nullptr, stream_of(A)),
              "gemm_swiglu");
   return C;

@@ -162,11 +162,13 @@ __global__ void copy_rows_kernel(const bf16* __restrict__ src, long src_stride, 
 extern "C" cudaError_t rt_rmsnorm_1p(const void* x, const void* h, const float* w, void* sum_out, void* out, long rows,
                                      int C, float eps, cudaStream_t stream) {
   const size_t smem = (size_t)C * sizeof(float);
-  if (h) {
+  if (smem > 48 * 1024) {  // only rows wider than 12288 need the opt-in (set once per width class)
     RT_CUDA_CHECK(cudaFuncSetAttribute(rmsnorm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    RT_CUDA_CHECK(cudaFuncSetAttribute(rmsnorm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  }
+  if (h) {
     rmsnorm_kernel<true><<<rows, 256, smem, stream>>>((const bf16*)x, (const bf16*)h, w, (bf16*)sum_out, (bf16*)out, C, eps);
   } else {
-    RT_CUDA_CHECK(cudaFuncSetAttribute(rmsnorm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     rmsnorm_kernel<false><<<rows, 256, smem, stream>>>((const bf16*)x, nullptr, w, nullptr, (bf16*)out, C, eps);
   }
   return cudaGetLastError();

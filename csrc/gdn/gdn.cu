@@ -321,9 +321,15 @@ cudaError_t rt_gdn_wy_forward(const void* qkv, long row_stride, const void* a, c
                               const float* A_log, const float* dt_bias, float* state, void* out, float* work, int B,
                               int T, int Hk, int Hv, int D, cudaStream_t stream);
 
+extern "C" cudaError_t rt_gdn_step(const void* qkv, long row_stride, const void* a, const void* b, long ab_stride,
+                                   const float* A_log, const float* dt_bias, float* state, void* out, int B, int T,
+                                   int Hk, int Hv, int D, cudaStream_t stream);
+
 namespace {
 constexpr int WY_MIN_T = 128;
+constexpr int STEP_MAX_T = 4;  // decode-sized calls: token-by-token kernel (gdn_step.cu), no workspace
 bool use_wy(int T, long row_stride, int D) { return T >= WY_MIN_T && (D == 64 || D == 128) && row_stride % 8 == 0; }
+bool use_step(int T, int D) { return T <= STEP_MAX_T && (D == 64 || D == 128); }
 }  // namespace
 
 // Scratch floats of the serial 16-step path alone.
@@ -334,6 +340,7 @@ extern "C" long rt_gdn_serial_workspace_floats(int B, int T, int Hk, int D) {
 
 // Scratch floats needed by rt_gdn_forward for these sizes (row_stride decides the path only through alignment).
 extern "C" long rt_gdn_workspace_floats(int B, int T, int Hk, int Hv, int D, long row_stride) {
+  if (use_step(T, D)) return 0;
   if (use_wy(T, row_stride, D)) return rt_gdn_wy_workspace_floats(B, T, Hk, Hv, D);
   return rt_gdn_serial_workspace_floats(B, T, Hk, D);
 }
@@ -358,6 +365,8 @@ extern "C" cudaError_t rt_gdn_forward(const void* qkv, long row_stride, const vo
                                       const float* A_log, const float* dt_bias, float* state, void* out, float* work,
                                       int B, int T, int Hk, int Hv, int D, cudaStream_t stream) {
   if (Hv % Hk) return cudaErrorInvalidValue;
+  if (use_step(T, D))
+    return rt_gdn_step(qkv, row_stride, a, b, ab_stride, A_log, dt_bias, state, out, B, T, Hk, Hv, D, stream);
   if (use_wy(T, row_stride, D))
     return rt_gdn_wy_forward(qkv, row_stride, a, b, ab_stride, A_log, dt_bias, state, out, work, B, T, Hk, Hv, D,
                              stream);

@@ -26,7 +26,7 @@
 
 namespace {
 
-enum Epi : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_F32_ACCUM = 2, EPI_SWIGLU = 3 };
+enum Epi : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_F32_ACCUM = 2, EPI_SWIGLU = 3, EPI_ATOMIC_T = 4 };
 
 constexpr int BM = 128, BK = 64, STAGES = 4, THREADS = 192;
 constexpr int MN_CHUNK_BYTES = 64 * BK * 2;  // one 64-wide MN-major chunk: BK rows x 128 B
@@ -37,12 +37,16 @@ struct Cfg {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + NB * B_BYTES;
+  // Pipeline depth: 4 stages for the compute-bound tiles; the skinny split-K tiles (weight streaming for decode)
+  // are memory-bound and keep 8 stages of 20 KB in flight.
+  static constexpr int ST = EPI == EPI_ATOMIC_T ? 8 : STAGES;
   static constexpr int ACC_COLS = NB * BN;
   static constexpr int TMEM_COLS = 2 * ACC_COLS;
   static constexpr uint32_t IDESC = sm100::idesc_bf16(BM, BN, A_MN, B_MN);
   static constexpr int BAR_BYTES = 256;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
-  static_assert(TMEM_COLS == 128 || TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM columns must be a power of 2");
+  static constexpr int SMEM_BYTES = ST * STAGE_BYTES + BAR_BYTES + 1024;
+  static_assert(TMEM_COLS == 64 || TMEM_COLS == 128 || TMEM_COLS == 256 || TMEM_COLS == 512,
+                "TMEM columns must be a power of 2 (>= 32)");
 };
 
 struct GemmArgs {
@@ -50,6 +54,7 @@ struct GemmArgs {
   void* C;
   long ldc;
   int tiles_m, tiles_n;
+  int splits, kchunk;  // split-K: tile t covers k-blocks [ks * kchunk, (ks + 1) * kchunk), ks = t / (tiles_m * tiles_n)
   float alpha;
   int* status;
 };
@@ -92,6 +97,11 @@ __device__ __forceinline__ void store_row(float (&v)[32], int epi, void* C, long
       for (int i = 0; i < 32; ++i)
         if (col + i < N) out[i] = v[i];
     }
+  } else if (epi == EPI_ATOMIC_T) {  // transposed fp32 partial sums: C[col + i][row] += v[i] (split-K)
+    float* base = reinterpret_cast<float*>(C) + row;
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (col + i < N) atomicAdd(base + (long)(col + i) * ldc, v[i]);
   } else {  // EPI_F32_ACCUM
     if (vec) {
       float4* dst = reinterpret_cast<float4*>(out);
@@ -116,21 +126,29 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
   using C_ = Cfg<BN, A_MN, B_MN, EPI>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * C_::STAGE_BYTES);
+  constexpr int ST = C_::ST;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + ST * C_::STAGE_BYTES);
   uint64_t* full = bars;
-  uint64_t* empty = bars + STAGES;
-  uint64_t* tfull = bars + 2 * STAGES;
+  uint64_t* empty = bars + ST;
+  uint64_t* tfull = bars + 2 * ST;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int total = args.tiles_m * args.tiles_n;
+  const int per_split = args.tiles_m * args.tiles_n;
+  const int total = per_split * args.splits;
   const int kblocks = (args.K + BK - 1) / BK;
+  // k-block range of a tile (all of K unless split-K)
+  auto krange = [&](int tile, int& k0, int& k1) {
+    const int ks = tile / per_split;
+    k0 = ks * args.kchunk;
+    k1 = min(kblocks, k0 + args.kchunk);
+  };
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < ST; ++s) {
       sm100::mbar_init(&full[s], 1);
       sm100::mbar_init(&empty[s], 1);
     }
@@ -163,8 +181,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
       uint32_t phase = 0;
       int issued = 0;
       for (int tile = blockIdx.x; tile < total && !*abort; tile += gridDim.x) {
-        const int tm = tile % args.tiles_m, tn = tile / args.tiles_m;
-        for (int kb = 0; kb < kblocks; ++kb) {
+        const int tm = tile % args.tiles_m, tn = (tile % per_split) / args.tiles_m;
+        int k0, k1;
+        krange(tile, k0, k1);
+        for (int kb = k0; kb < k1; ++kb) {
           if (!sm100::mbar_wait(&empty[stage], phase ^ 1, abort)) break;
           uint8_t* a_dst = smem + stage * C_::STAGE_BYTES;
           sm100::mbar_expect_tx(&full[stage], C_::STAGE_BYTES);
@@ -187,14 +207,14 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
             }
           }
           ++issued;
-          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+          if (++stage == ST) { stage = 0; phase ^= 1; }
         }
       }
       // Drain: every issued stage must have been consumed before shared memory goes away.
       (void)issued;
-      for (int s = 0; s < STAGES; ++s) {
+      for (int s = 0; s < ST; ++s) {
         if (!sm100::mbar_wait_bounded(&empty[stage], phase ^ 1)) break;
-        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        if (++stage == ST) { stage = 0; phase ^= 1; }
       }
     }
   } else if (warp == 1) {
@@ -207,7 +227,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
         sm100::tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * C_::ACC_COLS;
         bool ok = true;
-        for (int kb = 0; kb < kblocks; ++kb) {
+        int k0, k1;
+        krange(tile, k0, k1);
+        for (int kb = k0; kb < k1; ++kb) {
           if (!sm100::mbar_wait(&full[stage], phase, abort)) { ok = false; break; }
           sm100::tc_fence_after();
           const uint32_t a_base = sm100::smem_u32(smem + stage * C_::STAGE_BYTES);
@@ -220,11 +242,11 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
               const uint32_t b_base = a_base + C_::A_BYTES + j * C_::B_BYTES;
               const uint64_t bdesc = B_MN ? sm100::smem_desc(b_base + ks * 2048, MN_CHUNK_BYTES, 1024)
                                           : sm100::smem_desc(b_base + ks * 32, 16, 1024);
-              sm100::mma_bf16(d_tmem + j * BN, adesc, bdesc, C_::IDESC, (kb | ks) != 0);
+              sm100::mma_bf16(d_tmem + j * BN, adesc, bdesc, C_::IDESC, (kb != k0) || (ks != 0));
             }
           }
           sm100::mma_commit(&empty[stage]);
-          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+          if (++stage == ST) { stage = 0; phase ^= 1; }
         }
         if (!ok) break;
         sm100::mma_commit(&tfull[acc]);
@@ -240,7 +262,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < total && !*abort; tile += gridDim.x) {
-      const int tm = tile % args.tiles_m, tn = tile / args.tiles_m;
+      const int tm = tile % args.tiles_m, tn = (tile % per_split) / args.tiles_m;
       if (!sm100::mbar_wait(&tfull[acc], acc_phase, abort)) break;
       sm100::tc_fence_after();
       const int row = tm * BM + row_in_tile;
@@ -318,7 +340,7 @@ int num_sms_cached() {
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
 cudaError_t launch(const void* A, long lda, const void* B0, const void* B1, long ldb, void* C, long ldc, int M,
-                   int N, int K, float alpha, int* status, cudaStream_t stream) {
+                   int N, int K, float alpha, int* status, cudaStream_t stream, int splits = 1) {
   using C_ = Cfg<BN, A_MN, B_MN, EPI>;
   CUtensorMap ta, tb0, tb1;
   bool ok = A_MN ? make_tmap(&ta, A, M, K, lda * 2, 64, BK) : make_tmap(&ta, A, K, M, lda * 2, BK, BM);
@@ -332,7 +354,9 @@ cudaError_t launch(const void* A, long lda, const void* B0, const void* B1, long
   args.M = M; args.N = N; args.K = K; args.C = C; args.ldc = ldc; args.alpha = alpha; args.status = status;
   args.tiles_m = (M + BM - 1) / BM;
   args.tiles_n = (N + BN - 1) / BN;
-  const int total = args.tiles_m * args.tiles_n;
+  args.splits = splits;
+  args.kchunk = ((K + BK - 1) / BK + splits - 1) / splits;
+  const int total = args.tiles_m * args.tiles_n * splits;
   auto kern = gemm_kernel<BN, A_MN, B_MN, EPI>;
   RT_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C_::SMEM_BYTES));
   const int grid = total < num_sms_cached() ? total : num_sms_cached();
@@ -383,6 +407,55 @@ extern "C" cudaError_t rt_gemm_bf16(const void* A, long lda, int a_mn, const voi
   if (a_mn && !b_mn) { RT_G(true, false) }
   RT_G(true, true)
 #undef RT_G
+}
+
+namespace {
+
+// ws [M, N] fp32 partial sums -> out [M, N] bf16 (ldo), or silu(ws_g) * ws_u when ws_u is given.
+__global__ void skinny_finish_kernel(const float* __restrict__ ws, const float* __restrict__ ws_u,
+                                     __nv_bfloat16* __restrict__ out, long ldo, int M, int N) {
+  const long total = (long)M * N;
+  for (long e = (long)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (long)gridDim.x * blockDim.x) {
+    const int m = (int)(e / N), n = (int)(e % N);
+    float v = ws[e];
+    if (ws_u) v = rt::siluf_(v) * ws_u[e];
+    out[(long)m * ldo + n] = __float2bfloat16_rn(v);
+  }
+}
+
+// Split count for the skinny path: enough 128-row weight tiles to cover every SM twice, at least 4 k-blocks
+// (256 of K) per split.
+int skinny_splits(int N, int K) {
+  const int tiles = (N + BM - 1) / BM, kblocks = (K + BK - 1) / BK;
+  int splits = (2 * num_sms_cached() + tiles - 1) / tiles;
+  splits = splits < kblocks / 4 ? splits : kblocks / 4;
+  return splits < 1 ? 1 : splits;
+}
+
+}  // namespace
+
+// Decode-sized (M <= 32) y[M, N] = X[M, K] · W[N, K]^T as weight streaming: the tcgen05 tiles run swapped
+// (128 weight rows x 32 token rows per MMA, weights as the A operand), K is split across CTAs so every SM
+// streams weights, partial sums are added (fp32 atomics) into `ws` [M, N] (zeroed here), then converted.
+// With Wu given: out = silu(X·W^T) * (X·Wu^T) (ws holds 2 * M * N floats).
+extern "C" cudaError_t rt_gemm_skinny_bf16(const void* X, long ldx, const void* W, const void* Wu, long ldw,
+                                           float* ws, void* out, long ldo, int M, int N, int K, int* status,
+                                           cudaStream_t stream) {
+  if (M <= 0 || N <= 0 || K <= 0) return cudaSuccess;
+  if (M > 32 || (ldx & 7) || (ldw & 7) || (reinterpret_cast<uintptr_t>(X) & 15) ||
+      (reinterpret_cast<uintptr_t>(W) & 15) || (Wu && (reinterpret_cast<uintptr_t>(Wu) & 15)))
+    return cudaErrorInvalidValue;
+  const int parts = Wu ? 2 : 1;
+  RT_CUDA_CHECK(cudaMemsetAsync(ws, 0, sizeof(float) * (size_t)parts * M * N, stream));
+  const int splits = skinny_splits(N, K);
+  for (int p = 0; p < parts; ++p)
+    RT_CUDA_CHECK((launch<32, false, false, EPI_ATOMIC_T>(p ? Wu : W, ldw, X, X, ldx, ws + (size_t)p * M * N, N, N,
+                                                          M, K, 1.f, status, stream, splits)));
+  const long total = (long)M * N;
+  const int grid = (int)((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
+  skinny_finish_kernel<<<grid, 256, 0, stream>>>(ws, Wu ? ws + (size_t)M * N : nullptr,
+                                                 reinterpret_cast<__nv_bfloat16*>(out), ldo, M, N);
+  return cudaGetLastError();
 }
 
 // out[M,N] bf16 = silu(A · Bg^T) * (A · Bu^T); A, Bg, Bu K-major.

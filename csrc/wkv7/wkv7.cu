@@ -354,10 +354,19 @@ cudaError_t launch_fwd(int B, int T_, int H, int N, const void* r, const void* w
 // Chunk length used by the checkpoint layout [B, H, ceil(T/16) + 1, N, N].
 extern "C" int rt_wkv7_chunk_len() { return L; }
 
+extern "C" cudaError_t rt_wkv7_step(int dtype, int B, int T_, int H, int N, const void* r, const void* w,
+                                    const void* k, const void* v, const void* a, const void* b, const float* s0,
+                                    void* y, float* s_end, cudaStream_t stream);
+
+// Decode-sized calls without checkpoints (T <= 4) take the token-by-token kernel (wkv7_step.cu).
+constexpr int STEP_MAX_T = 4;
+
 extern "C" cudaError_t rt_wkv7_forward(int dtype, int B, int T_, int H, int N, const void* r, const void* w,
                                        const void* k, const void* v, const void* a, const void* b,
                                        const float* s0, void* y, float* s_end, float* checkpoints,
                                        cudaStream_t stream) {
+  if (!checkpoints && T_ <= STEP_MAX_T && (N == 32 || N == 64 || N == 128))
+    return rt_wkv7_step(dtype, B, T_, H, N, r, w, k, v, a, b, s0, y, s_end, stream);
   const int np = pick_np(N);
 #define RT_FWD(TYPE, NPV) return launch_fwd<TYPE, NPV>(B, T_, H, N, r, w, k, v, a, b, s0, y, s_end, checkpoints, stream)
 #define RT_FWD_NP(TYPE)                                   \

@@ -42,6 +42,8 @@ class AttentionAdapter(nn.Module):
         self.teacher_mode = False
         # A DDP wrapper must not be registered as a second child of the same core.
         self.__dict__["train_call"] = None
+        # Fused CUDA inference forward for frozen bf16 cores (set by ``install``); not a submodule.
+        self.__dict__["fast"] = None
 
     def forward(self, hidden_states, rope=None, cache=None, **_):
         if self.teacher_mode:
@@ -52,6 +54,8 @@ class AttentionAdapter(nn.Module):
             with torch.enable_grad():
                 y, state = self.train_call(self.teacher_input.detach(), self.state)
             self.prediction = y
+        elif self.fast is not None:
+            y, state = self.fast(hidden_states, self.state)
         else:
             y, state = self.core(hidden_states, self.state)
         self.state = detach_state(state)
@@ -81,6 +85,9 @@ def install(model, layer, options, weights=None, trainable=False, retain_teacher
     core.to(device=device, dtype=torch.float32 if trainable else torch.bfloat16)
     core.requires_grad_(trainable)
     adapter = AttentionAdapter(core)
+    if not trainable and device.type == "cuda" and options.get("backend", "cuda") == "cuda":
+        from .student_fused import FusedTimeMixInference
+        adapter.__dict__["fast"] = FusedTimeMixInference(core)
     if retain_teacher:
         adapter.teacher = model.model.layers[layer].self_attn
         adapter.teacher.requires_grad_(False).eval()

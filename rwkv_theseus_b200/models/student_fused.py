@@ -192,3 +192,59 @@ class FusedStudent:
         native().flat_adamw(flat.param, flat.grad, flat.exp_avg, flat.exp_avg_sq, self.shadow, st.decay_numel,
                             st.stats, self.norm2, st.report, float(lr), float(beta1), float(beta2),
                             float(cfg["adam_eps"]), float(cfg["weight_decay"]), float(cfg["clip_norm"]), int(step))
+
+
+class FusedTimeMixInference:
+    """Inference forward of an installed (frozen, bf16) TimeMix with the fused kernels of ``FusedStudent``.
+
+    Same math as ``TimeMix.forward`` (reference ``theseus/timemix.py:66-89``): 1 mix kernel, the r/k/v and
+    LoRA GEMMs, pre-WKV, WKV7 (token-by-token kernel for decode-sized calls), post-WKV and the output
+    GEMM. The small fp32 vectors are copied once at construction; the module's weights must not change
+    afterwards (installed students are frozen).
+    """
+
+    def __init__(self, core):
+        self.core = core
+        self.C, self.H, self.N = core.width, core.heads, core.head_size
+        f32 = lambda t: t.detach().float().reshape(-1).contiguous()  # noqa: E731
+        self.coef = torch.cat([f32(getattr(core, "x_" + n)) for n in "rwkvag"])
+        self.vec = {n: f32(getattr(core, n)) for n in ("w0", "a0", "k_k", "k_a", "r_k")}
+        self.ln_w, self.ln_b = f32(core.ln_x.weight), f32(core.ln_x.bias)
+        bf = lambda t: t.detach().to(torch.bfloat16).contiguous()  # noqa: E731
+        self.mat = {n: bf(getattr(core, n).weight) for n in ("receptance", "key", "value", "output")}
+        self.mat.update({n: bf(getattr(core, n)) for n in ("w1", "w2", "a1", "a2", "g1", "g2")})
+
+    @torch.no_grad()
+    def __call__(self, x, state):
+        B, T, C = x.shape
+        M, H, N = B * T, self.H, self.N
+        ext = native()
+        mm = lambda a, b, b_t: ext.gemm(a, False, b, b_t, 0, 1.0, None)  # noqa: E731
+        x = x.to(torch.bfloat16).contiguous()
+        if state is None:
+            shift = torch.zeros(B, C, device=x.device, dtype=torch.bfloat16)
+            wkv0 = torch.zeros(B, H, N, N, device=x.device, dtype=torch.float32)
+        else:
+            shift, wkv0 = state["shift"].to(torch.bfloat16).contiguous(), state["wkv"].float().contiguous()
+        mix = torch.empty(6, M, C, device=x.device, dtype=torch.bfloat16)
+        ext.tm_mix(x, shift, self.coef, mix)
+        xr, xw, xk, xv, xa, xg = mix.unbind(0)
+        W = self.mat
+        r, k, v = mm(xr, W["receptance"], False), mm(xk, W["key"], False), mm(xv, W["value"], False)
+        hw = mm(xw, W["w1"], True)
+        ext.act_(hw, 0)
+        lw = mm(hw, W["w2"], True)
+        la = mm(mm(xa, W["a1"], True), W["a2"], True)
+        hg = mm(xg, W["g1"], True)
+        ext.act_(hg, 1)
+        g = mm(hg, W["g2"], True)
+        w_in, k_in, a_in, b_in = (torch.empty_like(r) for _ in range(4))
+        V = self.vec
+        ext.tm_pre_wkv(k, lw, la, V["w0"], V["a0"], V["k_k"], V["k_a"], w_in, k_in, a_in, b_in, H, N)
+        shape = (B, T, H, N)
+        y, end, _ = ext.wkv7_forward(*[t.view(shape) for t in (r, w_in, k_in, v, a_in, b_in)], wkv0, False)
+        yg = torch.empty_like(r)
+        gn = torch.empty(M * H * 3, device=x.device)
+        ext.tm_post_wkv(y, r, k_in, v, g, self.ln_w, self.ln_b, V["r_k"], yg, gn, H, N)
+        out = mm(yg, W["output"], False)
+        return out.view(B, T, C), {"shift": x[:, -1].clone(), "wkv": end}

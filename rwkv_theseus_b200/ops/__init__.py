@@ -31,3 +31,17 @@ def available():
         return True
     except RuntimeError:
         return False
+
+
+def f32(t):
+    """fp32 contiguous copy of a (frozen) parameter, cached on the tensor and refreshed when it is modified
+    in place; fp32 inputs pass through. Keeps per-call dtype conversions of small weights off the GPU."""
+    import torch
+    if t.dtype == torch.float32 and t.is_contiguous():
+        return t
+    cached = getattr(t, "_rt_f32", None)
+    if cached is None or cached[0] != t._version:
+        cached = (t._version, t.detach().float().contiguous())
+        t._rt_f32 = cached
+    return cached[1]
+

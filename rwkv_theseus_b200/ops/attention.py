@@ -8,7 +8,7 @@ sigmoid(g) multiplies the attention output before ``o_proj``.
 import torch
 from torch.nn import functional as F
 
-from . import native
+from . import f32, native
 from .gemm import linear
 
 
@@ -53,11 +53,12 @@ def attention_block(module, x, rope, state):
     k = linear(x2, module.k_proj.weight)
     v = linear(x2, module.v_proj.weight)
     q = torch.empty(B, T, Hq, D, device=x.device, dtype=torch.bfloat16)
-    native().norm_rope_(qg, Hq, module.q_norm.weight, inv_freq, q, pos0, 0, rot, module.q_norm.eps)
+    native().norm_rope_(qg, Hq, f32(module.q_norm.weight), f32(inv_freq), q, pos0, 0, rot, module.q_norm.eps)
     if state is None:
         state = {}
     length = _ensure_cache(state, B, T, Hkv, D, x.device)
-    native().norm_rope_(k, Hkv, module.k_norm.weight, inv_freq, state["keys"], pos0, length, rot, module.k_norm.eps)
+    native().norm_rope_(k, Hkv, f32(module.k_norm.weight), f32(inv_freq), state["keys"], pos0, length, rot,
+                        module.k_norm.eps)
     native().copy_rows_(v, state["values"], length)
     state["length"] = length + T
     if D == 256:

@@ -3,7 +3,7 @@ carried window, chunked delta rule (two kernels: Gram/normalise prep and the
 recurrent chunk pass), gated RMSNorm, output projection."""
 import torch
 
-from . import native
+from . import f32, native
 from .gemm import linear
 
 
@@ -23,8 +23,8 @@ def gdn_forward(module, x, conv_state, rec_state):
     qkv = linear(x2, module.in_proj_qkv.weight)
     z = linear(x2, module.in_proj_z.weight)
     ab = linear(x2, _merged_ab(module))
-    qkv, conv_state = native().conv1d_silu(qkv.view(B, T, -1), conv_state.contiguous(), module.conv1d.weight)
+    qkv, conv_state = native().conv1d_silu(qkv.view(B, T, -1), conv_state.contiguous(), f32(module.conv1d.weight))
     rec_state = rec_state.contiguous()
-    core = native().gdn_forward(qkv, ab[:, :Hv], ab[:, Hv:], module.A_log, module.dt_bias, rec_state, Hk, Hv, D)
-    core = native().gated_rmsnorm(core, z, module.norm.weight, module.norm.eps)
+    core = native().gdn_forward(qkv, ab[:, :Hv], ab[:, Hv:], f32(module.A_log), f32(module.dt_bias), rec_state, Hk, Hv, D)
+    core = native().gated_rmsnorm(core, z, f32(module.norm.weight), module.norm.eps)
     return linear(core.view(B * T, Hv * D), module.out_proj.weight).view(B, T, C), conv_state, rec_state

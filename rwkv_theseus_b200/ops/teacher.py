@@ -10,7 +10,7 @@ import torch
 from torch.nn import functional as F
 
 from . import reference as R
-from . import native
+from . import f32, native
 
 
 def _cuda(x):
@@ -27,14 +27,14 @@ def linear(x, weight):
 
 def rmsnorm(x, weight, eps):
     if _cuda(x):
-        return native().rmsnorm_1p(x.contiguous(), weight, float(eps))
+        return native().rmsnorm_1p(x.contiguous(), f32(weight), float(eps))
     return R.rmsnorm_1p(x, weight, eps)
 
 
 def add_rmsnorm(x, h, weight, eps):
     """(x + h, rmsnorm(x + h)) with the sum rounded to x.dtype first (as HF does)."""
     if _cuda(x):
-        return tuple(native().add_rmsnorm_1p(x.contiguous(), h.contiguous(), weight, float(eps)))
+        return tuple(native().add_rmsnorm_1p(x.contiguous(), h.contiguous(), f32(weight), float(eps)))
     s = x + h
     return s, R.rmsnorm_1p(s, weight, eps)
 

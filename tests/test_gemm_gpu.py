@@ -63,3 +63,22 @@ def test_strided_rows_and_current_stream():
         out = native().gemm(A, False, B, False, 0, 1.0, None)
     torch.cuda.current_stream().wait_stream(stream)
     _check(out, ref)
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 5120, 5120), (8, 10240, 5120), (8, 5120, 17408), (32, 384, 200),
+                                   (5, 130, 72)])
+def test_skinny_decode_gemm_matches_fp32(M, N, K):
+    """M <= 32: split-K weight streaming path (swapped tiles, fp32 atomics), plain and SwiGLU."""
+    if not torch.cuda.is_available():
+        pytest.skip("CUDA unavailable")
+    from rwkv_theseus_b200.ops import native
+    g = torch.Generator(device="cuda").manual_seed(M * 7 + N)
+    x = (torch.randn(M, K, device="cuda", generator=g) * 0.5).to(torch.bfloat16)
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.05).to(torch.bfloat16)
+    u = (torch.randn(N, K, device="cuda", generator=g) * 0.05).to(torch.bfloat16)
+    ref = x.float() @ w.float().t()
+    got = native().gemm(x, False, w, False, 0, 1.0, None)
+    torch.testing.assert_close(got.float(), ref, atol=2e-2, rtol=2e-2)
+    sw = native().gemm_swiglu(x, w, u)
+    ref_sw = torch.nn.functional.silu(ref) * (x.float() @ u.float().t())
+    torch.testing.assert_close(sw.float(), ref_sw, atol=2e-2, rtol=2e-2)

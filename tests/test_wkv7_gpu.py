@@ -70,3 +70,18 @@ def test_runs_on_current_stream():
             actual, _ = wkv7(*xs, s0)
         torch.cuda.current_stream().wait_stream(stream)
     assert torch.equal(actual, expected)
+
+
+@cuda
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("B,T,H,N", [(8, 1, 4, 64), (2, 3, 2, 32), (3, 4, 2, 128), (1, 1, 80, 64)])
+def test_decode_step_kernel_matches_reference(dtype, B, T, H, N):
+    """Inference calls of 1-4 tokens (no checkpoints) use the token-by-token kernel."""
+    xs, s0 = _inputs(B, T, H, N, dtype)
+    xs = [x.detach() for x in xs]
+    with torch.no_grad():
+        y, state = wkv7(*xs, s0.detach())
+        yr, sr = reference(*xs, s0.detach())
+    bf = dtype == torch.bfloat16
+    torch.testing.assert_close(y, yr, atol=2e-3 if bf else 2e-5, rtol=2e-2 if bf else 1e-4)
+    torch.testing.assert_close(state, sr, atol=3e-5, rtol=3e-4)
