@@ -70,12 +70,18 @@ def main():
         B, H, N = 1, 80, 64
         xs = [torch.randn(B, T, H, N, device="cuda").to(torch.bfloat16) for _ in range(6)]
         s0 = torch.zeros(B, H, N, N, device="cuda")
-        ms = timed(lambda: ext.wkv7_forward(*xs, s0, True), a.warmup, a.iters)
+        fwd = lambda: ext.wkv7_forward(*xs, s0, True)  # noqa: E731
+        ms = timed(fwd, a.warmup, a.iters)
         print(json.dumps({"kernel": "wkv7_forward", "T": T, "ms": ms}), flush=True)
+        if a.profile:
+            kernel_times(fwd)
         y, end, ck = ext.wkv7_forward(*xs, s0, True)
         dy, dend = torch.randn_like(y), torch.zeros_like(end)
-        ms = timed(lambda: ext.wkv7_backward(*xs, ck, dy, dend), a.warmup, a.iters)
+        bwd = lambda: ext.wkv7_backward(*xs, ck, dy, dend)  # noqa: E731
+        ms = timed(bwd, a.warmup, a.iters)
         print(json.dumps({"kernel": "wkv7_backward", "T": T, "ms": ms}), flush=True)
+        if a.profile:
+            kernel_times(bwd)
 
 
 if __name__ == "__main__":

@@ -9,6 +9,10 @@ extern "C" {
 #endif
 
 int rt_wkv7_chunk_len();
+long rt_wkv7_scan_workspace_floats(int B, int T, int H, int N);
+cudaError_t rt_wkv7_scan_forward(int dtype, int B, int T, int H, int N, const void* r, const void* w, const void* k,
+                                 const void* v, const void* a, const void* b, const float* s0, void* y, float* s_end,
+                                 float* checkpoints, float* work, cudaStream_t stream);
 cudaError_t rt_wkv7_forward(int dtype, int B, int T, int H, int N, const void* r, const void* w, const void* k,
                             const void* v, const void* a, const void* b, const float* s0, void* y, float* s_end,
                             float* checkpoints, cudaStream_t stream);

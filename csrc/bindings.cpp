@@ -45,6 +45,16 @@ std::vector<at::Tensor> wkv7_forward(at::Tensor r, at::Tensor w, at::Tensor k, a
   auto y = at::empty_like(r);
   auto end = at::empty_like(s0);
   auto ckpt = save_checkpoints ? at::empty({B, H, chunks + 1, N, N}, s0.options()) : at::empty({0}, s0.options());
+  const long scan_ws = T > 4 ? rt_wkv7_scan_workspace_floats(B, T, H, N) : 0;
+  if (scan_ws > 0) {  // head sizes 32/64/128: parallel per-chunk pass + light serial scan
+    auto work = at::empty({scan_ws}, s0.options());
+    check_cuda(rt_wkv7_scan_forward(dtype_code(r), B, T, H, N, r.data_ptr(), w.data_ptr(), k.data_ptr(),
+                                    v.data_ptr(), a.data_ptr(), b.data_ptr(), s0.data_ptr<float>(), y.data_ptr(),
+                                    end.data_ptr<float>(), save_checkpoints ? ckpt.data_ptr<float>() : nullptr,
+                                    work.data_ptr<float>(), stream_of(r)),
+               "wkv7_forward (scan)");
+    return {y, end, ckpt};
+  }
   check_cuda(rt_wkv7_forward(dtype_code(r), B, T, H, N, r.data_ptr(), w.data_ptr(), k.data_ptr(), v.data_ptr(),
                              a.data_ptr(), b.data_ptr(), s0.data_ptr<float>(), y.data_ptr(), end.data_ptr<float>(),
                              save_checkpoints ? ckpt.data_ptr<float>() : nullptr, stream_of(r)),

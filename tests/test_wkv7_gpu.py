@@ -21,7 +21,7 @@ def _inputs(B, T, H, N, dtype, scale=.5):
 
 @cuda
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-@pytest.mark.parametrize("B,T,H,N", [(2, 7, 2, 8), (2, 7, 2, 64), (1, 37, 3, 64), (2, 16, 1, 128),
+@pytest.mark.parametrize("B,T,H,N", [(2, 7, 2, 8), (2, 7, 2, 64), (1, 37, 3, 64), (2, 16, 1, 128), (2, 70, 3, 32),
                                      (1, 50, 2, 40), (1, 1, 2, 64), (3, 100, 2, 16)])
 def test_forward_backward_match_autograd(dtype, B, T, H, N):
     xs, s0 = _inputs(B, T, H, N, dtype)
