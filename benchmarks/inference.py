@@ -31,6 +31,7 @@ def main():
     p.add_argument("--prefill-chunk", type=int, default=4096)
     p.add_argument("--model", choices=("27b", "small"), default="27b")
     p.add_argument("--profile", action="store_true", help="per-kernel times of one decode step (profiled)")
+    p.add_argument("--graph", action="store_true", help="replay the decode step as a CUDA graph")
     a = p.parse_args()
     spec = MODEL_27B if a.model == "27b" else MODEL_SMALL
     cfg = HybridConfig(**spec, layer_types=layer_types(spec["num_hidden_layers"]))
@@ -44,7 +45,7 @@ def main():
     g = torch.Generator(device=device).manual_seed(7)
     prompt = torch.randint(0, cfg.vocab_size, (a.batch, a.prompt), device=device, generator=g)
     warm = torch.randint(0, cfg.vocab_size, (a.batch, 64), device=device, generator=g)
-    generate(runner, warm, 4, prefill_chunk=a.prefill_chunk)  # warm-up: every kernel path once
+    generate(runner, warm, 4, prefill_chunk=a.prefill_chunk, graph=a.graph)  # warm-up: every kernel path once
     torch.cuda.synchronize()
     events = []
 
@@ -68,16 +69,17 @@ def main():
             events.append(e)
         return original(ids, *args, **kwargs)
     runner.forward = forward
-    out = generate(runner, prompt, a.new, prefill_chunk=a.prefill_chunk, on_token=on_token)
+    out = generate(runner, prompt, a.new, prefill_chunk=a.prefill_chunk, on_token=on_token, graph=a.graph)
     torch.cuda.synchronize()
     runner.forward = original
     prefill_ms = start.elapsed_time(prefilled)
-    steps = sorted(events[i].elapsed_time(events[i + 1]) for i in range(len(events) - 1))
+    steps = sorted(events[i].elapsed_time(events[i + 1]) for i in range(2, len(events) - 1))  # skip the graph build
     result = {"bench": "assembled_inference", "model": f"qwen3.5-hybrid-{a.model} + {len(order)} TimeMix",
               "batch": a.batch, "prompt": a.prompt, "new_tokens": a.new, "dtype": "bf16",
               "prefill_tokens_per_s": a.batch * a.prompt / (prefill_ms / 1000), "prefill_ms": prefill_ms,
               "decode_p50_ms": steps[len(steps) // 2], "decode_p90_ms": steps[int(len(steps) * 0.9)],
               "decode_tokens_per_s": a.batch * 1000 / steps[len(steps) // 2], "generated": list(out.shape),
+              "cuda_graph": a.graph,
               "data": "uniform-random prompt ids; random-init weights"}
     print(json.dumps(result), flush=True)
     if a.profile:

@@ -21,6 +21,9 @@
 // All waits are bounded (sm100.cuh); on timeout the kernel records status 1
 // in *status and unwinds, freeing its TMEM.
 #include <cuda.h>
+#include <map>
+#include <mutex>
+#include <tuple>
 #include "../common/common.cuh"
 #include "../common/sm100.cuh"
 
@@ -41,7 +44,8 @@ struct Cfg {
   // are memory-bound and keep 8 stages of 20 KB in flight.
   static constexpr int ST = EPI == EPI_ATOMIC_T ? 8 : STAGES;
   static constexpr int ACC_COLS = NB * BN;
-  static constexpr int TMEM_COLS = 2 * ACC_COLS;
+  // two accumulators, rounded up to the power-of-two column count tcgen05.alloc takes
+  static constexpr int TMEM_COLS = 2 * ACC_COLS <= 64 ? 64 : 2 * ACC_COLS <= 128 ? 128 : 2 * ACC_COLS <= 256 ? 256 : 512;
   static constexpr uint32_t IDESC = sm100::idesc_bf16(BM, BN, A_MN, B_MN);
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM_BYTES = ST * STAGE_BYTES + BAR_BYTES + 1024;
@@ -364,25 +368,112 @@ cudaError_t launch(const void* A, long lda, const void* B0, const void* B1, long
   return cudaGetLastError();
 }
 
-// Tile width: the widest tile (least L2 traffic per FLOP, most work per pipeline stage) whose tile count
-// still covers three quarters of the SMs; otherwise the narrowest (most tiles).
-int pick_bn(int M, int N, bool swiglu) {
+// Tile width: the one whose tile count fills the persistent grid best (fraction of the last wave that is
+// busy), preferring wider tiles (less L2 traffic per FLOP) when two are within 3%. Widths that are not a
+// multiple of 64 need a K-major B operand.
+int pick_bn(int M, int N, bool swiglu, bool b_mn) {
   if (swiglu) return 128;
   const int sms = num_sms_cached();
   const long tm = (M + BM - 1) / BM;
-  for (int bn : {256, 128}) {
-    if (N < bn / 2) continue;
-    if (tm * ((N + bn - 1) / bn) * 4 >= 3L * sms) return bn;
+  int best = 64;
+  double best_eff = -1.0;
+  for (int bn : {256, 224, 192, 160, 128, 64}) {
+    if (b_mn && bn % 64) continue;
+    if (N < bn / 2 && bn != 64) continue;
+    const long tiles = tm * ((N + bn - 1) / bn);
+    const long waves = (tiles + sms - 1) / sms;
+    // useful fraction: filled slots, and the padding of the last (partial) column tile
+    const double fill = (double)tiles / (double)(waves * sms);
+    const double pad = (double)N / (double)(((N + bn - 1) / bn) * bn);
+    const double eff = fill * pad * (bn >= 128 ? 1.0 : 0.85);  // narrow tiles: lower MMA and L2 efficiency
+    if (eff > best_eff * 1.03) {
+      best_eff = eff;
+      best = bn;
+    }
   }
-  return 64;
+  return best;
 }
 
 template <bool A_MN, bool B_MN, int EPI>
 cudaError_t dispatch_bn(int bn, const void* A, long lda, const void* B0, const void* B1, long ldb, void* C, long ldc,
                         int M, int N, int K, float alpha, int* status, cudaStream_t s) {
   if (bn == 256) return launch<256, A_MN, B_MN, EPI>(A, lda, B0, B1, ldb, C, ldc, M, N, K, alpha, status, s);
+  if (bn == 192) return launch<192, A_MN, B_MN, EPI>(A, lda, B0, B1, ldb, C, ldc, M, N, K, alpha, status, s);
   if (bn == 128) return launch<128, A_MN, B_MN, EPI>(A, lda, B0, B1, ldb, C, ldc, M, N, K, alpha, status, s);
+  if constexpr (!B_MN) {
+    if (bn == 224) return launch<224, A_MN, B_MN, EPI>(A, lda, B0, B1, ldb, C, ldc, M, N, K, alpha, status, s);
+    if (bn == 160) return launch<160, A_MN, B_MN, EPI>(A, lda, B0, B1, ldb, C, ldc, M, N, K, alpha, status, s);
+  }
   return launch<64, A_MN, B_MN, EPI>(A, lda, B0, B1, ldb, C, ldc, M, N, K, alpha, status, s);
+}
+
+cudaError_t gemm_with_bn(int bn, const void* A, long lda, int a_mn, const void* B, long ldb, int b_mn, void* C,
+                         long ldc, int M, int N, int K, int epi, float alpha, int* status, cudaStream_t stream);
+
+// Tile width per problem shape, measured once: the first call of a shape with a store epilogue (outside stream
+// capture) runs every candidate width on the real operands and keeps the fastest (every width computes each
+// output with the same MMA sequence over K, so the result does not depend on the choice). Accumulating calls
+// and calls under capture use the measured width of the shape when known, else the wave-fill estimate.
+struct TileKey {
+  int M, N, K, a_mn, b_mn;
+  bool operator<(const TileKey& o) const {
+    return std::tie(M, N, K, a_mn, b_mn) < std::tie(o.M, o.N, o.K, o.a_mn, o.b_mn);
+  }
+};
+std::map<TileKey, int>& tile_cache() {
+  static std::map<TileKey, int> cache;
+  return cache;
+}
+std::mutex& tile_mutex() {
+  static std::mutex m;
+  return m;
+}
+
+int measured_bn(const TileKey& key, const void* A, long lda, const void* B, long ldb, void* C, long ldc, int epi,
+                float alpha, int* status, cudaStream_t stream) {
+  {
+    std::lock_guard<std::mutex> lock(tile_mutex());
+    auto it = tile_cache().find(key);
+    if (it != tile_cache().end()) return it->second;
+  }
+  const int guess = pick_bn(key.M, key.N, false, key.b_mn != 0);
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (epi == EPI_F32_ACCUM || cudaStreamIsCapturing(stream, &cap) != cudaSuccess ||
+      cap != cudaStreamCaptureStatusNone)
+    return guess;
+  cudaEvent_t e0, e1;
+  if (cudaEventCreate(&e0) != cudaSuccess) return guess;
+  if (cudaEventCreate(&e1) != cudaSuccess) {
+    cudaEventDestroy(e0);
+    return guess;
+  }
+  int best = guess;
+  float best_ms = 1e30f;
+  for (int bn : {256, 224, 192, 160, 128}) {
+    if (key.b_mn && bn % 64) continue;
+    if (key.N < bn / 2) continue;
+    float ms = 1e30f;
+    for (int rep = 0; rep < 2; ++rep) {
+      cudaEventRecord(e0, stream);
+      if (gemm_with_bn(bn, A, lda, key.a_mn, B, ldb, key.b_mn, C, ldc, key.M, key.N, key.K, epi, alpha, status,
+                       stream) != cudaSuccess)
+        break;
+      cudaEventRecord(e1, stream);
+      if (cudaEventSynchronize(e1) != cudaSuccess) break;
+      float t = 0.f;
+      cudaEventElapsedTime(&t, e0, e1);
+      ms = rep ? (t < ms ? t : ms) : 1e30f;  // first run warms up
+    }
+    if (ms < best_ms) {
+      best_ms = ms;
+      best = bn;
+    }
+  }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  std::lock_guard<std::mutex> lock(tile_mutex());
+  tile_cache()[key] = best;
+  return best;
 }
 
 }  // namespace
@@ -395,7 +486,15 @@ extern "C" cudaError_t rt_gemm_bf16(const void* A, long lda, int a_mn, const voi
   if (M <= 0 || N <= 0 || K <= 0) return cudaSuccess;
   if ((lda & 7) || (ldb & 7) || (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15))
     return cudaErrorInvalidValue;
-  const int bn = pick_bn(M, N, false);
+  const TileKey key{M, N, K, a_mn != 0, b_mn != 0};
+  const int bn = measured_bn(key, A, lda, B, ldb, C, ldc, epi, alpha, status, stream);
+  return gemm_with_bn(bn, A, lda, a_mn, B, ldb, b_mn, C, ldc, M, N, K, epi, alpha, status, stream);
+}
+
+namespace {
+
+cudaError_t gemm_with_bn(int bn, const void* A, long lda, int a_mn, const void* B, long ldb, int b_mn, void* C,
+                         long ldc, int M, int N, int K, int epi, float alpha, int* status, cudaStream_t stream) {
 #define RT_G(AM, BMN)                                                                                         \
   switch (epi) {                                                                                              \
     case EPI_BF16: return dispatch_bn<AM, BMN, EPI_BF16>(bn, A, lda, B, B, ldb, C, ldc, M, N, K, alpha, status, stream); \
@@ -408,6 +507,8 @@ extern "C" cudaError_t rt_gemm_bf16(const void* A, long lda, int a_mn, const voi
   RT_G(true, true)
 #undef RT_G
 }
+
+}  // namespace
 
 namespace {
 

@@ -85,11 +85,68 @@ def load_export(path, device="cuda", base_model=None):
 
 
 @torch.no_grad()
-def generate(runner, prompt, new_tokens, prefill_chunk=4096, on_token=None):
+class DecodeGraph:
+    """One greedy decode step (T = 1 forward, lm_head, argmax) captured as a CUDA graph.
+
+    Built after an eager decode step, so every recurrent state exists in its final shape. The GDN conv
+    windows / delta-rule states and the TimeMix shift / WKV states are kept in persistent buffers: the
+    captured step reads them, and copies the new states back into them at its end (the delta-rule state is
+    already updated in place). Replays therefore advance exactly like eager steps; the host only writes the
+    input token and advances the cache cursor. Needs a model whose attention blocks are all replaced (no KV
+    cache grows during decoding).
+    """
+
+    def __init__(self, runner, token):
+        from .models.runner import AttentionAdapter
+        model = runner.model
+        layers = model.model.layers
+        if any(kind == "full_attention" and not isinstance(getattr(layers[i], "self_attn", None), AttentionAdapter)
+               for i, kind in enumerate(model.config.layer_types)):
+            raise ValueError("graph decoding needs every full-attention block replaced by a TimeMix")
+        self.runner = runner
+        self.ids = token.clone()
+        head = model.lm_head.weight
+        self.gdn = [(layer, layer["conv"], layer["recurrent"]) for layer in runner.cache.layers if "recurrent" in layer]
+        self.adapters = [(b.self_attn, {k: v.clone() for k, v in b.self_attn.state.items()})
+                         for b in layers if isinstance(getattr(b, "self_attn", None), AttentionAdapter)]
+        for adapter, persistent in self.adapters:
+            adapter.state = persistent
+        cursor = runner.cache.cursor
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(side), torch.cuda.graph(self.graph):
+            hidden = runner.forward(self.ids)
+            self.out = (hidden[:, -1:].to(head.dtype) @ head.t()).argmax(-1)
+            for layer, conv, rec in self.gdn:
+                if layer["conv"] is not conv:
+                    conv.copy_(layer["conv"])
+                if layer["recurrent"] is not rec:
+                    rec.copy_(layer["recurrent"])
+            for adapter, persistent in self.adapters:
+                for key, value in persistent.items():
+                    value.copy_(adapter.state[key])
+        torch.cuda.current_stream().wait_stream(side)
+        # capture ran nothing: point the Python-side state at the persistent buffers again
+        for layer, conv, rec in self.gdn:
+            layer["conv"], layer["recurrent"] = conv, rec
+        for adapter, persistent in self.adapters:
+            adapter.state = persistent
+        runner.cache.cursor = cursor
+
+    def step(self, token):
+        self.ids.copy_(token)
+        self.graph.replay()
+        self.runner.cache.cursor += 1
+        return self.out.clone()
+
+
+def generate(runner, prompt, new_tokens, prefill_chunk=4096, on_token=None, graph=False):
     """Greedy decoding: chunked prefill of ``prompt`` [B, T], then ``new_tokens`` T=1 steps.
 
     Returns the generated ids [B, new_tokens]. ``on_token(step, ids)`` is called
-    after each decode step (timing hooks, streaming).
+    after each decode step (timing hooks, streaming). ``graph=True`` replays the
+    decode step as a CUDA graph after the first eager step (assembled models).
     """
     runner.reset()
     head = runner.model.lm_head.weight
@@ -98,9 +155,15 @@ def generate(runner, prompt, new_tokens, prefill_chunk=4096, on_token=None):
         hidden = runner.forward(prompt[:, start:start + prefill_chunk])
     token = (hidden[:, -1:].to(head.dtype) @ head.t()).argmax(-1)
     out = [token]
+    stepper = None
     for step in range(1, new_tokens):
-        hidden = runner.forward(token)
-        token = (hidden[:, -1:].to(head.dtype) @ head.t()).argmax(-1)
+        if stepper is not None:
+            token = stepper.step(token)
+        else:
+            hidden = runner.forward(token)
+            token = (hidden[:, -1:].to(head.dtype) @ head.t()).argmax(-1)
+            if graph and step + 1 < new_tokens:
+                stepper = DecodeGraph(runner, token)
         out.append(token)
         if on_token is not None:
             on_token(step, token)

@@ -171,3 +171,26 @@ def test_fused_inference_forward_matches_module(B, T):
     # the module runs the decay LoRA in bf16, the fused path in fp32: a few state entries differ at bf16 level
     torch.testing.assert_close(got_state["wkv"], want_state["wkv"].float(), rtol=2e-2, atol=8e-3)
     assert torch.equal(got_state["shift"], want_state["shift"])
+
+
+@cuda
+def test_graph_decoding_matches_eager():
+    """Assembled small hybrid (every attention block a TimeMix): CUDA-graph decode steps give the same tokens."""
+    from rwkv_theseus_b200.inference import generate
+    from rwkv_theseus_b200.models.hf_io import random_model
+    from rwkv_theseus_b200.models.qwen35 import HybridConfig
+    from rwkv_theseus_b200.models.runner import Runner, install, migration_order
+    cfg = HybridConfig(vocab_size=512, hidden_size=256, intermediate_size=512, num_hidden_layers=4,
+                       num_attention_heads=4, num_key_value_heads=2, head_dim=64, linear_num_key_heads=2,
+                       linear_num_value_heads=4, linear_key_head_dim=64, linear_value_head_dim=64,
+                       linear_conv_kernel_dim=4, layer_types=["linear_attention", "full_attention"] * 2,
+                       rope_theta=1e6, partial_rotary_factor=0.25)
+    model = random_model(cfg, "cuda", seed=4)
+    for i, layer in enumerate(migration_order(model, 2)):
+        torch.manual_seed(i)
+        install(model, layer, {"head_size": 64, "backend": "cuda"})
+    runner = Runner(model)
+    prompt = torch.randint(0, 512, (2, 40), device="cuda", generator=torch.Generator(device="cuda").manual_seed(1))
+    eager = generate(runner, prompt, 12)
+    graphed = generate(runner, prompt, 12, graph=True)
+    assert torch.equal(eager, graphed)
