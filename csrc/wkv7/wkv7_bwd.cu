@@ -100,6 +100,21 @@ RT_DEVICE float rowdot(const float* x, const float* y) {
   return acc;
 }
 
+// sum_j x[j] y[j] z[j] over NP (float4; all three 16-byte aligned)
+template <int NP>
+RT_DEVICE float dot3(const float* x, const float* y, const float* z) {
+  const float4* p = reinterpret_cast<const float4*>(x);
+  const float4* q = reinterpret_cast<const float4*>(y);
+  const float4* w = reinterpret_cast<const float4*>(z);
+  float acc = 0.f;
+#pragma unroll 4
+  for (int u = 0; u < NP / 4; ++u) {
+    const float4 a = p[u], b = q[u], c = w[u];
+    acc += a.x * b.x * c.x + a.y * b.y * c.y + a.z * b.z * c.z + a.w * b.w * c.w;
+  }
+  return acc;
+}
+
 // W = (I - Mab)^{-1} for strictly lower Mab ([L][L+1]); 16 threads, one column each.
 RT_DEVICE void unit_lower_inverse(const float* Mab, float* W) {
   if (threadIdx.x < L) {
@@ -237,11 +252,7 @@ wkv7_bwd_state_kernel(int T_, int H, int N, const float* __restrict__ prep, cons
     // dU[s][i] = sum_j Bh[s][j] dS[i][j] + sum_{t>=s} Mrb[t][s] dY[t][i]
     for (int e = threadIdx.x; e < L * R; e += 128) {
       const int s = e / R, i = e % R;
-      float u = 0.f;
-      const float* bs = Bh + s * NP;
-      const float* di = dS + i * SP;
-#pragma unroll 8
-      for (int j = 0; j < NP; ++j) u += bs[j] * di[j];
+      float u = rowdot<NP>(Bh + s * NP, dS + i * SP);
       for (int t = s; t < L; ++t) u += Mrb[t * L + s] * dY[t * R + i];
       dU[e] = u;
     }
@@ -255,12 +266,22 @@ wkv7_bwd_state_kernel(int T_, int H, int N, const float* __restrict__ prep, cons
     }
     __syncthreads();
     // dS <- dS diag(D_L) + dY^T R~ + dZ^T A~
-    for (int e = threadIdx.x; e < R * NP; e += 128) {
-      const int i = e / NP, j = e % NP;
-      float acc = dS[i * SP + j] * DL[j];
+    for (int e = threadIdx.x; e < R * (NP / 4); e += 128) {  // four consecutive keys per thread
+      const int i = e / (NP / 4), j = (e % (NP / 4)) * 4;
+      float4 acc = *reinterpret_cast<const float4*>(dS + i * SP + j);
+      const float4 d = *reinterpret_cast<const float4*>(DL + j);
+      acc.x *= d.x; acc.y *= d.y; acc.z *= d.z; acc.w *= d.w;
 #pragma unroll
-      for (int t = 0; t < L; ++t) acc += dY[t * R + i] * Rt[t * NP + j] + dZ[t * R + i] * At[t * NP + j];
-      dS[i * SP + j] = acc;
+      for (int t = 0; t < L; ++t) {
+        const float y = dY[t * R + i], z = dZ[t * R + i];
+        const float4 r4 = *reinterpret_cast<const float4*>(Rt + t * NP + j);
+        const float4 a4 = *reinterpret_cast<const float4*>(At + t * NP + j);
+        acc.x += y * r4.x + z * a4.x;
+        acc.y += y * r4.y + z * a4.y;
+        acc.z += y * r4.z + z * a4.z;
+        acc.w += y * r4.w + z * a4.w;
+      }
+      *reinterpret_cast<float4*>(dS + i * SP + j) = acc;
     }
     __syncthreads();
   }
@@ -367,11 +388,7 @@ wkv7_bwd_grad_kernel(int T_, int H, int N, const T* __restrict__ pr, const T* __
       float z = rowdot<NP>(c.a + t * SP, S0 + ii * SP);
       for (int s2 = 0; s2 < t; ++s2) z += Mak[t * (L + 1) + s2] * V[s2 * VSP + ii];
       DZ[t * VSP + ii] = z;
-      float u = 0.f;
-      const float* bs = c.b + t * SP;
-      const float* di = DS + ii * SP;
-#pragma unroll 8
-      for (int j = 0; j < NP; ++j) u += bs[j] * c.dl[j] * di[j];
+      float u = dot3<NP>(c.b + t * SP, c.dl, DS + ii * SP);
       for (int t2 = t; t2 < L; ++t2) u += Mrb[t2 * (L + 1) + t] * DY[t2 * VSP + ii];
       DU[t * VSP + ii] = u;
     }
@@ -395,11 +412,7 @@ wkv7_bwd_grad_kernel(int T_, int H, int N, const T* __restrict__ pr, const T* __
     // dv (row-local, final)
     for (int e = threadIdx.x; e < L * VR; e += GT) {
       const int s2 = e / VR, ii = e % VR, i = i0 + ii;
-      float g = 0.f;
-      const float* ks = c.k + s2 * SP;
-      const float* di = DS + ii * SP;
-#pragma unroll 8
-      for (int j = 0; j < NP; ++j) g += ks[j] * c.dl[j] * di[j];
+      float g = dot3<NP>(c.k + s2 * SP, c.dl, DS + ii * SP);
       for (int t = s2; t < L; ++t) g += Mrk[t * (L + 1) + s2] * DY[t * VSP + ii];
       for (int t = s2 + 1; t < L; ++t) g += Mak[t * (L + 1) + s2] * DZ[t * VSP + ii];
       const int tg = t0 + s2;
@@ -410,28 +423,54 @@ wkv7_bwd_grad_kernel(int T_, int H, int N, const T* __restrict__ pr, const T* __
       const int which = e / (L * L), t = (e % (L * L)) / L, s2 = e % L;
       const bool keep = which < 2 ? s2 < t : s2 <= t;
       if (!keep) continue;
-      const float* x = (which < 2 ? DZ : DY) + t * VSP;
-      const float* y = ((which & 1) ? V : U) + s2 * VSP;
+      const float4* x = reinterpret_cast<const float4*>((which < 2 ? DZ : DY) + t * VSP);
+      const float4* y = reinterpret_cast<const float4*>(((which & 1) ? V : U) + s2 * VSP);
       float acc = 0.f;
-#pragma unroll 8
-      for (int ii = 0; ii < VR; ++ii) acc += x[ii] * y[ii];
+#pragma unroll 4
+      for (int q = 0; q < VR / 4; ++q) {
+        const float4 m = x[q], n = y[q];
+        acc += m.x * n.x + m.y * n.y + m.z * n.z + m.w * n.w;
+      }
       dM[which * MAT + t * (L + 1) + s2] += acc;
     }
-    for (int e = threadIdx.x; e < L * NP; e += GT) {
-      const int t = e / NP, j = e % NP, o = t * SP + j;
-      float rd = 0.f, ad = 0.f, bhat = 0.f, khat = 0.f;
-#pragma unroll 4
-      for (int ii = 0; ii < VR; ++ii) {
-        const float s0v = S0[ii * SP + j], dsv = DS[ii * SP + j];
-        rd += DY[t * VSP + ii] * s0v;
-        ad += DZ[t * VSP + ii] * s0v;
-        bhat += U[t * VSP + ii] * dsv;
-        khat += V[t * VSP + ii] * dsv;
+    {  // key-side sums over this pass's rows: thread = (4 steps, key j, part of the rows); 4 x 4 register block
+      constexpr int TQ = L / 4;
+      constexpr int PARTS0 = GT / (TQ * NP) > 0 ? GT / (TQ * NP) : 1;
+      constexpr int PARTS = PARTS0 < VR / 4 ? PARTS0 : VR / 4;  // at least 4 rows (one float4) per part
+      constexpr int ROWS = VR / PARTS;
+      for (int e = threadIdx.x; e < TQ * NP * PARTS; e += GT) {
+        const int part = e / (TQ * NP), tq = (e / NP) % TQ, j = e % NP, tb = 4 * tq;
+        float rd[4] = {}, ad[4] = {}, bh[4] = {}, kh[4] = {};
+        for (int i4 = part * ROWS; i4 < (part + 1) * ROWS; i4 += 4) {
+          float s0v[4], dsv[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            s0v[u] = S0[(i4 + u) * SP + j];
+            dsv[u] = DS[(i4 + u) * SP + j];
+          }
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            const int o = (tb + r) * VSP + i4;
+            const float4 dy4 = *reinterpret_cast<const float4*>(DY + o);
+            const float4 dz4 = *reinterpret_cast<const float4*>(DZ + o);
+            const float4 u4 = *reinterpret_cast<const float4*>(U + o);
+            const float4 v4 = *reinterpret_cast<const float4*>(V + o);
+            rd[r] += dy4.x * s0v[0] + dy4.y * s0v[1] + dy4.z * s0v[2] + dy4.w * s0v[3];
+            ad[r] += dz4.x * s0v[0] + dz4.y * s0v[1] + dz4.z * s0v[2] + dz4.w * s0v[3];
+            bh[r] += u4.x * dsv[0] + u4.y * dsv[1] + u4.z * dsv[2] + u4.w * dsv[3];
+            kh[r] += v4.x * dsv[0] + v4.y * dsv[1] + v4.z * dsv[2] + v4.w * dsv[3];
+          }
+        }
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const int o = (tb + r) * SP + j;
+          if (PARTS == 1) {
+            RD[o] += rd[r]; AD[o] += ad[r]; BH[o] += bh[r]; KH[o] += kh[r];
+          } else {
+            atomicAdd(RD + o, rd[r]); atomicAdd(AD + o, ad[r]); atomicAdd(BH + o, bh[r]); atomicAdd(KH + o, kh[r]);
+          }
+        }
       }
-      RD[o] += rd;
-      AD[o] += ad;
-      BH[o] += bhat;
-      KH[o] += khat;
     }
     if (threadIdx.x < NP) {
       const int j = threadIdx.x;

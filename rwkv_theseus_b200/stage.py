@@ -233,3 +233,17 @@ class Student:
         self.steps_done = int(scheduler["last_epoch"])
         if self.fused is not None:
             self.fused.refresh_weights()
+
+
+def promote(topo, model, layer, cfg):
+    """Legacy sequential-stage handoff (reference ``theseus/stage.py:47-57``): the leader's trained student
+    of ``layer`` is broadcast to every rank as bf16 and installed frozen in place of the attention block."""
+    from .models.runner import install
+    topo.barrier()
+    weights = None
+    if topo.rank == topo.leader:
+        core = model.model.layers[layer].self_attn.core
+        weights = {k: v.detach().cpu().to(torch.bfloat16) for k, v in core.state_dict().items()}
+    weights = topo.broadcast_weights(weights)
+    install(model, layer, cfg, weights=weights, trainable=False)
+    topo.barrier()
