@@ -59,13 +59,13 @@ def main():
     p = argparse.ArgumentParser()
     p.add_argument("--numel", type=int, default=112_459_520)
     p.add_argument("--iters", type=int, default=10)
-    p.add_argument("--blocks", type=int, default=148)
+    p.add_argument("--blocks", default="148", help="comma-separated block counts to compare")
     p.add_argument("--profile", action="store_true")
     a = p.parse_args()
     topo = Topology("nccl", 5)
     dev, n, N = topo.device, a.numel, topo.world
     st = student(n, dev)
-    ex = PeerGradExchange(topo, blocks=a.blocks, limit_s=60.0)
+    ex = PeerGradExchange(topo, blocks=int(a.blocks.split(",")[0]), limit_s=60.0)
     ex.register(st)
     g = torch.randn(n, device=dev)
     step = [0]
@@ -110,15 +110,20 @@ def main():
             for name, ts in sorted(rows.items(), key=lambda kv: -sum(kv[1])):
                 print(json.dumps({"kernel": name, "calls": len(ts), "avg_us": sum(ts) / len(ts)}), flush=True)
     base = timed(copy_only, a.iters, topo)
-    t_peer = timed(peer, a.iters, topo) - base
-    ex.check()
-    t_nccl = timed(nccl, a.iters, topo) - base
     frac = (N - 1) / N
     link_ms = 6 * n * frac / (LINK_GBS * 1e9) * 1e3
-    if topo.rank == 0:
-        print(json.dumps({"bench": "layer_exchange", "n_gpus": N, "numel": n, "peer_ms": t_peer, "nccl_ms": t_nccl,
-                          "nvlink_roofline_ms": link_ms, "peer_fraction_of_roofline": link_ms / t_peer,
-                          "speedup_vs_nccl": t_nccl / t_peer, "blocks": a.blocks}), flush=True)
+    t_nccl = None
+    for blocks in [int(b) for b in a.blocks.split(",")]:
+        ex.blocks = blocks
+        t_peer = timed(peer, a.iters, topo) - base
+        ex.check()
+        if t_nccl is None:
+            t_nccl = timed(nccl, a.iters, topo) - base
+        if topo.rank == 0:
+            print(json.dumps({"bench": "layer_exchange", "n_gpus": N, "numel": n, "peer_ms": t_peer,
+                              "nccl_ms": t_nccl, "nvlink_roofline_ms": link_ms,
+                              "peer_fraction_of_roofline": link_ms / t_peer, "speedup_vs_nccl": t_nccl / t_peer,
+                              "blocks": blocks}), flush=True)
     ex.close()
     topo.close()
 

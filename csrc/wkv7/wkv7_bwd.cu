@@ -317,7 +317,8 @@ __global__ void __launch_bounds__(GT)
 wkv7_bwd_grad_kernel(int T_, int H, int N, const T* __restrict__ pr, const T* __restrict__ pw,
                      const T* __restrict__ pk, const T* __restrict__ pv, const T* __restrict__ pa,
                      const T* __restrict__ pb, const T* __restrict__ pdy, const float* __restrict__ checkpoints,
-                     const float* __restrict__ dstate, float* __restrict__ dr, float* __restrict__ dw,
+                     const float* __restrict__ dstate, const float* __restrict__ prep, float* __restrict__ dr,
+                     float* __restrict__ dw,
                      float* __restrict__ dk, float* __restrict__ dv, float* __restrict__ da,
                      float* __restrict__ db) {
   using K = Keys<NP>;
@@ -350,22 +351,30 @@ wkv7_bwd_grad_kernel(int T_, int H, int N, const T* __restrict__ pr, const T* __
   const float* s0 = checkpoints + ((long)bh * (chunks + 1) + ch) * NN;
   const float* dse = dstate + ((long)bh * chunks + ch) * NN;
   load_keys<T, NP>(c, pr, pw, pk, pa, pb, T_, H, N, batch, head, t0, GT);
+  // W = (I - Mab)^{-1} and Mrb come from the prep record; Mak and Mrk are formed here
+  const float* rec = prep + ((long)bh * chunks + ch) * Prep<NP>::FLOATS + 3 * L * NP + NP;
   for (int e = threadIdx.x; e < 4 * L * L; e += GT) {
     const int which = e / (L * L), t = (e % (L * L)) / L, s = e % L;
-    const float* x = (which < 2 ? c.a : c.r) + t * SP;
-    const float* y = ((which & 1) ? c.k : c.b) + s * SP;
     const bool keep = which < 2 ? s < t : s <= t;
-    M[which * MAT + t * (L + 1) + s] = keep ? rowdot<NP>(x, y) : 0.f;
+    float m;
+    if (which == 0) {
+      m = 0.f;  // Mab itself is not needed once W is known
+    } else if (which == 2) {
+      m = rec[L * L + t * L + s];
+    } else {
+      const float* x = (which < 2 ? c.a : c.r) + t * SP;
+      m = keep ? rowdot<NP>(x, c.k + s * SP) : 0.f;
+    }
+    M[which * MAT + t * (L + 1) + s] = m;
     dM[which * MAT + t * (L + 1) + s] = 0.f;
+    if (which == 0) W[t * (L + 1) + s] = rec[t * L + s];
   }
   for (int e = threadIdx.x; e < L * SP; e += GT) RD[e] = AD[e] = BH[e] = KH[e] = 0.f;
   if (threadIdx.x < NP) dDLd[threadIdx.x] = 0.f;
   __syncthreads();
-  const float* Mab = M;
   const float* Mak = M + MAT;
   const float* Mrb = M + 2 * MAT;
   const float* Mrk = M + 3 * MAT;
-  unit_lower_inverse(Mab, W);
   for (int i0 = 0; i0 < NP; i0 += VR) {
     // slices of this pass: value rows i0 .. i0+VR
     for (int e = threadIdx.x; e < L * VR; e += GT) {
@@ -375,11 +384,19 @@ wkv7_bwd_grad_kernel(int T_, int H, int N, const T* __restrict__ pr, const T* __
       V[tt * VSP + ii] = ok ? rt::to_f<T>(pv[idx]) : 0.f;
       DY[tt * VSP + ii] = ok ? rt::to_f<T>(pdy[idx]) : 0.f;
     }
-    for (int e = threadIdx.x; e < VR * NP; e += GT) {
-      const int ii = e / NP, j = e % NP, i = i0 + ii;
-      const bool ok = i < N && j < N;
-      S0[ii * SP + j] = ok ? s0[(long)i * N + j] : 0.f;
-      DS[ii * SP + j] = ok ? dse[(long)i * N + j] : 0.f;
+    if (N == NP) {  // full rows: 16-byte loads
+      for (int e = threadIdx.x; e < VR * (NP / 4); e += GT) {
+        const int ii = e / (NP / 4), j = (e % (NP / 4)) * 4, i = i0 + ii;
+        *reinterpret_cast<float4*>(S0 + ii * SP + j) = __ldg(reinterpret_cast<const float4*>(s0 + (long)i * N + j));
+        *reinterpret_cast<float4*>(DS + ii * SP + j) = __ldg(reinterpret_cast<const float4*>(dse + (long)i * N + j));
+      }
+    } else {
+      for (int e = threadIdx.x; e < VR * NP; e += GT) {
+        const int ii = e / NP, j = e % NP, i = i0 + ii;
+        const bool ok = i < N && j < N;
+        S0[ii * SP + j] = ok ? s0[(long)i * N + j] : 0.f;
+        DS[ii * SP + j] = ok ? dse[(long)i * N + j] : 0.f;
+      }
     }
     __syncthreads();
     // Z (into DZ) and dU, row-local
@@ -558,7 +575,7 @@ cudaError_t launch(int B, int T_, int H, int N, const void* r, const void* w, co
                                      (int)g_bytes));
   wkv7_bwd_grad_kernel<T, NP><<<dim3(chunks, B * H), GT, g_bytes, stream>>>(
       T_, H, N, (const T*)r, (const T*)w, (const T*)k, (const T*)v, (const T*)a, (const T*)b, (const T*)dy, ckpt,
-      dstate, dr, dw, dk, dv, da, db);
+      dstate, prep, dr, dw, dk, dv, da, db);
   return cudaGetLastError();
 }
 
