@@ -83,8 +83,7 @@ RT_DEVICE bool wait_all(unsigned* sig, int base, int world, unsigned epoch, unsi
     unsigned spins = 0;
     while ((int)(ld_acquire_sys(sig + base + q) - epoch) < 0) {
       if ((++spins & 63u) == 0 && now_ns() - t0 > limit_ns) {
-        atomicCAS(sig + STATUS, 0u, (unsigned)code);
-        sig[WAITED] = (unsigned)q;
+        if (atomicCAS(sig + STATUS, 0u, (unsigned)code) == 0u) sig[WAITED] = (unsigned)q;  // first expiry only
         return false;
       }
       __nanosleep(64);

@@ -32,6 +32,7 @@ from .losses import metrics
 from .models.hf_io import load_model
 from .models.runner import Capture, Runner, install, migration_order, state_to_device
 from .parallel.topology import Topology
+from .profiling import StepProfiler
 from .schedule import lr_factor
 from .stage import Student
 from .tracking import Tracker
@@ -50,6 +51,25 @@ def emit(topo, cfg, event, **fields):
         topo.tracker.log(event, fields)
 
 
+def emit_profile(topo, cfg, step, phases):
+    """``profile`` event: per-phase milliseconds of the step, maximum over ranks (Gloo gather)."""
+    import torch.distributed as dist
+    if topo.world > 1:
+        everyone = [None] * topo.world
+        dist.all_gather_object(everyone, phases)
+    else:
+        everyone = [phases]
+    merged = {}
+    for entry in everyone:
+        for name, ms in entry.items():
+            merged[name] = max(merged.get(name, 0.0), ms)
+    teacher = merged.get("teacher", 0.0)
+    students = sum(v for k, v in merged.items() if k.startswith("student_"))
+    updates = sum(v for k, v in merged.items() if k.startswith("update_"))
+    emit(topo, cfg, "profile", step=step, teacher_ms=teacher, students_ms=students, updates_ms=updates,
+         exchange_join_ms=merged.get("exchange_join", 0.0), phases_ms=merged)
+
+
 class StepEngine:
     """The hot loop body: teacher forward + per-layer student updates."""
 
@@ -58,6 +78,7 @@ class StepEngine:
         self.order, self.students, self.captures = order, students, captures
         self.device = topo.device
         self._staging = None
+        self.profiler = StepProfiler(self.device)
 
     def _to_device(self, ids):
         """Stage token ids through a persistent pinned buffer, copy asynchronously."""
@@ -72,7 +93,8 @@ class StepEngine:
 
     def step(self, reader):
         """One optimizer update of every layer; returns per-layer device reports."""
-        cfg = self.cfg
+        cfg, prof = self.cfg, self.profiler
+        prof.reset()
         for micro in range(cfg["grad_accum_steps"]):
             batch = reader.next()
             if batch is not None:
@@ -82,17 +104,21 @@ class StepEngine:
                         student.state = None
                 if self.runner.cache.cursor != batch["position"]:
                     raise RuntimeError("Cache position differs from consumed token stream")
-                self.runner.forward(self._to_device(batch["ids"]))
+                with prof.phase("teacher"):
+                    self.runner.forward(self._to_device(batch["ids"]))
             last = micro == cfg["grad_accum_steps"] - 1
             for layer in self.order:
                 student, capture = self.students[layer], self.captures[layer]
                 if batch is not None:
-                    student.micro_step(capture.x, capture.y)
+                    with prof.phase(f"student_{layer:02d}"):
+                        student.micro_step(capture.x, capture.y)
                     capture.x = capture.y = None
                 if last:
-                    student.reduce()
-                    student.update()
-        self.topo.join_grad_sync()
+                    with prof.phase(f"update_{layer:02d}"):
+                        student.reduce()
+                        student.update()
+        with prof.phase("exchange_join"):
+            self.topo.join_grad_sync()
         return {layer: s.report for layer, s in self.students.items()}
 
     def read_metrics(self, reports):
@@ -222,6 +248,8 @@ def _run(cfg, resume, stop_after, tracker):
         if step % cfg["log_interval"] == 0 or step == 1:
             emit(topo, cfg, "train", step=step, **summary,
                  tokens=next(iter(layer_metrics.values()))["tokens"], layers=layer_metrics)
+        if engine.profiler.on:
+            emit_profile(topo, cfg, step, engine.profiler.summary())
         complete = step == max_steps
         if complete and cfg["training_mode"] == "epoch" and not reader.exhausted:
             raise RuntimeError("Training ended before the local token shard was exhausted")

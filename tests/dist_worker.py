@@ -56,5 +56,15 @@ def mismatch():
     topo.close()
 
 
+def failing():
+    """Rank 1 dies before a collective; rank 0's all-reduce must end with an error (short PG timeout)."""
+    topo = Topology("gloo", timeout_minutes=0.15)
+    if topo.rank == 1:
+        raise RuntimeError("injected failure on rank 1")
+    x = torch.ones(4)
+    dist.all_reduce(x, group=topo.student_group)  # never completes normally: rank 1 is gone
+    raise AssertionError("all-reduce with a dead peer returned")
+
+
 if __name__ == "__main__":
-    {"weighted": weighted, "mismatch": mismatch}[sys.argv[1]]()
+    {"weighted": weighted, "mismatch": mismatch, "failing": failing}[sys.argv[1]]()
