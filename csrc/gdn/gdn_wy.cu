@@ -17,6 +17,7 @@
 // Reference semantics: HF Qwen3_5GatedDeltaNet chunk rule (torch_chunk_gated_delta_rule), as invoked from the
 // reference's teacher adapter (theseus/hf_model.py:38-52).
 #include "../common/common.cuh"
+#include "../common/sm100.cuh"
 
 namespace rt_gdn_wy {
 
@@ -473,6 +474,154 @@ gdn_out_kernel(const float* __restrict__ qn, const float* __restrict__ kn, const
   }
 }
 
+// ---------------------------------------------------------------- 3 (D = 128): outputs on tcgen05
+// Same outputs as gdn_out_kernel, as three bf16 MMAs per (chunk, value head) with fp32 accumulators in TMEM:
+//   D_M = [Q; K] K^T   (128 x 64, rows 0..63 = q_t . k_s; the K K^T half is unused)
+//   D_1 = S0 Q^T       (128 value rows i x 64 steps t)
+//   D_2 = Vt^T M'^T    (128 x 64), M'[t][s] = e^{Lambda_t - Lambda_s} (q_t . k_s) for s <= t, built from D_M
+//   o[t][i] = e^{Lambda_t} D_1[i][t] + D_2[i][t].
+// Operands are written by the threads as K-major 128-byte-swizzled tiles (16-byte chunk c of row r at
+// c ^ (r & 7)); one elected thread issues the MMAs; waits are bounded (2 s) and give up cleanly.
+namespace tc {
+constexpr int ATOM = 128 * 128;  // one 64-wide K atom of a 128-row bf16 tile, bytes
+constexpr int QK_OFF = 0, S_OFF = 2 * ATOM, VT_OFF = 4 * ATOM, MP_OFF = 5 * ATOM;
+constexpr int BYTES = MP_OFF + 64 * 128 + 1024 /*align*/ + 512 /*lam, barriers*/;
+
+RT_DEVICE void put_chunk(uint8_t* tile, int rows, int r, int k8, const float* v) {  // k8: 16-byte chunk index along K
+  const int atom = k8 >> 3, c = k8 & 7;
+  __nv_bfloat162 p0 = __floats2bfloat162_rn(v[0], v[1]), p1 = __floats2bfloat162_rn(v[2], v[3]);
+  __nv_bfloat162 p2 = __floats2bfloat162_rn(v[4], v[5]), p3 = __floats2bfloat162_rn(v[6], v[7]);
+  uint4 u;
+  u.x = *reinterpret_cast<uint32_t*>(&p0); u.y = *reinterpret_cast<uint32_t*>(&p1);
+  u.z = *reinterpret_cast<uint32_t*>(&p2); u.w = *reinterpret_cast<uint32_t*>(&p3);
+  *reinterpret_cast<uint4*>(tile + atom * rows * 128 + r * 128 + ((c ^ (r & 7)) << 4)) = u;
+}
+RT_DEVICE void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+}  // namespace tc
+
+__global__ void __launch_bounds__(128)
+gdn_out_tc_kernel(const float* __restrict__ qn, const float* __restrict__ kn, const float* __restrict__ U,
+                  const float* __restrict__ lam_in, const float* __restrict__ S0, bf16* __restrict__ out, int T,
+                  int Tp, int Hk, int Hv, int* __restrict__ status) {
+  constexpr int D = 128;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* QK = sm + tc::QK_OFF;   // 128 rows (q_0..63, k_0..63) x 128 keys
+  uint8_t* Sx = sm + tc::S_OFF;    // 128 value rows x 128 keys
+  uint8_t* VT = sm + tc::VT_OFF;   // 128 value rows x 64 steps
+  uint8_t* MP = sm + tc::MP_OFF;   // 64 steps t x 64 steps s
+  float* lam = reinterpret_cast<float*>(MP + 64 * 128);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(lam + LC);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 2);
+  const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z, kh = h / (Hv / Hk);
+  const int chunks = Tp / LC, t0 = c * LC, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const long rowbase = ((long)b * Hv + h) * Tp + t0;
+  if (tid == 0) {
+    sm100::mbar_init(&bars[0], 1);
+    sm100::mbar_init(&bars[1], 1);
+    sm100::fence_barrier_init();
+  }
+  if (warp == 0) {
+    sm100::tmem_alloc(tslot, 256);
+    sm100::tmem_relinquish();
+  }
+  // operands: q/k rows (fp32 -> bf16), S0 rows, Vt transposed, Lambda
+  for (int e = tid; e < 128 * 16; e += 128) {
+    const int r = e >> 4, k8 = e & 15, t = t0 + (r & 63);
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (t < T) {
+      const float* src = (r < 64 ? qn : kn) + (((long)b * T + t) * Hk + kh) * D + 8 * k8;
+      const float4 x = *reinterpret_cast<const float4*>(src), y = *reinterpret_cast<const float4*>(src + 4);
+      v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w; v[4] = y.x; v[5] = y.y; v[6] = y.z; v[7] = y.w;
+    }
+    tc::put_chunk(QK, 128, r, k8, v);
+    const float* srow = S0 + (((long)b * Hv + h) * chunks + c) * D * D + (long)r * D + 8 * k8;
+    const float4 x = *reinterpret_cast<const float4*>(srow), y = *reinterpret_cast<const float4*>(srow + 4);
+    const float w[8] = {x.x, x.y, x.z, x.w, y.x, y.y, y.z, y.w};
+    tc::put_chunk(Sx, 128, r, k8, w);
+  }
+  {  // Vt^T: thread = value row i, 64 steps
+    const int i = tid;
+    for (int k8 = 0; k8 < 8; ++k8) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = t0 + 8 * k8 + u < T ? U[(rowbase + 8 * k8 + u) * D + i] : 0.f;
+      tc::put_chunk(VT, 128, i, k8, v);
+    }
+  }
+  if (tid < LC) lam[tid] = lam_in[rowbase + tid];
+  tc::fence_proxy_async();
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem = *tslot;
+  const uint32_t idesc = sm100::idesc_bf16(128, 64, false, false);
+  bool ok = true;
+  if (warp == 0 && sm100::elect_one()) {
+    const uint32_t qk = sm100::smem_u32(QK), sx = sm100::smem_u32(Sx);
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks) {  // K = 128 keys: two atoms, four 16-wide steps each
+      const uint32_t off = (ks >> 2) * tc::ATOM + (ks & 3) * 32;
+      sm100::mma_bf16(tmem + 0, sm100::smem_desc(qk + off, 16, 1024), sm100::smem_desc(qk + off + 64 * 128, 16, 1024),
+                      idesc, ks > 0);
+      sm100::mma_bf16(tmem + 64, sm100::smem_desc(sx + off, 16, 1024), sm100::smem_desc(qk + off, 16, 1024), idesc,
+                      ks > 0);
+    }
+    sm100::mma_commit(&bars[0]);
+  }
+  if (!sm100::mbar_wait_bounded(&bars[0], 0)) ok = false;
+  sm100::tc_fence_after();
+  if (ok && warp < 2) {  // M' rows t = 32 warp + lane
+    const int t = 32 * warp + lane;
+    float m[64];
+    sm100::tmem_ld32(tmem + ((uint32_t)(32 * warp) << 16) + 0, *reinterpret_cast<float(*)[32]>(m));
+    sm100::tmem_ld32(tmem + ((uint32_t)(32 * warp) << 16) + 32, *reinterpret_cast<float(*)[32]>(m + 32));
+    sm100::tmem_wait_ld();
+    const float lt = lam[t];
+#pragma unroll
+    for (int s = 0; s < 64; ++s) m[s] = s <= t ? expf(lt - lam[s]) * m[s] : 0.f;
+#pragma unroll
+    for (int k8 = 0; k8 < 8; ++k8) tc::put_chunk(MP, 64, t, k8, m + 8 * k8);
+  }
+  tc::fence_proxy_async();
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  if (ok && warp == 0 && sm100::elect_one()) {
+    const uint32_t vt = sm100::smem_u32(VT), mp = sm100::smem_u32(MP);
+#pragma unroll
+    for (int ks = 0; ks < LC / 16; ++ks)
+      sm100::mma_bf16(tmem + 128, sm100::smem_desc(vt + ks * 32, 16, 1024), sm100::smem_desc(mp + ks * 32, 16, 1024),
+                      idesc, ks > 0);
+    sm100::mma_commit(&bars[1]);
+  }
+  if (ok && !sm100::mbar_wait_bounded(&bars[1], 0)) ok = false;
+  sm100::tc_fence_after();
+  if (ok) {  // rows i = 32 warp + lane; 64 steps
+    const int i = 32 * warp + lane;
+    const uint32_t row = tmem + ((uint32_t)(32 * warp) << 16);
+#pragma unroll 1
+    for (int half = 0; half < 2; ++half) {
+      float d1[32], d2[32];
+      sm100::tmem_ld32(row + 64 + 32 * half, d1);
+      sm100::tmem_ld32(row + 128 + 32 * half, d2);
+      sm100::tmem_wait_ld();
+#pragma unroll
+      for (int u = 0; u < 32; ++u) {
+        const int t = 32 * half + u, tg = t0 + t;
+        if (tg < T) out[(((long)b * T + tg) * Hv + h) * D + i] = __float2bfloat16_rn(expf(lam[t]) * d1[u] + d2[u]);
+      }
+    }
+  }
+  if (!ok && tid == 0 && status) atomicExch(status, 1);
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem, 256);
+  }
+}
+
 // q/k normalisation: qn = q / |q| * D^-1/2, kn = k / |k| (eps 1e-6), fp32 rows [B, T, Hk, D]. grid (T, B).
 template <int D>
 __global__ void __launch_bounds__(128) gdn_norm_kernel(const bf16* __restrict__ qkv, long row_stride, int T, int Hk,
@@ -531,8 +680,14 @@ cudaError_t launch(const void* qkv, long row_stride, const void* a, const void* 
   RT_CUDA_CHECK(cudaGetLastError());
   gdn_state_kernel<D><<<dim3(D / VB, Hv, B), NT, s2, stream>>>(kn, W, U, lam, state, S0, T, Tp, Hk, Hv);
   RT_CUDA_CHECK(cudaGetLastError());
-  gdn_out_kernel<D><<<dim3(chunks, Hv, B * (D / OB)), NT, s3, stream>>>(qn, kn, U, lam, S0, (bf16*)out, T, Tp, Hk,
-                                                                        Hv);
+  if constexpr (D == 128) {
+    RT_CUDA_CHECK(cudaFuncSetAttribute(gdn_out_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::BYTES));
+    gdn_out_tc_kernel<<<dim3(chunks, Hv, B), 128, tc::BYTES, stream>>>(qn, kn, U, lam, S0, (bf16*)out, T, Tp, Hk, Hv,
+                                                                       nullptr);
+  } else {
+    gdn_out_kernel<D><<<dim3(chunks, Hv, B * (D / OB)), NT, s3, stream>>>(qn, kn, U, lam, S0, (bf16*)out, T, Tp, Hk,
+                                                                          Hv);
+  }
   return cudaGetLastError();
 }
 
