@@ -398,6 +398,7 @@ def main():
             "clocks": clocks,
             "e2e": None if args.no_e2e else {
                 "value": e2e_total / (e2e_max / 1000), "unit": "tokens/s",
+                "ms_per_step": e2e_max / args.steps, "tokens_timed": e2e_total,  # the next K batches
                 "h2d_bytes_per_step": 8 * args.chunk * args.micro_batch,
                 "d2h_bytes_per_step": 4 * 5 * 16 if args.impl == "ours" else 4 * 3 * 16},
             "gpu_launches": ours_launches * args.steps,
