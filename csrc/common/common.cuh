@@ -21,6 +21,24 @@ template <> RT_DEVICE __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __fl
 RT_DEVICE float sigmoidf_(float x) { return 1.f / (1.f + expf(-x)); }
 RT_DEVICE float siluf_(float x) { return x / (1.f + expf(-x)); }
 
+// 8 bf16 values in one 16-byte word <-> 8 floats
+RT_DEVICE void unpack8(const uint4& u, float* f) {
+  const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 x = __bfloat1622float2(p[i]);
+    f[2 * i] = x.x;
+    f[2 * i + 1] = x.y;
+  }
+}
+RT_DEVICE uint4 pack8(const float* f) {
+  uint4 u;
+  __nv_bfloat162* p = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) p[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+  return u;
+}
+
 RT_DEVICE float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

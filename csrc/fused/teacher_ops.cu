@@ -9,6 +9,8 @@
 // Each kernel streams its operands once (vectorised 16-byte accesses where
 // the row length allows) and keeps intermediate values in registers or
 // shared memory.
+#include <type_traits>
+
 #include "../common/common.cuh"
 
 namespace {
@@ -36,6 +38,47 @@ __global__ void rmsnorm_kernel(const bf16* __restrict__ x, const bf16* __restric
   const float total = rt::block_sum(acc, scratch);
   const float inv = rsqrtf(total / C + eps);
   for (int c = threadIdx.x; c < C; c += blockDim.x) out[row * C + c] = __float2bfloat16_rn(srow[c] * inv * (1.f + w[c]));
+}
+
+// Register-resident variant: rows of C % 8 == 0 with 16-byte aligned operands; each of the 128
+// threads keeps V 8-value words of the row (C <= 8192), so x and h are read once and w once per word.
+template <bool ADD, int V>
+__global__ void __launch_bounds__(128) rmsnorm_vec_kernel(const uint4* __restrict__ x, const uint4* __restrict__ h,
+                                                          const float4* __restrict__ w, uint4* __restrict__ sum_out,
+                                                          uint4* __restrict__ out, int C8, float eps) {
+  __shared__ float scratch[32];
+  const long row = blockIdx.x;
+  float v[V][8];
+  float acc = 0.f;
+#pragma unroll
+  for (int j = 0; j < V; ++j) {
+    const int c = threadIdx.x + 128 * j;
+    if (c < C8) {
+      rt::unpack8(x[row * C8 + c], v[j]);
+      if (ADD) {
+        float a[8];
+        rt::unpack8(h[row * C8 + c], a);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[j][u] = __bfloat162float(__float2bfloat16_rn(v[j][u] + a[u]));
+        sum_out[row * C8 + c] = rt::pack8(v[j]);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) acc += v[j][u] * v[j][u];
+    }
+  }
+  const float inv = rsqrtf(rt::block_sum(acc, scratch) / (8 * C8) + eps);
+#pragma unroll
+  for (int j = 0; j < V; ++j) {
+    const int c = threadIdx.x + 128 * j;
+    if (c < C8) {
+      const float4 w0 = w[2 * c], w1 = w[2 * c + 1];
+      const float ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+      float o[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) o[u] = v[j][u] * inv * (1.f + ww[u]);
+      out[row * C8 + c] = rt::pack8(o);
+    }
+  }
 }
 
 // ---------------------------------------------------------------- conv1d + SiLU
@@ -72,6 +115,58 @@ __global__ void conv1d_silu_kernel(const bf16* __restrict__ x, const bf16* __res
       const float v = t >= 0 ? rt::to_f(x[((long)b * T + t) * C + c])
                              : rt::to_f(state[((long)b * (K - 1) + (t + K - 1)) * C + c]);
       new_state[((long)b * (K - 1) + j) * C + c] = __float2bfloat16_rn(v);
+    }
+  }
+}
+
+// Vectorised variant (C % 8 == 0, 16-byte aligned rows): a thread owns 8 channels and CSEG steps. All
+// K-1+CSEG input words of the segment are loaded up front (CSEG+K-1 16-byte loads in flight per
+// thread), then the taps run from registers; K is a template parameter so nothing spills.
+constexpr int CSEG = 16;
+template <int K>
+__global__ void __launch_bounds__(128) conv1d_silu_vec_kernel(const uint4* __restrict__ x, const uint4* __restrict__ state,
+                                                              const float* __restrict__ weight, uint4* __restrict__ y,
+                                                              uint4* __restrict__ new_state, int T, int C8) {
+  constexpr int H = K - 1;
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  const int t0 = blockIdx.y * CSEG, b = blockIdx.z;
+  if (c >= C8) return;
+  uint4 raw[H + CSEG];
+#pragma unroll
+  for (int j = 0; j < H + CSEG; ++j) {
+    const int t = t0 - H + j;
+    raw[j] = t < 0 ? state[((long)b * H + (t + H)) * C8 + c]
+                   : (t < T ? x[((long)b * T + t) * C8 + c] : make_uint4(0u, 0u, 0u, 0u));
+  }
+  float wt[K][8];
+#pragma unroll
+  for (int u = 0; u < 8; ++u)
+#pragma unroll
+    for (int j = 0; j < K; ++j) wt[j][u] = weight[(8 * c + u) * K + j];
+#pragma unroll
+  for (int i = 0; i < CSEG; ++i) {
+    if (t0 + i < T) {
+      float o[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) o[u] = 0.f;
+#pragma unroll
+      for (int j = 0; j < K; ++j) {
+        float v[8];
+        rt::unpack8(raw[i + j], v);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) o[u] += v[u] * wt[j][u];
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) o[u] = rt::siluf_(o[u]);
+      y[((long)b * T + t0 + i) * C8 + c] = rt::pack8(o);
+    }
+  }
+  if (t0 + CSEG >= T) {  // the segment holding step T-1 writes the carried window: inputs T-H .. T-1,
+                         // all inside this segment's loaded range t0-H .. t0+CSEG-1
+#pragma unroll
+    for (int k = 0; k < H + CSEG; ++k) {
+      const int t = t0 - H + k;
+      if (t >= T - H && t < T) new_state[((long)b * H + (t - (T - H))) * C8 + c] = raw[k];
     }
   }
 }
@@ -161,6 +256,23 @@ __global__ void copy_rows_kernel(const bf16* __restrict__ src, long src_stride, 
 
 extern "C" cudaError_t rt_rmsnorm_1p(const void* x, const void* h, const float* w, void* sum_out, void* out, long rows,
                                      int C, float eps, cudaStream_t stream) {
+  const bool vec = C % 8 == 0 && C <= 8192 && ((uintptr_t)x | (uintptr_t)h | (uintptr_t)w | (uintptr_t)sum_out |
+                                                (uintptr_t)out) % 16 == 0;
+  if (vec) {
+    const int C8 = C / 8, V = (C8 + 127) / 128;
+    auto go = [&](auto add, auto v) {
+      rmsnorm_vec_kernel<decltype(add)::value, decltype(v)::value><<<rows, 128, 0, stream>>>(
+          (const uint4*)x, (const uint4*)h, (const float4*)w, (uint4*)sum_out, (uint4*)out, C8, eps);
+    };
+#define RT_RMS_V(n)                                                                      \
+  case n:                                                                                \
+    h ? go(std::true_type{}, std::integral_constant<int, n>{})                           \
+      : go(std::false_type{}, std::integral_constant<int, n>{});                         \
+    break;
+    switch (V) { RT_RMS_V(1) RT_RMS_V(2) RT_RMS_V(3) RT_RMS_V(4) RT_RMS_V(5) RT_RMS_V(6) RT_RMS_V(7) RT_RMS_V(8) }
+#undef RT_RMS_V
+    return cudaGetLastError();
+  }
   const size_t smem = (size_t)C * sizeof(float);
   if (smem > 48 * 1024) {  // only rows wider than 12288 need the opt-in (set once per width class)
     RT_CUDA_CHECK(cudaFuncSetAttribute(rmsnorm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
@@ -177,6 +289,19 @@ extern "C" cudaError_t rt_rmsnorm_1p(const void* x, const void* h, const float* 
 extern "C" cudaError_t rt_conv1d_silu(const void* x, const void* state, const float* weight, void* y, void* new_state,
                                       int B, int T, int C, int K, cudaStream_t stream) {
   if (K < 1 || K > 8) return cudaErrorInvalidValue;
+  if (C % 8 == 0 && (K == 4 || K == 2 || K == 3) &&
+      ((uintptr_t)x | (uintptr_t)state | (uintptr_t)y | (uintptr_t)new_state) % 16 == 0) {
+    const int C8 = C / 8;
+    const dim3 g((C8 + 127) / 128, (T + CSEG - 1) / CSEG, B);
+    auto go = [&](auto k) {
+      conv1d_silu_vec_kernel<decltype(k)::value><<<g, 128, 0, stream>>>(
+          (const uint4*)x, (const uint4*)state, weight, (uint4*)y, (uint4*)new_state, T, C8);
+    };
+    if (K == 4) go(std::integral_constant<int, 4>{});
+    else if (K == 3) go(std::integral_constant<int, 3>{});
+    else go(std::integral_constant<int, 2>{});
+    return cudaGetLastError();
+  }
   dim3 grid((C + 127) / 128, (T + SEG - 1) / SEG, B);
   conv1d_silu_kernel<<<grid, 128, 0, stream>>>((const bf16*)x, (const bf16*)state, weight, (bf16*)y, (bf16*)new_state,
                                                T, C, K);

@@ -66,18 +66,22 @@ def test_gdn_kernel_matches_reference_recurrence(B, T, Hk, Hv, D):
 
 
 @cuda
-def test_norm_conv_ops():
+@pytest.mark.parametrize("T,C", [(17, 512),     # vectorised paths, one conv segment
+                                 (70, 5120),    # 27B width: 5 words per thread, three conv segments
+                                 (2, 512),      # fewer steps than the conv window (state carried through)
+                                 (9, 516)])     # width not a multiple of 8: scalar paths
+def test_norm_conv_ops(T, C):
     torch.manual_seed(2)
-    x = torch.randn(3, 17, 512, device="cuda").to(torch.bfloat16)
+    x = torch.randn(3, T, C, device="cuda").to(torch.bfloat16)
     h = torch.randn_like(x)
-    w = torch.randn(512, device="cuda") * 0.1
+    w = torch.randn(C, device="cuda") * 0.1
     torch.testing.assert_close(native().rmsnorm_1p(x, w, 1e-6).float(), R.rmsnorm_1p(x.float(), w, 1e-6),
                                atol=3e-2, rtol=2e-2)
     s, n = native().add_rmsnorm_1p(x, h, w, 1e-6)
     torch.testing.assert_close(s, x + h)
     torch.testing.assert_close(n.float(), R.rmsnorm_1p((x + h).float(), w, 1e-6), atol=3e-2, rtol=2e-2)
-    state = torch.randn(3, 3, 512, device="cuda").to(torch.bfloat16)
-    cw = torch.randn(512, 1, 4, device="cuda") * 0.3
+    state = torch.randn(3, 3, C, device="cuda").to(torch.bfloat16)
+    cw = torch.randn(C, 1, 4, device="cuda") * 0.3
     y, ns = native().conv1d_silu(x, state, cw)
     ry, rns = R.causal_conv1d_silu(x.float(), state.float(), cw[:, 0].float())
     torch.testing.assert_close(y.float(), ry, atol=2e-2, rtol=2e-2)
