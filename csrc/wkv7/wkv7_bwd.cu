@@ -308,12 +308,14 @@ struct GradSmem {
                                 + 2 * VR * SP            // S0, DS row slices
                                 + 3 * VROWS              // U (Z), DU, DZ
                                 + 9 * K::MAT             // M (4), W, dM (4)
-                                + 4 * KEYROWS + NP       // RD, AD, BH, KH accumulators + direct dD_L
-                                + 2 * KEYROWS;           // AT, DDL
+                                + 4 * KEYROWS + NP;      // RD, AD, BH, KH accumulators + direct dD_L
+  // AT and DDL reuse the value-row region (V ..), which is dead once the value-row passes end; the
+  // total stays under half an SM's shared memory so two CTAs (2 x 512 threads, <= 64 registers) fit.
+  static_assert(2 * VROWS + 2 * VR * SP + 3 * VROWS >= 2 * KEYROWS, "AT/DDL alias");
 };
 
 template <typename T, int NP>
-__global__ void __launch_bounds__(GT)
+__global__ void __launch_bounds__(GT, NP <= 64 ? 2 : 1)
 wkv7_bwd_grad_kernel(int T_, int H, int N, const T* __restrict__ pr, const T* __restrict__ pw,
                      const T* __restrict__ pk, const T* __restrict__ pv, const T* __restrict__ pa,
                      const T* __restrict__ pb, const T* __restrict__ pdy, const float* __restrict__ checkpoints,
@@ -342,8 +344,8 @@ wkv7_bwd_grad_kernel(int T_, int H, int N, const T* __restrict__ pr, const T* __
   float* BH = AD + G::KEYROWS;           // [L][SP] sum_i U[t][i] dS[i][j]
   float* KH = BH + G::KEYROWS;           // [L][SP] sum_i v[t][i] dS[i][j]
   float* dDLd = KH + G::KEYROWS;         // [NP] sum_i S0[i][j] dS[i][j]
-  float* AT = dDLd + NP;                 // [L][SP] a~-term of d Lambda (belongs to step t-1)
-  float* DDL = AT + G::KEYROWS;          // [L][SP] per-step b^/k^ part of dD_L
+  float* AT = V;                         // [L][SP] a~-term of d Lambda (belongs to step t-1); after the passes
+  float* DDL = V + G::KEYROWS;           // [L][SP] per-step b^/k^ part of dD_L; after the passes
   const int ch = blockIdx.x, bh = blockIdx.y, batch = bh / H, head = bh % H;
   const int chunks = gridDim.x;
   const int t0 = ch * L;
