@@ -26,6 +26,9 @@ cudaError_t rt_wkv7_backward(int dtype, int B, int T, int H, int N, const void* 
 // epi: 0 bf16 store, 1 fp32 store, 2 fp32 accumulate (C += alpha * A.B^T).
 cudaError_t rt_gemm_bf16(const void* A, long lda, int a_mn, const void* B, long ldb, int b_mn, void* C, long ldc,
                          int M, int N, int K, int epi, float alpha, int* status, cudaStream_t stream);
+int rt_gemm_fault();
+cudaError_t rt_gemm_bf16_tile(const void* A, long lda, int a_mn, const void* B, long ldb, int b_mn, void* C, long ldc,
+                              int M, int N, int K, int epi, float alpha, int choice, int* status, cudaStream_t stream);
 cudaError_t rt_gemm_skinny_bf16(const void* X, long ldx, const void* W, const void* Wu, long ldw, float* ws,
                                 void* out, long ldo, int M, int N, int K, int* status, cudaStream_t stream);
 cudaError_t rt_gemm_swiglu_bf16(const void* A, long lda, const void* Bg, const void* Bu, long ldb, void* C, long ldc,

@@ -107,14 +107,15 @@ at::Tensor status_tensor(const at::Tensor& like) {
 
 // out = a_op(A) . b_op(B)^T where a_op is identity ([M,K]) or transpose ([K,M] stored), same for B.
 // epi 0: returns new bf16 [M,N]; epi 1: new fp32; epi 2: accumulates alpha * result into `out` (fp32).
-at::Tensor gemm(at::Tensor A, bool a_t, at::Tensor B, bool b_t, int64_t epi, double alpha, c10::optional<at::Tensor> out) {
+at::Tensor gemm(at::Tensor A, bool a_t, at::Tensor B, bool b_t, int64_t epi, double alpha, c10::optional<at::Tensor> out,
+                int64_t tile) {
   c10::cuda::CUDAGuard guard(A.device());
   auto a = operand(A, "A");
   auto b = operand(B, "B");
   const long M = a_t ? A.size(1) : A.size(0), K = a_t ? A.size(0) : A.size(1);
   const long N = b_t ? B.size(1) : B.size(0), KB = b_t ? B.size(0) : B.size(1);
   TORCH_CHECK(K == KB, "GEMM inner dimensions differ: ", K, " vs ", KB);
-  if (epi == 0 && M <= 32 && !a_t && !b_t && !out.has_value()) {  // decode-sized: split-K weight streaming
+  if (epi == 0 && M <= 32 && !a_t && !b_t && !out.has_value() && tile == 0) {  // decode-sized: split-K weight streaming
     auto C = at::empty({M, N}, A.options().dtype(at::kBFloat16));
     auto ws = at::empty({M, N}, A.options().dtype(at::kFloat));
     check_cuda(rt_gemm_skinny_bf16(a.ptr, a.ld, b.ptr, nullptr, b.ld, ws.data_ptr<float>(), C.data_ptr(), N, M, N,
@@ -135,6 +136,12 @@ at::Tensor gemm(at::Tensor A, bool a_t, at::Tensor B, bool b_t, int64_t epi, dou
                 "invalid output tensor");
   } else {
     C = at::empty({M, N}, A.options().dtype(epi == 0 ? at::kBFloat16 : at::kFloat));
+  }
+  if (tile) {
+    check_cuda(rt_gemm_bf16_tile(a.ptr, a.ld, a_t, b.ptr, b.ld, b_t, C.data_ptr(), C.stride(0), M, N, K, (int)epi,
+                                 (float)alpha, (int)tile, nullptr, stream_of(A)),
+               "gemm (fixed tile)");
+    return C;
   }
   check_cuda(rt_gemm_bf16(a.ptr, a.ld, a_t, b.ptr, b.ld, b_t, C.data_ptr(), C.stride(0), M, N, K, (int)epi,
                           (float)alpha, nullptr, stream_of(A)),
@@ -443,7 +450,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("wkv7_backward", &wkv7_backward, "chunked WKV7 backward (dr, dw, dk, dv, da, db, ds0)");
   m.def("gemm", &gemm, "tcgen05 GEMM: a_op(A) . b_op(B)^T with bf16/fp32/accumulate epilogue",
         py::arg("A"), py::arg("a_t"), py::arg("B"), py::arg("b_t"), py::arg("epi") = 0, py::arg("alpha") = 1.0,
-        py::arg("out") = py::none());
+        py::arg("out") = py::none(), py::arg("tile") = 0);
+  m.def("gemm_fault", []() { return rt_gemm_fault(); },
+        "1 if a GEMM gave up a bounded wait since the last call (then cleared); synchronizes the device");
   m.def("gemm_swiglu", &gemm_swiglu, "silu(A . Bg^T) * (A . Bu^T) in one tcgen05 GEMM");
   m.def("rmsnorm_1p", &rmsnorm_1p);
   m.def("add_rmsnorm_1p", &add_rmsnorm_1p);

@@ -18,6 +18,18 @@
 // gradient accumulation into the flat fp32 buffers), and SwiGLU with two B
 // operands (out = silu(A·Bg^T) * (A·Bu^T), bf16).
 //
+// Stream-K mode (single-B epilogues): when the tile count leaves the last wave
+// of the persistent grid mostly idle (e.g. 160 tiles of a 1024 x 5120 output on
+// 148 SMs), the tiles x k-blocks iteration space is split evenly over the CTAs.
+// CTA c owns the contiguous iterations [start(c), start(c+1)) and walks them
+// from the END, so the piece it finishes first is the one that ends mid-tile:
+// that piece is stored as an fp32 partial in slot c of a workspace and
+// counted on the tile's flag. The piece holding a tile's last k-block is the
+// first piece of its owner's range, processed last; its epilogue waits (bounded)
+// for the lower-index CTAs that hold the tile's earlier k-blocks, adds their
+// partials from the workspace and stores the tile, then clears the flag. Waits
+// only ever point at lower-index CTAs, which finished those pieces first.
+//
 // All waits are bounded (sm100.cuh); on timeout the kernel records status 1
 // in *status and unwinds, freeing its TMEM.
 #include <cuda.h>
@@ -61,7 +73,65 @@ struct GemmArgs {
   int splits, kchunk;  // split-K: tile t covers k-blocks [ks * kchunk, (ks + 1) * kchunk), ks = t / (tiles_m * tiles_n)
   float alpha;
   int* status;
+  // stream-K (sk = 1): CTA c owns iterations [c q + min(c, rem), (c + 1) q + min(c + 1, rem)) of tiles x k-blocks
+  int sk, q, rem;
+  float* ws;   // fp32 partial tiles, one BM x BN slot per CTA
+  int* flags;  // per tile: partial warps published (4 per contributing CTA); reset by the tile's final CTA
 };
+
+// Work of one CTA: whole (or split-K) tiles strided over the grid, or its stream-K pieces, last first.
+struct WorkIter {
+  int next_tile, total, stride, per_split, kchunk, kblocks;
+  bool sk;
+  int lo, cur;  // stream-K range still to walk: [lo, cur)
+  __device__ WorkIter(const GemmArgs& a, int kblocks_) {
+    kblocks = kblocks_;
+    per_split = a.tiles_m * a.tiles_n;
+    total = per_split * a.splits;
+    next_tile = blockIdx.x;
+    stride = gridDim.x;
+    kchunk = a.kchunk;
+    sk = a.sk != 0;
+    const int c = blockIdx.x;
+    lo = c * a.q + min(c, a.rem);
+    cur = (c + 1) * a.q + min(c + 1, a.rem);
+  }
+  __device__ bool next(int& tile, int& k0, int& k1) {
+    if (sk) {
+      if (cur <= lo) return false;
+      tile = (cur - 1) / kblocks;
+      const int ts = tile * kblocks, p0 = max(lo, ts);
+      k0 = p0 - ts;
+      k1 = cur - ts;
+      cur = p0;
+      return true;
+    }
+    if (next_tile >= total) return false;
+    tile = next_tile;
+    next_tile += stride;
+    k0 = (tile / per_split) * kchunk;
+    k1 = min(kblocks, k0 + kchunk);
+    return true;
+  }
+};
+
+// Stream-K owner of iteration i (inverse of the range formula above).
+__device__ __forceinline__ int sk_owner(int i, int q, int rem) {
+  const int big = rem * (q + 1);
+  return i < big ? i / (q + 1) : rem + (i - big) / q;
+}
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Partial-tile slot layout: for 32-column chunk c and float4 q of a row, the 128 rows are contiguous, so a
+// warp's 32 rows move as one 512-byte run.
+__device__ __forceinline__ float4* sk_slot(float* ws, int slot, int bn, int c, int q, int row) {
+  return reinterpret_cast<float4*>(ws) + (long)slot * BM * (bn / 4) + ((long)(c * 8 + q) * BM + row);
+}
 
 __device__ __forceinline__ void store_row(float (&v)[32], int epi, void* C, long ldc, int row, int col, int N,
                                           float alpha) {
@@ -123,6 +193,9 @@ __device__ __forceinline__ void store_row(float (&v)[32], int epi, void* C, long
   }
 }
 
+// Set by a launch without a status word whose bounded wait gave up (read and cleared by rt_gemm_fault).
+__device__ int gemm_fault_word = 0;
+
 template <int BN, bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(THREADS, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb0,
@@ -142,14 +215,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int per_split = args.tiles_m * args.tiles_n;
-  const int total = per_split * args.splits;
   const int kblocks = (args.K + BK - 1) / BK;
-  // k-block range of a tile (all of K unless split-K)
-  auto krange = [&](int tile, int& k0, int& k1) {
-    const int ks = tile / per_split;
-    k0 = ks * args.kchunk;
-    k1 = min(kblocks, k0 + args.kchunk);
-  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < ST; ++s) {
@@ -184,10 +250,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
       int stage = 0;
       uint32_t phase = 0;
       int issued = 0;
-      for (int tile = blockIdx.x; tile < total && !*abort; tile += gridDim.x) {
+      WorkIter work(args, kblocks);
+      int tile, k0, k1;
+      while (!*abort && work.next(tile, k0, k1)) {
         const int tm = tile % args.tiles_m, tn = (tile % per_split) / args.tiles_m;
-        int k0, k1;
-        krange(tile, k0, k1);
         for (int kb = k0; kb < k1; ++kb) {
           if (!sm100::mbar_wait(&empty[stage], phase ^ 1, abort)) break;
           uint8_t* a_dst = smem + stage * C_::STAGE_BYTES;
@@ -226,13 +292,13 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
     if (sm100::elect_one()) {
       int stage = 0, acc = 0;
       uint32_t phase = 0, acc_phase = 0;
-      for (int tile = blockIdx.x; tile < total && !*abort; tile += gridDim.x) {
+      WorkIter work(args, kblocks);
+      int tile, k0, k1;
+      while (!*abort && work.next(tile, k0, k1)) {
         if (!sm100::mbar_wait(&tempty[acc], acc_phase ^ 1, abort)) break;
         sm100::tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * C_::ACC_COLS;
         bool ok = true;
-        int k0, k1;
-        krange(tile, k0, k1);
         for (int kb = k0; kb < k1; ++kb) {
           if (!sm100::mbar_wait(&full[stage], phase, abort)) { ok = false; break; }
           sm100::tc_fence_after();
@@ -265,12 +331,36 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
     const int row_in_tile = quarter * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < total && !*abort; tile += gridDim.x) {
+    WorkIter work(args, kblocks);
+    int tile, k0, k1;
+    while (!*abort && work.next(tile, k0, k1)) {
       const int tm = tile % args.tiles_m, tn = (tile % per_split) / args.tiles_m;
       if (!sm100::mbar_wait(&tfull[acc], acc_phase, abort)) break;
       sm100::tc_fence_after();
       const int row = tm * BM + row_in_tile;
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * C_::ACC_COLS;
+      // stream-K roles of this piece (uniform over the warp; each warp syncs on its own)
+      const bool partial = C_::NB == 1 && args.sk && k1 < kblocks;          // ends mid-tile: publish fp32 partial
+      const bool fixup = C_::NB == 1 && args.sk && k1 == kblocks && k0 > 0;  // final piece: add earlier partials
+      int first_slot = 0;
+      int* flag = args.flags + 4 * tile + quarter;  // one counter per row quarter: warps sync pairwise
+      if (fixup) {
+        first_slot = sk_owner(tile * kblocks, args.q, args.rem);
+        const int need = (int)blockIdx.x - first_slot;
+        bool ok = true;
+        if (lane == 0) {
+          const uint64_t t0 = sm100::globaltimer();
+          for (uint32_t spin = 0; ld_acquire_gpu(flag) < need; ++spin) {
+            if ((spin & 63u) == 63u && (sm100::globaltimer() - t0 > RT_WAIT_LIMIT_NS || *abort)) {
+              ok = false;
+              break;
+            }
+          }
+          if (!ok) *abort = 1;
+        }
+        __syncwarp();
+        if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
+      }
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         float v[32];
@@ -284,11 +374,34 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
         } else {
           sm100::tmem_wait_ld();
         }
+        if (partial) {
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            __stcg(sk_slot(args.ws, blockIdx.x, BN, c, q, row_in_tile),
+                   make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
+          continue;
+        }
+        if (fixup) {
+          for (int slot = first_slot; slot < (int)blockIdx.x; ++slot) {
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const float4 p = __ldcg(sk_slot(args.ws, slot, BN, c, q, row_in_tile));
+              v[4 * q] += p.x; v[4 * q + 1] += p.y; v[4 * q + 2] += p.z; v[4 * q + 3] += p.w;
+            }
+          }
+        }
         if (row < args.M) store_row(v, EPI, args.C, args.ldc, row, tn * BN + c * 32, args.N, args.alpha);
       }
       sm100::tc_fence_before();
       sm100::mbar_arrive(&tempty[acc]);
       if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      if (partial) {  // publish this warp's 32 rows
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) atomicAdd(flag, 1);
+      } else if (fixup && lane == 0) {
+        *flag = 0;  // all contributions to this quarter arrived and were read; the next launch is stream-ordered
+      }
     }
   }
   sm100::tc_fence_before();
@@ -297,7 +410,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
     sm100::tc_fence_after();
     sm100::tmem_dealloc(tmem_base, C_::TMEM_COLS);
   }
-  if (threadIdx.x == 0 && *abort && args.status) atomicExch(args.status, 1);
+  if (threadIdx.x == 0 && *abort) atomicExch(args.status ? args.status : &gemm_fault_word, 1);
 }
 
 // The driver's tensor-map encoder, resolved through the runtime so the extension does not link libcuda
@@ -342,9 +455,40 @@ int num_sms_cached() {
   return sms;
 }
 
+// Stream-K workspace of one (device, stream): a BM x 256 fp32 partial slot per SM and 4 counters per tile.
+// Allocated on the first stream-K launch outside stream capture and kept (graphs may hold its address); the
+// counters are zeroed once and every launch leaves them zero again.
+constexpr int SK_MAX_FLAGS = 4 * 32768;
+struct SkWorkspace {
+  float* ws = nullptr;
+  int* flags = nullptr;
+};
+SkWorkspace* sk_workspace(cudaStream_t stream) {
+  static std::map<std::pair<int, cudaStream_t>, SkWorkspace> spaces;
+  static std::mutex m;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(m);
+  SkWorkspace& w = spaces[{dev, stream}];
+  if (w.ws) return &w;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) return nullptr;
+  float* ws = nullptr;
+  int* flags = nullptr;
+  if (cudaMalloc(&ws, (size_t)num_sms_cached() * BM * 256 * sizeof(float)) != cudaSuccess) return nullptr;
+  if (cudaMalloc(&flags, SK_MAX_FLAGS * sizeof(int)) != cudaSuccess ||
+      cudaMemsetAsync(flags, 0, SK_MAX_FLAGS * sizeof(int), stream) != cudaSuccess) {
+    cudaFree(ws);
+    return nullptr;
+  }
+  w.ws = ws;
+  w.flags = flags;
+  return &w;
+}
+
 template <int BN, bool A_MN, bool B_MN, int EPI>
 cudaError_t launch(const void* A, long lda, const void* B0, const void* B1, long ldb, void* C, long ldc, int M,
-                   int N, int K, float alpha, int* status, cudaStream_t stream, int splits = 1) {
+                   int N, int K, float alpha, int* status, cudaStream_t stream, int splits = 1, bool sk = false) {
   using C_ = Cfg<BN, A_MN, B_MN, EPI>;
   CUtensorMap ta, tb0, tb1;
   bool ok = A_MN ? make_tmap(&ta, A, M, K, lda * 2, 64, BK) : make_tmap(&ta, A, K, M, lda * 2, BK, BM);
@@ -361,9 +505,23 @@ cudaError_t launch(const void* A, long lda, const void* B0, const void* B1, long
   args.splits = splits;
   args.kchunk = ((K + BK - 1) / BK + splits - 1) / splits;
   const int total = args.tiles_m * args.tiles_n * splits;
+  args.sk = 0; args.q = 0; args.rem = 0; args.ws = nullptr; args.flags = nullptr;
+  int grid = total < num_sms_cached() ? total : num_sms_cached();
+  if (sk && C_::NB == 1 && splits == 1 && EPI != EPI_ATOMIC_T) {
+    const long iters = (long)args.tiles_m * args.tiles_n * ((K + BK - 1) / BK);
+    SkWorkspace* w = 4L * args.tiles_m * args.tiles_n <= SK_MAX_FLAGS && iters >= num_sms_cached() && iters < (1L << 30)
+                         ? sk_workspace(stream) : nullptr;
+    if (w) {
+      grid = num_sms_cached();
+      args.sk = 1;
+      args.q = (int)(iters / grid);
+      args.rem = (int)(iters % grid);
+      args.ws = w->ws;
+      args.flags = w->flags;
+    }
+  }
   auto kern = gemm_kernel<BN, A_MN, B_MN, EPI>;
   RT_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C_::SMEM_BYTES));
-  const int grid = total < num_sms_cached() ? total : num_sms_cached();
   kern<<<grid, THREADS, C_::SMEM_BYTES, stream>>>(ta, tb0, tb1, args);
   return cudaGetLastError();
 }
@@ -394,20 +552,27 @@ int pick_bn(int M, int N, bool swiglu, bool b_mn) {
   return best;
 }
 
+// Tile choice: width bn, plus SK_FLAG for the stream-K schedule.
+constexpr int SK_FLAG = 1 << 16;
+
 template <bool A_MN, bool B_MN, int EPI>
-cudaError_t dispatch_bn(int bn, const void* A, long lda, const void* B0, const void* B1, long ldb, void* C, long ldc,
-                        int M, int N, int K, float alpha, int* status, cudaStream_t s) {
-  if (bn == 256) return launch<256, A_MN, B_MN, EPI>(A, lda, B0, B1, ldb, C, ldc, M, N, K, alpha, status, s);
-  if (bn == 192) return launch<192, A_MN, B_MN, EPI>(A, lda, B0, B1, ldb, C, ldc, M, N, K, alpha, status, s);
-  if (bn == 128) return launch<128, A_MN, B_MN, EPI>(A, lda, B0, B1, ldb, C, ldc, M, N, K, alpha, status, s);
+cudaError_t dispatch_bn(int choice, const void* A, long lda, const void* B0, const void* B1, long ldb, void* C,
+                        long ldc, int M, int N, int K, float alpha, int* status, cudaStream_t s) {
+  const int bn = choice & (SK_FLAG - 1);
+  const bool sk = (choice & SK_FLAG) != 0;
+#define RT_L(W) return launch<W, A_MN, B_MN, EPI>(A, lda, B0, B1, ldb, C, ldc, M, N, K, alpha, status, s, 1, sk)
+  if (bn == 256) RT_L(256);
+  if (bn == 192) RT_L(192);
+  if (bn == 128) RT_L(128);
   if constexpr (!B_MN) {
-    if (bn == 224) return launch<224, A_MN, B_MN, EPI>(A, lda, B0, B1, ldb, C, ldc, M, N, K, alpha, status, s);
-    if (bn == 160) return launch<160, A_MN, B_MN, EPI>(A, lda, B0, B1, ldb, C, ldc, M, N, K, alpha, status, s);
+    if (bn == 224) RT_L(224);
+    if (bn == 160) RT_L(160);
   }
-  return launch<64, A_MN, B_MN, EPI>(A, lda, B0, B1, ldb, C, ldc, M, N, K, alpha, status, s);
+  RT_L(64);
+#undef RT_L
 }
 
-cudaError_t gemm_with_bn(int bn, const void* A, long lda, int a_mn, const void* B, long ldb, int b_mn, void* C,
+cudaError_t gemm_with_bn(int choice, const void* A, long lda, int a_mn, const void* B, long ldb, int b_mn, void* C,
                          long ldc, int M, int N, int K, int epi, float alpha, int* status, cudaStream_t stream);
 
 // Tile width per problem shape, measured once: the first call of a shape with a store epilogue (outside stream
@@ -449,13 +614,20 @@ int measured_bn(const TileKey& key, const void* A, long lda, const void* B, long
   }
   int best = guess;
   float best_ms = 1e30f;
-  for (int bn : {256, 224, 192, 160, 128}) {
+  const long kblocks = (key.K + BK - 1) / BK;
+  for (int choice : {256, 224, 192, 160, 128, 256 | SK_FLAG, 224 | SK_FLAG, 192 | SK_FLAG, 128 | SK_FLAG}) {
+    const int bn = choice & (SK_FLAG - 1);
     if (key.b_mn && bn % 64) continue;
     if (key.N < bn / 2) continue;
+    if (choice & SK_FLAG) {  // stream-K only where the whole-tile schedule leaves a wave partly idle
+      const long tiles = (long)((key.M + BM - 1) / BM) * ((key.N + bn - 1) / bn);
+      const int sms = num_sms_cached();
+      if (tiles % sms == 0 || tiles * kblocks < 2L * sms || kblocks < 8) continue;
+    }
     float ms = 1e30f;
     for (int rep = 0; rep < 4; ++rep) {
       cudaEventRecord(e0, stream);
-      if (gemm_with_bn(bn, A, lda, key.a_mn, B, ldb, key.b_mn, C, ldc, key.M, key.N, key.K, epi, alpha, status,
+      if (gemm_with_bn(choice, A, lda, key.a_mn, B, ldb, key.b_mn, C, ldc, key.M, key.N, key.K, epi, alpha, status,
                        stream) != cudaSuccess)
         break;
       cudaEventRecord(e1, stream);
@@ -465,10 +637,10 @@ int measured_bn(const TileKey& key, const void* A, long lda, const void* B, long
       ms = rep ? (t < ms ? t : ms) : 1e30f;  // first run warms up
     }
     // the estimate wins unless a candidate is more than 3% faster (single-launch timings are noisy)
-    const float score = bn == guess ? 0.97f * ms : ms;
+    const float score = choice == guess ? 0.97f * ms : ms;
     if (score < best_ms) {
       best_ms = score;
-      best = bn;
+      best = choice;
     }
   }
   cudaEventDestroy(e0);
@@ -493,15 +665,39 @@ extern "C" cudaError_t rt_gemm_bf16(const void* A, long lda, int a_mn, const voi
   return gemm_with_bn(bn, A, lda, a_mn, B, ldb, b_mn, C, ldc, M, N, K, epi, alpha, status, stream);
 }
 
+// 1 if a GEMM launched without a status word gave up a wait since the last call (synchronizes the device).
+extern "C" int rt_gemm_fault() {
+  int v = 0, zero = 0;
+  if (cudaMemcpyFromSymbol(&v, gemm_fault_word, sizeof(int)) != cudaSuccess) return -1;
+  if (v) cudaMemcpyToSymbol(gemm_fault_word, &zero, sizeof(int));
+  return v;
+}
+
+// Same with a fixed tile choice (width | 1 << 16 for stream-K); for tests and benchmarks of one schedule.
+extern "C" cudaError_t rt_gemm_bf16_tile(const void* A, long lda, int a_mn, const void* B, long ldb, int b_mn,
+                                         void* C, long ldc, int M, int N, int K, int epi, float alpha, int choice,
+                                         int* status, cudaStream_t stream) {
+  if (M <= 0 || N <= 0 || K <= 0) return cudaSuccess;
+  if ((lda & 7) || (ldb & 7) || (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15))
+    return cudaErrorInvalidValue;
+  const int bn = choice & (SK_FLAG - 1);
+  if (bn != 64 && bn != 128 && bn != 160 && bn != 192 && bn != 224 && bn != 256) return cudaErrorInvalidValue;
+  if (b_mn && bn % 64) return cudaErrorInvalidValue;
+  return gemm_with_bn(choice, A, lda, a_mn, B, ldb, b_mn, C, ldc, M, N, K, epi, alpha, status, stream);
+}
+
 namespace {
 
-cudaError_t gemm_with_bn(int bn, const void* A, long lda, int a_mn, const void* B, long ldb, int b_mn, void* C,
+cudaError_t gemm_with_bn(int choice, const void* A, long lda, int a_mn, const void* B, long ldb, int b_mn, void* C,
                          long ldc, int M, int N, int K, int epi, float alpha, int* status, cudaStream_t stream) {
-#define RT_G(AM, BMN)                                                                                         \
-  switch (epi) {                                                                                              \
-    case EPI_BF16: return dispatch_bn<AM, BMN, EPI_BF16>(bn, A, lda, B, B, ldb, C, ldc, M, N, K, alpha, status, stream); \
-    case EPI_F32: return dispatch_bn<AM, BMN, EPI_F32>(bn, A, lda, B, B, ldb, C, ldc, M, N, K, alpha, status, stream);   \
-    default: return dispatch_bn<AM, BMN, EPI_F32_ACCUM>(bn, A, lda, B, B, ldb, C, ldc, M, N, K, alpha, status, stream);  \
+#define RT_G(AM, BMN)                                                                                                 \
+  switch (epi) {                                                                                                      \
+    case EPI_BF16:                                                                                                    \
+      return dispatch_bn<AM, BMN, EPI_BF16>(choice, A, lda, B, B, ldb, C, ldc, M, N, K, alpha, status, stream);       \
+    case EPI_F32:                                                                                                     \
+      return dispatch_bn<AM, BMN, EPI_F32>(choice, A, lda, B, B, ldb, C, ldc, M, N, K, alpha, status, stream);        \
+    default:                                                                                                          \
+      return dispatch_bn<AM, BMN, EPI_F32_ACCUM>(choice, A, lda, B, B, ldb, C, ldc, M, N, K, alpha, status, stream);  \
   }
   if (!a_mn && !b_mn) { RT_G(false, false) }
   if (!a_mn && b_mn) { RT_G(false, true) }

@@ -31,6 +31,7 @@ from .data import digest_file, reader_for
 from .losses import metrics
 from .models.hf_io import load_model
 from .models.runner import Capture, Runner, install, migration_order, state_to_device
+from .ops import native
 from .parallel.topology import Topology
 from .profiling import StepProfiler
 from .schedule import lr_factor
@@ -125,6 +126,8 @@ class StepEngine:
         """One device-to-host copy of all layer reports; raises on update errors."""
         rows = torch.stack([reports[layer] for layer in self.order]).double().cpu().tolist()
         self.topo.check_grad_sync()
+        if self.topo.device.type == "cuda" and native().gemm_fault():
+            raise RuntimeError("a tcgen05 GEMM gave up a bounded wait (results of this step are invalid)")
         layer_metrics = {}
         for layer, (nmse, cos, count, norm, bad) in zip(self.order, rows):
             if count <= 0:

@@ -82,3 +82,32 @@ def test_skinny_decode_gemm_matches_fp32(M, N, K):
     sw = native().gemm_swiglu(x, w, u)
     ref_sw = torch.nn.functional.silu(ref) * (x.float() @ u.float().t())
     torch.testing.assert_close(sw.float(), ref_sw, atol=2e-2, rtol=2e-2)
+
+
+SK = 1 << 16
+
+
+@cuda
+@pytest.mark.parametrize("M,N,K,bn", [(1024, 5120, 5120, 256),   # 160 tiles on 148 SMs: tiles split over 2 CTAs
+                                      (256, 512, 5120, 256),     # 4 tiles of 80 k-blocks: ~37 CTAs per tile
+                                      (300, 1000, 1000, 192),    # ragged M, N and K tails
+                                      (1024, 5120, 17408, 224)])
+def test_stream_k_matches_fp32(M, N, K, bn):
+    A, B = _bf(M, K, seed=5), _bf(N, K, seed=6)
+    ref = A.float() @ B.float().t()
+    for rep in range(2):  # the second launch checks that the tile counters were left at zero
+        out = native().gemm(A, False, B, False, 0, 1.0, None, bn | SK)
+        _check(out, ref)
+    out32 = native().gemm(A, False, B, False, 1, 1.0, None, bn | SK)
+    _check(out32, ref, 1e-3)
+    whole = native().gemm(A, False, B, False, 1, 1.0, None, bn)
+    assert (out32 - whole).abs().max().item() <= 1e-4 * ref.abs().max().item()
+
+
+@cuda
+def test_stream_k_accumulate_mn_major():
+    dy, x = _bf(1024, 640, seed=7), _bf(1024, 5120, seed=8)  # dW = dy^T x: 5 x 20 tiles, 16 k-blocks
+    acc = torch.randn(640, 5120, device="cuda")
+    ref = acc + 0.5 * (dy.float().t() @ x.float())
+    native().gemm(dy, True, x, True, 2, 0.5, acc, 256 | SK)
+    _check(acc, ref, 1e-3)
