@@ -455,21 +455,22 @@ int num_sms_cached() {
   return sms;
 }
 
-// Stream-K workspace of one (device, stream): a BM x 256 fp32 partial slot per SM and 4 counters per tile.
-// Allocated on the first stream-K launch outside stream capture and kept (graphs may hold its address); the
-// counters are zeroed once and every launch leaves them zero again.
+// Stream-K workspace of one device: a BM x 256 fp32 partial slot per SM and 4 counters per tile. Allocated on
+// the first stream-K launch outside stream capture and kept (graphs hold its address); the counters are zeroed
+// once and every launch leaves them zero again. Stream-K launches of one device therefore must not run
+// concurrently on two streams; the framework issues all GEMMs of a device on one stream at a time.
 constexpr int SK_MAX_FLAGS = 4 * 32768;
 struct SkWorkspace {
   float* ws = nullptr;
   int* flags = nullptr;
 };
 SkWorkspace* sk_workspace(cudaStream_t stream) {
-  static std::map<std::pair<int, cudaStream_t>, SkWorkspace> spaces;
+  static std::map<int, SkWorkspace> spaces;
   static std::mutex m;
   int dev = 0;
   cudaGetDevice(&dev);
   std::lock_guard<std::mutex> lock(m);
-  SkWorkspace& w = spaces[{dev, stream}];
+  SkWorkspace& w = spaces[dev];
   if (w.ws) return &w;
   cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
   if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) return nullptr;
@@ -594,8 +595,8 @@ std::mutex& tile_mutex() {
   return m;
 }
 
-int measured_bn(const TileKey& key, const void* A, long lda, const void* B, long ldb, void* C, long ldc, int epi,
-                float alpha, int* status, cudaStream_t stream) {
+int measured_bn(const TileKey& key, int M, int K, const void* A, long lda, const void* B, long ldb, void* C, long ldc,
+                int epi, float alpha, int* status, cudaStream_t stream) {
   {
     std::lock_guard<std::mutex> lock(tile_mutex());
     auto it = tile_cache().find(key);
@@ -627,7 +628,7 @@ int measured_bn(const TileKey& key, const void* A, long lda, const void* B, long
     float ms = 1e30f;
     for (int rep = 0; rep < 4; ++rep) {
       cudaEventRecord(e0, stream);
-      if (gemm_with_bn(choice, A, lda, key.a_mn, B, ldb, key.b_mn, C, ldc, key.M, key.N, key.K, epi, alpha, status,
+      if (gemm_with_bn(choice, A, lda, key.a_mn, B, ldb, key.b_mn, C, ldc, M, key.N, K, epi, alpha, status,
                        stream) != cudaSuccess)
         break;
       cudaEventRecord(e1, stream);
@@ -660,8 +661,10 @@ extern "C" cudaError_t rt_gemm_bf16(const void* A, long lda, int a_mn, const voi
   if (M <= 0 || N <= 0 || K <= 0) return cudaSuccess;
   if ((lda & 7) || (ldb & 7) || (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15))
     return cudaErrorInvalidValue;
-  const TileKey key{M, N, K, a_mn != 0, b_mn != 0};
-  const int bn = measured_bn(key, A, lda, B, ldb, C, ldc, epi, alpha, status, stream);
+  // Shapes share a measured tile choice per bucket: M by 128-row tiles and K by 512 (the token count of a
+  // partial chunk varies from call to call; the choice affects speed only, never the result).
+  const TileKey key{(M + BM - 1) / BM * BM, N, (K + 511) / 512 * 512, a_mn != 0, b_mn != 0};
+  const int bn = measured_bn(key, M, K, A, lda, B, ldb, C, ldc, epi, alpha, status, stream);
   return gemm_with_bn(bn, A, lda, a_mn, B, ldb, b_mn, C, ldc, M, N, K, epi, alpha, status, stream);
 }
 

@@ -30,7 +30,7 @@ from safetensors.torch import load_file, save_file
 from .data import digest_file
 
 MUTABLE_KEYS = {"output", "log_interval", "checkpoint_interval", "validation_interval", "timeout_minutes",
-                "lr", "warmup_steps", "constant_steps", "min_lr", "fused_optimizer", "grad_sync"}
+                "lr", "warmup_steps", "constant_steps", "min_lr", "fused_optimizer", "grad_sync", "student_graphs"}
 
 
 def cpu_tree(obj):

@@ -16,6 +16,8 @@ Two optional keys are added on top of the reference schema (both default to
   ``"peer"`` (default; one-node NVLink peer-memory exchange with sharded
   AdamW, ``parallel/grad_sync.py``) or ``"nccl"`` (all-reduce, then the
   full update on every rank, as the reference does).
+* ``student_graphs`` replays each fused student micro-step as a CUDA graph
+  after its first eager run (default ``True``).
 """
 import json
 from pathlib import Path
@@ -36,7 +38,7 @@ DEFAULTS = {
     "distributed_backend": "nccl", "timeout_minutes": 60,
     # Extensions (not in the reference schema; defaults keep reference behaviour).
     "lora_rank": None, "gate_lora_rank": None, "fused_optimizer": True,
-    "grad_sync": "peer",
+    "grad_sync": "peer", "student_graphs": True,
 }
 
 _POSITIVE_INTS = ("chunk_tokens", "context_tokens", "grad_accum_steps", "micro_batch_size",
@@ -92,6 +94,8 @@ def _check(cfg):
         raise ValueError("fused_optimizer must be a boolean")
     if cfg["grad_sync"] not in ("peer", "nccl"):
         raise ValueError("grad_sync must be peer or nccl")
+    if not isinstance(cfg["student_graphs"], bool):
+        raise ValueError("student_graphs must be a boolean")
 
 
 def load_config(path):

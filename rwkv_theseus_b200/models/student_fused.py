@@ -22,12 +22,58 @@ backward
 Weight operands come from a bf16 copy of the flat fp32 parameters that the
 optimizer kernel refreshes after every update (the value autocast would use);
 transposed operands are read MN-major by the GEMM, never materialised.
+
+CUDA graphs: a micro-step is ~100 launches whose host-side issue costs more than
+their device time, so (config ``student_graphs``, default on) the second
+micro-step of a given shape is captured once as a CUDA graph and every later one
+is a replay (full ``chunk_tokens`` chunks only; the shorter last chunk of a
+document runs eagerly): the chunk's input and target are copied into static buffers, the
+carried state lives in static buffers (zeroed at a document boundary), and the
+statistics come back through a static buffer. The first micro-step of a shape runs
+eagerly, so the GEMM tile choices are measured before any capture. All students'
+graphs share one memory pool: their intermediates die inside the replay, and
+replays are serialised on the training stream.
 """
 import torch
 
 from ..ops import native
 
 _MIX = ("x_r", "x_w", "x_k", "x_v", "x_a", "x_g")
+_POOLS = {}  # device index -> memory pool shared by the micro-step graphs
+
+
+class _StepGraph:
+    """One captured micro-step of fixed input shape and ``first`` flag."""
+
+    def __init__(self, fused, shape, target_dtype, first, eps):
+        B, T, C = shape
+        dev = fused.device
+        self.x = torch.zeros(B, T, C, device=dev, dtype=torch.bfloat16)
+        self.y = torch.zeros(B, T, C, device=dev, dtype=target_dtype)
+        self.shift = torch.zeros(B, C, device=dev, dtype=torch.bfloat16)
+        self.wkv = torch.zeros(B, fused.H, fused.N, fused.N, device=dev, dtype=torch.float32)
+        self.stats = torch.zeros(3, device=dev)
+        self.state = {"shift": self.shift, "wkv": self.wkv}
+        pool = _POOLS.setdefault(dev.index, torch.cuda.graph_pool_handle())
+        self.graph = torch.cuda.CUDAGraph()
+        torch.cuda.synchronize(dev)
+        with torch.cuda.graph(self.graph, pool=pool, capture_error_mode="thread_local"):
+            stats, new_state = fused._forward_backward(self.x, self.y, self.state, eps, first)
+            self.stats.copy_(stats)
+            self.shift.copy_(new_state["shift"])
+            self.wkv.copy_(new_state["wkv"])
+
+    def run(self, x, target, state):
+        self.x.copy_(x)
+        self.y.copy_(target)
+        if state is None:
+            self.shift.zero_()
+            self.wkv.zero_()
+        elif state is not self.state:
+            self.shift.copy_(state["shift"])
+            self.wkv.copy_(state["wkv"])
+        self.graph.replay()
+        return self.stats, self.state
 
 
 class FusedStudent:
@@ -43,6 +89,8 @@ class FusedStudent:
             raise RuntimeError("unexpected flat parameter order")
         self.coef = flat.param[start:start + 6 * self.C]
         self.dcoef = flat.grad[start:start + 6 * self.C]
+        self.use_graphs = bool(student.cfg.get("student_graphs", True))
+        self.graphs = {}  # (shape, target dtype, first, eps) -> _StepGraph, or None after one eager run
         self.refresh_weights()
 
     # ------------------------------------------------------------------ helpers
@@ -125,7 +173,22 @@ class FusedStudent:
     @torch.no_grad()
     def forward_backward(self, x, target, state, eps, first=False):
         """One micro-step. ``first``: the gradient buffer holds a finished update's values; the four big
-        matrices' gradients are then stored (not accumulated) and the rest of the buffer is cleared."""
+        matrices' gradients are then stored (not accumulated) and the rest of the buffer is cleared.
+        Returns (statistics [3], new state); with graphs, both are static buffers of the step's graph that
+        the next replay of the same shape overwrites."""
+        if not self.use_graphs or x.shape[1] != self.student.cfg["chunk_tokens"]:
+            # graphs only for full chunks: the shorter last chunk of a document varies in length
+            return self._forward_backward(x, target, state, eps, first)
+        key = (tuple(x.shape), target.dtype, bool(first), float(eps))
+        step = self.graphs.get(key)
+        if step is None:
+            if key not in self.graphs:  # first use of this shape: eager (measures GEMM tiles), capture next time
+                self.graphs[key] = None
+                return self._forward_backward(x, target, state, eps, first)
+            step = self.graphs[key] = _StepGraph(self, tuple(x.shape), target.dtype, bool(first), float(eps))
+        return step.run(x, target, state)
+
+    def _forward_backward(self, x, target, state, eps, first):
         B, T, C = x.shape
         M, H, N = B * T, self.H, self.N
         ext = native()
