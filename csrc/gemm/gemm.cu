@@ -601,6 +601,23 @@ int measured_bn(const TileKey& key, int M, int K, const void* A, long lda, const
     std::lock_guard<std::mutex> lock(tile_mutex());
     auto it = tile_cache().find(key);
     if (it != tile_cache().end()) return it->second;
+    // A shorter chunk of a measured GEMM (same N and layouts, fewer rows or a shallower K): reuse the choice of
+    // the nearest larger measured bucket instead of timing again in the middle of training.
+    int best = -1;
+    long best_size = 0;
+    for (const auto& [k, choice] : tile_cache()) {
+      if (k.N != key.N || k.a_mn != key.a_mn || k.b_mn != key.b_mn) continue;
+      const bool rows = k.K == key.K && k.M > key.M, depth = k.M == key.M && k.K > key.K;
+      const long size = (long)k.M * k.K;
+      if ((rows || depth) && (best < 0 || size < best_size)) {
+        best = choice;
+        best_size = size;
+      }
+    }
+    if (best >= 0) {
+      tile_cache()[key] = best;
+      return best;
+    }
   }
   const int guess = pick_bn(key.M, key.N, false, key.b_mn != 0);
   cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;

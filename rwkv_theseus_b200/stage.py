@@ -60,6 +60,16 @@ class FlatBuffers:
         return buffer[self.offsets[i]:self.offsets[i + 1]].view(self.shapes[i])
 
 
+_UPDATE_STREAMS = {}
+
+
+def _update_stream(device):
+    """Side stream of a device for the local fused optimizer updates."""
+    if device.index not in _UPDATE_STREAMS:
+        _UPDATE_STREAMS[device.index] = torch.cuda.Stream(device)
+    return _UPDATE_STREAMS[device.index]
+
+
 class Student:
     def __init__(self, model_cfg, layer, cfg, topo, weights=None, total_steps=1):
         self.layer, self.cfg, self.topo = layer, cfg, topo
@@ -84,6 +94,8 @@ class Student:
         self.fused = None
         self.sharded = False           # fp32 masters / moments hold only this rank's shard (peer exchange)
         self.grads_live = False        # the flat gradient holds this update's micro-steps (fused path)
+        self._update_done = None       # event of a local fused update still running on the update stream
+        self.overlap_update = False    # run local fused updates on the side stream (set by the step engine)
         if device.type == "cuda" and cfg.get("fused_optimizer", True):
             from .models.student_fused import FusedStudent
             self.fused = FusedStudent(self)
@@ -92,8 +104,15 @@ class Student:
             exchange.register(self)
 
     # ---------------------------------------------------------------- forward/backward
+    def join_update(self):
+        """Make the current stream wait for this student's last local update (parameters, moments, report)."""
+        if self._update_done is not None:
+            torch.cuda.current_stream(self.topo.device).wait_event(self._update_done)
+            self._update_done = None
+
     def micro_step(self, x, target):
         """Forward + backward on one chunk; gradients accumulate into the flat buffer."""
+        self.join_update()
         eps = self.cfg["loss_epsilon"]
         if self.fused is not None:
             stats, self.state = self.fused.forward_backward(x, target, self.state, eps, first=not self.grads_live)
@@ -111,6 +130,7 @@ class Student:
     @torch.no_grad()
     def predict(self, x, state):
         """Inference forward (validation); returns (prediction, new state)."""
+        self.join_update()
         if self.fused is not None:
             return self.fused.forward(x, state)
         with torch.autocast(x.device.type, dtype=torch.bfloat16):
@@ -130,6 +150,7 @@ class Student:
         """Sum gradients and loss statistics over ranks (one bucket per layer).
 
         With the peer-memory exchange the reduction is part of ``update``."""
+        self.join_update()
         if self.fused is not None and not self.grads_live:
             self.flat.grad.zero_()  # no micro-step this update (exhausted rank): contribute zeros
             self.grads_live = True
@@ -153,12 +174,27 @@ class Student:
             self.grads_live = False
             return lr
         if self.fused is not None:
+            # Memory-bound; it runs on a side stream under the next layer's compute-bound micro-step and is
+            # joined where its results are next read (join_update).
+            self.join_update()
             if not self.grads_live:
                 self.flat.grad.zero_()
-            self.fused.update(lr, self.steps_done)
+            if not self.overlap_update:
+                self.fused.update(lr, self.steps_done)
+                self.stats.zero_()
+                self.grads_live = False
+                return lr
+            main = torch.cuda.current_stream(self.topo.device)
+            side = _update_stream(self.topo.device)
+            side.wait_stream(main)
+            with torch.cuda.stream(side):
+                self.fused.update(lr, self.steps_done)
+                self.stats.zero_()
+            self._update_done = torch.cuda.Event()
+            self._update_done.record(side)
             self.grads_live = False
-        else:
-            self._update_reference(lr, self.steps_done)
+            return lr
+        self._update_reference(lr, self.steps_done)
         self.stats.zero_()
         return lr
 
@@ -167,6 +203,7 @@ class Student:
 
         With the peer exchange each rank updates only its shard of the fp32 masters of the decay matrices and
         of the moments (compute reads the all-gathered bf16 copy)."""
+        self.join_update()
         exchange = self._exchange()
         if exchange is not None and self.sharded:
             exchange.gather_state(self)
@@ -193,12 +230,14 @@ class Student:
 
     # ---------------------------------------------------------------- state/IO
     def weights(self):
+        self.join_update()
         if self.sharded:
             raise RuntimeError("fp32 parameters are sharded across ranks; call sync_state() on every rank first")
         return {name: t.detach() for name, t in self.core.state_dict().items()}
 
     def optimizer_state_dict(self):
         """torch.optim.AdamW-compatible state_dict (same indices and groups)."""
+        self.join_update()
         if self.sharded:
             raise RuntimeError("Adam moments are sharded across ranks; call sync_state() on every rank first")
         flat, cfg = self.flat, self.cfg
@@ -222,6 +261,7 @@ class Student:
                 "_get_lr_called_within_step": False, "_last_lr": [lr, lr], "lr_lambdas": [None, None]}
 
     def load_optimizer_state(self, optimizer, scheduler):
+        self.join_update()
         flat = self.flat
         with torch.no_grad():
             for i, name in enumerate(flat.names):

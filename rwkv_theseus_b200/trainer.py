@@ -78,19 +78,32 @@ class StepEngine:
         self.cfg, self.topo, self.runner = cfg, topo, runner
         self.order, self.students, self.captures = order, students, captures
         self.device = topo.device
-        self._staging = None
+        self._staging = [None, None]   # pinned id buffers, used alternately
+        self._staged = [None, None]    # event after the copy out of each buffer
+        self._turn = 0
         self.profiler = StepProfiler(self.device)
+        if self.device.type == "cuda":
+            for student in students.values():
+                student.overlap_update = True
 
     def _to_device(self, ids):
-        """Stage token ids through a persistent pinned buffer, copy asynchronously."""
+        """Stage token ids through two persistent pinned buffers (alternating), copy asynchronously. A buffer
+        is refilled only after the copy that last read it has run (its event), since the host may be more
+        than a step ahead of the device."""
         if self.device.type != "cuda":
             return ids
-        n = ids.numel()
-        if self._staging is None or self._staging.numel() < n:
-            self._staging = torch.empty(max(n, 1 << 16), dtype=torch.int64, pin_memory=True)
-        host = self._staging[:n].view(ids.shape)
+        n, i = ids.numel(), self._turn
+        self._turn ^= 1
+        if self._staged[i] is not None:
+            self._staged[i].synchronize()
+        if self._staging[i] is None or self._staging[i].numel() < n:
+            self._staging[i] = torch.empty(max(n, 1 << 16), dtype=torch.int64, pin_memory=True)
+        host = self._staging[i][:n].view(ids.shape)
         host.copy_(ids)
-        return host.to(self.device, non_blocking=True)
+        out = host.to(self.device, non_blocking=True)
+        self._staged[i] = torch.cuda.Event()
+        self._staged[i].record()
+        return out
 
     def step(self, reader):
         """One optimizer update of every layer; returns per-layer device reports."""
@@ -124,6 +137,8 @@ class StepEngine:
 
     def read_metrics(self, reports):
         """One device-to-host copy of all layer reports; raises on update errors."""
+        for student in self.students.values():
+            student.join_update()
         rows = torch.stack([reports[layer] for layer in self.order]).double().cpu().tolist()
         self.topo.check_grad_sync()
         if self.topo.device.type == "cuda" and native().gemm_fault():
