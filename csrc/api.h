@@ -27,6 +27,10 @@ cudaError_t rt_wkv7_backward(int dtype, int B, int T, int H, int N, const void* 
 cudaError_t rt_gemm_bf16(const void* A, long lda, int a_mn, const void* B, long ldb, int b_mn, void* C, long ldc,
                          int M, int N, int K, int epi, float alpha, int* status, cudaStream_t stream);
 int rt_gemm_fault();
+cudaError_t rt_gemm_nmse_bf16(const void* A, long lda, const void* B, long ldb, void* dpred, long ldc, const void* target,
+                              float* rowsum, int M, int N, int K, float eps, int* status, cudaStream_t stream);
+cudaError_t rt_loss_rows_prep(const void* target, float* rowsum, long rows, int C, cudaStream_t stream);
+cudaError_t rt_loss_rows_finish(const float* rowsum, float* stats, long rows, int C, float eps, cudaStream_t stream);
 cudaError_t rt_gemm_bf16_tile(const void* A, long lda, int a_mn, const void* B, long ldb, int b_mn, void* C, long ldc,
                               int M, int N, int K, int epi, float alpha, int choice, int* status, cudaStream_t stream);
 cudaError_t rt_gemm_skinny_bf16(const void* X, long ldx, const void* W, const void* Wu, long ldw, float* ws,

@@ -348,6 +348,29 @@ void act_bwd_(at::Tensor h, at::Tensor dh, int64_t mode) {
   c10::cuda::CUDAGuard guard(h.device());
   check_cuda(rt_act_bwd(PTR(h), PTR(dh), h.numel(), mode, stream_of(h)), "act_bwd");
 }
+// Student output projection fused with the distillation loss: returns dpred [M, N] bf16; stats += [sum nmse,
+// sum cos, rows] (x [M, K] bf16, w [N, K] bf16, target [M, N] bf16; p = x w^T is never stored).
+at::Tensor gemm_nmse(at::Tensor x, at::Tensor w, at::Tensor target, at::Tensor stats, double eps) {
+  c10::cuda::CUDAGuard guard(x.device());
+  auto a = operand(x, "x");
+  auto b = operand(w, "w");
+  check_bf16(target, "target");
+  const long M = x.size(0), K = x.size(1), N = w.size(0);
+  TORCH_CHECK(w.size(1) == K && target.numel() == M * N, "gemm_nmse: shape mismatch");
+  TORCH_CHECK(stats.is_cuda() && stats.scalar_type() == at::kFloat && stats.numel() >= 3 && stats.is_contiguous(),
+              "stats must be fp32 [3]");
+  auto dpred = at::empty({M, N}, x.options().dtype(at::kBFloat16));
+  auto rowsum = at::empty({M, 4}, x.options().dtype(at::kFloat));
+  auto s = stream_of(x);
+  check_cuda(rt_loss_rows_prep(target.data_ptr(), rowsum.data_ptr<float>(), M, N, s), "loss_rows_prep");
+  check_cuda(rt_gemm_nmse_bf16(a.ptr, a.ld, b.ptr, b.ld, dpred.data_ptr(), N, target.data_ptr(),
+                               rowsum.data_ptr<float>(), M, N, K, (float)eps, nullptr, s),
+             "gemm_nmse");
+  check_cuda(rt_loss_rows_finish(rowsum.data_ptr<float>(), stats.data_ptr<float>(), M, N, (float)eps, s),
+             "loss_rows_finish");
+  return dpred;
+}
+
 void nmse_loss(at::Tensor pred, at::Tensor target, at::Tensor stats, c10::optional<at::Tensor> dpred, double eps) {
   need(pred.is_contiguous() && target.is_contiguous() && pred.sizes() == target.sizes(), "loss operands");
   c10::cuda::CUDAGuard guard(pred.device());
@@ -453,6 +476,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("out") = py::none(), py::arg("tile") = 0);
   m.def("gemm_fault", []() { return rt_gemm_fault(); },
         "1 if a GEMM gave up a bounded wait since the last call (then cleared); synchronizes the device");
+  m.def("gemm_nmse", &gemm_nmse, "output GEMM with the NMSE/cosine loss in the epilogue: returns d loss / d p",
+        py::arg("x"), py::arg("w"), py::arg("target"), py::arg("stats"), py::arg("eps"));
   m.def("gemm_swiglu", &gemm_swiglu, "silu(A . Bg^T) * (A . Bu^T) in one tcgen05 GEMM");
   m.def("rmsnorm_1p", &rmsnorm_1p);
   m.def("add_rmsnorm_1p", &add_rmsnorm_1p);

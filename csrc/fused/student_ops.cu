@@ -402,6 +402,49 @@ __global__ void nmse_loss_kernel(const bf16* __restrict__ pred, const bf16* __re
   }
 }
 
+// Fused-loss path (output GEMM epilogue computes dpred and the row sums): rowsum [rows, 4] = {sum t^2, 0, 0, 0}
+// before the GEMM; after it, one block turns the rows' sums into stats += [sum nmse, sum cos, rows] in a fixed
+// order (deterministic).
+__global__ void loss_rows_prep_kernel(const bf16* __restrict__ target, float* __restrict__ rowsum, int C) {
+  __shared__ float scratch[32];
+  const long row = blockIdx.x;
+  float tt = 0.f;
+  if (C % 8 == 0 && (reinterpret_cast<uintptr_t>(target) & 15) == 0) {
+    const uint4* t8 = reinterpret_cast<const uint4*>(target + row * C);
+    for (int c = threadIdx.x; c < C / 8; c += blockDim.x) {
+      float t[8];
+      rt::unpack8(__ldg(t8 + c), t);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) tt += t[u] * t[u];
+    }
+  } else {
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+      const float t = rt::to_f(target[row * C + c]);
+      tt += t * t;
+    }
+  }
+  tt = rt::block_sum(tt, scratch);
+  if (threadIdx.x < 4) rowsum[4 * row + threadIdx.x] = threadIdx.x == 0 ? tt : 0.f;
+}
+
+__global__ void loss_rows_finish_kernel(const float4* __restrict__ rowsum, float* __restrict__ stats, long rows, int C,
+                                        float eps) {
+  __shared__ float scratch[32];
+  float nmse = 0.f, cosv = 0.f;
+  for (long r = threadIdx.x; r < rows; r += blockDim.x) {
+    const float4 q = rowsum[r];  // {tt, se, pp, pt}
+    nmse += (q.y / C) / fmaxf(q.x / C, eps);
+    cosv += q.w / sqrtf(fmaxf(q.z * q.x, eps * eps));
+  }
+  nmse = rt::block_sum(nmse, scratch);
+  cosv = rt::block_sum(cosv, scratch);
+  if (threadIdx.x == 0) {
+    stats[0] += nmse;
+    stats[1] += cosv;
+    stats[2] += (float)rows;
+  }
+}
+
 // ---------------------------------------------------------------- optimizer
 // The gradient buffer is read, never written: the next micro-step's GEMMs store the four big matrices' gradients
 // and the rest of the buffer is cleared when that micro-step starts (models/student_fused.py).
@@ -574,6 +617,19 @@ extern "C" cudaError_t rt_act(void* x, long n, int mode, cudaStream_t s) {
 
 extern "C" cudaError_t rt_act_bwd(const void* h, void* dh, long n, int mode, cudaStream_t s) {
   act_bwd_kernel<<<(n + 255) / 256, 256, 0, s>>>((const bf16*)h, (bf16*)dh, n, mode);
+  return cudaGetLastError();
+}
+
+extern "C" cudaError_t rt_loss_rows_prep(const void* target, float* rowsum, long rows, int C, cudaStream_t s) {
+  if (rows <= 0) return cudaSuccess;
+  loss_rows_prep_kernel<<<rows, 128, 0, s>>>((const bf16*)target, rowsum, C);
+  return cudaGetLastError();
+}
+
+extern "C" cudaError_t rt_loss_rows_finish(const float* rowsum, float* stats, long rows, int C, float eps,
+                                           cudaStream_t s) {
+  if (reinterpret_cast<uintptr_t>(rowsum) & 15) return cudaErrorInvalidValue;
+  loss_rows_finish_kernel<<<1, 1024, 0, s>>>((const float4*)rowsum, stats, rows, C, eps);
   return cudaGetLastError();
 }
 

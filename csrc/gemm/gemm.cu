@@ -41,7 +41,7 @@
 
 namespace {
 
-enum Epi : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_F32_ACCUM = 2, EPI_SWIGLU = 3, EPI_ATOMIC_T = 4 };
+enum Epi : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_F32_ACCUM = 2, EPI_SWIGLU = 3, EPI_ATOMIC_T = 4, EPI_NMSE = 5 };
 
 constexpr int BM = 128, BK = 64, STAGES = 4, THREADS = 192;
 constexpr int MN_CHUNK_BYTES = 64 * BK * 2;  // one 64-wide MN-major chunk: BK rows x 128 B
@@ -77,6 +77,11 @@ struct GemmArgs {
   int sk, q, rem;
   float* ws;   // fp32 partial tiles, one BM x BN slot per CTA
   int* flags;  // per tile: partial warps published (4 per contributing CTA); reset by the tile's final CTA
+  // EPI_NMSE: target [M, N] bf16 (row stride N) and per-row sums [M, 4] = {sum t^2 (given), sum (p-t)^2, sum p^2,
+  // sum p t}; C receives d loss / d p = 2 (p - t) / (N max(mean t^2, eps)) in bf16.
+  const __nv_bfloat16* target;
+  float* rowsum;
+  float eps;
 };
 
 // Work of one CTA: whole (or split-K) tiles strided over the grid, or its stream-K pieces, last first.
@@ -189,6 +194,42 @@ __device__ __forceinline__ void store_row(float (&v)[32], int epi, void* C, long
 #pragma unroll
       for (int i = 0; i < 32; ++i)
         if (col + i < N) out[i] += alpha * v[i];
+    }
+  }
+}
+
+// Distillation-loss epilogue for one row's 32 columns: dpred to C, partial sums of (p-t)^2, p^2, p t.
+__device__ __forceinline__ void loss_row(const float (&v)[32], const GemmArgs& a, int row, int col, float& se,
+                                         float& pp, float& pt) {
+  const float tt = a.rowsum[4 * (long)row];
+  const float k = 2.f / (a.N * fmaxf(tt / a.N, a.eps));
+  const __nv_bfloat16* trow = a.target + (long)row * a.N + col;
+  __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.C) + (long)row * a.ldc + col;
+  if (col + 32 <= a.N && ((reinterpret_cast<uintptr_t>(trow) | reinterpret_cast<uintptr_t>(out)) & 15) == 0) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float t[8], d[8];
+      rt::unpack8(__ldg(reinterpret_cast<const uint4*>(trow) + q), t);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float p = v[8 * q + u], e = p - t[u];
+        se += e * e;
+        pp += p * p;
+        pt += p * t[u];
+        d[u] = k * e;
+      }
+      reinterpret_cast<uint4*>(out)[q] = rt::pack8(d);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      if (col + i < a.N) {
+        const float p = v[i], t = __bfloat162float(trow[i]), e = p - t;
+        se += e * e;
+        pp += p * p;
+        pt += p * t;
+        out[i] = __float2bfloat16_rn(k * e);
+      }
     }
   }
 }
@@ -344,6 +385,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
       const bool fixup = C_::NB == 1 && args.sk && k1 == kblocks && k0 > 0;  // final piece: add earlier partials
       int first_slot = 0;
       int* flag = args.flags + 4 * tile + quarter;  // one counter per row quarter: warps sync pairwise
+      float se = 0.f, pp = 0.f, pt = 0.f;           // EPI_NMSE row sums over this tile's columns
       if (fixup) {
         first_slot = sk_owner(tile * kblocks, args.q, args.rem);
         const int need = (int)blockIdx.x - first_slot;
@@ -390,7 +432,17 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
             }
           }
         }
-        if (row < args.M) store_row(v, EPI, args.C, args.ldc, row, tn * BN + c * 32, args.N, args.alpha);
+        if (row < args.M) {
+          if (EPI == EPI_NMSE)
+            loss_row(v, args, row, tn * BN + c * 32, se, pp, pt);
+          else
+            store_row(v, EPI, args.C, args.ldc, row, tn * BN + c * 32, args.N, args.alpha);
+        }
+      }
+      if (EPI == EPI_NMSE && !partial && row < args.M) {
+        atomicAdd(args.rowsum + 4 * (long)row + 1, se);
+        atomicAdd(args.rowsum + 4 * (long)row + 2, pp);
+        atomicAdd(args.rowsum + 4 * (long)row + 3, pt);
       }
       sm100::tc_fence_before();
       sm100::mbar_arrive(&tempty[acc]);
@@ -487,9 +539,16 @@ SkWorkspace* sk_workspace(cudaStream_t stream) {
   return &w;
 }
 
+struct LossArgs {
+  const void* target = nullptr;
+  float* rowsum = nullptr;
+  float eps = 0.f;
+};
+
 template <int BN, bool A_MN, bool B_MN, int EPI>
 cudaError_t launch(const void* A, long lda, const void* B0, const void* B1, long ldb, void* C, long ldc, int M,
-                   int N, int K, float alpha, int* status, cudaStream_t stream, int splits = 1, bool sk = false) {
+                   int N, int K, float alpha, int* status, cudaStream_t stream, int splits = 1, bool sk = false,
+                   LossArgs loss = LossArgs()) {
   using C_ = Cfg<BN, A_MN, B_MN, EPI>;
   CUtensorMap ta, tb0, tb1;
   bool ok = A_MN ? make_tmap(&ta, A, M, K, lda * 2, 64, BK) : make_tmap(&ta, A, K, M, lda * 2, BK, BM);
@@ -507,6 +566,9 @@ cudaError_t launch(const void* A, long lda, const void* B0, const void* B1, long
   args.kchunk = ((K + BK - 1) / BK + splits - 1) / splits;
   const int total = args.tiles_m * args.tiles_n * splits;
   args.sk = 0; args.q = 0; args.rem = 0; args.ws = nullptr; args.flags = nullptr;
+  args.target = static_cast<const __nv_bfloat16*>(loss.target);
+  args.rowsum = loss.rowsum;
+  args.eps = loss.eps;
   int grid = total < num_sms_cached() ? total : num_sms_cached();
   if (sk && C_::NB == 1 && splits == 1 && EPI != EPI_ATOMIC_T) {
     const long iters = (long)args.tiles_m * args.tiles_n * ((K + BK - 1) / BK);
@@ -621,7 +683,7 @@ int measured_bn(const TileKey& key, int M, int K, const void* A, long lda, const
   }
   const int guess = pick_bn(key.M, key.N, false, key.b_mn != 0);
   cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
-  if (epi == EPI_F32_ACCUM || cudaStreamIsCapturing(stream, &cap) != cudaSuccess ||
+  if (epi == EPI_F32_ACCUM || epi == EPI_NMSE || cudaStreamIsCapturing(stream, &cap) != cudaSuccess ||
       cap != cudaStreamCaptureStatusNone)
     return guess;
   cudaEvent_t e0, e1;
@@ -683,6 +745,42 @@ extern "C" cudaError_t rt_gemm_bf16(const void* A, long lda, int a_mn, const voi
   const TileKey key{(M + BM - 1) / BM * BM, N, (K + 511) / 512 * 512, a_mn != 0, b_mn != 0};
   const int bn = measured_bn(key, M, K, A, lda, B, ldb, C, ldc, epi, alpha, status, stream);
   return gemm_with_bn(bn, A, lda, a_mn, B, ldb, b_mn, C, ldc, M, N, K, epi, alpha, status, stream);
+}
+
+namespace {
+cudaError_t nmse_dispatch(int choice, const void* A, long lda, const void* B, long ldb, void* C, long ldc, int M, int N,
+                          int K, const LossArgs& loss, int* status, cudaStream_t s) {
+  const int bn = choice & (SK_FLAG - 1);
+  const bool sk = (choice & SK_FLAG) != 0;
+#define RT_L(W) return launch<W, false, false, EPI_NMSE>(A, lda, B, B, ldb, C, ldc, M, N, K, 1.f, status, s, 1, sk, loss)
+  if (bn == 256) RT_L(256);
+  if (bn == 224) RT_L(224);
+  if (bn == 192) RT_L(192);
+  if (bn == 160) RT_L(160);
+  if (bn == 128) RT_L(128);
+  RT_L(64);
+#undef RT_L
+}
+}  // namespace
+
+// Student output projection with the distillation loss in the epilogue: p = A B^T (A [M, K], B [N, K], both K-major)
+// is never stored; dpred [M, N] (ldc) = 2 (p - t) / (N max(mean_row t^2, eps)) in bf16, and rowsum [M, 4] (whose
+// column 0 holds sum_row t^2 on entry) gains the row's sums of (p - t)^2, p^2 and p t. Tile choice: the one measured
+// for this shape bucket by a store-epilogue call, else the wave-fill estimate (timing would repeat the sums).
+extern "C" cudaError_t rt_gemm_nmse_bf16(const void* A, long lda, const void* B, long ldb, void* dpred, long ldc,
+                                         const void* target, float* rowsum, int M, int N, int K, float eps,
+                                         int* status, cudaStream_t stream) {
+  if (M <= 0 || N <= 0 || K <= 0) return cudaSuccess;
+  if ((lda & 7) || (ldb & 7) || (ldc & 7) || (reinterpret_cast<uintptr_t>(A) & 15) ||
+      (reinterpret_cast<uintptr_t>(B) & 15))
+    return cudaErrorInvalidValue;
+  const TileKey key{(M + BM - 1) / BM * BM, N, (K + 511) / 512 * 512, 0, 0};
+  const int choice = measured_bn(key, M, K, A, lda, B, ldb, dpred, ldc, EPI_NMSE, 1.f, status, stream);
+  LossArgs loss;
+  loss.target = target;
+  loss.rowsum = rowsum;
+  loss.eps = eps;
+  return nmse_dispatch(choice, A, lda, B, ldb, dpred, ldc, M, N, K, loss, status, stream);
 }
 
 // 1 if a GEMM launched without a status word gave up a wait since the last call (synchronizes the device).

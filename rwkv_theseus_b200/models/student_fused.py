@@ -9,8 +9,8 @@ forward
     pre-WKV (decay, ICL rate, kk, k', a/b inputs)   1 kernel
     chunked WKV7 (chunk checkpoints kept)            1 kernel
     post-WKV (GroupNorm, bonus, output gate)         1 kernel
-    output projection                                1 GEMM
-    NMSE/cosine sums + d loss / d prediction         1 kernel
+    output projection + NMSE/cosine row sums and     1 GEMM (loss in the epilogue; the prediction
+      d loss / d prediction                            is never stored) + row prep / finish
 backward
     output projection dX / dW                        2 GEMMs (dW accumulates into the fp32 flat buffer)
     post-WKV backward (+ ln_x, r_k partial sums)     1 kernel
@@ -127,7 +127,7 @@ class FusedStudent:
         return state["shift"].to(torch.bfloat16).contiguous(), state["wkv"].float().contiguous()
 
     # ------------------------------------------------------------------ forward
-    def _forward(self, x, state, keep):
+    def _forward(self, x, state, keep, project=True):
         B, T, C = x.shape
         M, H, N = B * T, self.H, self.N
         x = x.to(torch.bfloat16).contiguous()
@@ -156,7 +156,7 @@ class FusedStudent:
         yg = torch.empty_like(r)
         gn = torch.empty(M * H * 3, device=x.device)
         ext.tm_post_wkv(y, r, k_in, v, g, self.p("ln_x.weight"), self.p("ln_x.bias"), self.p("r_k"), yg, gn, H, N)
-        pred = self.mm(yg, False, self.w("output.weight"), False)
+        pred = self.mm(yg, False, self.w("output.weight"), False) if project else None
         new_state = {"shift": x[:, -1].clone(), "wkv": end}
         saved = None
         if keep:
@@ -194,10 +194,12 @@ class FusedStudent:
         ext = native()
         if first:
             self.student.flat.grad[self.student.decay_numel:].zero_()
-        pred, new_state, s = self._forward(x, state, True)
+        _, new_state, s = self._forward(x, state, True, project=False)
         stats = torch.zeros(3, device=x.device)
-        dpred = torch.empty_like(pred)
-        ext.nmse_loss(pred, target.reshape(M, C).to(torch.bfloat16).contiguous(), stats, dpred, float(eps))
+        # output projection with the loss in its epilogue: d loss / d prediction directly (no prediction tensor)
+        dpred = ext.gemm_nmse(s["yg"], self.w("output.weight"), target.reshape(M, C).to(torch.bfloat16).contiguous(),
+                              stats, float(eps))
+        pred = dpred  # shape/dtype template for the gradient buffers below
         # output projection
         dyg = self.mm(dpred, False, self.w("output.weight"), True)
         self.mm_grad("output.weight", first, dpred, True, s["yg"], True)

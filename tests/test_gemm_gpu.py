@@ -111,3 +111,27 @@ def test_stream_k_accumulate_mn_major():
     ref = acc + 0.5 * (dy.float().t() @ x.float())
     native().gemm(dy, True, x, True, 2, 0.5, acc, 256 | SK)
     _check(acc, ref, 1e-3)
+
+
+@cuda
+@pytest.mark.parametrize("M,N,K,tuned", [(1024, 5120, 5120, True), (300, 1000, 1000, False), (37, 256, 512, False)])
+def test_fused_loss_epilogue_matches_fp32(M, N, K, tuned):
+    """Output GEMM with the NMSE/cosine loss in its epilogue vs the fp32 statistics and their gradient."""
+    from rwkv_theseus_b200.losses import statistics
+    x, w = _bf(M, K, seed=11), _bf(N, K, seed=12)
+    target = (_bf(M, N, seed=13).float() * 3).to(torch.bfloat16)
+    if tuned:  # a measured (possibly stream-K) tile choice for this shape bucket
+        native().gemm(x, False, w, False, 0, 1.0, None)
+    p = x.float() @ w.float().t()
+    eps = 1e-6
+    ref = statistics(p, target.float(), eps)
+    denom = target.float().square().mean(-1, keepdim=True).clamp_min(eps)
+    ref_grad = 2 * (p - target.float()) / (N * denom)
+    stats = torch.zeros(3, device="cuda")
+    dpred = native().gemm_nmse(x, w, target, stats, eps)
+    torch.testing.assert_close(stats, ref, rtol=1e-3, atol=1e-3)
+    _check(dpred, ref_grad)
+    stats2 = torch.zeros(3, device="cuda")
+    dpred2 = native().gemm_nmse(x, w, target, stats2, eps)
+    assert torch.equal(dpred, dpred2)
+    torch.testing.assert_close(stats2, stats, rtol=1e-5, atol=0)  # row sums gather tiles with float atomics
