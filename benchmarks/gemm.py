@@ -48,7 +48,13 @@ def main():
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--only", default=None)
+    p.add_argument("--tile", default=None,
+                   help="fixed tile choice instead of the measured one: width, with suffix 'sk' for stream-K")
+    p.add_argument("--no-cublas", action="store_true")
     args = p.parse_args()
+    tile = 0
+    if args.tile:
+        tile = int(args.tile.rstrip("sk")) | ((1 << 16) if args.tile.endswith("sk") else 0)
     results = []
     for name, M, N, K, a_t, b_t in SHAPES:
         if args.only and args.only not in name:
@@ -60,7 +66,7 @@ def main():
         out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
 
         def ours(i):
-            native().gemm(As[i % sets], a_t, Bs[i % sets], b_t, 0, 1.0, out)
+            native().gemm(As[i % sets], a_t, Bs[i % sets], b_t, 0, 1.0, out, tile)
 
         def cublas(i):
             a = As[i % sets].t() if a_t else As[i % sets]
@@ -69,9 +75,9 @@ def main():
 
         flops = 2.0 * M * N * K
         t_ours = timed(ours, args.warmup, args.iters)
-        t_cub = timed(cublas, args.warmup, args.iters)
+        t_cub = float("nan") if args.no_cublas else timed(cublas, args.warmup, args.iters)
         ref = torch.matmul(As[0].t() if a_t else As[0], Bs[0] if b_t else Bs[0].t()).float()
-        native().gemm(As[0], a_t, Bs[0], b_t, 0, 1.0, out)
+        native().gemm(As[0], a_t, Bs[0], b_t, 0, 1.0, out, tile)
         rel = ((out.float() - ref).abs().max() / ref.abs().max()).item()
         row = {"shape": name, "M": M, "N": N, "K": K, "ours_ms": t_ours, "cublas_ms": t_cub,
                "ours_tflops": flops / t_ours / 1e9, "cublas_tflops": flops / t_cub / 1e9,
