@@ -348,6 +348,21 @@ void act_bwd_(at::Tensor h, at::Tensor dh, int64_t mode) {
   c10::cuda::CUDAGuard guard(h.device());
   check_cuda(rt_act_bwd(PTR(h), PTR(dh), h.numel(), mode, stream_of(h)), "act_bwd");
 }
+// Per-row KL(softmax(teacher) || softmax(student)) of two [rows, V] logit matrices (bf16 or fp32, unit inner stride).
+at::Tensor kl_rows(at::Tensor student, at::Tensor teacher) {
+  c10::cuda::CUDAGuard guard(student.device());
+  TORCH_CHECK(student.is_cuda() && teacher.is_cuda() && student.dim() == 2 && student.sizes() == teacher.sizes() &&
+                  student.scalar_type() == teacher.scalar_type() && student.stride(1) == 1 && teacher.stride(1) == 1,
+              "kl_rows: two CUDA [rows, V] logit matrices of one dtype with unit inner stride");
+  TORCH_CHECK(student.scalar_type() == at::kBFloat16 || student.scalar_type() == at::kFloat, "kl_rows: bf16 or fp32");
+  auto out = at::empty({student.size(0)}, student.options().dtype(at::kFloat));
+  check_cuda(rt_kl_rows(student.scalar_type() == at::kBFloat16 ? 1 : 0, student.data_ptr(), teacher.data_ptr(),
+                        student.size(0), student.size(1), student.stride(0), teacher.stride(0), out.data_ptr<float>(),
+                        stream_of(student)),
+             "kl_rows");
+  return out;
+}
+
 // Student output projection fused with the distillation loss: returns dpred [M, N] bf16; stats += [sum nmse,
 // sum cos, rows] (x [M, K] bf16, w [N, K] bf16, target [M, N] bf16; p = x w^T is never stored).
 at::Tensor gemm_nmse(at::Tensor x, at::Tensor w, at::Tensor target, at::Tensor stats, double eps) {
@@ -476,6 +491,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("out") = py::none(), py::arg("tile") = 0);
   m.def("gemm_fault", []() { return rt_gemm_fault(); },
         "1 if a GEMM gave up a bounded wait since the last call (then cleared); synchronizes the device");
+  m.def("kl_rows", &kl_rows, "per-row KL(teacher || student) over the vocabulary in one pass", py::arg("student"),
+        py::arg("teacher"));
   m.def("gemm_nmse", &gemm_nmse, "output GEMM with the NMSE/cosine loss in the epilogue: returns d loss / d p",
         py::arg("x"), py::arg("w"), py::arg("target"), py::arg("stats"), py::arg("eps"));
   m.def("gemm_swiglu", &gemm_swiglu, "silu(A . Bg^T) * (A . Bu^T) in one tcgen05 GEMM");

@@ -31,7 +31,18 @@ def metrics(stats):
 
 
 def kl_sum(student_logits, teacher_logits):
-    """Sum over tokens of KL(teacher || student) on the full vocabulary."""
+    """Sum over tokens of KL(teacher || student) on the full vocabulary.
+
+    CUDA tensors take the one-pass kernel (``csrc/fused/kl.cu``: online max / sums per row, per-row results
+    summed here in a fixed order); otherwise two log_softmax passes (reference ``theseus/losses.py:27-30``)."""
+    if student_logits.is_cuda:
+        from .ops import native
+        V = student_logits.shape[-1]
+        s = student_logits.reshape(-1, V)
+        t = teacher_logits.reshape(-1, V)
+        if s.dtype not in (torch.bfloat16, torch.float32) or s.dtype != t.dtype:
+            s, t = s.float(), t.float()
+        return native().kl_rows(s.contiguous(), t.contiguous()).sum()
     teacher = F.log_softmax(teacher_logits.float(), dim=-1)
     student = F.log_softmax(student_logits.float(), dim=-1)
     return (teacher.exp() * (teacher - student)).sum()

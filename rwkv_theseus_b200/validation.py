@@ -103,12 +103,20 @@ def validate_original_kl(topo, cfg, runner):
             hidden = runner.forward(batch["ids"].to(topo.device))
             for start in range(0, hidden.shape[1], cfg["kl_token_block"]):
                 stop = start + cfg["kl_token_block"]
-                logits = hidden[:, start:stop].to(head.dtype) @ head.t()
-                target = teacher[:, start:stop].to(device=topo.device, dtype=head.dtype) @ head.t()
+                logits = _logits(hidden[:, start:stop], head)
+                target = _logits(teacher[:, start:stop].to(topo.device), head)
                 total[0] += kl_sum(logits, target)
                 total[1] += logits.shape[0] * logits.shape[1]
     topo.student_sum(total)
     return {"original_teacher_kl": (total[0] / total[1]).item()}
+
+
+def _logits(hidden, head):
+    """lm_head logits in the head's dtype (tcgen05 GEMM on CUDA bf16, matmul otherwise)."""
+    if hidden.is_cuda and head.dtype == torch.bfloat16:
+        from .ops.gemm import linear
+        return linear(hidden.to(torch.bfloat16), head)
+    return hidden.to(head.dtype) @ head.t()
 
 
 @torch.no_grad()
