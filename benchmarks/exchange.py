@@ -61,6 +61,7 @@ def main():
     p.add_argument("--iters", type=int, default=10)
     p.add_argument("--blocks", default="148", help="comma-separated block counts to compare")
     p.add_argument("--profile", action="store_true")
+    p.add_argument("--modes", default="split", help="comma-separated: split (update, then all-gather), fused")
     a = p.parse_args()
     topo = Topology("nccl", 5)
     dev, n, N = topo.device, a.numel, topo.world
@@ -113,17 +114,19 @@ def main():
     frac = (N - 1) / N
     link_ms = 6 * n * frac / (LINK_GBS * 1e9) * 1e3
     t_nccl = None
-    for blocks in [int(b) for b in a.blocks.split(",")]:
-        ex.blocks = blocks
-        t_peer = timed(peer, a.iters, topo) - base
-        ex.check()
-        if t_nccl is None:
-            t_nccl = timed(nccl, a.iters, topo) - base
-        if topo.rank == 0:
-            print(json.dumps({"bench": "layer_exchange", "n_gpus": N, "numel": n, "peer_ms": t_peer,
-                              "nccl_ms": t_nccl, "nvlink_roofline_ms": link_ms,
-                              "peer_fraction_of_roofline": link_ms / t_peer, "speedup_vs_nccl": t_nccl / t_peer,
-                              "blocks": blocks}), flush=True)
+    for mode in a.modes.split(","):
+        ex.fused = mode == "fused"
+        for blocks in [int(b) for b in a.blocks.split(",")]:
+            ex.blocks = blocks
+            t_peer = timed(peer, a.iters, topo) - base
+            ex.check()
+            if t_nccl is None:
+                t_nccl = timed(nccl, a.iters, topo) - base
+            if topo.rank == 0:
+                print(json.dumps({"bench": "layer_exchange", "n_gpus": N, "numel": n, "peer_ms": t_peer,
+                                  "nccl_ms": t_nccl, "nvlink_roofline_ms": link_ms,
+                                  "peer_fraction_of_roofline": link_ms / t_peer, "speedup_vs_nccl": t_nccl / t_peer,
+                                  "blocks": blocks, "mode": mode}), flush=True)
     ex.close()
     topo.close()
 

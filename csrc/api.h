@@ -101,7 +101,8 @@ int rt_exchange_signal_words();
 cudaError_t rt_exchange_update(float* const* grads, float* const* params, void* const* shadows, unsigned* const* sigs,
                                int rank, int world, long n, float* m, float* v, float* stats, float* report, float lr,
                                float beta1, float beta2, float eps, float weight_decay, float clip, int step,
-                               long decay_numel, unsigned epoch, double limit_s, int blocks, cudaStream_t s);
+                               long decay_numel, unsigned epoch, double limit_s, int blocks, int mode,
+                               cudaStream_t s);
 void rt_exchange_shard(long n, int rank, int world, long* out4);
 cudaError_t rt_ipc_export(const void* ptr, void* handle64, long* offset);
 cudaError_t rt_ipc_open(const void* handle64, void** base);

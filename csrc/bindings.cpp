@@ -415,7 +415,8 @@ void to_bf16_(at::Tensor src, at::Tensor dst) {
 void exchange_update(std::vector<int64_t> grads, std::vector<int64_t> params, std::vector<int64_t> shadows,
                      std::vector<int64_t> sigs, int64_t rank, int64_t world, int64_t n, at::Tensor m, at::Tensor v,
                      at::Tensor stats, at::Tensor report, double lr, double beta1, double beta2, double eps, double wd,
-                     double clip, int64_t step, int64_t decay_numel, int64_t epoch, double limit_s, int64_t blocks) {
+                     double clip, int64_t step, int64_t decay_numel, int64_t epoch, double limit_s, int64_t blocks,
+                     int64_t mode) {
   need((int64_t)grads.size() == world && (int64_t)params.size() == world && (int64_t)shadows.size() == world &&
            (int64_t)sigs.size() == world, "one pointer per rank");
   need(m.numel() == n && v.numel() == n && m.is_cuda() && m.scalar_type() == at::kFloat, "moment buffers");
@@ -431,7 +432,7 @@ void exchange_update(std::vector<int64_t> grads, std::vector<int64_t> params, st
   c10::cuda::CUDAGuard guard(m.device());
   check_cuda(rt_exchange_update(g.data(), p.data(), sh.data(), sg.data(), (int)rank, (int)world, n, FPTR(m), FPTR(v),
                                 FPTR(stats), FPTR(report), lr, beta1, beta2, eps, wd, clip, (int)step, decay_numel,
-                                (unsigned)epoch, limit_s, (int)blocks, stream_of(m)),
+                                (unsigned)epoch, limit_s, (int)blocks, (int)mode, stream_of(m)),
              "exchange_update");
 }
 py::tuple ipc_export(at::Tensor t) {

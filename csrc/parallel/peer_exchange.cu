@@ -48,7 +48,9 @@ constexpr int WAITED = 27;     // rank whose flag was missing at the timeout
 constexpr int NORM_SLOT = 32;  // [MAXR] float partial norm^2 of rank q
 constexpr int STAT_SLOT = 40;  // [MAXR][3] float loss statistics of rank q
 constexpr int PARTIAL = 64;    // [grid] float per-block partial norm^2 (local)
-constexpr int SIG_WORDS = 1024;
+constexpr int SLICE = 1024;    // [update blocks] epoch of this rank's updated slice b (polled by peers)
+constexpr int MAX_SLICES = 1024;
+constexpr int SIG_WORDS = SLICE + MAX_SLICES;
 
 struct Peers {
   float* grad[MAXR];
@@ -321,6 +323,176 @@ exchange_gather_kernel(Peers peers, int rank, long n, long n8, long decay4, unsi
   }
 }
 
+// ---------------------------------------------------------------- B+C fused: slice updates and slice pulls at once
+// One kernel with two roles. Blocks [0, U) update this rank's shard slice by slice (S slices, slice s by block
+// s mod U, in increasing s): clip + AdamW into the fp32 master, moments and bf16 copy, then raise the slice's flag.
+// Blocks [U, U + P) pull: slice s of every peer's shard (bf16 copy and fp32 non-decay parameters), each as soon
+// as that peer's flag for it is up. Local HBM-bound updates and NVLink pulls run at the same time, and no grid-wide
+// barrier separates them. Update blocks have the lower indices, so they are dispatched before any pull block can
+// occupy an SM; pull waits only ever point at other ranks' update blocks. Slices are contiguous ranges of 8-element
+// units; the scalar tail [8 n8, n) belongs to the last rank's last slice.
+RT_DEVICE void slice_of(long n8, int q, int W, int sl, int S, long& lo, long& hi) {
+  const long slo = n8 * q / W, shi = n8 * (q + 1) / W;
+  lo = slo + (shi - slo) * sl / S;
+  hi = slo + (shi - slo) * (sl + 1) / S;
+}
+
+template <int W>
+__global__ void __launch_bounds__(THREADS_B)
+exchange_update_pull_kernel(Peers peers, int rank, long n, long n8, long decay4, int U, int S, float* __restrict__ m,
+                            float* __restrict__ v, float* __restrict__ stats, float* __restrict__ report, Adam a,
+                            unsigned epoch, unsigned long long limit_ns) {
+  constexpr int world = W;
+  constexpr int UNROLL = 2;
+  __shared__ int ok;
+  unsigned* sig = peers.sig[rank];
+  const int b = blockIdx.x;
+  if (b < U) {
+    // ---------------- update role
+    if (threadIdx.x == 0) ok = wait_all(sig, NORMF, world, epoch, limit_ns, 2);
+    __syncthreads();
+    if (!ok) return;
+    const float* slots = reinterpret_cast<const float*>(sig);
+    float norm2 = 0.f, s0 = 0.f, s1 = 0.f, count = 0.f;
+    for (int q = 0; q < world; ++q) {  // same order on every rank: identical clip coefficient everywhere
+      norm2 += __ldcg(slots + NORM_SLOT + q);
+      s0 += __ldcg(slots + STAT_SLOT + 3 * q + 0);
+      s1 += __ldcg(slots + STAT_SLOT + 3 * q + 1);
+      count += __ldcg(slots + STAT_SLOT + 3 * q + 2);
+    }
+    const float inv = count > 0.f ? 1.f / count : 0.f;
+    const float norm = sqrtf(norm2) * inv;
+    const float gscale = inv * fminf(1.f, a.clip / (norm + 1e-6f));
+    const float step = a.lr / a.bias1;
+    float4* __restrict__ p4s = reinterpret_cast<float4*>(peers.param[rank]);
+    const float4* __restrict__ g4s = reinterpret_cast<const float4*>(peers.grad[rank]);
+    float4* __restrict__ m4s = reinterpret_cast<float4*>(m);
+    float4* __restrict__ v4s = reinterpret_cast<float4*>(v);
+    uint2* __restrict__ sh2 = reinterpret_cast<uint2*>(peers.shadow[rank]);
+#pragma unroll 1
+    for (int sl = b; sl < S; sl += U) {
+      long lo, hi;
+      slice_of(n8, rank, W, sl, S, lo, hi);
+      const long lo4 = 2 * lo, hi4 = 2 * hi;
+      for (long i0 = lo4 + threadIdx.x; i0 < hi4; i0 += UNROLL * THREADS_B) {
+        float4 g4[UNROLL], p4[UNROLL], m4[UNROLL], v4[UNROLL];
+#pragma unroll
+        for (int u = 0; u < UNROLL; ++u) {
+          const long i = i0 + u * THREADS_B;
+          if (i < hi4) {
+            g4[u] = __ldcs(g4s + i);
+            p4[u] = p4s[i];
+            m4[u] = __ldcs(m4s + i);
+            v4[u] = __ldcs(v4s + i);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < UNROLL; ++u) {
+          const long i = i0 + u * THREADS_B;
+          if (i < hi4) {
+            const long e = 4 * i;
+            adam_one(g4[u].x * gscale, p4[u].x, m4[u].x, v4[u].x, e + 0, a, step);
+            adam_one(g4[u].y * gscale, p4[u].y, m4[u].y, v4[u].y, e + 1, a, step);
+            adam_one(g4[u].z * gscale, p4[u].z, m4[u].z, v4[u].z, e + 2, a, step);
+            adam_one(g4[u].w * gscale, p4[u].w, m4[u].w, v4[u].w, e + 3, a, step);
+            __stcs(m4s + i, m4[u]);
+            __stcs(v4s + i, v4[u]);
+            p4s[i] = p4[u];
+            __nv_bfloat162 l2 = __floats2bfloat162_rn(p4[u].x, p4[u].y);
+            __nv_bfloat162 h2 = __floats2bfloat162_rn(p4[u].z, p4[u].w);
+            uint2 packed;
+            packed.x = *reinterpret_cast<unsigned*>(&l2);
+            packed.y = *reinterpret_cast<unsigned*>(&h2);
+            sh2[i] = packed;
+          }
+        }
+      }
+      if (rank == W - 1 && sl == S - 1) {  // scalar tail
+        float* p = peers.param[rank];
+        const float* g = peers.grad[rank];
+        bf16* sh = peers.shadow[rank];
+        for (long i = 8 * n8 + threadIdx.x; i < n; i += THREADS_B) {
+          float pv = p[i], mv = m[i], vv = v[i];
+          adam_one(g[i] * gscale, pv, mv, vv, i, a, step);
+          m[i] = mv;
+          v[i] = vv;
+          p[i] = pv;
+          sh[i] = __float2bfloat16_rn(pv);
+        }
+      }
+      __threadfence_system();
+      __syncthreads();
+      if (threadIdx.x == 0) st_release_sys(sig + SLICE + sl, epoch);  // peers poll this word
+    }
+    if (b == 0 && threadIdx.x == 0) {
+      report[0] = s0;
+      report[1] = s1;
+      report[2] = count;
+      report[3] = norm;
+      report[4] = (!isfinite(norm) || count <= 0.f) ? 1.f : 0.f;
+      stats[0] = stats[1] = stats[2] = 0.f;
+    }
+    return;
+  }
+  // ---------------- pull role
+  const int P = gridDim.x - U;
+  constexpr int PU = 4;
+#pragma unroll 1
+  for (int sl = b - U; sl < S; sl += P) {
+#pragma unroll 1
+    for (int k = 1; k < W; ++k) {
+      const int q = (rank + k) % W;
+      if (threadIdx.x == 0) {
+        const unsigned long long t0 = now_ns();
+        unsigned spins = 0;
+        ok = 1;
+        while ((int)(ld_acquire_sys(peers.sig[q] + SLICE + sl) - epoch) < 0) {
+          if ((++spins & 63u) == 0 && now_ns() - t0 > limit_ns) {
+            if (atomicCAS(sig + STATUS, 0u, 3u) == 0u) sig[WAITED] = (unsigned)q;
+            ok = 0;
+            break;
+          }
+          __nanosleep(128);
+        }
+      }
+      __syncthreads();
+      if (!ok) return;
+      long qlo, qhi;
+      slice_of(n8, q, W, sl, S, qlo, qhi);
+      const uint4* src = reinterpret_cast<const uint4*>(peers.shadow[q]);
+      uint4* dst = reinterpret_cast<uint4*>(peers.shadow[rank]);
+      for (long i0 = qlo + threadIdx.x; i0 < qhi; i0 += PU * THREADS_B) {
+        uint4 r[PU];
+#pragma unroll
+        for (int u = 0; u < PU; ++u)
+          if (i0 + u * THREADS_B < qhi) r[u] = __ldcg(src + i0 + u * THREADS_B);
+#pragma unroll
+        for (int u = 0; u < PU; ++u)
+          if (i0 + u * THREADS_B < qhi) dst[i0 + u * THREADS_B] = r[u];
+      }
+      const long flo = 2 * qlo > decay4 ? 2 * qlo : decay4, fhi = 2 * qhi;  // fp32 non-decay parameters
+      const float4* fsrc = reinterpret_cast<const float4*>(peers.param[q]);
+      float4* fdst = reinterpret_cast<float4*>(peers.param[rank]);
+      for (long i0 = flo + threadIdx.x; i0 < fhi; i0 += PU * THREADS_B) {
+        float4 r[PU];
+#pragma unroll
+        for (int u = 0; u < PU; ++u)
+          if (i0 + u * THREADS_B < fhi) r[u] = __ldcg(fsrc + i0 + u * THREADS_B);
+#pragma unroll
+        for (int u = 0; u < PU; ++u)
+          if (i0 + u * THREADS_B < fhi) fdst[i0 + u * THREADS_B] = r[u];
+      }
+      if (q == W - 1 && sl == S - 1) {  // scalar tail of the last rank
+        for (long i = 8 * n8 + threadIdx.x; i < n; i += THREADS_B) {
+          peers.shadow[rank][i] = peers.shadow[q][i];
+          peers.param[rank][i] = peers.param[q][i];
+        }
+      }
+      __syncthreads();  // `ok` is reused by the next wait
+    }
+  }
+}
+
 // Shard of rank r: float4 body [lo4, hi4) in units of 8 elements, plus the scalar tail (owned by the last rank).
 void shard(long n, int rank, int world, long& lo4, long& hi4, long& tail_lo, long& tail_hi) {
   const long n8 = n / 8;
@@ -336,13 +508,14 @@ extern "C" int rt_exchange_signal_words() { return SIG_WORDS; }
 
 // grads/params/shadows/sigs: `world` device pointers each (index = rank; peers mapped into this process).
 // m, v: this rank's moment buffers; stats: this rank's [3] loss sums (cleared); report: [5].
-// All pointers 16-byte aligned. `blocks` <= SIG_WORDS - PARTIAL.
+// All pointers 16-byte aligned. `blocks` <= SLICE - PARTIAL. mode 0: reduce kernel + update/pull kernel; 1: reduce,
+// update and all-gather kernels.
 extern "C" cudaError_t rt_exchange_update(float* const* grads, float* const* params, void* const* shadows,
                                           unsigned* const* sigs, int rank, int world, long n, float* m, float* v,
                                           float* stats, float* report, float lr, float beta1, float beta2, float eps,
                                           float weight_decay, float clip, int step, long decay_numel,
-                                          unsigned epoch, double limit_s, int blocks, cudaStream_t s) {
-  if (world < 1 || world > MAXR || rank < 0 || rank >= world || blocks < 1 || blocks > SIG_WORDS - PARTIAL)
+                                          unsigned epoch, double limit_s, int blocks, int mode, cudaStream_t s) {
+  if (world < 1 || world > MAXR || rank < 0 || rank >= world || blocks < 1 || blocks > SLICE - PARTIAL)
     return cudaErrorInvalidValue;
   Peers peers = {};
   for (int q = 0; q < world; ++q) {
@@ -363,16 +536,25 @@ extern "C" cudaError_t rt_exchange_update(float* const* grads, float* const* par
   a.bias2_sqrt = (float)sqrt(1.0 - pow((double)beta2, (double)step));
   a.decay_numel = decay_numel;
   const long n8 = n / 8, decay4 = decay_numel / 4;
+  // fused update + pull (default): `slices` blocks, each one slice of every shard; else three-phase kernels
+  const bool fused = mode == 0;
+  const int upd = 2 * blocks;                      // update blocks (as many pull blocks)
+  const int slices = 8 * blocks < MAX_SLICES ? 8 * blocks : MAX_SLICES;  // 4 slices per update block
   switch (world) {
 #define RT_EXCHANGE_CASE(W)                                                                                        \
   case W:                                                                                                          \
     exchange_reduce_kernel<W><<<blocks, THREADS, 0, s>>>(peers, rank, lo4, hi4, tail_lo, tail_hi, stats, epoch,   \
                                                          limit_ns);                                                \
     RT_CUDA_CHECK(cudaGetLastError());                                                                             \
-    exchange_update_kernel<W><<<4 * blocks, THREADS_B, 0, s>>>(peers, rank, n, lo4, hi4, tail_lo, tail_hi, m, v, stats, \
-                                                         report, a, epoch, limit_ns);                              \
-    RT_CUDA_CHECK(cudaGetLastError());                                                                             \
-    exchange_gather_kernel<W><<<blocks, THREADS, 0, s>>>(peers, rank, n, n8, decay4, epoch, limit_ns);             \
+    if (fused) {                                                                                                   \
+      exchange_update_pull_kernel<W><<<2 * upd, THREADS_B, 0, s>>>(peers, rank, n, n8, decay4, upd, slices, m, v,    \
+                                                                   stats, report, a, epoch, limit_ns);             \
+    } else {                                                                                                       \
+      exchange_update_kernel<W><<<4 * blocks, THREADS_B, 0, s>>>(peers, rank, n, lo4, hi4, tail_lo, tail_hi, m, v,  \
+                                                                 stats, report, a, epoch, limit_ns);               \
+      RT_CUDA_CHECK(cudaGetLastError());                                                                           \
+      exchange_gather_kernel<W><<<blocks, THREADS, 0, s>>>(peers, rank, n, n8, decay4, epoch, limit_ns);           \
+    }                                                                                                              \
     break;
     RT_EXCHANGE_CASE(1)
     RT_EXCHANGE_CASE(2)
