@@ -33,7 +33,9 @@
 // All waits are bounded (sm100.cuh); on timeout the kernel records status 1
 // in *status and unwinds, freeing its TMEM.
 #include <cuda.h>
+#include <algorithm>
 #include <map>
+#include <vector>
 #include <mutex>
 #include <tuple>
 #include "../common/common.cuh"
@@ -75,6 +77,9 @@ struct GemmArgs {
   int* status;
   // stream-K (sk = 1): CTA c owns iterations [c q + min(c, rem), (c + 1) q + min(c + 1, rem)) of tiles x k-blocks
   int sk, q, rem;
+  // parallel split-K (splitp = S > 1): CTA c computes k-part c % S of tile c / S, publishes it as an fp32 partial,
+  // and after all S parts of the tile are published reduces rows [part BM / S, (part + 1) BM / S) of the tile
+  int splitp;
   float* ws;   // fp32 partial tiles, one BM x BN slot per CTA
   int* flags;  // per tile: partial warps published (4 per contributing CTA); reset by the tile's final CTA
   // EPI_NMSE: target [M, N] bf16 (row stride N) and per-row sums [M, 4] = {sum t^2 (given), sum (p-t)^2, sum p^2,
@@ -100,8 +105,20 @@ struct WorkIter {
     const int c = blockIdx.x;
     lo = c * a.q + min(c, a.rem);
     cur = (c + 1) * a.q + min(c + 1, a.rem);
+    splitp = a.splitp;
+    sp_done = 0;
   }
+  int splitp, sp_done;
   __device__ bool next(int& tile, int& k0, int& k1) {
+    if (splitp > 1) {
+      if (sp_done) return false;
+      sp_done = 1;
+      const int part = blockIdx.x % splitp;
+      tile = blockIdx.x / splitp;
+      k0 = (int)((long)kblocks * part / splitp);
+      k1 = (int)((long)kblocks * (part + 1) / splitp);
+      return true;
+    }
     if (sk) {
       if (cur <= lo) return false;
       tile = (cur - 1) / kblocks;
@@ -380,6 +397,79 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
       sm100::tc_fence_after();
       const int row = tm * BM + row_in_tile;
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * C_::ACC_COLS;
+      if (C_::NB == 1 && EPI != EPI_NMSE && EPI != EPI_ATOMIC_T && args.splitp > 1) {
+        // ---- parallel split-K: publish this part, wait for the tile's other parts, reduce this CTA's row band
+        const int S = args.splitp, part = blockIdx.x % S;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          sm100::tmem_ld32(t_row + c * 32, v);
+          sm100::tmem_wait_ld();
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            __stcg(sk_slot(args.ws, blockIdx.x, BN, c, q, row_in_tile),
+                   make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
+        }
+        sm100::tc_fence_before();
+        sm100::mbar_arrive(&tempty[acc]);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+        int* arrive = args.flags + 4 * tile;
+        int* depart = arrive + 1;
+        __threadfence();
+        __syncwarp();
+        bool ok = true;
+        if (lane == 0) {
+          atomicAdd(arrive, 1);
+          const uint64_t t0 = sm100::globaltimer();
+          for (uint32_t spin = 0; ld_acquire_gpu(arrive) < 4 * S; ++spin) {
+            if ((spin & 63u) == 63u && (sm100::globaltimer() - t0 > RT_WAIT_LIMIT_NS || *abort)) {
+              ok = false;
+              break;
+            }
+          }
+          if (!ok) *abort = 1;
+        }
+        __syncwarp();
+        if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
+        // rows [r0, r1) of the tile, all BN columns, summed over the S parts' slots (4 warps share the band)
+        const int r0 = BM * part / S, r1 = BM * (part + 1) / S, rows = r1 - r0;
+        const int etid = threadIdx.x - 64;  // 0..127 over the epilogue warps
+        for (int e = etid; e < rows * (BN / 4); e += 128) {
+          const int r = r0 + e % rows, cq = e / rows;
+          float4 acc4 = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int s2 = 0; s2 < S; ++s2) {
+            const float4 p4 = __ldcg(sk_slot(args.ws, tile * S + s2, BN, cq >> 3, cq & 7, r));
+            acc4.x += p4.x; acc4.y += p4.y; acc4.z += p4.z; acc4.w += p4.w;
+          }
+          const int grow = tm * BM + r, gcol = tn * BN + 4 * cq;
+          if (grow >= args.M || gcol >= args.N) continue;
+          const float vals[4] = {acc4.x, acc4.y, acc4.z, acc4.w};
+          if (EPI == EPI_BF16) {
+            __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(args.C) + (long)grow * args.ldc + gcol;
+            if (gcol + 4 <= args.N && (reinterpret_cast<uintptr_t>(o) & 7) == 0) {
+              __nv_bfloat162 a2 = __floats2bfloat162_rn(vals[0], vals[1]), b2 = __floats2bfloat162_rn(vals[2], vals[3]);
+              uint2 pk;
+              pk.x = *reinterpret_cast<uint32_t*>(&a2);
+              pk.y = *reinterpret_cast<uint32_t*>(&b2);
+              *reinterpret_cast<uint2*>(o) = pk;
+            } else {
+              for (int u = 0; u < 4 && gcol + u < args.N; ++u) o[u] = __float2bfloat16_rn(vals[u]);
+            }
+          } else {
+            float* o = reinterpret_cast<float*>(args.C) + (long)grow * args.ldc + gcol;
+            for (int u = 0; u < 4 && gcol + u < args.N; ++u) {
+              if (EPI == EPI_F32) o[u] = vals[u];
+              else o[u] += args.alpha * vals[u];
+            }
+          }
+        }
+        __syncwarp();
+        if (lane == 0 && atomicAdd(depart, 1) == 4 * S - 1) {  // last warp out: every wait has passed
+          *arrive = 0;
+          *depart = 0;
+        }
+        continue;
+      }
       // stream-K roles of this piece (uniform over the warp; each warp syncs on its own)
       const bool partial = C_::NB == 1 && args.sk && k1 < kblocks;          // ends mid-tile: publish fp32 partial
       const bool fixup = C_::NB == 1 && args.sk && k1 == kblocks && k0 > 0;  // final piece: add earlier partials
@@ -548,7 +638,7 @@ struct LossArgs {
 template <int BN, bool A_MN, bool B_MN, int EPI>
 cudaError_t launch(const void* A, long lda, const void* B0, const void* B1, long ldb, void* C, long ldc, int M,
                    int N, int K, float alpha, int* status, cudaStream_t stream, int splits = 1, bool sk = false,
-                   LossArgs loss = LossArgs()) {
+                   LossArgs loss = LossArgs(), int splitp = 0) {
   using C_ = Cfg<BN, A_MN, B_MN, EPI>;
   CUtensorMap ta, tb0, tb1;
   bool ok = A_MN ? make_tmap(&ta, A, M, K, lda * 2, 64, BK) : make_tmap(&ta, A, K, M, lda * 2, BK, BM);
@@ -565,12 +655,24 @@ cudaError_t launch(const void* A, long lda, const void* B0, const void* B1, long
   args.splits = splits;
   args.kchunk = ((K + BK - 1) / BK + splits - 1) / splits;
   const int total = args.tiles_m * args.tiles_n * splits;
-  args.sk = 0; args.q = 0; args.rem = 0; args.ws = nullptr; args.flags = nullptr;
+  args.sk = 0; args.q = 0; args.rem = 0; args.ws = nullptr; args.flags = nullptr; args.splitp = 0;
   args.target = static_cast<const __nv_bfloat16*>(loss.target);
   args.rowsum = loss.rowsum;
   args.eps = loss.eps;
   int grid = total < num_sms_cached() ? total : num_sms_cached();
-  if (sk && C_::NB == 1 && splits == 1 && EPI != EPI_ATOMIC_T) {
+  if (splitp > 1 && C_::NB == 1 && splits == 1 && EPI != EPI_ATOMIC_T && EPI != EPI_NMSE) {
+    const int tiles = args.tiles_m * args.tiles_n;
+    const int kb = (K + BK - 1) / BK;
+    int S = splitp;
+    while (S > 1 && (tiles * S > num_sms_cached() || kb < 2 * S)) --S;  // co-resident CTAs, >= 2 k-blocks each
+    SkWorkspace* w = S > 1 && 4L * tiles <= SK_MAX_FLAGS ? sk_workspace(stream) : nullptr;
+    if (w) {
+      grid = tiles * S;
+      args.splitp = S;
+      args.ws = w->ws;
+      args.flags = w->flags;
+    }
+  } else if (sk && C_::NB == 1 && splits == 1 && EPI != EPI_ATOMIC_T) {
     const long iters = (long)args.tiles_m * args.tiles_n * ((K + BK - 1) / BK);
     SkWorkspace* w = 4L * args.tiles_m * args.tiles_n <= SK_MAX_FLAGS && iters >= num_sms_cached() && iters < (1L << 30)
                          ? sk_workspace(stream) : nullptr;
@@ -617,13 +719,16 @@ int pick_bn(int M, int N, bool swiglu, bool b_mn) {
 
 // Tile choice: width bn, plus SK_FLAG for the stream-K schedule.
 constexpr int SK_FLAG = 1 << 16;
+constexpr int SP_SHIFT = 20;  // choice bits 20..27: parallel split-K factor S (0 = off)
 
 template <bool A_MN, bool B_MN, int EPI>
 cudaError_t dispatch_bn(int choice, const void* A, long lda, const void* B0, const void* B1, long ldb, void* C,
                         long ldc, int M, int N, int K, float alpha, int* status, cudaStream_t s) {
   const int bn = choice & (SK_FLAG - 1);
   const bool sk = (choice & SK_FLAG) != 0;
-#define RT_L(W) return launch<W, A_MN, B_MN, EPI>(A, lda, B0, B1, ldb, C, ldc, M, N, K, alpha, status, s, 1, sk)
+  const int sp = (choice >> SP_SHIFT) & 255;
+#define RT_L(W) \
+  return launch<W, A_MN, B_MN, EPI>(A, lda, B0, B1, ldb, C, ldc, M, N, K, alpha, status, s, 1, sk, LossArgs(), sp)
   if (bn == 256) RT_L(256);
   if (bn == 192) RT_L(192);
   if (bn == 128) RT_L(128);
@@ -663,13 +768,15 @@ int measured_bn(const TileKey& key, int M, int K, const void* A, long lda, const
     std::lock_guard<std::mutex> lock(tile_mutex());
     auto it = tile_cache().find(key);
     if (it != tile_cache().end()) return it->second;
-    // A shorter chunk of a measured GEMM (same N and layouts, fewer rows or a shallower K): reuse the choice of
-    // the nearest larger measured bucket instead of timing again in the middle of training.
+    // A shorter chunk of a measured GEMM: same N and layouts, fewer token rows (K-major A: M is the token count)
+    // or a shallower K (MN-major A, weight gradients: K is the token count), at most 8x smaller. Reuse the choice
+    // of the nearest larger measured bucket instead of timing again in the middle of training.
     int best = -1;
     long best_size = 0;
     for (const auto& [k, choice] : tile_cache()) {
       if (k.N != key.N || k.a_mn != key.a_mn || k.b_mn != key.b_mn) continue;
-      const bool rows = k.K == key.K && k.M > key.M, depth = k.M == key.M && k.K > key.K;
+      const bool rows = !key.a_mn && k.K == key.K && k.M > key.M && k.M <= 8 * key.M;
+      const bool depth = key.a_mn && k.M == key.M && k.K > key.K && k.K <= 8 * key.K;
       const long size = (long)k.M * k.K;
       if ((rows || depth) && (best < 0 || size < best_size)) {
         best = choice;
@@ -695,26 +802,45 @@ int measured_bn(const TileKey& key, int M, int K, const void* A, long lda, const
   int best = guess;
   float best_ms = 1e30f;
   const long kblocks = (key.K + BK - 1) / BK;
-  for (int choice : {256, 224, 192, 160, 128, 256 | SK_FLAG, 224 | SK_FLAG, 192 | SK_FLAG, 128 | SK_FLAG}) {
+  std::vector<int> choices = {256, 224, 192, 160, 128, 64, 256 | SK_FLAG, 224 | SK_FLAG, 192 | SK_FLAG, 128 | SK_FLAG};
+  {  // parallel split-K where the tiles fill under half of the SMs and K is deep
+    const int sms = num_sms_cached();
+    for (int bn : {64, 128, 192, 256}) {
+      const long tiles = (long)((key.M + BM - 1) / BM) * ((key.N + bn - 1) / bn);
+      if (tiles * 2 > sms || (key.N < bn / 2 && bn != 64) || (key.b_mn && bn % 64)) continue;
+      const long smax = std::min<long>({sms / tiles, kblocks / 2, 255});
+      for (long S : {smax, smax / 2})
+        if (S >= 2) choices.push_back(bn | (int)(S << SP_SHIFT));
+    }
+  }
+  for (int choice : choices) {
     const int bn = choice & (SK_FLAG - 1);
     if (key.b_mn && bn % 64) continue;
-    if (key.N < bn / 2) continue;
+    if (key.N < bn / 2 && bn != 64) continue;
     if (choice & SK_FLAG) {  // stream-K only where the whole-tile schedule leaves a wave partly idle
       const long tiles = (long)((key.M + BM - 1) / BM) * ((key.N + bn - 1) / bn);
       const int sms = num_sms_cached();
       if (tiles % sms == 0 || tiles * kblocks < 2L * sms || kblocks < 8) continue;
     }
+    // one warm-up launch, then the best of two batches of four back-to-back launches (short kernels: the
+    // batch amortises the event and launch jitter that dominates a single 10-20 us launch)
     float ms = 1e30f;
-    for (int rep = 0; rep < 4; ++rep) {
+    bool failed = gemm_with_bn(choice, A, lda, key.a_mn, B, ldb, key.b_mn, C, ldc, M, key.N, K, epi, alpha, status,
+                               stream) != cudaSuccess;
+    for (int rep = 0; rep < 2 && !failed; ++rep) {
       cudaEventRecord(e0, stream);
-      if (gemm_with_bn(choice, A, lda, key.a_mn, B, ldb, key.b_mn, C, ldc, M, key.N, K, epi, alpha, status,
-                       stream) != cudaSuccess)
-        break;
+      for (int l = 0; l < 4 && !failed; ++l)
+        failed = gemm_with_bn(choice, A, lda, key.a_mn, B, ldb, key.b_mn, C, ldc, M, key.N, K, epi, alpha, status,
+                              stream) != cudaSuccess;
       cudaEventRecord(e1, stream);
-      if (cudaEventSynchronize(e1) != cudaSuccess) break;
+      if (failed || cudaEventSynchronize(e1) != cudaSuccess) break;
       float t = 0.f;
       cudaEventElapsedTime(&t, e0, e1);
-      ms = rep ? (t < ms ? t : ms) : 1e30f;  // first run warms up
+      ms = std::min(ms, t / 4);
+    }
+    if (failed) {
+      cudaGetLastError();  // a candidate the shape cannot take (e.g. alignment): skip it
+      continue;
     }
     // the estimate wins unless a candidate is more than 3% faster (single-launch timings are noisy)
     const float score = choice == guess ? 0.97f * ms : ms;

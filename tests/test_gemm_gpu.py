@@ -135,3 +135,24 @@ def test_fused_loss_epilogue_matches_fp32(M, N, K, tuned):
     dpred2 = native().gemm_nmse(x, w, target, stats2, eps)
     assert torch.equal(dpred, dpred2)
     torch.testing.assert_close(stats2, stats, rtol=1e-5, atol=0)  # row sums gather tiles with float atomics
+
+
+SP = 20  # tile choice bits 20..27: parallel split-K factor
+
+
+@cuda
+@pytest.mark.parametrize("M,N,K,tile", [(1024, 192, 5120, 64 | 16 << SP),    # LoRA down: 16 tiles x 9 parts
+                                        (1024, 352, 5120, 128 | 8 << SP),    # 24 tiles x 6 parts (clamped)
+                                        (300, 96, 1000, 64 | 12 << SP),      # ragged M, N, K
+                                        (1024, 1024, 5120, 256 | 4 << SP)])
+def test_parallel_split_k_matches_fp32(M, N, K, tile):
+    A, B = _bf(M, K, seed=21), _bf(N, K, seed=22)
+    ref = A.float() @ B.float().t()
+    for rep in range(2):  # the second launch checks that the tile counters were reset
+        _check(native().gemm(A, False, B, False, 0, 1.0, None, tile), ref)
+    _check(native().gemm(A, False, B, False, 1, 1.0, None, tile), ref, 1e-3)
+    dy, x = _bf(1024, 192, seed=23), _bf(1024, 640, seed=24)   # weight-gradient form, accumulate epilogue
+    acc = torch.randn(192, 640, device="cuda")
+    want = acc + 0.5 * (dy.float().t() @ x.float())
+    native().gemm(dy, True, x, True, 2, 0.5, acc, 64 | 8 << SP)
+    _check(acc, want, 1e-3)

@@ -11,7 +11,8 @@ cuda = pytest.mark.skipif(not torch.cuda.is_available(), reason="CUDA unavailabl
 
 
 @cuda
-def test_exchange_wait_for_absent_peer_times_out_with_status():
+@pytest.mark.parametrize("mode", [1, 0])  # three-kernel path; fused update/pull kernel
+def test_exchange_wait_for_absent_peer_times_out_with_status(mode):
     ext = native()
     n, dev = 1024, torch.device("cuda", 0)
     mine = {k: torch.zeros(n, device=dev) for k in ("g", "p", "m", "v")}
@@ -22,7 +23,7 @@ def test_exchange_wait_for_absent_peer_times_out_with_status():
     ext.exchange_update([mine["g"].data_ptr(), ghost["g"].data_ptr()], [mine["p"].data_ptr(), ghost["p"].data_ptr()],
                         [shadow[0].data_ptr(), shadow[1].data_ptr()], [sig[0].data_ptr(), sig[1].data_ptr()],
                         0, 2, n, mine["m"], mine["v"], stats, report, 1e-3, 0.9, 0.999, 1e-8, 0.0, 1.0, 1, n,
-                        1, 0.3, 4)
+                        1, 0.3, 4, mode)
     torch.cuda.synchronize()  # returns after the three bounded waits (about 1 s), the context stays usable
     words = sig[0][24:28].cpu().tolist()
     assert words[0] == 1 and words[3] == 1  # status "gradients ready" missing from rank 1
