@@ -43,12 +43,12 @@ cudaError_t rt_gemm_swiglu_bf16(const void* A, long lda, const void* Bg, const v
 // Teacher-block kernels (bf16 activations, fp32 parameters).
 cudaError_t rt_rmsnorm_1p(const void* x, const void* h, const float* w, void* sum_out, void* out, long rows, int C,
                           float eps, cudaStream_t stream);
-cudaError_t rt_conv1d_silu(const void* x, const void* state, const float* weight, void* y, void* new_state, int B,
-                           int T, int C, int K, cudaStream_t stream);
-cudaError_t rt_gated_rmsnorm(const void* x, const void* z, const float* w, void* out, long rows, int D, float eps,
-                             cudaStream_t stream);
-cudaError_t rt_norm_rope(const void* src, long src_stride, const float* w, const float* inv_freq, void* dst, int B,
-                         int T, int heads, long dst_batch_stride, int pos0, int D, int rot, float eps,
+cudaError_t rt_conv1d_silu(const void* x, long xs, const void* state, const float* weight, void* y, void* new_state,
+                           int B, int T, int C, int K, cudaStream_t stream);
+cudaError_t rt_gated_rmsnorm(const void* x, const void* z, const float* w, void* out, long rows, int D, int heads,
+                             long zs, float eps, cudaStream_t stream);
+cudaError_t rt_norm_rope(const void* src, long src_stride, long head_stride, const float* w, const float* inv_freq,
+                         void* dst, int B, int T, int heads, long dst_batch_stride, int pos0, int D, int rot, float eps,
                          cudaStream_t stream);
 cudaError_t rt_copy_rows(const void* src, long src_stride, void* dst, int B, int T, long dst_batch_stride, int width,
                          cudaStream_t stream);

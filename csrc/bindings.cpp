@@ -203,29 +203,37 @@ std::vector<at::Tensor> add_rmsnorm_1p(at::Tensor x, at::Tensor h, at::Tensor w,
   return {sum, out};
 }
 
+// x: [B, T, C] bf16 with unit channel stride and any token stride (a column slice of a wider projection output).
 std::vector<at::Tensor> conv1d_silu(at::Tensor x, at::Tensor state, at::Tensor weight) {
-  check_bf16(x, "x");
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 3 && x.stride(2) == 1,
+              "x must be [B, T, C] bf16 rows (unit channel stride)");
+  const long xs = x.size(1) > 1 ? x.stride(1) : x.stride(0);  // token row stride (a size-1 dim has any stride)
+  TORCH_CHECK(x.size(0) == 1 || x.stride(0) == x.size(1) * xs, "x rows must be evenly spaced over batch and time");
   check_bf16(state, "state");
   c10::cuda::CUDAGuard guard(x.device());
   const int B = x.size(0), T = x.size(1), C = x.size(2), K = weight.size(-1);
   TORCH_CHECK(state.size(0) == B && state.size(1) == K - 1 && state.size(2) == C, "conv state must be [B, K-1, C]");
   auto wf = f32(weight.reshape({C, K}));
-  auto y = at::empty_like(x), ns = at::empty_like(state);
-  check_cuda(rt_conv1d_silu(x.data_ptr(), state.data_ptr(), wf.data_ptr<float>(), y.data_ptr(), ns.data_ptr(), B, T, C,
-                            K, stream_of(x)),
+  auto y = at::empty({B, T, C}, x.options()), ns = at::empty_like(state);
+  check_cuda(rt_conv1d_silu(x.data_ptr(), xs, state.data_ptr(), wf.data_ptr<float>(), y.data_ptr(),
+                            ns.data_ptr(), B, T, C, K, stream_of(x)),
              "conv1d_silu");
   return {y, ns};
 }
 
+// x: contiguous [..., D] rows; z: the same rows as [tokens, heads * D] with unit inner stride and any token stride.
 at::Tensor gated_rmsnorm(at::Tensor x, at::Tensor z, at::Tensor w, double eps) {
   check_bf16(x, "x");
-  check_bf16(z, "z");
   c10::cuda::CUDAGuard guard(x.device());
   const long D = w.numel(), rows = x.numel() / D;
+  TORCH_CHECK(z.is_cuda() && z.scalar_type() == at::kBFloat16 && z.stride(-1) == 1, "z must be bf16 rows");
+  const at::Tensor z2 = z.dim() == 2 ? z : z.contiguous().view({-1, z.size(-1)});
+  TORCH_CHECK(z2.size(1) % D == 0 && z2.size(0) * (z2.size(1) / D) == rows, "z rows do not match x");
+  const int heads = z2.size(1) / D;
   auto wf = f32(w);
   auto out = at::empty_like(x);
-  check_cuda(rt_gated_rmsnorm(x.data_ptr(), z.data_ptr(), wf.data_ptr<float>(), out.data_ptr(), rows, D, eps,
-                              stream_of(x)),
+  check_cuda(rt_gated_rmsnorm(x.data_ptr(), z2.data_ptr(), wf.data_ptr<float>(), out.data_ptr(), rows, D, heads,
+                              z2.stride(0), eps, stream_of(x)),
              "gated_rmsnorm");
   return out;
 }
@@ -243,7 +251,8 @@ void norm_rope_(at::Tensor src, int64_t heads, at::Tensor w, at::Tensor inv_freq
   const int T = src.size(0) / B;
   TORCH_CHECK(dst_pos0 + T <= dst.size(1), "cache too small");
   auto wf = f32(w), fq = f32(inv_freq);
-  check_cuda(rt_norm_rope(src.data_ptr(), src.stride(0), wf.data_ptr<float>(), fq.data_ptr<float>(),
+  TORCH_CHECK(src.size(1) % heads == 0, "src width must be heads x head stride");
+  check_cuda(rt_norm_rope(src.data_ptr(), src.stride(0), src.size(1) / heads, wf.data_ptr<float>(), fq.data_ptr<float>(),
                           dst.data_ptr<at::BFloat16>() + dst_pos0 * heads * D, B, T, heads, dst.stride(0),
                           (int)rope_pos0, D, rot, eps, stream_of(src)),
              "norm_rope");
@@ -472,10 +481,11 @@ at::Tensor flash_attention(at::Tensor q, at::Tensor keys, at::Tensor values, at:
   TORCH_CHECK(qg.is_cuda() && qg.scalar_type() == at::kBFloat16 && qg.stride(-1) == 1, "gate must be bf16 rows");
   c10::cuda::CUDAGuard guard(q.device());
   const int B = q.size(0), T = q.size(1), Hq = q.size(2), Hkv = keys.size(2), cap = keys.size(1);
-  TORCH_CHECK(qg.numel() == (long)B * T * Hq * 512, "gate buffer must be [B*T, Hq*512]");
+  TORCH_CHECK(qg.dim() == 2 && qg.size(0) == (long)B * T && qg.size(1) >= (long)Hq * 512,
+              "gate rows must be [B*T, >= Hq*512] (per head [q | gate])");
   auto out = at::empty_like(q);
   check_cuda(rt_flash_attention_fwd(q.data_ptr(), keys.data_ptr(), values.data_ptr(),
-                                    static_cast<const at::BFloat16*>(qg.data_ptr()) + 256, (long)Hq * 512, 512,
+                                    static_cast<const at::BFloat16*>(qg.data_ptr()) + 256, (long)qg.stride(0), 512,
                                     out.data_ptr(), B, T, Hq, Hkv, (int)offset, cap, nullptr, stream_of(q)),
              "flash_attention");
   return out;

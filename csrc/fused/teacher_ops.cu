@@ -85,7 +85,7 @@ __global__ void __launch_bounds__(128) rmsnorm_vec_kernel(const uint4* __restric
 // x: [B, T, C] bf16; state: [B, K-1, C] bf16 (oldest first); weight: [C, K] fp32 (tap K-1 = newest).
 // Each thread owns one channel and a segment of SEG time steps.
 constexpr int SEG = 64;
-__global__ void conv1d_silu_kernel(const bf16* __restrict__ x, const bf16* __restrict__ state,
+__global__ void conv1d_silu_kernel(const bf16* __restrict__ x, long xs, const bf16* __restrict__ state,
                                    const float* __restrict__ weight, bf16* __restrict__ y, bf16* __restrict__ new_state,
                                    int T, int C, int K) {
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
@@ -98,11 +98,11 @@ __global__ void conv1d_silu_kernel(const bf16* __restrict__ x, const bf16* __res
   // Window holds inputs t0-(K-1) .. t0-1.
   for (int j = 0; j < K - 1; ++j) {
     const int t = t0 - (K - 1) + j;
-    win[j] = t >= 0 ? rt::to_f(x[((long)b * T + t) * C + c]) : rt::to_f(state[((long)b * (K - 1) + (t + K - 1)) * C + c]);
+    win[j] = t >= 0 ? rt::to_f(x[((long)b * T + t) * xs + c]) : rt::to_f(state[((long)b * (K - 1) + (t + K - 1)) * C + c]);
   }
   const int t1 = min(T, t0 + SEG);
   for (int t = t0; t < t1; ++t) {
-    const float cur = rt::to_f(x[((long)b * T + t) * C + c]);
+    const float cur = rt::to_f(x[((long)b * T + t) * xs + c]);
     float acc = cur * wt[K - 1];
     for (int j = 0; j < K - 1; ++j) acc += win[j] * wt[j];
     for (int j = 0; j + 1 < K - 1; ++j) win[j] = win[j + 1];
@@ -112,7 +112,7 @@ __global__ void conv1d_silu_kernel(const bf16* __restrict__ x, const bf16* __res
   if (t1 == T) {  // the segment holding the last K-1 inputs writes the carried window
     for (int j = 0; j < K - 1; ++j) {
       const int t = T - (K - 1) + j;
-      const float v = t >= 0 ? rt::to_f(x[((long)b * T + t) * C + c])
+      const float v = t >= 0 ? rt::to_f(x[((long)b * T + t) * xs + c])
                              : rt::to_f(state[((long)b * (K - 1) + (t + K - 1)) * C + c]);
       new_state[((long)b * (K - 1) + j) * C + c] = __float2bfloat16_rn(v);
     }
@@ -124,7 +124,8 @@ __global__ void conv1d_silu_kernel(const bf16* __restrict__ x, const bf16* __res
 // thread), then the taps run from registers; K is a template parameter so nothing spills.
 constexpr int CSEG = 16;
 template <int K>
-__global__ void __launch_bounds__(128) conv1d_silu_vec_kernel(const uint4* __restrict__ x, const uint4* __restrict__ state,
+__global__ void __launch_bounds__(128) conv1d_silu_vec_kernel(const uint4* __restrict__ x, long xs8,
+                                                              const uint4* __restrict__ state,
                                                               const float* __restrict__ weight, uint4* __restrict__ y,
                                                               uint4* __restrict__ new_state, int T, int C8) {
   constexpr int H = K - 1;
@@ -136,7 +137,7 @@ __global__ void __launch_bounds__(128) conv1d_silu_vec_kernel(const uint4* __res
   for (int j = 0; j < H + CSEG; ++j) {
     const int t = t0 - H + j;
     raw[j] = t < 0 ? state[((long)b * H + (t + H)) * C8 + c]
-                   : (t < T ? x[((long)b * T + t) * C8 + c] : make_uint4(0u, 0u, 0u, 0u));
+                   : (t < T ? x[((long)b * T + t) * xs8 + c] : make_uint4(0u, 0u, 0u, 0u));
   }
   float wt[K][8];
 #pragma unroll
@@ -174,10 +175,11 @@ __global__ void __launch_bounds__(128) conv1d_silu_vec_kernel(const uint4* __res
 // ---------------------------------------------------------------- gated RMSNorm (GDN output)
 // rows of D (<= 256) values; one warp per row.
 __global__ void gated_rmsnorm_kernel(const bf16* __restrict__ x, const bf16* __restrict__ z, const float* __restrict__ w,
-                                     bf16* __restrict__ out, long rows, int D, float eps) {
+                                     bf16* __restrict__ out, long rows, int D, int heads, long zs, float eps) {
   const long row = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
+  const bf16* zr = z + (row / heads) * zs + (row % heads) * D;  // z rows: one token of `heads` heads, stride zs
   float v[8];
   float acc = 0.f;
   for (int j = 0; j < 8; ++j) {
@@ -192,7 +194,7 @@ __global__ void gated_rmsnorm_kernel(const bf16* __restrict__ x, const bf16* __r
     if (c < D) {
       const float n = __bfloat162float(__float2bfloat16_rn(v[j] * inv));
       const float p = __bfloat162float(__float2bfloat16_rn(w[c] * n));
-      out[row * D + c] = __float2bfloat16_rn(p * rt::siluf_(rt::to_f(z[row * D + c])));
+      out[row * D + c] = __float2bfloat16_rn(p * rt::siluf_(rt::to_f(zr[c])));
     }
   }
 }
@@ -200,9 +202,10 @@ __global__ void gated_rmsnorm_kernel(const bf16* __restrict__ x, const bf16* __r
 // ---------------------------------------------------------------- q/k norm + RoPE + cache write
 // One warp per (token, head) row of D <= 256 values. src rows have stride `src_stride` elements;
 // rotate_half RoPE on the first `rot` dims with angle pos * inv_freq[i mod rot/2].
-__global__ void norm_rope_kernel(const bf16* __restrict__ src, long src_stride, const float* __restrict__ w,
-                                 const float* __restrict__ inv_freq, bf16* __restrict__ dst, int heads, int T,
-                                 long dst_batch_stride, int pos0, int D, int rot, float eps, long rows) {
+__global__ void norm_rope_kernel(const bf16* __restrict__ src, long src_stride, long head_stride,
+                                 const float* __restrict__ w, const float* __restrict__ inv_freq, bf16* __restrict__ dst,
+                                 int heads, int T, long dst_batch_stride, int pos0, int D, int rot, float eps,
+                                 long rows) {
   extern __shared__ float buf[];
   const int wib = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long row = (long)blockIdx.x * (blockDim.x >> 5) + wib;
@@ -212,7 +215,7 @@ __global__ void norm_rope_kernel(const bf16* __restrict__ src, long src_stride, 
   const long bt = row / heads;
   const int t = bt % T;
   const long b = bt / T;
-  const bf16* in = src + bt * src_stride + (long)head * (src_stride / heads);
+  const bf16* in = src + bt * src_stride + (long)head * head_stride;
   float acc = 0.f;
   for (int c = lane; c < D; c += 32) {
     const float v = rt::to_f(in[c]);
@@ -286,16 +289,16 @@ extern "C" cudaError_t rt_rmsnorm_1p(const void* x, const void* h, const float* 
   return cudaGetLastError();
 }
 
-extern "C" cudaError_t rt_conv1d_silu(const void* x, const void* state, const float* weight, void* y, void* new_state,
-                                      int B, int T, int C, int K, cudaStream_t stream) {
-  if (K < 1 || K > 8) return cudaErrorInvalidValue;
-  if (C % 8 == 0 && (K == 4 || K == 2 || K == 3) &&
+extern "C" cudaError_t rt_conv1d_silu(const void* x, long xs, const void* state, const float* weight, void* y,
+                                      void* new_state, int B, int T, int C, int K, cudaStream_t stream) {
+  if (K < 1 || K > 8 || xs < C) return cudaErrorInvalidValue;
+  if (C % 8 == 0 && xs % 8 == 0 && (K == 4 || K == 2 || K == 3) &&
       ((uintptr_t)x | (uintptr_t)state | (uintptr_t)y | (uintptr_t)new_state) % 16 == 0) {
     const int C8 = C / 8;
     const dim3 g((C8 + 127) / 128, (T + CSEG - 1) / CSEG, B);
     auto go = [&](auto k) {
       conv1d_silu_vec_kernel<decltype(k)::value><<<g, 128, 0, stream>>>(
-          (const uint4*)x, (const uint4*)state, weight, (uint4*)y, (uint4*)new_state, T, C8);
+          (const uint4*)x, xs / 8, (const uint4*)state, weight, (uint4*)y, (uint4*)new_state, T, C8);
     };
     if (K == 4) go(std::integral_constant<int, 4>{});
     else if (K == 3) go(std::integral_constant<int, 3>{});
@@ -303,28 +306,29 @@ extern "C" cudaError_t rt_conv1d_silu(const void* x, const void* state, const fl
     return cudaGetLastError();
   }
   dim3 grid((C + 127) / 128, (T + SEG - 1) / SEG, B);
-  conv1d_silu_kernel<<<grid, 128, 0, stream>>>((const bf16*)x, (const bf16*)state, weight, (bf16*)y, (bf16*)new_state,
-                                               T, C, K);
+  conv1d_silu_kernel<<<grid, 128, 0, stream>>>((const bf16*)x, xs, (const bf16*)state, weight, (bf16*)y,
+                                               (bf16*)new_state, T, C, K);
   return cudaGetLastError();
 }
 
 extern "C" cudaError_t rt_gated_rmsnorm(const void* x, const void* z, const float* w, void* out, long rows, int D,
-                                        float eps, cudaStream_t stream) {
-  if (D > 256) return cudaErrorInvalidValue;
+                                        int heads, long zs, float eps, cudaStream_t stream) {
+  if (D > 256 || heads < 1) return cudaErrorInvalidValue;
   const int warps = 8;
   gated_rmsnorm_kernel<<<(rows + warps - 1) / warps, warps * 32, 0, stream>>>((const bf16*)x, (const bf16*)z, w,
-                                                                               (bf16*)out, rows, D, eps);
+                                                                               (bf16*)out, rows, D, heads, zs, eps);
   return cudaGetLastError();
 }
 
-extern "C" cudaError_t rt_norm_rope(const void* src, long src_stride, const float* w, const float* inv_freq, void* dst,
-                                    int B, int T, int heads, long dst_batch_stride, int pos0, int D, int rot, float eps,
-                                    cudaStream_t stream) {
+extern "C" cudaError_t rt_norm_rope(const void* src, long src_stride, long head_stride, const float* w,
+                                    const float* inv_freq, void* dst, int B, int T, int heads, long dst_batch_stride,
+                                    int pos0, int D, int rot, float eps, cudaStream_t stream) {
   if (D > 256 || (rot & 1)) return cudaErrorInvalidValue;
   const long rows = (long)B * T * heads;
   const int warps = 4;
   norm_rope_kernel<<<(rows + warps - 1) / warps, warps * 32, warps * D * sizeof(float), stream>>>(
-      (const bf16*)src, src_stride, w, inv_freq, (bf16*)dst, heads, T, dst_batch_stride, pos0, D, rot, eps, rows);
+      (const bf16*)src, src_stride, head_stride, w, inv_freq, (bf16*)dst, heads, T, dst_batch_stride, pos0, D, rot, eps,
+      rows);
   return cudaGetLastError();
 }
 

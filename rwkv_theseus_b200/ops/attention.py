@@ -9,6 +9,7 @@ import torch
 from torch.nn import functional as F
 
 from . import f32, native
+from .gdn import fused_weight
 from .gemm import linear
 
 
@@ -49,9 +50,11 @@ def attention_block(module, x, rope, state):
     inv_freq, pos0 = rope[2], rope[3]
     rot = cfg.rotary_dim
     x2 = x.reshape(B * T, C)
-    qg = linear(x2, module.q_proj.weight)                   # [BT, Hq * 2D]: per head [q | gate]
-    k = linear(x2, module.k_proj.weight)
-    v = linear(x2, module.v_proj.weight)
+    proj = linear(x2, fused_weight(module, ("q_proj", "k_proj", "v_proj"), "_qkv_weight"))  # one GEMM: q|g, k, v
+    nq, nk = module.q_proj.weight.shape[0], module.k_proj.weight.shape[0]
+    qg = proj[:, :nq]                                       # [BT, Hq * 2D]: per head [q | gate]
+    k = proj[:, nq:nq + nk]
+    v = proj[:, nq + nk:]
     q = torch.empty(B, T, Hq, D, device=x.device, dtype=torch.bfloat16)
     native().norm_rope_(qg, Hq, f32(module.q_norm.weight), f32(inv_freq), q, pos0, 0, rot, module.q_norm.eps)
     if state is None:
