@@ -16,6 +16,8 @@
 // Padded steps past T get beta = 0 and g = 0, so they add nothing.
 // Reference semantics: HF Qwen3_5GatedDeltaNet chunk rule (torch_chunk_gated_delta_rule), as invoked from the
 // reference's teacher adapter (theseus/hf_model.py:38-52).
+#include <cstdlib>
+
 #include "../common/common.cuh"
 #include "../common/sm100.cuh"
 
@@ -622,6 +624,199 @@ gdn_out_tc_kernel(const float* __restrict__ qn, const float* __restrict__ kn, co
   }
 }
 
+// ---------------------------------------------------------------- 2 (D = 128): state pass on tcgen05
+// Same recurrence as gdn_state_kernel, one CTA (128 threads, thread i = value row i = TMEM lane i) per head. The
+// fp32 state S[i][j] lives in TMEM columns [0, 128) as the accumulator of the chunk's rank-64 update, so it sums in
+// fp32; only the products take tf32 operands. Per chunk:
+//   1. S (TMEM) -> registers -> chunk-start state S0out and the K-major operand tile A1 = S; TMEM <- e^{Lambda_L} S;
+//   2. D1 (TMEM cols [128, 192)) = A1 W^T             (M = 128 i, N = 64 t, K = 128 j, 16 tf32 MMAs);
+//   3. Vt[t][i] = U0[t][i] + D1[i][t] (to U), A2[i][t] = Vt[t][i] e^{Lambda_L - Lambda_t};
+//   4. S += A2 K                                      (M = 128 i, N = 128 j, K = 64 t, 8 tf32 MMAs).
+// Operand tiles are 128-byte-swizzled K-major (16-byte chunk c of row r at c ^ (r & 7)); W, U0 and Lambda of the
+// next chunk stream in with cp.async during step 4; K is transposed to [j][t] by the threads. Waits are bounded.
+namespace tcs {
+constexpr int A1_OFF = 0;                    // S: 128 rows x 128 fp32 (4 atoms of 16 KB)
+constexpr int B1_OFF = A1_OFF + 64 * 1024;   // W: 64 rows x 128 fp32 (4 atoms of 8 KB)
+constexpr int A2_OFF = B1_OFF + 32 * 1024;   // Vt^T scaled: 128 rows x 64 fp32 (2 atoms of 16 KB)
+constexpr int B2_OFF = A2_OFF + 32 * 1024;   // K^T: 128 rows x 64 fp32 (2 atoms of 16 KB)
+constexpr int U0_OFF = B2_OFF + 32 * 1024;   // U0: [64 t][128 i] fp32, natural layout
+constexpr int MISC_OFF = U0_OFF + 32 * 1024; // lam[64], fac[64], barrier, TMEM slot
+constexpr int BYTES = MISC_OFF + 1024 + 1024 /*align*/;
+
+// 16-byte chunk q (4 fp32) of row r in a K-major SW128 tile of `rows` rows
+RT_DEVICE uint32_t chunk_off(int rows, int r, int q) {
+  return (uint32_t)((q >> 3) * rows * 128 + r * 128 + (((q & 7) ^ (r & 7)) << 4));
+}
+}  // namespace tcs
+
+__global__ void __launch_bounds__(128)
+gdn_state_tc_kernel(const float* __restrict__ kn, const float* __restrict__ W, float* __restrict__ U,
+                    const float* __restrict__ lam_in, float* __restrict__ state, float* __restrict__ S0out, int T,
+                    int Tp, int Hk, int Hv, int* __restrict__ status) {
+  constexpr int D = 128;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* U0s = reinterpret_cast<float*>(sm + tcs::U0_OFF);
+  float* lam = reinterpret_cast<float*>(sm + tcs::MISC_OFF);
+  float* fac = lam + LC;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(fac + LC);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 1);
+  const int h = blockIdx.x, b = blockIdx.y, kh = h / (Hv / Hk);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int chunks = Tp / LC;
+  const long rowbase = ((long)b * Hv + h) * Tp;
+  float* st = state + ((long)b * Hv + h) * D * D;  // [j][i]
+  if (tid == 0) {
+    sm100::mbar_init(bar, 1);
+    sm100::fence_barrier_init();
+  }
+  if (warp == 0) {
+    sm100::tmem_alloc(tslot, 256);
+    sm100::tmem_relinquish();
+  }
+  auto prefetch = [&](int c) {  // W (swizzled B1), U0 (natural), lam of chunk c: one cp.async group
+    for (int e = tid; e < LC * 32; e += 128) {
+      const int t = e >> 5, q = e & 31;
+      rt::cp_async16(sm + tcs::B1_OFF + tcs::chunk_off(LC, t, q), W + (rowbase + c * LC + t) * D + 4 * q, true);
+      rt::cp_async16(U0s + t * D + 4 * q, U + (rowbase + c * LC + t) * D + 4 * q, true);
+    }
+    if (tid < LC / 4) rt::cp_async16(lam + 4 * tid, lam_in + rowbase + c * LC + 4 * tid, true);
+    rt::cp_async_commit();
+  };
+  prefetch(0);
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tm = *tslot;
+  const uint32_t trow = tm + ((uint32_t)(warp * 32) << 16);
+  {  // initial state: lane i, columns j
+#pragma unroll 1
+    for (int q = 0; q < 4; ++q) {
+      float v[32];
+#pragma unroll
+      for (int u = 0; u < 32; ++u) v[u] = st[(long)(32 * q + u) * D + tid];
+      sm100::tmem_st32(trow + 32 * q, v);
+    }
+    sm100::tmem_wait_st();
+  }
+  const uint32_t idesc1 = sm100::idesc_tf32(128, 64), idesc2 = sm100::idesc_tf32(128, 128);
+  const uint32_t a1 = sm100::smem_u32(sm + tcs::A1_OFF), b1 = sm100::smem_u32(sm + tcs::B1_OFF);
+  const uint32_t a2 = sm100::smem_u32(sm + tcs::A2_OFF), b2 = sm100::smem_u32(sm + tcs::B2_OFF);
+  uint32_t phase = 0;
+  bool ok = true;
+#pragma unroll 1
+  for (int c = 0; c < chunks && ok; ++c) {
+    // ---- 1. S -> S0out, A1; TMEM <- e^{Lambda_L} S
+    rt::cp_async_wait<0>();
+    __syncthreads();  // W, U0, lam of chunk c visible to every thread
+    if (tid < LC) fac[tid] = expf(lam[LC - 1] - lam[tid]);
+    const float eL = expf(lam[LC - 1]);
+    float* s0 = S0out + (((long)b * Hv + h) * chunks + c) * D * D + (long)tid * D;
+#pragma unroll 1
+    for (int q = 0; q < 4; ++q) {
+      float v[32];
+      sm100::tmem_ld32(trow + 32 * q, v);
+      sm100::tmem_wait_ld();
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float4 f = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+        *reinterpret_cast<float4*>(s0 + 32 * q + 4 * u) = f;
+        *reinterpret_cast<float4*>(sm + tcs::A1_OFF + tcs::chunk_off(128, tid, 8 * q + u)) = f;
+      }
+#pragma unroll
+      for (int u = 0; u < 32; ++u) v[u] *= eL;
+      sm100::tmem_st32(trow + 32 * q, v);
+    }
+    // K^T of chunk c (thread = key j): rows t < T, zero beyond
+    {
+      const int j = tid;
+#pragma unroll 1
+      for (int q = 0; q < LC / 4; ++q) {
+        float k4[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int tg = c * LC + 4 * q + u;
+          k4[u] = tg < T ? kn[(((long)b * T + tg) * Hk + kh) * D + j] : 0.f;
+        }
+        *reinterpret_cast<float4*>(sm + tcs::B2_OFF + tcs::chunk_off(128, j, q)) = make_float4(k4[0], k4[1], k4[2], k4[3]);
+      }
+    }
+    sm100::tmem_wait_st();
+    tc::fence_proxy_async();
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::tc_fence_after();
+    // ---- 2. D1 = A1 W^T
+    if (tid == 0) {
+#pragma unroll
+      for (int ks = 0; ks < D / 8; ++ks) {
+        const uint32_t ka = (ks >> 2) * (128 * 128) + (ks & 3) * 32, kb = (ks >> 2) * (LC * 128) + (ks & 3) * 32;
+        sm100::mma_tf32(tm + 128, sm100::smem_desc(a1 + ka, 16, 1024), sm100::smem_desc(b1 + kb, 16, 1024), idesc1,
+                        ks > 0);
+      }
+      sm100::mma_commit(bar);
+    }
+    ok = __syncthreads_and(sm100::mbar_wait_bounded(bar, phase) ? 1 : 0) != 0;  // uniform: every thread agrees
+    phase ^= 1;
+    sm100::tc_fence_after();
+    if (!ok) break;
+    // ---- 3. Vt = U0 + D1 (to U), A2 = Vt^T scaled
+    {
+      float d[64];
+      sm100::tmem_ld32(trow + 128, *reinterpret_cast<float(*)[32]>(d));
+      sm100::tmem_ld32(trow + 160, *reinterpret_cast<float(*)[32]>(d + 32));
+      sm100::tmem_wait_ld();
+      const int i = tid;
+#pragma unroll
+      for (int t = 0; t < LC; ++t) {
+        const float v = U0s[t * D + i] + d[t];
+        U[(rowbase + c * LC + t) * D + i] = v;
+        d[t] = v * fac[t];
+      }
+#pragma unroll
+      for (int q = 0; q < LC / 4; ++q)
+        *reinterpret_cast<float4*>(sm + tcs::A2_OFF + tcs::chunk_off(128, i, q)) =
+            make_float4(d[4 * q], d[4 * q + 1], d[4 * q + 2], d[4 * q + 3]);
+    }
+    tc::fence_proxy_async();
+    sm100::tc_fence_before();
+    __syncthreads();  // A2 complete; W, U0, lam, fac of chunk c no longer read
+    sm100::tc_fence_after();
+    if (c + 1 < chunks) prefetch(c + 1);
+    // ---- 4. S += A2 K
+    if (tid == 0) {
+#pragma unroll
+      for (int ks = 0; ks < LC / 8; ++ks) {
+        const uint32_t ko = (ks >> 2) * (128 * 128) + (ks & 3) * 32;
+        sm100::mma_tf32(tm, sm100::smem_desc(a2 + ko, 16, 1024), sm100::smem_desc(b2 + ko, 16, 1024), idesc2, 1);
+      }
+      sm100::mma_commit(bar);
+    }
+    ok = __syncthreads_and(sm100::mbar_wait_bounded(bar, phase) ? 1 : 0) != 0;
+    phase ^= 1;
+    sm100::tc_fence_after();
+  }
+  rt::cp_async_wait<0>();
+  if (ok) {  // final state, [j][i]
+#pragma unroll 1
+    for (int q = 0; q < 4; ++q) {
+      float v[32];
+      sm100::tmem_ld32(trow + 32 * q, v);
+      sm100::tmem_wait_ld();
+#pragma unroll
+      for (int u = 0; u < 32; ++u) st[(long)(32 * q + u) * D + tid] = v[u];
+    }
+  } else if (tid == 0 && status) {
+    atomicExch(status, 1);
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tm, 256);
+  }
+}
+
 // q/k normalisation: qn = q / |q| * D^-1/2, kn = k / |k| (eps 1e-6), fp32 rows [B, T, Hk, D]. grid (T, B).
 template <int D>
 __global__ void __launch_bounds__(128) gdn_norm_kernel(const bf16* __restrict__ qkv, long row_stride, int T, int Hk,
@@ -678,7 +873,17 @@ cudaError_t launch(const void* qkv, long row_stride, const void* a, const void* 
                                                              (const bf16*)bb, ab_stride, A_log, dt_bias, W, U, lam, T,
                                                              Tp, Hk, Hv);
   RT_CUDA_CHECK(cudaGetLastError());
-  gdn_state_kernel<D><<<dim3(D / VB, Hv, B), NT, s2, stream>>>(kn, W, U, lam, state, S0, T, Tp, Hk, Hv);
+  // tcgen05 state pass (head dim 128) when THESEUS_GDN_STATE_TC=1; the SIMT pass otherwise
+  static const bool state_tc = [] {
+    const char* e = getenv("THESEUS_GDN_STATE_TC");
+    return e && e[0] == '1';
+  }();
+  if (D == 128 && state_tc) {
+    RT_CUDA_CHECK(cudaFuncSetAttribute(gdn_state_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, tcs::BYTES));
+    gdn_state_tc_kernel<<<dim3(Hv, B), 128, tcs::BYTES, stream>>>(kn, W, U, lam, state, S0, T, Tp, Hk, Hv, nullptr);
+  } else {
+    gdn_state_kernel<D><<<dim3(D / VB, Hv, B), NT, s2, stream>>>(kn, W, U, lam, state, S0, T, Tp, Hk, Hv);
+  }
   RT_CUDA_CHECK(cudaGetLastError());
   if constexpr (D == 128) {
     RT_CUDA_CHECK(cudaFuncSetAttribute(gdn_out_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::BYTES));
