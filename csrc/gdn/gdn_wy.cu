@@ -633,7 +633,8 @@ gdn_out_tc_kernel(const float* __restrict__ qn, const float* __restrict__ kn, co
 //   3. Vt[t][i] = U0[t][i] + D1[i][t] (to U), A2[i][t] = Vt[t][i] e^{Lambda_L - Lambda_t};
 //   4. S += A2 K                                      (M = 128 i, N = 128 j, K = 64 t, 8 tf32 MMAs).
 // Operand tiles are 128-byte-swizzled K-major (16-byte chunk c of row r at c ^ (r & 7)); W, U0 and Lambda of the
-// next chunk stream in with cp.async during step 4; K is transposed to [j][t] by the threads. Waits are bounded.
+// next chunk stream in with cp.async during step 4; K is transposed to [j][t] by the threads from registers loaded
+// one chunk ahead (the loads are in flight during the MMAs). Waits are bounded.
 namespace tcs {
 constexpr int A1_OFF = 0;                    // S: 128 rows x 128 fp32 (4 atoms of 16 KB)
 constexpr int B1_OFF = A1_OFF + 64 * 1024;   // W: 64 rows x 128 fp32 (4 atoms of 8 KB)
@@ -704,6 +705,16 @@ gdn_state_tc_kernel(const float* __restrict__ kn, const float* __restrict__ W, f
   const uint32_t a2 = sm100::smem_u32(sm + tcs::A2_OFF), b2 = sm100::smem_u32(sm + tcs::B2_OFF);
   uint32_t phase = 0;
   bool ok = true;
+  // column j = tid of K for one chunk (rows t < T, zero beyond): 64 independent loads in flight
+  float kreg[LC];
+  auto load_k = [&](int c) {
+#pragma unroll
+    for (int t = 0; t < LC; ++t) {
+      const int tg = c * LC + t;
+      kreg[t] = tg < T ? __ldg(kn + (((long)b * T + tg) * Hk + kh) * D + tid) : 0.f;
+    }
+  };
+  load_k(0);
 #pragma unroll 1
   for (int c = 0; c < chunks && ok; ++c) {
     // ---- 1. S -> S0out, A1; TMEM <- e^{Lambda_L} S
@@ -727,20 +738,11 @@ gdn_state_tc_kernel(const float* __restrict__ kn, const float* __restrict__ W, f
       for (int u = 0; u < 32; ++u) v[u] *= eL;
       sm100::tmem_st32(trow + 32 * q, v);
     }
-    // K^T of chunk c (thread = key j): rows t < T, zero beyond
-    {
-      const int j = tid;
-#pragma unroll 1
-      for (int q = 0; q < LC / 4; ++q) {
-        float k4[4];
+    // K^T of chunk c (thread = key j), loaded into registers during the previous chunk
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int tg = c * LC + 4 * q + u;
-          k4[u] = tg < T ? kn[(((long)b * T + tg) * Hk + kh) * D + j] : 0.f;
-        }
-        *reinterpret_cast<float4*>(sm + tcs::B2_OFF + tcs::chunk_off(128, j, q)) = make_float4(k4[0], k4[1], k4[2], k4[3]);
-      }
-    }
+    for (int q = 0; q < LC / 4; ++q)
+      *reinterpret_cast<float4*>(sm + tcs::B2_OFF + tcs::chunk_off(128, tid, q)) =
+          make_float4(kreg[4 * q], kreg[4 * q + 1], kreg[4 * q + 2], kreg[4 * q + 3]);
     sm100::tmem_wait_st();
     tc::fence_proxy_async();
     sm100::tc_fence_before();
@@ -756,6 +758,7 @@ gdn_state_tc_kernel(const float* __restrict__ kn, const float* __restrict__ W, f
       }
       sm100::mma_commit(bar);
     }
+    if (c + 1 < chunks) load_k(c + 1);  // B2 was copied out of kreg above; these loads land during the MMAs
     ok = __syncthreads_and(sm100::mbar_wait_bounded(bar, phase) ? 1 : 0) != 0;  // uniform: every thread agrees
     phase ^= 1;
     sm100::tc_fence_after();
