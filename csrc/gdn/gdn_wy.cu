@@ -650,11 +650,13 @@ RT_DEVICE uint32_t chunk_off(int rows, int r, int q) {
 }
 }  // namespace tcs
 
-__global__ void __launch_bounds__(128)
+// 256 threads: two warpgroups address the same 128 TMEM lanes (thread i and i + 128 own value row i) and split
+// every per-row pass by columns (state columns j, steps t, K rows).
+__global__ void __launch_bounds__(256)
 gdn_state_tc_kernel(const float* __restrict__ kn, const float* __restrict__ W, float* __restrict__ U,
                     const float* __restrict__ lam_in, float* __restrict__ state, float* __restrict__ S0out, int T,
                     int Tp, int Hk, int Hv, int* __restrict__ status) {
-  constexpr int D = 128;
+  constexpr int D = 128, NTH = 256;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* U0s = reinterpret_cast<float*>(sm + tcs::U0_OFF);
@@ -664,6 +666,7 @@ gdn_state_tc_kernel(const float* __restrict__ kn, const float* __restrict__ W, f
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 1);
   const int h = blockIdx.x, b = blockIdx.y, kh = h / (Hv / Hk);
   const int tid = threadIdx.x, warp = tid >> 5;
+  const int row = tid & 127, half = tid >> 7;  // value row i (TMEM lane) and column half
   const int chunks = Tp / LC;
   const long rowbase = ((long)b * Hv + h) * Tp;
   float* st = state + ((long)b * Hv + h) * D * D;  // [j][i]
@@ -676,7 +679,7 @@ gdn_state_tc_kernel(const float* __restrict__ kn, const float* __restrict__ W, f
     sm100::tmem_relinquish();
   }
   auto prefetch = [&](int c) {  // W (swizzled B1), U0 (natural), lam of chunk c: one cp.async group
-    for (int e = tid; e < LC * 32; e += 128) {
+    for (int e = tid; e < LC * 32; e += NTH) {
       const int t = e >> 5, q = e & 31;
       rt::cp_async16(sm + tcs::B1_OFF + tcs::chunk_off(LC, t, q), W + (rowbase + c * LC + t) * D + 4 * q, true);
       rt::cp_async16(U0s + t * D + 4 * q, U + (rowbase + c * LC + t) * D + 4 * q, true);
@@ -689,13 +692,13 @@ gdn_state_tc_kernel(const float* __restrict__ kn, const float* __restrict__ W, f
   __syncthreads();
   sm100::tc_fence_after();
   const uint32_t tm = *tslot;
-  const uint32_t trow = tm + ((uint32_t)(warp * 32) << 16);
-  {  // initial state: lane i, columns j
+  const uint32_t trow = tm + ((uint32_t)((warp & 3) * 32) << 16);
+  {  // initial state: lane i, this half's columns j
 #pragma unroll 1
-    for (int q = 0; q < 4; ++q) {
+    for (int q = 2 * half; q < 2 * half + 2; ++q) {
       float v[32];
 #pragma unroll
-      for (int u = 0; u < 32; ++u) v[u] = st[(long)(32 * q + u) * D + tid];
+      for (int u = 0; u < 32; ++u) v[u] = st[(long)(32 * q + u) * D + row];
       sm100::tmem_st32(trow + 32 * q, v);
     }
     sm100::tmem_wait_st();
@@ -705,26 +708,26 @@ gdn_state_tc_kernel(const float* __restrict__ kn, const float* __restrict__ W, f
   const uint32_t a2 = sm100::smem_u32(sm + tcs::A2_OFF), b2 = sm100::smem_u32(sm + tcs::B2_OFF);
   uint32_t phase = 0;
   bool ok = true;
-  // column j = tid of K for one chunk (rows t < T, zero beyond): 64 independent loads in flight
-  float kreg[LC];
+  // K[t][j = row] for this half's 32 steps of a chunk (rows t < T, zero beyond): 32 independent loads in flight
+  float kreg[LC / 2];
   auto load_k = [&](int c) {
 #pragma unroll
-    for (int t = 0; t < LC; ++t) {
-      const int tg = c * LC + t;
-      kreg[t] = tg < T ? __ldg(kn + (((long)b * T + tg) * Hk + kh) * D + tid) : 0.f;
+    for (int u = 0; u < LC / 2; ++u) {
+      const int tg = c * LC + (LC / 2) * half + u;
+      kreg[u] = tg < T ? __ldg(kn + (((long)b * T + tg) * Hk + kh) * D + row) : 0.f;
     }
   };
   load_k(0);
 #pragma unroll 1
   for (int c = 0; c < chunks && ok; ++c) {
-    // ---- 1. S -> S0out, A1; TMEM <- e^{Lambda_L} S
+    // ---- 1. S -> S0out, A1; TMEM <- e^{Lambda_L} S (this half's 64 columns)
     rt::cp_async_wait<0>();
     __syncthreads();  // W, U0, lam of chunk c visible to every thread
     if (tid < LC) fac[tid] = expf(lam[LC - 1] - lam[tid]);
     const float eL = expf(lam[LC - 1]);
-    float* s0 = S0out + (((long)b * Hv + h) * chunks + c) * D * D + (long)tid * D;
+    float* s0 = S0out + (((long)b * Hv + h) * chunks + c) * D * D + (long)row * D;
 #pragma unroll 1
-    for (int q = 0; q < 4; ++q) {
+    for (int q = 2 * half; q < 2 * half + 2; ++q) {
       float v[32];
       sm100::tmem_ld32(trow + 32 * q, v);
       sm100::tmem_wait_ld();
@@ -732,16 +735,16 @@ gdn_state_tc_kernel(const float* __restrict__ kn, const float* __restrict__ W, f
       for (int u = 0; u < 8; ++u) {
         const float4 f = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
         *reinterpret_cast<float4*>(s0 + 32 * q + 4 * u) = f;
-        *reinterpret_cast<float4*>(sm + tcs::A1_OFF + tcs::chunk_off(128, tid, 8 * q + u)) = f;
+        *reinterpret_cast<float4*>(sm + tcs::A1_OFF + tcs::chunk_off(128, row, 8 * q + u)) = f;
       }
 #pragma unroll
       for (int u = 0; u < 32; ++u) v[u] *= eL;
       sm100::tmem_st32(trow + 32 * q, v);
     }
-    // K^T of chunk c (thread = key j), loaded into registers during the previous chunk
+    // K^T rows j = row, this half's steps (chunks q of 4 steps), from registers loaded during the previous chunk
 #pragma unroll
-    for (int q = 0; q < LC / 4; ++q)
-      *reinterpret_cast<float4*>(sm + tcs::B2_OFF + tcs::chunk_off(128, tid, q)) =
+    for (int q = 0; q < LC / 8; ++q)
+      *reinterpret_cast<float4*>(sm + tcs::B2_OFF + tcs::chunk_off(128, row, (LC / 8) * half + q)) =
           make_float4(kreg[4 * q], kreg[4 * q + 1], kreg[4 * q + 2], kreg[4 * q + 3]);
     sm100::tmem_wait_st();
     tc::fence_proxy_async();
@@ -758,27 +761,26 @@ gdn_state_tc_kernel(const float* __restrict__ kn, const float* __restrict__ W, f
       }
       sm100::mma_commit(bar);
     }
-    if (c + 1 < chunks) load_k(c + 1);  // B2 was copied out of kreg above; these loads land during the MMAs
+    if (c + 1 < chunks) load_k(c + 1);  // B2 was written from kreg above; these loads land during the MMAs
     ok = __syncthreads_and(sm100::mbar_wait_bounded(bar, phase) ? 1 : 0) != 0;  // uniform: every thread agrees
     phase ^= 1;
     sm100::tc_fence_after();
     if (!ok) break;
-    // ---- 3. Vt = U0 + D1 (to U), A2 = Vt^T scaled
+    // ---- 3. Vt = U0 + D1 (to U), A2 = Vt^T scaled: this half's 32 steps
     {
-      float d[64];
-      sm100::tmem_ld32(trow + 128, *reinterpret_cast<float(*)[32]>(d));
-      sm100::tmem_ld32(trow + 160, *reinterpret_cast<float(*)[32]>(d + 32));
+      float d[32];
+      sm100::tmem_ld32(trow + 128 + 32 * half, d);
       sm100::tmem_wait_ld();
-      const int i = tid;
 #pragma unroll
-      for (int t = 0; t < LC; ++t) {
-        const float v = U0s[t * D + i] + d[t];
-        U[(rowbase + c * LC + t) * D + i] = v;
-        d[t] = v * fac[t];
+      for (int u = 0; u < 32; ++u) {
+        const int t = 32 * half + u;
+        const float v = U0s[t * D + row] + d[u];
+        U[(rowbase + c * LC + t) * D + row] = v;
+        d[u] = v * fac[t];
       }
 #pragma unroll
-      for (int q = 0; q < LC / 4; ++q)
-        *reinterpret_cast<float4*>(sm + tcs::A2_OFF + tcs::chunk_off(128, i, q)) =
+      for (int q = 0; q < 8; ++q)
+        *reinterpret_cast<float4*>(sm + tcs::A2_OFF + tcs::chunk_off(128, row, 8 * half + q)) =
             make_float4(d[4 * q], d[4 * q + 1], d[4 * q + 2], d[4 * q + 3]);
     }
     tc::fence_proxy_async();
@@ -800,14 +802,14 @@ gdn_state_tc_kernel(const float* __restrict__ kn, const float* __restrict__ W, f
     sm100::tc_fence_after();
   }
   rt::cp_async_wait<0>();
-  if (ok) {  // final state, [j][i]
+  if (ok) {  // final state, [j][i]: this half's columns
 #pragma unroll 1
-    for (int q = 0; q < 4; ++q) {
+    for (int q = 2 * half; q < 2 * half + 2; ++q) {
       float v[32];
       sm100::tmem_ld32(trow + 32 * q, v);
       sm100::tmem_wait_ld();
 #pragma unroll
-      for (int u = 0; u < 32; ++u) st[(long)(32 * q + u) * D + tid] = v[u];
+      for (int u = 0; u < 32; ++u) st[(long)(32 * q + u) * D + row] = v[u];
     }
   } else if (tid == 0 && status) {
     atomicExch(status, 1);
@@ -883,7 +885,7 @@ cudaError_t launch(const void* qkv, long row_stride, const void* a, const void* 
   }();
   if (D == 128 && state_tc) {
     RT_CUDA_CHECK(cudaFuncSetAttribute(gdn_state_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, tcs::BYTES));
-    gdn_state_tc_kernel<<<dim3(Hv, B), 128, tcs::BYTES, stream>>>(kn, W, U, lam, state, S0, T, Tp, Hk, Hv, nullptr);
+    gdn_state_tc_kernel<<<dim3(Hv, B), 256, tcs::BYTES, stream>>>(kn, W, U, lam, state, S0, T, Tp, Hk, Hv, nullptr);
   } else {
     gdn_state_kernel<D><<<dim3(D / VB, Hv, B), NT, s2, stream>>>(kn, W, U, lam, state, S0, T, Tp, Hk, Hv);
   }
