@@ -878,10 +878,10 @@ cudaError_t launch(const void* qkv, long row_stride, const void* a, const void* 
                                                              (const bf16*)bb, ab_stride, A_log, dt_bias, W, U, lam, T,
                                                              Tp, Hk, Hv);
   RT_CUDA_CHECK(cudaGetLastError());
-  // tcgen05 state pass (head dim 128) when THESEUS_GDN_STATE_TC=1; the SIMT pass otherwise
+  // tcgen05 state pass for head dim 128 (THESEUS_GDN_STATE_TC=0 selects the SIMT pass, which other sizes use)
   static const bool state_tc = [] {
     const char* e = getenv("THESEUS_GDN_STATE_TC");
-    return e && e[0] == '1';
+    return !(e && e[0] == '0');
   }();
   if (D == 128 && state_tc) {
     RT_CUDA_CHECK(cudaFuncSetAttribute(gdn_state_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, tcs::BYTES));
