@@ -24,6 +24,8 @@ SHAPES = [  # (name, M, N, K, a_t, b_t)
     ("student_fwd", 1024, 5120, 5120, False, False),
     ("student_dx", 1024, 5120, 5120, False, True),
     ("student_dw", 5120, 5120, 1024, True, True),
+    ("lora_down", 1024, 192, 5120, False, False),
+    ("gdn_ab", 1024, 96, 5120, False, False),
     ("big_square", 8192, 8192, 8192, False, False),
 ]
 
@@ -49,12 +51,17 @@ def main():
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--only", default=None)
     p.add_argument("--tile", default=None,
-                   help="fixed tile choice instead of the measured one: width, with suffix 'sk' for stream-K")
+                   help="fixed tile choice instead of the measured one: width, then 'sk' for stream-K or "
+                        "'spS' for parallel split-K over S CTAs per tile (e.g. 256sk, 64sp16)")
     p.add_argument("--no-cublas", action="store_true")
     args = p.parse_args()
     tile = 0
     if args.tile:
-        tile = int(args.tile.rstrip("sk")) | ((1 << 16) if args.tile.endswith("sk") else 0)
+        if "sp" in args.tile:
+            width, parts = args.tile.split("sp")
+            tile = int(width) | (int(parts) << 20)
+        else:
+            tile = int(args.tile.rstrip("sk")) | ((1 << 16) if args.tile.endswith("sk") else 0)
     results = []
     for name, M, N, K, a_t, b_t in SHAPES:
         if args.only and args.only not in name:
