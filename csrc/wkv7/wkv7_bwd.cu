@@ -115,6 +115,30 @@ RT_DEVICE float dot3(const float* x, const float* y, const float* z) {
   return acc;
 }
 
+// Register tile of a chunk product over keys: acc[r][k] += sum_j X[tb + r][j] (dl[j]) Y[i_k][j] for 4 steps
+// tb..tb+3 and two value rows i0, i1 (rows of stride SP, NP keys, float4 loads). X rows are shared by a warp
+// (broadcast); Y rows i0 = consecutive per thread (conflict-free for SP = NP + 4).
+template <int NP, bool SCALE>
+RT_DEVICE void tile42(const float* X, int tb, const float* Y, int i0, int i1, const float* dl, int SP,
+                      float (&acc)[4][2]) {
+#pragma unroll 4
+  for (int q = 0; q < NP / 4; ++q) {
+    float4 y0 = reinterpret_cast<const float4*>(Y + i0 * SP)[q];
+    float4 y1 = reinterpret_cast<const float4*>(Y + i1 * SP)[q];
+    if (SCALE) {
+      const float4 d = reinterpret_cast<const float4*>(dl)[q];
+      y0.x *= d.x; y0.y *= d.y; y0.z *= d.z; y0.w *= d.w;
+      y1.x *= d.x; y1.y *= d.y; y1.z *= d.z; y1.w *= d.w;
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const float4 x = reinterpret_cast<const float4*>(X + (tb + r) * SP)[q];
+      acc[r][0] += x.x * y0.x + x.y * y0.y + x.z * y0.z + x.w * y0.w;
+      acc[r][1] += x.x * y1.x + x.y * y1.y + x.z * y1.z + x.w * y1.w;
+    }
+  }
+}
+
 // W = (I - Mab)^{-1} for strictly lower Mab ([L][L+1]); 16 threads, one column each.
 RT_DEVICE void unit_lower_inverse(const float* Mab, float* W) {
   if (threadIdx.x < L) {
@@ -401,15 +425,34 @@ wkv7_bwd_grad_kernel(int T_, int H, int N, const T* __restrict__ pr, const T* __
       }
     }
     __syncthreads();
-    // Z (into DZ) and dU, row-local
-    for (int e = threadIdx.x; e < L * VR; e += GT) {
-      const int t = e / VR, ii = e % VR;
-      float z = rowdot<NP>(c.a + t * SP, S0 + ii * SP);
-      for (int s2 = 0; s2 < t; ++s2) z += Mak[t * (L + 1) + s2] * V[s2 * VSP + ii];
-      DZ[t * VSP + ii] = z;
-      float u = dot3<NP>(c.b + t * SP, c.dl, DS + ii * SP);
-      for (int t2 = t; t2 < L; ++t2) u += Mrb[t2 * (L + 1) + t] * DY[t2 * VSP + ii];
-      DU[t * VSP + ii] = u;
+    // Z (into DZ) and dU, row-local: the key products A~ S0^T and (b D_L) dS^T as 4 x 2 register tiles, then the
+    // chunk-triangular terms per element
+    {
+      constexpr int IP = VR / 2, TILES = (L / 4) * IP;
+      for (int e = threadIdx.x; e < 2 * TILES; e += GT) {
+        const int which = e / TILES, r = e % TILES, tb = 4 * (r / IP), ia = r % IP, ib = ia + IP;
+        float acc[4][2] = {};
+        if (which == 0)
+          tile42<NP, false>(c.a, tb, S0, ia, ib, nullptr, SP, acc);
+        else
+          tile42<NP, true>(c.b, tb, DS, ia, ib, c.dl, SP, acc);
+#pragma unroll
+        for (int rr = 0; rr < 4; ++rr) {
+          const int t = tb + rr;
+#pragma unroll
+          for (int k = 0; k < 2; ++k) {
+            const int ii = k ? ib : ia;
+            float v = acc[rr][k];
+            if (which == 0) {
+              for (int s2 = 0; s2 < t; ++s2) v += Mak[t * (L + 1) + s2] * V[s2 * VSP + ii];
+              DZ[t * VSP + ii] = v;
+            } else {
+              for (int t2 = t; t2 < L; ++t2) v += Mrb[t2 * (L + 1) + t] * DY[t2 * VSP + ii];
+              DU[t * VSP + ii] = v;
+            }
+          }
+        }
+      }
     }
     __syncthreads();
     // U = W Z
@@ -428,14 +471,26 @@ wkv7_bwd_grad_kernel(int T_, int H, int N, const T* __restrict__ pr, const T* __
       DZ[s2 * VSP + ii] = z;
     }
     __syncthreads();
-    // dv (row-local, final)
-    for (int e = threadIdx.x; e < L * VR; e += GT) {
-      const int s2 = e / VR, ii = e % VR, i = i0 + ii;
-      float g = dot3<NP>(c.k + s2 * SP, c.dl, DS + ii * SP);
-      for (int t = s2; t < L; ++t) g += Mrk[t * (L + 1) + s2] * DY[t * VSP + ii];
-      for (int t = s2 + 1; t < L; ++t) g += Mak[t * (L + 1) + s2] * DZ[t * VSP + ii];
-      const int tg = t0 + s2;
-      if (tg < T_ && i < N) dv[((long)(batch * T_ + tg) * H + head) * N + i] = g;
+    // dv (row-local, final): (k D_L) dS^T as 4 x 2 register tiles, then the chunk-triangular terms
+    {
+      constexpr int IP = VR / 2, TILES = (L / 4) * IP;
+      for (int e = threadIdx.x; e < TILES; e += GT) {
+        const int sb = 4 * (e / IP), ia = e % IP, ib = ia + IP;
+        float acc[4][2] = {};
+        tile42<NP, true>(c.k, sb, DS, ia, ib, c.dl, SP, acc);
+#pragma unroll
+        for (int rr = 0; rr < 4; ++rr) {
+          const int s2 = sb + rr, tg = t0 + s2;
+#pragma unroll
+          for (int k = 0; k < 2; ++k) {
+            const int ii = k ? ib : ia, i = i0 + ii;
+            float g = acc[rr][k];
+            for (int t = s2; t < L; ++t) g += Mrk[t * (L + 1) + s2] * DY[t * VSP + ii];
+            for (int t = s2 + 1; t < L; ++t) g += Mak[t * (L + 1) + s2] * DZ[t * VSP + ii];
+            if (tg < T_ && i < N) dv[((long)(batch * T_ + tg) * H + head) * N + i] = g;
+          }
+        }
+      }
     }
     // sums over this pass's value rows
     for (int e = threadIdx.x; e < 4 * L * L; e += GT) {
