@@ -27,8 +27,10 @@ cudaError_t rt_wkv7_backward(int dtype, int B, int T, int H, int N, const void* 
 cudaError_t rt_gemm_bf16(const void* A, long lda, int a_mn, const void* B, long ldb, int b_mn, void* C, long ldc,
                          int M, int N, int K, int epi, float alpha, int* status, cudaStream_t stream);
 int rt_gemm_fault();
+int rt_kl_segments(long rows, long V);
+long rt_kl_workspace_floats(long rows, int segments);
 cudaError_t rt_kl_rows(int dtype, const void* student, const void* teacher, long rows, long V, long ld_s, long ld_t,
-                       float* out, cudaStream_t stream);
+                       int segments, float* work, float* out, cudaStream_t stream);
 cudaError_t rt_gemm_nmse_bf16(const void* A, long lda, const void* B, long ldb, void* dpred, long ldc, const void* target,
                               float* rowsum, int M, int N, int K, float eps, int* status, cudaStream_t stream);
 cudaError_t rt_loss_rows_prep(const void* target, float* rowsum, long rows, int C, cudaStream_t stream);

@@ -364,9 +364,12 @@ at::Tensor kl_rows(at::Tensor student, at::Tensor teacher) {
                   student.scalar_type() == teacher.scalar_type() && student.stride(1) == 1 && teacher.stride(1) == 1,
               "kl_rows: two CUDA [rows, V] logit matrices of one dtype with unit inner stride");
   TORCH_CHECK(student.scalar_type() == at::kBFloat16 || student.scalar_type() == at::kFloat, "kl_rows: bf16 or fp32");
-  auto out = at::empty({student.size(0)}, student.options().dtype(at::kFloat));
-  check_cuda(rt_kl_rows(student.scalar_type() == at::kBFloat16 ? 1 : 0, student.data_ptr(), teacher.data_ptr(),
-                        student.size(0), student.size(1), student.stride(0), teacher.stride(0), out.data_ptr<float>(),
+  const long rows = student.size(0), V = student.size(1);
+  auto out = at::empty({rows}, student.options().dtype(at::kFloat));
+  const int segments = rt_kl_segments(rows, V);
+  auto work = at::empty({std::max(1L, rt_kl_workspace_floats(rows, segments))}, out.options());
+  check_cuda(rt_kl_rows(student.scalar_type() == at::kBFloat16 ? 1 : 0, student.data_ptr(), teacher.data_ptr(), rows, V,
+                        student.stride(0), teacher.stride(0), segments, work.data_ptr<float>(), out.data_ptr<float>(),
                         stream_of(student)),
              "kl_rows");
   return out;
