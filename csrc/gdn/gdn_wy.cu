@@ -725,18 +725,15 @@ gdn_state_tc_kernel(const float* __restrict__ kn, const float* __restrict__ W, f
     __syncthreads();  // W, U0, lam of chunk c visible to every thread
     if (tid < LC) fac[tid] = expf(lam[LC - 1] - lam[tid]);
     const float eL = expf(lam[LC - 1]);
-    float* s0 = S0out + (((long)b * Hv + h) * chunks + c) * D * D + (long)row * D;
 #pragma unroll 1
     for (int q = 2 * half; q < 2 * half + 2; ++q) {
       float v[32];
       sm100::tmem_ld32(trow + 32 * q, v);
       sm100::tmem_wait_ld();
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const float4 f = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
-        *reinterpret_cast<float4*>(s0 + 32 * q + 4 * u) = f;
-        *reinterpret_cast<float4*>(sm + tcs::A1_OFF + tcs::chunk_off(128, row, 8 * q + u)) = f;
-      }
+      for (int u = 0; u < 8; ++u)
+        *reinterpret_cast<float4*>(sm + tcs::A1_OFF + tcs::chunk_off(128, row, 8 * q + u)) =
+            make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
 #pragma unroll
       for (int u = 0; u < 32; ++u) v[u] *= eL;
       sm100::tmem_st32(trow + 32 * q, v);
@@ -751,7 +748,8 @@ gdn_state_tc_kernel(const float* __restrict__ kn, const float* __restrict__ W, f
     sm100::tc_fence_before();
     __syncthreads();
     sm100::tc_fence_after();
-    // ---- 2. D1 = A1 W^T
+    // ---- 2. D1 = A1 W^T; meanwhile the chunk-start state goes from the A1 tile to S0out, one row per warp
+    // instruction (coalesced; MMA and copy only read A1)
     if (tid == 0) {
 #pragma unroll
       for (int ks = 0; ks < D / 8; ++ks) {
@@ -760,6 +758,14 @@ gdn_state_tc_kernel(const float* __restrict__ kn, const float* __restrict__ W, f
                         ks > 0);
       }
       sm100::mma_commit(bar);
+    }
+    {
+      float* s0 = S0out + (((long)b * Hv + h) * chunks + c) * D * D;
+      for (int e = tid; e < 128 * 32; e += NTH) {  // e: row (e / 32), 16-byte chunk (e % 32)
+        const int r = e >> 5, qq = e & 31;
+        *reinterpret_cast<float4*>(s0 + (long)r * D + 4 * qq) =
+            *reinterpret_cast<const float4*>(sm + tcs::A1_OFF + tcs::chunk_off(128, r, qq));
+      }
     }
     if (c + 1 < chunks) load_k(c + 1);  // B2 was written from kreg above; these loads land during the MMAs
     ok = __syncthreads_and(sm100::mbar_wait_bounded(bar, phase) ? 1 : 0) != 0;  // uniform: every thread agrees
