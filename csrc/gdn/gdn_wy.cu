@@ -527,28 +527,49 @@ gdn_out_tc_kernel(const float* __restrict__ qn, const float* __restrict__ kn, co
     sm100::tmem_alloc(tslot, 256);
     sm100::tmem_relinquish();
   }
-  // operands: q/k rows (fp32 -> bf16), S0 rows, Vt transposed, Lambda
-  for (int e = tid; e < 128 * 16; e += 128) {
-    const int r = e >> 4, k8 = e & 15, t = t0 + (r & 63);
-    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    if (t < T) {
-      const float* src = (r < 64 ? qn : kn) + (((long)b * T + t) * Hk + kh) * D + 8 * k8;
-      const float4 x = *reinterpret_cast<const float4*>(src), y = *reinterpret_cast<const float4*>(src + 4);
-      v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w; v[4] = y.x; v[5] = y.y; v[6] = y.z; v[7] = y.w;
-    }
-    tc::put_chunk(QK, 128, r, k8, v);
-    const float* srow = S0 + (((long)b * Hv + h) * chunks + c) * D * D + (long)r * D + 8 * k8;
-    const float4 x = *reinterpret_cast<const float4*>(srow), y = *reinterpret_cast<const float4*>(srow + 4);
-    const float w[8] = {x.x, x.y, x.z, x.w, y.x, y.y, y.z, y.w};
-    tc::put_chunk(Sx, 128, r, k8, w);
-  }
-  {  // Vt^T: thread = value row i, 64 steps
-    const int i = tid;
-    for (int k8 = 0; k8 < 8; ++k8) {
-      float v[8];
+  // operands: q/k rows (fp32 -> bf16), S0 rows, Vt transposed, Lambda. Loads of four iterations are issued
+  // before their shared-memory stores so that 16 (then 32) global loads per thread are in flight.
+  const float* s0c = S0 + (((long)b * Hv + h) * chunks + c) * D * D;
+#pragma unroll 1
+  for (int e0 = tid; e0 < 128 * 16; e0 += 4 * 128) {
+    float4 qk[4][2], sv[4][2];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) v[u] = t0 + 8 * k8 + u < T ? U[(rowbase + 8 * k8 + u) * D + i] : 0.f;
-      tc::put_chunk(VT, 128, i, k8, v);
+    for (int g = 0; g < 4; ++g) {
+      const int e = e0 + g * 128, r = e >> 4, k8 = e & 15, t = t0 + (r & 63);
+      if (t < T) {
+        const float* src = (r < 64 ? qn : kn) + (((long)b * T + t) * Hk + kh) * D + 8 * k8;
+        qk[g][0] = __ldg(reinterpret_cast<const float4*>(src));
+        qk[g][1] = __ldg(reinterpret_cast<const float4*>(src + 4));
+      } else {
+        qk[g][0] = qk[g][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      const float* srow = s0c + (long)r * D + 8 * k8;
+      sv[g][0] = __ldg(reinterpret_cast<const float4*>(srow));
+      sv[g][1] = __ldg(reinterpret_cast<const float4*>(srow + 4));
+    }
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const int e = e0 + g * 128, r = e >> 4, k8 = e & 15;
+      const float v[8] = {qk[g][0].x, qk[g][0].y, qk[g][0].z, qk[g][0].w, qk[g][1].x, qk[g][1].y, qk[g][1].z, qk[g][1].w};
+      tc::put_chunk(QK, 128, r, k8, v);
+      const float w[8] = {sv[g][0].x, sv[g][0].y, sv[g][0].z, sv[g][0].w, sv[g][1].x, sv[g][1].y, sv[g][1].z, sv[g][1].w};
+      tc::put_chunk(Sx, 128, r, k8, w);
+    }
+  }
+  {  // Vt^T: thread = value row i, 64 steps (32 loads in flight)
+    const int i = tid;
+#pragma unroll 1
+    for (int k0 = 0; k0 < 8; k0 += 4) {
+      float v[4][8];
+#pragma unroll
+      for (int g = 0; g < 4; ++g)
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int tt = 8 * (k0 + g) + u;
+          v[g][u] = t0 + tt < T ? __ldg(U + (rowbase + tt) * D + i) : 0.f;
+        }
+#pragma unroll
+      for (int g = 0; g < 4; ++g) tc::put_chunk(VT, 128, i, k0 + g, v[g]);
     }
   }
   if (tid < LC) lam[tid] = lam_in[rowbase + tid];
