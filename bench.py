@@ -34,7 +34,7 @@ import time
 from pathlib import Path
 
 ROOT = Path(__file__).resolve().parent
-BASELINE_TOKENS_PER_S = None  # the reference publishes no throughput
+BASELINE_TOKENS_PER_S = None  # the reference project publishes no throughput figure for this config
 
 MODEL_27B = dict(vocab_size=248077, hidden_size=5120, intermediate_size=17408, num_hidden_layers=64,
                  num_attention_heads=24, num_key_value_heads=4, head_dim=256, linear_num_key_heads=16,
