@@ -50,3 +50,17 @@ def test_strongest_decay_over_a_64_step_chunk_stays_in_fp32_range():
     y32, s32 = wkv7_chunked(*xs, chunk=64, dtype=torch.float32)
     assert torch.isfinite(y32).all() and torch.isfinite(s32).all()
     torch.testing.assert_close(y32.double(), y_ref, rtol=2e-3, atol=2e-3)
+
+
+@pytest.mark.parametrize("T,chunk", [(150, 64), (37, 16), (64, 64)])
+def test_chunked_backward_matches_autograd_of_the_recurrence(T, chunk):
+    from rwkv_theseus_b200.ops.wkv7_chunked import wkv7_chunked_backward
+    xs = [x.clone().requires_grad_(True) for x in _inputs(2, T, 2, 16, seed=7 * T + chunk)]
+    y, s = _recurrence64(*xs)
+    g = torch.Generator().manual_seed(11)
+    dy = torch.randn(y.shape, generator=g, dtype=torch.float64)
+    ds = torch.randn(s.shape, generator=g, dtype=torch.float64)
+    ref = torch.autograd.grad((y * dy).sum() + (s * ds).sum(), xs)
+    got = wkv7_chunked_backward(*[x.detach() for x in xs], dy, ds, chunk=chunk)
+    for name, g_got, g_ref in zip(("r", "w", "k", "v", "a", "b", "state"), got, ref):
+        torch.testing.assert_close(g_got, g_ref, rtol=1e-8, atol=1e-9, msg=name)
