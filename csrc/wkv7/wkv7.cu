@@ -1,4 +1,5 @@
 // Chunked RWKV7 (WKV7) state recurrence, forward and backward, for sm_100a.
+// The recurrence is RWKV7's (RWKV-LM, Apache-2.0; see NOTICE at the project root); this code is our own.
 //
 // Semantics match the reference kernel (kernels/wkv7_state.cu:12-79 of the
 // reference project): state S[value i][key j] per (batch, head),

@@ -1,4 +1,5 @@
 // WKV7 backward for sm_100a in three kernels (chunk length 16):
+// The recurrence is RWKV7's (RWKV-LM, Apache-2.0; see NOTICE at the project root); this code is our own.
 //
 //   1. prep   (one CTA per head and chunk, parallel): cumulative log decay,
 //             decayed vectors r~, a~, b^ = b~ D_L, D_L, the chunk matrix M_rb

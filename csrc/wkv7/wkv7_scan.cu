@@ -1,4 +1,5 @@
 // WKV7 forward as a parallel per-chunk pass plus a light serial scan, sm_100a (head sizes 32, 64, 128).
+// The recurrence is RWKV7's (RWKV-LM, Apache-2.0; see NOTICE at the project root); this code is our own.
 //
 // Same chunk algebra as wkv7.cu (chunks of L = 16, decayed vectors a~ = a e^{Lambda_{t-1}}, r~ = r e^{Lambda_t},
 // b~ = b e^{-Lambda_s}, k~ = k e^{-Lambda_s}, chunk matrices Mab, Mak (s < t), Mrb, Mrk (s <= t)), with every

@@ -1,4 +1,5 @@
 // WKV7 token-by-token update for decoding (T small, no checkpoints), sm_100a.
+// The recurrence is RWKV7's (RWKV-LM, Apache-2.0; see NOTICE at the project root); this code is our own.
 //
 // Per (batch, head) one CTA of N threads; thread i owns value row i of the fp32 state S[i][:] in registers:
 //   sa = S[i] . a_t,   S[i][j] = S[i][j] d_t[j] + sa b_t[j] + v_t[i] k_t[j],   y_t[i] = S[i] . r_t,

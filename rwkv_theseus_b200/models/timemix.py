@@ -1,5 +1,13 @@
 """RWKV7 TimeMix student: the module that replaces one full-attention block.
 
+Attribution: the TimeMix formulas (token-shift lerps, decay / in-context
+learning-rate / gate LoRAs, the RWKV7 state update, per-head GroupNorm and
+bonus term) and the initialisation schedule follow RWKV7 ``RWKV_Tmix_x070``
+and ``generate_init_weight`` of RWKV-LM (BlinkDL; RWKV-Vibe/RWKV-LM-V7,
+commit 665472dab30952de9379a3a3a01eaa3453f1ad4e, ``src/model.py``), licensed
+under the Apache License 2.0 (see ``NOTICE`` at the project root). This file
+restates them in its own code; it adds no v_first path between layers.
+
 Parameter schema (23 tensors, names/shapes/order as reference
 ``theseus/timemix.py:29-59``)::
 

@@ -1,5 +1,11 @@
 """RWKV7 state recurrence (the DPLR "WKV7" operator).
 
+Attribution: the recurrence (decay clamp, state update and readout) is the
+RWKV7 one of RWKV-LM (BlinkDL; RWKV-Vibe/RWKV-LM-V7, commit
+665472dab30952de9379a3a3a01eaa3453f1ad4e, ``cuda/rwkv7_clampw.cu``), Apache
+License 2.0 (see ``NOTICE`` at the project root). The chunked kernels that
+evaluate it here are this project's own.
+
 State layout ``[batch, head, value i, key j]``. Per step (reference
 ``theseus/wkv7.py:16-28`` and ``kernels/wkv7_state.cu:12-40``)::
 

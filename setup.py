@@ -25,7 +25,7 @@ setup(
     name="rwkv_theseus_b200",
     version="0.1.0",
     packages=["rwkv_theseus_b200", "rwkv_theseus_b200.models", "rwkv_theseus_b200.ops",
-              "rwkv_theseus_b200.parallel", "rwkv_theseus_b200.utils"],
+              "rwkv_theseus_b200.parallel", "rwkv_theseus_b200.convert"],
     ext_modules=[CUDAExtension(
         name="rwkv_theseus_b200._C",
         sources=sources(),
