@@ -6,6 +6,9 @@
 #include "gdn_noalloc.h"
 #include "../api.h"
 
+#include <atomic>
+#include <stdint.h>
+
 namespace {
 
 // The scratch itself. In host code this name is only a stand-in for the
@@ -13,7 +16,9 @@ namespace {
 static __device__ __align__(256) float g_gdn_scratch[RT_GDN_NOALLOC_MAX_FLOATS];
 
 constexpr int kMaxDevices = 64;
-float* g_scratch_ptr[kMaxDevices] = {nullptr};
+// Per-device cache of the resolved address. Atomic so that first calls from several host threads are not a data
+// race: two threads may both resolve the address, and they store the same value.
+std::atomic<float*> g_scratch_ptr[kMaxDevices];
 
 // Resolves (once per device, with that device current) the scratch's device address.
 cudaError_t scratch_for_current_device(float** out) {
@@ -21,15 +26,19 @@ cudaError_t scratch_for_current_device(float** out) {
   cudaError_t err = cudaGetDevice(&dev);
   if (err != cudaSuccess) return err;
   if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
-  if (!g_scratch_ptr[dev]) {
+  float* cached = g_scratch_ptr[dev].load(std::memory_order_acquire);
+  if (!cached) {
     void* ptr = nullptr;
     err = cudaGetSymbolAddress(&ptr, g_gdn_scratch);
     if (err != cudaSuccess) return err;
-    g_scratch_ptr[dev] = static_cast<float*>(ptr);
+    cached = static_cast<float*>(ptr);
+    g_scratch_ptr[dev].store(cached, std::memory_order_release);
   }
-  *out = g_scratch_ptr[dev];
+  *out = cached;
   return cudaSuccess;
 }
+
+bool aligned(const void* p, uintptr_t bytes) { return (reinterpret_cast<uintptr_t>(p) & (bytes - 1)) == 0; }
 
 }  // namespace
 
@@ -40,6 +49,12 @@ extern "C" cudaError_t rt_gdn_forward_noalloc(const void* qkv, long row_stride, 
                                               float* state, void* out, int B, int T, int Hk, int Hv, int D,
                                               cudaStream_t stream) {
   if (B <= 0 || T <= 0 || Hk <= 0 || Hv <= 0 || D <= 0) return cudaErrorInvalidValue;
+  if (!qkv || !a || !b || !A_log || !dt_bias || !state || !out) return cudaErrorInvalidValue;
+  // The kernels copy v rows of qkv 16 bytes at a time and read a / b as bf16 scalars.
+  if (Hv % Hk != 0 || row_stride % 8 != 0 || row_stride < (long)(2 * Hk + Hv) * D || ab_stride < Hv)
+    return cudaErrorInvalidValue;
+  if (!aligned(qkv, 16) || !aligned(a, 2) || !aligned(b, 2) || !aligned(state, 4) || !aligned(out, 2))
+    return cudaErrorInvalidValue;
   if (rt_gdn_serial_workspace_floats(B, T, Hk, D) > RT_GDN_NOALLOC_MAX_FLOATS) return cudaErrorInvalidValue;
   float* work = nullptr;
   cudaError_t err = scratch_for_current_device(&work);

@@ -13,6 +13,13 @@
 // file-scope device array, so the call allocates nothing. The caller still
 // passes every input and output buffer.
 //
+// Preconditions (checked; a call that breaks one returns cudaErrorInvalidValue
+// and launches nothing):
+//   * qkv is 16-byte aligned, row_stride is a multiple of 8 elements and at
+//     least (2 * Hk + Hv) * D (q | k | v of one token);
+//   * Hv is a multiple of Hk, ab_stride >= Hv;
+//   * a, b, out are bf16-aligned and state is float-aligned; no pointer is null.
+//
 // Limits and behaviour:
 //   * the scratch holds RT_GDN_NOALLOC_MAX_FLOATS floats (4 MiB); calls whose
 //     workspace (rt_gdn_serial_workspace_floats(B, T, Hk, D)) exceeds it return
@@ -22,7 +29,9 @@
 //     process exits;
 //   * the first call on a device resolves the array's device address with
 //     cudaGetSymbolAddress (with that device current) and caches it; make
-//     that first call before any stream capture;
+//     that first call before any stream capture. cudaDeviceReset invalidates
+//     the cached address: after a reset, do not call this entry point again in
+//     the same process;
 //   * all calls share the one array and it keeps the previous call's
 //     contents: every scratch value the kernels read is written earlier in the
 //     same call, so nothing needs clearing, but calls that overlap on the GPU

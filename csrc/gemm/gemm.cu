@@ -606,13 +606,13 @@ struct SkWorkspace {
   float* ws = nullptr;
   int* flags = nullptr;
 };
+std::map<int, SkWorkspace> g_sk_spaces;
+std::mutex g_sk_mutex;
 SkWorkspace* sk_workspace(cudaStream_t stream) {
-  static std::map<int, SkWorkspace> spaces;
-  static std::mutex m;
   int dev = 0;
   cudaGetDevice(&dev);
-  std::lock_guard<std::mutex> lock(m);
-  SkWorkspace& w = spaces[dev];
+  std::lock_guard<std::mutex> lock(g_sk_mutex);
+  SkWorkspace& w = g_sk_spaces[dev];
   if (w.ws) return &w;
   cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
   if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) return nullptr;
@@ -910,10 +910,22 @@ extern "C" cudaError_t rt_gemm_nmse_bf16(const void* A, long lda, const void* B,
 }
 
 // 1 if a GEMM launched without a status word gave up a wait since the last call (synchronizes the device).
+// A launch that gave up a wait leaves its tile's split-K arrive/depart counters and stream-K quarter flags
+// nonzero (only the success path clears them); later launches would then pass their waits early on the stale
+// counts. So a fault also zeroes the current device's schedule counters, after the device is idle.
 extern "C" int rt_gemm_fault() {
   int v = 0, zero = 0;
   if (cudaMemcpyFromSymbol(&v, gemm_fault_word, sizeof(int)) != cudaSuccess) return -1;
-  if (v) cudaMemcpyToSymbol(gemm_fault_word, &zero, sizeof(int));
+  if (v) {
+    cudaMemcpyToSymbol(gemm_fault_word, &zero, sizeof(int));
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(g_sk_mutex);
+    auto it = g_sk_spaces.find(dev);
+    if (it != g_sk_spaces.end() && it->second.flags && (cudaDeviceSynchronize() != cudaSuccess ||
+                                                        cudaMemset(it->second.flags, 0, SK_MAX_FLAGS * sizeof(int)) != cudaSuccess))
+      return -1;
+  }
   return v;
 }
 

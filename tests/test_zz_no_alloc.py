@@ -70,3 +70,33 @@ def test_noalloc_rejects_work_beyond_its_scratch():
     A_log, dt_bias = torch.zeros(Hv, device="cuda"), torch.zeros(Hv, device="cuda")
     assert _call(fn, qkv, ab, Hv, A_log, dt_bias, state, out, B, T, Hk, D) == CUDA_ERROR_INVALID_VALUE
     assert torch.count_nonzero(out) == 0 and torch.count_nonzero(state) == 0
+
+
+@cuda
+@pytest.mark.parametrize("case", ["odd_row_stride", "short_row_stride", "short_ab_stride", "misaligned_qkv"])
+def test_noalloc_rejects_strides_and_pointers_the_kernels_cannot_read(case):
+    """Plain C callers pass raw strides and pointers; a layout the 16-byte row copies cannot read is refused
+    before anything is launched (no output or state is written)."""
+    ext, fn, _ = _entry()
+    B, T, Hk, Hv, D = 1, 20, 2, 6, 64
+    width = 2 * Hk * D + Hv * D
+    qkv_buf = torch.zeros(B * T * (width + 16) + 64, device="cuda", dtype=torch.bfloat16)
+    row_stride, ab_stride, offset = width, 2 * Hv, 0
+    if case == "odd_row_stride":
+        row_stride = width + 3
+    elif case == "short_row_stride":
+        row_stride = width - 8
+    elif case == "short_ab_stride":
+        ab_stride = Hv - 1
+    else:
+        offset = 1  # one bf16 past a 16-byte boundary
+    ab = torch.zeros(B * T, 2 * Hv, device="cuda", dtype=torch.bfloat16)
+    state = torch.zeros(B, Hv, D, D, device="cuda")
+    out = torch.zeros(B, T, Hv, D, device="cuda", dtype=torch.bfloat16)
+    A_log, dt_bias = torch.zeros(Hv, device="cuda"), torch.zeros(Hv, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    rc = fn(qkv_buf.data_ptr() + 2 * offset, row_stride, ab.data_ptr(), ab[:, Hv:].data_ptr(), ab_stride,
+            A_log.data_ptr(), dt_bias.data_ptr(), state.data_ptr(), out.data_ptr(), B, T, Hk, Hv, D, stream)
+    torch.cuda.synchronize()
+    assert rc == CUDA_ERROR_INVALID_VALUE
+    assert torch.count_nonzero(out) == 0 and torch.count_nonzero(state) == 0
