@@ -75,9 +75,9 @@ def main():
         print(json.dumps({"kernel": "wkv7_forward", "T": T, "ms": ms}), flush=True)
         if a.profile:
             kernel_times(fwd)
-        y, end, ck = ext.wkv7_forward(*xs, s0, True)
+        y, end, ck, rec = ext.wkv7_forward(*xs, s0, True)
         dy, dend = torch.randn_like(y), torch.zeros_like(end)
-        bwd = lambda: ext.wkv7_backward(*xs, ck, dy, dend)  # noqa: E731
+        bwd = lambda: ext.wkv7_backward(*xs, ck, rec, dy, dend)  # noqa: E731
         ms = timed(bwd, a.warmup, a.iters)
         print(json.dumps({"kernel": "wkv7_backward", "T": T, "ms": ms}), flush=True)
         if a.profile:

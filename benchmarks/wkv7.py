@@ -46,8 +46,8 @@ def ours_step_fn():
     ext = native()
 
     def run(xs, state, dy):
-        y, end, ckpt = ext.wkv7_forward(*xs, state, True)
-        grads = ext.wkv7_backward(*xs, ckpt, dy, torch.zeros_like(end))
+        y, end, ckpt, rec = ext.wkv7_forward(*xs, state, True)
+        grads = ext.wkv7_backward(*xs, ckpt, rec, dy, torch.zeros_like(end))
         return end, grads
     return run
 

@@ -16,6 +16,19 @@ cudaError_t rt_wkv7_scan_forward(int dtype, int B, int T, int H, int N, const vo
 cudaError_t rt_wkv7_forward(int dtype, int B, int T, int H, int N, const void* r, const void* w, const void* k,
                             const void* v, const void* a, const void* b, const float* s0, void* y, float* s_end,
                             float* checkpoints, cudaStream_t stream);
+// tcgen05 path (bf16, head size 64, chunks of 64 steps): wkv7_tc_fwd.cu / wkv7_tc_bwd.cu.
+int rt_wkv7_tc_chunk_len();
+long rt_wkv7_tc_workspace_floats(int B, int T, int H);
+long rt_wkv7_tc_backward_workspace_floats(int B, int T, int H);
+int rt_wkv7_tc_fault();
+int rt_wkv7_tc_bwd_fault();
+cudaError_t rt_wkv7_tc_forward(int B, int T, int H, const void* r, const void* w, const void* k, const void* v,
+                               const void* a, const void* b, const float* s0, void* y, float* s_end, float* ckpt,
+                               float* ws, cudaStream_t stream);
+cudaError_t rt_wkv7_tc_backward(int B, int T, int H, const void* r, const void* w, const void* k, const void* v,
+                                const void* a, const void* b, const float* ckpt, const float* rec, const void* dy,
+                                const float* dend, float* dr, float* dw, float* dk, float* dv, float* da, float* db,
+                                float* ds0, float* work, cudaStream_t stream);
 long rt_wkv7_backward_workspace_floats(int B, int T, int H, int N);
 cudaError_t rt_wkv7_backward(int dtype, int B, int T, int H, int N, const void* r, const void* w, const void* k,
                              const void* v, const void* a, const void* b, const float* checkpoints, const void* dy,

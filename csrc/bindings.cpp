@@ -33,6 +33,16 @@ void check_wkv(const at::Tensor& r, const std::vector<at::Tensor>& xs) {
                 "WKV7 input mismatch");
 }
 
+// The tcgen05 path (chunks of 64 steps) serves bf16 inputs with head size 64 and at least 128 steps; shorter
+// calls, fp32 inputs and other head sizes run the chunk-16 CUDA-core kernels.
+bool g_wkv7_tc_enabled = false;  // switched on once validated on a B200
+bool wkv7_use_tc(const at::Tensor& r) {
+  return g_wkv7_tc_enabled && r.scalar_type() == at::kBFloat16 && r.size(3) == 64 && r.size(1) >= 128;
+}
+
+// Returns (y, end, checkpoints, records). `checkpoints` [B, H, chunks + 1, N, N] holds the chunk-start states
+// and the final state; `records` is the tcgen05 path's per-chunk record (G, H0, Q, Y0, T; the backward reads
+// it) and is empty on the CUDA-core path.
 std::vector<at::Tensor> wkv7_forward(at::Tensor r, at::Tensor w, at::Tensor k, at::Tensor v, at::Tensor a,
                                      at::Tensor b, at::Tensor s0, bool save_checkpoints) {
   check_wkv(r, {w, k, v, a, b});
@@ -41,10 +51,22 @@ std::vector<at::Tensor> wkv7_forward(at::Tensor r, at::Tensor w, at::Tensor k, a
   TORCH_CHECK(s0.device() == r.device() && s0.scalar_type() == at::kFloat && s0.is_contiguous() &&
                   s0.sizes() == at::IntArrayRef({B, H, N, N}),
               "s0 must be contiguous CUDA fp32 [B,H,N,N]");
-  const int chunks = (T + rt_wkv7_chunk_len() - 1) / rt_wkv7_chunk_len();
   auto y = at::empty_like(r);
   auto end = at::empty_like(s0);
-  auto ckpt = save_checkpoints ? at::empty({B, H, chunks + 1, N, N}, s0.options()) : at::empty({0}, s0.options());
+  auto none = at::empty({0}, s0.options());
+  if (wkv7_use_tc(r)) {
+    const int chunks = (T + rt_wkv7_tc_chunk_len() - 1) / rt_wkv7_tc_chunk_len();
+    auto ckpt = at::empty({B, H, chunks + 1, N, N}, s0.options());
+    auto rec = at::empty({rt_wkv7_tc_workspace_floats(B, T, H)}, s0.options());
+    check_cuda(rt_wkv7_tc_forward(B, T, H, r.data_ptr(), w.data_ptr(), k.data_ptr(), v.data_ptr(), a.data_ptr(),
+                                  b.data_ptr(), s0.data_ptr<float>(), y.data_ptr(), end.data_ptr<float>(),
+                                  ckpt.data_ptr<float>(), rec.data_ptr<float>(), stream_of(r)),
+               "wkv7_forward (tcgen05)");
+    if (!save_checkpoints) return {y, end, none, none};
+    return {y, end, ckpt, rec};
+  }
+  const int chunks = (T + rt_wkv7_chunk_len() - 1) / rt_wkv7_chunk_len();
+  auto ckpt = save_checkpoints ? at::empty({B, H, chunks + 1, N, N}, s0.options()) : none;
   const long scan_ws = T > 4 ? rt_wkv7_scan_workspace_floats(B, T, H, N) : 0;
   if (scan_ws > 0) {  // head sizes 32/64/128: parallel per-chunk pass + light serial scan
     auto work = at::empty({scan_ws}, s0.options());
@@ -53,21 +75,25 @@ std::vector<at::Tensor> wkv7_forward(at::Tensor r, at::Tensor w, at::Tensor k, a
                                     end.data_ptr<float>(), save_checkpoints ? ckpt.data_ptr<float>() : nullptr,
                                     work.data_ptr<float>(), stream_of(r)),
                "wkv7_forward (scan)");
-    return {y, end, ckpt};
+    return {y, end, ckpt, none};
   }
   check_cuda(rt_wkv7_forward(dtype_code(r), B, T, H, N, r.data_ptr(), w.data_ptr(), k.data_ptr(), v.data_ptr(),
                              a.data_ptr(), b.data_ptr(), s0.data_ptr<float>(), y.data_ptr(), end.data_ptr<float>(),
                              save_checkpoints ? ckpt.data_ptr<float>() : nullptr, stream_of(r)),
              "wkv7_forward");
-  return {y, end, ckpt};
+  return {y, end, ckpt, none};
 }
 
 std::vector<at::Tensor> wkv7_backward(at::Tensor r, at::Tensor w, at::Tensor k, at::Tensor v, at::Tensor a,
-                                      at::Tensor b, at::Tensor ckpt, at::Tensor dy, at::Tensor dend) {
+                                      at::Tensor b, at::Tensor ckpt, at::Tensor rec, at::Tensor dy, at::Tensor dend) {
   check_wkv(r, {w, k, v, a, b, dy});
   c10::cuda::CUDAGuard guard(r.device());
   const int B = r.size(0), T = r.size(1), H = r.size(2), N = r.size(3);
-  const int chunks = (T + rt_wkv7_chunk_len() - 1) / rt_wkv7_chunk_len();
+  const bool tc = rec.numel() > 0;
+  TORCH_CHECK(!tc || (r.scalar_type() == at::kBFloat16 && N == 64),
+              "tcgen05 WKV7 records given for a call the tcgen05 path does not serve");
+  const int len = tc ? rt_wkv7_tc_chunk_len() : rt_wkv7_chunk_len();
+  const int chunks = (T + len - 1) / len;
   TORCH_CHECK(ckpt.device() == r.device() && ckpt.scalar_type() == at::kFloat && ckpt.is_contiguous() &&
                   ckpt.sizes() == at::IntArrayRef({B, H, chunks + 1, N, N}),
               "invalid chunk checkpoints");
@@ -78,6 +104,20 @@ std::vector<at::Tensor> wkv7_backward(at::Tensor r, at::Tensor w, at::Tensor k, 
   std::vector<at::Tensor> g;
   for (int i = 0; i < 6; ++i) g.push_back(at::empty(r.sizes(), opts));
   g.push_back(at::empty({B, H, N, N}, opts));
+  if (tc) {
+    TORCH_CHECK(rec.device() == r.device() && rec.scalar_type() == at::kFloat && rec.is_contiguous() &&
+                    rec.numel() == rt_wkv7_tc_workspace_floats(B, T, H),
+                "invalid tcgen05 WKV7 records");
+    auto work = at::empty({rt_wkv7_tc_backward_workspace_floats(B, T, H)}, opts);
+    check_cuda(rt_wkv7_tc_backward(B, T, H, r.data_ptr(), w.data_ptr(), k.data_ptr(), v.data_ptr(), a.data_ptr(),
+                                   b.data_ptr(), ckpt.data_ptr<float>(), rec.data_ptr<float>(), dy.data_ptr(),
+                                   dend.data_ptr<float>(), g[0].data_ptr<float>(), g[1].data_ptr<float>(),
+                                   g[2].data_ptr<float>(), g[3].data_ptr<float>(), g[4].data_ptr<float>(),
+                                   g[5].data_ptr<float>(), g[6].data_ptr<float>(), work.data_ptr<float>(),
+                                   stream_of(r)),
+               "wkv7_backward (tcgen05)");
+    return g;
+  }
   auto work = at::empty({rt_wkv7_backward_workspace_floats(B, T, H, N)}, opts);
   check_cuda(rt_wkv7_backward(dtype_code(r), B, T, H, N, r.data_ptr(), w.data_ptr(), k.data_ptr(), v.data_ptr(),
                               a.data_ptr(), b.data_ptr(), ckpt.data_ptr<float>(), dy.data_ptr(),
@@ -498,7 +538,7 @@ at::Tensor flash_attention(at::Tensor q, at::Tensor keys, at::Tensor values, at:
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels of rwkv_theseus_b200";
-  m.def("wkv7_forward", &wkv7_forward, "chunked WKV7 forward (y, end state, chunk checkpoints)");
+  m.def("wkv7_forward", &wkv7_forward, "chunked WKV7 forward (y, end state, chunk checkpoints, tcgen05 records)");
   m.def("wkv7_backward", &wkv7_backward, "chunked WKV7 backward (dr, dw, dk, dv, da, db, ds0)");
   m.def("gemm", &gemm, "tcgen05 GEMM: a_op(A) . b_op(B)^T with bf16/fp32/accumulate epilogue",
         py::arg("A"), py::arg("a_t"), py::arg("B"), py::arg("b_t"), py::arg("epi") = 0, py::arg("alpha") = 1.0,
@@ -537,4 +577,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_open", &ipc_open);
   m.def("ipc_close", &ipc_close);
   m.def("wkv7_chunk_len", []() { return rt_wkv7_chunk_len(); });
+  m.def("wkv7_tc_fault", []() { return rt_wkv7_tc_fault() | rt_wkv7_tc_bwd_fault(); },
+        "1 if a tcgen05 WKV7 kernel gave up a bounded wait since the last call (synchronizes)");
+  m.def("wkv7_tc_enable", [](bool on) { g_wkv7_tc_enabled = on; },
+        "route bf16 head-64 calls of >= 128 steps to the tcgen05 kernels (default) or to the chunk-16 kernels");
 }

@@ -1,0 +1,739 @@
+// WKV7 backward on tcgen05 (head size 64, chunks of 64 steps), the adjoint of wkv7_tc_fwd.cu, sm_100a.
+// The recurrence is RWKV7's (RWKV-LM, Apache-2.0; see NOTICE at the project root); this code is our own.
+//
+// With dS the gradient of a chunk's end state and dY of its outputs, the chunk-start gradient is
+//     dS0 = dS G^T + dY^T Q                       (G, Q from the forward records),
+// a serial scan over chunks (kernel 1). Per chunk, from the chunk-start state S0 (forward checkpoint), dS and
+// the stored T = (I - M_ab)^{-1}:
+//     U  = T (A~ S0^T + M_ak V)                    (the chunk's u_t = S_{t-1} a_t rows)
+//     dU = M_rb^T dY + B^ dS^T,  dZ = T^T dU,  dV = M_rk^T dY + K^ dS^T + M_ak^T dZ          (kernel 2)
+//     dM_ab = (dZ U^T) strict, dM_ak = (dZ V^T) strict, dM_rb = (dY U^T) incl, dM_rk = (dY V^T) incl
+//     dA~ = dZ S0 + dM_ab B~ + dM_ak K~,   dR~ = dY S0 + dM_rb B~ + dM_rk K~
+//     dB~ = dM_ab^T A~ + dM_rb^T R~ + E,   dK~ = dM_ak^T A~ + dM_rk^T R~ + F,   [E; F] = [U; V] dS diag(D_L)
+//                                                                                          (kernel 3)
+// and the raw gradients da = dA~ e^{Lambda_{t-1}}, dr = dR~ e^{Lambda_t}, db = dB~ e^{-Lambda_t},
+// dk = dK~ e^{-Lambda_t}; the decay gradient is the reverse cumulative sum over the chunk of
+//     dLambda_t = dr r - db b - dk k + (da a)_{t+1},   plus  sum_i dS S0 D_L + sum_s (E b~ + F k~)  at the end,
+// times d log d / dw = -e^{-1/2} sigmoid(w) (1 - sigmoid(w)). Every product is a tf32 MMA into TMEM; the
+// masks, transposes and the decay factors are applied by the threads that move tiles between TMEM and shared
+// memory. No atomics, fixed summation order (deterministic). Every wait is bounded.
+#include "wkv7_tc.cuh"
+#include "../common/tmap.cuh"
+
+namespace {
+
+using namespace wtc;
+constexpr int KB = 1024;
+constexpr int MAT = N * N;
+enum { REC_G = 0, REC_H0 = 1, REC_Q = 2, REC_Y0 = 3, REC_T = 4, REC_MATS = 5 };  // forward record (fwd file)
+enum { WK_DS = 0, WK_U = 1, WK_DZ = 2, WK_MATS = 3 };                             // backward work record
+
+__device__ int wkv7_tc_bwd_fault_word = 0;
+
+RT_DEVICE uint8_t* align1024(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+RT_DEVICE bool wait_all(uint64_t* bar, uint32_t parity) {
+  const bool ok = sm100::mbar_wait_bounded(bar, parity);
+  return __syncthreads_and(ok ? 1 : 0) != 0;
+}
+RT_DEVICE float bf(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+
+// Lambda (plain swizzled) from the raw w tile: columns split over two halves of 32 steps.
+RT_DEVICE void build_lambda(const uint8_t* Rw, float* lam, int nvalid, int tid) {
+  {
+    const int j = tid & 63, t0 = (tid >> 6) * 32;
+    float acc = 0.f;
+#pragma unroll 4
+    for (int u = 0; u < 32; ++u) {
+      const int t = t0 + u;
+      acc += t < nvalid ? -DECAY_SCALE * rt::sigmoidf_(raw(Rw, t, j)) : 0.f;
+      lam[poff(t, j)] = acc;
+    }
+  }
+  __syncthreads();
+  if (tid >= 64) {
+    const int j = tid - 64;
+    const float base = lam[poff(31, j)];
+    for (int t = 32; t < 64; ++t) lam[poff(t, j)] += base;
+  }
+  __syncthreads();
+}
+
+// Row `row` of a K-major tile of `rows` rows from 64 fp32 values in global memory (rounded to tf32).
+RT_DEVICE void tile_row_from_global(uint8_t* tile, int rows, int row, const float* src) {
+#pragma unroll 4
+  for (int k = 0; k < 64; k += 4) {
+    const float4 x = __ldg(reinterpret_cast<const float4*>(src + k));
+    put4(tile, rows, row, k, x.x, x.y, x.z, x.w);
+  }
+}
+
+// ---------------------------------------------------------------- 1: reverse scan dS <- dS G^T + dY^T Q
+// grid (B*H, 8 row blocks of 8 value rows), 128 threads: thread = column j and rows r0..r0+3 of the block.
+constexpr int BS_ROWS = 8;
+constexpr int GP = 68;  // padded row of G (conflict-free float4 reads of G[j][j'..j'+3] across j)
+constexpr int BSCAN_SMEM = (2 * 64 * GP + 2 * MAT + BS_ROWS * 64 + BS_ROWS * 64) * 4;
+__global__ void __launch_bounds__(128)
+wkv7_tc_bscan_kernel(const float* __restrict__ rec, const __nv_bfloat16* __restrict__ dy,
+                     const float* __restrict__ dend, float* __restrict__ work, float* __restrict__ ds0, int T, int H,
+                     int chunks) {
+  extern __shared__ __align__(16) float bsm[];
+  float* Gs = bsm;                     // [2][64][GP]
+  float* Qs = Gs + 2 * 64 * GP;        // [2][64][64]
+  float* dS = Qs + 2 * MAT;            // [8][64]
+  float* dYs = dS + BS_ROWS * 64;      // [64 t][8 rows]
+  const int bh = blockIdx.x, rb = blockIdx.y * BS_ROWS, tid = threadIdx.x;
+  const int b = bh / H, h = bh % H;
+  const int j = tid & 63, r0 = (tid >> 6) * 4;
+  const float* rec0 = rec + (long)bh * chunks * REC_MATS * MAT;
+  auto prefetch = [&](int c) {
+    const float* g = rec0 + (long)c * REC_MATS * MAT + REC_G * MAT;
+    const float* q = rec0 + (long)c * REC_MATS * MAT + REC_Q * MAT;
+    float* gd = Gs + (c & 1) * 64 * GP;
+    float* qd = Qs + (c & 1) * MAT;
+    for (int e = tid; e < MAT / 4; e += 128) {
+      rt::cp_async16(gd + (e >> 4) * GP + 4 * (e & 15), g + 4 * e, true);
+      rt::cp_async16(qd + 4 * e, q + 4 * e, true);
+    }
+    rt::cp_async_commit();
+  };
+  prefetch(chunks - 1);
+  float s[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    s[q] = dend[((long)bh * N + rb + r0 + q) * N + j];
+    dS[(r0 + q) * 64 + j] = s[q];
+  }
+#pragma unroll 1
+  for (int c = chunks - 1; c >= 0; --c) {
+    float* wk = work + ((long)bh * chunks + c) * WK_MATS * MAT + WK_DS * MAT;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) wk[(rb + r0 + q) * N + j] = s[q];
+    if (tid < 64) {  // dY rows t of this block's 8 value columns (one 16-byte load per step)
+      const int t = tid, tg = c * L + t;
+      float v[8];
+      if (tg < T) {
+        rt::unpack8(__ldg(reinterpret_cast<const uint4*>(dy + (((long)b * T + tg) * H + h) * N + rb)), v);
+      } else {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) dYs[t * 8 + u] = v[u];
+    }
+    rt::cp_async_wait<0>();
+    __syncthreads();  // G_c, Q_c landed; dS, dY visible; the other buffers are no longer read
+    if (c > 0) prefetch(c - 1);
+    const float* g = Gs + (c & 1) * 64 * GP;
+    const float* qm = Qs + (c & 1) * MAT;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+    for (int jp = 0; jp < 64; jp += 4) {
+      const float4 gv = *reinterpret_cast<const float4*>(g + j * GP + jp);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 sv = *reinterpret_cast<const float4*>(dS + (r0 + q) * 64 + jp);
+        acc[q] += sv.x * gv.x + sv.y * gv.y + sv.z * gv.z + sv.w * gv.w;
+      }
+    }
+#pragma unroll 4
+    for (int t = 0; t < 64; ++t) {
+      const float qv = qm[t * 64 + j];
+      const float4 d4 = *reinterpret_cast<const float4*>(dYs + t * 8 + r0);
+      acc[0] += d4.x * qv;
+      acc[1] += d4.y * qv;
+      acc[2] += d4.z * qv;
+      acc[3] += d4.w * qv;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      s[q] = acc[q];
+      dS[(r0 + q) * 64 + j] = s[q];
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < 4; ++q) ds0[((long)bh * N + rb + r0 + q) * N + j] = s[q];
+}
+
+// ---------------------------------------------------------------- 2: U, dZ, dV per chunk
+namespace ka {
+constexpr int RAW = 0;          // r, w, k, v, a, b, dY (8 KB each)
+constexpr int LAM = 56 * KB;
+constexpr int MISC = 72 * KB;
+constexpr int X1 = 73 * KB;     // [A~; R~]                     -> Zf^T (73..89), dU^T (89..105)
+constexpr int X2 = 105 * KB;    // [B~; K~] -> [M_rb^T; M_rk^T]  -> T^T (105..121)
+constexpr int VT = 137 * KB;    // V^T (64 rows)                 -> M_ak^T at 129..145 after MMA-Z
+constexpr int BKH = 153 * KB;   // [B^; K^] (128 rows)
+constexpr int DYT = 185 * KB;   // dY^T (64 rows)
+// after phase A (raw, Lambda dead): S0 (0..16), dS (16..32), T (32..48), M_ak (48..64; read as 128 rows)
+constexpr int SMEM = 201 * KB + 1024;
+}  // namespace ka
+
+__global__ void __launch_bounds__(128, 1)
+wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_constant__ CUtensorMap m_w,
+                         const __grid_constant__ CUtensorMap m_k, const __grid_constant__ CUtensorMap m_v,
+                         const __grid_constant__ CUtensorMap m_a, const __grid_constant__ CUtensorMap m_b,
+                         const __grid_constant__ CUtensorMap m_dy, const __grid_constant__ CUtensorMap m_t,
+                         const float* __restrict__ ckpt, float* __restrict__ work, float* __restrict__ dv, int T,
+                         int H, int chunks) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = align1024(smem_raw);
+  const int c = blockIdx.x, h = blockIdx.y, bb = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  uint8_t* Rr = sm + ka::RAW;
+  uint8_t *Rw = Rr + 8 * KB, *Rk = Rr + 16 * KB, *Rv = Rr + 24 * KB, *Ra = Rr + 32 * KB, *Rb = Rr + 40 * KB;
+  uint8_t* Rdy = Rr + 48 * KB;
+  float* lam = reinterpret_cast<float*>(sm + ka::LAM);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + ka::MISC);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + ka::MISC + 32);
+  uint8_t *X1 = sm + ka::X1, *X2 = sm + ka::X2, *VT = sm + ka::VT, *BKH = sm + ka::BKH, *DYT = sm + ka::DYT;
+  uint8_t *S0t = sm, *DSt = sm + 16 * KB, *Tt = sm + 32 * KB, *MAK = sm + 48 * KB;
+  uint8_t *MRT = X2, *ZFT = X1, *DUT = X1 + 16 * KB, *TTt = X2, *MAKT = sm + 129 * KB, *DZT = sm;
+  const long bh = (long)bb * H + h, ch = bh * chunks + c;
+  const float* S0g = ckpt + (bh * (chunks + 1) + c) * MAT;
+  float* wk = work + ch * WK_MATS * MAT;
+  const int nvalid = min(L, T - c * L);
+
+  if (tid == 0) {
+    sm100::mbar_init(&bars[0], 1);
+    sm100::mbar_init(&bars[1], 1);
+    sm100::mbar_init(&bars[2], 1);
+    sm100::fence_barrier_init();
+  }
+  if (warp == 0) {
+    sm100::tmem_alloc(tslot, 256);
+    sm100::tmem_relinquish();
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem = *tslot;
+  if (tid == 0) {
+    sm100::mbar_expect_tx(&bars[0], 7 * 8192);
+    const int x = h * N, y = c * L;
+    sm100::tma_load_3d(Rr, &m_r, &bars[0], x, y, bb);
+    sm100::tma_load_3d(Rw, &m_w, &bars[0], x, y, bb);
+    sm100::tma_load_3d(Rk, &m_k, &bars[0], x, y, bb);
+    sm100::tma_load_3d(Rv, &m_v, &bars[0], x, y, bb);
+    sm100::tma_load_3d(Ra, &m_a, &bars[0], x, y, bb);
+    sm100::tma_load_3d(Rb, &m_b, &bars[0], x, y, bb);
+    sm100::tma_load_3d(Rdy, &m_dy, &bars[0], x, y, bb);
+  }
+  bool ok = wait_all(&bars[0], 0);
+  const bool t_issued = ok;
+  uint32_t mph = 0;
+  if (ok) {
+    build_lambda(Rw, lam, nvalid, tid);
+    {  // X1 (A~ / R~), X2 (B~ / K~), BKH (B^ / K^): row tid
+      const int t = tid & 63;
+      const bool hi = tid >= 64;
+      const uint8_t* s1 = hi ? Rr : Ra;
+      const uint8_t* s2 = hi ? Rk : Rb;
+#pragma unroll 1
+      for (int j0 = 0; j0 < 64; j0 += 4) {
+        float x1[4], xb[4], xh[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int j = j0 + q;
+          const float lt = lam[poff(t, j)], lL = lam[poff(63, j)];
+          const float lp = (!hi && t > 0) ? lam[poff(t - 1, j)] : 0.f;
+          const float x2 = raw(s2, t, j);
+          x1[q] = raw(s1, t, j) * expf(hi ? lt : lp);
+          xb[q] = x2 * expf(-lt);
+          xh[q] = x2 * expf(lL - lt);
+        }
+        put4(X1, 128, tid, j0, x1[0], x1[1], x1[2], x1[3]);
+        put4(X2, 128, tid, j0, xb[0], xb[1], xb[2], xb[3]);
+        put4(BKH, 128, tid, j0, xh[0], xh[1], xh[2], xh[3]);
+      }
+    }
+    {  // V^T (row i < 64), dY^T (row i, threads 64..127)
+      const int i = tid & 63;
+      uint8_t* dst = tid < 64 ? VT : DYT;
+      const uint8_t* src = tid < 64 ? Rv : Rdy;
+#pragma unroll 1
+      for (int s = 0; s < 64; s += 4)
+        put4(dst, 64, i, s, raw(src, s, i), raw(src, s + 1, i), raw(src, s + 2, i), raw(src, s + 3, i));
+    }
+    tc_sync();
+    // ---- MMA1 (cols 0..127): chunk matrices
+    if (tid == 0) {
+      mma_tf32_tiles(tmem, sm100::smem_u32(X1), 128, sm100::smem_u32(X2), 128, 8, sm100::idesc_tf32(128, 128),
+                     false);
+      sm100::mma_commit(&bars[1]);
+    }
+    // raw tiles and Lambda are dead: S0 and dS rows (rounded) by the threads, T by TMA
+    if (tid == 0) {
+      sm100::mbar_expect_tx(&bars[2], 16 * KB);
+      const int trow = (int)((ch * REC_MATS + REC_T) * N);
+      sm100::tma_load_2d(Tt, &m_t, &bars[2], 0, trow);
+      sm100::tma_load_2d(Tt + 8 * KB, &m_t, &bars[2], 32, trow);
+    }
+    if (tid < 64) tile_row_from_global(S0t, 64, tid, S0g + tid * N);
+    else tile_row_from_global(DSt, 64, tid - 64, wk + WK_DS * MAT + (tid - 64) * N);
+    ok = wait_all(&bars[1], mph);
+    mph ^= 1;
+    sm100::tc_fence_after();
+  }
+  if (ok) {
+    // ---- epilogue 1: M_ak (strict) -> MAK rows; [M_rb^T; M_rk^T] -> MRT (transposed, from rows t >= 64)
+    float d[64];
+    const int t = tid & 63;
+    if (tid < 64) {
+      tmem_row64(tmem, warp, 64, d);
+#pragma unroll
+      for (int s = 0; s < 64; s += 4)
+        put4(MAK, 64, t, s, s < t ? d[s] : 0.f, s + 1 < t ? d[s + 1] : 0.f, s + 2 < t ? d[s + 2] : 0.f,
+             s + 3 < t ? d[s + 3] : 0.f);
+    } else {
+      tmem_row64(tmem, warp, 0, d);
+#pragma unroll
+      for (int s = 0; s < 64; ++s) put1(MRT, 128, s, t, s <= t ? d[s] : 0.f);
+      tmem_row64(tmem, warp, 64, d);
+#pragma unroll
+      for (int s = 0; s < 64; ++s) put1(MRT, 128, 64 + s, t, s <= t ? d[s] : 0.f);
+    }
+    tc_sync();
+    // ---- MMA-Z (cols 128..191): [A~ S0^T + M_ak V; *];  MMA-dU (cols 192..255): [dU; dV'] =
+    //      [M_rb^T; M_rk^T] dY + [B^; K^] dS^T
+    if (tid == 0) {
+      mma_tf32_tiles(tmem + 128, sm100::smem_u32(X1), 128, sm100::smem_u32(S0t), 64, 8, sm100::idesc_tf32(128, 64),
+                     false);
+      mma_tf32_tiles(tmem + 128, sm100::smem_u32(MAK), 64, sm100::smem_u32(VT), 64, 8, sm100::idesc_tf32(128, 64),
+                     true);
+      mma_tf32_tiles(tmem + 192, sm100::smem_u32(MRT), 128, sm100::smem_u32(DYT), 64, 8, sm100::idesc_tf32(128, 64),
+                     false);
+      mma_tf32_tiles(tmem + 192, sm100::smem_u32(BKH), 128, sm100::smem_u32(DSt), 64, 8, sm100::idesc_tf32(128, 64),
+                     true);
+      sm100::mma_commit(&bars[1]);
+    }
+    ok = wait_all(&bars[1], mph) && wait_all(&bars[2], 0);
+    mph ^= 1;
+    sm100::tc_fence_after();
+  }
+  if (ok) {
+    // ---- epilogue 2: Z^T and dU^T (transposed, rows t < 64); T^T and M_ak^T (threads 64..127, from smem/TMEM)
+    if (tid < 64) {
+      float d[64];
+      tmem_row64(tmem, warp, 128, d);
+#pragma unroll
+      for (int i = 0; i < 64; ++i) put1(ZFT, 64, i, tid, d[i]);
+      tmem_row64(tmem, warp, 192, d);
+#pragma unroll
+      for (int i = 0; i < 64; ++i) put1(DUT, 64, i, tid, d[i]);
+      tmem_row64(tmem, warp, 64, d);  // M_ak row t (still in TMEM) -> M_ak^T column t
+#pragma unroll
+      for (int s = 0; s < 64; ++s) put1(MAKT, 64, s, tid, s < tid ? d[s] : 0.f);
+    } else {
+      const int s = tid - 64;  // T^T row s = column s of T
+#pragma unroll 1
+      for (int t0 = 0; t0 < 64; t0 += 4)
+        put4(TTt, 64, s, t0, get1(Tt, 64, t0, s), get1(Tt, 64, t0 + 1, s), get1(Tt, 64, t0 + 2, s),
+             get1(Tt, 64, t0 + 3, s));
+    }
+    tc_sync();
+    // ---- MMA-U (cols 64..127): U = T Z;  MMA-dZ (cols 0..63): dZ = T^T dU  (64-row operands read as 128 rows)
+    if (tid == 0) {
+      mma_tf32_tiles(tmem + 64, sm100::smem_u32(Tt), 64, sm100::smem_u32(ZFT), 64, 8, sm100::idesc_tf32(128, 64),
+                     false);
+      mma_tf32_tiles(tmem, sm100::smem_u32(TTt), 64, sm100::smem_u32(DUT), 64, 8, sm100::idesc_tf32(128, 64), false);
+      sm100::mma_commit(&bars[1]);
+    }
+    ok = wait_all(&bars[1], mph);
+    mph ^= 1;
+    sm100::tc_fence_after();
+  }
+  if (ok) {
+    // ---- epilogue 3: U and dZ rows (tf32) to the work record; dZ^T for dV
+    if (tid < 64) {
+      float d[64];
+      tmem_row64(tmem, warp, 0, d);
+      float* gz = wk + WK_DZ * MAT + tid * N;
+#pragma unroll
+      for (int i = 0; i < 64; i += 4)
+        *reinterpret_cast<float4*>(gz + i) = make_float4(tf32r(d[i]), tf32r(d[i + 1]), tf32r(d[i + 2]), tf32r(d[i + 3]));
+#pragma unroll
+      for (int i = 0; i < 64; ++i) put1(DZT, 64, i, tid, d[i]);
+      tmem_row64(tmem, warp, 64, d);
+      float* gu = wk + WK_U * MAT + tid * N;
+#pragma unroll
+      for (int i = 0; i < 64; i += 4)
+        *reinterpret_cast<float4*>(gu + i) = make_float4(tf32r(d[i]), tf32r(d[i + 1]), tf32r(d[i + 2]), tf32r(d[i + 3]));
+    }
+    tc_sync();
+    // ---- MMA-dV (cols 192..255, rows 64..127): dV += M_ak^T dZ  (M_ak^T read as the lower half of 128 rows)
+    if (tid == 0) {
+      mma_tf32_tiles(tmem + 192, sm100::smem_u32(MAKT) - 8192, 64, sm100::smem_u32(DZT), 64, 8,
+                     sm100::idesc_tf32(128, 64), true);
+      sm100::mma_commit(&bars[1]);
+    }
+    ok = wait_all(&bars[1], mph);
+    mph ^= 1;
+    sm100::tc_fence_after();
+  }
+  if (ok && tid >= 64) {  // dV rows s
+    const int s = tid - 64, tg = c * L + s;
+    if (s < nvalid) {
+      float d[64];
+      tmem_row64(tmem, warp, 192, d);
+      float* out = dv + (((long)bb * T + tg) * H + h) * N;
+#pragma unroll
+      for (int i = 0; i < 64; i += 4) *reinterpret_cast<float4*>(out + i) = make_float4(d[i], d[i + 1], d[i + 2], d[i + 3]);
+    }
+  }
+  if (!ok && tid == 0) atomicExch(&wkv7_tc_bwd_fault_word, 1);
+  if (!ok) {
+    sm100::mbar_wait_bounded(&bars[1], mph);
+    if (t_issued) sm100::mbar_wait_bounded(&bars[2], 0);
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem, 256);
+  }
+}
+
+// ---------------------------------------------------------------- 3: input gradients per chunk
+namespace kb {
+constexpr int RAW = 0;          // r, w, k, v, a, b, dY; later S0^T (0..16), (dS D_L)^T (16..32); then P/Q arrays
+constexpr int LAM = 56 * KB;
+constexpr int MISC = 72 * KB;
+constexpr int DZY = 73 * KB;    // [dZ; dY] (128 rows, K = i)  -> stage tiles
+constexpr int UV = 105 * KB;    // [U; V]   (128 rows, K = i)  -> stage tiles
+constexpr int X1T = 137 * KB;   // [A~^T | R~^T] (64 rows j, K = 128) -> E arrays
+constexpr int X2T = 169 * KB;   // [B~^T | K~^T]
+constexpr int SMEM = 201 * KB + 1024;
+}  // namespace kb
+
+__global__ void __launch_bounds__(128, 1)
+wkv7_tc_bwd_grad_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_constant__ CUtensorMap m_w,
+                        const __grid_constant__ CUtensorMap m_k, const __grid_constant__ CUtensorMap m_v,
+                        const __grid_constant__ CUtensorMap m_a, const __grid_constant__ CUtensorMap m_b,
+                        const __grid_constant__ CUtensorMap m_dy, const __grid_constant__ CUtensorMap m_wk,
+                        const __nv_bfloat16* __restrict__ pr, const __nv_bfloat16* __restrict__ pw,
+                        const __nv_bfloat16* __restrict__ pk, const __nv_bfloat16* __restrict__ pa,
+                        const __nv_bfloat16* __restrict__ pb, const float* __restrict__ ckpt,
+                        const float* __restrict__ work, float* __restrict__ dr, float* __restrict__ dw,
+                        float* __restrict__ dk, float* __restrict__ da, float* __restrict__ db, int T, int H,
+                        int chunks) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = align1024(smem_raw);
+  const int c = blockIdx.x, h = blockIdx.y, bb = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  uint8_t* Rr = sm + kb::RAW;
+  uint8_t *Rw = Rr + 8 * KB, *Rk = Rr + 16 * KB, *Rv = Rr + 24 * KB, *Ra = Rr + 32 * KB, *Rb = Rr + 40 * KB;
+  uint8_t* Rdy = Rr + 48 * KB;
+  float* lam = reinterpret_cast<float*>(sm + kb::LAM);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kb::MISC);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + kb::MISC + 32);
+  float* DL = reinterpret_cast<float*>(sm + kb::MISC + 64);
+  float* colsum = DL + 64;  // [64]: sum_i dS S0 D_L + sum_s (E b~ + F k~), per key
+  uint8_t *DZY = sm + kb::DZY, *UV = sm + kb::UV, *X1T = sm + kb::X1T, *X2T = sm + kb::X2T;
+  uint8_t *S0T = sm, *DST = sm + 16 * KB;
+  uint8_t *SA = DZY, *SB = UV;  // stage tiles (32 KB each)
+  float* PA = reinterpret_cast<float*>(sm);            // dr r - dk k          (rows of the r~ / k~ half)
+  float* PB = PA + MAT;                                 // -db b                (rows of the a~ / b~ half)
+  float* QA = PB + MAT;                                 // da a
+  float* EA = reinterpret_cast<float*>(sm + kb::X1T);  // E b~
+  float* EB = EA + MAT;                                 // F k~
+  const long bh = (long)bb * H + h, ch = bh * chunks + c;
+  const float* S0g = ckpt + (bh * (chunks + 1) + c) * MAT;
+  const float* wk = work + ch * WK_MATS * MAT;
+  const int nvalid = min(L, T - c * L);
+
+  if (tid == 0) {
+    for (int i = 0; i < 3; ++i) sm100::mbar_init(&bars[i], 1);
+    sm100::fence_barrier_init();
+  }
+  if (warp == 0) {
+    sm100::tmem_alloc(tslot, 512);
+    sm100::tmem_relinquish();
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem = *tslot;
+  if (tid == 0) {
+    sm100::mbar_expect_tx(&bars[0], 7 * 8192 + 32 * KB);
+    const int x = h * N, y = c * L;
+    sm100::tma_load_3d(Rr, &m_r, &bars[0], x, y, bb);
+    sm100::tma_load_3d(Rw, &m_w, &bars[0], x, y, bb);
+    sm100::tma_load_3d(Rk, &m_k, &bars[0], x, y, bb);
+    sm100::tma_load_3d(Rv, &m_v, &bars[0], x, y, bb);
+    sm100::tma_load_3d(Ra, &m_a, &bars[0], x, y, bb);
+    sm100::tma_load_3d(Rb, &m_b, &bars[0], x, y, bb);
+    sm100::tma_load_3d(Rdy, &m_dy, &bars[0], x, y, bb);
+    const int zrow = (int)((ch * WK_MATS + WK_DZ) * N), urow = (int)((ch * WK_MATS + WK_U) * N);
+    for (int a = 0; a < 2; ++a) {  // top halves (rows 0..63) of the two 128-row operands
+      sm100::tma_load_2d(DZY + a * 16 * KB, &m_wk, &bars[0], 32 * a, zrow);
+      sm100::tma_load_2d(UV + a * 16 * KB, &m_wk, &bars[0], 32 * a, urow);
+    }
+  }
+  bool ok = wait_all(&bars[0], 0);
+  uint32_t mph = 0;
+  bool second_issued = false;
+  if (ok) {
+    // ---- dY and V rows into the lower halves; the dM product can start
+    {
+      const int t = tid & 63;
+      uint8_t* dst = tid < 64 ? DZY : UV;
+      const uint8_t* src = tid < 64 ? Rdy : Rv;
+#pragma unroll 1
+      for (int i = 0; i < 64; i += 8) {
+        float x[8];
+        raw8(src, t, i, x);
+        put4(dst, 128, 64 + t, i, x[0], x[1], x[2], x[3]);
+        put4(dst, 128, 64 + t, i + 4, x[4], x[5], x[6], x[7]);
+      }
+    }
+    tc_sync();
+    if (tid == 0) {  // dM block (cols 0..127) = [dZ; dY] [U; V]^T
+      mma_tf32_tiles(tmem, sm100::smem_u32(DZY), 128, sm100::smem_u32(UV), 128, 8, sm100::idesc_tf32(128, 128),
+                     false);
+      sm100::mma_commit(&bars[1]);
+    }
+    build_lambda(Rw, lam, nvalid, tid);
+    if (tid < 64) DL[tid] = expf(lam[poff(63, tid)]);
+    // X1T row j: A~[t][j] (k = t), R~[t][j] (k = 64 + t); X2T row j: B~ / K~ (column owners)
+    {
+      const int j = tid & 63;
+      uint8_t* dst = tid < 64 ? X1T : X2T;
+      const uint8_t* s1 = tid < 64 ? Ra : Rb;
+      const uint8_t* s2 = tid < 64 ? Rr : Rk;
+#pragma unroll 1
+      for (int t = 0; t < 64; t += 4) {
+        float x1[4], x2[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int tt = t + q;
+          const float lt = lam[poff(tt, j)];
+          if (tid < 64) {
+            const float lp = tt ? lam[poff(tt - 1, j)] : 0.f;
+            x1[q] = raw(s1, tt, j) * expf(lp);
+            x2[q] = raw(s2, tt, j) * expf(lt);
+          } else {
+            x1[q] = raw(s1, tt, j) * expf(-lt);
+            x2[q] = raw(s2, tt, j) * expf(-lt);
+          }
+        }
+        put4(dst, 64, j, t, x1[0], x1[1], x1[2], x1[3]);
+        put4(dst, 64, j, 64 + t, x2[0], x2[1], x2[2], x2[3]);
+      }
+    }
+    __syncthreads();  // raw tiles dead from here on
+    {  // S0^T (row j = tid < 64, K = i) and (dS D_L)^T (row j, threads 64..127): column loads from global
+      const int j = tid & 63;
+      const float* src = tid < 64 ? S0g : wk + WK_DS * MAT;
+      uint8_t* dst = tid < 64 ? S0T : DST;
+      const float sc = tid < 64 ? 1.f : DL[j];
+#pragma unroll 1
+      for (int i = 0; i < 64; i += 4)
+        put4(dst, 64, j, i, src[i * N + j] * sc, src[(i + 1) * N + j] * sc, src[(i + 2) * N + j] * sc,
+             src[(i + 3) * N + j] * sc);
+    }
+    tc_sync();
+    if (tid == 0) {  // [dZ S0; dY S0] (cols 128..191) and [E; F] = [U; V] (dS D_L) (cols 256..319)
+      mma_tf32_tiles(tmem + 128, sm100::smem_u32(DZY), 128, sm100::smem_u32(S0T), 64, 8, sm100::idesc_tf32(128, 64),
+                     false);
+      mma_tf32_tiles(tmem + 256, sm100::smem_u32(UV), 128, sm100::smem_u32(DST), 64, 8, sm100::idesc_tf32(128, 64),
+                     false);
+      sm100::mma_commit(&bars[2]);  // own barrier: both commits may complete before either wait
+    }
+    second_issued = true;
+    ok = wait_all(&bars[1], mph);  // dM
+    mph ^= 1;
+    if (ok) ok = wait_all(&bars[2], 0);  // S0 and dS products (DZY, UV, S0^T, dS^T free after this)
+    sm100::tc_fence_after();
+  }
+  // dM stage tiles. Stage 1: SA = [dM_ab; dM_rb] (rows t, K = s), SB = [dM_ab^T; dM_ak^T] (rows s, K = t).
+  //                 Stage 2: SA = [dM_ak; dM_rk],               SB = [dM_rb^T; dM_rk^T].
+#pragma unroll 1
+  for (int stage = 0; stage < 2 && ok; ++stage) {
+    {
+      float d[64];
+      const int t = tid & 63;
+      const int lim = tid < 64 ? t : t + 1;  // strict for the a~ rows, inclusive for the r~ rows
+      if (stage == 0) {
+        tmem_row64(tmem, warp, 0, d);  // dM_ab (t < 64) / dM_rb
+#pragma unroll
+        for (int s = 0; s < 64; s += 4)
+          put4(SA, 128, tid, s, s < lim ? d[s] : 0.f, s + 1 < lim ? d[s + 1] : 0.f, s + 2 < lim ? d[s + 2] : 0.f,
+               s + 3 < lim ? d[s + 3] : 0.f);
+        if (tid < 64) {
+#pragma unroll
+          for (int s = 0; s < 64; ++s) put1(SB, 128, s, t, s < lim ? d[s] : 0.f);
+          tmem_row64(tmem, warp, 64, d);  // dM_ak
+#pragma unroll
+          for (int s = 0; s < 64; ++s) put1(SB, 128, 64 + s, t, s < lim ? d[s] : 0.f);
+        }
+      } else {
+        tmem_row64(tmem, warp, 64, d);  // dM_ak / dM_rk
+#pragma unroll
+        for (int s = 0; s < 64; s += 4)
+          put4(SA, 128, tid, s, s < lim ? d[s] : 0.f, s + 1 < lim ? d[s + 1] : 0.f, s + 2 < lim ? d[s + 2] : 0.f,
+               s + 3 < lim ? d[s + 3] : 0.f);
+        if (tid >= 64) {
+#pragma unroll
+          for (int s = 0; s < 64; ++s) put1(SB, 128, 64 + s, t, s < lim ? d[s] : 0.f);
+          tmem_row64(tmem, warp, 0, d);  // dM_rb
+#pragma unroll
+          for (int s = 0; s < 64; ++s) put1(SB, 128, s, t, s < lim ? d[s] : 0.f);
+        }
+      }
+    }
+    tc_sync();
+    if (tid == 0) {
+      // [dA~; dR~] += SA . (B~^T | K~^T);  [dB~; dK~] (cols 192..255) (+)= SB . (A~^T | R~^T)
+      mma_tf32_tiles(tmem + 128, sm100::smem_u32(SA), 128, sm100::smem_u32(X2T) + stage * 16 * KB, 64, 8,
+                     sm100::idesc_tf32(128, 64), true);
+      mma_tf32_tiles(tmem + 192, sm100::smem_u32(SB), 128, sm100::smem_u32(X1T) + stage * 16 * KB, 64, 8,
+                     sm100::idesc_tf32(128, 64), stage > 0);
+      sm100::mma_commit(&bars[1]);
+    }
+    ok = wait_all(&bars[1], mph);
+    mph ^= 1;
+    sm100::tc_fence_after();
+  }
+  if (ok) {
+    // ---- row epilogue: raw gradients and the dLambda terms (thread = row t of its half)
+    const int t = tid & 63, tg = c * L + t;
+    const bool lo = tid < 64;  // rows of a~ / b~ (da, db) vs r~ / k~ (dr, dk)
+    const bool valid = tg < T;
+    const long go = (((long)bb * T + (valid ? tg : 0)) * H + h) * N;
+    const uint32_t row = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
+#pragma unroll 1
+    for (int half = 0; half < 2; ++half) {
+      float d1[32], d2[32], d3[32];
+      sm100::tmem_ld32(row + 128 + 32 * half, d1);  // dA~ / dR~
+      sm100::tmem_ld32(row + 192 + 32 * half, d2);  // dB~' / dK~'
+      sm100::tmem_ld32(row + 256 + 32 * half, d3);  // E / F
+      sm100::tmem_wait_ld();
+#pragma unroll 4
+      for (int u = 0; u < 32; ++u) {
+        const int j = 32 * half + u;
+        const float lt = lam[poff(t, j)];
+        if (lo) {
+          const float lp = t ? lam[poff(t - 1, j)] : 0.f;
+          const float av = valid ? bf(pa + go + j) : 0.f, bv = valid ? bf(pb + go + j) : 0.f;
+          const float gda = d1[u] * expf(lp);
+          const float gdb = (d2[u] + d3[u]) * expf(-lt);
+          QA[poff(t, j)] = gda * av;
+          PB[poff(t, j)] = -gdb * bv;
+          EA[poff(t, j)] = d3[u] * bv * expf(-lt);  // E b~ (E carries D_L)
+          if (valid) {
+            da[go + j] = gda;
+            db[go + j] = gdb;
+          }
+        } else {
+          const float rv = valid ? bf(pr + go + j) : 0.f, kv = valid ? bf(pk + go + j) : 0.f;
+          const float gdr = d1[u] * expf(lt);
+          const float gdk = (d2[u] + d3[u]) * expf(-lt);
+          PA[poff(t, j)] = gdr * rv - gdk * kv;
+          EB[poff(t, j)] = d3[u] * kv * expf(-lt);  // F k~
+          if (valid) {
+            dr[go + j] = gdr;
+            dk[go + j] = gdk;
+          }
+        }
+      }
+    }
+    __syncthreads();
+    // ---- column pass: key j. Threads 64..127: the chunk-end terms; threads 0..63: the reverse scan.
+    if (tid >= 64) {
+      const int j = tid - 64;
+      const float* dS = wk + WK_DS * MAT;
+      float acc = 0.f;
+      for (int i = 0; i < 64; ++i) acc += dS[i * N + j] * S0g[i * N + j];
+      acc *= DL[j];
+      for (int s = 0; s < 64; ++s) acc += EA[poff(s, j)] + EB[poff(s, j)];
+      colsum[j] = acc;
+    }
+    __syncthreads();
+    if (tid < 64) {
+      const int j = tid;
+      float acc = colsum[j];
+      for (int tt = 63; tt >= 0; --tt) {
+        acc += PA[poff(tt, j)] + PB[poff(tt, j)] + (tt < 63 ? QA[poff(tt + 1, j)] : 0.f);
+        const int tgg = c * L + tt;
+        if (tgg < T) {
+          const long o = (((long)bb * T + tgg) * H + h) * N + j;
+          const float sg = rt::sigmoidf_(bf(pw + o));
+          dw[o] = acc * (-DECAY_SCALE) * sg * (1.f - sg);
+        }
+      }
+    }
+  }
+  if (!ok && tid == 0) atomicExch(&wkv7_tc_bwd_fault_word, 1);
+  if (!ok) {
+    sm100::mbar_wait_bounded(&bars[1], mph);
+    if (second_issued) sm100::mbar_wait_bounded(&bars[2], 0);
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem, 512);
+  }
+}
+
+bool input_map(CUtensorMap* m, const void* base, int B, int T, int H) {
+  const uint64_t dims[3] = {(uint64_t)H * N, (uint64_t)T, (uint64_t)B};
+  const uint64_t strides[2] = {(uint64_t)H * N * 2, (uint64_t)T * H * N * 2};
+  const uint32_t box[3] = {64, 64, 1};
+  return tmap::encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box);
+}
+
+bool fp32_rows_map(CUtensorMap* m, const float* base, long rows) {
+  const uint64_t dims[2] = {64, (uint64_t)rows};
+  const uint64_t strides[1] = {64 * 4};
+  const uint32_t box[2] = {32, 64};
+  return tmap::encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box);
+}
+
+}  // namespace
+
+extern "C" long rt_wkv7_tc_backward_workspace_floats(int B, int T, int H) {
+  const long chunks = (T + L - 1) / L;
+  return chunks * B * H * WK_MATS * MAT;
+}
+
+// 1 if a tcgen05 WKV7 backward kernel gave up a bounded wait since the last call (synchronizes the device).
+extern "C" int rt_wkv7_tc_bwd_fault() {
+  int v = 0, zero = 0;
+  if (cudaMemcpyFromSymbol(&v, wkv7_tc_bwd_fault_word, sizeof(int)) != cudaSuccess) return -1;
+  if (v) cudaMemcpyToSymbol(wkv7_tc_bwd_fault_word, &zero, sizeof(int));
+  return v;
+}
+
+// Gradients (fp32 [B, T, H, 64]) of the tcgen05 forward; ckpt and rec as written by rt_wkv7_tc_forward; dy bf16.
+extern "C" cudaError_t rt_wkv7_tc_backward(int B, int T, int H, const void* r, const void* w, const void* k,
+                                           const void* v, const void* a, const void* b, const float* ckpt,
+                                           const float* rec, const void* dy, const float* dend, float* dr, float* dw,
+                                           float* dk, float* dv, float* da, float* db, float* ds0, float* work,
+                                           cudaStream_t stream) {
+  if (B <= 0 || T <= 0 || H <= 0) return cudaErrorInvalidValue;
+  const int chunks = (T + L - 1) / L;
+  CUtensorMap mr, mw, mk, mv, ma, mb, mdy, mt, mwk;
+  bool ok = input_map(&mr, r, B, T, H) && input_map(&mw, w, B, T, H) && input_map(&mk, k, B, T, H) &&
+            input_map(&mv, v, B, T, H) && input_map(&ma, a, B, T, H) && input_map(&mb, b, B, T, H) &&
+            input_map(&mdy, dy, B, T, H);
+  ok = ok && fp32_rows_map(&mt, rec, (long)B * H * chunks * REC_MATS * N) &&
+       fp32_rows_map(&mwk, work, (long)B * H * chunks * WK_MATS * N);
+  if (!ok) return cudaErrorInvalidValue;
+  RT_CUDA_CHECK(cudaFuncSetAttribute(wkv7_tc_bscan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BSCAN_SMEM));
+  wkv7_tc_bscan_kernel<<<dim3(B * H, N / BS_ROWS), 128, BSCAN_SMEM, stream>>>(
+      rec, (const __nv_bfloat16*)dy, dend, work, ds0, T, H, chunks);
+  RT_CUDA_CHECK(cudaGetLastError());
+  RT_CUDA_CHECK(cudaFuncSetAttribute(wkv7_tc_bwd_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ka::SMEM));
+  wkv7_tc_bwd_state_kernel<<<dim3(chunks, H, B), 128, ka::SMEM, stream>>>(mr, mw, mk, mv, ma, mb, mdy, mt, ckpt, work,
+                                                                          dv, T, H, chunks);
+  RT_CUDA_CHECK(cudaGetLastError());
+  RT_CUDA_CHECK(cudaFuncSetAttribute(wkv7_tc_bwd_grad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kb::SMEM));
+  wkv7_tc_bwd_grad_kernel<<<dim3(chunks, H, B), 128, kb::SMEM, stream>>>(
+      mr, mw, mk, mv, ma, mb, mdy, mwk, (const __nv_bfloat16*)r, (const __nv_bfloat16*)w, (const __nv_bfloat16*)k,
+      (const __nv_bfloat16*)a, (const __nv_bfloat16*)b, ckpt, work, dr, dw, dk, da, db, T, H, chunks);
+  return cudaGetLastError();
+}

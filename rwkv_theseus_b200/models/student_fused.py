@@ -152,7 +152,7 @@ class FusedStudent:
                        w_in, k_in, a_in, b_in, H, N)
         shape = (B, T, H, N)
         wkv_in = [t.view(shape) for t in (r, w_in, k_in, v, a_in, b_in)]
-        y, end, ckpt = ext.wkv7_forward(*wkv_in, wkv0, keep)
+        y, end, ckpt, rec = ext.wkv7_forward(*wkv_in, wkv0, keep)
         yg = torch.empty_like(r)
         gn = torch.empty(M * H * 3, device=x.device)
         ext.tm_post_wkv(y, r, k_in, v, g, self.p("ln_x.weight"), self.p("ln_x.bias"), self.p("r_k"), yg, gn, H, N)
@@ -161,7 +161,7 @@ class FusedStudent:
         saved = None
         if keep:
             saved = dict(x=x, shift=shift, mix=mix, r=r, k=k, v=v, hw=hw, ha=ha, hg=hg, lw=lw, la=la, g=g,
-                         w_in=w_in, k_in=k_in, a_in=a_in, b_in=b_in, y=y, ckpt=ckpt, yg=yg, gn=gn)
+                         w_in=w_in, k_in=k_in, a_in=a_in, b_in=b_in, y=y, ckpt=ckpt, rec=rec, yg=yg, gn=gn)
         return pred, new_state, saved
 
     @torch.no_grad()
@@ -213,7 +213,7 @@ class FusedStudent:
         shape = (B, T, H, N)
         wkv_in = [s[n].view(shape) for n in ("r", "w_in", "k_in", "v", "a_in", "b_in")]
         dend = torch.zeros(B, H, N, N, device=x.device)
-        gw = ext.wkv7_backward(*wkv_in, s["ckpt"], dy.view(shape), dend)
+        gw = ext.wkv7_backward(*wkv_in, s["ckpt"], s["rec"], dy.view(shape), dend)
         dr, dk, dv, dlw, dla = (torch.empty_like(pred) for _ in range(5))
         ext.tm_pre_wkv_bwd(list(gw[:6]), bonus, s["k"], s["la"], self.p("w0"), self.p("a0"), self.p("k_k"),
                            self.p("k_a"), [dr, dk, dv, dlw, dla],
@@ -307,7 +307,7 @@ class FusedTimeMixInference:
         V = self.vec
         ext.tm_pre_wkv(k, lw, la, V["w0"], V["a0"], V["k_k"], V["k_a"], w_in, k_in, a_in, b_in, H, N)
         shape = (B, T, H, N)
-        y, end, _ = ext.wkv7_forward(*[t.view(shape) for t in (r, w_in, k_in, v, a_in, b_in)], wkv0, False)
+        y, end, _, _ = ext.wkv7_forward(*[t.view(shape) for t in (r, w_in, k_in, v, a_in, b_in)], wkv0, False)
         yg = torch.empty_like(r)
         gn = torch.empty(M * H * 3, device=x.device)
         ext.tm_post_wkv(y, r, k_in, v, g, self.ln_w, self.ln_b, V["r_k"], yg, gn, H, N)

@@ -63,18 +63,19 @@ class _WKV7(torch.autograd.Function):
     def forward(ctx, r, w, k, v, a, b, s0):
         xs = [x.contiguous() for x in (r, w, k, v, a, b)]
         s0 = s0.float().contiguous()
-        y, end, checkpoints = native().wkv7_forward(*xs, s0, True)
-        ctx.save_for_backward(*xs, checkpoints)
+        y, end, checkpoints, records = native().wkv7_forward(*xs, s0, True)
+        ctx.save_for_backward(*xs, checkpoints, records)
         return y, end
 
     @staticmethod
     def backward(ctx, dy, dend):
-        *xs, checkpoints = ctx.saved_tensors
+        *xs, checkpoints, records = ctx.saved_tensors
         if dy is None:
             dy = torch.zeros_like(xs[0])
         if dend is None:
             dend = torch.zeros_like(checkpoints[:, :, 0])
-        grads = native().wkv7_backward(*xs, checkpoints, dy.contiguous(), dend.float().contiguous())
+        grads = native().wkv7_backward(*xs, checkpoints, records, dy.to(xs[0].dtype).contiguous(),
+                                       dend.float().contiguous())
         return tuple(g.to(x.dtype) for g, x in zip(grads[:6], xs)) + (grads[6],)
 
 
@@ -90,6 +91,6 @@ def wkv7(r, w, k, v, a, b, state, backend="cuda"):
     needs_grad = torch.is_grad_enabled() and any(x.requires_grad for x in (r, w, k, v, a, b, state))
     if not needs_grad:
         xs = [x.contiguous() for x in (r, w, k, v, a, b)]
-        y, end, _ = native().wkv7_forward(*xs, state.float().contiguous(), False)
+        y, end, _, _ = native().wkv7_forward(*xs, state.float().contiguous(), False)
         return y, end
     return _WKV7.apply(r, w, k, v, a, b, state)
