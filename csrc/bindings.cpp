@@ -577,7 +577,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_open", &ipc_open);
   m.def("ipc_close", &ipc_close);
   m.def("wkv7_chunk_len", []() { return rt_wkv7_chunk_len(); });
-  m.def("wkv7_tc_fault", []() { return rt_wkv7_tc_fault() | rt_wkv7_tc_bwd_fault(); },
+  m.def("wkv7_tc_fault", []() { return rt_wkv7_tc_fault() | (rt_wkv7_tc_bwd_fault() << 12); },
         "1 if a tcgen05 WKV7 kernel gave up a bounded wait since the last call (synchronizes)");
   m.def("wkv7_tc_enable", [](bool on) { g_wkv7_tc_enabled = on; },
         "route bf16 head-64 calls of >= 128 steps to the tcgen05 kernels (default) or to the chunk-16 kernels");

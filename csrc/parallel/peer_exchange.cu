@@ -34,7 +34,10 @@ namespace {
 
 using bf16 = __nv_bfloat16;
 constexpr int MAXR = 8;
-constexpr int THREADS = 512;
+// Small blocks with capped registers: every exchange kernel fits on an SM beside one persistent tcgen05 GEMM CTA
+// (192 threads, <= 152 registers, <= 195 KB of shared memory), so an exchange running on the side stream under the
+// next layer's GEMMs never holds an SM that a GEMM CTA waits for.
+constexpr int THREADS = 128;
 constexpr int THREADS_B = 256;  // update kernel: 4x the grid of the copy kernels
 
 // Signal-buffer layout (32-bit words) of every rank.
@@ -98,7 +101,7 @@ RT_DEVICE float block_sum(float v, float* scratch) { return rt::block_sum(v, scr
 
 // ---------------------------------------------------------------- A: reduce-scatter + norm
 template <int W>
-__global__ void __launch_bounds__(THREADS)
+__global__ void __launch_bounds__(THREADS, 4)
 exchange_reduce_kernel(Peers peers, int rank, long lo4, long hi4, long tail_lo, long tail_hi,
                        const float* __restrict__ stats, unsigned epoch, unsigned long long limit_ns) {
   constexpr int world = W;
@@ -176,7 +179,7 @@ RT_DEVICE float adam_one(float g, float& p, float& m, float& v, long i, const Ad
 }
 
 template <int W>
-__global__ void __launch_bounds__(THREADS_B)
+__global__ void __launch_bounds__(THREADS_B, 2)
 exchange_update_kernel(Peers peers, int rank, long n, long lo4, long hi4, long tail_lo, long tail_hi,
                        float* __restrict__ m, float* __restrict__ v, float* __restrict__ stats,
                        float* __restrict__ report, Adam a, unsigned epoch, unsigned long long limit_ns) {
@@ -274,7 +277,7 @@ exchange_update_kernel(Peers peers, int rank, long n, long lo4, long hi4, long t
 // the forward). The decay-group fp32 masters stay sharded until gather_state. No completion flags are needed:
 // a peer changes its shard again only in its next update of this layer, which waits for this rank's next norm.
 template <int W>
-__global__ void __launch_bounds__(THREADS)
+__global__ void __launch_bounds__(THREADS, 4)
 exchange_gather_kernel(Peers peers, int rank, long n, long n8, long decay4, unsigned epoch,
                        unsigned long long limit_ns) {
   constexpr int UNROLL = 8;
@@ -338,7 +341,7 @@ RT_DEVICE void slice_of(long n8, int q, int W, int sl, int S, long& lo, long& hi
 }
 
 template <int W>
-__global__ void __launch_bounds__(THREADS_B)
+__global__ void __launch_bounds__(THREADS_B, 2)
 exchange_update_pull_kernel(Peers peers, int rank, long n, long n8, long decay4, int U, int S, float* __restrict__ m,
                             float* __restrict__ v, float* __restrict__ stats, float* __restrict__ report, Adam a,
                             unsigned epoch, unsigned long long limit_ns) {

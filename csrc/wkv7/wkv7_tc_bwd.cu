@@ -221,6 +221,7 @@ wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_c
     sm100::tma_load_3d(Rb, &m_b, &bars[0], x, y, bb);
     sm100::tma_load_3d(Rdy, &m_dy, &bars[0], x, y, bb);
   }
+  int stage = 1;
   bool ok = wait_all(&bars[0], 0);
   const bool t_issued = ok;
   uint32_t mph = 0;
@@ -273,6 +274,7 @@ wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_c
     }
     if (tid < 64) tile_row_from_global(S0t, 64, tid, S0g + tid * N);
     else tile_row_from_global(DSt, 64, tid - 64, wk + WK_DS * MAT + (tid - 64) * N);
+    stage = 2;
     ok = wait_all(&bars[1], mph);
     mph ^= 1;
     sm100::tc_fence_after();
@@ -309,7 +311,12 @@ wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_c
                      true);
       sm100::mma_commit(&bars[1]);
     }
-    ok = wait_all(&bars[1], mph) && wait_all(&bars[2], 0);
+    stage = 3;
+    ok = wait_all(&bars[1], mph);
+    if (ok) {
+      stage = 4;
+      ok = wait_all(&bars[2], 0);
+    }
     mph ^= 1;
     sm100::tc_fence_after();
   }
@@ -341,6 +348,7 @@ wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_c
       mma_tf32_tiles(tmem, sm100::smem_u32(TTt), 64, sm100::smem_u32(DUT), 64, 8, sm100::idesc_tf32(128, 64), false);
       sm100::mma_commit(&bars[1]);
     }
+    stage = 5;
     ok = wait_all(&bars[1], mph);
     mph ^= 1;
     sm100::tc_fence_after();
@@ -369,24 +377,25 @@ wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_c
                      sm100::idesc_tf32(128, 64), true);
       sm100::mma_commit(&bars[1]);
     }
+    stage = 6;
     ok = wait_all(&bars[1], mph);
     mph ^= 1;
     sm100::tc_fence_after();
   }
-  if (ok && tid >= 64) {  // dV rows s
+  if (ok && tid >= 64) {  // dV rows s (the TMEM load is warp-collective; only rows inside the sequence store)
     const int s = tid - 64, tg = c * L + s;
+    float d[64];
+    tmem_row64(tmem, warp, 192, d);
     if (s < nvalid) {
-      float d[64];
-      tmem_row64(tmem, warp, 192, d);
       float* out = dv + (((long)bb * T + tg) * H + h) * N;
 #pragma unroll
       for (int i = 0; i < 64; i += 4) *reinterpret_cast<float4*>(out + i) = make_float4(d[i], d[i + 1], d[i + 2], d[i + 3]);
     }
   }
-  if (!ok && tid == 0) atomicExch(&wkv7_tc_bwd_fault_word, 1);
+  if (!ok && tid == 0) atomicCAS(&wkv7_tc_bwd_fault_word, 0, 0x200 | stage);  // state kernel, failing wait
   if (!ok) {
-    sm100::mbar_wait_bounded(&bars[1], mph);
-    if (t_issued) sm100::mbar_wait_bounded(&bars[2], 0);
+    if (stage > 1) sm100::mbar_wait_bounded(&bars[1], mph);
+    if (t_issued && stage != 4) sm100::mbar_wait_bounded(&bars[2], 0);
   }
   sm100::tc_fence_before();
   __syncthreads();
@@ -472,6 +481,7 @@ wkv7_tc_bwd_grad_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_co
       sm100::tma_load_2d(UV + a * 16 * KB, &m_wk, &bars[0], 32 * a, urow);
     }
   }
+  int stage = 1;
   bool ok = wait_all(&bars[0], 0);
   uint32_t mph = 0;
   bool second_issued = false;
@@ -543,20 +553,24 @@ wkv7_tc_bwd_grad_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_co
       sm100::mma_commit(&bars[2]);  // own barrier: both commits may complete before either wait
     }
     second_issued = true;
+    stage = 2;
     ok = wait_all(&bars[1], mph);  // dM
     mph ^= 1;
-    if (ok) ok = wait_all(&bars[2], 0);  // S0 and dS products (DZY, UV, S0^T, dS^T free after this)
+    if (ok) {
+      stage = 3;
+      ok = wait_all(&bars[2], 0);  // S0 and dS products (DZY, UV, S0^T, dS^T free after this)
+    }
     sm100::tc_fence_after();
   }
   // dM stage tiles. Stage 1: SA = [dM_ab; dM_rb] (rows t, K = s), SB = [dM_ab^T; dM_ak^T] (rows s, K = t).
   //                 Stage 2: SA = [dM_ak; dM_rk],               SB = [dM_rb^T; dM_rk^T].
 #pragma unroll 1
-  for (int stage = 0; stage < 2 && ok; ++stage) {
+  for (int stage_ = 0; stage_ < 2 && ok; ++stage_) {
     {
       float d[64];
       const int t = tid & 63;
       const int lim = tid < 64 ? t : t + 1;  // strict for the a~ rows, inclusive for the r~ rows
-      if (stage == 0) {
+      if (stage_ == 0) {
         tmem_row64(tmem, warp, 0, d);  // dM_ab (t < 64) / dM_rb
 #pragma unroll
         for (int s = 0; s < 64; s += 4)
@@ -587,12 +601,13 @@ wkv7_tc_bwd_grad_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_co
     tc_sync();
     if (tid == 0) {
       // [dA~; dR~] += SA . (B~^T | K~^T);  [dB~; dK~] (cols 192..255) (+)= SB . (A~^T | R~^T)
-      mma_tf32_tiles(tmem + 128, sm100::smem_u32(SA), 128, sm100::smem_u32(X2T) + stage * 16 * KB, 64, 8,
+      mma_tf32_tiles(tmem + 128, sm100::smem_u32(SA), 128, sm100::smem_u32(X2T) + stage_ * 16 * KB, 64, 8,
                      sm100::idesc_tf32(128, 64), true);
-      mma_tf32_tiles(tmem + 192, sm100::smem_u32(SB), 128, sm100::smem_u32(X1T) + stage * 16 * KB, 64, 8,
-                     sm100::idesc_tf32(128, 64), stage > 0);
+      mma_tf32_tiles(tmem + 192, sm100::smem_u32(SB), 128, sm100::smem_u32(X1T) + stage_ * 16 * KB, 64, 8,
+                     sm100::idesc_tf32(128, 64), stage_ > 0);
       sm100::mma_commit(&bars[1]);
     }
+    stage = 4 + stage_;
     ok = wait_all(&bars[1], mph);
     mph ^= 1;
     sm100::tc_fence_after();
@@ -666,10 +681,10 @@ wkv7_tc_bwd_grad_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_co
       }
     }
   }
-  if (!ok && tid == 0) atomicExch(&wkv7_tc_bwd_fault_word, 1);
+  if (!ok && tid == 0) atomicCAS(&wkv7_tc_bwd_fault_word, 0, 0x400 | stage);  // gradient kernel, failing wait
   if (!ok) {
-    sm100::mbar_wait_bounded(&bars[1], mph);
-    if (second_issued) sm100::mbar_wait_bounded(&bars[2], 0);
+    if (stage > 1) sm100::mbar_wait_bounded(&bars[1], mph);
+    if (second_issued && stage != 3) sm100::mbar_wait_bounded(&bars[2], 0);
   }
   sm100::tc_fence_before();
   __syncthreads();
@@ -700,7 +715,8 @@ extern "C" long rt_wkv7_tc_backward_workspace_floats(int B, int T, int H) {
   return chunks * B * H * WK_MATS * MAT;
 }
 
-// 1 if a tcgen05 WKV7 backward kernel gave up a bounded wait since the last call (synchronizes the device).
+// Nonzero if a backward kernel gave up a bounded wait since the last call (synchronizes the device):
+// 0x200 | wait index for the U/dZ/dV kernel, 0x400 | wait index for the gradient kernel.
 extern "C" int rt_wkv7_tc_bwd_fault() {
   int v = 0, zero = 0;
   if (cudaMemcpyFromSymbol(&v, wkv7_tc_bwd_fault_word, sizeof(int)) != cudaSuccess) return -1;

@@ -159,6 +159,7 @@ wkv7_tc_chunk_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_const
     sm100::tma_load_3d(Ra, &m_a, &bars[0], x, y, bb);
     sm100::tma_load_3d(Rb, &m_b, &bars[0], x, y, bb);
   }
+  int stage = 1;  // which wait a failure happened at (recorded in the fault word)
   bool ok = wait_all(&bars[0], 0);
   uint32_t mph = 0;  // parity of the next MMA-barrier completion
   const int nvalid = min(L, T - c * L);
@@ -240,6 +241,7 @@ wkv7_tc_chunk_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_const
                      false);
       sm100::mma_commit(&bars[1]);
     }
+    stage = 2;
     ok = wait_all(&bars[1], mph);
     mph ^= 1;
     sm100::tc_fence_after();
@@ -292,6 +294,7 @@ wkv7_tc_chunk_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_const
         *reinterpret_cast<float4*>(g + j) = make_float4(tf32r(x.x), tf32r(x.y), tf32r(x.z), tf32r(x.w));
       }
     }
+    stage = 3;
     ok = wait_all(&bars[1], mph);  // MMA2 done
     mph ^= 1;
     tc_sync();
@@ -302,6 +305,7 @@ wkv7_tc_chunk_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_const
       sm100::mma_commit(&bars[1]);
     }
     if (ok) {
+      stage = 4;
       ok = wait_all(&bars[1], mph);
       mph ^= 1;
       sm100::tc_fence_after();
@@ -337,6 +341,7 @@ wkv7_tc_chunk_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_const
                      false);
       sm100::mma_commit(&bars[1]);
     }
+    stage = 5;
     ok = wait_all(&bars[1], mph);
     mph ^= 1;
     sm100::tc_fence_after();
@@ -390,6 +395,7 @@ wkv7_tc_chunk_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_const
                      sm100::idesc_tf32(128, 64), false);
       sm100::mma_commit(&bars[1]);
     }
+    stage = 6;
     ok = wait_all(&bars[1], mph);
     mph ^= 1;
     sm100::tc_fence_after();
@@ -414,8 +420,8 @@ wkv7_tc_chunk_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_const
       for (int u = 0; u < 32; u += 4) *reinterpret_cast<float4*>(g + u) = make_float4(d[u], d[u + 1], d[u + 2], d[u + 3]);
     }
   }
-  if (!ok && tid == 0) atomicExch(&wkv7_tc_fault_word, 1);
-  if (!ok) sm100::mbar_wait_bounded(&bars[1], mph);  // an MMA may still be in flight; let it finish first
+  if (!ok && tid == 0) atomicCAS(&wkv7_tc_fault_word, 0, 0x100 | stage);  // kernel 1, failing wait
+  if (!ok && stage > 1) sm100::mbar_wait_bounded(&bars[1], mph);  // an MMA may still be in flight
   sm100::tc_fence_before();
   __syncthreads();
   if (warp == 0) {
@@ -515,6 +521,7 @@ wkv7_tc_out_kernel(const __grid_constant__ CUtensorMap m_q, const __grid_constan
     }
   }
   bool ok = wait_all(&bars[0], 0);
+  int stage = ok ? 2 : 1;
   if (ok && tid == 0) {
     sm100::tc_fence_after();
     mma_tf32_tiles(tmem, sm100::smem_u32(A), 128, sm100::smem_u32(Bt), 128, 8, sm100::idesc_tf32(128, 128), false);
@@ -523,15 +530,17 @@ wkv7_tc_out_kernel(const __grid_constant__ CUtensorMap m_q, const __grid_constan
   if (ok) ok = wait_all(&bars[1], 0);
   sm100::tc_fence_after();
   const int p = tid >> 6, t = tid & 63, cc = p ? c1 : c0, tg = cc * L + t;
-  if (ok && !(p == 1 && c1 == c0) && tg < T) {
+  const bool store = !(p == 1 && c1 == c0) && tg < T;
+  if (ok) {  // tcgen05.ld is warp-collective: every lane loads, only rows inside the sequence store
     const uint32_t row = tmem + ((uint32_t)(32 * warp) << 16) + 64 * p;
     const float* y0 = ws + ((bh * chunks + cc) * REC_MATS + REC_Y0) * MAT + t * N;
-    __nv_bfloat16* out = y + (((long)bb * T + tg) * H + h) * N;
+    __nv_bfloat16* out = y + (((long)bb * T + (store ? tg : 0)) * H + h) * N;
 #pragma unroll 1
     for (int half = 0; half < 2; ++half) {
       float d[32];
       sm100::tmem_ld32(row + 32 * half, d);
       sm100::tmem_wait_ld();
+      if (!store) continue;
 #pragma unroll
       for (int u = 0; u < 32; u += 8) {
         float v[8];
@@ -543,7 +552,7 @@ wkv7_tc_out_kernel(const __grid_constant__ CUtensorMap m_q, const __grid_constan
       }
     }
   }
-  if (!ok && tid == 0) atomicExch(&wkv7_tc_fault_word, 1);
+  if (!ok && tid == 0) atomicCAS(&wkv7_tc_fault_word, 0, 0x300 | stage);  // kernel 3, failing wait
   sm100::tc_fence_before();
   __syncthreads();
   if (warp == 0) {
@@ -576,7 +585,8 @@ extern "C" long rt_wkv7_tc_workspace_floats(int B, int T, int H) {
 
 extern "C" int rt_wkv7_tc_chunk_len() { return L; }
 
-// 1 if a tcgen05 WKV7 forward kernel gave up a bounded wait since the last call (synchronizes the device).
+// Nonzero if a tcgen05 WKV7 forward kernel gave up a bounded wait since the last call (synchronizes the device):
+// 0x100 | wait index for the chunk kernel, 0x300 | wait index for the output kernel (first failure recorded).
 extern "C" int rt_wkv7_tc_fault() {
   int v = 0, zero = 0;
   if (cudaMemcpyFromSymbol(&v, wkv7_tc_fault_word, sizeof(int)) != cudaSuccess) return -1;
