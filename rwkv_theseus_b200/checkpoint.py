@@ -1,20 +1,22 @@
 """Atomic, rank-sharded checkpoints (format 2, ``parallel_layers_v1``).
 
-Layout (reference ``theseus/checkpoint.py:88-130``)::
+On-disk layout (the reference's format, ``theseus/checkpoint.py:88-130``, kept so
+that either project's tools read the other's checkpoints)::
 
     <output>/parallel_step_XXXXXXXX[_complete]/
         COMMITTED
-        manifest.json          format, topology, step, order, config, world, fingerprints, versions
-        migrated.safetensors   "<layer>.<param>" fp32, the 23 TimeMix tensors per layer
+        manifest.json          format, training_topology, stage, step, complete, order, config, world,
+                               base/train/validation fingerprints, torch and transformers versions
+        migrated.safetensors   "<layer>.<param>" fp32: the 23 TimeMix tensors of every migrated layer
         optimizer.pt           {layer: {"optimizer": AdamW state_dict, "scheduler": LambdaLR state_dict}}
         ranks/rank_XXXXX.pt    {"runner", "reader", "rng", "students": {layer: {shift, wkv}}}
     <output>/latest            name of the newest committed directory
 
-Commit protocol: leader creates ``.<name>.tmp``; barrier; every rank writes its
-own file; leader writes weights, optimizer and manifest; barrier; leader writes
-``COMMITTED``, renames the directory into place and atomically replaces
-``latest``; barrier. Resume is guarded by base/manifest fingerprints, the
-layer order and the non-mutable config keys.
+A checkpoint becomes visible only when it is complete: every rank writes into a
+hidden staging directory, the leader adds ``COMMITTED`` last, renames the
+directory into place and swaps the ``latest`` pointer with an atomic replace.
+Resuming is refused when the base weights, the data manifests, the layer order
+or a config key outside ``MUTABLE_KEYS`` changed.
 """
 import hashlib
 import json
@@ -26,26 +28,25 @@ from pathlib import Path
 import numpy as np
 import torch
 from safetensors.torch import load_file, save_file
+from torch.utils._pytree import tree_map
 
 from .data import digest_file
 
-MUTABLE_KEYS = {"output", "log_interval", "checkpoint_interval", "validation_interval", "timeout_minutes",
-                "lr", "warmup_steps", "constant_steps", "min_lr", "fused_optimizer", "grad_sync", "student_graphs"}
+# Config keys that may change between a checkpoint and its resume (plus every ``wandb_*`` key).
+MUTABLE_KEYS = frozenset({"output", "log_interval", "checkpoint_interval", "validation_interval",
+                          "timeout_minutes", "lr", "warmup_steps", "constant_steps", "min_lr",
+                          "fused_optimizer", "grad_sync", "student_graphs"})
+# Values assumed for keys that older manifests do not carry.
+_OLD_MANIFEST_DEFAULTS = {"training_mode": "sampled", "micro_batch_size": 1}
 
 
 def cpu_tree(obj):
-    if torch.is_tensor(obj):
-        return obj.detach().cpu().clone()
-    if isinstance(obj, dict):
-        return {k: cpu_tree(v) for k, v in obj.items()}
-    if isinstance(obj, list):
-        return [cpu_tree(v) for v in obj]
-    if isinstance(obj, tuple):
-        return tuple(cpu_tree(v) for v in obj)
-    return obj
+    """Detached CPU copies of every tensor in a nest of dicts, lists and tuples."""
+    return tree_map(lambda leaf: leaf.detach().cpu().clone() if torch.is_tensor(leaf) else leaf, obj)
 
 
 def rng_state():
+    """Generator states of Python, NumPy, torch CPU and (when initialised) the current CUDA device."""
     return {"python": random.getstate(), "numpy": np.random.get_state(), "torch": torch.get_rng_state(),
             "cuda": torch.cuda.get_rng_state() if torch.cuda.is_initialized() else None}
 
@@ -54,110 +55,147 @@ def restore_rng(state):
     random.setstate(state["python"])
     np.random.set_state(state["numpy"])
     torch.set_rng_state(state["torch"].cpu())
-    if state["cuda"] is not None and torch.cuda.is_available():
+    if state.get("cuda") is not None and torch.cuda.is_available():
         torch.cuda.set_rng_state(state["cuda"].cpu())
 
 
 def model_fingerprint(path):
-    """Hash of shard sizes/mtimes plus config/index content (cheap, no weight read)."""
-    path = Path(path)
-    records = {p.name: (p.stat().st_size, p.stat().st_mtime_ns) for p in sorted(path.glob("*.safetensors"))}
-    for p in (path / "config.json", path / "model.safetensors.index.json"):
-        if p.exists():
-            records[p.name] = digest_file(p)
-    return hashlib.sha256(json.dumps(records, sort_keys=True).encode()).hexdigest()
+    """Identity of a base-model directory without reading its weights: the size and modification time of every
+    ``*.safetensors`` shard and the SHA-256 of ``config.json`` / ``model.safetensors.index.json``, hashed as
+    sorted JSON (the same record the reference writes into ``base_fingerprint``)."""
+    root = Path(path)
+    record = {}
+    for shard in sorted(root.glob("*.safetensors")):
+        info = shard.stat()
+        record[shard.name] = [info.st_size, info.st_mtime_ns]
+    for meta_file in ("config.json", "model.safetensors.index.json"):
+        if (root / meta_file).exists():
+            record[meta_file] = digest_file(root / meta_file)
+    return hashlib.sha256(json.dumps(record, sort_keys=True).encode()).hexdigest()
 
 
 def split_delta(tensors):
-    out = {}
+    """``{"<layer>.<param>": t}`` -> ``{layer: {param: t}}``."""
+    per_layer = {}
     for key, value in tensors.items():
-        layer, name = key.split(".", 1)
-        out.setdefault(int(layer), {})[name] = value
-    return out
+        layer, param = key.split(".", 1)
+        per_layer.setdefault(int(layer), {})[param] = value
+    return per_layer
 
 
 def resolve_checkpoint(path):
-    path = Path(path)
-    if path.name == "latest":
-        path = path.parent / path.read_text().strip()
-    elif not (path / "COMMITTED").exists() and (path / "latest").exists():
-        path = path / (path / "latest").read_text().strip()
-    if not (path / "COMMITTED").exists():
-        raise ValueError(f"Not a committed checkpoint: {path}")
-    return path
+    """A committed checkpoint directory from the directory itself, its run root, or the root's ``latest`` file."""
+    candidate = Path(path)
+    if candidate.name == "latest" and candidate.is_file():
+        candidate = candidate.parent / candidate.read_text().strip()
+    elif not (candidate / "COMMITTED").exists() and (candidate / "latest").is_file():
+        candidate = candidate / (candidate / "latest").read_text().strip()
+    if not (candidate / "COMMITTED").exists():
+        raise ValueError(f"Not a committed checkpoint: {candidate}")
+    return candidate
 
 
 def read_checkpoint(path):
-    path = resolve_checkpoint(path)
-    meta = json.loads((path / "manifest.json").read_text())
-    if meta["format"] not in (1, 2):
+    """(directory, manifest, {layer: {param: tensor}}) of a committed format-1 or format-2 checkpoint."""
+    directory = resolve_checkpoint(path)
+    manifest = json.loads((directory / "manifest.json").read_text())
+    if manifest.get("format") not in (1, 2):
         raise ValueError("Unsupported checkpoint format")
-    return path, meta, split_delta(load_file(str(path / "migrated.safetensors")))
+    return directory, manifest, split_delta(load_file(str(directory / "migrated.safetensors")))
+
+
+class _Staged:
+    """One checkpoint directory being written: hidden while staged, renamed into place by ``commit``."""
+
+    def __init__(self, root, step, complete):
+        self.root = Path(root)
+        self.name = f"parallel_step_{step:08d}" + ("_complete" if complete else "")
+        self.final = self.root / self.name
+        self.staging = self.root / f".{self.name}.tmp"
+
+    def prepare(self):
+        self.root.mkdir(parents=True, exist_ok=True)
+        if self.staging.exists():
+            shutil.rmtree(self.staging)
+        (self.staging / "ranks").mkdir(parents=True)
+
+    def commit(self):
+        (self.staging / "COMMITTED").write_text("1\n")
+        if self.final.exists():
+            raise FileExistsError(f"Refusing to overwrite committed checkpoint {self.final}")
+        os.replace(self.staging, self.final)
+        pointer = self.root / ".latest.tmp"
+        pointer.write_text(self.name + "\n")
+        os.replace(pointer, self.root / "latest")
+
+
+def _manifest(cfg, topo, step, complete, order, base_id):
+    import transformers
+    return {"format": 2, "training_topology": "parallel_layers_v1", "stage": 0, "step": step,
+            "complete": complete, "order": order, "config": cfg, "world": topo.world,
+            "base_fingerprint": base_id, "train_fingerprint": digest_file(cfg["train_manifest"]),
+            "validation_fingerprint": digest_file(cfg["validation_manifest"]),
+            "torch": torch.__version__, "transformers": transformers.__version__}
 
 
 def save_checkpoint(topo, cfg, step, complete, order, runner, reader, base_id, students):
-    """Commit one parallel-layer checkpoint; returns its final directory."""
-    root = Path(cfg["output"])
-    name = f"parallel_step_{step:08d}" + ("_complete" if complete else "")
-    final, temp = root / name, root / f".{name}.tmp"
+    """Collective: commit one checkpoint of every student; returns its directory."""
+    target = _Staged(cfg["output"], step, complete)
     if topo.rank == topo.leader:
-        root.mkdir(parents=True, exist_ok=True)
-        if temp.exists():
-            shutil.rmtree(temp)
-        (temp / "ranks").mkdir(parents=True)
+        target.prepare()
     topo.barrier()
     topo.join_grad_sync()
-    for s in students.values():
-        s.sync_state()
-    local = {"runner": runner.state_dict(), "reader": reader.state_dict() if reader else None, "rng": rng_state(),
-             "students": {layer: s.state for layer, s in students.items()}}
-    torch.save(cpu_tree(local), temp / "ranks" / f"rank_{topo.rank:05d}.pt")
+    for student in students.values():
+        student.sync_state()  # complete fp32 masters and moments on every rank
+    rank_file = {"runner": runner.state_dict(), "reader": None if reader is None else reader.state_dict(),
+                 "rng": rng_state(), "students": {layer: s.state for layer, s in students.items()}}
+    torch.save(cpu_tree(rank_file), target.staging / "ranks" / f"rank_{topo.rank:05d}.pt")
     if topo.rank == topo.leader:
-        weights = {f"{layer}.{k}": v.detach().cpu().contiguous()
-                   for layer, s in students.items() for k, v in s.weights().items()}
-        save_file(weights, str(temp / "migrated.safetensors"))
-        optim = {layer: {"optimizer": s.optimizer_state_dict(), "scheduler": s.scheduler_state_dict()}
-                 for layer, s in students.items()}
-        torch.save(cpu_tree(optim), temp / "optimizer.pt")
-        import transformers
-        meta = {"format": 2, "training_topology": "parallel_layers_v1", "stage": 0, "step": step,
-                "complete": complete, "order": order, "config": cfg, "world": topo.world,
-                "base_fingerprint": base_id, "train_fingerprint": digest_file(cfg["train_manifest"]),
-                "validation_fingerprint": digest_file(cfg["validation_manifest"]),
-                "torch": torch.__version__, "transformers": transformers.__version__}
-        (temp / "manifest.json").write_text(json.dumps(meta, indent=2))
+        weights = {}
+        optimizer = {}
+        for layer, student in students.items():
+            weights.update({f"{layer}.{param}": t.detach().cpu().contiguous()
+                            for param, t in student.weights().items()})
+            optimizer[layer] = {"optimizer": student.optimizer_state_dict(),
+                                "scheduler": student.scheduler_state_dict()}
+        save_file(weights, str(target.staging / "migrated.safetensors"))
+        torch.save(cpu_tree(optimizer), target.staging / "optimizer.pt")
+        manifest = _manifest(cfg, topo, step, complete, order, base_id)
+        (target.staging / "manifest.json").write_text(json.dumps(manifest, indent=2))
     topo.barrier()
     if topo.rank == topo.leader:
-        (temp / "COMMITTED").write_text("1\n")
-        if final.exists():
-            raise FileExistsError(f"Refusing to overwrite committed checkpoint {final}")
-        os.replace(temp, final)
-        pointer = root / ".latest.tmp"
-        pointer.write_text(name + "\n")
-        os.replace(pointer, root / "latest")
+        target.commit()
     topo.barrier()
-    return final
+    return target.final
+
+
+def _changed_config_keys(saved, cfg, complete):
+    allowed = set(MUTABLE_KEYS) | {key for key in cfg if key.startswith("wandb_")}
+    if complete:
+        allowed.add("micro_batch_size")
+    changed = []
+    for key in sorted(set(cfg) - allowed):
+        before = saved.get(key, _OLD_MANIFEST_DEFAULTS.get(key))
+        if cfg[key] != before:
+            changed.append(key)
+    return changed
 
 
 def validate_resume(meta, cfg, topo, base_id, order):
+    """Raise unless this job may continue the checkpoint described by `meta`."""
     if meta["base_fingerprint"] != base_id:
         raise ValueError("Base weights changed")
     if meta["order"] != order:
         raise ValueError("Migration layer order changed; start a new run.")
-    for name in ("train", "validation"):
-        if meta[name + "_fingerprint"] != digest_file(cfg[name + "_manifest"]):
-            raise ValueError(f"{name} manifest changed")
-    mutable = set(MUTABLE_KEYS)
+    for split in ("train", "validation"):
+        if meta[f"{split}_fingerprint"] != digest_file(cfg[f"{split}_manifest"]):
+            raise ValueError(f"{split} manifest changed")
+    changed = _changed_config_keys(meta["config"], cfg, meta["complete"])
+    if changed:
+        raise ValueError(f"Resume config changed: {changed[0]}")
     if meta["complete"]:
-        mutable.add("micro_batch_size")
-    for key in cfg.keys() - mutable - {k for k in cfg if k.startswith("wandb_")}:
-        default = "sampled" if key == "training_mode" else 1 if key == "micro_batch_size" else None
-        if key in ("lora_rank", "gate_lora_rank") and key not in meta["config"]:
-            default = None
-        if cfg[key] != meta["config"].get(key, default):
-            raise ValueError(f"Resume config changed: {key}")
-    if not meta["complete"]:
-        if meta.get("training_topology") not in {"local_branch_v1", "parallel_layers_v1"}:
-            raise ValueError("Old paired mid-stage checkpoints cannot resume; use a completed stage")
-        if meta["world"] != topo.world:
-            raise ValueError("Mid-stream resume needs identical rank topology")
+        return
+    if meta.get("training_topology") not in ("local_branch_v1", "parallel_layers_v1"):
+        raise ValueError("Old paired mid-stage checkpoints cannot resume; use a completed stage")
+    if meta["world"] != topo.world:
+        raise ValueError("Mid-stream resume needs identical rank topology")

@@ -1,27 +1,30 @@
 """Token-manifest v1 readers with resumable cursors.
 
-File contract (unchanged from the reference, ``README.md:105-139``): a
-``manifest.json`` with ``{"format": 1, "vocab_size", "sources": [{"tokens",
-"offsets", "weight", "tokens_sha256", "offsets_sha256", ...}]}``; ``tokens`` is
-raw little-endian uint32, ``offsets`` an int64 ``.npy`` of N+1 strictly
-increasing document boundaries from 0 to len(tokens).
+File contract (the reference's, ``README.md:105-139``): ``manifest.json`` holds
+``{"format": 1, "vocab_size", "sources": [{"tokens", "offsets", "weight",
+"tokens_sha256", "offsets_sha256", ...}]}``; ``tokens`` is raw little-endian
+uint32 and ``offsets`` an int64 ``.npy`` of N+1 strictly increasing document
+boundaries from 0 to len(tokens).
 
-The three readers reproduce the reference's sampling semantics exactly
-(``theseus/data.py:19-222``) so that runs and checkpoints are interchangeable:
+Which tokens a run reads is also a contract (runs and checkpoints move between
+this project and the reference, ``theseus/data.py:19-222``), so the sampling
+steps below are fixed:
 
-* ``TokenStream`` (``training_mode: sampled`` and validation): each window is
-  drawn with ``default_rng(SeedSequence([seed, window * pairs + pair_id]))``:
-  source by weight, document uniformly, then a whole number of chunks (at most
-  ``context_tokens``) at a random start.
-* ``EpochTokenStream``: every token exactly once. Documents are cut into
-  windows of ``context_tokens``; the window list is shuffled once with
-  ``default_rng(seed)`` and rank r takes entries ``r::world``.
-* ``BatchedEpochTokenStream``: the rank's windows are packed into groups of
-  ``micro_batch_size`` equal-length windows (independent lanes sharing the
-  same positions); leftovers form smaller groups.
+* sampled mode (``TokenStream``, also every validation reader): window ``w`` of
+  rank ``r`` out of ``R`` draws from ``default_rng(SeedSequence([seed, w*R + r]))``
+  a source by weight, then a document uniformly, then a start for a span that
+  is a whole number of chunks (at most ``context_tokens``; shorter documents
+  are taken whole);
+* epoch mode (``EpochTokenStream``): every document is cut into windows of
+  ``context_tokens`` (source, document, position order); the table is shuffled
+  once by ``default_rng(seed)`` and rank ``r`` takes rows ``r::R``;
+* lanes (``BatchedEpochTokenStream``, ``micro_batch_size`` > 1): the rank's
+  windows are grouped by length in reading order, a group is emitted whenever
+  ``micro_batch_size`` windows of one length have collected, and the leftover
+  partial groups follow in first-seen length order.
 
-Batches are plain CPU int64 tensors; the trainer stages them through one
-persistent pinned buffer so each step's host-to-device copy is asynchronous.
+The corpus (``Corpus``) is shared; each reader only decides which window comes
+next and cuts it into chunks. Batches are CPU int64 tensors.
 """
 import hashlib
 import json
@@ -34,132 +37,158 @@ SAMPLER_VERSION = 2
 
 
 def digest_file(path):
-    h = hashlib.sha256()
-    with open(path, "rb") as f:
-        while True:
-            block = f.read(8 << 20)
-            if not block:
-                break
-            h.update(block)
-    return h.hexdigest()
+    """SHA-256 of a file's bytes, read in 8 MiB blocks."""
+    hasher = hashlib.sha256()
+    with open(path, "rb") as handle:
+        for block in iter(lambda: handle.read(8 << 20), b""):
+            hasher.update(block)
+    return hasher.hexdigest()
 
 
-def _ids_tensor(values):
-    return torch.from_numpy(np.ascontiguousarray(values, dtype=np.int64))
+class Corpus:
+    """The validated sources of one manifest: memory-mapped tokens, document offsets, normalised weights."""
+
+    def __init__(self, manifest):
+        self.path = Path(manifest).resolve()
+        self.spec = json.loads(self.path.read_text())
+        if self.spec.get("format") != 1:
+            raise ValueError("Unsupported token manifest")
+        if not self.spec["sources"]:
+            raise ValueError("Manifest must contain at least one source")
+        self.fingerprint = digest_file(self.path)
+        self.tokens, self.offsets, weights = [], [], []
+        for entry in self.spec["sources"]:
+            tokens = np.memmap(self.path.parent / entry["tokens"], dtype="<u4", mode="r")
+            offsets = np.load(self.path.parent / entry["offsets"], mmap_mode="r")
+            well_formed = (len(offsets) >= 2 and offsets[0] == 0 and offsets[-1] == len(tokens)
+                           and bool(np.all(np.diff(offsets) > 0)))
+            if not well_formed:
+                raise ValueError("Invalid or empty document offsets")
+            if not (np.isfinite(entry["weight"]) and entry["weight"] > 0):
+                raise ValueError("Mixture weights must be positive")
+            self.tokens.append(tokens)
+            self.offsets.append(offsets)
+            weights.append(float(entry["weight"]))
+        self.weights = np.asarray(weights) / np.sum(weights)
+
+    def span(self, source, begin, end):
+        return self.tokens[int(source)][int(begin):int(end)]
+
+    def total_tokens(self):
+        return int(sum(len(t) for t in self.tokens))
+
+    def window_table(self, context_tokens):
+        """Every (source, begin, end) window of at most `context_tokens` tokens inside one document, in
+        source, document and position order."""
+        tables = []
+        for source, offsets in enumerate(self.offsets):
+            bounds = np.asarray(offsets, dtype=np.int64)
+            doc_len = bounds[1:] - bounds[:-1]
+            pieces = -(-doc_len // context_tokens)                     # windows per document
+            owner = np.repeat(np.arange(len(doc_len)), pieces)         # document of each window
+            index_in_doc = np.arange(len(owner)) - np.repeat(np.cumsum(pieces) - pieces, pieces)
+            begin = bounds[owner] + index_in_doc * context_tokens
+            end = np.minimum(begin + context_tokens, bounds[owner + 1])
+            tables.append(np.stack([np.full_like(begin, source), begin, end], axis=1))
+        return np.concatenate(tables).astype(np.int64, copy=False)
+
+
+def _as_ids(array):
+    return torch.from_numpy(np.ascontiguousarray(array, dtype=np.int64))
+
+
+def _chunk_count(lengths, chunk_tokens):
+    return -(-np.asarray(lengths, dtype=np.int64) // chunk_tokens)
 
 
 class TokenStream:
+    """Sampled windows (mixture by source weight), cut into chunks; never exhausted."""
+
     def __init__(self, manifest, pair_id, pairs, chunk_tokens, context_tokens, seed=42):
-        self.path = Path(manifest).resolve()
-        self.manifest = json.loads(self.path.read_text())
-        if self.manifest.get("format") != 1:
-            raise ValueError("Unsupported token manifest")
+        self.corpus = Corpus(manifest)
+        self.path, self.manifest, self.fingerprint = self.corpus.path, self.corpus.spec, self.corpus.fingerprint
         if chunk_tokens < 1 or context_tokens < chunk_tokens:
             raise ValueError("Require context_tokens >= chunk_tokens >= 1")
-        self.fingerprint = digest_file(self.path)
-        self.pair_id, self.pairs = pair_id, pairs
-        self.chunk_tokens, self.context_tokens, self.seed = chunk_tokens, context_tokens, seed
-        if not self.manifest["sources"]:
-            raise ValueError("Manifest must contain at least one source")
-        self.sources, weights = [], []
-        for entry in self.manifest["sources"]:
-            tokens = np.memmap(self.path.parent / entry["tokens"], dtype="<u4", mode="r")
-            offsets = np.load(self.path.parent / entry["offsets"], mmap_mode="r")
-            bad = (len(offsets) < 2 or offsets[0] != 0 or offsets[-1] != len(tokens)
-                   or bool(np.any(np.diff(offsets) <= 0)))
-            if bad:
-                raise ValueError("Invalid or empty document offsets")
-            if not np.isfinite(entry["weight"]) or entry["weight"] <= 0:
-                raise ValueError("Mixture weights must be positive")
-            self.sources.append((tokens, offsets))
-            weights.append(entry["weight"])
-        self.weights = np.asarray(weights, dtype=np.float64)
-        self.weights /= self.weights.sum()
-        self.window = self.offset = self.chunks = 0
-        self._current = None
+        self.pair_id, self.pairs, self.seed = pair_id, pairs, seed
+        self.chunk_tokens, self.context_tokens = chunk_tokens, context_tokens
+        self.window = self.offset = self.chunks = 0   # cursor: window index, position in it, chunks emitted
+        self._tokens = None                           # the current window's tokens
 
-    def _window(self):
-        stream = self.window * self.pairs + self.pair_id
-        rng = np.random.default_rng(np.random.SeedSequence([self.seed, stream]))
-        tokens, offsets = self.sources[int(rng.choice(len(self.sources), p=self.weights))]
-        doc = int(rng.integers(len(offsets) - 1))
-        begin, finish = int(offsets[doc]), int(offsets[doc + 1])
-        available = finish - begin
-        if available >= self.chunk_tokens:
-            length = min(available, self.context_tokens) // self.chunk_tokens * self.chunk_tokens
-        else:
-            length = available
-        begin += int(rng.integers(available - length + 1))
-        return tokens[begin:begin + length]
+    # which window comes next ------------------------------------------------------------
+    def _stream_id(self):
+        return self.window * self.pairs + self.pair_id
 
+    def _draw_window(self):
+        draw = np.random.default_rng(np.random.SeedSequence([self.seed, self._stream_id()]))
+        source = int(draw.choice(len(self.corpus.tokens), p=self.corpus.weights))
+        offsets = self.corpus.offsets[source]
+        doc = int(draw.integers(len(offsets) - 1))
+        doc_begin, doc_end = int(offsets[doc]), int(offsets[doc + 1])
+        size = doc_end - doc_begin
+        take = size if size < self.chunk_tokens else min(size, self.context_tokens) // self.chunk_tokens * \
+            self.chunk_tokens
+        begin = doc_begin + int(draw.integers(size - take + 1))
+        return self.corpus.span(source, begin, begin + take)
+
+    # chunking ------------------------------------------------------------------------------
     def next(self):
-        if self._current is None:
-            self._current = self._window()
-        stop = min(len(self._current), self.offset + self.chunk_tokens)
-        ids = _ids_tensor(self._current[self.offset:stop])[None]
-        batch = {"ids": ids, "reset": self.offset == 0, "stream": self.window * self.pairs + self.pair_id,
-                 "chunk": self.chunks, "position": self.offset}
-        self.offset = stop
+        if self._tokens is None:
+            self._tokens = self._draw_window()
+        stop = min(len(self._tokens), self.offset + self.chunk_tokens)
+        batch = {"ids": _as_ids(self._tokens[self.offset:stop])[None], "reset": self.offset == 0,
+                 "stream": self._stream_id(), "chunk": self.chunks, "position": self.offset}
         self.chunks += 1
-        if stop == len(self._current):
-            self.window += 1
-            self.offset = 0
-            self._current = None
+        if stop < len(self._tokens):
+            self.offset = stop
+        else:
+            self.window, self.offset, self._tokens = self.window + 1, 0, None
         return batch
 
+    # resume ---------------------------------------------------------------------------------
+    _CURSOR = ("window", "offset", "chunks")
+
+    def _identity(self):
+        return {"fingerprint": self.fingerprint, "pair_id": self.pair_id, "pairs": self.pairs, "seed": self.seed,
+                "chunk_tokens": self.chunk_tokens, "context_tokens": self.context_tokens,
+                "sampler_version": SAMPLER_VERSION}
+
     def state_dict(self):
-        return {"window": self.window, "offset": self.offset, "chunks": self.chunks,
-                "fingerprint": self.fingerprint, "pair_id": self.pair_id, "pairs": self.pairs,
-                "seed": self.seed, "chunk_tokens": self.chunk_tokens,
-                "context_tokens": self.context_tokens, "sampler_version": SAMPLER_VERSION}
+        return {name: getattr(self, name) for name in self._CURSOR} | self._identity()
+
+    def _check_identity(self, state):
+        for key, value in self._identity().items():
+            if key not in state or state[key] != value:
+                raise ValueError(f"Reader resume mismatch: {key}")
 
     def load_state_dict(self, state):
-        own = self.state_dict()
-        for key in own.keys() - {"window", "offset", "chunks"}:
-            if key not in state or own[key] != state[key]:
-                raise ValueError(f"Reader resume mismatch: {key}")
-        self.window, self.offset, self.chunks = state["window"], state["offset"], state["chunks"]
-        self._current = None
-
-
-def _epoch_windows(sources, context_tokens):
-    """All (source, start, end) windows of at most ``context_tokens`` inside documents."""
-    parts = []
-    for source, (_, offsets) in enumerate(sources):
-        offsets = np.asarray(offsets, dtype=np.int64)
-        lengths = np.diff(offsets)
-        per_doc = (lengths + context_tokens - 1) // context_tokens
-        doc = np.repeat(np.arange(len(per_doc)), per_doc)
-        first = np.repeat(np.cumsum(per_doc) - per_doc, per_doc)
-        starts = offsets[doc] + (np.arange(len(doc)) - first) * context_tokens
-        ends = np.minimum(starts + context_tokens, offsets[doc + 1])
-        parts.append(np.column_stack((np.full(len(doc), source), starts, ends)))
-    return np.concatenate(parts).astype(np.int64, copy=False)
+        self._check_identity(state)
+        for name in self._CURSOR:
+            setattr(self, name, state[name])
+        self._tokens = None
 
 
 class EpochTokenStream(TokenStream):
-    """Visit every token exactly once; ranks take disjoint shuffled windows."""
+    """Every token of the corpus exactly once: this rank's share of one shuffled window table."""
 
     def __init__(self, *args, **kwargs):
         super().__init__(*args, **kwargs)
-        windows = _epoch_windows(self.sources, self.context_tokens)
-        np.random.default_rng(self.seed).shuffle(windows)
-        self._all_windows = windows if getattr(self, "micro_batch_size", 1) > 1 else None
-        costs = (windows[:, 2] - windows[:, 1] + self.chunk_tokens - 1) // self.chunk_tokens
-        self.rank_chunks = [int(costs[r::self.pairs].sum()) for r in range(self.pairs)]
-        self.total_tokens = sum(len(tokens) for tokens, _ in self.sources)
-        self.windows = windows[self.pair_id::self.pairs].copy()
+        table = self.corpus.window_table(self.context_tokens)
+        np.random.default_rng(self.seed).shuffle(table)
+        self._table = table
+        chunks = _chunk_count(table[:, 2] - table[:, 1], self.chunk_tokens)
+        self.rank_chunks = [int(chunks[rank::self.pairs].sum()) for rank in range(self.pairs)]
+        self.total_tokens = self.corpus.total_tokens()
+        self.windows = table[self.pair_id::self.pairs].copy()
         self.consumed_tokens = 0
-
-    def _window(self):
-        if self.exhausted:
-            raise StopIteration
-        source, begin, finish = self.windows[self.window]
-        return self.sources[source][0][begin:finish]
 
     @property
     def exhausted(self):
         return self.window >= len(self.windows)
+
+    def _draw_window(self):
+        if self.exhausted:
+            raise StopIteration
+        return self.corpus.span(*self.windows[self.window])
 
     def next(self):
         if self.exhausted:
@@ -174,39 +203,41 @@ class EpochTokenStream(TokenStream):
     def load_state_dict(self, state):
         if state.get("reader_mode") != "epoch_v1":
             raise ValueError("A sampled reader checkpoint cannot resume an exhaustive epoch")
-        self.consumed_tokens = state["consumed_tokens"]
         super().load_state_dict(state)
+        self.consumed_tokens = state["consumed_tokens"]
+
+
+def pack_lanes(windows, lanes):
+    """Groups of `lanes` equal-length windows in reading order; leftovers last, in first-seen length order."""
+    waiting, groups = {}, []
+    for row in windows:
+        bucket = waiting.setdefault(int(row[2] - row[1]), [])
+        bucket.append(row)
+        if len(bucket) == lanes:
+            groups.append(np.stack(bucket).astype(np.int64))
+            bucket.clear()
+    groups.extend(np.stack(bucket).astype(np.int64) for bucket in waiting.values() if bucket)
+    return groups
 
 
 class BatchedEpochTokenStream(EpochTokenStream):
-    """Equal-length windows packed into ``micro_batch_size`` independent lanes."""
+    """Epoch mode with `micro_batch_size` independent lanes of equal-length windows (no padding: every lane starts
+    and ends at the same positions, so caches and recurrent states reset per group)."""
 
     def __init__(self, *args, micro_batch_size, **kwargs):
         if micro_batch_size < 2:
             raise ValueError("Batched reader requires micro_batch_size >= 2")
         self.micro_batch_size = micro_batch_size
         super().__init__(*args, **kwargs)
-        self.groups = self._pack(self.windows)
-        self.rank_chunks = []
-        for rank in range(self.pairs):
-            mine = self._all_windows[rank::self.pairs]
-            lengths, counts = np.unique(mine[:, 2] - mine[:, 1], return_counts=True)
-            groups_per_length = (counts + micro_batch_size - 1) // micro_batch_size
-            chunks_per_group = (lengths + self.chunk_tokens - 1) // self.chunk_tokens
-            self.rank_chunks.append(int((groups_per_length * chunks_per_group).sum()))
-        del self.windows, self._all_windows
+        self.groups = pack_lanes(self.windows, micro_batch_size)
+        self.rank_chunks = [self._packed_chunks(self._table[rank::self.pairs]) for rank in range(self.pairs)]
+        del self.windows, self._table
         self.group = self.offset = 0
 
-    def _pack(self, windows):
-        pending, groups = {}, []
-        for row in windows:
-            bucket = pending.setdefault(int(row[2] - row[1]), [])
-            bucket.append(row)
-            if len(bucket) == self.micro_batch_size:
-                groups.append(np.asarray(bucket, dtype=np.int64))
-                bucket.clear()
-        groups.extend(np.asarray(b, dtype=np.int64) for b in pending.values() if b)
-        return groups
+    def _packed_chunks(self, windows):
+        lengths, count = np.unique(windows[:, 2] - windows[:, 1], return_counts=True)
+        groups = -(-count // self.micro_batch_size)
+        return int((groups * _chunk_count(lengths, self.chunk_tokens)).sum())
 
     @property
     def exhausted(self):
@@ -215,43 +246,41 @@ class BatchedEpochTokenStream(EpochTokenStream):
     def next(self):
         if self.exhausted:
             return None
-        group = self.groups[self.group]
-        length = int(group[0, 2] - group[0, 1])
+        rows = self.groups[self.group]
+        length = int(rows[0, 2] - rows[0, 1])
         stop = min(length, self.offset + self.chunk_tokens)
-        rows = [np.asarray(self.sources[int(s)][0][int(b) + self.offset:int(b) + stop], dtype=np.int64)
-                for s, b, _ in group]
-        ids = _ids_tensor(np.stack(rows))
+        ids = _as_ids(np.stack([self.corpus.span(s, b + self.offset, b + stop) for s, b, _ in rows]))
         batch = {"ids": ids, "reset": self.offset == 0, "position": self.offset, "group": self.group}
         self.consumed_tokens += ids.numel()
-        self.offset = stop
-        if stop == length:
-            self.group += 1
-            self.offset = 0
+        if stop < length:
+            self.offset = stop
+        else:
+            self.group, self.offset = self.group + 1, 0
         return batch
 
+    _CURSOR = ("group", "offset", "consumed_tokens")
+
+    def _identity(self):
+        return super()._identity() | {"reader_mode": "batched_epoch_v1", "micro_batch_size": self.micro_batch_size}
+
     def state_dict(self):
-        return {"reader_mode": "batched_epoch_v1", "fingerprint": self.fingerprint,
-                "pair_id": self.pair_id, "pairs": self.pairs, "seed": self.seed,
-                "chunk_tokens": self.chunk_tokens, "context_tokens": self.context_tokens,
-                "sampler_version": SAMPLER_VERSION, "micro_batch_size": self.micro_batch_size,
-                "group": self.group, "offset": self.offset, "consumed_tokens": self.consumed_tokens}
+        return self._identity() | {name: getattr(self, name) for name in self._CURSOR}
 
     def load_state_dict(self, state):
-        own = self.state_dict()
-        for key in own.keys() - {"group", "offset", "consumed_tokens"}:
-            if own[key] != state.get(key):
+        for key, value in self._identity().items():
+            if state.get(key) != value:
                 raise ValueError(f"Reader resume mismatch: {key}")
-        self.group, self.offset = state["group"], state["offset"]
-        self.consumed_tokens = state["consumed_tokens"]
+        for name in self._CURSOR:
+            setattr(self, name, state[name])
 
 
 def reader_for(cfg, topo, validation=False):
-    """Reader class selection (reference ``theseus/validation.py:13-22``)."""
-    if validation or cfg.get("training_mode", "sampled") != "epoch":
-        cls, extra = TokenStream, {}
-    elif cfg.get("micro_batch_size", 1) > 1:
-        cls, extra = BatchedEpochTokenStream, {"micro_batch_size": cfg["micro_batch_size"]}
-    else:
-        cls, extra = EpochTokenStream, {}
+    """The reader a run uses (reference ``theseus/validation.py:13-22``): sampled windows for validation and for
+    ``training_mode: sampled``, the epoch reader otherwise (lane-packed when ``micro_batch_size`` > 1)."""
     manifest = cfg["validation_manifest" if validation else "train_manifest"]
-    return cls(manifest, topo.rank, topo.world, cfg["chunk_tokens"], cfg["context_tokens"], cfg["seed"], **extra)
+    common = (manifest, topo.rank, topo.world, cfg["chunk_tokens"], cfg["context_tokens"], cfg["seed"])
+    if validation or cfg.get("training_mode", "sampled") != "epoch":
+        return TokenStream(*common)
+    if cfg.get("micro_batch_size", 1) > 1:
+        return BatchedEpochTokenStream(*common, micro_batch_size=cfg["micro_batch_size"])
+    return EpochTokenStream(*common)

@@ -221,12 +221,16 @@ class TextModel(nn.Module):
         inv_freq = 1.0 / (cfg.rope_theta ** (torch.arange(0, dim, 2, dtype=torch.int64).float() / dim))
         self.register_buffer("inv_freq", inv_freq, persistent=False)
 
-    def forward(self, ids, positions, cache):
-        """``positions``: first absolute position (int) or a tensor of consecutive positions."""
+    def forward(self, ids, positions, cache, stop_at=None):
+        """``positions``: first absolute position (int) or a tensor of consecutive positions. With ``stop_at``
+        the pass ends inside block ``stop_at`` and returns its mixer (attention) output: the blocks before it and
+        its own mixer update the cache; its residual and MLP, the later blocks and the final norm are not run."""
         start = int(positions[0]) if torch.is_tensor(positions) else int(positions)
         x = self.embed_tokens(ids)
         rope = T.rope_tables(self.inv_freq, start, ids.shape[1], x.device, x.dtype)
-        for layer in self.layers:
+        for index, layer in enumerate(self.layers):
+            if index == stop_at:
+                return layer.mixer(layer.input_layernorm(x), rope, cache)
             x = layer(x, rope, cache)
         return self.norm(x)
 

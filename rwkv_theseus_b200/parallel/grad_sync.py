@@ -18,9 +18,10 @@ loss statistics are summed in rank order on every rank, so all ranks apply the
 identical clip coefficient.
 
 The kernels run on a side stream: the main stream continues with the next
-layer's student while the exchange of this one moves over NVLink, and
-``wait`` joins the streams before the parameters are used again (the next
-step). The fp32 masters of the four decay matrices and the Adam moments are
+layer's student (or the next step's teacher forward) while the exchange of
+this one moves over NVLink. ``update`` returns an event per layer; the student
+waits on it where its parameters are next read (its next micro-step, a
+prediction, a checkpoint), so no step-wide join is needed. The fp32 masters of the four decay matrices and the Adam moments are
 sharded (each rank updates only its own range; compute reads the bf16 copy);
 ``gather_state`` assembles them on every rank for a checkpoint or export.
 
@@ -37,7 +38,7 @@ _WHAT = {1: "gradients ready", 2: "partial norm", 3: "updated shard"}
 
 
 class PeerGradExchange:
-    def __init__(self, topo, blocks=64, limit_s=300.0, fused=False):
+    def __init__(self, topo, blocks=256, limit_s=300.0, fused=False):
         if topo.world > 8:
             raise ValueError("peer exchange supports at most 8 ranks per node")
         self.topo = topo
@@ -82,7 +83,8 @@ class PeerGradExchange:
 
     # ---------------------------------------------------------------- update
     def update(self, student, lr, step):
-        """Reduce, clip, AdamW and all-gather one layer on the side stream."""
+        """Reduce, clip, AdamW and all-gather one layer on the side stream; returns the event that marks the end of
+        this layer's exchange (the caller waits on it where the layer's parameters are next read)."""
         tables = getattr(student, "peer_tables", None)
         if tables is None:
             raise RuntimeError("student buffers are not registered with the peer exchange")
@@ -98,7 +100,10 @@ class PeerGradExchange:
                                      float(cfg["weight_decay"]), float(cfg["clip_norm"]), int(step),
                                      int(student.decay_numel), self.epoch & 0xFFFFFFFF, self.limit_s, self.blocks,
                                      0 if self.fused else 1)
+        done = torch.cuda.Event()
+        done.record(self.stream)
         self.pending = True
+        return done
 
     def wait(self):
         """Join the exchange stream into the current stream."""

@@ -105,7 +105,8 @@ class Student:
 
     # ---------------------------------------------------------------- forward/backward
     def join_update(self):
-        """Make the current stream wait for this student's last local update (parameters, moments, report)."""
+        """Make the current stream wait for this student's last update (local fused update or peer exchange):
+        parameters, moments and report."""
         if self._update_done is not None:
             torch.cuda.current_stream(self.topo.device).wait_event(self._update_done)
             self._update_done = None
@@ -169,7 +170,7 @@ class Student:
         exchange = self._exchange()
         if exchange is not None:
             # Reduce-scatter, clip, AdamW on this rank's shard, all-gather; clears grad and stats on its stream.
-            exchange.update(self, lr, self.steps_done)
+            self._update_done = exchange.update(self, lr, self.steps_done)
             self.sharded = True
             self.grads_live = False
             return lr

@@ -1,17 +1,57 @@
-"""Optional Weights & Biases logging on the leader rank only.
+"""Optional Weights & Biases logging, on the leader rank only.
 
-Same observable contract as the reference ``theseus/tracking.py:7-54``:
-``wandb_run.json`` keeps the run identity so an online run resumes under its
-old id; metrics use ``progress/global_step`` as x-axis; ``train`` events log
-``sum_loss``/``mean_cos`` and ``layer_XX/{nmse,cosine,rrms,grad_norm,lr}``;
-``validation`` events log the same under ``val/``. Disabled mode never
-imports the SDK.
+Observable contract kept from the reference (``theseus/tracking.py:7-54``):
+
+* ``<output>/wandb_run.json`` records ``{project, entity, id, mode}``; a resumed
+  online run with the same project and entity continues under the old id;
+* ``progress/global_step`` is the x-axis of ``sum_loss``, ``mean_cos``,
+  ``layer_*`` and ``val/*``;
+* a ``train`` event logs ``sum_loss``, ``mean_cos`` and
+  ``layer_XX/{nmse,cosine,rrms,grad_norm,lr}``; a ``validation`` event logs the
+  same names under ``val/``; other events are not sent;
+* with ``wandb_mode: disabled`` (or on any other rank) the SDK is never imported.
 """
 import json
 from pathlib import Path
 from uuid import uuid4
 
-_LAYER_KEYS = {"nmse", "cosine", "rrms", "grad_norm", "lr"}
+TRACKED_LAYER_FIELDS = ("nmse", "cosine", "rrms", "grad_norm", "lr")
+STEP_AXIS = "progress/global_step"
+
+
+def flatten(event, fields):
+    """The W&B payload of one emitted event (``None`` for events that are not tracked)."""
+    prefix = {"train": "", "validation": "val/"}.get(event)
+    if prefix is None:
+        return None
+    payload = {STEP_AXIS: fields["step"], prefix + "sum_loss": fields["sum_loss"],
+               prefix + "mean_cos": fields["mean_cos"]}
+    for layer, values in fields["layers"].items():
+        payload.update({f"{prefix}{layer}/{name}": values[name] for name in TRACKED_LAYER_FIELDS if name in values})
+    return payload
+
+
+class RunIdentity:
+    """The ``wandb_run.json`` record: which run id a (resumed) job logs to."""
+
+    def __init__(self, output, cfg):
+        self.path = Path(output) / "wandb_run.json"
+        self.owner = {"project": cfg["wandb_project"], "entity": cfg["wandb_entity"]}
+        self.mode = cfg["wandb_mode"]
+
+    def resumable_id(self, resume):
+        """The previous run's id when this job may continue it: an online resume of an online run of the same
+        project and entity."""
+        if not (resume and self.mode == "online" and self.path.exists()):
+            return None
+        old = json.loads(self.path.read_text())
+        same_owner = all(old.get(key) == value for key, value in self.owner.items())
+        return old.get("id") if old.get("mode") == "online" and same_owner else None
+
+    def record(self, run_id):
+        staging = self.path.with_suffix(".tmp")
+        staging.write_text(json.dumps({**self.owner, "id": run_id, "mode": self.mode}))
+        staging.replace(self.path)
 
 
 class Tracker:
@@ -24,43 +64,29 @@ class Tracker:
             return
         import wandb
         self.cfg = cfg
-        root = Path(cfg["output"])
-        root.mkdir(parents=True, exist_ok=True)
-        identity_file = root / "wandb_run.json"
-        identity = {"project": cfg["wandb_project"], "entity": cfg["wandb_entity"]}
-        previous = None
-        if resume and identity_file.exists():
-            previous = json.loads(identity_file.read_text())
-        reuse = (cfg["wandb_mode"] == "online" and previous is not None
-                 and previous.get("mode") == "online"
-                 and all(previous.get(key) == value for key, value in identity.items()))
-        run_id = previous["id"] if reuse else uuid4().hex[:8]
-        self.run = wandb.init(
-            project=cfg["wandb_project"], entity=cfg["wandb_entity"], name=cfg["wandb_name"],
-            id=run_id, mode=cfg["wandb_mode"], resume="allow" if reuse else None, dir=str(root),
-            config={k: v for k, v in cfg.items() if not k.startswith("wandb_")}, save_code=False,
-            settings=wandb.Settings(init_timeout=60, console="off"))
-        tmp = identity_file.with_suffix(".tmp")
-        tmp.write_text(json.dumps({**identity, "id": run_id, "mode": cfg["wandb_mode"]}))
-        tmp.replace(identity_file)
-        self.run.define_metric("progress/global_step")
-        for pattern in ("sum_loss", "mean_cos", "layer_*", "val/*"):
-            self.run.define_metric(pattern, step_metric="progress/global_step")
+        output = Path(cfg["output"])
+        output.mkdir(parents=True, exist_ok=True)
+        identity = RunIdentity(output, cfg)
+        continued = identity.resumable_id(resume)
+        run_id = continued or uuid4().hex[:8]
+        self.run = wandb.init(project=cfg["wandb_project"], entity=cfg["wandb_entity"], name=cfg["wandb_name"],
+                              id=run_id, mode=cfg["wandb_mode"], resume="allow" if continued else None,
+                              dir=str(output), save_code=False,
+                              config={key: value for key, value in cfg.items() if not key.startswith("wandb_")},
+                              settings=wandb.Settings(init_timeout=60, console="off"))
+        identity.record(run_id)
+        self.run.define_metric(STEP_AXIS)
+        for series in ("sum_loss", "mean_cos", "layer_*", "val/*"):
+            self.run.define_metric(series, step_metric=STEP_AXIS)
 
     def log(self, event, fields):
-        if self.run is None or event not in ("train", "validation"):
+        if self.run is None:
             return
-        prefix = "val/" if event == "validation" else ""
-        values = {"progress/global_step": fields["step"]}
-        for key in ("sum_loss", "mean_cos"):
-            values[prefix + key] = fields[key]
-        for layer, details in fields["layers"].items():
-            for key, value in details.items():
-                if key in _LAYER_KEYS:
-                    values[f"{prefix}{layer}/{key}"] = value
-        self.run.log(values)
+        payload = flatten(event, fields)
+        if payload is not None:
+            self.run.log(payload)
 
     def finish(self, exit_code=0):
-        if self.run is not None:
-            self.run.finish(exit_code=exit_code)
-            self.run = None
+        run, self.run = self.run, None
+        if run is not None:
+            run.finish(exit_code=exit_code)

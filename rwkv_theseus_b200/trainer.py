@@ -1,20 +1,27 @@
-"""Parallel Layer Migration training loop (reference ``train.py:52-260``).
+"""Parallel Layer Migration training (reference ``train.py:52-260``).
 
-Per optimizer step and micro-batch: ONE frozen-teacher forward captures the
-input (after ``input_layernorm``) and attention output of every full-attention
-block; then, layer by layer, the TimeMix student of that block runs forward
-and backward on the captured pair with its own carried state (detached at
-chunk boundaries, reset at window boundaries). On the last micro-batch each
-layer's gradient bucket is reduced across ranks and the layer is updated
-(1/count scale, clip, AdamW) immediately, before the next layer's work.
+Per optimizer step and micro-batch: ONE frozen-teacher forward captures, at
+every full-attention block, the attention input (after ``input_layernorm``)
+and output; then, layer by layer, that block's TimeMix student runs forward and
+backward on the captured pair with its own carried state (detached between
+chunks, reset at window starts). On the last micro-batch each layer's gradients
+are reduced across ranks and the layer is updated (1/count, clip, AdamW) right
+away, before the next layer's work.
 
-Differences from the reference loop, all semantics-preserving:
-* exhausted ranks contribute zero gradients and a zero token count to the
-  explicit per-layer collective instead of running a dummy forward;
-* count, grad norm and error flags stay on the device; the step's metrics are
-  read with one device-to-host copy at the end of the step, where a
-  non-finite norm or an empty update raises as ``clip_grad_norm_(...,
-  error_if_nonfinite=True)`` / the token check would.
+Semantics kept from the reference, mechanics of this implementation:
+* exhausted ranks add zero gradients and a zero token count to the explicit
+  per-layer reduction instead of running a dummy forward;
+* the teacher forward ends at the last migrated block's attention output (the
+  blocks after it, its MLP and the final norm feed no capture);
+* token count, grad norm and error flags stay on the device; one copy per step
+  brings them to the host, where a non-finite norm or an empty update raises as
+  ``clip_grad_norm_(..., error_if_nonfinite=True)`` and the token check would;
+* with the peer-memory exchange each layer's update runs on a side stream and
+  the layer's next use waits for it (no step-wide join).
+
+``MigrationJob`` is the whole run (set-up, resume, steps with logging,
+validation and checkpoints, final assembly and export); ``StepEngine`` is the
+hot loop body that ``bench.py`` also drives.
 """
 import gc
 import json
@@ -25,7 +32,7 @@ from pathlib import Path
 import numpy as np
 import torch
 
-from .checkpoint import model_fingerprint, read_checkpoint, restore_rng, save_checkpoint, validate_resume, cpu_tree
+from .checkpoint import cpu_tree, model_fingerprint, read_checkpoint, restore_rng, save_checkpoint, validate_resume
 from .config import steps_for
 from .data import digest_file, reader_for
 from .losses import metrics
@@ -40,110 +47,123 @@ from .tracking import Tracker
 from .validation import summarize_layers, validate_composition, validate_parallel
 
 
+class Journal:
+    """``metrics.jsonl`` in the output directory plus the tracker; written by the leader only."""
+
+    def __init__(self, topo, cfg):
+        self.topo = topo
+        self.path = Path(cfg["output"]) / "metrics.jsonl"
+
+    def __call__(self, event, **fields):
+        if self.topo.rank != self.topo.leader:
+            return
+        self.path.parent.mkdir(parents=True, exist_ok=True)
+        with self.path.open("a") as sink:
+            sink.write(json.dumps({"event": event, **fields}, ensure_ascii=False) + "\n")
+        if self.topo.tracker is not None:
+            self.topo.tracker.log(event, fields)
+
+
 def emit(topo, cfg, event, **fields):
-    if topo.rank != topo.leader:
-        return
-    line = json.dumps({"event": event, **fields}, ensure_ascii=False)
-    root = Path(cfg["output"])
-    root.mkdir(parents=True, exist_ok=True)
-    with (root / "metrics.jsonl").open("a") as f:
-        f.write(line + "\n")
-    if topo.tracker is not None:
-        topo.tracker.log(event, fields)
+    Journal(topo, cfg)(event, **fields)
 
 
 def emit_profile(topo, cfg, step, phases):
     """``profile`` event: per-phase milliseconds of the step, maximum over ranks (Gloo gather)."""
     import torch.distributed as dist
+    per_rank = [phases]
     if topo.world > 1:
-        everyone = [None] * topo.world
-        dist.all_gather_object(everyone, phases)
-    else:
-        everyone = [phases]
-    merged = {}
-    for entry in everyone:
+        per_rank = [None] * topo.world
+        dist.all_gather_object(per_rank, phases)
+    slowest = {}
+    for entry in per_rank:
         for name, ms in entry.items():
-            merged[name] = max(merged.get(name, 0.0), ms)
-    teacher = merged.get("teacher", 0.0)
-    students = sum(v for k, v in merged.items() if k.startswith("student_"))
-    updates = sum(v for k, v in merged.items() if k.startswith("update_"))
-    emit(topo, cfg, "profile", step=step, teacher_ms=teacher, students_ms=students, updates_ms=updates,
-         exchange_join_ms=merged.get("exchange_join", 0.0), phases_ms=merged)
+            slowest[name] = max(slowest.get(name, 0.0), ms)
+    by_kind = lambda prefix: sum(ms for name, ms in slowest.items() if name.startswith(prefix))  # noqa: E731
+    emit(topo, cfg, "profile", step=step, teacher_ms=slowest.get("teacher", 0.0), students_ms=by_kind("student_"),
+         updates_ms=by_kind("update_"), exchange_join_ms=slowest.get("exchange_join", 0.0), phases_ms=slowest)
 
 
 class StepEngine:
-    """The hot loop body: teacher forward + per-layer student updates."""
+    """One optimizer step of every layer: teacher forward(s), per-layer micro-steps and updates."""
 
     def __init__(self, cfg, topo, runner, order, students, captures):
         self.cfg, self.topo, self.runner = cfg, topo, runner
         self.order, self.students, self.captures = order, students, captures
         self.device = topo.device
-        self._staging = [None, None]   # pinned id buffers, used alternately
-        self._staged = [None, None]    # event after the copy out of each buffer
-        self._turn = 0
+        self.last_capture = max(order)
         self.profiler = StepProfiler(self.device)
+        self._pinned = [None, None]   # two pinned id buffers used in turn
+        self._copied = [None, None]   # event after the copy that last read each buffer
+        self._turn = 0
         if self.device.type == "cuda":
             for student in students.values():
                 student.overlap_update = True
 
     def _to_device(self, ids):
-        """Stage token ids through two persistent pinned buffers (alternating), copy asynchronously. A buffer
-        is refilled only after the copy that last read it has run (its event), since the host may be more
-        than a step ahead of the device."""
+        """Token ids to the device through two alternating pinned buffers (asynchronous copy). A buffer is
+        refilled only after the copy that last read it ran, since the host may run ahead of the device."""
         if self.device.type != "cuda":
             return ids
-        n, i = ids.numel(), self._turn
+        slot = self._turn
         self._turn ^= 1
-        if self._staged[i] is not None:
-            self._staged[i].synchronize()
-        if self._staging[i] is None or self._staging[i].numel() < n:
-            self._staging[i] = torch.empty(max(n, 1 << 16), dtype=torch.int64, pin_memory=True)
-        host = self._staging[i][:n].view(ids.shape)
-        host.copy_(ids)
-        out = host.to(self.device, non_blocking=True)
-        self._staged[i] = torch.cuda.Event()
-        self._staged[i].record()
-        return out
+        if self._copied[slot] is not None:
+            self._copied[slot].synchronize()
+        if self._pinned[slot] is None or self._pinned[slot].numel() < ids.numel():
+            self._pinned[slot] = torch.empty(max(ids.numel(), 1 << 16), dtype=torch.int64, pin_memory=True)
+        staged = self._pinned[slot][:ids.numel()].view(ids.shape)
+        staged.copy_(ids)
+        on_device = staged.to(self.device, non_blocking=True)
+        self._copied[slot] = torch.cuda.Event()
+        self._copied[slot].record()
+        return on_device
+
+    def _teacher(self, batch):
+        if batch["reset"]:
+            self.runner.reset()
+            for student in self.students.values():
+                student.state = None
+        if self.runner.cache.cursor != batch["position"]:
+            raise RuntimeError("Cache position differs from consumed token stream")
+        with self.profiler.phase("teacher"):
+            self.runner.forward(self._to_device(batch["ids"]), through_layer=self.last_capture)
 
     def step(self, reader):
-        """One optimizer update of every layer; returns per-layer device reports."""
-        cfg, prof = self.cfg, self.profiler
-        prof.reset()
-        for micro in range(cfg["grad_accum_steps"]):
+        """One optimizer update of every layer; returns {layer: device report [nmse, cos, count, norm, error]}."""
+        profiler = self.profiler
+        profiler.reset()
+        micro_steps = self.cfg["grad_accum_steps"]
+        for micro in range(micro_steps):
             batch = reader.next()
             if batch is not None:
-                if batch["reset"]:
-                    self.runner.reset()
-                    for student in self.students.values():
-                        student.state = None
-                if self.runner.cache.cursor != batch["position"]:
-                    raise RuntimeError("Cache position differs from consumed token stream")
-                with prof.phase("teacher"):
-                    self.runner.forward(self._to_device(batch["ids"]))
-            last = micro == cfg["grad_accum_steps"] - 1
+                self._teacher(batch)
+            updating = micro == micro_steps - 1
             for layer in self.order:
                 student, capture = self.students[layer], self.captures[layer]
                 if batch is not None:
-                    with prof.phase(f"student_{layer:02d}"):
+                    with profiler.phase(f"student_{layer:02d}"):
                         student.micro_step(capture.x, capture.y)
                     capture.x = capture.y = None
-                if last:
-                    with prof.phase(f"update_{layer:02d}"):
+                if updating:
+                    with profiler.phase(f"update_{layer:02d}"):
                         student.reduce()
                         student.update()
-        with prof.phase("exchange_join"):
-            self.topo.join_grad_sync()
-        return {layer: s.report for layer, s in self.students.items()}
+        return {layer: student.report for layer, student in self.students.items()}
 
     def read_metrics(self, reports):
-        """One device-to-host copy of all layer reports; raises on update errors."""
+        """One device-to-host copy of all layer reports; raises on update errors or a kernel that gave up a
+        bounded wait."""
         for student in self.students.values():
             student.join_update()
         rows = torch.stack([reports[layer] for layer in self.order]).double().cpu().tolist()
         self.topo.check_grad_sync()
-        if self.topo.device.type == "cuda" and native().gemm_fault():
-            raise RuntimeError("a tcgen05 GEMM gave up a bounded wait (results of this step are invalid)")
-        layer_metrics = {}
+        if self.topo.device.type == "cuda":
+            ext = native()
+            if ext.gemm_fault():
+                raise RuntimeError("a tcgen05 GEMM gave up a bounded wait (results of this step are invalid)")
+            if ext.wkv7_tc_fault():
+                raise RuntimeError("a tcgen05 WKV7 kernel gave up a bounded wait (results of this step are invalid)")
+        report = {}
         for layer, (nmse, cos, count, norm, bad) in zip(self.order, rows):
             if count <= 0:
                 raise RuntimeError("No training tokens in update")
@@ -151,161 +171,210 @@ class StepEngine:
                 raise RuntimeError(f"The total norm of gradients for layer {layer} is non-finite")
             student = self.students[layer]
             lr = self.cfg["lr"] * lr_factor(student.steps_done - 1, self.cfg, student.total_steps)
-            layer_metrics[f"layer_{layer:02d}"] = metrics(torch.tensor([nmse, cos, count])) | {
-                "grad_norm": norm, "lr": lr}
-        return layer_metrics
+            report[f"layer_{layer:02d}"] = metrics(torch.tensor([nmse, cos, count])) | {"grad_norm": norm, "lr": lr}
+        return report
 
 
 def run(cfg, resume=None, stop_after=None):
+    """Train (or resume) a migration run end to end; the tracker is closed with the run's outcome."""
     tracker = Tracker()
     try:
-        _run(cfg, resume, stop_after, tracker)
+        MigrationJob(cfg, resume, stop_after, tracker).run()
     except BaseException:
         tracker.finish(exit_code=1)
         raise
-    else:
-        tracker.finish()
+    tracker.finish()
 
 
-def _check_data(cfg):
-    for manifest in (cfg["train_manifest"], cfg["validation_manifest"]):
-        data = json.loads(Path(manifest).read_text())
-        for source in data["sources"]:
-            for field in ("tokens", "offsets"):
-                if digest_file(Path(manifest).parent / source[field]) != source[field + "_sha256"]:
-                    raise ValueError(f"Data content changed: {source[field]}")
+class MigrationJob:
+    def __init__(self, cfg, resume, stop_after, tracker):
+        self.cfg, self.resume, self.stop_after, self.tracker = cfg, resume, stop_after, tracker
+        self.checkpoint = self.meta = None
+        self.delta = {}
 
+    # ---------------------------------------------------------------- set-up
+    def _agree_and_seed(self):
+        topo, cfg = self.topo, self.cfg
+        topo.assert_same({"config": cfg, "resume": self.resume, "stop_after": self.stop_after,
+                          "profile": os.environ.get("THESEUS_PROFILE", "0")}, "run configuration")
+        torch.set_num_threads(1)
+        random.seed(cfg["seed"] + topo.rank)
+        np.random.seed(cfg["seed"] + topo.rank)
+        torch.manual_seed(cfg["seed"])
 
-def _check_vocab(cfg, model):
-    for manifest in (cfg["train_manifest"], cfg["validation_manifest"]):
-        data = json.loads(Path(manifest).read_text())
-        if data["vocab_size"] > model.config.vocab_size:
-            raise ValueError("Dataset vocabulary exceeds model embedding size")
-        for name, expected in data.get("tokenizer_files", {}).items():
-            token_file = Path(cfg["model"]) / name
-            if not token_file.exists() or digest_file(token_file) != expected:
-                raise ValueError(f"Dataset/model tokenizer differs: {name}")
+    def _manifests(self):
+        return [(manifest, json.loads(Path(manifest).read_text()))
+                for manifest in (self.cfg["train_manifest"], self.cfg["validation_manifest"])]
 
+    def _check_data_bytes(self):
+        for manifest, spec in self._manifests():
+            for source in spec["sources"]:
+                for field in ("tokens", "offsets"):
+                    if digest_file(Path(manifest).parent / source[field]) != source[f"{field}_sha256"]:
+                        raise ValueError(f"Data content changed: {source[field]}")
 
-def _run(cfg, resume, stop_after, tracker):
-    from tqdm.auto import tqdm
-    topo = Topology(cfg["distributed_backend"], cfg["timeout_minutes"])
-    topo.tracker = tracker
-    topo.assert_same({"config": cfg, "resume": resume, "stop_after": stop_after,
-                      "profile": os.environ.get("THESEUS_PROFILE", "0")}, "run configuration")
-    torch.set_num_threads(1)
-    random.seed(cfg["seed"] + topo.rank)
-    np.random.seed(cfg["seed"] + topo.rank)
-    torch.manual_seed(cfg["seed"])
-    if topo.rank == 0:
-        _check_data(cfg)
-    if not resume and (Path(cfg["output"]) / "latest").exists():
-        raise ValueError("Output already has checkpoints; use --resume or a new output directory")
-    topo.barrier()
-    base_id = topo.broadcast_object(model_fingerprint(cfg["model"]) if topo.rank == topo.leader else None)
-    model = load_model(cfg["model"], topo.device)
-    _check_vocab(cfg, model)
-    order = migration_order(model, cfg["expected_attention_layers"])
-    if cfg["cosine_weight"] != 0:
-        raise ValueError("Parallel migration requires cosine_weight=0")
-    meta, delta, checkpoint = None, {}, None
-    if resume:
-        checkpoint, meta, delta = read_checkpoint(resume)
-        if meta.get("training_topology") != "parallel_layers_v1":
+    def _check_data_fits_model(self):
+        for _, spec in self._manifests():
+            if spec["vocab_size"] > self.model.config.vocab_size:
+                raise ValueError("Dataset vocabulary exceeds model embedding size")
+            for name, expected in spec.get("tokenizer_files", {}).items():
+                found = Path(self.cfg["model"]) / name
+                if not found.exists() or digest_file(found) != expected:
+                    raise ValueError(f"Dataset/model tokenizer differs: {name}")
+
+    def _open(self):
+        cfg = self.cfg
+        self.topo = Topology(cfg["distributed_backend"], cfg["timeout_minutes"])
+        self.topo.tracker = self.tracker
+        self.journal = Journal(self.topo, cfg)
+        self._agree_and_seed()
+        if self.topo.rank == 0:
+            self._check_data_bytes()   # before any model allocation
+        if not self.resume and (Path(cfg["output"]) / "latest").exists():
+            raise ValueError("Output already has checkpoints; use --resume or a new output directory")
+        self.topo.barrier()
+        leader = self.topo.rank == self.topo.leader
+        self.base_id = self.topo.broadcast_object(model_fingerprint(cfg["model"]) if leader else None)
+        self.model = load_model(cfg["model"], self.topo.device)
+        self._check_data_fits_model()
+        self.order = migration_order(self.model, cfg["expected_attention_layers"])
+        if cfg["cosine_weight"] != 0:
+            raise ValueError("Parallel migration requires cosine_weight=0")
+
+    def _load_resume(self):
+        """Read the checkpoint to resume. True when it is complete and already exported (nothing left to do)."""
+        if not self.resume:
+            return False
+        self.checkpoint, self.meta, self.delta = read_checkpoint(self.resume)
+        if self.meta.get("training_topology") != "parallel_layers_v1":
             raise ValueError("Sequential checkpoints cannot resume parallel migration; start a new run")
-        validate_resume(meta, cfg, topo, base_id, order)
-        if set(delta) != set(order):
+        validate_resume(self.meta, self.cfg, self.topo, self.base_id, self.order)
+        if set(self.delta) != set(self.order):
             raise ValueError("Checkpoint must contain every migration layer")
-    export_meta = Path(cfg["output"]) / "converted" / "theseus.json"
-    if meta and meta["complete"] and export_meta.exists():
-        exported = json.loads(export_meta.read_text())
-        if (exported.get("migration_fingerprint") != digest_file(checkpoint / "migrated.safetensors")
-                or exported.get("base_fingerprint") != base_id):
+        exported = Path(self.cfg["output"]) / "converted" / "theseus.json"
+        if not (self.meta["complete"] and exported.exists()):
+            return False
+        record = json.loads(exported.read_text())
+        if (record.get("migration_fingerprint") != digest_file(self.checkpoint / "migrated.safetensors")
+                or record.get("base_fingerprint") != self.base_id):
             raise ValueError("Existing converted model differs from resumed checkpoint; choose a new output")
-        topo.close()
-        return
-    saved = checkpoint
-    tracker.start(cfg, topo, resume=bool(resume))
-    runner = Runner(model)
-    reader = reader_for(cfg, topo)
-    if cfg["training_mode"] == "epoch":
-        max_steps = (max(reader.rank_chunks) + cfg["grad_accum_steps"] - 1) // cfg["grad_accum_steps"]
-    else:
-        max_steps = steps_for(cfg, 0)
-    step0 = meta["step"] if meta else 0
-    students, captures = {}, {}
-    for index, layer in enumerate(order):
-        torch.manual_seed(cfg["seed"] + index)
-        students[layer] = Student(model.config, layer, cfg, topo, delta.get(layer), total_steps=max_steps)
-        captures[layer] = Capture(model.model.layers[layer].self_attn)
-    if meta and not meta["complete"]:
-        local = torch.load(checkpoint / "ranks" / f"rank_{topo.rank:05d}.pt", map_location="cpu", weights_only=False)
-        runner.load_state_dict(local["runner"])
-        reader.load_state_dict(local["reader"])
-        opt = torch.load(checkpoint / "optimizer.pt", map_location=topo.device, weights_only=False)
-        for layer, student in students.items():
-            student.state = state_to_device(local["students"][layer], topo.device)
-            student.load_optimizer_state(opt[layer]["optimizer"], opt[layer]["scheduler"])
-            if student.steps_done != step0:
+        return True
+
+    def _build(self):
+        cfg = self.cfg
+        self.runner = Runner(self.model)
+        self.reader = reader_for(cfg, self.topo)
+        if cfg["training_mode"] == "epoch":
+            self.max_steps = -(-max(self.reader.rank_chunks) // cfg["grad_accum_steps"])
+        else:
+            self.max_steps = steps_for(cfg, 0)
+        self.step0 = self.meta["step"] if self.meta else 0
+        self.students, self.captures = {}, {}
+        for index, layer in enumerate(self.order):
+            torch.manual_seed(cfg["seed"] + index)  # the same per-layer init stream as the reference
+            self.students[layer] = Student(self.model.config, layer, cfg, self.topo, self.delta.get(layer),
+                                           total_steps=self.max_steps)
+            self.captures[layer] = Capture(self.model.model.layers[layer].self_attn)
+        if self.meta and not self.meta["complete"]:
+            self._restore_midstream()
+        self.delta = {}
+        self.topo.barrier()
+        self.engine = StepEngine(cfg, self.topo, self.runner, self.order, self.students, self.captures)
+
+    def _restore_midstream(self):
+        device = self.topo.device
+        mine = torch.load(self.checkpoint / "ranks" / f"rank_{self.topo.rank:05d}.pt", map_location="cpu",
+                          weights_only=False)
+        self.runner.load_state_dict(mine["runner"])
+        self.reader.load_state_dict(mine["reader"])
+        optimizer = torch.load(self.checkpoint / "optimizer.pt", map_location=device, weights_only=False)
+        for layer, student in self.students.items():
+            student.state = state_to_device(mine["students"][layer], device)
+            student.load_optimizer_state(optimizer[layer]["optimizer"], optimizer[layer]["scheduler"])
+            if student.steps_done != self.step0:
                 raise ValueError("Checkpoint scheduler step differs from manifest step")
-        restore_rng(local["rng"])
-        del local, opt
-    delta.clear()
-    topo.barrier()
-    engine = StepEngine(cfg, topo, runner, order, students, captures)
-    progress = tqdm(total=max_steps, initial=step0, desc=f"Parallel migration ({len(order)} layers)",
-                    unit="step", dynamic_ncols=True, mininterval=0.5,
-                    disable=topo.rank != topo.leader or os.environ.get("TQDM_DISABLE") == "1")
-    for step in range(step0 + 1, max_steps + 1):
-        reports = engine.step(reader)
-        layer_metrics = engine.read_metrics(reports)
+        restore_rng(mine["rng"])
+
+    # ---------------------------------------------------------------- steps
+    def _log_step(self, step, layer_metrics, progress):
         summary = summarize_layers(layer_metrics)
         progress.set_postfix(sum_loss=f"{summary['sum_loss']:.5f}", mean_cos=f"{summary['mean_cos']:.5f}",
                              refresh=False)
         progress.update(1)
-        if step % cfg["log_interval"] == 0 or step == 1:
-            emit(topo, cfg, "train", step=step, **summary,
-                 tokens=next(iter(layer_metrics.values()))["tokens"], layers=layer_metrics)
-        if engine.profiler.on:
-            emit_profile(topo, cfg, step, engine.profiler.summary())
-        complete = step == max_steps
-        if complete and cfg["training_mode"] == "epoch" and not reader.exhausted:
-            raise RuntimeError("Training ended before the local token shard was exhausted")
-        if complete or (cfg["validation_interval"] and step % cfg["validation_interval"] == 0):
-            result = validate_parallel(topo, cfg, runner, students, captures)
-            emit(topo, cfg, "validation", step=step, **result)
-        stopping = stop_after is not None and step - step0 >= stop_after
-        if complete or stopping or (cfg["checkpoint_interval"] and step % cfg["checkpoint_interval"] == 0):
-            saved = save_checkpoint(topo, cfg, step, complete, order, runner, reader, base_id, students)
-            emit(topo, cfg, "checkpoint", path=str(saved), complete=complete)
-        if stopping and not complete:
+        if step == 1 or step % self.cfg["log_interval"] == 0:
+            tokens = next(iter(layer_metrics.values()))["tokens"]
+            self.journal("train", step=step, **summary, tokens=tokens, layers=layer_metrics)
+        if self.engine.profiler.on:
+            emit_profile(self.topo, self.cfg, step, self.engine.profiler.summary())
+
+    def _due(self, step, interval_key, complete):
+        interval = self.cfg[interval_key]
+        return complete or bool(interval and step % interval == 0)
+
+    def _train(self):
+        """The step loop. Returns False when ``stop_after`` ended it before the last step."""
+        from tqdm.auto import tqdm
+        cfg = self.cfg
+        progress = tqdm(total=self.max_steps, initial=self.step0, unit="step", dynamic_ncols=True,
+                        desc=f"Parallel migration ({len(self.order)} layers)", mininterval=0.5,
+                        disable=self.topo.rank != self.topo.leader or os.environ.get("TQDM_DISABLE") == "1")
+        self.saved = self.checkpoint
+        try:
+            for step in range(self.step0 + 1, self.max_steps + 1):
+                layer_metrics = self.engine.read_metrics(self.engine.step(self.reader))
+                self._log_step(step, layer_metrics, progress)
+                complete = step == self.max_steps
+                if complete and cfg["training_mode"] == "epoch" and not self.reader.exhausted:
+                    raise RuntimeError("Training ended before the local token shard was exhausted")
+                if self._due(step, "validation_interval", complete):
+                    result = validate_parallel(self.topo, cfg, self.runner, self.students, self.captures)
+                    self.journal("validation", step=step, **result)
+                stopping = self.stop_after is not None and step - self.step0 >= self.stop_after
+                if stopping or self._due(step, "checkpoint_interval", complete):
+                    self.saved = save_checkpoint(self.topo, cfg, step, complete, self.order, self.runner,
+                                                 self.reader, self.base_id, self.students)
+                    self.journal("checkpoint", path=str(self.saved), complete=complete)
+                if stopping and not complete:
+                    return False
+            return True
+        finally:
             progress.close()
-            for capture in captures.values():
+            for capture in self.captures.values():
                 capture.close()
-            topo.close()
+
+    # ---------------------------------------------------------------- assembly
+    def _assemble_and_export(self):
+        """Reload the pristine base, install every trained student in place of its attention, validate the
+        assembled model and write the export."""
+        cfg = self.cfg
+        self.topo.join_grad_sync()
+        for student in self.students.values():
+            student.sync_state()
+        trained = {layer: cpu_tree(student.weights()) for layer, student in self.students.items()}
+        self.students.clear()
+        self.runner = self.model = self.engine = None
+        gc.collect()
+        if self.topo.device.type == "cuda":
+            torch.cuda.empty_cache()
+        self.model = load_model(cfg["model"], self.topo.device)
+        for layer in self.order:
+            install(self.model, layer, cfg, trained.pop(layer))
+        result = validate_composition(self.topo, cfg, Runner(self.model))
+        self.journal("composition_validation", **result)
+        export = Path(cfg["output"]) / "converted"
+        if self.topo.rank == self.topo.leader:
+            from .inference import save_export
+            save_export(self.model, export, cfg, self.order, self.base_id, checkpoint=self.saved)
+        self.topo.barrier()
+        self.journal("finished", layers=len(self.order), export=str(export))
+
+    def run(self):
+        self._open()
+        if self._load_resume():
+            self.topo.close()
             return
-    progress.close()
-    for capture in captures.values():
-        capture.close()
-    topo.join_grad_sync()
-    for s in students.values():
-        s.sync_state()
-    weights = {layer: cpu_tree(s.weights()) for layer, s in students.items()}
-    students.clear()
-    del runner, model, engine
-    gc.collect()
-    if topo.device.type == "cuda":
-        torch.cuda.empty_cache()
-    model = load_model(cfg["model"], topo.device)
-    for layer in order:
-        install(model, layer, cfg, weights[layer])
-    del weights
-    runner = Runner(model)
-    result = validate_composition(topo, cfg, runner)
-    emit(topo, cfg, "composition_validation", **result)
-    if topo.rank == topo.leader:
-        from .inference import save_export
-        save_export(model, Path(cfg["output"]) / "converted", cfg, order, base_id, checkpoint=saved)
-    topo.barrier()
-    emit(topo, cfg, "finished", layers=len(order), export=str(Path(cfg["output"]) / "converted"))
-    topo.close()
+        self.tracker.start(self.cfg, self.topo, resume=bool(self.resume))
+        self._build()
+        if self._train():
+            self._assemble_and_export()
+        self.topo.close()
