@@ -23,6 +23,23 @@
 namespace {
 
 using namespace wtc;
+
+// Optional phase timing (compile with -DWKV7_TC_TRACE): thread 0 of every CTA adds the %globaltimer time spent
+// since the previous mark to a per-phase total; rt_wkv7_tc_trace_read copies the totals out. Off by default.
+#ifdef WKV7_TC_TRACE
+__device__ unsigned long long wkv7_trace_ns[64];
+#define WKV_TRACE_BEGIN unsigned long long trace_t0_ = threadIdx.x == 0 ? sm100::globaltimer() : 0ull;
+#define WKV_TRACE(slot)                                                       \
+  if (threadIdx.x == 0) {                                                     \
+    const unsigned long long trace_now_ = sm100::globaltimer();               \
+    atomicAdd(&wkv7_trace_ns[(slot)], trace_now_ - trace_t0_);                \
+    trace_t0_ = trace_now_;                                                   \
+  }
+#else
+#define WKV_TRACE_BEGIN
+#define WKV_TRACE(slot)
+#endif
+
 constexpr int KB = 1024;
 constexpr int MAT = N * N;
 enum { REC_G = 0, REC_H0 = 1, REC_Q = 2, REC_Y0 = 3, REC_T = 4, REC_MATS = 5 };  // forward record (fwd file)
@@ -195,6 +212,7 @@ wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_c
   const float* S0g = ckpt + (bh * (chunks + 1) + c) * MAT;
   float* wk = work + ch * WK_MATS * MAT;
   const int nvalid = min(L, T - c * L);
+  WKV_TRACE_BEGIN
 
   if (tid == 0) {
     sm100::mbar_init(&bars[0], 1);
@@ -225,6 +243,7 @@ wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_c
   bool ok = wait_all(&bars[0], 0);
   const bool t_issued = ok;
   uint32_t mph = 0;
+  WKV_TRACE(16)
   if (ok) {
     build_lambda(Rw, lam, nvalid, tid);
     {  // X1 (A~ / R~), X2 (B~ / K~), BKH (B^ / K^): row tid
@@ -250,6 +269,7 @@ wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_c
         put4(BKH, 128, tid, j0, xh[0], xh[1], xh[2], xh[3]);
       }
     }
+    WKV_TRACE(17)
     {  // V^T (row i < 64), dY^T (row i, threads 64..127)
       const int i = tid & 63;
       uint8_t* dst = tid < 64 ? VT : DYT;
@@ -259,6 +279,7 @@ wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_c
         put4(dst, 64, i, s, raw(src, s, i), raw(src, s + 1, i), raw(src, s + 2, i), raw(src, s + 3, i));
     }
     tc_sync();
+    WKV_TRACE(18)
     // ---- MMA1 (cols 0..127): chunk matrices
     if (tid == 0) {
       mma_tf32_tiles(tmem, sm100::smem_u32(X1), 128, sm100::smem_u32(X2), 128, 8, sm100::idesc_tf32(128, 128),
@@ -280,6 +301,7 @@ wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_c
     sm100::tc_fence_after();
   }
   if (ok) {
+    WKV_TRACE(19)
     // ---- epilogue 1: M_ak (strict) -> MAK rows; [M_rb^T; M_rk^T] -> MRT (transposed, from rows t >= 64)
     float d[64];
     const int t = tid & 63;
@@ -321,6 +343,7 @@ wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_c
     sm100::tc_fence_after();
   }
   if (ok) {
+    WKV_TRACE(20)
     // ---- epilogue 2: Z^T and dU^T (transposed, rows t < 64); T^T and M_ak^T (threads 64..127, from smem/TMEM)
     if (tid < 64) {
       float d[64];
@@ -341,6 +364,7 @@ wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_c
              get1(Tt, 64, t0 + 3, s));
     }
     tc_sync();
+    WKV_TRACE(21)
     // ---- MMA-U (cols 64..127): U = T Z;  MMA-dZ (cols 0..63): dZ = T^T dU  (64-row operands read as 128 rows)
     if (tid == 0) {
       mma_tf32_tiles(tmem + 64, sm100::smem_u32(Tt), 64, sm100::smem_u32(ZFT), 64, 8, sm100::idesc_tf32(128, 64),
@@ -354,6 +378,7 @@ wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_c
     sm100::tc_fence_after();
   }
   if (ok) {
+    WKV_TRACE(22)
     // ---- epilogue 3: U and dZ rows (tf32) to the work record; dZ^T for dV
     if (tid < 64) {
       float d[64];
@@ -371,6 +396,7 @@ wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_c
         *reinterpret_cast<float4*>(gu + i) = make_float4(tf32r(d[i]), tf32r(d[i + 1]), tf32r(d[i + 2]), tf32r(d[i + 3]));
     }
     tc_sync();
+    WKV_TRACE(23)
     // ---- MMA-dV (cols 192..255, rows 64..127): dV += M_ak^T dZ  (M_ak^T read as the lower half of 128 rows)
     if (tid == 0) {
       mma_tf32_tiles(tmem + 192, sm100::smem_u32(MAKT) - 8192, 64, sm100::smem_u32(DZT), 64, 8,
@@ -392,6 +418,7 @@ wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_c
       for (int i = 0; i < 64; i += 4) *reinterpret_cast<float4*>(out + i) = make_float4(d[i], d[i + 1], d[i + 2], d[i + 3]);
     }
   }
+  WKV_TRACE(24)
   if (!ok && tid == 0) atomicCAS(&wkv7_tc_bwd_fault_word, 0, 0x200 | stage);  // state kernel, failing wait
   if (!ok) {
     if (stage > 1) sm100::mbar_wait_bounded(&bars[1], mph);
@@ -450,7 +477,9 @@ wkv7_tc_bwd_grad_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_co
   float* EB = EA + MAT;                                 // F k~
   const long bh = (long)bb * H + h, ch = bh * chunks + c;
   const float* S0g = ckpt + (bh * (chunks + 1) + c) * MAT;
+
   const float* wk = work + ch * WK_MATS * MAT;
+  WKV_TRACE_BEGIN
   const int nvalid = min(L, T - c * L);
 
   if (tid == 0) {
@@ -485,6 +514,7 @@ wkv7_tc_bwd_grad_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_co
   bool ok = wait_all(&bars[0], 0);
   uint32_t mph = 0;
   bool second_issued = false;
+  WKV_TRACE(32)
   if (ok) {
     // ---- dY and V rows into the lower halves; the dM product can start
     {
@@ -507,6 +537,7 @@ wkv7_tc_bwd_grad_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_co
     }
     build_lambda(Rw, lam, nvalid, tid);
     if (tid < 64) DL[tid] = expf(lam[poff(63, tid)]);
+    WKV_TRACE(33)
     // X1T row j: A~[t][j] (k = t), R~[t][j] (k = 64 + t); X2T row j: B~ / K~ (column owners)
     {
       const int j = tid & 63;
@@ -534,6 +565,7 @@ wkv7_tc_bwd_grad_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_co
       }
     }
     __syncthreads();  // raw tiles dead from here on
+    WKV_TRACE(34)
     {  // S0^T (row j = tid < 64, K = i) and (dS D_L)^T (row j, threads 64..127): column loads from global
       const int j = tid & 63;
       const float* src = tid < 64 ? S0g : wk + WK_DS * MAT;
@@ -553,6 +585,7 @@ wkv7_tc_bwd_grad_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_co
       sm100::mma_commit(&bars[2]);  // own barrier: both commits may complete before either wait
     }
     second_issued = true;
+    WKV_TRACE(35)
     stage = 2;
     ok = wait_all(&bars[1], mph);  // dM
     mph ^= 1;
@@ -562,6 +595,7 @@ wkv7_tc_bwd_grad_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_co
     }
     sm100::tc_fence_after();
   }
+  WKV_TRACE(36)
   // dM stage tiles. Stage 1: SA = [dM_ab; dM_rb] (rows t, K = s), SB = [dM_ab^T; dM_ak^T] (rows s, K = t).
   //                 Stage 2: SA = [dM_ak; dM_rk],               SB = [dM_rb^T; dM_rk^T].
 #pragma unroll 1
@@ -607,12 +641,15 @@ wkv7_tc_bwd_grad_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_co
                      sm100::idesc_tf32(128, 64), stage_ > 0);
       sm100::mma_commit(&bars[1]);
     }
+    WKV_TRACE(37 + 2 * stage_)
     stage = 4 + stage_;
     ok = wait_all(&bars[1], mph);
     mph ^= 1;
     sm100::tc_fence_after();
+    WKV_TRACE(38 + 2 * stage_)
   }
   if (ok) {
+    WKV_TRACE(41)
     // ---- row epilogue: raw gradients and the dLambda terms (thread = row t of its half)
     const int t = tid & 63, tg = c * L + t;
     const bool lo = tid < 64;  // rows of a~ / b~ (da, db) vs r~ / k~ (dr, dk)
@@ -656,6 +693,7 @@ wkv7_tc_bwd_grad_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_co
       }
     }
     __syncthreads();
+    WKV_TRACE(42)
     // ---- column pass: key j. Threads 64..127: the chunk-end terms; threads 0..63: the reverse scan.
     if (tid >= 64) {
       const int j = tid - 64;
@@ -681,6 +719,7 @@ wkv7_tc_bwd_grad_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_co
       }
     }
   }
+  WKV_TRACE(43)
   if (!ok && tid == 0) atomicCAS(&wkv7_tc_bwd_fault_word, 0, 0x400 | stage);  // gradient kernel, failing wait
   if (!ok) {
     if (stage > 1) sm100::mbar_wait_bounded(&bars[1], mph);
@@ -709,6 +748,16 @@ bool fp32_rows_map(CUtensorMap* m, const float* base, long rows) {
 }
 
 }  // namespace
+
+#ifdef WKV7_TC_TRACE
+extern "C" void rt_wkv7_tc_bwd_trace(unsigned long long* out, int reset) {
+  cudaMemcpyFromSymbol(out, wkv7_trace_ns, sizeof(unsigned long long) * 64);
+  if (reset) {
+    static unsigned long long zeros[64] = {};
+    cudaMemcpyToSymbol(wkv7_trace_ns, zeros, sizeof(zeros));
+  }
+}
+#endif
 
 extern "C" long rt_wkv7_tc_backward_workspace_floats(int B, int T, int H) {
   const long chunks = (T + L - 1) / L;

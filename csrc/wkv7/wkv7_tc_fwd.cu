@@ -26,6 +26,23 @@
 namespace {
 
 using namespace wtc;
+
+// Optional phase timing (compile with -DWKV7_TC_TRACE): thread 0 of every CTA adds the %globaltimer time spent
+// since the previous mark to a per-phase total; rt_wkv7_tc_trace_read copies the totals out. Off by default.
+#ifdef WKV7_TC_TRACE
+__device__ unsigned long long wkv7_trace_ns[64];
+#define WKV_TRACE_BEGIN unsigned long long trace_t0_ = threadIdx.x == 0 ? sm100::globaltimer() : 0ull;
+#define WKV_TRACE(slot)                                                       \
+  if (threadIdx.x == 0) {                                                     \
+    const unsigned long long trace_now_ = sm100::globaltimer();               \
+    atomicAdd(&wkv7_trace_ns[(slot)], trace_now_ - trace_t0_);                \
+    trace_t0_ = trace_now_;                                                   \
+  }
+#else
+#define WKV_TRACE_BEGIN
+#define WKV_TRACE(slot)
+#endif
+
 constexpr int KB = 1024;
 constexpr int MAT = N * N;  // floats of one 64 x 64 matrix
 
@@ -135,6 +152,7 @@ wkv7_tc_chunk_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_const
   float* rtmp = reinterpret_cast<float*>(sm + OFF_INV);
   float* td = rtmp + 16 * 48;
   float* rec = ws + (((long)bb * H + h) * chunks + c) * (REC_MATS * MAT);
+  WKV_TRACE_BEGIN
 
   if (tid == 0) {
     sm100::mbar_init(&bars[0], 1);
@@ -161,6 +179,7 @@ wkv7_tc_chunk_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_const
   }
   int stage = 1;  // which wait a failure happened at (recorded in the fault word)
   bool ok = wait_all(&bars[0], 0);
+  WKV_TRACE(0)
   uint32_t mph = 0;  // parity of the next MMA-barrier completion
   const int nvalid = min(L, T - c * L);
 
@@ -184,6 +203,7 @@ wkv7_tc_chunk_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_const
     }
     __syncthreads();
     if (tid < 64) DL[tid] = expf(lam[poff(63, tid)]);
+    WKV_TRACE(1)
     // ---- phase-A tiles. X1 row tid: A~ (tid < 64) / R~; X2 row tid: B~ / K~ (thread = row).
     {
       const int t = tid & 63;
@@ -215,6 +235,7 @@ wkv7_tc_chunk_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_const
         put4(X2, 128, tid, j0 + 4, x2[4], x2[5], x2[6], x2[7]);
       }
     }
+    WKV_TRACE(2)
     // V^T (row i = tid < 64), B^T / K^T (row j; thread j < 64 and 64 + j): x[s][j] e^{Lambda_L - Lambda_s}
     {
       const int j = tid & 63;
@@ -235,6 +256,7 @@ wkv7_tc_chunk_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_const
       }
     }
     tc_sync();
+    WKV_TRACE(3)
     // ---- MMA1: [M_ab M_ak; M_rb M_rk] = [A~; R~] [B~; K~]^T  (TMEM cols 0..127)
     if (tid == 0) {
       mma_tf32_tiles(tmem, sm100::smem_u32(X1), 128, sm100::smem_u32(X2), 128, 8, sm100::idesc_tf32(128, 128),
@@ -247,6 +269,7 @@ wkv7_tc_chunk_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_const
     sm100::tc_fence_after();
   }
   if (ok) {
+    WKV_TRACE(4)
     // ---- epilogue 1: masks; M_ab -> MPL (plain), [M_ak; M_rk] -> MAK, M_rb -> MRB
     {
       float d[64];
@@ -278,7 +301,9 @@ wkv7_tc_chunk_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_const
                      false);
       sm100::mma_commit(&bars[1]);
     }
+    WKV_TRACE(5)
     invert_unit_lower(MPL, rtmp, td, tid);
+    WKV_TRACE(6)
     // T^T -> TT (row s' = tid < 64); T rows -> TP rows 0..63 and to the record (tf32, an MMA operand later)
     if (tid < 64) {
 #pragma unroll 1
@@ -294,6 +319,7 @@ wkv7_tc_chunk_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_const
         *reinterpret_cast<float4*>(g + j) = make_float4(tf32r(x.x), tf32r(x.y), tf32r(x.z), tf32r(x.w));
       }
     }
+    WKV_TRACE(7)
     stage = 3;
     ok = wait_all(&bars[1], mph);  // MMA2 done
     mph ^= 1;
@@ -312,6 +338,7 @@ wkv7_tc_chunk_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_const
     }
   }
   if (ok) {
+    WKV_TRACE(8)
     // ---- P rows -> TP rows 64..127; [A~^T; Z^T] -> AZT (B operand of MMA3, N = 128)
     if (tid < 64) {
       float d[64];
@@ -335,6 +362,7 @@ wkv7_tc_chunk_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_const
       }
     }
     tc_sync();
+    WKV_TRACE(9)
     // ---- MMA3: [W U0; P A~  P Z] = [T; P] [A~ | Z]  (cols 0..127)
     if (tid == 0) {
       mma_tf32_tiles(tmem, sm100::smem_u32(TP), 128, sm100::smem_u32(AZT), 128, 8, sm100::idesc_tf32(128, 128),
@@ -347,6 +375,7 @@ wkv7_tc_chunk_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_const
     sm100::tc_fence_after();
   }
   if (ok) {
+    WKV_TRACE(10)
     // ---- epilogue 3: W, U0 -> [W^T; U0^T] (WUT); Q = R~ + P A~, Y0 = M_rk V + P Z -> record
     if (tid < 64) {
       float d[64];
@@ -387,6 +416,7 @@ wkv7_tc_chunk_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_const
       }
     }
     tc_sync();
+    WKV_TRACE(11)
     // ---- MMA4: [W^T B^; U0^T B^] (cols 128..191) and [*; V^T K^] (cols 192..255; V^T read as rows 64..127)
     if (tid == 0) {
       mma_tf32_tiles(tmem + 128, sm100::smem_u32(WUT), 128, sm100::smem_u32(BT), 64, 8, sm100::idesc_tf32(128, 64),
@@ -401,6 +431,7 @@ wkv7_tc_chunk_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_const
     sm100::tc_fence_after();
   }
   if (ok) {
+    WKV_TRACE(12)
     // ---- epilogue 4: G = diag(D_L) + W^T B^ (rows j), H0 = U0^T B^ + V^T K^ (rows i)
     const uint32_t row = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
     const int r = tid & 63;
@@ -420,6 +451,7 @@ wkv7_tc_chunk_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_const
       for (int u = 0; u < 32; u += 4) *reinterpret_cast<float4*>(g + u) = make_float4(d[u], d[u + 1], d[u + 2], d[u + 3]);
     }
   }
+  WKV_TRACE(13)
   if (!ok && tid == 0) atomicCAS(&wkv7_tc_fault_word, 0, 0x100 | stage);  // kernel 1, failing wait
   if (!ok && stage > 1) sm100::mbar_wait_bounded(&bars[1], mph);  // an MMA may still be in flight
   sm100::tc_fence_before();
@@ -578,6 +610,16 @@ bool fp32_rows_map(CUtensorMap* m, const float* base, long rows) {
 }  // namespace
 
 // Floats of the per-chunk record workspace (G, H0, Q, Y0, T per chunk and head). The backward reads G, Q, T.
+#ifdef WKV7_TC_TRACE
+extern "C" void rt_wkv7_tc_fwd_trace(unsigned long long* out, int reset) {
+  cudaMemcpyFromSymbol(out, wkv7_trace_ns, sizeof(unsigned long long) * 64);
+  if (reset) {
+    static unsigned long long zeros[64] = {};
+    cudaMemcpyToSymbol(wkv7_trace_ns, zeros, sizeof(zeros));
+  }
+}
+#endif
+
 extern "C" long rt_wkv7_tc_workspace_floats(int B, int T, int H) {
   const long chunks = (T + L - 1) / L;
   return chunks * B * H * REC_MATS * MAT;
