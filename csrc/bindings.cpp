@@ -35,7 +35,7 @@ void check_wkv(const at::Tensor& r, const std::vector<at::Tensor>& xs) {
 
 // The tcgen05 path (chunks of 64 steps) serves bf16 inputs with head size 64 and at least 128 steps; shorter
 // calls, fp32 inputs and other head sizes run the chunk-16 CUDA-core kernels.
-bool g_wkv7_tc_enabled = false;  // switched on once validated on a B200
+bool g_wkv7_tc_enabled = true;
 bool wkv7_use_tc(const at::Tensor& r) {
   return g_wkv7_tc_enabled && r.scalar_type() == at::kBFloat16 && r.size(3) == 64 && r.size(1) >= 128;
 }

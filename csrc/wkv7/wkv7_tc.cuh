@@ -88,4 +88,100 @@ RT_DEVICE void tmem_row64(uint32_t tmem, int warp, int col, float (&v)[64]) {
   sm100::tmem_wait_ld();
 }
 
+// Lambda_t[j] = sum_{tau <= t} log d_tau[j] (plain swizzled 64 x 64 in `lam`) from the raw w tile, 128 threads:
+// thread j and 64 + j take steps [0, 32) and [32, 64) of column j. Loads and sigmoids are independent (staged in
+// registers); only the running sum is serial. Steps at or past `nvalid` have log d = 0. Ends with a barrier.
+RT_DEVICE void build_lambda(const uint8_t* Rw, float* lam, float* carry, int nvalid, int tid) {
+  const int j = tid & 63, half = tid >> 6, t0 = 32 * half;
+  float v[32];
+#pragma unroll
+  for (int u = 0; u < 32; ++u) v[u] = raw(Rw, t0 + u, j);
+#pragma unroll
+  for (int u = 0; u < 32; ++u) v[u] = t0 + u < nvalid ? -DECAY_SCALE * rt::sigmoidf_(v[u]) : 0.f;
+#pragma unroll
+  for (int u = 1; u < 32; ++u) v[u] += v[u - 1];
+  if (half == 0) carry[j] = v[31];
+  __syncthreads();
+  const float base = half ? carry[j] : 0.f;
+#pragma unroll
+  for (int u = 0; u < 32; ++u) lam[poff(t0 + u, j)] = v[u] + base;
+  __syncthreads();
+}
+
+// One 16 x 16 block (bi, bj) of the inverse being built: diagonal blocks from `td`, the others from `mpl`.
+RT_DEVICE float tblock(const float* mpl, const float* td, int bi, int bj, int r, int c) {
+  return bi == bj ? td[bi * 256 + r * 16 + c] : mpl[poff(16 * bi + r, 16 * bj + c)];
+}
+
+// T = (I - M)^{-1} for the strictly lower 64 x 64 M in `mpl` (plain swizzled), in place; 128 threads.
+//  1. the four diagonal 16 x 16 blocks by right-looking substitution (thread = column; after x[s] is final every
+//     later row's sum takes its term, so the updates of one step are independent);
+//  2. the off-diagonal blocks by distance d = i - j = 1, 2, 3:  R_j = sum_{k=j}^{i-1} M_ik T_kj, then T_ij = T_ii R_j,
+//     each a batch of independent 16 x 16 block products spread over all threads (up to six outputs per thread).
+// Scratch: rtmp >= 768 floats, td >= 1024 floats.
+RT_DEVICE void invert_unit_lower(float* mpl, float* rtmp, float* td, int tid) {
+  if (tid < 64) {
+    const int kb = tid >> 4, cc = tid & 15, base = 16 * kb;
+    float acc[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) acc[r] = r == cc ? 1.f : 0.f;
+#pragma unroll
+    for (int s = 0; s < 16; ++s) {
+      const float xs = s >= cc ? acc[s] : 0.f;
+      acc[s] = xs;
+#pragma unroll
+      for (int r = s + 1; r < 16; ++r) acc[r] += mpl[poff(base + r, base + s)] * xs;
+    }
+#pragma unroll
+    for (int r = 0; r < 16; ++r) td[kb * 256 + r * 16 + cc] = acc[r];
+  }
+  __syncthreads();
+#pragma unroll 1
+  for (int d = 1; d < 4; ++d) {
+    const int nb = 4 - d;  // blocks (j + d, j), j = 0 .. nb - 1
+    float acc[6];
+#pragma unroll
+    for (int q = 0; q < 6; ++q) acc[q] = 0.f;
+#pragma unroll 1
+    for (int kk = 0; kk < d; ++kk) {
+#pragma unroll 4
+      for (int m = 0; m < 16; ++m) {
+#pragma unroll
+        for (int q = 0; q < 6; ++q) {
+          const int e = tid + 128 * q, j = e >> 8, r = (e >> 4) & 15, c = e & 15;
+          if (q < 2 * nb) {
+            const int k = j + kk;
+            acc[q] += mpl[poff(16 * (j + d) + r, 16 * k + m)] * tblock(mpl, td, k, j, m, c);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 6; ++q)
+      if (q < 2 * nb) rtmp[tid + 128 * q] = acc[q];
+    __syncthreads();
+#pragma unroll
+    for (int q = 0; q < 6; ++q) acc[q] = 0.f;
+#pragma unroll 4
+    for (int m = 0; m < 16; ++m) {
+#pragma unroll
+      for (int q = 0; q < 6; ++q) {
+        const int e = tid + 128 * q, j = e >> 8, r = (e >> 4) & 15, c = e & 15;
+        if (q < 2 * nb) acc[q] += td[(j + d) * 256 + r * 16 + m] * rtmp[j * 256 + m * 16 + c];
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 6; ++q) {
+      const int e = tid + 128 * q, j = e >> 8, r = (e >> 4) & 15, c = e & 15;
+      if (q < 2 * nb) mpl[poff(16 * (j + d) + r, 16 * j + c)] = acc[q];
+    }
+    __syncthreads();
+  }
+  for (int e = tid; e < 4 * 256; e += 128) {
+    const int kb = e >> 8, r = (e >> 4) & 15, c = e & 15;
+    mpl[poff(16 * kb + r, 16 * kb + c)] = td[e];
+  }
+  __syncthreads();
+}
+
 }  // namespace wtc

@@ -56,27 +56,6 @@ RT_DEVICE bool wait_all(uint64_t* bar, uint32_t parity) {
 }
 RT_DEVICE float bf(const __nv_bfloat16* p) { return __bfloat162float(*p); }
 
-// Lambda (plain swizzled) from the raw w tile: columns split over two halves of 32 steps.
-RT_DEVICE void build_lambda(const uint8_t* Rw, float* lam, int nvalid, int tid) {
-  {
-    const int j = tid & 63, t0 = (tid >> 6) * 32;
-    float acc = 0.f;
-#pragma unroll 4
-    for (int u = 0; u < 32; ++u) {
-      const int t = t0 + u;
-      acc += t < nvalid ? -DECAY_SCALE * rt::sigmoidf_(raw(Rw, t, j)) : 0.f;
-      lam[poff(t, j)] = acc;
-    }
-  }
-  __syncthreads();
-  if (tid >= 64) {
-    const int j = tid - 64;
-    const float base = lam[poff(31, j)];
-    for (int t = 32; t < 64; ++t) lam[poff(t, j)] += base;
-  }
-  __syncthreads();
-}
-
 // Row `row` of a K-major tile of `rows` rows from 64 fp32 values in global memory (rounded to tf32).
 RT_DEVICE void tile_row_from_global(uint8_t* tile, int rows, int row, const float* src) {
 #pragma unroll 4
@@ -245,28 +224,42 @@ wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_c
   uint32_t mph = 0;
   WKV_TRACE(16)
   if (ok) {
-    build_lambda(Rw, lam, nvalid, tid);
-    {  // X1 (A~ / R~), X2 (B~ / K~), BKH (B^ / K^): row tid
+    float* DLs = reinterpret_cast<float*>(sm + ka::MISC + 64);
+    build_lambda(Rw, lam, DLs, nvalid, tid);
+    if (tid < 64) DLs[tid] = expf(lam[poff(63, tid)]);
+    __syncthreads();
+    {  // X1 (A~ / R~), X2 (B~ / K~), BKH (B^ = B~ D_L / K^ = K~ D_L): row tid, eight keys at a time
       const int t = tid & 63;
       const bool hi = tid >= 64;
       const uint8_t* s1 = hi ? Rr : Ra;
       const uint8_t* s2 = hi ? Rk : Rb;
 #pragma unroll 1
-      for (int j0 = 0; j0 < 64; j0 += 4) {
-        float x1[4], xb[4], xh[4];
+      for (int j0 = 0; j0 < 64; j0 += 8) {
+        float x1[8], x2[8], lt[8], lp[8];
+        raw8(s1, t, j0, x1);
+        raw8(s2, t, j0, x2);
+        *reinterpret_cast<float4*>(lt) = *reinterpret_cast<const float4*>(&lam[poff(t, j0)]);
+        *reinterpret_cast<float4*>(lt + 4) = *reinterpret_cast<const float4*>(&lam[poff(t, j0 + 4)]);
+        if (!hi && t > 0) {
+          *reinterpret_cast<float4*>(lp) = *reinterpret_cast<const float4*>(&lam[poff(t - 1, j0)]);
+          *reinterpret_cast<float4*>(lp + 4) = *reinterpret_cast<const float4*>(&lam[poff(t - 1, j0 + 4)]);
+        } else {
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int j = j0 + q;
-          const float lt = lam[poff(t, j)], lL = lam[poff(63, j)];
-          const float lp = (!hi && t > 0) ? lam[poff(t - 1, j)] : 0.f;
-          const float x2 = raw(s2, t, j);
-          x1[q] = raw(s1, t, j) * expf(hi ? lt : lp);
-          xb[q] = x2 * expf(-lt);
-          xh[q] = x2 * expf(lL - lt);
+          for (int q = 0; q < 8; ++q) lp[q] = 0.f;
         }
-        put4(X1, 128, tid, j0, x1[0], x1[1], x1[2], x1[3]);
-        put4(X2, 128, tid, j0, xb[0], xb[1], xb[2], xb[3]);
-        put4(BKH, 128, tid, j0, xh[0], xh[1], xh[2], xh[3]);
+        float xh[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          x1[q] *= expf(hi ? lt[q] : lp[q]);
+          x2[q] *= expf(-lt[q]);
+          xh[q] = x2[q] * DLs[j0 + q];
+        }
+#pragma unroll
+        for (int q = 0; q < 8; q += 4) {
+          put4(X1, 128, tid, j0 + q, x1[q], x1[q + 1], x1[q + 2], x1[q + 3]);
+          put4(X2, 128, tid, j0 + q, x2[q], x2[q + 1], x2[q + 2], x2[q + 3]);
+          put4(BKH, 128, tid, j0 + q, xh[q], xh[q + 1], xh[q + 2], xh[q + 3]);
+        }
       }
     }
     WKV_TRACE(17)
@@ -275,8 +268,13 @@ wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_c
       uint8_t* dst = tid < 64 ? VT : DYT;
       const uint8_t* src = tid < 64 ? Rv : Rdy;
 #pragma unroll 1
-      for (int s = 0; s < 64; s += 4)
-        put4(dst, 64, i, s, raw(src, s, i), raw(src, s + 1, i), raw(src, s + 2, i), raw(src, s + 3, i));
+      for (int s0 = 0; s0 < 64; s0 += 16) {
+        float x[16];
+#pragma unroll
+        for (int q = 0; q < 16; ++q) x[q] = raw(src, s0 + q, i);
+#pragma unroll
+        for (int q = 0; q < 16; q += 4) put4(dst, 64, i, s0 + q, x[q], x[q + 1], x[q + 2], x[q + 3]);
+      }
     }
     tc_sync();
     WKV_TRACE(18)
@@ -466,7 +464,8 @@ wkv7_tc_bwd_grad_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_co
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kb::MISC);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + kb::MISC + 32);
   float* DL = reinterpret_cast<float*>(sm + kb::MISC + 64);
-  float* colsum = DL + 64;  // [64]: sum_i dS S0 D_L + sum_s (E b~ + F k~), per key
+  float* colsum = reinterpret_cast<float*>(sm + kb::X2T);  // [192] (after the stage MMAs): the chunk-end term
+                                                           // in two halves, then the upper half's sum of g
   uint8_t *DZY = sm + kb::DZY, *UV = sm + kb::UV, *X1T = sm + kb::X1T, *X2T = sm + kb::X2T;
   uint8_t *S0T = sm, *DST = sm + 16 * KB;
   uint8_t *SA = DZY, *SB = UV;  // stage tiles (32 KB each)
@@ -475,6 +474,7 @@ wkv7_tc_bwd_grad_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_co
   float* QA = PB + MAT;                                 // da a
   float* EA = reinterpret_cast<float*>(sm + kb::X1T);  // E b~
   float* EB = EA + MAT;                                 // F k~
+  float* FW = reinterpret_cast<float*>(sm + kb::DZY);  // d log d / dw per element
   const long bh = (long)bb * H + h, ch = bh * chunks + c;
   const float* S0g = ckpt + (bh * (chunks + 1) + c) * MAT;
 
@@ -535,7 +535,7 @@ wkv7_tc_bwd_grad_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_co
                      false);
       sm100::mma_commit(&bars[1]);
     }
-    build_lambda(Rw, lam, nvalid, tid);
+    build_lambda(Rw, lam, DL, nvalid, tid);
     if (tid < 64) DL[tid] = expf(lam[poff(63, tid)]);
     WKV_TRACE(33)
     // X1T row j: A~[t][j] (k = t), R~[t][j] (k = 64 + t); X2T row j: B~ / K~ (column owners)
@@ -545,23 +545,31 @@ wkv7_tc_bwd_grad_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_co
       const uint8_t* s1 = tid < 64 ? Ra : Rb;
       const uint8_t* s2 = tid < 64 ? Rr : Rk;
 #pragma unroll 1
-      for (int t = 0; t < 64; t += 4) {
-        float x1[4], x2[4];
+      for (int t0 = 0; t0 < 64; t0 += 16) {  // 16 steps at a time: loads first, then exponentials, then stores
+        float x1[16], x2[16], lt[17];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int tt = t + q;
-          const float lt = lam[poff(tt, j)];
-          if (tid < 64) {
-            const float lp = tt ? lam[poff(tt - 1, j)] : 0.f;
-            x1[q] = raw(s1, tt, j) * expf(lp);
-            x2[q] = raw(s2, tt, j) * expf(lt);
-          } else {
-            x1[q] = raw(s1, tt, j) * expf(-lt);
-            x2[q] = raw(s2, tt, j) * expf(-lt);
+        for (int q = 0; q < 16; ++q) {
+          x1[q] = raw(s1, t0 + q, j);
+          x2[q] = raw(s2, t0 + q, j);
+          lt[q + 1] = lam[poff(t0 + q, j)];
+        }
+        lt[0] = t0 ? lam[poff(t0 - 1, j)] : 0.f;
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+          if (tid < 64) {  // A~ = a e^{Lambda_{t-1}}, R~ = r e^{Lambda_t}
+            x1[q] *= expf(lt[q]);
+            x2[q] *= expf(lt[q + 1]);
+          } else {         // B~ = b e^{-Lambda_t}, K~ = k e^{-Lambda_t}
+            const float dn = expf(-lt[q + 1]);
+            x1[q] *= dn;
+            x2[q] *= dn;
           }
         }
-        put4(dst, 64, j, t, x1[0], x1[1], x1[2], x1[3]);
-        put4(dst, 64, j, 64 + t, x2[0], x2[1], x2[2], x2[3]);
+#pragma unroll
+        for (int q = 0; q < 16; q += 4) {
+          put4(dst, 64, j, t0 + q, x1[q], x1[q + 1], x1[q + 2], x1[q + 3]);
+          put4(dst, 64, j, 64 + t0 + q, x2[q], x2[q + 1], x2[q + 2], x2[q + 3]);
+        }
       }
     }
     __syncthreads();  // raw tiles dead from here on
@@ -571,10 +579,15 @@ wkv7_tc_bwd_grad_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_co
       const float* src = tid < 64 ? S0g : wk + WK_DS * MAT;
       uint8_t* dst = tid < 64 ? S0T : DST;
       const float sc = tid < 64 ? 1.f : DL[j];
-#pragma unroll 1
-      for (int i = 0; i < 64; i += 4)
-        put4(dst, 64, j, i, src[i * N + j] * sc, src[(i + 1) * N + j] * sc, src[(i + 2) * N + j] * sc,
-             src[(i + 3) * N + j] * sc);
+#pragma unroll
+      for (int h2 = 0; h2 < 2; ++h2) {  // 32 independent column loads in flight, then the row of the tile
+        float col[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) col[i] = __ldg(src + (32 * h2 + i) * N + j);
+#pragma unroll
+        for (int i = 0; i < 32; i += 4)
+          put4(dst, 64, j, 32 * h2 + i, col[i] * sc, col[i + 1] * sc, col[i + 2] * sc, col[i + 3] * sc);
+      }
     }
     tc_sync();
     if (tid == 0) {  // [dZ S0; dY S0] (cols 128..191) and [E; F] = [U; V] (dS D_L) (cols 256..319)
@@ -650,72 +663,123 @@ wkv7_tc_bwd_grad_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_co
   }
   if (ok) {
     WKV_TRACE(41)
-    // ---- row epilogue: raw gradients and the dLambda terms (thread = row t of its half)
+    // ---- row epilogue: raw gradients and the dLambda terms (thread = row t of its half). The raw input rows come
+    // in as 16-byte loads, the gradient rows leave as 16-byte stores, and the decay-gradient factor of w is formed
+    // here (row-wise) for the column pass.
     const int t = tid & 63, tg = c * L + t;
     const bool lo = tid < 64;  // rows of a~ / b~ (da, db) vs r~ / k~ (dr, dk)
     const bool valid = tg < T;
     const long go = (((long)bb * T + (valid ? tg : 0)) * H + h) * N;
     const uint32_t row = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
+    const __nv_bfloat16* src1 = lo ? pa : pr;  // a / r
+    const __nv_bfloat16* src2 = lo ? pb : pk;  // b / k
+    float* out1 = lo ? da : dr;
+    float* out2 = lo ? db : dk;
 #pragma unroll 1
     for (int half = 0; half < 2; ++half) {
-      float d1[32], d2[32], d3[32];
+      float d1[32], d2[32], d3[32], x1[32], x2[32];
       sm100::tmem_ld32(row + 128 + 32 * half, d1);  // dA~ / dR~
       sm100::tmem_ld32(row + 192 + 32 * half, d2);  // dB~' / dK~'
       sm100::tmem_ld32(row + 256 + 32 * half, d3);  // E / F
-      sm100::tmem_wait_ld();
-#pragma unroll 4
-      for (int u = 0; u < 32; ++u) {
-        const int j = 32 * half + u;
-        const float lt = lam[poff(t, j)];
-        if (lo) {
-          const float lp = t ? lam[poff(t - 1, j)] : 0.f;
-          const float av = valid ? bf(pa + go + j) : 0.f, bv = valid ? bf(pb + go + j) : 0.f;
-          const float gda = d1[u] * expf(lp);
-          const float gdb = (d2[u] + d3[u]) * expf(-lt);
-          QA[poff(t, j)] = gda * av;
-          PB[poff(t, j)] = -gdb * bv;
-          EA[poff(t, j)] = d3[u] * bv * expf(-lt);  // E b~ (E carries D_L)
-          if (valid) {
-            da[go + j] = gda;
-            db[go + j] = gdb;
-          }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        if (valid) {
+          rt::unpack8(__ldg(reinterpret_cast<const uint4*>(src1 + go + 32 * half + 8 * q)), x1 + 8 * q);
+          rt::unpack8(__ldg(reinterpret_cast<const uint4*>(src2 + go + 32 * half + 8 * q)), x2 + 8 * q);
         } else {
-          const float rv = valid ? bf(pr + go + j) : 0.f, kv = valid ? bf(pk + go + j) : 0.f;
-          const float gdr = d1[u] * expf(lt);
-          const float gdk = (d2[u] + d3[u]) * expf(-lt);
-          PA[poff(t, j)] = gdr * rv - gdk * kv;
-          EB[poff(t, j)] = d3[u] * kv * expf(-lt);  // F k~
-          if (valid) {
-            dr[go + j] = gdr;
-            dk[go + j] = gdk;
+#pragma unroll
+          for (int u = 0; u < 8; ++u) x1[8 * q + u] = x2[8 * q + u] = 0.f;
+        }
+      }
+      if (lo && valid) {  // w factor of this row: -e^{-1/2} sigmoid(w) (1 - sigmoid(w))
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          float wv[8];
+          rt::unpack8(__ldg(reinterpret_cast<const uint4*>(pw + go + 32 * half + 8 * q)), wv);
+#pragma unroll
+          for (int u = 0; u < 8; u += 4) {
+            float f[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float sg = rt::sigmoidf_(wv[u + e]);
+              f[e] = -DECAY_SCALE * sg * (1.f - sg);
+            }
+            *reinterpret_cast<float4*>(&FW[poff(t, 32 * half + 8 * q + u)]) = make_float4(f[0], f[1], f[2], f[3]);
           }
+        }
+      }
+      sm100::tmem_wait_ld();
+#pragma unroll
+      for (int u = 0; u < 32; u += 4) {
+        const int j = 32 * half + u;
+        const float4 lt4 = *reinterpret_cast<const float4*>(&lam[poff(t, j)]);
+        const float lt[4] = {lt4.x, lt4.y, lt4.z, lt4.w};
+        float lp[4] = {0.f, 0.f, 0.f, 0.f};
+        if (lo && t > 0) {
+          const float4 lp4 = *reinterpret_cast<const float4*>(&lam[poff(t - 1, j)]);
+          lp[0] = lp4.x; lp[1] = lp4.y; lp[2] = lp4.z; lp[3] = lp4.w;
+        }
+        float g1[4], g2[4], pv[4], qv[4], ev[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float up = expf(lo ? lp[e] : lt[e]);  // e^{Lambda_{t-1}} (a) or e^{Lambda_t} (r)
+          const float dn = expf(-lt[e]);              // e^{-Lambda_t} (b, k)
+          g1[e] = d1[u + e] * up;                     // da / dr
+          g2[e] = (d2[u + e] + d3[u + e]) * dn;       // db / dk
+          ev[e] = d3[u + e] * x2[u + e] * dn;         // E b~ / F k~
+          qv[e] = g1[e] * x1[u + e];                  // da a / dr r
+          pv[e] = -g2[e] * x2[u + e];                 // -db b / -dk k
+        }
+        if (lo) {
+          *reinterpret_cast<float4*>(&QA[poff(t, j)]) = make_float4(qv[0], qv[1], qv[2], qv[3]);
+          *reinterpret_cast<float4*>(&PB[poff(t, j)]) = make_float4(pv[0], pv[1], pv[2], pv[3]);
+          *reinterpret_cast<float4*>(&EA[poff(t, j)]) = make_float4(ev[0], ev[1], ev[2], ev[3]);
+        } else {
+          *reinterpret_cast<float4*>(&PA[poff(t, j)]) =
+              make_float4(qv[0] + pv[0], qv[1] + pv[1], qv[2] + pv[2], qv[3] + pv[3]);
+          *reinterpret_cast<float4*>(&EB[poff(t, j)]) = make_float4(ev[0], ev[1], ev[2], ev[3]);
+        }
+        if (valid) {
+          *reinterpret_cast<float4*>(out1 + go + j) = make_float4(g1[0], g1[1], g1[2], g1[3]);
+          *reinterpret_cast<float4*>(out2 + go + j) = make_float4(g2[0], g2[1], g2[2], g2[3]);
         }
       }
     }
     __syncthreads();
     WKV_TRACE(42)
-    // ---- column pass: key j. Threads 64..127: the chunk-end terms; threads 0..63: the reverse scan.
-    if (tid >= 64) {
-      const int j = tid - 64;
+    // ---- column pass, key j: thread j and 64 + j split every column sum in two halves.
+    {
+      const int j = tid & 63, hi = tid >> 6;
       const float* dS = wk + WK_DS * MAT;
-      float acc = 0.f;
-      for (int i = 0; i < 64; ++i) acc += dS[i * N + j] * S0g[i * N + j];
-      acc *= DL[j];
-      for (int s = 0; s < 64; ++s) acc += EA[poff(s, j)] + EB[poff(s, j)];
-      colsum[j] = acc;
-    }
-    __syncthreads();
-    if (tid < 64) {
-      const int j = tid;
-      float acc = colsum[j];
-      for (int tt = 63; tt >= 0; --tt) {
-        acc += PA[poff(tt, j)] + PB[poff(tt, j)] + (tt < 63 ? QA[poff(tt + 1, j)] : 0.f);
-        const int tgg = c * L + tt;
-        if (tgg < T) {
-          const long o = (((long)bb * T + tgg) * H + h) * N + j;
-          const float sg = rt::sigmoidf_(bf(pw + o));
-          dw[o] = acc * (-DECAY_SCALE) * sg * (1.f - sg);
-        }
+      float ds[32], sv[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        ds[i] = __ldg(dS + (32 * hi + i) * N + j);
+        sv[i] = __ldg(S0g + (32 * hi + i) * N + j);
+      }
+      float acc = 0.f, eacc = 0.f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) acc += ds[i] * sv[i];
+#pragma unroll
+      for (int s2 = 0; s2 < 32; ++s2) eacc += EA[poff(32 * hi + s2, j)] + EB[poff(32 * hi + s2, j)];
+      // g_t = (dr r - dk k) + (-db b) + (da a)_{t+1} for this thread's 32 steps, as suffix sums
+      float g[32];
+#pragma unroll
+      for (int u = 0; u < 32; ++u) {
+        const int tt = 32 * hi + u;
+        g[u] = PA[poff(tt, j)] + PB[poff(tt, j)] + (tt < 63 ? QA[poff(tt + 1, j)] : 0.f);
+      }
+#pragma unroll
+      for (int u = 30; u >= 0; --u) g[u] += g[u + 1];
+      colsum[hi * 64 + j] = acc * DL[j] + eacc;  // the chunk-end term, in two halves
+      colsum[128 + hi * 64 + j] = g[0];          // this half's total of g
+      __syncthreads();
+      // dLogd_t = (sum_i dS S0 D_L + sum_s (E b~ + F k~)) + sum_{t' >= t} g_t'
+      const float base = colsum[j] + colsum[64 + j] + (hi ? 0.f : colsum[128 + 64 + j]);
+#pragma unroll
+      for (int u = 0; u < 32; ++u) {
+        const int tgg = c * L + 32 * hi + u;
+        if (tgg < T) dw[(((long)bb * T + tgg) * H + h) * N + j] = (g[u] + base) * FW[poff(32 * hi + u, j)];
       }
     }
   }

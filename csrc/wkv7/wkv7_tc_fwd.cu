@@ -78,52 +78,6 @@ RT_DEVICE bool wait_all(uint64_t* bar, uint32_t parity) {
   return __syncthreads_and(ok ? 1 : 0) != 0;
 }
 
-// T = (I - M)^{-1} for the strictly lower 64 x 64 M held in `mpl` (plain layout), in place. Diagonal 16 x 16
-// blocks by substitution, then block rows 1..3: R = sum_{k < i} M_ik T_k (the rows of T above), T_i = T_ii R.
-RT_DEVICE void invert_unit_lower(float* mpl, float* rtmp, float* td, int tid) {
-  if (tid < 64) {
-    const int kb = tid >> 4, cc = tid & 15, base = 16 * kb;
-    float x[16];
-#pragma unroll
-    for (int r = 0; r < 16; ++r) {
-      float v = r == cc ? 1.f : 0.f;
-#pragma unroll
-      for (int s = 0; s < r; ++s)
-        if (s >= cc) v += mpl[poff(base + r, base + s)] * x[s];
-      x[r] = r >= cc ? v : 0.f;
-    }
-#pragma unroll
-    for (int r = 0; r < 16; ++r) td[kb * 256 + r * 16 + cc] = x[r];
-  }
-  __syncthreads();
-#pragma unroll 1
-  for (int ib = 1; ib < 4; ++ib) {
-    const int ncols = 16 * ib;
-    for (int e = tid; e < 16 * ncols; e += 128) {
-      const int r = e / ncols, cc = e % ncols;
-      float acc = 0.f;
-      for (int s = cc; s < ncols; ++s) {
-        const float tv = (s >> 4) == (cc >> 4) ? td[(s >> 4) * 256 + (s & 15) * 16 + (cc & 15)] : mpl[poff(s, cc)];
-        acc += mpl[poff(16 * ib + r, s)] * tv;
-      }
-      rtmp[r * 48 + cc] = acc;
-    }
-    __syncthreads();
-    for (int e = tid; e < 16 * ncols; e += 128) {
-      const int r = e / ncols, cc = e % ncols;
-      float acc = 0.f;
-      for (int rp = 0; rp <= r; ++rp) acc += td[ib * 256 + r * 16 + rp] * rtmp[rp * 48 + cc];
-      mpl[poff(16 * ib + r, cc)] = acc;
-    }
-    __syncthreads();
-  }
-  for (int e = tid; e < 4 * 256; e += 128) {
-    const int kb = e >> 8, r = (e >> 4) & 15, cc = e & 15;
-    mpl[poff(16 * kb + r, 16 * kb + cc)] = td[e];
-  }
-  __syncthreads();
-}
-
 __global__ void __launch_bounds__(128, 1)
 wkv7_tc_chunk_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_constant__ CUtensorMap m_w,
                      const __grid_constant__ CUtensorMap m_k, const __grid_constant__ CUtensorMap m_v,
@@ -184,24 +138,7 @@ wkv7_tc_chunk_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_const
   const int nvalid = min(L, T - c * L);
 
   if (ok) {
-    // ---- Lambda: column j, two halves of 32 steps (padded steps have log d = 0)
-    {
-      const int j = tid & 63, t0 = (tid >> 6) * 32;
-      float acc = 0.f;
-#pragma unroll 4
-      for (int u = 0; u < 32; ++u) {
-        const int t = t0 + u;
-        acc += t < nvalid ? -DECAY_SCALE * rt::sigmoidf_(raw(Rw, t, j)) : 0.f;
-        lam[poff(t, j)] = acc;
-      }
-    }
-    __syncthreads();
-    if (tid >= 64) {
-      const int j = tid - 64;
-      const float base = lam[poff(31, j)];
-      for (int t = 32; t < 64; ++t) lam[poff(t, j)] += base;
-    }
-    __syncthreads();
+    build_lambda(Rw, lam, DL, nvalid, tid);  // DL doubles as the carry scratch until it is written
     if (tid < 64) DL[tid] = expf(lam[poff(63, tid)]);
     WKV_TRACE(1)
     // ---- phase-A tiles. X1 row tid: A~ (tid < 64) / R~; X2 row tid: B~ / K~ (thread = row).
@@ -241,18 +178,29 @@ wkv7_tc_chunk_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_const
       const int j = tid & 63;
       if (tid < 64) {
 #pragma unroll 1
-        for (int s = 0; s < 64; s += 4)
-          put4(VT, 64, j, s, raw(Rv, s, j), raw(Rv, s + 1, j), raw(Rv, s + 2, j), raw(Rv, s + 3, j));
+        for (int s0 = 0; s0 < 64; s0 += 16) {
+          float x[16];
+#pragma unroll
+          for (int q = 0; q < 16; ++q) x[q] = raw(Rv, s0 + q, j);
+#pragma unroll
+          for (int q = 0; q < 16; q += 4) put4(VT, 64, j, s0 + q, x[q], x[q + 1], x[q + 2], x[q + 3]);
+        }
       }
       const uint8_t* src = tid < 64 ? Rb : Rk;
       uint8_t* dst = tid < 64 ? BT : KT;
       const float lL = lam[poff(63, j)];
 #pragma unroll 1
-      for (int s = 0; s < 64; s += 4) {
-        float v[4];
+      for (int s0 = 0; s0 < 64; s0 += 16) {  // loads first, then exponentials, then stores
+        float x[16], ls[16];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) v[q] = raw(src, s + q, j) * expf(lL - lam[poff(s + q, j)]);
-        put4(dst, 64, j, s, v[0], v[1], v[2], v[3]);
+        for (int q = 0; q < 16; ++q) {
+          x[q] = raw(src, s0 + q, j);
+          ls[q] = lam[poff(s0 + q, j)];
+        }
+#pragma unroll
+        for (int q = 0; q < 16; ++q) x[q] *= expf(lL - ls[q]);
+#pragma unroll
+        for (int q = 0; q < 16; q += 4) put4(dst, 64, j, s0 + q, x[q], x[q + 1], x[q + 2], x[q + 3]);
       }
     }
     tc_sync();
@@ -351,14 +299,17 @@ wkv7_tc_chunk_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_const
     } else {
       const int j = tid - 64;
 #pragma unroll 1
-      for (int s = 0; s < 64; s += 4) {
-        float v[4];
+      for (int s0 = 0; s0 < 64; s0 += 16) {
+        float x[16], lp[16];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int ss = s + q;
-          v[q] = raw(Ra, ss, j) * (ss ? expf(lam[poff(ss - 1, j)]) : 1.f);
+        for (int q = 0; q < 16; ++q) {
+          x[q] = raw(Ra, s0 + q, j);
+          lp[q] = s0 + q ? lam[poff(s0 + q - 1, j)] : 0.f;
         }
-        put4(AZT, 128, j, s, v[0], v[1], v[2], v[3]);
+#pragma unroll
+        for (int q = 0; q < 16; ++q) x[q] *= expf(lp[q]);
+#pragma unroll
+        for (int q = 0; q < 16; q += 4) put4(AZT, 128, j, s0 + q, x[q], x[q + 1], x[q + 2], x[q + 3]);
       }
     }
     tc_sync();
