@@ -19,7 +19,9 @@ total token count over all ranks divided by the slowest rank's time. The
 working set (54 GB of teacher weights per step) exceeds L2, so no flush is
 needed between steps. ``e2e`` repeats K steps through the public step API
 with the per-step host-to-device copy of token ids from pinned memory and the
-device-to-host read of the step's loss metrics inside the timed region.
+device-to-host read of every step's loss metrics inside the timed region; the
+read of step s completes after step s + 1 is issued, and the last step's read
+completes before the clock stops.
 
 --impl reference runs the unmodified reference package (installed under
 baseline/_ref) through its own API on the same synthetic data.
@@ -166,12 +168,23 @@ def build_ours(args, topo, manifest, model_spec):
     engine = StepEngine(cfg, topo, runner, order, students, captures)
     reader = reader_for(cfg, topo)
 
+    pending = []
+
     def step(read):
+        """One step; with `read` the step's metrics are started towards the host and the previous step's are
+        read and validated (the host issues step s + 1 before it waits for step s's metrics)."""
         before = reader.consumed_tokens
         reports = engine.step(reader)
         if read:
-            engine.read_metrics(reports)
+            pending.append(engine.read_metrics_async(reports))
+            if len(pending) > 1:
+                pending.pop(0).result()
         return reader.consumed_tokens - before
+
+    def finish():
+        while pending:
+            pending.pop(0).result()
+    step.finish = finish
     return step
 
 
@@ -370,6 +383,8 @@ def main():
         t0 = time.perf_counter()
         for _ in range(args.steps):
             e2e_tokens += step(True)
+        if hasattr(step, "finish"):
+            step.finish()  # the last step's metrics, inside the timed region
         barrier()
         e2e_ms = (time.perf_counter() - t0) * 1000
     stats = torch.tensor([ms, float(tokens), e2e_ms or 0.0, float(e2e_tokens)], device=device, dtype=torch.float64)
@@ -400,7 +415,9 @@ def main():
                 "value": e2e_total / (e2e_max / 1000), "unit": "tokens/s",
                 "ms_per_step": e2e_max / args.steps, "tokens_timed": e2e_total,  # the next K batches
                 "h2d_bytes_per_step": 8 * args.chunk * args.micro_batch,
-                "d2h_bytes_per_step": 4 * 5 * 16 if args.impl == "ours" else 4 * 3 * 16},
+                # ours: 16 reports of 5 fp32, 3 fault words, 4 exchange status words (world > 1)
+                "d2h_bytes_per_step": (4 * 5 * 16 + 4 * 3 + (16 if world > 1 else 0)) if args.impl == "ours"
+                else 4 * 3 * 16},
             "gpu_launches": ours_launches * args.steps,
             "other_launches_per_step": other_launches,
         }

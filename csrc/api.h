@@ -22,6 +22,8 @@ long rt_wkv7_tc_workspace_floats(int B, int T, int H);
 long rt_wkv7_tc_backward_workspace_floats(int B, int T, int H);
 int rt_wkv7_tc_fault();
 int rt_wkv7_tc_bwd_fault();
+cudaError_t rt_wkv7_tc_fault_async(int* dst, cudaStream_t stream);
+cudaError_t rt_wkv7_tc_bwd_fault_async(int* dst, cudaStream_t stream);
 cudaError_t rt_wkv7_tc_forward(int B, int T, int H, const void* r, const void* w, const void* k, const void* v,
                                const void* a, const void* b, const float* s0, void* y, float* s_end, float* ckpt,
                                float* ws, cudaStream_t stream);
@@ -40,6 +42,7 @@ cudaError_t rt_wkv7_backward(int dtype, int B, int T, int H, int N, const void* 
 cudaError_t rt_gemm_bf16(const void* A, long lda, int a_mn, const void* B, long ldb, int b_mn, void* C, long ldc,
                          int M, int N, int K, int epi, float alpha, int* status, cudaStream_t stream);
 int rt_gemm_fault();
+cudaError_t rt_gemm_fault_async(int* dst, cudaStream_t stream);
 int rt_kl_segments(long rows, long V);
 long rt_kl_workspace_floats(long rows, int segments);
 cudaError_t rt_kl_rows(int dtype, const void* student, const void* teacher, long rows, long V, long ld_s, long ld_t,

@@ -579,6 +579,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("wkv7_chunk_len", []() { return rt_wkv7_chunk_len(); });
   m.def("wkv7_tc_fault", []() { return rt_wkv7_tc_fault() | (rt_wkv7_tc_bwd_fault() << 12); },
         "1 if a tcgen05 WKV7 kernel gave up a bounded wait since the last call (synchronizes)");
+  m.def("fault_words_async", [](at::Tensor out) {
+        TORCH_CHECK(out.scalar_type() == at::kInt && out.numel() >= 3 && out.is_contiguous(),
+                    "fault_words_async needs a contiguous int32 tensor of 3 words");
+        cudaStream_t s = at::cuda::getCurrentCUDAStream();
+        int* p = out.data_ptr<int>();
+        check_cuda(rt_gemm_fault_async(p, s), "gemm fault word");
+        check_cuda(rt_wkv7_tc_fault_async(p + 1, s), "wkv7 forward fault word");
+        check_cuda(rt_wkv7_tc_bwd_fault_async(p + 2, s), "wkv7 backward fault word");
+      },
+      "enqueue on the current stream: copy the GEMM / WKV7 fault words into `out` (pinned) and clear them");
   m.def("wkv7_tc_enable", [](bool on) { g_wkv7_tc_enabled = on; },
         "route bf16 head-64 calls of >= 128 steps to the tcgen05 kernels (default) or to the chunk-16 kernels");
 }

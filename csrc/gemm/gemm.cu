@@ -929,6 +929,16 @@ extern "C" int rt_gemm_fault() {
   return v;
 }
 
+// Asynchronous form of rt_gemm_fault for a per-step metrics snapshot: on `stream`, copy the fault word to `dst`
+// (pinned host or device memory) and clear it. A nonzero copy means a launch before it gave up a wait; the
+// schedule counters are then reset by a later rt_gemm_fault call (the host raises and stops launching first).
+extern "C" cudaError_t rt_gemm_fault_async(int* dst, cudaStream_t stream) {
+  void* word = nullptr;
+  RT_CUDA_CHECK(cudaGetSymbolAddress(&word, gemm_fault_word));
+  RT_CUDA_CHECK(cudaMemcpyAsync(dst, word, sizeof(int), cudaMemcpyDefault, stream));
+  return cudaMemsetAsync(word, 0, sizeof(int), stream);
+}
+
 // Same with a fixed tile choice (width | 1 << 16 for stream-K); for tests and benchmarks of one schedule.
 extern "C" cudaError_t rt_gemm_bf16_tile(const void* A, long lda, int a_mn, const void* B, long ldb, int b_mn,
                                          void* C, long ldc, int M, int N, int K, int epi, float alpha, int choice,

@@ -610,3 +610,11 @@ extern "C" cudaError_t rt_wkv7_tc_forward(int B, int T, int H, const void* r, co
                                                                              chunks);
   return cudaGetLastError();
 }
+
+// Asynchronous form of the fault read: on `stream`, copy the fault word to `dst` and clear it.
+extern "C" cudaError_t rt_wkv7_tc_fault_async(int* dst, cudaStream_t stream) {
+  void* word = nullptr;
+  RT_CUDA_CHECK(cudaGetSymbolAddress(&word, wkv7_tc_fault_word));
+  RT_CUDA_CHECK(cudaMemcpyAsync(dst, word, sizeof(int), cudaMemcpyDefault, stream));
+  return cudaMemsetAsync(word, 0, sizeof(int), stream);
+}

@@ -111,12 +111,19 @@ class PeerGradExchange:
             torch.cuda.current_stream(self.device).wait_stream(self.stream)
             self.pending = False
 
-    def check(self):
-        """Raise if a device wait of any exchange so far ran out (host read of one status word)."""
-        words = self.sig[STATUS_WORD:WAITED_WORD + 1].cpu().tolist()
+    def status_words(self):
+        """The device status words (failure code .. waited rank) that ``check`` reads, as a tensor view."""
+        return self.sig[STATUS_WORD:WAITED_WORD + 1]
+
+    def raise_for(self, words):
+        """Raise for status words read from the device (``words`` as returned by ``status_words``)."""
         if words[0]:
             raise RuntimeError(f"peer gradient exchange on rank {self.rank} timed out waiting for rank "
                                f"{words[3]}'s {_WHAT.get(words[0], 'signal')} after {self.limit_s:.0f} s")
+
+    def check(self):
+        """Raise if a device wait of any exchange so far ran out (host read of one status word)."""
+        self.raise_for(self.status_words().cpu().tolist())
 
     # ---------------------------------------------------------------- sharded state
     def shard(self, n, rank):

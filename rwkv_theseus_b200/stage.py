@@ -162,6 +162,18 @@ class Student:
         dist.all_reduce(self.flat.grad, group=topo.student_group)
         dist.all_reduce(self.stats, group=topo.student_group)
 
+    def update_stream(self):
+        """The CUDA stream this student's updates run on (and write ``report`` on): the peer exchange's stream,
+        the device's side update stream, or None for the current stream."""
+        if self.topo.device.type != "cuda":
+            return None
+        exchange = self._exchange()
+        if exchange is not None:
+            return exchange.stream
+        if self.fused is not None and self.overlap_update:
+            return _update_stream(self.topo.device)
+        return None
+
     @torch.no_grad()
     def update(self):
         """Scale by 1/count, clip, AdamW, clear gradients; stats go to ``report``."""

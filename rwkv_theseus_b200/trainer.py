@@ -13,9 +13,10 @@ Semantics kept from the reference, mechanics of this implementation:
   per-layer reduction instead of running a dummy forward;
 * the teacher forward ends at the last migrated block's attention output (the
   blocks after it, its MLP and the final norm feed no capture);
-* token count, grad norm and error flags stay on the device; one copy per step
-  brings them to the host, where a non-finite norm or an empty update raises as
-  ``clip_grad_norm_(..., error_if_nonfinite=True)`` and the token check would;
+* token count, grad norm and error flags stay on the device; one asynchronous copy
+  per step brings them to the host, which reads step s while step s + 1 runs and
+  raises there, as ``clip_grad_norm_(..., error_if_nonfinite=True)`` and the token
+  check would (before any validation, checkpoint or stop the step is read first);
 * with the peer-memory exchange each layer's update runs on a side stream and
   the layer's next use waits for it (no step-wide join).
 
@@ -93,6 +94,12 @@ class StepEngine:
         self.device = topo.device
         self.last_capture = max(order)
         self.profiler = StepProfiler(self.device)
+        self._snap = None                     # [layers, 5] device copy of the step's reports (update stream)
+        self._slot = 0                        # pinned metric buffers used in turn
+        self._pinned_rows = [None, None]
+        self._pinned_faults = [None, None]
+        self._pinned_status = [None, None]
+        self._pending_events = [(), ()]
         self._pinned = [None, None]   # two pinned id buffers used in turn
         self._copied = [None, None]   # event after the copy that last read each buffer
         self._turn = 0
@@ -129,7 +136,9 @@ class StepEngine:
             self.runner.forward(self._to_device(batch["ids"]), through_layer=self.last_capture)
 
     def step(self, reader):
-        """One optimizer update of every layer; returns {layer: device report [nmse, cos, count, norm, error]}."""
+        """One optimizer update of every layer; returns {layer: device report [nmse, cos, count, norm, error]}.
+        Each report is also copied into the engine's step snapshot on the stream its update ran on, so that
+        ``read_metrics_async`` can read a step while the next one already runs."""
         profiler = self.profiler
         profiler.reset()
         micro_steps = self.cfg["grad_accum_steps"]
@@ -138,7 +147,7 @@ class StepEngine:
             if batch is not None:
                 self._teacher(batch)
             updating = micro == micro_steps - 1
-            for layer in self.order:
+            for index, layer in enumerate(self.order):
                 student, capture = self.students[layer], self.captures[layer]
                 if batch is not None:
                     with profiler.phase(f"student_{layer:02d}"):
@@ -148,31 +157,96 @@ class StepEngine:
                     with profiler.phase(f"update_{layer:02d}"):
                         student.reduce()
                         student.update()
+                    self._snapshot_report(index, student)
         return {layer: student.report for layer, student in self.students.items()}
 
+    # ---------------------------------------------------------------- metrics
+    def _snapshot_report(self, index, student):
+        if self._snap is None:
+            self._snap = torch.zeros(len(self.order), 5, device=self.device)
+        stream = student.update_stream()
+        if stream is None:
+            self._snap[index].copy_(student.report)
+            return
+        with torch.cuda.stream(stream):
+            self._snap[index].copy_(student.report)
+
+    def read_metrics_async(self, reports):
+        """Start bringing this step's reports, the kernels' fault words and the exchange status to the host; returns
+        a ``PendingMetrics`` whose ``result()`` waits for them and validates. The host may issue the next step in
+        between. The reports and the exchange status are copied on the stream the updates ran on (ordered after
+        this step's updates and before the next step's); the fault words are copied and cleared on the current
+        stream, in order with the kernels that set them."""
+        lrs = [self.cfg["lr"] * lr_factor(self.students[layer].steps_done - 1, self.cfg, self.students[layer].total_steps)
+               for layer in self.order]
+        if self.device.type != "cuda":
+            return PendingMetrics(self, torch.stack([reports[layer] for layer in self.order]), None, None, (), lrs)
+        slot = self._slot
+        self._slot ^= 1
+        for event in self._pending_events[slot]:
+            event.synchronize()  # the host has read that slot's previous step
+        if self._pinned_rows[slot] is None:
+            self._pinned_rows[slot] = torch.empty(len(self.order), 5, pin_memory=True)
+            self._pinned_faults[slot] = torch.zeros(3, dtype=torch.int32, pin_memory=True)
+            self._pinned_status[slot] = torch.zeros(4, dtype=torch.int32, pin_memory=True)
+        first = self.students[self.order[0]]
+        exchange = first._exchange()
+        main = torch.cuda.current_stream(self.device)
+        side = first.update_stream() or main
+        with torch.cuda.stream(side):
+            self._pinned_rows[slot].copy_(self._snap, non_blocking=True)
+            if exchange is not None:
+                self._pinned_status[slot].copy_(exchange.status_words(), non_blocking=True)
+            reports_copied = torch.cuda.Event()
+            reports_copied.record(side)
+        native().fault_words_async(self._pinned_faults[slot])
+        faults_copied = torch.cuda.Event()
+        faults_copied.record(main)
+        self._pending_events[slot] = (reports_copied, faults_copied)
+        return PendingMetrics(self, self._pinned_rows[slot], self._pinned_faults[slot],
+                              self._pinned_status[slot] if exchange is not None else None,
+                              self._pending_events[slot], lrs)
+
     def read_metrics(self, reports):
-        """One device-to-host copy of all layer reports; raises on update errors or a kernel that gave up a
-        bounded wait."""
-        for student in self.students.values():
-            student.join_update()
-        rows = torch.stack([reports[layer] for layer in self.order]).double().cpu().tolist()
-        self.topo.check_grad_sync()
-        if self.topo.device.type == "cuda":
-            ext = native()
-            if ext.gemm_fault():
-                raise RuntimeError("a tcgen05 GEMM gave up a bounded wait (results of this step are invalid)")
-            if ext.wkv7_tc_fault():
-                raise RuntimeError("a tcgen05 WKV7 kernel gave up a bounded wait (results of this step are invalid)")
+        """Synchronous form: the validated metrics of the step that produced `reports`."""
+        return self.read_metrics_async(reports).result()
+
+    def _validate(self, rows, faults, status, lrs):
+        if status is not None:
+            self.topo.grad_sync().raise_for(status)
+        if faults is not None and faults[0]:
+            native().gemm_fault()  # resets the GEMM schedule counters before the error propagates
+            raise RuntimeError("a tcgen05 GEMM gave up a bounded wait (results of this step are invalid)")
+        if faults is not None and (faults[1] or faults[2]):
+            raise RuntimeError(f"a tcgen05 WKV7 kernel gave up a bounded wait (fault words {faults[1]:#x}, "
+                               f"{faults[2]:#x}; results of this step are invalid)")
         report = {}
-        for layer, (nmse, cos, count, norm, bad) in zip(self.order, rows):
+        for layer, (nmse, cos, count, norm, bad), lr in zip(self.order, rows, lrs):
             if count <= 0:
                 raise RuntimeError("No training tokens in update")
             if bad or not np.isfinite(norm):
                 raise RuntimeError(f"The total norm of gradients for layer {layer} is non-finite")
-            student = self.students[layer]
-            lr = self.cfg["lr"] * lr_factor(student.steps_done - 1, self.cfg, student.total_steps)
             report[f"layer_{layer:02d}"] = metrics(torch.tensor([nmse, cos, count])) | {"grad_norm": norm, "lr": lr}
         return report
+
+
+class PendingMetrics:
+    """One step's metrics on their way to the host (``StepEngine.read_metrics_async``)."""
+
+    def __init__(self, engine, rows, faults, status, events, lrs):
+        self.engine, self.rows, self.faults, self.status, self.events = engine, rows, faults, status, events
+        self.lrs = lrs
+        self._value = None
+
+    def result(self):
+        if self._value is None:
+            for event in self.events:
+                event.synchronize()
+            rows = self.rows.double().tolist()
+            faults = None if self.faults is None else self.faults.tolist()
+            status = None if self.status is None else self.status.tolist()
+            self._value = self.engine._validate(rows, faults, status, self.lrs)
+        return self._value
 
 
 def run(cfg, resume=None, stop_after=None):
@@ -319,23 +393,34 @@ class MigrationJob:
                         desc=f"Parallel migration ({len(self.order)} layers)", mininterval=0.5,
                         disable=self.topo.rank != self.topo.leader or os.environ.get("TQDM_DISABLE") == "1")
         self.saved = self.checkpoint
+        pending = None  # (step, PendingMetrics) read after the next step is issued
         try:
             for step in range(self.step0 + 1, self.max_steps + 1):
-                layer_metrics = self.engine.read_metrics(self.engine.step(self.reader))
-                self._log_step(step, layer_metrics, progress)
+                reports = self.engine.step(self.reader)
+                if pending is not None:
+                    self._log_step(pending[0], pending[1].result(), progress)
+                pending = (step, self.engine.read_metrics_async(reports))
                 complete = step == self.max_steps
+                stopping = self.stop_after is not None and step - self.step0 >= self.stop_after
+                boundary = (complete or stopping or self.engine.profiler.on
+                            or self._due(step, "validation_interval", complete)
+                            or self._due(step, "checkpoint_interval", complete))
+                if boundary:  # validation, checkpoint, stop and profiling act on a finished, logged step
+                    self._log_step(pending[0], pending[1].result(), progress)
+                    pending = None
                 if complete and cfg["training_mode"] == "epoch" and not self.reader.exhausted:
                     raise RuntimeError("Training ended before the local token shard was exhausted")
                 if self._due(step, "validation_interval", complete):
                     result = validate_parallel(self.topo, cfg, self.runner, self.students, self.captures)
                     self.journal("validation", step=step, **result)
-                stopping = self.stop_after is not None and step - self.step0 >= self.stop_after
                 if stopping or self._due(step, "checkpoint_interval", complete):
                     self.saved = save_checkpoint(self.topo, cfg, step, complete, self.order, self.runner,
                                                  self.reader, self.base_id, self.students)
                     self.journal("checkpoint", path=str(self.saved), complete=complete)
                 if stopping and not complete:
                     return False
+            if pending is not None:
+                self._log_step(pending[0], pending[1].result(), progress)
             return True
         finally:
             progress.close()
