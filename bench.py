@@ -184,7 +184,28 @@ def build_ours(args, topo, manifest, model_spec):
     def finish():
         while pending:
             pending.pop(0).result()
+
+    def phases():
+        """Milliseconds per phase kind of one extra, untimed step: device time between CUDA events on the compute
+        stream (updates: the enqueue on that stream; the optimizer and exchange kernels run on a side stream) and
+        host time spent issuing the phase, plus the whole step's device time."""
+        engine.profiler.on = True
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        try:
+            start.record()
+            engine.step(reader)
+            stop.record()
+            dev, host = engine.profiler.summary(), engine.profiler.host_summary()
+            stop.synchronize()
+        finally:
+            engine.profiler.on = False
+        out = {"step_ms": start.elapsed_time(stop)}
+        for key, prefix in (("teacher", "teacher"), ("students", "student_"), ("updates", "update_")):
+            out[f"{key}_ms"] = sum(v for k, v in dev.items() if k.startswith(prefix))
+            out[f"{key}_host_ms"] = sum(v for k, v in host.items() if k.startswith(prefix))
+        return {k: round(v, 3) for k, v in out.items()}
     step.finish = finish
+    step.phases = phases
     return step
 
 
@@ -271,9 +292,10 @@ def count_launches(step_fn):
     """Kernels launched by one step, split into this package's kernels and others (profiled, untimed)."""
     import torch
     from torch.profiler import ProfilerActivity, profile
-    mine = ("wkv7_", "gemm_kernel", "rmsnorm_kernel", "conv1d_silu", "gdn_", "mix_kernel", "mix_bwd", "pre_wkv",
+    mine = ("wkv7_", "gemm_kernel", "rmsnorm_", "conv1d_silu", "gdn_", "mix_kernel", "mix_bwd", "pre_wkv",
             "post_wkv", "nmse_loss", "adamw_kernel", "scale_norm", "act_kernel", "act_bwd", "norm_rope",
-            "copy_rows", "to_bf16", "report_kernel", "gated_rmsnorm", "flash_attn", "exchange_")
+            "copy_rows", "to_bf16", "report_kernel", "gated_rmsnorm", "flash_attn", "exchange_", "loss_rows",
+            "norm2_kernel", "skinny_", "kl_")
     with profile(activities=[ProfilerActivity.CUDA]) as prof:
         step_fn(False)
         torch.cuda.synchronize()
@@ -290,6 +312,19 @@ def count_launches(step_fn):
     return ours, other, names
 
 
+def kernel_group(name):
+    """Kernel name without parameters and namespaces; GEMMs keep their tile width and epilogue code."""
+    if name.startswith("Memcpy") or name.startswith("Memset"):
+        return name.split(" ")[0]
+    plain = name.replace("(anonymous namespace)::", "")
+    head = (plain[5:] if plain.startswith("void ") else plain).split("(")[0]
+    if "gemm_kernel<" in name:
+        args = name.split("gemm_kernel<", 1)[1].split(">")[0].split(",")
+        return f"gemm_kernel<BN {args[0].strip()}, EPI {args[-1].strip()}>"
+    head = head.split("<")[0]
+    return head.rsplit("::", 1)[-1] or name[:60]
+
+
 def print_breakdown(step_fn, rank):
     """Per-kernel device time of one step, grouped by kernel name (profiled; not a benchmark number)."""
     import torch
@@ -302,14 +337,7 @@ def print_breakdown(step_fn, rank):
     for evt in prof.events():
         if evt.device_type != torch.autograd.DeviceType.CUDA:
             continue
-        name = evt.name
-        for key in ("gemm_kernel<256", "gemm_kernel<128", "gemm_kernel<64", "wkv7_forward", "wkv7_backward",
-                    "gdn_chunk", "gdn_prep", "fmha", "sdpa", "flash", "efficient_attention", "adamw", "scale_norm",
-                    "rmsnorm", "conv1d", "post_wkv_bwd", "pre_wkv_bwd", "post_wkv", "pre_wkv", "mix_bwd",
-                    "mix_kernel", "nmse", "gated_rmsnorm", "norm_rope", "elementwise", "Memcpy", "Memset"):
-            if key in name:
-                name = key
-                break
+        name = kernel_group(evt.name)
         dur = evt.device_time_total if hasattr(evt, "device_time_total") else evt.cuda_time_total
         groups[name] = groups.get(name, [0.0, 0])
         groups[name][0] += dur
@@ -319,6 +347,43 @@ def print_breakdown(step_fn, rank):
         for name, (us, n) in sorted(groups.items(), key=lambda kv: -kv[1][0])[:30]:
             print(f"{us / 1000:9.3f} ms {100 * us / total:5.1f}% {n:6d}  {name[:90]}")
         print(f"{total / 1000:9.3f} ms total kernel time")
+        print_timeline(prof)
+
+
+def print_timeline(prof):
+    """Busy time per stream, the step's span and the largest idle gaps of the device (all streams together)."""
+    import torch
+    spans = []
+    for e in prof.profiler.kineto_results.events():
+        if e.device_type() != torch.autograd.DeviceType.CUDA or e.duration_ns() <= 0:
+            continue
+        spans.append((e.start_ns(), e.end_ns(), e.device_resource_id(), kernel_group(e.name())))
+    if not spans:
+        return
+    spans.sort()
+    t0, t1 = spans[0][0], max(s[1] for s in spans)
+    busy = {}
+    for stream in {s[2] for s in spans}:
+        end, total = 0, 0
+        for a, b, st, _ in spans:
+            if st != stream:
+                continue
+            a = max(a, end)
+            if b > a:
+                total += b - a
+                end = b
+        busy[stream] = total
+    gaps, end, before = [], spans[0][1], spans[0][3]
+    for a, b, _, name in spans[1:]:
+        if a > end:
+            gaps.append((a - end, before, name))
+        if b > end:
+            end, before = b, name
+    print(f"step span {(t1 - t0) / 1e6:.3f} ms; busy per stream (ms): "
+          + ", ".join(f"{st}: {ns / 1e6:.3f}" for st, ns in sorted(busy.items(), key=lambda kv: -kv[1])))
+    print(f"device idle {sum(g[0] for g in gaps) / 1e6:.3f} ms in {len(gaps)} gaps; largest:")
+    for ns, a, b in sorted(gaps, reverse=True)[:12]:
+        print(f"  {ns / 1e3:9.1f} us  after {a[:40]}  before {b[:40]}")
 
 
 def main():
@@ -397,6 +462,7 @@ def main():
     total_tokens = sum(g[1].item() for g in gathered)
     e2e_max = max(g[2].item() for g in gathered)
     e2e_total = sum(g[3].item() for g in gathered)
+    phases = step.phases() if hasattr(step, "phases") else None
     ours_launches, other_launches, other_names = count_launches(step) if args.impl == "ours" else (0, 0, {})
     value = total_tokens / (ms_max / 1000)
     if rank == 0:
@@ -418,6 +484,7 @@ def main():
                 # ours: 16 reports of 5 fp32, 3 fault words, 4 exchange status words (world > 1)
                 "d2h_bytes_per_step": (4 * 5 * 16 + 4 * 3 + (16 if world > 1 else 0)) if args.impl == "ours"
                 else 4 * 3 * 16},
+            "phases_ms": phases,  # one extra untimed step (rank 0): device and host ms per phase kind
             "gpu_launches": ours_launches * args.steps,
             "other_launches_per_step": other_launches,
         }

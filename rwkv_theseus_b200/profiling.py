@@ -24,9 +24,11 @@ class StepProfiler:
         self.on = enabled() if on is None else on
         self.cuda = device.type == "cuda"
         self.marks = []  # (name, start, end)
+        self.host = {}   # phase -> host seconds spent issuing it
 
     def reset(self):
         self.marks = []
+        self.host = {}
 
     @contextmanager
     def phase(self, name):
@@ -37,9 +39,11 @@ class StepProfiler:
             torch.cuda.nvtx.range_push(name)
             start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             start.record()
+            t0 = time.perf_counter()
             try:
                 yield
             finally:
+                self.host[name] = self.host.get(name, 0.0) + time.perf_counter() - t0
                 end.record()
                 torch.cuda.nvtx.range_pop()
                 self.marks.append((name, start, end))
@@ -49,6 +53,10 @@ class StepProfiler:
                 yield
             finally:
                 self.marks.append((name, t0, time.perf_counter()))
+
+    def host_summary(self):
+        """{phase: ms} of host time spent issuing each phase in the last step (summed over repeats)."""
+        return {name: 1000.0 * sec for name, sec in self.host.items()}
 
     def summary(self):
         """{phase: ms} summed over repeated phases of the step (synchronizes the device once)."""
