@@ -228,11 +228,21 @@ class TextModel(nn.Module):
         start = int(positions[0]) if torch.is_tensor(positions) else int(positions)
         x = self.embed_tokens(ids)
         rope = T.rope_tables(self.inv_freq, start, ids.shape[1], x.device, x.dtype)
+        # Each block's MLP residual is added by the next norm's fused add + RMSNorm kernel (x + mlp rounded to
+        # x.dtype, then normalised), the same values as DecoderLayer.forward followed by the next input norm.
+        pending = None
         for index, layer in enumerate(self.layers):
+            norm = layer.input_layernorm
+            if pending is None:
+                normed = norm(x)
+            else:
+                x, normed = T.add_rmsnorm(x, pending, norm.weight, norm.eps)
+            h = layer.mixer(normed, rope, cache)
             if index == stop_at:
-                return layer.mixer(layer.input_layernorm(x), rope, cache)
-            x = layer(x, rope, cache)
-        return self.norm(x)
+                return h
+            x, h = T.add_rmsnorm(x, h, layer.post_attention_layernorm.weight, layer.post_attention_layernorm.eps)
+            pending = layer.mlp(h)
+        return T.add_rmsnorm(x, pending, self.norm.weight, self.norm.eps)[1]
 
 
 class HybridForCausalLM(nn.Module):
