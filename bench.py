@@ -17,8 +17,9 @@ Timing: W untimed warm-up steps, then K steps bracketed by a barrier and
 device synchronisation, timed with CUDA events; the reported number is the
 total token count over all ranks divided by the slowest rank's time. The
 working set (54 GB of teacher weights per step) exceeds L2, so no flush is
-needed between steps. ``e2e`` repeats K steps through the public step API
-with the per-step host-to-device copy of token ids from pinned memory and the
+needed between steps. ``e2e`` runs the same K batches again (reader, teacher
+cache and student states restored) through the public step API with the
+per-step host-to-device copy of token ids from pinned memory and the
 device-to-host read of every step's loss metrics inside the timed region; the
 read of step s completes after step s + 1 is issued, and the last step's read
 completes before the clock stops.
@@ -27,6 +28,7 @@ completes before the clock stops.
 baseline/_ref) through its own API on the same synthetic data.
 """
 import argparse
+import copy
 import json
 import os
 import subprocess
@@ -204,8 +206,27 @@ def build_ours(args, topo, manifest, model_spec):
             out[f"{key}_ms"] = sum(v for k, v in dev.items() if k.startswith(prefix))
             out[f"{key}_host_ms"] = sum(v for k, v in host.items() if k.startswith(prefix))
         return {k: round(v, 3) for k, v in out.items()}
+    def snapshot():
+        """Reader position, teacher cache and student states, so that the e2e pass replays the timed batches."""
+        states = {layer: None if st.state is None else {k: v.clone() for k, v in st.state.items()}
+                  for layer, st in students.items()}
+        return copy.deepcopy(reader.state_dict()), runner.state_dict(), states
+
+    def restore(snap):
+        reader.load_state_dict(copy.deepcopy(snap[0]))
+        runner.load_state_dict(snap[1])
+        for layer, state in snap[2].items():
+            students[layer].state = state
+    def set_overlap(on):
+        for student in students.values():
+            student.overlap_update = on
+
+    def profiled(on):
+        engine.profiler.on = on
     step.finish = finish
     step.phases = phases
+    step.snapshot, step.restore = snapshot, restore
+    step.set_overlap, step.profiled = set_overlap, profiled
     return step
 
 
@@ -326,16 +347,33 @@ def kernel_group(name):
 
 
 def print_breakdown(step_fn, rank):
-    """Per-kernel device time of one step, grouped by kernel name (profiled; not a benchmark number)."""
+    """Per-kernel device time of one step, grouped by kernel name, then by step phase (profiled; not a benchmark
+    number). Also the phase split of one step with the optimizer updates overlapped (the default) and serial."""
     import torch
     from torch.profiler import ProfilerActivity, profile
-    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+    if hasattr(step_fn, "phases"):
+        snap = step_fn.snapshot()  # both splits and the profiled step run the same batch
+        overlapped = step_fn.phases()
+        step_fn.restore(snap)
+        snap = step_fn.snapshot()
+        step_fn.set_overlap(False)
+        serial = step_fn.phases()
+        step_fn.set_overlap(True)
+        step_fn.restore(snap)
+        if rank == 0:
+            print("phases, updates overlapped:", json.dumps(overlapped))
+            print("phases, updates serial:    ", json.dumps(serial))
+    if hasattr(step_fn, "profiled"):
+        step_fn.profiled(True)
+    with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA]) as prof:
         step_fn(False)
         torch.cuda.synchronize()
+    if hasattr(step_fn, "profiled"):
+        step_fn.profiled(False)
     groups = {}
     total = 0.0
     for evt in prof.events():
-        if evt.device_type != torch.autograd.DeviceType.CUDA:
+        if evt.device_type != torch.autograd.DeviceType.CUDA or evt.name.startswith("phase:"):
             continue
         name = kernel_group(evt.name)
         dur = evt.device_time_total if hasattr(evt, "device_time_total") else evt.cuda_time_total
@@ -348,6 +386,37 @@ def print_breakdown(step_fn, rank):
             print(f"{us / 1000:9.3f} ms {100 * us / total:5.1f}% {n:6d}  {name[:90]}")
         print(f"{total / 1000:9.3f} ms total kernel time")
         print_timeline(prof)
+        print_phase_kernels(prof)
+
+
+def print_phase_kernels(prof):
+    """Kernel time per step phase: each kernel is charged to the innermost ``phase:`` range that contains the host
+    call that launched it (the launch's correlation id; a CUDA graph replay charges all its kernels)."""
+    import torch
+    cpu, cuda = torch.autograd.DeviceType.CPU, torch.autograd.DeviceType.CUDA
+    events = prof.profiler.kineto_results.events()
+    ranges = sorted((e.start_ns(), e.end_ns(), e.name()[6:]) for e in events
+                    if e.device_type() == cpu and e.name().startswith("phase:"))
+    launch_at = {e.correlation_id(): e.start_ns() for e in events
+                 if e.device_type() == cpu and e.name().startswith("cuda")}
+    per = {}
+    for e in events:
+        if e.device_type() != cuda or e.name().startswith("phase:") or e.duration_ns() <= 0:
+            continue
+        at = launch_at.get(e.correlation_id())
+        phase = "other"
+        if at is not None:
+            inside = [r for r in ranges if r[0] <= at <= r[1]]
+            if inside:
+                name = min(inside, key=lambda r: r[1] - r[0])[2]
+                phase = name.split("_")[0]
+        kinds = per.setdefault(phase, {})
+        group = kernel_group(e.name())
+        kinds[group] = kinds.get(group, 0) + e.duration_ns()
+    for phase, kinds in sorted(per.items(), key=lambda kv: -sum(kv[1].values())):
+        print(f"phase {phase}: {sum(kinds.values()) / 1e6:.3f} ms of kernels")
+        for group, ns in sorted(kinds.items(), key=lambda kv: -kv[1])[:12]:
+            print(f"    {ns / 1e6:8.3f} ms  {group[:80]}")
 
 
 def print_timeline(prof):
@@ -355,7 +424,7 @@ def print_timeline(prof):
     import torch
     spans = []
     for e in prof.profiler.kineto_results.events():
-        if e.device_type() != torch.autograd.DeviceType.CUDA or e.duration_ns() <= 0:
+        if e.device_type() != torch.autograd.DeviceType.CUDA or e.duration_ns() <= 0 or e.name().startswith("phase:"):
             continue
         spans.append((e.start_ns(), e.end_ns(), e.device_resource_id(), kernel_group(e.name())))
     if not spans:
@@ -430,6 +499,7 @@ def main():
     time.sleep(2.0)
     for _ in range(args.warmup):
         step(False)
+    snap = step.snapshot() if hasattr(step, "snapshot") else None
     barrier()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
@@ -444,6 +514,9 @@ def main():
     e2e_ms = None
     e2e_tokens = 0
     if not args.no_e2e:
+        if snap is not None:
+            step.restore(snap)  # the e2e pass runs the same K batches as the device-timed pass
+            del snap
         barrier()
         t0 = time.perf_counter()
         for _ in range(args.steps):
@@ -479,7 +552,8 @@ def main():
             "clocks": clocks,
             "e2e": None if args.no_e2e else {
                 "value": e2e_total / (e2e_max / 1000), "unit": "tokens/s",
-                "ms_per_step": e2e_max / args.steps, "tokens_timed": e2e_total,  # the next K batches
+                "ms_per_step": e2e_max / args.steps, "tokens_timed": e2e_total,
+                "batches": "the device-timed K batches again" if args.impl == "ours" else "the next K batches",
                 "h2d_bytes_per_step": 8 * args.chunk * args.micro_batch,
                 # ours: 16 reports of 5 fp32, 3 fault words, 4 exchange status words (world > 1)
                 "d2h_bytes_per_step": (4 * 5 * 16 + 4 * 3 + (16 if world > 1 else 0)) if args.impl == "ours"

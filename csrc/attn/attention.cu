@@ -78,7 +78,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 flash_attn_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                       const __grid_constant__ CUtensorMap tv, const AttnArgs args) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem = sm100::align_smem_1024(smem_raw);
   uint8_t* sQ = smem;
   uint8_t* sKV = sQ + Q_BYTES;                  // stage s: K at s*KV_BYTES, V at s*KV_BYTES + DCH*KCH_BYTES
   uint8_t* sP = sKV + 2 * KV_BYTES;             // buffer b at b*P_BYTES

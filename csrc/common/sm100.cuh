@@ -28,6 +28,13 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// The dynamic shared-memory base rounded up to 1024 bytes (what the 128-byte swizzled tiles need), as an offset
+// from the array itself: unlike rounding through an integer cast, the result keeps the array's address space, so
+// accesses through it compile to shared loads and stores instead of generic ones.
+__device__ __forceinline__ uint8_t* align_smem_1024(uint8_t* smem) {
+  return smem + ((1024u - (smem_u32(smem) & 1023u)) & 1023u);
+}
+
 __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

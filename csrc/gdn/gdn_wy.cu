@@ -507,7 +507,7 @@ gdn_out_tc_kernel(const float* __restrict__ qn, const float* __restrict__ kn, co
                   int Tp, int Hk, int Hv, int* __restrict__ status) {
   constexpr int D = 128;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sm = sm100::align_smem_1024(smem_raw);
   uint8_t* QK = sm + tc::QK_OFF;   // 128 rows (q_0..63, k_0..63) x 128 keys
   uint8_t* Sx = sm + tc::S_OFF;    // 128 value rows x 128 keys
   uint8_t* VT = sm + tc::VT_OFF;   // 128 value rows x 64 steps
@@ -679,7 +679,7 @@ gdn_state_tc_kernel(const float* __restrict__ kn, const float* __restrict__ W, f
                     int Tp, int Hk, int Hv, int* __restrict__ status) {
   constexpr int D = 128, NTH = 256;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sm = sm100::align_smem_1024(smem_raw);
   float* U0s = reinterpret_cast<float*>(sm + tcs::U0_OFF);
   float* lam = reinterpret_cast<float*>(sm + tcs::MISC_OFF);
   float* fac = lam + LC;

@@ -108,80 +108,80 @@ RT_DEVICE void build_lambda(const uint8_t* Rw, float* lam, float* carry, int nva
   __syncthreads();
 }
 
-// One 16 x 16 block (bi, bj) of the inverse being built: diagonal blocks from `td`, the others from `mpl`.
-RT_DEVICE float tblock(const float* mpl, const float* td, int bi, int bj, int r, int c) {
-  return bi == bj ? td[bi * 256 + r * 16 + c] : mpl[poff(16 * bi + r, 16 * bj + c)];
+// Triangular solves with the strictly lower 64 x 64 chunk matrix M (plain swizzled rows in `mpl`, zero on and
+// above the diagonal), one right-hand side per thread held in registers. Every thread reads the same M entries
+// (broadcast float4 loads). With one warp per scheduler the loads' latency is not hidden by other warps, so the
+// row needed next is loaded into registers while the current row's products run (explicit double buffer); all
+// loops unroll, so x and the buffers stay in registers.
+// Shared-space address of M for the solves. The empty volatile asm pins the point where the address is taken
+// (after the barrier that published M), so the loads below, which depend on it, cannot be hoisted above it.
+RT_DEVICE uint32_t shared_base(const float* p) {
+  uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
+  asm volatile("" : "+r"(a));
+  return a;
+}
+// 16-byte shared load of M[t][4g .. 4g+3] (an explicit ld.shared: the plain pointer reaches here through integer
+// alignment arithmetic, which hides its address space from the compiler).
+RT_DEVICE float4 mrow4(uint32_t mpl, int t, int g) {
+  float4 v;
+  asm("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+      : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+      : "r"(mpl + 4u * (uint32_t)poff(t, 4 * g)));
+  return v;
 }
 
-// T = (I - M)^{-1} for the strictly lower 64 x 64 M in `mpl` (plain swizzled), in place; 128 threads.
-//  1. the four diagonal 16 x 16 blocks by right-looking substitution (thread = column; after x[s] is final every
-//     later row's sum takes its term, so the updates of one step are independent);
-//  2. the off-diagonal blocks by distance d = i - j = 1, 2, 3:  R_j = sum_{k=j}^{i-1} M_ik T_kj, then T_ij = T_ii R_j,
-//     each a batch of independent 16 x 16 block products spread over all threads (up to six outputs per thread).
-// Scratch: rtmp >= 768 floats, td >= 1024 floats.
-RT_DEVICE void invert_unit_lower(float* mpl, float* rtmp, float* td, int tid) {
-  if (tid < 64) {
-    const int kb = tid >> 4, cc = tid & 15, base = 16 * kb;
-    float acc[16];
+// x <- (I - M)^{-1} x: forward substitution, left-looking: x_t += sum_{s < t} M[t][s] x_s (four partial sums).
+RT_DEVICE void solve_lower(const float* mpl_ptr, float (&x)[64]) {
+  const uint32_t mpl = shared_base(mpl_ptr);
+  float4 cur[16], nxt[16];
+  cur[0] = mrow4(mpl, 1, 0);
 #pragma unroll
-    for (int r = 0; r < 16; ++r) acc[r] = r == cc ? 1.f : 0.f;
+  for (int t = 1; t < 64; ++t) {
+    const int n = (t + 3) >> 2;  // float4 groups holding M[t][0..t-1]
+    if (t + 1 < 64) {
 #pragma unroll
-    for (int s = 0; s < 16; ++s) {
-      const float xs = s >= cc ? acc[s] : 0.f;
-      acc[s] = xs;
-#pragma unroll
-      for (int r = s + 1; r < 16; ++r) acc[r] += mpl[poff(base + r, base + s)] * xs;
+      for (int g = 0; g < ((t + 4) >> 2); ++g) nxt[g] = mrow4(mpl, t + 1, g);
     }
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int r = 0; r < 16; ++r) td[kb * 256 + r * 16 + cc] = acc[r];
+    for (int g = 0; g < n; ++g) {
+      const int s = 4 * g;
+      acc[0] += cur[g].x * x[s];
+      if (s + 1 < t) acc[1] += cur[g].y * x[s + 1];
+      if (s + 2 < t) acc[2] += cur[g].z * x[s + 2];
+      if (s + 3 < t) acc[3] += cur[g].w * x[s + 3];
+    }
+    x[t] += (acc[0] + acc[1]) + (acc[2] + acc[3]);
+#pragma unroll
+    for (int g = 0; g < 16; ++g) cur[g] = nxt[g];
   }
-  __syncthreads();
-#pragma unroll 1
-  for (int d = 1; d < 4; ++d) {
-    const int nb = 4 - d;  // blocks (j + d, j), j = 0 .. nb - 1
-    float acc[6];
+}
+
+// x <- (I - M)^{-T} x: back substitution, right-looking from the last row: once x_t is final,
+// x_s += M[t][s] x_t for every s < t (independent updates).
+RT_DEVICE void solve_upper_t(const float* mpl_ptr, float (&x)[64]) {
+  const uint32_t mpl = shared_base(mpl_ptr);
+  float4 cur[16], nxt[16];
 #pragma unroll
-    for (int q = 0; q < 6; ++q) acc[q] = 0.f;
-#pragma unroll 1
-    for (int kk = 0; kk < d; ++kk) {
-#pragma unroll 4
-      for (int m = 0; m < 16; ++m) {
+  for (int g = 0; g < 16; ++g) cur[g] = mrow4(mpl, 63, g);
 #pragma unroll
-        for (int q = 0; q < 6; ++q) {
-          const int e = tid + 128 * q, j = e >> 8, r = (e >> 4) & 15, c = e & 15;
-          if (q < 2 * nb) {
-            const int k = j + kk;
-            acc[q] += mpl[poff(16 * (j + d) + r, 16 * k + m)] * tblock(mpl, td, k, j, m, c);
-          }
-        }
-      }
+  for (int t = 63; t >= 1; --t) {
+    if (t > 1) {
+#pragma unroll
+      for (int g = 0; g < ((t + 2) >> 2); ++g) nxt[g] = mrow4(mpl, t - 1, g);  // M[t-1][0..t-2]
+    }
+    const float xt = x[t];
+#pragma unroll
+    for (int g = 0; g < ((t + 3) >> 2); ++g) {
+      const int s = 4 * g;
+      x[s] += cur[g].x * xt;
+      if (s + 1 < t) x[s + 1] += cur[g].y * xt;
+      if (s + 2 < t) x[s + 2] += cur[g].z * xt;
+      if (s + 3 < t) x[s + 3] += cur[g].w * xt;
     }
 #pragma unroll
-    for (int q = 0; q < 6; ++q)
-      if (q < 2 * nb) rtmp[tid + 128 * q] = acc[q];
-    __syncthreads();
-#pragma unroll
-    for (int q = 0; q < 6; ++q) acc[q] = 0.f;
-#pragma unroll 4
-    for (int m = 0; m < 16; ++m) {
-#pragma unroll
-      for (int q = 0; q < 6; ++q) {
-        const int e = tid + 128 * q, j = e >> 8, r = (e >> 4) & 15, c = e & 15;
-        if (q < 2 * nb) acc[q] += td[(j + d) * 256 + r * 16 + m] * rtmp[j * 256 + m * 16 + c];
-      }
-    }
-#pragma unroll
-    for (int q = 0; q < 6; ++q) {
-      const int e = tid + 128 * q, j = e >> 8, r = (e >> 4) & 15, c = e & 15;
-      if (q < 2 * nb) mpl[poff(16 * (j + d) + r, 16 * j + c)] = acc[q];
-    }
-    __syncthreads();
+    for (int g = 0; g < 16; ++g) cur[g] = nxt[g];
   }
-  for (int e = tid; e < 4 * 256; e += 128) {
-    const int kb = e >> 8, r = (e >> 4) & 15, c = e & 15;
-    mpl[poff(16 * kb + r, 16 * kb + c)] = td[e];
-  }
-  __syncthreads();
 }
 
 }  // namespace wtc

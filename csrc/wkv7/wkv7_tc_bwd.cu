@@ -3,8 +3,8 @@
 //
 // With dS the gradient of a chunk's end state and dY of its outputs, the chunk-start gradient is
 //     dS0 = dS G^T + dY^T Q                       (G, Q from the forward records),
-// a serial scan over chunks (kernel 1). Per chunk, from the chunk-start state S0 (forward checkpoint), dS and
-// the stored T = (I - M_ab)^{-1}:
+// a serial scan over chunks (kernel 1). Per chunk, from the chunk-start state S0 (forward checkpoint) and dS,
+// with T = (I - M_ab)^{-1} applied by fp32 triangular solves (never formed):
 //     U  = T (A~ S0^T + M_ak V)                    (the chunk's u_t = S_{t-1} a_t rows)
 //     dU = M_rb^T dY + B^ dS^T,  dZ = T^T dU,  dV = M_rk^T dY + K^ dS^T + M_ak^T dZ          (kernel 2)
 //     dM_ab = (dZ U^T) strict, dM_ak = (dZ V^T) strict, dM_rb = (dY U^T) incl, dM_rk = (dY V^T) incl
@@ -42,19 +42,16 @@ __device__ unsigned long long wkv7_trace_ns[64];
 
 constexpr int KB = 1024;
 constexpr int MAT = N * N;
-enum { REC_G = 0, REC_H0 = 1, REC_Q = 2, REC_Y0 = 3, REC_T = 4, REC_MATS = 5 };  // forward record (fwd file)
+enum { REC_G = 0, REC_H0 = 1, REC_Q = 2, REC_Y0 = 3, REC_MATS = 4 };  // forward record (fwd file)
 enum { WK_DS = 0, WK_U = 1, WK_DZ = 2, WK_MATS = 3 };                             // backward work record
 
 __device__ int wkv7_tc_bwd_fault_word = 0;
 
-RT_DEVICE uint8_t* align1024(uint8_t* p) {
-  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
-}
+RT_DEVICE uint8_t* align1024(uint8_t* p) { return sm100::align_smem_1024(p); }
 RT_DEVICE bool wait_all(uint64_t* bar, uint32_t parity) {
   const bool ok = sm100::mbar_wait_bounded(bar, parity);
   return __syncthreads_and(ok ? 1 : 0) != 0;
 }
-RT_DEVICE float bf(const __nv_bfloat16* p) { return __bfloat162float(*p); }
 
 // Row `row` of a K-major tile of `rows` rows from 64 fp32 values in global memory (rounded to tf32).
 RT_DEVICE void tile_row_from_global(uint8_t* tile, int rows, int row, const float* src) {
@@ -163,7 +160,7 @@ constexpr int X2 = 105 * KB;    // [B~; K~] -> [M_rb^T; M_rk^T]  -> T^T (105..12
 constexpr int VT = 137 * KB;    // V^T (64 rows)                 -> M_ak^T at 129..145 after MMA-Z
 constexpr int BKH = 153 * KB;   // [B^; K^] (128 rows)
 constexpr int DYT = 185 * KB;   // dY^T (64 rows)
-// after phase A (raw, Lambda dead): S0 (0..16), dS (16..32), T (32..48), M_ak (48..64; read as 128 rows)
+// after phase A (raw, Lambda dead): S0 (0..16), dS (16..32), M_ab plain (32..48), M_ak (48..64; read as 128 rows)
 constexpr int SMEM = 201 * KB + 1024;
 }  // namespace ka
 
@@ -171,8 +168,7 @@ __global__ void __launch_bounds__(128, 1)
 wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_constant__ CUtensorMap m_w,
                          const __grid_constant__ CUtensorMap m_k, const __grid_constant__ CUtensorMap m_v,
                          const __grid_constant__ CUtensorMap m_a, const __grid_constant__ CUtensorMap m_b,
-                         const __grid_constant__ CUtensorMap m_dy, const __grid_constant__ CUtensorMap m_t,
-                         const float* __restrict__ ckpt, float* __restrict__ work, float* __restrict__ dv, int T,
+                         const __grid_constant__ CUtensorMap m_dy, const float* __restrict__ ckpt, float* __restrict__ work, float* __restrict__ dv, int T,
                          int H, int chunks) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
@@ -185,8 +181,11 @@ wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_c
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + ka::MISC);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + ka::MISC + 32);
   uint8_t *X1 = sm + ka::X1, *X2 = sm + ka::X2, *VT = sm + ka::VT, *BKH = sm + ka::BKH, *DYT = sm + ka::DYT;
-  uint8_t *S0t = sm, *DSt = sm + 16 * KB, *Tt = sm + 32 * KB, *MAK = sm + 48 * KB;
-  uint8_t *MRT = X2, *ZFT = X1, *DUT = X1 + 16 * KB, *TTt = X2, *MAKT = sm + 129 * KB, *DZT = sm;
+  uint8_t *S0t = sm, *DSt = sm + 16 * KB, *MAK = sm + 48 * KB;
+  float* MPL = reinterpret_cast<float*>(sm + 32 * KB);
+  float* ZP = reinterpret_cast<float*>(X1);             // Zf^T, plain (row i = column i of Zf)
+  float* DUP = reinterpret_cast<float*>(X1 + 16 * KB);  // dU^T, plain
+  uint8_t *MRT = X2, *MAKT = sm + 129 * KB, *DZT = sm;
   const long bh = (long)bb * H + h, ch = bh * chunks + c;
   const float* S0g = ckpt + (bh * (chunks + 1) + c) * MAT;
   float* wk = work + ch * WK_MATS * MAT;
@@ -196,7 +195,6 @@ wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_c
   if (tid == 0) {
     sm100::mbar_init(&bars[0], 1);
     sm100::mbar_init(&bars[1], 1);
-    sm100::mbar_init(&bars[2], 1);
     sm100::fence_barrier_init();
   }
   if (warp == 0) {
@@ -220,7 +218,6 @@ wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_c
   }
   int stage = 1;
   bool ok = wait_all(&bars[0], 0);
-  const bool t_issued = ok;
   uint32_t mph = 0;
   WKV_TRACE(16)
   if (ok) {
@@ -284,13 +281,7 @@ wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_c
                      false);
       sm100::mma_commit(&bars[1]);
     }
-    // raw tiles and Lambda are dead: S0 and dS rows (rounded) by the threads, T by TMA
-    if (tid == 0) {
-      sm100::mbar_expect_tx(&bars[2], 16 * KB);
-      const int trow = (int)((ch * REC_MATS + REC_T) * N);
-      sm100::tma_load_2d(Tt, &m_t, &bars[2], 0, trow);
-      sm100::tma_load_2d(Tt + 8 * KB, &m_t, &bars[2], 32, trow);
-    }
+    // raw tiles and Lambda are dead: S0 and dS rows (rounded) by the threads
     if (tid < 64) tile_row_from_global(S0t, 64, tid, S0g + tid * N);
     else tile_row_from_global(DSt, 64, tid - 64, wk + WK_DS * MAT + (tid - 64) * N);
     stage = 2;
@@ -300,10 +291,17 @@ wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_c
   }
   if (ok) {
     WKV_TRACE(19)
-    // ---- epilogue 1: M_ak (strict) -> MAK rows; [M_rb^T; M_rk^T] -> MRT (transposed, from rows t >= 64)
+    // ---- epilogue 1: M_ab (strict) -> MPL (plain), M_ak (strict) -> MAK rows; [M_rb^T; M_rk^T] -> MRT
+    //      (transposed, from rows t >= 64)
     float d[64];
     const int t = tid & 63;
     if (tid < 64) {
+      tmem_row64(tmem, warp, 0, d);
+#pragma unroll
+      for (int s = 0; s < 64; s += 4)
+        *reinterpret_cast<float4*>(&MPL[poff(t, s)]) =
+            make_float4(s < t ? d[s] : 0.f, s + 1 < t ? d[s + 1] : 0.f, s + 2 < t ? d[s + 2] : 0.f,
+                        s + 3 < t ? d[s + 3] : 0.f);
       tmem_row64(tmem, warp, 64, d);
 #pragma unroll
       for (int s = 0; s < 64; s += 4)
@@ -333,65 +331,52 @@ wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_c
     }
     stage = 3;
     ok = wait_all(&bars[1], mph);
-    if (ok) {
-      stage = 4;
-      ok = wait_all(&bars[2], 0);
-    }
     mph ^= 1;
     sm100::tc_fence_after();
   }
   if (ok) {
     WKV_TRACE(20)
-    // ---- epilogue 2: Z^T and dU^T (transposed, rows t < 64); T^T and M_ak^T (threads 64..127, from smem/TMEM)
+    // ---- epilogue 2: Zf and dU rows t (threads t < 64) -> columns t of the plain Zf^T, dU^T; M_ak^T
+    float d[64];
     if (tid < 64) {
-      float d[64];
-      tmem_row64(tmem, warp, 128, d);
+      const uint32_t trow = tmem + ((uint32_t)(32 * warp) << 16);
+#pragma unroll 1
+      for (int part = 0; part < 4; ++part) {  // Zf cols 128..191, dU cols 192..255, 32 at a time
+        float e[32];
+        sm100::tmem_ld32(trow + 128 + 32 * part, e);
+        sm100::tmem_wait_ld();
+        float* dst = part < 2 ? ZP : DUP;
 #pragma unroll
-      for (int i = 0; i < 64; ++i) put1(ZFT, 64, i, tid, d[i]);
-      tmem_row64(tmem, warp, 192, d);
-#pragma unroll
-      for (int i = 0; i < 64; ++i) put1(DUT, 64, i, tid, d[i]);
+        for (int i = 0; i < 32; ++i) dst[poff(32 * (part & 1) + i, tid)] = e[i];
+      }
       tmem_row64(tmem, warp, 64, d);  // M_ak row t (still in TMEM) -> M_ak^T column t
 #pragma unroll
       for (int s = 0; s < 64; ++s) put1(MAKT, 64, s, tid, s < tid ? d[s] : 0.f);
-    } else {
-      const int s = tid - 64;  // T^T row s = column s of T
-#pragma unroll 1
-      for (int t0 = 0; t0 < 64; t0 += 4)
-        put4(TTt, 64, s, t0, get1(Tt, 64, t0, s), get1(Tt, 64, t0 + 1, s), get1(Tt, 64, t0 + 2, s),
-             get1(Tt, 64, t0 + 3, s));
     }
-    tc_sync();
+    __syncthreads();
     WKV_TRACE(21)
-    // ---- MMA-U (cols 64..127): U = T Z;  MMA-dZ (cols 0..63): dZ = T^T dU  (64-row operands read as 128 rows)
-    if (tid == 0) {
-      mma_tf32_tiles(tmem + 64, sm100::smem_u32(Tt), 64, sm100::smem_u32(ZFT), 64, 8, sm100::idesc_tf32(128, 64),
-                     false);
-      mma_tf32_tiles(tmem, sm100::smem_u32(TTt), 64, sm100::smem_u32(DUT), 64, 8, sm100::idesc_tf32(128, 64), false);
-      sm100::mma_commit(&bars[1]);
-    }
-    stage = 5;
-    ok = wait_all(&bars[1], mph);
-    mph ^= 1;
-    sm100::tc_fence_after();
-  }
-  if (ok) {
-    WKV_TRACE(22)
-    // ---- epilogue 3: U and dZ rows (tf32) to the work record; dZ^T for dV
-    if (tid < 64) {
-      float d[64];
-      tmem_row64(tmem, warp, 0, d);
-      float* gz = wk + WK_DZ * MAT + tid * N;
+    // ---- U = T Zf (threads i < 64: column i, forward substitution), dZ = T^T dU (threads 64 + i: column i, back
+    //      substitution); U and dZ (tf32) to the work record, dZ columns as rows of dZ^T for dV
+    {
+      const int i = tid & 63;
+      const float* src = tid < 64 ? ZP : DUP;
 #pragma unroll
-      for (int i = 0; i < 64; i += 4)
-        *reinterpret_cast<float4*>(gz + i) = make_float4(tf32r(d[i]), tf32r(d[i + 1]), tf32r(d[i + 2]), tf32r(d[i + 3]));
+      for (int s = 0; s < 64; s += 4) {
+        const float4 z = *reinterpret_cast<const float4*>(&src[poff(i, s)]);
+        d[s] = z.x;
+        d[s + 1] = z.y;
+        d[s + 2] = z.z;
+        d[s + 3] = z.w;
+      }
+      if (tid < 64) solve_lower(MPL, d);
+      else solve_upper_t(MPL, d);
+      float* g = wk + (tid < 64 ? WK_U : WK_DZ) * MAT + i;
 #pragma unroll
-      for (int i = 0; i < 64; ++i) put1(DZT, 64, i, tid, d[i]);
-      tmem_row64(tmem, warp, 64, d);
-      float* gu = wk + WK_U * MAT + tid * N;
+      for (int s = 0; s < 64; ++s) g[s * N] = tf32r(d[s]);
+      if (tid >= 64) {
 #pragma unroll
-      for (int i = 0; i < 64; i += 4)
-        *reinterpret_cast<float4*>(gu + i) = make_float4(tf32r(d[i]), tf32r(d[i + 1]), tf32r(d[i + 2]), tf32r(d[i + 3]));
+        for (int s = 0; s < 64; s += 4) put4(DZT, 64, i, s, d[s], d[s + 1], d[s + 2], d[s + 3]);
+      }
     }
     tc_sync();
     WKV_TRACE(23)
@@ -418,10 +403,7 @@ wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_c
   }
   WKV_TRACE(24)
   if (!ok && tid == 0) atomicCAS(&wkv7_tc_bwd_fault_word, 0, 0x200 | stage);  // state kernel, failing wait
-  if (!ok) {
-    if (stage > 1) sm100::mbar_wait_bounded(&bars[1], mph);
-    if (t_issued && stage != 4) sm100::mbar_wait_bounded(&bars[2], 0);
-  }
+  if (!ok && stage > 1) sm100::mbar_wait_bounded(&bars[1], mph);
   sm100::tc_fence_before();
   __syncthreads();
   if (warp == 0) {
@@ -845,20 +827,19 @@ extern "C" cudaError_t rt_wkv7_tc_backward(int B, int T, int H, const void* r, c
                                            cudaStream_t stream) {
   if (B <= 0 || T <= 0 || H <= 0) return cudaErrorInvalidValue;
   const int chunks = (T + L - 1) / L;
-  CUtensorMap mr, mw, mk, mv, ma, mb, mdy, mt, mwk;
+  CUtensorMap mr, mw, mk, mv, ma, mb, mdy, mwk;
   bool ok = input_map(&mr, r, B, T, H) && input_map(&mw, w, B, T, H) && input_map(&mk, k, B, T, H) &&
             input_map(&mv, v, B, T, H) && input_map(&ma, a, B, T, H) && input_map(&mb, b, B, T, H) &&
             input_map(&mdy, dy, B, T, H);
-  ok = ok && fp32_rows_map(&mt, rec, (long)B * H * chunks * REC_MATS * N) &&
-       fp32_rows_map(&mwk, work, (long)B * H * chunks * WK_MATS * N);
+  ok = ok && fp32_rows_map(&mwk, work, (long)B * H * chunks * WK_MATS * N);
   if (!ok) return cudaErrorInvalidValue;
   RT_CUDA_CHECK(cudaFuncSetAttribute(wkv7_tc_bscan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BSCAN_SMEM));
   wkv7_tc_bscan_kernel<<<dim3(B * H, N / BS_ROWS), 128, BSCAN_SMEM, stream>>>(
       rec, (const __nv_bfloat16*)dy, dend, work, ds0, T, H, chunks);
   RT_CUDA_CHECK(cudaGetLastError());
   RT_CUDA_CHECK(cudaFuncSetAttribute(wkv7_tc_bwd_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ka::SMEM));
-  wkv7_tc_bwd_state_kernel<<<dim3(chunks, H, B), 128, ka::SMEM, stream>>>(mr, mw, mk, mv, ma, mb, mdy, mt, ckpt, work,
-                                                                          dv, T, H, chunks);
+  wkv7_tc_bwd_state_kernel<<<dim3(chunks, H, B), 128, ka::SMEM, stream>>>(mr, mw, mk, mv, ma, mb, mdy, ckpt, work, dv,
+                                                                          T, H, chunks);
   RT_CUDA_CHECK(cudaGetLastError());
   RT_CUDA_CHECK(cudaFuncSetAttribute(wkv7_tc_bwd_grad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kb::SMEM));
   wkv7_tc_bwd_grad_kernel<<<dim3(chunks, H, B), 128, kb::SMEM, stream>>>(

@@ -10,9 +10,10 @@
 //     W = T A~,  U0 = T (M_ak V),  G = diag(D_L) + W^T B^,  H0 = U0^T B^ + V^T K^,
 //     Q = R~ + M_rb W,  Y0 = M_rk V + M_rb U0.
 // Three kernels:
-//   1. wkv7_tc_chunk (grid chunks x H x B, parallel): TMA brings the six raw input tiles; the chunk matrices,
-//      W | U0 and the products for Q, Y0, G, H0 are tf32 MMAs into TMEM; T comes from a blocked 16 x 16
-//      inversion on the CUDA cores. Writes G, H0, Q, Y0 and T (kept for the backward) per chunk.
+//   1. wkv7_tc_chunk (grid chunks x H x B, parallel): TMA brings the six raw input tiles; the chunk matrices, Z,
+//      and the products for Q, Y0, G, H0 are tf32 MMAs into TMEM; W and U0 come from fp32 triangular solves
+//      with I - M_ab on the CUDA cores (one right-hand-side column per thread, in registers; T itself is never
+//      formed). Writes G, H0, Q, Y0 per chunk.
 //   2. wkv7_tc_scan (grid B*H x 8 row blocks): S_{c+1} = S_c G_c + H0_c in fp32 on the CUDA cores, storing the
 //      chunk-start states (checkpoints).
 //   3. wkv7_tc_out (grid chunk pairs x H x B): y = Q S0^T + Y0, one M = 128 MMA per pair of chunks with Q and S0
@@ -46,31 +47,29 @@ __device__ unsigned long long wkv7_trace_ns[64];
 constexpr int KB = 1024;
 constexpr int MAT = N * N;  // floats of one 64 x 64 matrix
 
-// Workspace record per (batch, head, chunk): G, H0, Q, Y0, T (row-major 64 x 64 fp32 each).
-enum { REC_G = 0, REC_H0 = 1, REC_Q = 2, REC_Y0 = 3, REC_T = 4, REC_MATS = 5 };
+// Workspace record per (batch, head, chunk): G, H0, Q, Y0 (row-major 64 x 64 fp32 each).
+enum { REC_G = 0, REC_H0 = 1, REC_Q = 2, REC_Y0 = 3, REC_MATS = 4 };
 
 // Shared-memory map of the chunk kernel (offsets from a 1024-byte aligned base; tiles are K-major SW128).
 // Regions are reused once their last reader is done (noted per line).
-constexpr int OFF_RAW = 0;           // six bf16 64 x 64 tiles r, w, k, v, a, b (8 KB each); w, k, v, b die after
-                                     // the phase-A tiles are built
-constexpr int OFF_TT = 8 * KB;       // T^T (64 rows), over raw w and k
-constexpr int OFF_INV = 40 * KB;     // inversion scratch (7 KB), over raw b
+constexpr int OFF_RAW = 0;           // six bf16 64 x 64 tiles r, w, k, v, a, b (8 KB each)
 constexpr int OFF_LAM = 48 * KB;     // Lambda, plain swizzled 64 x 64 fp32
 constexpr int OFF_MISC = 64 * KB;    // mbarriers, TMEM slot, D_L
-constexpr int OFF_X1 = 65 * KB;      // [A~; R~] (128 rows) -> T in plain form (MPL) -> [W^T; U0^T]
-constexpr int OFF_X2 = 97 * KB;      // [B~; K~] (128 rows) -> [M_ak; M_rk] -> [A~^T; Z^T]
+constexpr int OFF_X1 = 65 * KB;      // [A~; R~] (128 rows) -> [W^T; U0^T]
+constexpr int OFF_X2 = 97 * KB;      // [B~; K~] (128 rows) -> [M_ak; M_rk]
 constexpr int OFF_VT = 129 * KB;     // V^T (64 rows)
 constexpr int OFF_BT = 145 * KB;     // B^T (64 rows)
 constexpr int OFF_KT = 161 * KB;     // K^T (64 rows)
-constexpr int OFF_MRB = 177 * KB;    // M_rb (64 rows; read as the top half of a 128-row operand)
-constexpr int OFF_TP = 193 * KB;     // [T; P] (128 rows), P = M_rb T
+constexpr int OFF_MRB = 177 * KB;    // M_rb (64 rows; read as the lower half of a 128-row operand)
+constexpr int OFF_MPL = 193 * KB;    // M_ab, plain swizzled (the solves read its rows)
+constexpr int OFF_ZT = 209 * KB;     // Z^T, plain swizzled (row i = column i of Z = M_ak V)
 constexpr int CHUNK_SMEM = 225 * KB + 1024;
+constexpr int CHUNK_TMEM = 512;      // [0,128) chunk matrices, then M_rb [W | U0]; [128,192) [W^T; U0^T] B^;
+                                     // [192,256) V^T K^; [256,320) [Z; M_rk V]
 
 __device__ int wkv7_tc_fault_word = 0;
 
-RT_DEVICE uint8_t* align1024(uint8_t* p) {
-  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
-}
+RT_DEVICE uint8_t* align1024(uint8_t* p) { return sm100::align_smem_1024(p); }
 
 // Bounded wait on an MMA/TMA barrier that every thread takes part in; false (uniformly) if it gave up.
 RT_DEVICE bool wait_all(uint64_t* bar, uint32_t parity) {
@@ -98,13 +97,11 @@ wkv7_tc_chunk_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_const
   uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + OFF_MISC + 16);
   float* DL = reinterpret_cast<float*>(sm + OFF_MISC + 64);
   uint8_t *X1 = sm + OFF_X1, *X2 = sm + OFF_X2, *VT = sm + OFF_VT, *BT = sm + OFF_BT, *KT = sm + OFF_KT;
-  uint8_t *MRB = sm + OFF_MRB, *TP = sm + OFF_TP, *TT = sm + OFF_TT;
-  float* MPL = reinterpret_cast<float*>(X1);
+  uint8_t* MRB = sm + OFF_MRB;
+  float* MPL = reinterpret_cast<float*>(sm + OFF_MPL);
+  float* ZT = reinterpret_cast<float*>(sm + OFF_ZT);
   uint8_t* MAK = X2;
-  uint8_t* AZT = X2;
   uint8_t* WUT = X1;
-  float* rtmp = reinterpret_cast<float*>(sm + OFF_INV);
-  float* td = rtmp + 16 * 48;
   float* rec = ws + (((long)bb * H + h) * chunks + c) * (REC_MATS * MAT);
   WKV_TRACE_BEGIN
 
@@ -114,7 +111,7 @@ wkv7_tc_chunk_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_const
     sm100::fence_barrier_init();
   }
   if (warp == 0) {
-    sm100::tmem_alloc(tslot, 256);
+    sm100::tmem_alloc(tslot, CHUNK_TMEM);
     sm100::tmem_relinquish();
   }
   sm100::tc_fence_before();
@@ -243,173 +240,144 @@ wkv7_tc_chunk_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_const
              s + 3 < lim ? d[s + 3] : 0.f);
     }
     tc_sync();
-    // ---- MMA2: [Z; M_rk V] = [M_ak; M_rk] V  (cols 128..191), running during the inversion
+    // ---- MMA2: [Z; M_rk V] = [M_ak; M_rk] V  (cols 256..319)
     if (tid == 0) {
-      mma_tf32_tiles(tmem + 128, sm100::smem_u32(MAK), 128, sm100::smem_u32(VT), 64, 8, sm100::idesc_tf32(128, 64),
+      mma_tf32_tiles(tmem + 256, sm100::smem_u32(MAK), 128, sm100::smem_u32(VT), 64, 8, sm100::idesc_tf32(128, 64),
                      false);
       sm100::mma_commit(&bars[1]);
     }
     WKV_TRACE(5)
-    invert_unit_lower(MPL, rtmp, td, tid);
-    WKV_TRACE(6)
-    // T^T -> TT (row s' = tid < 64); T rows -> TP rows 0..63 and to the record (tf32, an MMA operand later)
-    if (tid < 64) {
-#pragma unroll 1
-      for (int s = 0; s < 64; s += 4)
-        put4(TT, 64, tid, s, MPL[poff(s, tid)], MPL[poff(s + 1, tid)], MPL[poff(s + 2, tid)], MPL[poff(s + 3, tid)]);
-    } else {
-      const int t = tid - 64;
-      float* g = rec + REC_T * MAT + t * 64;
-#pragma unroll 1
-      for (int j = 0; j < 64; j += 4) {
-        const float4 x = *reinterpret_cast<const float4*>(&MPL[poff(t, j)]);
-        put4(TP, 128, t, j, x.x, x.y, x.z, x.w);
-        *reinterpret_cast<float4*>(g + j) = make_float4(tf32r(x.x), tf32r(x.y), tf32r(x.z), tf32r(x.w));
-      }
-    }
-    WKV_TRACE(7)
-    stage = 3;
-    ok = wait_all(&bars[1], mph);  // MMA2 done
-    mph ^= 1;
-    tc_sync();
-    // ---- MMA-P: P = M_rb T  (cols 192..255, lanes 0..63)
-    if (ok && tid == 0) {
-      mma_tf32_tiles(tmem + 192, sm100::smem_u32(MRB), 64, sm100::smem_u32(TT), 64, 8, sm100::idesc_tf32(128, 64),
-                     false);
-      sm100::mma_commit(&bars[1]);
-    }
-    if (ok) {
-      stage = 4;
-      ok = wait_all(&bars[1], mph);
-      mph ^= 1;
-      sm100::tc_fence_after();
-    }
+  }
+  // Right-hand sides of the solves, one column per thread: A~ column j (threads 64 + j, built while MMA2 runs)
+  // and Z column i (threads i < 64, from Z^T after MMA2).
+  float x[64];
+  if (ok && tid >= 64) {
+    const int j = tid - 64;
+#pragma unroll
+    for (int t = 0; t < 64; ++t) x[t] = raw(Ra, t, j);
+#pragma unroll
+    for (int t = 1; t < 64; ++t) x[t] *= expf(lam[poff(t - 1, j)]);
   }
   if (ok) {
-    WKV_TRACE(8)
-    // ---- P rows -> TP rows 64..127; [A~^T; Z^T] -> AZT (B operand of MMA3, N = 128)
-    if (tid < 64) {
-      float d[64];
-      tmem_row64(tmem, warp, 192, d);
-#pragma unroll
-      for (int j = 0; j < 64; j += 4) put4(TP, 128, 64 + tid, j, d[j], d[j + 1], d[j + 2], d[j + 3]);
-      tmem_row64(tmem, warp, 128, d);  // Z row s = tid
-#pragma unroll
-      for (int i = 0; i < 64; ++i) put1(AZT, 128, 64 + i, tid, d[i]);
-    } else {
-      const int j = tid - 64;
-#pragma unroll 1
-      for (int s0 = 0; s0 < 64; s0 += 16) {
-        float x[16], lp[16];
-#pragma unroll
-        for (int q = 0; q < 16; ++q) {
-          x[q] = raw(Ra, s0 + q, j);
-          lp[q] = s0 + q ? lam[poff(s0 + q - 1, j)] : 0.f;
-        }
-#pragma unroll
-        for (int q = 0; q < 16; ++q) x[q] *= expf(lp[q]);
-#pragma unroll
-        for (int q = 0; q < 16; q += 4) put4(AZT, 128, j, s0 + q, x[q], x[q + 1], x[q + 2], x[q + 3]);
-      }
-    }
-    tc_sync();
-    WKV_TRACE(9)
-    // ---- MMA3: [W U0; P A~  P Z] = [T; P] [A~ | Z]  (cols 0..127)
-    if (tid == 0) {
-      mma_tf32_tiles(tmem, sm100::smem_u32(TP), 128, sm100::smem_u32(AZT), 128, 8, sm100::idesc_tf32(128, 128),
-                     false);
-      sm100::mma_commit(&bars[1]);
-    }
-    stage = 5;
-    ok = wait_all(&bars[1], mph);
+    stage = 3;
+    ok = wait_all(&bars[1], mph);  // MMA2 done
     mph ^= 1;
     sm100::tc_fence_after();
   }
   if (ok) {
-    WKV_TRACE(10)
-    // ---- epilogue 3: W, U0 -> [W^T; U0^T] (WUT); Q = R~ + P A~, Y0 = M_rk V + P Z -> record
-    if (tid < 64) {
-      float d[64];
-      tmem_row64(tmem, warp, 0, d);
+    WKV_TRACE(6)
+    if (tid < 64) {  // Z row t -> column t of Z^T
+      const uint32_t zrow = tmem + ((uint32_t)(32 * warp) << 16) + 256;
 #pragma unroll
-      for (int j = 0; j < 64; ++j) put1(WUT, 128, j, tid, d[j]);
-      tmem_row64(tmem, warp, 64, d);
-#pragma unroll
-      for (int i = 0; i < 64; ++i) put1(WUT, 128, 64 + i, tid, d[i]);
-    } else {
-      const int t = tid - 64;
-      const uint32_t row = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
-#pragma unroll 1
       for (int half = 0; half < 2; ++half) {
         float d[32];
-        sm100::tmem_ld32(row + 32 * half, d);
+        sm100::tmem_ld32(zrow + 32 * half, d);
         sm100::tmem_wait_ld();
-        float* gq = rec + REC_Q * MAT + t * 64 + 32 * half;
 #pragma unroll
-        for (int j8 = 0; j8 < 32; j8 += 8) {
-          float x[8];
-          raw8(Rr, t, 32 * half + j8, x);
-          float q[8];
-#pragma unroll
-          for (int u = 0; u < 8; ++u) q[u] = tf32r(x[u] * expf(lam[poff(t, 32 * half + j8 + u)]) + d[j8 + u]);
-          *reinterpret_cast<float4*>(gq + j8) = make_float4(q[0], q[1], q[2], q[3]);
-          *reinterpret_cast<float4*>(gq + j8 + 4) = make_float4(q[4], q[5], q[6], q[7]);
-        }
-        float e[32];
-        sm100::tmem_ld32(row + 64 + 32 * half, d);
-        sm100::tmem_ld32(row + 128 + 32 * half, e);
-        sm100::tmem_wait_ld();
-        float* gy = rec + REC_Y0 * MAT + t * 64 + 32 * half;
-#pragma unroll
-        for (int u = 0; u < 32; u += 4)
-          *reinterpret_cast<float4*>(gy + u) = make_float4(d[u] + e[u], d[u + 1] + e[u + 1], d[u + 2] + e[u + 2],
-                                                           d[u + 3] + e[u + 3]);
+        for (int i = 0; i < 32; ++i) ZT[poff(32 * half + i, tid)] = d[i];
       }
     }
+    __syncthreads();
+    if (tid < 64) {
+#pragma unroll
+      for (int t = 0; t < 64; t += 4) {
+        const float4 z = *reinterpret_cast<const float4*>(&ZT[poff(tid, t)]);
+        x[t] = z.x;
+        x[t + 1] = z.y;
+        x[t + 2] = z.z;
+        x[t + 3] = z.w;
+      }
+    }
+    WKV_TRACE(7)
+    // ---- W = T A~ (threads 64 + j: column j) and U0 = T Z (threads i: column i), T = (I - M_ab)^{-1}; the
+    //      columns become the rows of [W^T; U0^T] (X1's [A~; R~] was last read by MMA1)
+    solve_lower(MPL, x);
+    {
+      const int row = tid < 64 ? 64 + tid : tid - 64;
+#pragma unroll
+      for (int t = 0; t < 64; t += 4) put4(WUT, 128, row, t, x[t], x[t + 1], x[t + 2], x[t + 3]);
+    }
     tc_sync();
-    WKV_TRACE(11)
-    // ---- MMA4: [W^T B^; U0^T B^] (cols 128..191) and [*; V^T K^] (cols 192..255; V^T read as rows 64..127)
+    WKV_TRACE(8)
+    // ---- MMA3: M_rb [W | U0] (cols 0..127, rows 64..127 from M_rb read as the lower half of 128 rows),
+    //      [W^T; U0^T] B^ (cols 128..191), V^T K^ (cols 192..255, rows 64..127 likewise)
     if (tid == 0) {
+      mma_tf32_tiles(tmem, sm100::smem_u32(MRB) - 8192, 64, sm100::smem_u32(WUT), 128, 8,
+                     sm100::idesc_tf32(128, 128), false);
       mma_tf32_tiles(tmem + 128, sm100::smem_u32(WUT), 128, sm100::smem_u32(BT), 64, 8, sm100::idesc_tf32(128, 64),
                      false);
       mma_tf32_tiles(tmem + 192, sm100::smem_u32(VT) - 8192, 64, sm100::smem_u32(KT), 64, 8,
                      sm100::idesc_tf32(128, 64), false);
       sm100::mma_commit(&bars[1]);
     }
-    stage = 6;
+    stage = 4;
     ok = wait_all(&bars[1], mph);
     mph ^= 1;
     sm100::tc_fence_after();
   }
   if (ok) {
-    WKV_TRACE(12)
-    // ---- epilogue 4: G = diag(D_L) + W^T B^ (rows j), H0 = U0^T B^ + V^T K^ (rows i)
+    WKV_TRACE(9)
     const uint32_t row = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
-    const int r = tid & 63;
+    if (tid < 64) {  // G = diag(D_L) + W^T B^ (row j = tid)
+      const int r = tid;
 #pragma unroll 1
-    for (int half = 0; half < 2; ++half) {
-      float d[32], e[32];
-      sm100::tmem_ld32(row + 128 + 32 * half, d);
-      if (tid >= 64) sm100::tmem_ld32(row + 192 + 32 * half, e);
-      sm100::tmem_wait_ld();
-      float* g = rec + (tid < 64 ? REC_G : REC_H0) * MAT + r * 64 + 32 * half;
+      for (int half = 0; half < 2; ++half) {
+        float d[32];
+        sm100::tmem_ld32(row + 128 + 32 * half, d);
+        sm100::tmem_wait_ld();
+        float* g = rec + REC_G * MAT + r * 64 + 32 * half;
 #pragma unroll
-      for (int u = 0; u < 32; ++u) {
-        const int col = 32 * half + u;
-        d[u] += tid < 64 ? (col == r ? DL[r] : 0.f) : e[u];
+        for (int u = 0; u < 32; ++u) d[u] += 32 * half + u == r ? DL[r] : 0.f;
+#pragma unroll
+        for (int u = 0; u < 32; u += 4) *reinterpret_cast<float4*>(g + u) = make_float4(d[u], d[u + 1], d[u + 2], d[u + 3]);
       }
+    } else {  // row t = tid - 64: Q = R~ + M_rb W (tf32: an MMA operand later), Y0 = M_rk V + M_rb U0,
+              // H0 = U0^T B^ + V^T K^ (row i = t)
+      const int t = tid - 64;
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {
+        float d[32], e[32];
+        sm100::tmem_ld32(row + 32 * half, d);
+        sm100::tmem_wait_ld();
+        float* gq = rec + REC_Q * MAT + t * 64 + 32 * half;
 #pragma unroll
-      for (int u = 0; u < 32; u += 4) *reinterpret_cast<float4*>(g + u) = make_float4(d[u], d[u + 1], d[u + 2], d[u + 3]);
+        for (int j8 = 0; j8 < 32; j8 += 8) {
+          float xr[8], lt[8], q[8];
+          raw8(Rr, t, 32 * half + j8, xr);
+          *reinterpret_cast<float4*>(lt) = *reinterpret_cast<const float4*>(&lam[poff(t, 32 * half + j8)]);
+          *reinterpret_cast<float4*>(lt + 4) = *reinterpret_cast<const float4*>(&lam[poff(t, 32 * half + j8 + 4)]);
+#pragma unroll
+          for (int u = 0; u < 8; ++u) q[u] = tf32r(xr[u] * expf(lt[u]) + d[j8 + u]);
+          *reinterpret_cast<float4*>(gq + j8) = make_float4(q[0], q[1], q[2], q[3]);
+          *reinterpret_cast<float4*>(gq + j8 + 4) = make_float4(q[4], q[5], q[6], q[7]);
+        }
+        sm100::tmem_ld32(row + 64 + 32 * half, d);
+        sm100::tmem_ld32(row + 256 + 32 * half, e);
+        sm100::tmem_wait_ld();
+        float* gy = rec + REC_Y0 * MAT + t * 64 + 32 * half;
+#pragma unroll
+        for (int u = 0; u < 32; u += 4)
+          *reinterpret_cast<float4*>(gy + u) = make_float4(d[u] + e[u], d[u + 1] + e[u + 1], d[u + 2] + e[u + 2],
+                                                           d[u + 3] + e[u + 3]);
+        sm100::tmem_ld32(row + 128 + 32 * half, d);
+        sm100::tmem_ld32(row + 192 + 32 * half, e);
+        sm100::tmem_wait_ld();
+        float* gh = rec + REC_H0 * MAT + t * 64 + 32 * half;
+#pragma unroll
+        for (int u = 0; u < 32; u += 4)
+          *reinterpret_cast<float4*>(gh + u) = make_float4(d[u] + e[u], d[u + 1] + e[u + 1], d[u + 2] + e[u + 2],
+                                                           d[u + 3] + e[u + 3]);
+      }
     }
   }
-  WKV_TRACE(13)
+  WKV_TRACE(10)
   if (!ok && tid == 0) atomicCAS(&wkv7_tc_fault_word, 0, 0x100 | stage);  // kernel 1, failing wait
   if (!ok && stage > 1) sm100::mbar_wait_bounded(&bars[1], mph);  // an MMA may still be in flight
   sm100::tc_fence_before();
   __syncthreads();
   if (warp == 0) {
     sm100::tc_fence_after();
-    sm100::tmem_dealloc(tmem, 256);
+    sm100::tmem_dealloc(tmem, CHUNK_TMEM);
   }
 }
 
@@ -560,7 +528,7 @@ bool fp32_rows_map(CUtensorMap* m, const float* base, long rows) {
 
 }  // namespace
 
-// Floats of the per-chunk record workspace (G, H0, Q, Y0, T per chunk and head). The backward reads G, Q, T.
+// Floats of the per-chunk record workspace (G, H0, Q, Y0 per chunk and head). The backward reads G and Q.
 #ifdef WKV7_TC_TRACE
 extern "C" void rt_wkv7_tc_fwd_trace(unsigned long long* out, int reset) {
   cudaMemcpyFromSymbol(out, wkv7_trace_ns, sizeof(unsigned long long) * 64);
