@@ -3,6 +3,9 @@
 // dtype and device checks, allocates outputs, and launches on the current
 // stream of the tensors' device.
 #include <torch/extension.h>
+
+#include <map>
+#include <string>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <vector>
@@ -534,6 +537,153 @@ at::Tensor flash_attention(at::Tensor q, at::Tensor keys, at::Tensor values, at:
   return out;
 }
 
+// Native executor of one fused TimeMix student micro-step (reference theseus/timemix.py:66-89 forward, with the
+// hand-written backward): mix, the r/k/v and LoRA GEMMs, pre-WKV, WKV7, post-WKV, the output GEMM with the loss in
+// its epilogue, and the backward of all of it, issued from C++ on the current stream (about 40 launches; the Python
+// sequence of the same calls cost milliseconds of host time per micro-step). Weights are bf16 views, the small
+// parameter vectors fp32 views, gradients views into the flat fp32 gradient buffer; all of them stay valid for the
+// life of the student (the flat buffers are never reallocated).
+class StudentStep {
+ public:
+  StudentStep(std::map<std::string, at::Tensor> w, std::map<std::string, at::Tensor> p,
+              std::map<std::string, at::Tensor> g, c10::optional<at::Tensor> grad_tail, int64_t H, int64_t N)
+      : W_(std::move(w)), P_(std::move(p)), G_(std::move(g)), tail_(grad_tail), H_(H), N_(N) {
+    for (const char* n : {"receptance", "key", "value", "output", "w1", "w2", "a1", "a2", "g1", "g2"})
+      need(W_.count(n) && W_.at(n).scalar_type() == at::kBFloat16, "StudentStep: missing bf16 weight");
+    for (const char* n : {"coef", "w0", "a0", "k_k", "k_a", "r_k", "ln_w", "ln_b"})
+      need(P_.count(n) && P_.at(n).scalar_type() == at::kFloat && P_.at(n).is_contiguous(),
+           "StudentStep: missing fp32 parameter vector");
+  }
+
+  // Inference forward: (prediction [B, T, C] bf16, new shift [B, C], end state [B, H, N, N]).
+  std::vector<at::Tensor> forward(at::Tensor x, c10::optional<at::Tensor> shift, c10::optional<at::Tensor> wkv0) {
+    c10::cuda::CUDAGuard guard(x.device());
+    Saved s = run_forward(x, shift, wkv0, false);
+    auto pred = mm(s.yg, W_.at("output"), false);
+    return {pred.view(x.sizes()), s.x.select(1, s.x.size(1) - 1).clone(), s.end};
+  }
+
+  // Training micro-step: stats (fp32 [3]) += [sum nmse, sum cos, tokens]; gradients stored (first) or accumulated
+  // into the flat buffer. Returns (new shift, end state).
+  std::vector<at::Tensor> forward_backward(at::Tensor x, at::Tensor target, c10::optional<at::Tensor> shift,
+                                           c10::optional<at::Tensor> wkv0, double eps, bool first, at::Tensor stats) {
+    need(!G_.empty(), "StudentStep: built without gradient buffers");
+    c10::cuda::CUDAGuard guard(x.device());
+    const int64_t B = x.size(0), T = x.size(1), C = x.size(2), M = B * T, H = H_, N = N_;
+    if (first && tail_.has_value()) tail_->zero_();
+    Saved s = run_forward(x, shift, wkv0, true);
+    auto dpred = gemm_nmse(s.yg, W_.at("output"), target.reshape({M, C}).to(at::kBFloat16).contiguous(), stats, eps);
+    // output projection
+    auto dyg = mm(dpred, W_.at("output"), true);
+    grad(dpred, true, s.yg, true, "output", first);
+    // post-WKV backward
+    auto dy = at::empty_like(dpred), dg = at::empty_like(dpred);
+    auto f32 = dpred.options().dtype(at::kFloat);
+    std::vector<at::Tensor> bonus = {at::empty({M, C}, f32), at::empty({M, C}, f32), at::empty({M, C}, f32)};
+    tm_post_wkv_bwd(dyg, s.y, s.r, s.k_in, s.v, s.g, P_.at("ln_w"), P_.at("ln_b"), P_.at("r_k"), s.gn, dy, dg,
+                    bonus[0], bonus[1], bonus[2], G_.at("ln_w"), G_.at("ln_b"), G_.at("r_k"), H, N);
+    const std::vector<int64_t> shape = {B, T, H, N};
+    auto dend = at::zeros({B, H, N, N}, f32);
+    auto gw = wkv7_backward(s.r.view(shape), s.w_in.view(shape), s.k_in.view(shape), s.v.view(shape),
+                            s.a_in.view(shape), s.b_in.view(shape), s.ckpt, s.rec, dy.view(shape), dend);
+    std::vector<at::Tensor> d5;
+    for (int i = 0; i < 5; ++i) d5.push_back(at::empty_like(dpred));  // dr, dk, dv, dlw, dla
+    tm_pre_wkv_bwd({gw[0], gw[1], gw[2], gw[3], gw[4], gw[5]}, bonus, s.k, s.la, P_.at("w0"), P_.at("a0"),
+                   P_.at("k_k"), P_.at("k_a"), d5, {G_.at("w0"), G_.at("a0"), G_.at("k_k"), G_.at("k_a")}, H, N);
+    gw.clear();
+    bonus.clear();
+    auto dmix = at::empty_like(s.mix);
+    auto xm = [&](int i) { return s.mix.select(0, i); };  // xr, xw, xk, xv, xa, xg
+    // r, k, v projections
+    const std::pair<int, const char*> proj[3] = {{0, "receptance"}, {2, "key"}, {3, "value"}};
+    const at::Tensor* douts[3] = {&d5[0], &d5[1], &d5[2]};
+    for (int i = 0; i < 3; ++i) {
+      gemm(*douts[i], false, W_.at(proj[i].second), true, 0, 1.0, dmix.select(0, proj[i].first), 0);
+      grad(*douts[i], true, xm(proj[i].first), true, proj[i].second, first);
+    }
+    // decay LoRA: lw = tanh(xw w1) w2
+    acc(s.hw, d5[3], "w2");
+    auto dhw = mm(d5[3], W_.at("w2"), false);
+    act_bwd_(s.hw, dhw, 0);
+    acc(xm(1), dhw, "w1");
+    gemm(dhw, false, W_.at("w1"), false, 0, 1.0, dmix.select(0, 1), 0);
+    // in-context-rate LoRA: la = (xa a1) a2
+    acc(s.ha, d5[4], "a2");
+    auto dha = mm(d5[4], W_.at("a2"), false);
+    acc(xm(4), dha, "a1");
+    gemm(dha, false, W_.at("a1"), false, 0, 1.0, dmix.select(0, 4), 0);
+    // gate LoRA: g = sigmoid(xg g1) g2
+    acc(s.hg, dg, "g2");
+    auto dhg = mm(dg, W_.at("g2"), false);
+    act_bwd_(s.hg, dhg, 1);
+    acc(xm(5), dhg, "g1");
+    gemm(dhg, false, W_.at("g1"), false, 0, 1.0, dmix.select(0, 5), 0);
+    tm_mix_bwd(s.x, s.shift, dmix, G_.at("coef"));
+    return {s.x.select(1, T - 1).clone(), s.end};
+  }
+
+ private:
+  struct Saved {
+    at::Tensor x, shift, mix, r, k, v, hw, ha, hg, lw, la, g, w_in, k_in, a_in, b_in, y, ckpt, rec, yg, gn, end;
+  };
+
+  static at::Tensor mm(const at::Tensor& a, const at::Tensor& b, bool b_t) {
+    return gemm(a, false, b, b_t, 0, 1.0, c10::nullopt, 0);
+  }
+  // Gradient of a big matrix: stored on the first micro-step of an update, accumulated after.
+  void grad(const at::Tensor& a, bool a_t, const at::Tensor& b, bool b_t, const char* name, bool first) {
+    gemm(a, a_t, b, b_t, first ? 1 : 2, 1.0, G_.at(name), 0);
+  }
+  // LoRA gradient: always accumulated (the tail of the flat buffer was cleared on the first micro-step).
+  void acc(const at::Tensor& a, const at::Tensor& b, const char* name) {
+    gemm(a, true, b, true, 2, 1.0, G_.at(name), 0);
+  }
+
+  Saved run_forward(at::Tensor x_in, c10::optional<at::Tensor> shift, c10::optional<at::Tensor> wkv0, bool keep) {
+    Saved s;
+    const int64_t B = x_in.size(0), T = x_in.size(1), C = x_in.size(2), M = B * T, H = H_, N = N_;
+    s.x = x_in.to(at::kBFloat16).contiguous();
+    s.shift = shift.has_value() ? shift->to(at::kBFloat16).contiguous() : at::zeros({B, C}, s.x.options());
+    auto state = wkv0.has_value() ? wkv0->to(at::kFloat).contiguous()
+                                  : at::zeros({B, H, N, N}, s.x.options().dtype(at::kFloat));
+    s.mix = at::empty({6, M, C}, s.x.options());
+    tm_mix(s.x, s.shift, P_.at("coef"), s.mix);
+    auto xm = [&](int i) { return s.mix.select(0, i); };
+    s.r = mm(xm(0), W_.at("receptance"), false);
+    s.k = mm(xm(2), W_.at("key"), false);
+    s.v = mm(xm(3), W_.at("value"), false);
+    s.hw = mm(xm(1), W_.at("w1"), true);
+    act_(s.hw, 0);
+    s.lw = mm(s.hw, W_.at("w2"), true);
+    s.ha = mm(xm(4), W_.at("a1"), true);
+    s.la = mm(s.ha, W_.at("a2"), true);
+    s.hg = mm(xm(5), W_.at("g1"), true);
+    act_(s.hg, 1);
+    s.g = mm(s.hg, W_.at("g2"), true);
+    s.w_in = at::empty_like(s.r);
+    s.k_in = at::empty_like(s.r);
+    s.a_in = at::empty_like(s.r);
+    s.b_in = at::empty_like(s.r);
+    tm_pre_wkv(s.k, s.lw, s.la, P_.at("w0"), P_.at("a0"), P_.at("k_k"), P_.at("k_a"), s.w_in, s.k_in, s.a_in, s.b_in,
+               H, N);
+    const std::vector<int64_t> shape = {B, T, H, N};
+    auto out = wkv7_forward(s.r.view(shape), s.w_in.view(shape), s.k_in.view(shape), s.v.view(shape),
+                            s.a_in.view(shape), s.b_in.view(shape), state, keep);
+    s.y = out[0];
+    s.end = out[1];
+    s.ckpt = out[2];
+    s.rec = out[3];
+    s.yg = at::empty_like(s.r);
+    s.gn = at::empty({M * H * 3}, s.x.options().dtype(at::kFloat));
+    tm_post_wkv(s.y, s.r, s.k_in, s.v, s.g, P_.at("ln_w"), P_.at("ln_b"), P_.at("r_k"), s.yg, s.gn, H, N);
+    return s;
+  }
+
+  std::map<std::string, at::Tensor> W_, P_, G_;
+  c10::optional<at::Tensor> tail_;
+  int64_t H_, N_;
+};
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -589,6 +739,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         check_cuda(rt_wkv7_tc_bwd_fault_async(p + 2, s), "wkv7 backward fault word");
       },
       "enqueue on the current stream: copy the GEMM / WKV7 fault words into `out` (pinned) and clear them");
+  py::class_<StudentStep>(m, "StudentStep")
+      .def(py::init<std::map<std::string, at::Tensor>, std::map<std::string, at::Tensor>,
+                    std::map<std::string, at::Tensor>, c10::optional<at::Tensor>, int64_t, int64_t>(),
+           py::arg("weights"), py::arg("params"), py::arg("grads"), py::arg("grad_tail"), py::arg("H"), py::arg("N"))
+      .def("forward", &StudentStep::forward, py::arg("x"), py::arg("shift"), py::arg("wkv0"))
+      .def("forward_backward", &StudentStep::forward_backward, py::arg("x"), py::arg("target"), py::arg("shift"),
+           py::arg("wkv0"), py::arg("eps"), py::arg("first"), py::arg("stats"));
   m.def("wkv7_tc_enable", [](bool on) { g_wkv7_tc_enabled = on; },
         "route bf16 head-64 calls of >= 128 steps to the tcgen05 kernels (default) or to the chunk-16 kernels");
 }

@@ -260,7 +260,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
             const __grid_constant__ CUtensorMap tb1, const GemmArgs args) {
   using C_ = Cfg<BN, A_MN, B_MN, EPI>;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem = sm100::align_smem_1024(smem_raw);
   constexpr int ST = C_::ST;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + ST * C_::STAGE_BYTES);
   uint64_t* full = bars;
@@ -771,18 +771,24 @@ int measured_bn(const TileKey& key, int M, int K, const void* A, long lda, const
     // A shorter chunk of a measured GEMM: same N and layouts, fewer token rows (K-major A: M is the token count)
     // or a shallower K (MN-major A, weight gradients: K is the token count), at most 8x smaller. Reuse the choice
     // of the nearest larger measured bucket instead of timing again in the middle of training.
+    // Further than 8x from every measured bucket of the shape, the wave-fill estimate is used (still no timing).
     int best = -1;
     long best_size = 0;
+    bool larger_known = false;
     for (const auto& [k, choice] : tile_cache()) {
       if (k.N != key.N || k.a_mn != key.a_mn || k.b_mn != key.b_mn) continue;
-      const bool rows = !key.a_mn && k.K == key.K && k.M > key.M && k.M <= 8 * key.M;
-      const bool depth = key.a_mn && k.M == key.M && k.K > key.K && k.K <= 8 * key.K;
+      const bool rows_any = !key.a_mn && k.K == key.K && k.M > key.M;
+      const bool depth_any = key.a_mn && k.M == key.M && k.K > key.K;
+      larger_known = larger_known || rows_any || depth_any;
+      const bool rows = rows_any && k.M <= 8 * key.M;
+      const bool depth = depth_any && k.K <= 8 * key.K;
       const long size = (long)k.M * k.K;
       if ((rows || depth) && (best < 0 || size < best_size)) {
         best = choice;
         best_size = size;
       }
     }
+    if (best < 0 && larger_known) best = pick_bn(key.M, key.N, false, key.b_mn != 0);
     if (best >= 0) {
       tile_cache()[key] = best;
       return best;

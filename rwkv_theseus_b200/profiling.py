@@ -41,7 +41,8 @@ class StepProfiler:
             start.record()
             t0 = time.perf_counter()
             try:
-                yield
+                with torch.profiler.record_function("phase:" + name):  # kernel attribution under torch.profiler
+                    yield
             finally:
                 self.host[name] = self.host.get(name, 0.0) + time.perf_counter() - t0
                 end.record()
