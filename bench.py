@@ -11,7 +11,10 @@ shard (weak scaling).
 
 A step is one optimizer update of all sixteen layers on one chunk: one
 teacher forward, sixteen student forward/backward passes, sixteen gradient
-reductions (world > 1) and sixteen clip+AdamW updates.
+reductions (world > 1) and sixteen clip+AdamW updates. The engine issues a
+step's updates at the start of the next step (they run under its teacher
+forward); the timed region starts after the warm-up's updates are issued and
+ends after the K-th step's updates, so it holds exactly K steps of work.
 
 Timing: W untimed warm-up steps, then K steps bracketed by a barrier and
 device synchronisation, timed with CUDA events; the reported number is the
@@ -189,18 +192,23 @@ def build_ours(args, topo, manifest, model_spec):
 
     def phases():
         """Milliseconds per phase kind of one extra, untimed step: device time between CUDA events on the compute
-        stream (updates: the enqueue on that stream; the optimizer and exchange kernels run on a side stream) and
-        host time spent issuing the phase, plus the whole step's device time."""
+        stream (updates: the enqueue on that stream of the previous step's updates, which run on a side stream
+        under the teacher phase) and host time spent issuing the phase, plus the whole step's device time."""
         engine.profiler.on = True
         start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        try:
+        try:  # a steady-state step: the previous step's updates are issued under its teacher forward
             start.record()
-            engine.step(reader)
+            reports = engine.step(reader)
             stop.record()
             dev, host = engine.profiler.summary(), engine.profiler.host_summary()
             stop.synchronize()
+            engine.read_metrics(reports)  # the phase step is validated like every other (faults, exchange status)
         finally:
             engine.profiler.on = False
+        if topo.world > 1:  # every rank's split, for skew between ranks
+            print(json.dumps({"rank": topo.rank, "phases_dev_ms": {k: round(v, 3) for k, v in dev.items()},
+                              "phases_host_ms": {k: round(v, 3) for k, v in host.items()}}), file=sys.stderr,
+                  flush=True)
         out = {"step_ms": start.elapsed_time(stop)}
         for key, prefix in (("teacher", "teacher"), ("students", "student_"), ("updates", "update_")):
             out[f"{key}_ms"] = sum(v for k, v in dev.items() if k.startswith(prefix))
@@ -224,6 +232,7 @@ def build_ours(args, topo, manifest, model_spec):
     def profiled(on):
         engine.profiler.on = on
     step.finish = finish
+    step.flush_updates = engine.flush  # issue the last step's deferred per-layer updates
     step.phases = phases
     step.snapshot, step.restore = snapshot, restore
     step.set_overlap, step.profiled = set_overlap, profiled
@@ -231,10 +240,27 @@ def build_ours(args, topo, manifest, model_spec):
 
 
 # ---------------------------------------------------------------------------- reference implementation
+def reference_teacher(model_spec, device):
+    """Random-init HF ``Qwen3_5ForCausalLM`` of the spec (bf16, frozen, sdpa attention): the teacher the unmodified
+    reference package runs on (as its own tests construct it; the reference's ``load_model`` needs a checkpoint)."""
+    import torch
+    from transformers import Qwen3_5TextConfig, Qwen3_5ForCausalLM
+    spec = dict(model_spec)
+    theta, partial = spec.pop("rope_theta"), spec.pop("partial_rotary_factor")
+    tcfg = Qwen3_5TextConfig(**spec, layer_types=layer_types(spec["num_hidden_layers"]),
+                             rope_parameters={"rope_type": "default", "rope_theta": theta,
+                                              "partial_rotary_factor": partial, "mrope_section": [11, 11, 10]})
+    tcfg._attn_implementation = "sdpa"
+    torch.set_default_dtype(torch.bfloat16)
+    with torch.device(device):
+        model = Qwen3_5ForCausalLM(tcfg)
+    torch.set_default_dtype(torch.float32)
+    return model.requires_grad_(False).eval()
+
+
 def build_reference(args, topo_unused, manifest, model_spec):
     sys.path.insert(0, str(ROOT / "baseline" / "_ref"))
     import torch
-    from transformers import Qwen3_5TextConfig, Qwen3_5ForCausalLM
     from theseus.config import DEFAULTS
     from theseus.distributed import Topology
     from theseus.hf_model import Capture, Runner, migration_order
@@ -242,18 +268,9 @@ def build_reference(args, topo_unused, manifest, model_spec):
     from theseus.stage import prepare_student
     from theseus.timemix import detach_state
     from theseus.validation import reader_for
-    spec = dict(model_spec)
-    theta, partial = spec.pop("rope_theta"), spec.pop("partial_rotary_factor")
-    tcfg = Qwen3_5TextConfig(**spec, layer_types=layer_types(spec["num_hidden_layers"]),
-                             rope_parameters={"rope_type": "default", "rope_theta": theta,
-                                              "partial_rotary_factor": partial, "mrope_section": [11, 11, 10]})
-    tcfg._attn_implementation = "sdpa"
     topo = Topology("nccl", 30)
-    torch.set_default_dtype(torch.bfloat16)
-    with torch.device(topo.device):
-        model = Qwen3_5ForCausalLM(tcfg)
-    torch.set_default_dtype(torch.float32)
-    model.requires_grad_(False).eval()
+    model = reference_teacher(model_spec, topo.device)
+    tcfg = model.config
     order = migration_order(model, len([t for t in tcfg.layer_types if t == "full_attention"]))
     cfg = DEFAULTS | {"train_manifest": str(manifest), "validation_manifest": str(manifest), "head_size": 64,
                       "chunk_tokens": args.chunk, "context_tokens": args.context,
@@ -309,14 +326,18 @@ def build_reference(args, topo_unused, manifest, model_spec):
 
 
 # ---------------------------------------------------------------------------- driver
+# Name fragments of this package's kernels (csrc/); everything else in a trace is a library or ATen kernel.
+OWN_KERNELS = ("wkv7_", "gemm_kernel", "rmsnorm_", "conv1d_silu", "gdn_", "mix_kernel", "mix_bwd", "pre_wkv",
+               "post_wkv", "nmse_loss", "adamw_kernel", "scale_norm", "act_kernel", "act_bwd", "norm_rope",
+               "copy_rows", "to_bf16", "report_kernel", "gated_rmsnorm", "flash_attn", "exchange_", "loss_rows",
+               "norm2_kernel", "skinny_", "kl_", "zero_f32")
+
+
 def count_launches(step_fn):
     """Kernels launched by one step, split into this package's kernels and others (profiled, untimed)."""
     import torch
     from torch.profiler import ProfilerActivity, profile
-    mine = ("wkv7_", "gemm_kernel", "rmsnorm_", "conv1d_silu", "gdn_", "mix_kernel", "mix_bwd", "pre_wkv",
-            "post_wkv", "nmse_loss", "adamw_kernel", "scale_norm", "act_kernel", "act_bwd", "norm_rope",
-            "copy_rows", "to_bf16", "report_kernel", "gated_rmsnorm", "flash_attn", "exchange_", "loss_rows",
-            "norm2_kernel", "skinny_", "kl_")
+    mine = OWN_KERNELS
     with profile(activities=[ProfilerActivity.CUDA]) as prof:
         step_fn(False)
         torch.cuda.synchronize()
@@ -366,7 +387,7 @@ def print_breakdown(step_fn, rank):
     if hasattr(step_fn, "profiled"):
         step_fn.profiled(True)
     with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA]) as prof:
-        step_fn(False)
+        step_fn(False)  # steady state: the previous step's updates run under this step's teacher forward
         torch.cuda.synchronize()
     if hasattr(step_fn, "profiled"):
         step_fn.profiled(False)
@@ -417,6 +438,17 @@ def print_phase_kernels(prof):
         print(f"phase {phase}: {sum(kinds.values()) / 1e6:.3f} ms of kernels")
         for group, ns in sorted(kinds.items(), key=lambda kv: -kv[1])[:12]:
             print(f"    {ns / 1e6:8.3f} ms  {group[:80]}")
+        foreign = {}
+        for e in events:
+            if e.device_type() != cuda or e.duration_ns() <= 0 or any(k in e.name() for k in OWN_KERNELS):
+                continue
+            at = launch_at.get(e.correlation_id())
+            inside = [r for r in ranges if at is not None and r[0] <= at <= r[1]]
+            name = min(inside, key=lambda r: r[1] - r[0])[2].split("_")[0] if inside else "other"
+            if name == phase and not e.name().startswith("phase:"):
+                foreign[e.name()[:90]] = foreign.get(e.name()[:90], 0) + 1
+        for name, n in sorted(foreign.items(), key=lambda kv: -kv[1])[:8]:
+            print(f"    library/ATen x{n}: {name}")
 
 
 def print_timeline(prof):
@@ -499,6 +531,8 @@ def main():
     time.sleep(2.0)
     for _ in range(args.warmup):
         step(False)
+    if hasattr(step, "flush_updates"):
+        step.flush_updates()  # the last warm-up step's updates stay outside the timed region
     snap = step.snapshot() if hasattr(step, "snapshot") else None
     barrier()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -507,6 +541,8 @@ def main():
     tokens = 0
     for _ in range(args.steps):
         tokens += step(False)
+    if hasattr(step, "flush_updates"):
+        step.flush_updates()  # the K-th step's updates are inside the timed region
     stop.record()
     barrier()
     clocks = sampler.stop()

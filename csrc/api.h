@@ -104,9 +104,11 @@ cudaError_t rt_act(void* x, long n, int mode, cudaStream_t s);
 cudaError_t rt_act_bwd(const void* h, void* dh, long n, int mode, cudaStream_t s);
 cudaError_t rt_nmse_loss(const void* pred, const void* target, float* stats, void* dpred, long rows, int C, float eps,
                          cudaStream_t s);
+int rt_flat_adamw_scratch();
 cudaError_t rt_flat_adamw(float* p, float* g, float* m, float* v, void* shadow, long n, long decay_numel,
-                          const float* stats, float* norm2, float* report, float lr, float beta1, float beta2,
+                          float* stats, float* scratch, float* report, float lr, float beta1, float beta2,
                           float eps, float weight_decay, float clip, int step, cudaStream_t s);
+cudaError_t rt_zero_f32(float* p, long n, cudaStream_t s);
 cudaError_t rt_to_bf16(const float* src, void* dst, long n, cudaStream_t s);
 
 // Flash attention forward (head_dim 256, GQA, causal with cache offset, fused sigmoid gate).

@@ -100,9 +100,11 @@ std::vector<at::Tensor> wkv7_backward(at::Tensor r, at::Tensor w, at::Tensor k, 
   TORCH_CHECK(ckpt.device() == r.device() && ckpt.scalar_type() == at::kFloat && ckpt.is_contiguous() &&
                   ckpt.sizes() == at::IntArrayRef({B, H, chunks + 1, N, N}),
               "invalid chunk checkpoints");
-  TORCH_CHECK(dend.device() == r.device() && dend.scalar_type() == at::kFloat && dend.is_contiguous() &&
-                  dend.sizes() == at::IntArrayRef({B, H, N, N}),
+  // An undefined dend stands for a zero end-state gradient (the kernels then read none).
+  TORCH_CHECK(!dend.defined() || (dend.device() == r.device() && dend.scalar_type() == at::kFloat &&
+                                  dend.is_contiguous() && dend.sizes() == at::IntArrayRef({B, H, N, N})),
               "invalid dend");
+  const float* dend_ptr = dend.defined() ? dend.data_ptr<float>() : nullptr;
   auto opts = r.options().dtype(at::kFloat);
   std::vector<at::Tensor> g;
   for (int i = 0; i < 6; ++i) g.push_back(at::empty(r.sizes(), opts));
@@ -114,7 +116,7 @@ std::vector<at::Tensor> wkv7_backward(at::Tensor r, at::Tensor w, at::Tensor k, 
     auto work = at::empty({rt_wkv7_tc_backward_workspace_floats(B, T, H)}, opts);
     check_cuda(rt_wkv7_tc_backward(B, T, H, r.data_ptr(), w.data_ptr(), k.data_ptr(), v.data_ptr(), a.data_ptr(),
                                    b.data_ptr(), ckpt.data_ptr<float>(), rec.data_ptr<float>(), dy.data_ptr(),
-                                   dend.data_ptr<float>(), g[0].data_ptr<float>(), g[1].data_ptr<float>(),
+                                   dend_ptr, g[0].data_ptr<float>(), g[1].data_ptr<float>(),
                                    g[2].data_ptr<float>(), g[3].data_ptr<float>(), g[4].data_ptr<float>(),
                                    g[5].data_ptr<float>(), g[6].data_ptr<float>(), work.data_ptr<float>(),
                                    stream_of(r)),
@@ -124,7 +126,7 @@ std::vector<at::Tensor> wkv7_backward(at::Tensor r, at::Tensor w, at::Tensor k, 
   auto work = at::empty({rt_wkv7_backward_workspace_floats(B, T, H, N)}, opts);
   check_cuda(rt_wkv7_backward(dtype_code(r), B, T, H, N, r.data_ptr(), w.data_ptr(), k.data_ptr(), v.data_ptr(),
                               a.data_ptr(), b.data_ptr(), ckpt.data_ptr<float>(), dy.data_ptr(),
-                              dend.data_ptr<float>(), g[0].data_ptr<float>(), g[1].data_ptr<float>(),
+                              dend_ptr, g[0].data_ptr<float>(), g[1].data_ptr<float>(),
                               g[2].data_ptr<float>(), g[3].data_ptr<float>(), g[4].data_ptr<float>(),
                               g[5].data_ptr<float>(), g[6].data_ptr<float>(), work.data_ptr<float>(), stream_of(r)),
              "wkv7_backward");
@@ -453,6 +455,8 @@ void flat_adamw(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, c10::opt
                 int64_t decay_numel, at::Tensor stats, at::Tensor norm2, at::Tensor report, double lr, double beta1,
                 double beta2, double eps, double wd, double clip, int64_t step) {
   need(p.numel() == g.numel() && p.numel() == m.numel() && p.numel() == v.numel(), "flat buffer sizes");
+  need(norm2.scalar_type() == at::kFloat && norm2.numel() >= rt_flat_adamw_scratch(),
+       "flat_adamw scratch needs flat_adamw_scratch() fp32 words");
   c10::cuda::CUDAGuard guard(p.device());
   check_cuda(rt_flat_adamw(FPTR(p), FPTR(g), FPTR(m), FPTR(v), shadow ? PTR(*shadow) : nullptr, p.numel(), decay_numel,
                            FPTR(stats), FPTR(norm2), FPTR(report), lr, beta1, beta2, eps, wd, clip, step,
@@ -570,7 +574,8 @@ class StudentStep {
     need(!G_.empty(), "StudentStep: built without gradient buffers");
     c10::cuda::CUDAGuard guard(x.device());
     const int64_t B = x.size(0), T = x.size(1), C = x.size(2), M = B * T, H = H_, N = N_;
-    if (first && tail_.has_value()) tail_->zero_();
+    if (first && tail_.has_value() && tail_->numel() > 0)
+      check_cuda(rt_zero_f32(tail_->data_ptr<float>(), tail_->numel(), stream_of(x)), "zero gradient tail");
     Saved s = run_forward(x, shift, wkv0, true);
     auto dpred = gemm_nmse(s.yg, W_.at("output"), target.reshape({M, C}).to(at::kBFloat16).contiguous(), stats, eps);
     // output projection
@@ -583,9 +588,8 @@ class StudentStep {
     tm_post_wkv_bwd(dyg, s.y, s.r, s.k_in, s.v, s.g, P_.at("ln_w"), P_.at("ln_b"), P_.at("r_k"), s.gn, dy, dg,
                     bonus[0], bonus[1], bonus[2], G_.at("ln_w"), G_.at("ln_b"), G_.at("r_k"), H, N);
     const std::vector<int64_t> shape = {B, T, H, N};
-    auto dend = at::zeros({B, H, N, N}, f32);
     auto gw = wkv7_backward(s.r.view(shape), s.w_in.view(shape), s.k_in.view(shape), s.v.view(shape),
-                            s.a_in.view(shape), s.b_in.view(shape), s.ckpt, s.rec, dy.view(shape), dend);
+                            s.a_in.view(shape), s.b_in.view(shape), s.ckpt, s.rec, dy.view(shape), at::Tensor());
     std::vector<at::Tensor> d5;
     for (int i = 0; i < 5; ++i) d5.push_back(at::empty_like(dpred));  // dr, dk, dv, dlw, dla
     tm_pre_wkv_bwd({gw[0], gw[1], gw[2], gw[3], gw[4], gw[5]}, bonus, s.k, s.la, P_.at("w0"), P_.at("a0"),
@@ -717,7 +721,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("act_bwd_", &act_bwd_);
   m.def("nmse_loss", &nmse_loss, py::arg("pred"), py::arg("target"), py::arg("stats"), py::arg("dpred"),
         py::arg("eps"));
-  m.def("flat_adamw", &flat_adamw);
+  m.def("flat_adamw", &flat_adamw, "norm (fixed-order sum), clip, AdamW, bf16 refresh, report; clears stats");
+  m.def("flat_adamw_scratch", []() { return rt_flat_adamw_scratch(); });
+  m.def("zero_", [](at::Tensor t) {
+        TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kFloat && t.is_contiguous(), "zero_ needs contiguous fp32");
+        c10::cuda::CUDAGuard guard(t.device());
+        check_cuda(rt_zero_f32(t.data_ptr<float>(), t.numel(), stream_of(t)), "zero");
+      });
   m.def("to_bf16_", &to_bf16_);
   m.def("flash_attention", &flash_attention);
   m.def("exchange_update", &exchange_update, "peer-memory reduce-scatter + clip + AdamW + all-gather of one layer");

@@ -22,6 +22,7 @@
 // Adam moments with bias correction, refreshes the bf16 copy used by the
 // GEMMs, clears the gradient and writes the step report
 // [sum nmse, sum cos, count, norm, error].
+#include <algorithm>
 #include "../common/common.cuh"
 
 namespace {
@@ -447,10 +448,12 @@ __global__ void loss_rows_finish_kernel(const float4* __restrict__ rowsum, float
 
 // ---------------------------------------------------------------- optimizer
 // The gradient buffer is read, never written: the next micro-step's GEMMs store the four big matrices' gradients
-// and the rest of the buffer is cleared when that micro-step starts (models/student_fused.py).
-// norm2 += sum g^2 (raw sums; the 1/count scale is applied in adamw_kernel).
+// and the rest of the buffer is cleared when that micro-step starts (StudentStep in bindings.cpp).
+// Per-block partial sums of g^2 (raw sums; the 1/count scale is applied later), one slot per block: the report
+// kernel adds them in block order, so the norm does not depend on the order blocks finish in.
+constexpr int NORM_BLOCKS = 1024;
 __global__ void norm2_kernel(const float4* __restrict__ g, long n4, const float* __restrict__ g_tail, long tail,
-                             float* __restrict__ norm2) {
+                             float* __restrict__ partial) {
   __shared__ float scratch[32];
   float acc = 0.f;
   for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (long)gridDim.x * blockDim.x) {
@@ -460,7 +463,7 @@ __global__ void norm2_kernel(const float4* __restrict__ g, long n4, const float*
   if (blockIdx.x == 0)
     for (long i = threadIdx.x; i < tail; i += blockDim.x) acc += g_tail[i] * g_tail[i];
   acc = rt::block_sum(acc, scratch);
-  if (threadIdx.x == 0) atomicAdd(norm2, acc);
+  if (threadIdx.x == 0) partial[blockIdx.x] = acc;
 }
 
 struct AdamArgs {
@@ -475,15 +478,34 @@ RT_DEVICE void adam_elem(float g, float& p, float& m, float& v, long i, const Ad
   p -= step * m / (sqrtf(v) / a.bias2_sqrt + a.eps);
 }
 
+// One block: the norm from the partial sums (fixed order), the report [nmse, cos, count, norm, error], the
+// gradient scale for adamw_kernel in scale[0], and the update's statistics cleared for the next update.
+__global__ void report_kernel(float* __restrict__ stats, const float* __restrict__ partial, int nblocks,
+                              float* __restrict__ scale, float* __restrict__ report, float clip) {
+  __shared__ float scratch[32];
+  float acc = 0.f;
+  for (int b = threadIdx.x; b < nblocks; b += blockDim.x) acc += partial[b];
+  acc = rt::block_sum(acc, scratch);
+  if (threadIdx.x == 0) {
+    const float count = stats[2];
+    const float inv = count > 0.f ? 1.f / count : 0.f;
+    const float norm = sqrtf(acc) * inv;
+    report[0] = stats[0];
+    report[1] = stats[1];
+    report[2] = count;
+    report[3] = norm;
+    report[4] = (!isfinite(norm) || count <= 0.f) ? 1.f : 0.f;
+    scale[0] = inv * fminf(1.f, clip / (norm + 1e-6f));
+    stats[0] = stats[1] = stats[2] = 0.f;
+  }
+}
+
 // g is scaled by (1/count) * min(1, clip / (|g| / count + 1e-6)): the reference's division by the token count
-// followed by clip_grad_norm_ on the divided gradients.
+// followed by clip_grad_norm_ on the divided gradients (the factor comes from report_kernel).
 __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
-                             float* __restrict__ v, bf16* __restrict__ shadow, long n, const float* __restrict__ norm2,
-                             const float* __restrict__ stats, AdamArgs a) {
-  const float count = stats[2];
-  const float inv = count > 0.f ? 1.f / count : 0.f;
-  const float norm = sqrtf(*norm2) * inv;
-  const float gscale = inv * fminf(1.f, a.clip / (norm + 1e-6f));
+                             float* __restrict__ v, bf16* __restrict__ shadow, long n, const float* __restrict__ scale,
+                             AdamArgs a) {
+  const float gscale = scale[0];
   const float step = a.lr / a.bias1;
   const long n4 = n / 4;
   for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (long)gridDim.x * blockDim.x) {
@@ -519,15 +541,11 @@ __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g,
   }
 }
 
-__global__ void report_kernel(const float* __restrict__ stats, const float* __restrict__ norm2,
-                              float* __restrict__ report) {
-  const float count = stats[2];
-  const float norm = sqrtf(*norm2) * (count > 0.f ? 1.f / count : 0.f);
-  report[0] = stats[0];
-  report[1] = stats[1];
-  report[2] = count;
-  report[3] = norm;
-  report[4] = (!isfinite(norm) || count <= 0.f) ? 1.f : 0.f;
+__global__ void zero_f32_kernel(float4* __restrict__ p, long n4, float* __restrict__ tail, long ntail) {
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (long)gridDim.x * blockDim.x)
+    p[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (blockIdx.x == 0)
+    for (long i = threadIdx.x; i < ntail; i += blockDim.x) tail[i] = 0.f;
 }
 
 __global__ void to_bf16_kernel(const float* __restrict__ src, bf16* __restrict__ dst, long n) {
@@ -639,29 +657,41 @@ extern "C" cudaError_t rt_nmse_loss(const void* pred, const void* target, float*
   return cudaGetLastError();
 }
 
-// Reduces the flat gradient's norm, scales by 1/count, clips, applies AdamW, refreshes the bf16 shadow and
-// writes the report; the gradient itself is left untouched. `norm2` is one float of scratch (zeroed here).
-// p, g, m, v and shadow must be 16-byte aligned (flat buffers from the caching allocator are).
+// Reduces the flat gradient's norm, scales by 1/count, clips, applies AdamW, refreshes the bf16 shadow, writes
+// the report and clears `stats`; the gradient itself is left untouched. `scratch` holds >= rt_flat_adamw_scratch()
+// floats (per-block partial norms and the scale). p, g, m, v and shadow must be 16-byte aligned (flat buffers
+// from the caching allocator are).
+extern "C" int rt_flat_adamw_scratch() { return NORM_BLOCKS + 4; }
+
 extern "C" cudaError_t rt_flat_adamw(float* p, float* g, float* m, float* v, void* shadow, long n, long decay_numel,
-                                     const float* stats, float* norm2, float* report, float lr, float beta1,
-                                     float beta2, float eps, float weight_decay, float clip, int step,
-                                     cudaStream_t s) {
+                                     float* stats, float* scratch, float* report, float lr, float beta1, float beta2,
+                                     float eps, float weight_decay, float clip, int step, cudaStream_t s) {
   if ((reinterpret_cast<uintptr_t>(p) | reinterpret_cast<uintptr_t>(g) | reinterpret_cast<uintptr_t>(m) |
        reinterpret_cast<uintptr_t>(v)) & 15 || reinterpret_cast<uintptr_t>(shadow) & 7)
     return cudaErrorMisalignedAddress;
-  RT_CUDA_CHECK(cudaMemsetAsync(norm2, 0, sizeof(float), s));
   const long n4 = n / 4;
-  norm2_kernel<<<grid_for(n4, 512), 512, 0, s>>>(reinterpret_cast<const float4*>(g), n4, g + 4 * n4, n - 4 * n4,
-                                                 norm2);
+  const int nblocks = (int)std::min<long>(grid_for(n4, 512), NORM_BLOCKS);
+  norm2_kernel<<<nblocks, 512, 0, s>>>(reinterpret_cast<const float4*>(g), n4, g + 4 * n4, n - 4 * n4, scratch);
   RT_CUDA_CHECK(cudaGetLastError());
-  report_kernel<<<1, 1, 0, s>>>(stats, norm2, report);
+  float* scale = scratch + NORM_BLOCKS;
+  report_kernel<<<1, 256, 0, s>>>(stats, scratch, nblocks, scale, report, clip);
   RT_CUDA_CHECK(cudaGetLastError());
   AdamArgs a;
   a.lr = lr; a.beta1 = beta1; a.beta2 = beta2; a.eps = eps; a.weight_decay = weight_decay; a.clip = clip;
   a.bias1 = (float)(1.0 - pow((double)beta1, (double)step));
   a.bias2_sqrt = (float)sqrt(1.0 - pow((double)beta2, (double)step));
   a.decay_numel = decay_numel;
-  adamw_kernel<<<grid_for(n4, 256, 148 * 12), 256, 0, s>>>(p, g, m, v, (bf16*)shadow, n, norm2, stats, a);
+  adamw_kernel<<<grid_for(n4, 256, 148 * 12), 256, 0, s>>>(p, g, m, v, (bf16*)shadow, n, scale, a);
+  return cudaGetLastError();
+}
+
+// p[0 .. n) = 0 (own kernel, so that the step's launches stay this package's).
+extern "C" cudaError_t rt_zero_f32(float* p, long n, cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  const bool aligned = (reinterpret_cast<uintptr_t>(p) & 15) == 0;
+  const long n4 = aligned ? n / 4 : 0;
+  zero_f32_kernel<<<grid_for(std::max<long>(n4, 1), 256, 148 * 4), 256, 0, s>>>(reinterpret_cast<float4*>(p), n4,
+                                                                                 p + 4 * n4, n - 4 * n4);
   return cudaGetLastError();
 }
 

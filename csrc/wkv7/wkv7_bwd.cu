@@ -249,7 +249,7 @@ wkv7_bwd_state_kernel(int T_, int H, int N, const float* __restrict__ prep, cons
   state_issue<NP>(stage[(chunks - 1) & 1], prep + ((long)bh * chunks + chunks - 1) * PREP, row0);
   for (int e = threadIdx.x; e < R * NP; e += 128) {
     const int i = e / NP, j = e % NP, row = row0 + i;
-    dS[i * SP + j] = (row < N && j < N) ? dend[bh * NN + (long)row * N + j] : 0.f;
+    dS[i * SP + j] = (row < N && j < N && dend) ? dend[bh * NN + (long)row * N + j] : 0.f;
   }
   for (int ch = chunks - 1; ch >= 0; --ch) {
     // gradient w.r.t. this chunk's end state

@@ -95,7 +95,7 @@ wkv7_tc_bscan_kernel(const float* __restrict__ rec, const __nv_bfloat16* __restr
   float s[4];
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
-    s[q] = dend[((long)bh * N + rb + r0 + q) * N + j];
+    s[q] = dend ? dend[((long)bh * N + rb + r0 + q) * N + j] : 0.f;  // null: zero end-state gradient
     dS[(r0 + q) * 64 + j] = s[q];
   }
 #pragma unroll 1

@@ -33,7 +33,7 @@ micro-step of a given shape is captured once as a CUDA graph and every later one
 is a replay (full ``chunk_tokens`` chunks only; the shorter last chunk of a
 document runs eagerly): the chunk's input and target are copied into static buffers, the
 carried state lives in static buffers (zeroed at a document boundary), and the
-statistics come back through a static buffer. The first micro-step of a shape runs
+loss sums accumulate straight into the student's statistics tensor. The first micro-step of a shape runs
 eagerly, so the GEMM tile choices are measured before any capture. All students'
 graphs share one memory pool: their intermediates die inside the replay, and
 replays are serialised on the training stream.
@@ -49,21 +49,19 @@ _POOLS = {}  # device index -> memory pool shared by the micro-step graphs
 class _StepGraph:
     """One captured micro-step of fixed input shape and ``first`` flag."""
 
-    def __init__(self, fused, shape, target_dtype, first, eps):
+    def __init__(self, fused, shape, target_dtype, first, eps, stats):
         B, T, C = shape
         dev = fused.device
         self.x = torch.zeros(B, T, C, device=dev, dtype=torch.bfloat16)
         self.y = torch.zeros(B, T, C, device=dev, dtype=target_dtype)
         self.shift = torch.zeros(B, C, device=dev, dtype=torch.bfloat16)
         self.wkv = torch.zeros(B, fused.H, fused.N, fused.N, device=dev, dtype=torch.float32)
-        self.stats = torch.zeros(3, device=dev)
         self.state = {"shift": self.shift, "wkv": self.wkv}
         pool = _POOLS.setdefault(dev.index, torch.cuda.graph_pool_handle())
         self.graph = torch.cuda.CUDAGraph()
         torch.cuda.synchronize(dev)
-        with torch.cuda.graph(self.graph, pool=pool, capture_error_mode="thread_local"):
-            stats, new_state = fused._forward_backward(self.x, self.y, self.state, eps, first)
-            self.stats.copy_(stats)
+        with torch.cuda.graph(self.graph, pool=pool, capture_error_mode="thread_local"):  # records, runs nothing
+            new_state = fused._forward_backward(self.x, self.y, self.state, eps, stats, first)
             self.shift.copy_(new_state["shift"])
             self.wkv.copy_(new_state["wkv"])
 
@@ -77,7 +75,7 @@ class _StepGraph:
             self.shift.copy_(state["shift"])
             self.wkv.copy_(state["wkv"])
         self.graph.replay()
-        return self.stats, self.state
+        return self.state
 
 
 class FusedStudent:
@@ -87,7 +85,7 @@ class FusedStudent:
         self.C, self.H, self.N = core.width, core.heads, core.head_size
         self.device = flat.param.device
         self.shadow = torch.empty(flat.numel, device=self.device, dtype=torch.bfloat16)
-        self.norm2 = torch.zeros(1, device=self.device)
+        self.scratch = torch.zeros(native().flat_adamw_scratch(), device=self.device)  # optimizer partial norms
         start = flat.offsets[flat.names.index("x_r")]
         if [flat.names[flat.names.index("x_r") + i] for i in range(6)] != list(_MIX):
             raise RuntimeError("unexpected flat parameter order")
@@ -144,28 +142,27 @@ class FusedStudent:
 
     # ------------------------------------------------------------------ training micro-step
     @torch.no_grad()
-    def forward_backward(self, x, target, state, eps, first=False):
-        """One micro-step. ``first``: the gradient buffer holds a finished update's values; the four big
-        matrices' gradients are then stored (not accumulated) and the rest of the buffer is cleared.
-        Returns (statistics [3], new state); with graphs, both are static buffers of the step's graph that
-        the next replay of the same shape overwrites."""
+    def forward_backward(self, x, target, state, eps, stats, first=False):
+        """One micro-step; ``stats`` (fp32 [3], a persistent tensor) += [sum nmse, sum cos, tokens]. ``first``: the
+        gradient buffer holds a finished update's values; the four big matrices' gradients are then stored (not
+        accumulated) and the rest of the buffer is cleared. Returns the new state; with graphs, its tensors are
+        static buffers of the step's graph that the next replay of the same shape overwrites."""
         if not self.use_graphs or x.shape[1] != self.student.cfg["chunk_tokens"]:
             # graphs only for full chunks: the shorter last chunk of a document varies in length
-            return self._forward_backward(x, target, state, eps, first)
-        key = (tuple(x.shape), target.dtype, bool(first), float(eps))
+            return self._forward_backward(x, target, state, eps, stats, first)
+        key = (tuple(x.shape), target.dtype, bool(first), float(eps), stats.data_ptr())
         step = self.graphs.get(key)
         if step is None:
             if key not in self.graphs:  # first use of this shape: eager (measures GEMM tiles), capture next time
                 self.graphs[key] = None
-                return self._forward_backward(x, target, state, eps, first)
-            step = self.graphs[key] = _StepGraph(self, tuple(x.shape), target.dtype, bool(first), float(eps))
+                return self._forward_backward(x, target, state, eps, stats, first)
+            step = self.graphs[key] = _StepGraph(self, tuple(x.shape), target.dtype, bool(first), float(eps), stats)
         return step.run(x, target, state)
 
-    def _forward_backward(self, x, target, state, eps, first):
-        stats = torch.zeros(3, device=x.device)
+    def _forward_backward(self, x, target, state, eps, stats, first):
         shift, wkv0 = (None, None) if state is None else (state["shift"], state["wkv"])
         new_shift, end = self.native.forward_backward(x, target, shift, wkv0, float(eps), bool(first), stats)
-        return stats, {"shift": new_shift, "wkv": end}
+        return {"shift": new_shift, "wkv": end}
 
     # ------------------------------------------------------------------ update
     @torch.no_grad()
@@ -174,7 +171,7 @@ class FusedStudent:
         cfg, flat = st.cfg, st.flat
         beta1, beta2 = cfg["betas"]
         native().flat_adamw(flat.param, flat.grad, flat.exp_avg, flat.exp_avg_sq, self.shadow, st.decay_numel,
-                            st.stats, self.norm2, st.report, float(lr), float(beta1), float(beta2),
+                            st.stats, self.scratch, st.report, float(lr), float(beta1), float(beta2),
                             float(cfg["adam_eps"]), float(cfg["weight_decay"]), float(cfg["clip_norm"]), int(step))
 
 

@@ -115,10 +115,9 @@ class Student:
         """Forward + backward on one chunk; gradients accumulate into the flat buffer."""
         self.join_update()
         eps = self.cfg["loss_epsilon"]
-        if self.fused is not None:
-            stats, self.state = self.fused.forward_backward(x, target, self.state, eps, first=not self.grads_live)
+        if self.fused is not None:  # the loss sums accumulate into self.stats on the device
+            self.state = self.fused.forward_backward(x, target, self.state, eps, self.stats, first=not self.grads_live)
             self.grads_live = True
-            self.stats += stats
             return
         from .losses import statistics
         with torch.autocast(x.device.type, dtype=torch.bfloat16):
@@ -193,8 +192,7 @@ class Student:
             if not self.grads_live:
                 self.flat.grad.zero_()
             if not self.overlap_update:
-                self.fused.update(lr, self.steps_done)
-                self.stats.zero_()
+                self.fused.update(lr, self.steps_done)  # also clears stats for the next update
                 self.grads_live = False
                 return lr
             main = torch.cuda.current_stream(self.topo.device)
@@ -202,7 +200,6 @@ class Student:
             side.wait_stream(main)
             with torch.cuda.stream(side):
                 self.fused.update(lr, self.steps_done)
-                self.stats.zero_()
             self._update_done = torch.cuda.Event()
             self._update_done.record(side)
             self.grads_live = False

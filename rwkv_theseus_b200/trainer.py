@@ -94,7 +94,11 @@ class StepEngine:
         self.device = topo.device
         self.last_capture = max(order)
         self.profiler = StepProfiler(self.device)
-        self._snap = None                     # [layers, 5] device copy of the step's reports (update stream)
+        # [layers, 5] the step's reports: each student's report is a row of this tensor (written in place by its
+        # update on the update stream), so the whole step's reports leave in one copy
+        self._snap = torch.zeros(len(order), 5, device=self.device)
+        for index, layer in enumerate(order):
+            students[layer].report = self._snap[index]
         self._slot = 0                        # pinned metric buffers used in turn
         self._pinned_rows = [None, None]
         self._pinned_faults = [None, None]
@@ -103,6 +107,12 @@ class StepEngine:
         self._pinned = [None, None]   # two pinned id buffers used in turn
         self._copied = [None, None]   # event after the copy that last read each buffer
         self._turn = 0
+        # On CUDA a step's per-layer updates (local AdamW, or the peer exchange) are issued at the start of the next
+        # step, on their side stream, so that they run under its teacher forward (which reads no student parameter)
+        # instead of competing with the next layers' student work; each layer's next micro-step waits for its own.
+        self.defer_updates = self.device.type == "cuda"
+        self._deferred = []           # students whose update of the last step is not issued yet
+        self._waiting_reads = []      # metric reads of that step, issued right after its updates
         if self.device.type == "cuda":
             for student in students.values():
                 student.overlap_update = True
@@ -137,50 +147,72 @@ class StepEngine:
 
     def step(self, reader):
         """One optimizer update of every layer; returns {layer: device report [nmse, cos, count, norm, error]}.
-        Each report is also copied into the engine's step snapshot on the stream its update ran on, so that
+        The reports are rows of one engine tensor, written on the stream their updates ran on, so that
         ``read_metrics_async`` can read a step while the next one already runs."""
         profiler = self.profiler
         profiler.reset()
+        self.flush()  # the previous step's updates, under this step's teacher forward
         micro_steps = self.cfg["grad_accum_steps"]
         for micro in range(micro_steps):
             batch = reader.next()
             if batch is not None:
                 self._teacher(batch)
             updating = micro == micro_steps - 1
-            for index, layer in enumerate(self.order):
+            for layer in self.order:
                 student, capture = self.students[layer], self.captures[layer]
                 if batch is not None:
                     with profiler.phase(f"student_{layer:02d}"):
                         student.micro_step(capture.x, capture.y)
                     capture.x = capture.y = None
                 if updating:
-                    with profiler.phase(f"update_{layer:02d}"):
-                        student.reduce()
-                        student.update()
-                    self._snapshot_report(index, student)
+                    if self.defer_updates:
+                        self._deferred.append(student)
+                    else:
+                        with profiler.phase(f"update_{layer:02d}"):
+                            student.reduce()
+                            student.update()
         return {layer: student.report for layer, student in self.students.items()}
 
+    def flush(self):
+        """Issue the updates deferred from the last step (in layer order, the same on every rank) and the metric
+        reads waiting for them. Called at the start of every step; call it before anything that reads student
+        parameters outside a step (validation, checkpoints, export) or before a step-exact device timing ends."""
+        deferred, self._deferred = self._deferred, []
+        for student in deferred:
+            with self.profiler.phase(f"update_{student.layer:02d}"):
+                student.reduce()
+                student.update()
+        waiting, self._waiting_reads = self._waiting_reads, []
+        for pending in waiting:
+            self._issue_read(pending)
+
     # ---------------------------------------------------------------- metrics
-    def _snapshot_report(self, index, student):
-        if self._snap is None:
-            self._snap = torch.zeros(len(self.order), 5, device=self.device)
-        stream = student.update_stream()
-        if stream is None:
-            self._snap[index].copy_(student.report)
-            return
-        with torch.cuda.stream(stream):
-            self._snap[index].copy_(student.report)
 
     def read_metrics_async(self, reports):
         """Start bringing this step's reports, the kernels' fault words and the exchange status to the host; returns
         a ``PendingMetrics`` whose ``result()`` waits for them and validates. The host may issue the next step in
         between. The reports and the exchange status are copied on the stream the updates ran on (ordered after
         this step's updates and before the next step's); the fault words are copied and cleared on the current
-        stream, in order with the kernels that set them."""
-        lrs = [self.cfg["lr"] * lr_factor(self.students[layer].steps_done - 1, self.cfg, self.students[layer].total_steps)
-               for layer in self.order]
+        stream, in order with the kernels that set them. With deferred updates the copies are issued right after
+        the updates, at the start of the next step (or by ``flush``, which ``result()`` calls if needed)."""
         if self.device.type != "cuda":
-            return PendingMetrics(self, torch.stack([reports[layer] for layer in self.order]), None, None, (), lrs)
+            pending = PendingMetrics(self)
+            lrs = self._learning_rates()
+            pending.issued(torch.stack([reports[layer] for layer in self.order]), None, None, (), lrs)
+            return pending
+        pending = PendingMetrics(self)
+        if self._deferred:
+            self._waiting_reads.append(pending)
+        else:
+            self._issue_read(pending)
+        return pending
+
+    def _learning_rates(self):
+        """Learning rate each layer's last update used."""
+        return [self.cfg["lr"] * lr_factor(self.students[layer].steps_done - 1, self.cfg,
+                                           self.students[layer].total_steps) for layer in self.order]
+
+    def _issue_read(self, pending):
         slot = self._slot
         self._slot ^= 1
         for event in self._pending_events[slot]:
@@ -203,9 +235,9 @@ class StepEngine:
         faults_copied = torch.cuda.Event()
         faults_copied.record(main)
         self._pending_events[slot] = (reports_copied, faults_copied)
-        return PendingMetrics(self, self._pinned_rows[slot], self._pinned_faults[slot],
-                              self._pinned_status[slot] if exchange is not None else None,
-                              self._pending_events[slot], lrs)
+        pending.issued(self._pinned_rows[slot], self._pinned_faults[slot],
+                       self._pinned_status[slot] if exchange is not None else None, self._pending_events[slot],
+                       self._learning_rates())
 
     def read_metrics(self, reports):
         """Synchronous form: the validated metrics of the step that produced `reports`."""
@@ -233,13 +265,18 @@ class StepEngine:
 class PendingMetrics:
     """One step's metrics on their way to the host (``StepEngine.read_metrics_async``)."""
 
-    def __init__(self, engine, rows, faults, status, events, lrs):
-        self.engine, self.rows, self.faults, self.status, self.events = engine, rows, faults, status, events
-        self.lrs = lrs
+    def __init__(self, engine):
+        self.engine = engine
+        self.rows = None  # set when the copies are issued
         self._value = None
+
+    def issued(self, rows, faults, status, events, lrs):
+        self.rows, self.faults, self.status, self.events, self.lrs = rows, faults, status, events, lrs
 
     def result(self):
         if self._value is None:
+            if self.rows is None:
+                self.engine.flush()  # the step's updates (and with them this read) were still deferred
             for event in self.events:
                 event.synchronize()
             rows = self.rows.double().tolist()
