@@ -39,6 +39,8 @@ def main():
     p.add_argument("--profile", action="store_true", help="per-kernel times of one decode step (profiled)")
     p.add_argument("--graph", action="store_true", help="replay the decode step as a CUDA graph")
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--profile-prefill", action="store_true",
+                   help="after the timed run, per-kernel times of a second prefill (profiled)")
     a = p.parse_args()
     if a.impl == "reference":
         return run_reference(a)
@@ -53,8 +55,10 @@ def main():
     runner = Runner(model)
     g = torch.Generator(device=device).manual_seed(7)
     prompt = torch.randint(0, cfg.vocab_size, (a.batch, a.prompt), device=device, generator=g)
-    warm = torch.randint(0, cfg.vocab_size, (a.batch, 64), device=device, generator=g)
-    generate(runner, warm, 4, prefill_chunk=a.prefill_chunk, graph=a.graph)  # warm-up: every kernel path once
+    # warm-up: every kernel path once at the timed shapes (a full prefill chunk, then decode steps), so that the
+    # GEMM tile choices are measured before the clock starts, as a serving process does once at start-up
+    warm = torch.randint(0, cfg.vocab_size, (a.batch, min(a.prompt, a.prefill_chunk)), device=device, generator=g)
+    generate(runner, warm, 4, prefill_chunk=a.prefill_chunk, graph=a.graph)
     torch.cuda.synchronize()
     events = []
 
@@ -91,6 +95,21 @@ def main():
               "cuda_graph": a.graph,
               "data": "uniform-random prompt ids; random-init weights"}
     print(json.dumps(result), flush=True)
+    if a.profile_prefill:
+        from torch.profiler import ProfilerActivity, profile
+        runner.reset()
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            for c in range(0, a.prompt, a.prefill_chunk):
+                runner.forward(prompt[:, c:c + a.prefill_chunk])
+            torch.cuda.synchronize()
+        rows = {}
+        for evt in prof.events():
+            if evt.device_type == torch.autograd.DeviceType.CUDA:
+                key = evt.name[:60]
+                n, t = rows.get(key, (0, 0.0))
+                rows[key] = (n + 1, t + evt.device_time)
+        for name, (n, us) in sorted(rows.items(), key=lambda kv: -kv[1][1])[:25]:
+            print(json.dumps({"prefill_kernel": name, "calls": n, "us": round(us, 1)}), flush=True)
     if a.profile:
         from torch.profiler import ProfilerActivity, profile
         token = out[:, -1:]
@@ -128,7 +147,8 @@ def run_reference(a):
     def greedy(hidden):
         return model.lm_head(hidden[:, -1]).argmax(-1, keepdim=True)
 
-    warm = torch.randint(0, model.config.vocab_size, (a.batch, 64), device=device, generator=g)
+    warm = torch.randint(0, model.config.vocab_size, (a.batch, min(a.prompt, a.prefill_chunk)), device=device,
+                         generator=g)
     tok = greedy(runner.forward(warm))
     for _ in range(3):
         tok = greedy(runner.forward(tok))
