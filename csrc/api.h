@@ -109,6 +109,7 @@ cudaError_t rt_flat_adamw(float* p, float* g, float* m, float* v, void* shadow, 
                           float* stats, float* scratch, float* report, float lr, float beta1, float beta2,
                           float eps, float weight_decay, float clip, int step, cudaStream_t s);
 cudaError_t rt_zero_f32(float* p, long n, cudaStream_t s);
+cudaError_t rt_copy_bytes(void* dst, const void* src, long nbytes, cudaStream_t s);
 cudaError_t rt_to_bf16(const float* src, void* dst, long n, cudaStream_t s);
 
 // Flash attention forward (head_dim 256, GQA, causal with cache offset, fused sigmoid gate).

@@ -564,7 +564,7 @@ class StudentStep {
     c10::cuda::CUDAGuard guard(x.device());
     Saved s = run_forward(x, shift, wkv0, false);
     auto pred = mm(s.yg, W_.at("output"), false);
-    return {pred.view(x.sizes()), s.x.select(1, s.x.size(1) - 1).clone(), s.end};
+    return {pred.view(x.sizes()), last_token(s.x), s.end};
   }
 
   // Training micro-step: stats (fp32 [3]) += [sum nmse, sum cos, tokens]; gradients stored (first) or accumulated
@@ -623,13 +623,25 @@ class StudentStep {
     acc(xm(5), dhg, "g1");
     gemm(dhg, false, W_.at("g1"), false, 0, 1.0, dmix.select(0, 5), 0);
     tm_mix_bwd(s.x, s.shift, dmix, G_.at("coef"));
-    return {s.x.select(1, T - 1).clone(), s.end};
+    return {last_token(s.x), s.end};
   }
 
  private:
   struct Saved {
     at::Tensor x, shift, mix, r, k, v, hw, ha, hg, lw, la, g, w_in, k_in, a_in, b_in, y, ckpt, rec, yg, gn, end;
   };
+
+  // x[:, T - 1] as a new [B, C] tensor (the next chunk's token-shift state), copied by this package's kernel.
+  static at::Tensor last_token(const at::Tensor& x) {
+    const int64_t B = x.size(0), T = x.size(1), C = x.size(2);
+    auto out = at::empty({B, C}, x.options());
+    const long row = C * (long)x.element_size();
+    for (int64_t b = 0; b < B; ++b)
+      check_cuda(rt_copy_bytes(static_cast<uint8_t*>(out.data_ptr()) + b * row,
+                               static_cast<const uint8_t*>(x.data_ptr()) + (b * T + T - 1) * row, row, stream_of(x)),
+                 "last token");
+    return out;
+  }
 
   static at::Tensor mm(const at::Tensor& a, const at::Tensor& b, bool b_t) {
     return gemm(a, false, b, b_t, 0, 1.0, c10::nullopt, 0);
@@ -647,9 +659,15 @@ class StudentStep {
     Saved s;
     const int64_t B = x_in.size(0), T = x_in.size(1), C = x_in.size(2), M = B * T, H = H_, N = N_;
     s.x = x_in.to(at::kBFloat16).contiguous();
-    s.shift = shift.has_value() ? shift->to(at::kBFloat16).contiguous() : at::zeros({B, C}, s.x.options());
-    auto state = wkv0.has_value() ? wkv0->to(at::kFloat).contiguous()
-                                  : at::zeros({B, H, N, N}, s.x.options().dtype(at::kFloat));
+    auto zeros = [&](std::vector<int64_t> shape, at::ScalarType type) {  // cleared by this package's kernel
+      auto t = at::empty(shape, s.x.options().dtype(type));
+      check_cuda(rt_zero_f32(static_cast<float*>(t.data_ptr()), t.numel() * (long)t.element_size() / 4,
+                             stream_of(t)),
+                 "zero state");
+      return t;
+    };
+    s.shift = shift.has_value() ? shift->to(at::kBFloat16).contiguous() : zeros({B, C}, at::kBFloat16);
+    auto state = wkv0.has_value() ? wkv0->to(at::kFloat).contiguous() : zeros({B, H, N, N}, at::kFloat);
     s.mix = at::empty({6, M, C}, s.x.options());
     tm_mix(s.x, s.shift, P_.at("coef"), s.mix);
     auto xm = [&](int i) { return s.mix.select(0, i); };
@@ -724,10 +742,20 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flat_adamw", &flat_adamw, "norm (fixed-order sum), clip, AdamW, bf16 refresh, report; clears stats");
   m.def("flat_adamw_scratch", []() { return rt_flat_adamw_scratch(); });
   m.def("zero_", [](at::Tensor t) {
-        TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kFloat && t.is_contiguous(), "zero_ needs contiguous fp32");
+        const long bytes = t.numel() * (long)t.element_size();
+        TORCH_CHECK(t.is_cuda() && t.is_contiguous() && bytes % 4 == 0, "zero_ needs a contiguous CUDA tensor of 4k bytes");
         c10::cuda::CUDAGuard guard(t.device());
-        check_cuda(rt_zero_f32(t.data_ptr<float>(), t.numel(), stream_of(t)), "zero");
-      });
+        check_cuda(rt_zero_f32(static_cast<float*>(t.data_ptr()), bytes / 4, stream_of(t)), "zero");
+      }, "t = 0 with this package's kernel");
+  m.def("copy_", [](at::Tensor dst, at::Tensor src) {
+        TORCH_CHECK(dst.is_cuda() && src.is_cuda() && dst.is_contiguous() && src.is_contiguous() &&
+                        dst.scalar_type() == src.scalar_type() && dst.numel() == src.numel(),
+                    "copy_ needs contiguous CUDA tensors of one dtype and size");
+        c10::cuda::CUDAGuard guard(dst.device());
+        check_cuda(rt_copy_bytes(dst.data_ptr(), src.data_ptr(), dst.numel() * (long)dst.element_size(),
+                                 stream_of(dst)),
+                   "copy");
+      }, "dst = src with this package's kernel");
   m.def("to_bf16_", &to_bf16_);
   m.def("flash_attention", &flash_attention);
   m.def("exchange_update", &exchange_update, "peer-memory reduce-scatter + clip + AdamW + all-gather of one layer");

@@ -685,6 +685,26 @@ extern "C" cudaError_t rt_flat_adamw(float* p, float* g, float* m, float* v, voi
   return cudaGetLastError();
 }
 
+__global__ void copy_bytes_kernel(uint4* __restrict__ dst, const uint4* __restrict__ src, long n16,
+                                  uint8_t* __restrict__ dtail, const uint8_t* __restrict__ stail, long ntail) {
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += (long)gridDim.x * blockDim.x)
+    dst[i] = __ldcs(src + i);
+  if (blockIdx.x == 0)
+    for (long i = threadIdx.x; i < ntail; i += blockDim.x) dtail[i] = stail[i];
+}
+
+// dst[0 .. nbytes) = src[0 .. nbytes) on the device (own kernel: 16-byte moves when both are 16-byte aligned).
+extern "C" cudaError_t rt_copy_bytes(void* dst, const void* src, long nbytes, cudaStream_t s) {
+  if (nbytes <= 0) return cudaSuccess;
+  const bool aligned = ((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) & 15) == 0;
+  const long n16 = aligned ? nbytes / 16 : 0;
+  copy_bytes_kernel<<<grid_for(std::max<long>(n16, 1), 256, 148 * 4), 256, 0, s>>>(
+      reinterpret_cast<uint4*>(dst), reinterpret_cast<const uint4*>(src), n16,
+      reinterpret_cast<uint8_t*>(dst) + 16 * n16, reinterpret_cast<const uint8_t*>(src) + 16 * n16,
+      nbytes - 16 * n16);
+  return cudaGetLastError();
+}
+
 // p[0 .. n) = 0 (own kernel, so that the step's launches stay this package's).
 extern "C" cudaError_t rt_zero_f32(float* p, long n, cudaStream_t s) {
   if (n <= 0) return cudaSuccess;

@@ -286,6 +286,17 @@ class HybridCache:
     def get_seq_length(self, layer_idx=0):
         return self.cursor
 
+    def reset(self):
+        """Start a new window: position 0, empty KV caches and zero recurrent states. The buffers are kept (their
+        stale entries are never read: attention masks keys past the length, and a fresh recurrent state is
+        cleared in place before its first use), so document starts allocate and copy nothing."""
+        self.cursor = 0
+        for layer in self.layers:
+            if "keys" in layer:
+                layer["length"] = 0
+            if "recurrent" in layer:
+                layer["fresh"] = True
+
     def state_dict(self):
         out = []
         for layer in self.layers:

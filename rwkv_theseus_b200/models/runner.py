@@ -135,7 +135,8 @@ class Runner:
         self.cache = HybridCache(model.config)
 
     def reset(self):
-        self.cache = HybridCache(self.model.config)
+        """New window: the cache restarts at position 0 with empty states (its buffers are reused)."""
+        self.cache.reset()
         for adapter in adapters(self.model).values():
             adapter.state = None
 
@@ -170,7 +171,9 @@ def isolated_state(runner):
     """Run the body on a fresh cache and fresh student states; the live ones are put back afterwards."""
     live_cache = runner.cache
     live_states = {index: adapter.state for index, adapter in adapters(runner.model).items()}
-    runner.reset()
+    runner.cache = HybridCache(runner.model.config)  # a separate cache (reset() would clear the live one)
+    for adapter in adapters(runner.model).values():
+        adapter.state = None
     try:
         yield runner
     finally:

@@ -60,20 +60,22 @@ class _StepGraph:
         pool = _POOLS.setdefault(dev.index, torch.cuda.graph_pool_handle())
         self.graph = torch.cuda.CUDAGraph()
         torch.cuda.synchronize(dev)
+        ext = native()
         with torch.cuda.graph(self.graph, pool=pool, capture_error_mode="thread_local"):  # records, runs nothing
             new_state = fused._forward_backward(self.x, self.y, self.state, eps, stats, first)
-            self.shift.copy_(new_state["shift"])
-            self.wkv.copy_(new_state["wkv"])
+            ext.copy_(self.shift, new_state["shift"])
+            ext.copy_(self.wkv, new_state["wkv"])
 
     def run(self, x, target, state):
-        self.x.copy_(x)
-        self.y.copy_(target)
+        ext = native()  # copies and clears by this package's kernels
+        ext.copy_(self.x, x.contiguous())
+        ext.copy_(self.y, target.contiguous())
         if state is None:
-            self.shift.zero_()
-            self.wkv.zero_()
+            ext.zero_(self.shift)
+            ext.zero_(self.wkv)
         elif state is not self.state:
-            self.shift.copy_(state["shift"])
-            self.wkv.copy_(state["wkv"])
+            ext.copy_(self.shift, state["shift"].to(torch.bfloat16).contiguous())
+            ext.copy_(self.wkv, state["wkv"].float().contiguous())
         self.graph.replay()
         return self.state
 

@@ -22,9 +22,12 @@ def _ensure_cache(state, B, T, Hkv, D, device):
     need = length + T
     if keys is None or keys.shape[1] < need:
         cap = max(need, 2 * (keys.shape[1] if keys is not None else 0), 1024)
-        # Zero-filled: attention tiles read whole key blocks, and masked keys must hold finite values.
-        new_k = torch.zeros(B, cap, Hkv, D, device=device, dtype=torch.bfloat16)
-        new_v = torch.zeros_like(new_k)
+        # Zero-filled: attention tiles read whole key blocks, and masked keys must hold finite values. The cache
+        # outlives window resets (the length restarts at 0), so it grows only until it holds the longest window.
+        new_k = torch.empty(B, cap, Hkv, D, device=device, dtype=torch.bfloat16)
+        new_v = torch.empty_like(new_k)
+        native().zero_(new_k)
+        native().zero_(new_v)
         if keys is not None and length:
             new_k[:, :length].copy_(keys[:, :length])
             new_v[:, :length].copy_(state["values"][:, :length])

@@ -61,15 +61,23 @@ def swiglu_mlp(x, w_gate, w_up, w_down):
 
 
 def _gdn_state(module, state, B, device, dtype):
+    """(conv window, recurrent state) of the layer: the carried ones, or zeros at a window start (a kept buffer
+    cleared in place by this package's kernel when the cache was reset)."""
     cfg = module.cfg
     K = cfg.linear_conv_kernel_dim
-    fresh = state is None or "recurrent" not in state or state["recurrent"].shape[0] != B
-    if fresh:
-        conv = torch.zeros(B, K - 1, cfg.conv_dim, device=device, dtype=dtype)
-        rec = torch.zeros(B, cfg.linear_num_value_heads, cfg.linear_key_head_dim, cfg.linear_value_head_dim,
-                          device=device, dtype=torch.float32)
-        return conv, rec
-    return state["conv"], state["recurrent"]
+    if state is not None and "recurrent" in state and state["recurrent"].shape[0] == B:
+        if state.pop("fresh", False):
+            if device.type == "cuda":
+                native().zero_(state["conv"])
+                native().zero_(state["recurrent"])
+            else:
+                state["conv"].zero_()
+                state["recurrent"].zero_()
+        return state["conv"], state["recurrent"]
+    conv = torch.zeros(B, K - 1, cfg.conv_dim, device=device, dtype=dtype)
+    rec = torch.zeros(B, cfg.linear_num_value_heads, cfg.linear_key_head_dim, cfg.linear_value_head_dim,
+                      device=device, dtype=torch.float32)
+    return conv, rec
 
 
 def gated_deltanet(module, x, state):
