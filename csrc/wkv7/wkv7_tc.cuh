@@ -108,6 +108,28 @@ RT_DEVICE void build_lambda(const uint8_t* Rw, float* lam, float* carry, int nva
   __syncthreads();
 }
 
+// build_lambda for NT threads (NT = 128 or 256): thread j + 64 p takes steps [S p, S p + S), S = 4096 / NT, of
+// column j. `carry` holds NT floats (the parts' totals). Ends with a barrier.
+template <int NT>
+RT_DEVICE void build_lambda_nt(const uint8_t* Rw, float* lam, float* carry, int nvalid, int tid) {
+  constexpr int S = 64 * 64 / NT;
+  const int j = tid & 63, part = tid >> 6, t0 = S * part;
+  float v[S];
+#pragma unroll
+  for (int u = 0; u < S; ++u) v[u] = raw(Rw, t0 + u, j);
+#pragma unroll
+  for (int u = 0; u < S; ++u) v[u] = t0 + u < nvalid ? -DECAY_SCALE * rt::sigmoidf_(v[u]) : 0.f;
+#pragma unroll
+  for (int u = 1; u < S; ++u) v[u] += v[u - 1];
+  carry[part * 64 + j] = v[S - 1];
+  __syncthreads();
+  float base = 0.f;
+  for (int q = 0; q < part; ++q) base += carry[q * 64 + j];
+#pragma unroll
+  for (int u = 0; u < S; ++u) lam[poff(t0 + u, j)] = v[u] + base;
+  __syncthreads();
+}
+
 // Triangular solves with the strictly lower 64 x 64 chunk matrix M (plain swizzled rows in `mpl`, zero on and
 // above the diagonal), one right-hand side per thread held in registers. Every thread reads the same M entries
 // (broadcast float4 loads). With one warp per scheduler the loads' latency is not hidden by other warps, so the

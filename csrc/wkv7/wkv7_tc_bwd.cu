@@ -424,7 +424,12 @@ constexpr int X2T = 169 * KB;   // [B~^T | K~^T]
 constexpr int SMEM = 201 * KB + 1024;
 }  // namespace kb
 
-__global__ void __launch_bounds__(128, 1)
+// 256 threads (8 warps): warps w and w + 4 read the same TMEM lane quarter (rows 32 (w % 4) ..) and split the
+// columns between them; the SIMT phases split their row or column ranges the same way, so every phase has twice
+// the warps of a 128-thread CTA to hide its latencies (the shared-memory map allows one CTA per SM).
+constexpr int GRAD_THREADS = 256;
+
+__global__ void __launch_bounds__(GRAD_THREADS, 1)
 wkv7_tc_bwd_grad_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_constant__ CUtensorMap m_w,
                         const __grid_constant__ CUtensorMap m_k, const __grid_constant__ CUtensorMap m_v,
                         const __grid_constant__ CUtensorMap m_a, const __grid_constant__ CUtensorMap m_b,
@@ -439,6 +444,8 @@ wkv7_tc_bwd_grad_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_co
   uint8_t* sm = align1024(smem_raw);
   const int c = blockIdx.x, h = blockIdx.y, bb = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5;
+  const int quarter = warp & 3;  // TMEM lane quarter of this warp
+  const int colh = warp >> 2;    // which 32 of a 64-column TMEM block this warp reads
   uint8_t* Rr = sm + kb::RAW;
   uint8_t *Rw = Rr + 8 * KB, *Rk = Rr + 16 * KB, *Rv = Rr + 24 * KB, *Ra = Rr + 32 * KB, *Rb = Rr + 40 * KB;
   uint8_t* Rdy = Rr + 48 * KB;
@@ -446,8 +453,9 @@ wkv7_tc_bwd_grad_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_co
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kb::MISC);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + kb::MISC + 32);
   float* DL = reinterpret_cast<float*>(sm + kb::MISC + 64);
-  float* colsum = reinterpret_cast<float*>(sm + kb::X2T);  // [192] (after the stage MMAs): the chunk-end term
-                                                           // in two halves, then the upper half's sum of g
+  float* colsum = reinterpret_cast<float*>(sm + kb::X2T);  // [512] (after the stage MMAs): the chunk-end term
+                                                           // in four parts, then each quarter's sum of g
+  float* carry = reinterpret_cast<float*>(sm + kb::X2T);   // [256] Lambda carries (before X2T is built)
   uint8_t *DZY = sm + kb::DZY, *UV = sm + kb::UV, *X1T = sm + kb::X1T, *X2T = sm + kb::X2T;
   uint8_t *S0T = sm, *DST = sm + 16 * KB;
   uint8_t *SA = DZY, *SB = UV;  // stage tiles (32 KB each)
@@ -498,13 +506,13 @@ wkv7_tc_bwd_grad_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_co
   bool second_issued = false;
   WKV_TRACE(32)
   if (ok) {
-    // ---- dY and V rows into the lower halves; the dM product can start
+    // ---- dY and V rows into the lower halves (thread: one row, 32 columns); the dM product can start
     {
-      const int t = tid & 63;
-      uint8_t* dst = tid < 64 ? DZY : UV;
-      const uint8_t* src = tid < 64 ? Rdy : Rv;
-#pragma unroll 1
-      for (int i = 0; i < 64; i += 8) {
+      const int r = tid & 127, t = r & 63, i0 = 32 * (tid >> 7);
+      uint8_t* dst = r < 64 ? DZY : UV;
+      const uint8_t* src = r < 64 ? Rdy : Rv;
+#pragma unroll
+      for (int i = i0; i < i0 + 32; i += 8) {
         float x[8];
         raw8(src, t, i, x);
         put4(dst, 128, 64 + t, i, x[0], x[1], x[2], x[3]);
@@ -517,17 +525,17 @@ wkv7_tc_bwd_grad_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_co
                      false);
       sm100::mma_commit(&bars[1]);
     }
-    build_lambda(Rw, lam, DL, nvalid, tid);
+    build_lambda_nt<GRAD_THREADS>(Rw, lam, carry, nvalid, tid);
     if (tid < 64) DL[tid] = expf(lam[poff(63, tid)]);
     WKV_TRACE(33)
-    // X1T row j: A~[t][j] (k = t), R~[t][j] (k = 64 + t); X2T row j: B~ / K~ (column owners)
+    // X1T row j: A~[t][j] (k = t), R~[t][j] (k = 64 + t); X2T row j: B~ / K~ (column owners; a thread takes 32 steps)
     {
-      const int j = tid & 63;
-      uint8_t* dst = tid < 64 ? X1T : X2T;
-      const uint8_t* s1 = tid < 64 ? Ra : Rb;
-      const uint8_t* s2 = tid < 64 ? Rr : Rk;
+      const int j = tid & 63, second = (tid >> 6) & 1, tbase = 32 * (tid >> 7);
+      uint8_t* dst = second ? X2T : X1T;
+      const uint8_t* s1 = second ? Rb : Ra;
+      const uint8_t* s2 = second ? Rk : Rr;
 #pragma unroll 1
-      for (int t0 = 0; t0 < 64; t0 += 16) {  // 16 steps at a time: loads first, then exponentials, then stores
+      for (int t0 = tbase; t0 < tbase + 32; t0 += 16) {  // 16 steps at a time: loads, exponentials, stores
         float x1[16], x2[16], lt[17];
 #pragma unroll
         for (int q = 0; q < 16; ++q) {
@@ -538,10 +546,10 @@ wkv7_tc_bwd_grad_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_co
         lt[0] = t0 ? lam[poff(t0 - 1, j)] : 0.f;
 #pragma unroll
         for (int q = 0; q < 16; ++q) {
-          if (tid < 64) {  // A~ = a e^{Lambda_{t-1}}, R~ = r e^{Lambda_t}
+          if (!second) {  // A~ = a e^{Lambda_{t-1}}, R~ = r e^{Lambda_t}
             x1[q] *= expf(lt[q]);
             x2[q] *= expf(lt[q + 1]);
-          } else {         // B~ = b e^{-Lambda_t}, K~ = k e^{-Lambda_t}
+          } else {        // B~ = b e^{-Lambda_t}, K~ = k e^{-Lambda_t}
             const float dn = expf(-lt[q + 1]);
             x1[q] *= dn;
             x2[q] *= dn;
@@ -556,20 +564,17 @@ wkv7_tc_bwd_grad_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_co
     }
     __syncthreads();  // raw tiles dead from here on
     WKV_TRACE(34)
-    {  // S0^T (row j = tid < 64, K = i) and (dS D_L)^T (row j, threads 64..127): column loads from global
-      const int j = tid & 63;
-      const float* src = tid < 64 ? S0g : wk + WK_DS * MAT;
-      uint8_t* dst = tid < 64 ? S0T : DST;
-      const float sc = tid < 64 ? 1.f : DL[j];
+    {  // S0^T (row j, K = i) and (dS D_L)^T (row j): column loads from global, 32 values per thread
+      const int j = tid & 63, second = (tid >> 6) & 1, i0 = 32 * (tid >> 7);
+      const float* src = second ? wk + WK_DS * MAT : S0g;
+      uint8_t* dst = second ? DST : S0T;
+      const float sc = second ? DL[j] : 1.f;
+      float col[32];
 #pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {  // 32 independent column loads in flight, then the row of the tile
-        float col[32];
+      for (int i = 0; i < 32; ++i) col[i] = __ldg(src + (i0 + i) * N + j);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) col[i] = __ldg(src + (32 * h2 + i) * N + j);
-#pragma unroll
-        for (int i = 0; i < 32; i += 4)
-          put4(dst, 64, j, 32 * h2 + i, col[i] * sc, col[i + 1] * sc, col[i + 2] * sc, col[i + 3] * sc);
-      }
+      for (int i = 0; i < 32; i += 4)
+        put4(dst, 64, j, i0 + i, col[i] * sc, col[i + 1] * sc, col[i + 2] * sc, col[i + 3] * sc);
     }
     tc_sync();
     if (tid == 0) {  // [dZ S0; dY S0] (cols 128..191) and [E; F] = [U; V] (dS D_L) (cols 256..319)
@@ -593,38 +598,35 @@ wkv7_tc_bwd_grad_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_co
   WKV_TRACE(36)
   // dM stage tiles. Stage 1: SA = [dM_ab; dM_rb] (rows t, K = s), SB = [dM_ab^T; dM_ak^T] (rows s, K = t).
   //                 Stage 2: SA = [dM_ak; dM_rk],               SB = [dM_rb^T; dM_rk^T].
+  // Thread: row 32 quarter + lane of the 128 rows, columns [32 colh, 32 colh + 32) of each 64-column block.
+  const int row = 32 * quarter + (tid & 31), t = row & 63, s0 = 32 * colh;
+  const uint32_t trow = tmem + ((uint32_t)(32 * quarter) << 16);
 #pragma unroll 1
   for (int stage_ = 0; stage_ < 2 && ok; ++stage_) {
     {
-      float d[64];
-      const int t = tid & 63;
-      const int lim = tid < 64 ? t : t + 1;  // strict for the a~ rows, inclusive for the r~ rows
-      if (stage_ == 0) {
-        tmem_row64(tmem, warp, 0, d);  // dM_ab (t < 64) / dM_rb
+      float d[32];
+      const bool lo = row < 64;
+      const int lim = lo ? t : t + 1;  // strict for the a~ rows, inclusive for the r~ rows
+      sm100::tmem_ld32(trow + (stage_ ? 64 : 0) + s0, d);  // stage 0: dM_ab / dM_rb; stage 1: dM_ak / dM_rk
+      sm100::tmem_wait_ld();
 #pragma unroll
-        for (int s = 0; s < 64; s += 4)
-          put4(SA, 128, tid, s, s < lim ? d[s] : 0.f, s + 1 < lim ? d[s + 1] : 0.f, s + 2 < lim ? d[s + 2] : 0.f,
-               s + 3 < lim ? d[s + 3] : 0.f);
-        if (tid < 64) {
+      for (int u = 0; u < 32; u += 4) {
+        const int s = s0 + u;
+        put4(SA, 128, row, s, s < lim ? d[u] : 0.f, s + 1 < lim ? d[u + 1] : 0.f, s + 2 < lim ? d[u + 2] : 0.f,
+             s + 3 < lim ? d[u + 3] : 0.f);
+      }
+      // transposes: stage 0 from the a~ rows (dM_ab, then dM_ak), stage 1 from the r~ rows (dM_rk, then dM_rb)
+      const bool owner = stage_ == 0 ? lo : !lo;
+      if (owner) {
 #pragma unroll
-          for (int s = 0; s < 64; ++s) put1(SB, 128, s, t, s < lim ? d[s] : 0.f);
-          tmem_row64(tmem, warp, 64, d);  // dM_ak
+        for (int u = 0; u < 32; ++u) put1(SB, 128, (stage_ ? 64 : 0) + s0 + u, t, s0 + u < lim ? d[u] : 0.f);
+      }
+      // warp-collective TMEM load outside the per-row condition
+      sm100::tmem_ld32(trow + (stage_ ? 0 : 64) + s0, d);
+      sm100::tmem_wait_ld();
+      if (owner) {
 #pragma unroll
-          for (int s = 0; s < 64; ++s) put1(SB, 128, 64 + s, t, s < lim ? d[s] : 0.f);
-        }
-      } else {
-        tmem_row64(tmem, warp, 64, d);  // dM_ak / dM_rk
-#pragma unroll
-        for (int s = 0; s < 64; s += 4)
-          put4(SA, 128, tid, s, s < lim ? d[s] : 0.f, s + 1 < lim ? d[s + 1] : 0.f, s + 2 < lim ? d[s + 2] : 0.f,
-               s + 3 < lim ? d[s + 3] : 0.f);
-        if (tid >= 64) {
-#pragma unroll
-          for (int s = 0; s < 64; ++s) put1(SB, 128, 64 + s, t, s < lim ? d[s] : 0.f);
-          tmem_row64(tmem, warp, 0, d);  // dM_rb
-#pragma unroll
-          for (int s = 0; s < 64; ++s) put1(SB, 128, s, t, s < lim ? d[s] : 0.f);
-        }
+        for (int u = 0; u < 32; ++u) put1(SB, 128, (stage_ ? 0 : 64) + s0 + u, t, s0 + u < lim ? d[u] : 0.f);
       }
     }
     tc_sync();
@@ -645,24 +647,23 @@ wkv7_tc_bwd_grad_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_co
   }
   if (ok) {
     WKV_TRACE(41)
-    // ---- row epilogue: raw gradients and the dLambda terms (thread = row t of its half). The raw input rows come
-    // in as 16-byte loads, the gradient rows leave as 16-byte stores, and the decay-gradient factor of w is formed
-    // here (row-wise) for the column pass.
-    const int t = tid & 63, tg = c * L + t;
-    const bool lo = tid < 64;  // rows of a~ / b~ (da, db) vs r~ / k~ (dr, dk)
+    // ---- row epilogue: raw gradients and the dLambda terms (thread = row t of its half, 32 columns). The raw input
+    // rows come in as 16-byte loads, the gradient rows leave as 16-byte stores, and the decay-gradient factor of w
+    // is formed here (row-wise) for the column pass.
+    const int tg = c * L + t;
+    const bool lo = row < 64;  // rows of a~ / b~ (da, db) vs r~ / k~ (dr, dk)
     const bool valid = tg < T;
     const long go = (((long)bb * T + (valid ? tg : 0)) * H + h) * N;
-    const uint32_t row = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
     const __nv_bfloat16* src1 = lo ? pa : pr;  // a / r
     const __nv_bfloat16* src2 = lo ? pb : pk;  // b / k
     float* out1 = lo ? da : dr;
     float* out2 = lo ? db : dk;
-#pragma unroll 1
-    for (int half = 0; half < 2; ++half) {
+    const int half = colh;
+    {
       float d1[32], d2[32], d3[32], x1[32], x2[32];
-      sm100::tmem_ld32(row + 128 + 32 * half, d1);  // dA~ / dR~
-      sm100::tmem_ld32(row + 192 + 32 * half, d2);  // dB~' / dK~'
-      sm100::tmem_ld32(row + 256 + 32 * half, d3);  // E / F
+      sm100::tmem_ld32(trow + 128 + 32 * half, d1);  // dA~ / dR~
+      sm100::tmem_ld32(trow + 192 + 32 * half, d2);  // dB~' / dK~'
+      sm100::tmem_ld32(trow + 256 + 32 * half, d3);  // E / F
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         if (valid) {
@@ -729,39 +730,40 @@ wkv7_tc_bwd_grad_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_co
     }
     __syncthreads();
     WKV_TRACE(42)
-    // ---- column pass, key j: thread j and 64 + j split every column sum in two halves.
+    // ---- column pass, key j: threads j + 64 q split every column sum in four parts of 16 steps.
     {
-      const int j = tid & 63, hi = tid >> 6;
+      const int j = tid & 63, q = tid >> 6, r0 = 16 * q;
       const float* dS = wk + WK_DS * MAT;
-      float ds[32], sv[32];
+      float ds[16], sv[16];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        ds[i] = __ldg(dS + (32 * hi + i) * N + j);
-        sv[i] = __ldg(S0g + (32 * hi + i) * N + j);
+      for (int i = 0; i < 16; ++i) {
+        ds[i] = __ldg(dS + (r0 + i) * N + j);
+        sv[i] = __ldg(S0g + (r0 + i) * N + j);
       }
       float acc = 0.f, eacc = 0.f;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) acc += ds[i] * sv[i];
+      for (int i = 0; i < 16; ++i) acc += ds[i] * sv[i];
 #pragma unroll
-      for (int s2 = 0; s2 < 32; ++s2) eacc += EA[poff(32 * hi + s2, j)] + EB[poff(32 * hi + s2, j)];
-      // g_t = (dr r - dk k) + (-db b) + (da a)_{t+1} for this thread's 32 steps, as suffix sums
-      float g[32];
+      for (int s2 = 0; s2 < 16; ++s2) eacc += EA[poff(r0 + s2, j)] + EB[poff(r0 + s2, j)];
+      // g_t = (dr r - dk k) + (-db b) + (da a)_{t+1} for this thread's 16 steps, as suffix sums
+      float g[16];
 #pragma unroll
-      for (int u = 0; u < 32; ++u) {
-        const int tt = 32 * hi + u;
+      for (int u = 0; u < 16; ++u) {
+        const int tt = r0 + u;
         g[u] = PA[poff(tt, j)] + PB[poff(tt, j)] + (tt < 63 ? QA[poff(tt + 1, j)] : 0.f);
       }
 #pragma unroll
-      for (int u = 30; u >= 0; --u) g[u] += g[u + 1];
-      colsum[hi * 64 + j] = acc * DL[j] + eacc;  // the chunk-end term, in two halves
-      colsum[128 + hi * 64 + j] = g[0];          // this half's total of g
+      for (int u = 14; u >= 0; --u) g[u] += g[u + 1];
+      colsum[q * 64 + j] = acc * DL[j] + eacc;  // the chunk-end term, in four parts
+      colsum[256 + q * 64 + j] = g[0];         // this part's total of g
       __syncthreads();
       // dLogd_t = (sum_i dS S0 D_L + sum_s (E b~ + F k~)) + sum_{t' >= t} g_t'
-      const float base = colsum[j] + colsum[64 + j] + (hi ? 0.f : colsum[128 + 64 + j]);
+      float base = colsum[j] + colsum[64 + j] + colsum[128 + j] + colsum[192 + j];
+      for (int p2 = q + 1; p2 < 4; ++p2) base += colsum[256 + p2 * 64 + j];
 #pragma unroll
-      for (int u = 0; u < 32; ++u) {
-        const int tgg = c * L + 32 * hi + u;
-        if (tgg < T) dw[(((long)bb * T + tgg) * H + h) * N + j] = (g[u] + base) * FW[poff(32 * hi + u, j)];
+      for (int u = 0; u < 16; ++u) {
+        const int tgg = c * L + r0 + u;
+        if (tgg < T) dw[(((long)bb * T + tgg) * H + h) * N + j] = (g[u] + base) * FW[poff(r0 + u, j)];
       }
     }
   }
@@ -842,7 +844,7 @@ extern "C" cudaError_t rt_wkv7_tc_backward(int B, int T, int H, const void* r, c
                                                                           T, H, chunks);
   RT_CUDA_CHECK(cudaGetLastError());
   RT_CUDA_CHECK(cudaFuncSetAttribute(wkv7_tc_bwd_grad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kb::SMEM));
-  wkv7_tc_bwd_grad_kernel<<<dim3(chunks, H, B), 128, kb::SMEM, stream>>>(
+  wkv7_tc_bwd_grad_kernel<<<dim3(chunks, H, B), GRAD_THREADS, kb::SMEM, stream>>>(
       mr, mw, mk, mv, ma, mb, mdy, mwk, (const __nv_bfloat16*)r, (const __nv_bfloat16*)w, (const __nv_bfloat16*)k,
       (const __nv_bfloat16*)a, (const __nv_bfloat16*)b, ckpt, work, dr, dw, dk, da, db, T, H, chunks);
   return cudaGetLastError();
