@@ -82,7 +82,7 @@ def main():
         st.flat.grad.copy_(g)
         st.stats.fill_(1.0)
 
-    norm2 = torch.zeros(1, device=dev)
+    norm2 = torch.zeros(native().flat_adamw_scratch(), device=dev)  # optimizer scratch (partial norms)
 
     def nccl():
         st.flat.grad.copy_(g)
@@ -110,10 +110,14 @@ def main():
                     rows.setdefault(evt.name[:48], []).append(evt.device_time)
             for name, ts in sorted(rows.items(), key=lambda kv: -sum(kv[1])):
                 print(json.dumps({"kernel": name, "calls": len(ts), "avg_us": sum(ts) / len(ts)}), flush=True)
+    from bench import ClockSampler  # nvidia-smi clocks and throttle reasons of this rank's GPU while timing
+    uuid = str(torch.cuda.get_device_properties(dev).uuid)
+    sampler = ClockSampler(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
     base = timed(copy_only, a.iters, topo)
     frac = (N - 1) / N
     link_ms = 6 * n * frac / (LINK_GBS * 1e9) * 1e3
     t_nccl = None
+    results = []
     for mode in a.modes.split(","):
         ex.fused = mode == "fused"
         for blocks in [int(b) for b in a.blocks.split(",")]:
@@ -122,11 +126,14 @@ def main():
             ex.check()
             if t_nccl is None:
                 t_nccl = timed(nccl, a.iters, topo) - base
-            if topo.rank == 0:
-                print(json.dumps({"bench": "layer_exchange", "n_gpus": N, "numel": n, "peer_ms": t_peer,
-                                  "nccl_ms": t_nccl, "nvlink_roofline_ms": link_ms,
-                                  "peer_fraction_of_roofline": link_ms / t_peer, "speedup_vs_nccl": t_nccl / t_peer,
-                                  "blocks": blocks, "mode": mode}), flush=True)
+            results.append({"bench": "layer_exchange", "n_gpus": N, "numel": n, "peer_ms": t_peer,
+                            "nccl_ms": t_nccl, "nvlink_roofline_ms": link_ms,
+                            "peer_fraction_of_roofline": link_ms / t_peer, "speedup_vs_nccl": t_nccl / t_peer,
+                            "blocks": blocks, "mode": mode})
+    clocks = sampler.stop()
+    if topo.rank == 0:
+        for line in results:
+            print(json.dumps(line | {"clocks_rank0": clocks}), flush=True)
     ex.close()
     topo.close()
 

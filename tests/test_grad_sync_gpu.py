@@ -26,7 +26,14 @@ def _port():
         return s.getsockname()[1]
 
 
-def _launch(mode, nproc=2):
+def _ranks():
+    """Ranks per test: THESEUS_TEST_RANKS (up to the visible GPUs), else 2."""
+    want = int(os.environ.get("THESEUS_TEST_RANKS", "2"))
+    return max(2, min(want, torch.cuda.device_count()))
+
+
+def _launch(mode, nproc=None):
+    nproc = nproc or _ranks()
     env = dict(os.environ, NCCL_NVLS_ENABLE="0", PYTHONPATH=str(ROOT))
     cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            f"--nproc-per-node={nproc}", "--master-addr=127.0.0.1", f"--master-port={_port()}", __file__, mode]
