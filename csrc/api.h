@@ -82,8 +82,9 @@ cudaError_t rt_gdn_forward(const void* qkv, long row_stride, const void* a, cons
 // TimeMix student stages and the flat optimizer (student_ops.cu).
 cudaError_t rt_tm_mix(const void* x, const void* shift, const float* coef, void* out, int B, int T, int C,
                       cudaStream_t s);
+long rt_tm_mix_bwd_scratch(int B, int T, int C);
 cudaError_t rt_tm_mix_bwd(const void* x, const void* shift, const void* dmix, float* dcoef, int B, int T, int C,
-                          cudaStream_t s);
+                          float* scratch, cudaStream_t s);
 cudaError_t rt_tm_pre_wkv(const void* k, const void* lw, const void* la, const float* w0, const float* a0,
                           const float* k_k, const float* k_a, void* w_in, void* k_in, void* a_in, void* b_in,
                           long rows, int H, int N, cudaStream_t s);

@@ -354,7 +354,10 @@ void tm_mix(at::Tensor x, at::Tensor shift, at::Tensor coef, at::Tensor out) {
 }
 void tm_mix_bwd(at::Tensor x, at::Tensor shift, at::Tensor dmix, at::Tensor dcoef) {
   c10::cuda::CUDAGuard guard(x.device());
-  check_cuda(rt_tm_mix_bwd(PTR(x), PTR(shift), PTR(dmix), FPTR(dcoef), x.size(0), x.size(1), x.size(2), stream_of(x)),
+  const long n = rt_tm_mix_bwd_scratch(x.size(0), x.size(1), x.size(2));
+  auto scratch = n > 0 ? at::empty({n}, x.options().dtype(at::kFloat)) : at::Tensor();
+  check_cuda(rt_tm_mix_bwd(PTR(x), PTR(shift), PTR(dmix), FPTR(dcoef), x.size(0), x.size(1), x.size(2),
+                           n > 0 ? scratch.data_ptr<float>() : nullptr, stream_of(x)),
              "tm_mix_bwd");
 }
 void tm_pre_wkv(at::Tensor k, at::Tensor lw, at::Tensor la, at::Tensor w0, at::Tensor a0, at::Tensor k_k,

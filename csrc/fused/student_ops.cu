@@ -70,6 +70,83 @@ __global__ void mix_bwd_kernel(const bf16* __restrict__ x, const bf16* __restric
   for (int n = 0; n < 6; ++n) atomicAdd(&dcoef[n * C + c], acc[n]);
 }
 
+// Vectorised forms (C % 8 == 0, 16-byte aligned rows): a thread takes eight columns of a row with 16-byte loads
+// and stores. The backward sums each band of MIXV_ROWS rows into a partial row (no atomics), and a second kernel
+// adds the partials in band order, so dcoef does not depend on scheduling.
+constexpr int MIXV_ROWS = 16;
+
+__global__ void mix_vec_kernel(const bf16* __restrict__ x, const bf16* __restrict__ shift,
+                               const float* __restrict__ coef, bf16* __restrict__ out, int T, int C, long M) {
+  const int C8 = C / 8;
+  const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= M * C8) return;
+  const long row = idx / C8;
+  const int c = (int)(idx % C8) * 8;
+  const int t = row % T;
+  const long b = row / T;
+  float xv[8], pv[8], delta[8];
+  rt::unpack8(__ldg(reinterpret_cast<const uint4*>(x + row * C + c)), xv);
+  rt::unpack8(__ldg(reinterpret_cast<const uint4*>(t ? x + (row - 1) * C + c : shift + b * C + c)), pv);
+#pragma unroll
+  for (int u = 0; u < 8; ++u) delta[u] = bf(pv[u] - xv[u]);
+#pragma unroll
+  for (int n = 0; n < 6; ++n) {
+    const float4 c0 = __ldg(reinterpret_cast<const float4*>(coef + n * C + c));
+    const float4 c1 = __ldg(reinterpret_cast<const float4*>(coef + n * C + c + 4));
+    const float cf[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+    float o[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) o[u] = xv[u] + delta[u] * cf[u];
+    *reinterpret_cast<uint4*>(out + (long)n * M * C + row * C + c) = rt::pack8(o);
+  }
+}
+
+// partial[band][n][c] = sum over the band's rows of dmix_n[row][c] * delta[row][c]; grid (ceil(C/8/128), bands)
+__global__ void mix_bwd_part_kernel(const bf16* __restrict__ x, const bf16* __restrict__ shift,
+                                    const bf16* __restrict__ dmix, float* __restrict__ partial, int T, int C, long M) {
+  const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (c >= C) return;
+  const long r0 = (long)blockIdx.y * MIXV_ROWS;
+  const long r1 = min(M, r0 + MIXV_ROWS);
+  float acc[6][8];
+#pragma unroll
+  for (int n = 0; n < 6; ++n)
+#pragma unroll
+    for (int u = 0; u < 8; ++u) acc[n][u] = 0.f;
+#pragma unroll 2
+  for (long row = r0; row < r1; ++row) {
+    const int t = row % T;
+    const long b = row / T;
+    float xv[8], pv[8], dm[6][8];
+    rt::unpack8(__ldg(reinterpret_cast<const uint4*>(x + row * C + c)), xv);
+    rt::unpack8(__ldg(reinterpret_cast<const uint4*>(t ? x + (row - 1) * C + c : shift + b * C + c)), pv);
+#pragma unroll
+    for (int n = 0; n < 6; ++n)
+      rt::unpack8(__ldcs(reinterpret_cast<const uint4*>(dmix + (long)n * M * C + row * C + c)), dm[n]);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const float delta = bf(pv[u] - xv[u]);
+#pragma unroll
+      for (int n = 0; n < 6; ++n) acc[n][u] += dm[n][u] * delta;
+    }
+  }
+  float* dst = partial + (long)blockIdx.y * 6 * C;
+#pragma unroll
+  for (int n = 0; n < 6; ++n) {
+    *reinterpret_cast<float4*>(dst + n * C + c) = make_float4(acc[n][0], acc[n][1], acc[n][2], acc[n][3]);
+    *reinterpret_cast<float4*>(dst + n * C + c + 4) = make_float4(acc[n][4], acc[n][5], acc[n][6], acc[n][7]);
+  }
+}
+
+__global__ void mix_bwd_sum_kernel(const float* __restrict__ partial, float* __restrict__ dcoef, int bands,
+                                   int C6) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= C6) return;
+  float s = 0.f;
+  for (int b = 0; b < bands; ++b) s += partial[(long)b * C6 + i];
+  dcoef[i] += s;
+}
+
 // ---------------------------------------------------------------- pre-WKV
 // One warp per (row, head); N <= 128 (4 values per lane).
 struct PreParams {
@@ -560,16 +637,44 @@ int grid_for(long n, int threads, int cap = 148 * 8) {
 
 }  // namespace
 
+namespace {
+bool mix_vectorizable(const void* x, const void* shift, const void* other, const float* coef, int C) {
+  return C % 8 == 0 &&
+         ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(shift) | reinterpret_cast<uintptr_t>(other) |
+           reinterpret_cast<uintptr_t>(coef)) & 15) == 0;
+}
+}  // namespace
+
 extern "C" cudaError_t rt_tm_mix(const void* x, const void* shift, const float* coef, void* out, int B, int T, int C,
                                  cudaStream_t s) {
   const long M = (long)B * T;
+  if (mix_vectorizable(x, shift, out, coef, C)) {
+    const long items = M * (C / 8);
+    mix_vec_kernel<<<(items + 255) / 256, 256, 0, s>>>((const bf16*)x, (const bf16*)shift, coef, (bf16*)out, T, C,
+                                                        M);
+    return cudaGetLastError();
+  }
   mix_kernel<<<dim3((C + 255) / 256, M), 256, 0, s>>>((const bf16*)x, (const bf16*)shift, coef, (bf16*)out, T, C, M);
   return cudaGetLastError();
 }
 
-extern "C" cudaError_t rt_tm_mix_bwd(const void* x, const void* shift, const void* dmix, float* dcoef, int B, int T,
-                                     int C, cudaStream_t s) {
+// Floats of scratch rt_tm_mix_bwd needs for its partial sums (0: the atomic fallback needs none).
+extern "C" long rt_tm_mix_bwd_scratch(int B, int T, int C) {
   const long M = (long)B * T;
+  return C % 8 == 0 ? ((M + MIXV_ROWS - 1) / MIXV_ROWS) * 6L * C : 0;
+}
+
+extern "C" cudaError_t rt_tm_mix_bwd(const void* x, const void* shift, const void* dmix, float* dcoef, int B, int T,
+                                     int C, float* scratch, cudaStream_t s) {
+  const long M = (long)B * T;
+  if (scratch && mix_vectorizable(x, shift, dmix, dcoef, C) && (reinterpret_cast<uintptr_t>(scratch) & 15) == 0) {
+    const int bands = (int)((M + MIXV_ROWS - 1) / MIXV_ROWS);
+    mix_bwd_part_kernel<<<dim3((C / 8 + 127) / 128, bands), 128, 0, s>>>((const bf16*)x, (const bf16*)shift,
+                                                                        (const bf16*)dmix, scratch, T, C, M);
+    RT_CUDA_CHECK(cudaGetLastError());
+    mix_bwd_sum_kernel<<<(6 * C + 255) / 256, 256, 0, s>>>(scratch, dcoef, bands, 6 * C);
+    return cudaGetLastError();
+  }
   mix_bwd_kernel<<<dim3((C + 255) / 256, (M + MIX_ROWS - 1) / MIX_ROWS), 256, 0, s>>>(
       (const bf16*)x, (const bf16*)shift, (const bf16*)dmix, dcoef, T, C, M);
   return cudaGetLastError();

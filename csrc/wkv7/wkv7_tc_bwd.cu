@@ -53,15 +53,6 @@ RT_DEVICE bool wait_all(uint64_t* bar, uint32_t parity) {
   return __syncthreads_and(ok ? 1 : 0) != 0;
 }
 
-// Row `row` of a K-major tile of `rows` rows from 64 fp32 values in global memory (rounded to tf32).
-RT_DEVICE void tile_row_from_global(uint8_t* tile, int rows, int row, const float* src) {
-#pragma unroll 4
-  for (int k = 0; k < 64; k += 4) {
-    const float4 x = __ldg(reinterpret_cast<const float4*>(src + k));
-    put4(tile, rows, row, k, x.x, x.y, x.z, x.w);
-  }
-}
-
 // ---------------------------------------------------------------- 1: reverse scan dS <- dS G^T + dY^T Q
 // grid (B*H, 8 row blocks of 8 value rows), 128 threads: thread = column j and rows r0..r0+3 of the block.
 constexpr int BS_ROWS = 8;
@@ -164,16 +155,22 @@ constexpr int DYT = 185 * KB;   // dY^T (64 rows)
 constexpr int SMEM = 201 * KB + 1024;
 }  // namespace ka
 
-__global__ void __launch_bounds__(128, 1)
+// 256 threads: the tile and epilogue phases split their rows or TMEM columns over two threads (warps w and w + 4
+// share a TMEM lane quarter); the two triangular solves keep one right-hand-side column per thread on the first
+// 128 threads.
+constexpr int STATE_THREADS = 256;
+
+__global__ void __launch_bounds__(STATE_THREADS, 1)
 wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_constant__ CUtensorMap m_w,
                          const __grid_constant__ CUtensorMap m_k, const __grid_constant__ CUtensorMap m_v,
                          const __grid_constant__ CUtensorMap m_a, const __grid_constant__ CUtensorMap m_b,
-                         const __grid_constant__ CUtensorMap m_dy, const float* __restrict__ ckpt, float* __restrict__ work, float* __restrict__ dv, int T,
-                         int H, int chunks) {
+                         const __grid_constant__ CUtensorMap m_dy, const float* __restrict__ ckpt,
+                         float* __restrict__ work, float* __restrict__ dv, int T, int H, int chunks) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
   const int c = blockIdx.x, h = blockIdx.y, bb = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5;
+  const int quarter = warp & 3, colh = warp >> 2;
   uint8_t* Rr = sm + ka::RAW;
   uint8_t *Rw = Rr + 8 * KB, *Rk = Rr + 16 * KB, *Rv = Rr + 24 * KB, *Ra = Rr + 32 * KB, *Rb = Rr + 40 * KB;
   uint8_t* Rdy = Rr + 48 * KB;
@@ -185,11 +182,13 @@ wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_c
   float* MPL = reinterpret_cast<float*>(sm + 32 * KB);
   float* ZP = reinterpret_cast<float*>(X1);             // Zf^T, plain (row i = column i of Zf)
   float* DUP = reinterpret_cast<float*>(X1 + 16 * KB);  // dU^T, plain
+  float* carry = reinterpret_cast<float*>(BKH);         // Lambda carries (before BKH is built)
   uint8_t *MRT = X2, *MAKT = sm + 129 * KB, *DZT = sm;
   const long bh = (long)bb * H + h, ch = bh * chunks + c;
   const float* S0g = ckpt + (bh * (chunks + 1) + c) * MAT;
   float* wk = work + ch * WK_MATS * MAT;
   const int nvalid = min(L, T - c * L);
+  const uint32_t trow_off = (uint32_t)(32 * quarter) << 16;
   WKV_TRACE_BEGIN
 
   if (tid == 0) {
@@ -222,16 +221,16 @@ wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_c
   WKV_TRACE(16)
   if (ok) {
     float* DLs = reinterpret_cast<float*>(sm + ka::MISC + 64);
-    build_lambda(Rw, lam, DLs, nvalid, tid);
+    build_lambda_nt<STATE_THREADS>(Rw, lam, carry, nvalid, tid);
     if (tid < 64) DLs[tid] = expf(lam[poff(63, tid)]);
     __syncthreads();
-    {  // X1 (A~ / R~), X2 (B~ / K~), BKH (B^ = B~ D_L / K^ = K~ D_L): row tid, eight keys at a time
-      const int t = tid & 63;
-      const bool hi = tid >= 64;
+    {  // X1 (A~ / R~), X2 (B~ / K~), BKH (B^ = B~ D_L / K^ = K~ D_L): row tid % 128, 32 keys, eight at a time
+      const int r = tid & 127, t = r & 63, j1 = 32 * (tid >> 7);
+      const bool hi = r >= 64;
       const uint8_t* s1 = hi ? Rr : Ra;
       const uint8_t* s2 = hi ? Rk : Rb;
 #pragma unroll 1
-      for (int j0 = 0; j0 < 64; j0 += 8) {
+      for (int j0 = j1; j0 < j1 + 32; j0 += 8) {
         float x1[8], x2[8], lt[8], lp[8];
         raw8(s1, t, j0, x1);
         raw8(s2, t, j0, x2);
@@ -253,19 +252,19 @@ wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_c
         }
 #pragma unroll
         for (int q = 0; q < 8; q += 4) {
-          put4(X1, 128, tid, j0 + q, x1[q], x1[q + 1], x1[q + 2], x1[q + 3]);
-          put4(X2, 128, tid, j0 + q, x2[q], x2[q + 1], x2[q + 2], x2[q + 3]);
-          put4(BKH, 128, tid, j0 + q, xh[q], xh[q + 1], xh[q + 2], xh[q + 3]);
+          put4(X1, 128, r, j0 + q, x1[q], x1[q + 1], x1[q + 2], x1[q + 3]);
+          put4(X2, 128, r, j0 + q, x2[q], x2[q + 1], x2[q + 2], x2[q + 3]);
+          put4(BKH, 128, r, j0 + q, xh[q], xh[q + 1], xh[q + 2], xh[q + 3]);
         }
       }
     }
     WKV_TRACE(17)
-    {  // V^T (row i < 64), dY^T (row i, threads 64..127)
-      const int i = tid & 63;
-      uint8_t* dst = tid < 64 ? VT : DYT;
-      const uint8_t* src = tid < 64 ? Rv : Rdy;
+    {  // V^T (row i, threads with bit 6 clear), dY^T (row i, bit 6 set); 32 steps per thread
+      const int i = tid & 63, s1 = 32 * (tid >> 7);
+      uint8_t* dst = (tid & 64) ? DYT : VT;
+      const uint8_t* src = (tid & 64) ? Rdy : Rv;
 #pragma unroll 1
-      for (int s0 = 0; s0 < 64; s0 += 16) {
+      for (int s0 = s1; s0 < s1 + 32; s0 += 16) {
         float x[16];
 #pragma unroll
         for (int q = 0; q < 16; ++q) x[q] = raw(src, s0 + q, i);
@@ -281,9 +280,17 @@ wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_c
                      false);
       sm100::mma_commit(&bars[1]);
     }
-    // raw tiles and Lambda are dead: S0 and dS rows (rounded) by the threads
-    if (tid < 64) tile_row_from_global(S0t, 64, tid, S0g + tid * N);
-    else tile_row_from_global(DSt, 64, tid - 64, wk + WK_DS * MAT + (tid - 64) * N);
+    // raw tiles and Lambda are dead: S0 and dS rows (rounded) by the threads, half a row each
+    {
+      const int r = tid & 127, k0 = 32 * (tid >> 7);
+      uint8_t* tile = r < 64 ? S0t : DSt;
+      const float* src = (r < 64 ? S0g : wk + WK_DS * MAT) + (r & 63) * N;
+#pragma unroll
+      for (int k = k0; k < k0 + 32; k += 4) {
+        const float4 v4 = __ldg(reinterpret_cast<const float4*>(src + k));
+        put4(tile, 64, r & 63, k, v4.x, v4.y, v4.z, v4.w);
+      }
+    }
     stage = 2;
     ok = wait_all(&bars[1], mph);
     mph ^= 1;
@@ -291,29 +298,36 @@ wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_c
   }
   if (ok) {
     WKV_TRACE(19)
-    // ---- epilogue 1: M_ab (strict) -> MPL (plain), M_ak (strict) -> MAK rows; [M_rb^T; M_rk^T] -> MRT
-    //      (transposed, from rows t >= 64)
-    float d[64];
-    const int t = tid & 63;
-    if (tid < 64) {
-      tmem_row64(tmem, warp, 0, d);
+    // ---- epilogue 1 (32 columns of each 64-column block per thread): M_ab (strict) -> MPL (plain), M_ak (strict)
+    //      -> MAK rows; [M_rb^T; M_rk^T] -> MRT (transposed, from rows t >= 64)
+    const int row = 32 * quarter + (tid & 31), t = row & 63, s0 = 32 * colh;
+    float d[32];
+    sm100::tmem_ld32(tmem + trow_off + s0, d);  // M_ab / M_rb
+    sm100::tmem_wait_ld();
+    if (row < 64) {
 #pragma unroll
-      for (int s = 0; s < 64; s += 4)
+      for (int u = 0; u < 32; u += 4) {
+        const int s = s0 + u;
         *reinterpret_cast<float4*>(&MPL[poff(t, s)]) =
-            make_float4(s < t ? d[s] : 0.f, s + 1 < t ? d[s + 1] : 0.f, s + 2 < t ? d[s + 2] : 0.f,
-                        s + 3 < t ? d[s + 3] : 0.f);
-      tmem_row64(tmem, warp, 64, d);
-#pragma unroll
-      for (int s = 0; s < 64; s += 4)
-        put4(MAK, 64, t, s, s < t ? d[s] : 0.f, s + 1 < t ? d[s + 1] : 0.f, s + 2 < t ? d[s + 2] : 0.f,
-             s + 3 < t ? d[s + 3] : 0.f);
+            make_float4(s < t ? d[u] : 0.f, s + 1 < t ? d[u + 1] : 0.f, s + 2 < t ? d[u + 2] : 0.f,
+                        s + 3 < t ? d[u + 3] : 0.f);
+      }
     } else {
-      tmem_row64(tmem, warp, 0, d);
 #pragma unroll
-      for (int s = 0; s < 64; ++s) put1(MRT, 128, s, t, s <= t ? d[s] : 0.f);
-      tmem_row64(tmem, warp, 64, d);
+      for (int u = 0; u < 32; ++u) put1(MRT, 128, s0 + u, t, s0 + u <= t ? d[u] : 0.f);
+    }
+    sm100::tmem_ld32(tmem + trow_off + 64 + s0, d);  // M_ak / M_rk
+    sm100::tmem_wait_ld();
+    if (row < 64) {
 #pragma unroll
-      for (int s = 0; s < 64; ++s) put1(MRT, 128, 64 + s, t, s <= t ? d[s] : 0.f);
+      for (int u = 0; u < 32; u += 4) {
+        const int s = s0 + u;
+        put4(MAK, 64, t, s, s < t ? d[u] : 0.f, s + 1 < t ? d[u + 1] : 0.f, s + 2 < t ? d[u + 2] : 0.f,
+             s + 3 < t ? d[u + 3] : 0.f);
+      }
+    } else {
+#pragma unroll
+      for (int u = 0; u < 32; ++u) put1(MRT, 128, 64 + s0 + u, t, s0 + u <= t ? d[u] : 0.f);
     }
     tc_sync();
     // ---- MMA-Z (cols 128..191): [A~ S0^T + M_ak V; *];  MMA-dU (cols 192..255): [dU; dV'] =
@@ -336,28 +350,30 @@ wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_c
   }
   if (ok) {
     WKV_TRACE(20)
-    // ---- epilogue 2: Zf and dU rows t (threads t < 64) -> columns t of the plain Zf^T, dU^T; M_ak^T
-    float d[64];
-    if (tid < 64) {
-      const uint32_t trow = tmem + ((uint32_t)(32 * warp) << 16);
+    // ---- epilogue 2: Zf and dU rows t (lanes 0..63; 32 columns per thread) -> columns t of the plain Zf^T, dU^T;
+    //      M_ak row t -> column t of M_ak^T
+    const int row = 32 * quarter + (tid & 31), s0 = 32 * colh;
+    if (quarter < 2) {
+      float e[32];
 #pragma unroll 1
-      for (int part = 0; part < 4; ++part) {  // Zf cols 128..191, dU cols 192..255, 32 at a time
-        float e[32];
-        sm100::tmem_ld32(trow + 128 + 32 * part, e);
+      for (int part = 0; part < 2; ++part) {  // Zf cols 128.., dU cols 192..
+        sm100::tmem_ld32(tmem + trow_off + 128 + 64 * part + s0, e);
         sm100::tmem_wait_ld();
-        float* dst = part < 2 ? ZP : DUP;
+        float* dst = part ? DUP : ZP;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) dst[poff(32 * (part & 1) + i, tid)] = e[i];
+        for (int i = 0; i < 32; ++i) dst[poff(s0 + i, row)] = e[i];
       }
-      tmem_row64(tmem, warp, 64, d);  // M_ak row t (still in TMEM) -> M_ak^T column t
+      sm100::tmem_ld32(tmem + trow_off + 64 + s0, e);  // M_ak row t (still in TMEM)
+      sm100::tmem_wait_ld();
 #pragma unroll
-      for (int s = 0; s < 64; ++s) put1(MAKT, 64, s, tid, s < tid ? d[s] : 0.f);
+      for (int u = 0; u < 32; ++u) put1(MAKT, 64, s0 + u, row, s0 + u < row ? e[u] : 0.f);
     }
     __syncthreads();
     WKV_TRACE(21)
     // ---- U = T Zf (threads i < 64: column i, forward substitution), dZ = T^T dU (threads 64 + i: column i, back
     //      substitution); U and dZ (tf32) to the work record, dZ columns as rows of dZ^T for dV
-    {
+    if (tid < 128) {
+      float d[64];
       const int i = tid & 63;
       const float* src = tid < 64 ? ZP : DUP;
 #pragma unroll
@@ -391,14 +407,15 @@ wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_c
     mph ^= 1;
     sm100::tc_fence_after();
   }
-  if (ok && tid >= 64) {  // dV rows s (the TMEM load is warp-collective; only rows inside the sequence store)
-    const int s = tid - 64, tg = c * L + s;
-    float d[64];
-    tmem_row64(tmem, warp, 192, d);
+  if (ok && quarter >= 2) {  // dV rows s (lanes 64..127, 32 columns per thread; the TMEM load is warp-collective)
+    const int s = 32 * quarter + (tid & 31) - 64, tg = c * L + s, i0 = 32 * colh;
+    float d[32];
+    sm100::tmem_ld32(tmem + trow_off + 192 + i0, d);
+    sm100::tmem_wait_ld();
     if (s < nvalid) {
-      float* out = dv + (((long)bb * T + tg) * H + h) * N;
+      float* out = dv + (((long)bb * T + tg) * H + h) * N + i0;
 #pragma unroll
-      for (int i = 0; i < 64; i += 4) *reinterpret_cast<float4*>(out + i) = make_float4(d[i], d[i + 1], d[i + 2], d[i + 3]);
+      for (int i = 0; i < 32; i += 4) *reinterpret_cast<float4*>(out + i) = make_float4(d[i], d[i + 1], d[i + 2], d[i + 3]);
     }
   }
   WKV_TRACE(24)
@@ -414,14 +431,18 @@ wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_c
 
 // ---------------------------------------------------------------- 3: input gradients per chunk
 namespace kb {
-constexpr int RAW = 0;          // r, w, k, v, a, b, dY; later S0^T (0..16), (dS D_L)^T (16..32); then P/Q arrays
+constexpr int RAW = 0;          // r, w, k, v, a, b, dY (8 KB each); r, w, k, a, b stay until the row epilogue,
+                                // v and dY die once copied, and their slots hold the two atoms of (dS D_L)^T
 constexpr int LAM = 56 * KB;
 constexpr int MISC = 72 * KB;
-constexpr int DZY = 73 * KB;    // [dZ; dY] (128 rows, K = i)  -> stage tiles
-constexpr int UV = 105 * KB;    // [U; V]   (128 rows, K = i)  -> stage tiles
+constexpr int DZY = 73 * KB;    // [dZ; dY] (128 rows, K = i)  -> stage tile SA -> FW (73..89), QA (89..105)
+constexpr int UV = 105 * KB;    // [U; V]   (128 rows, K = i)  -> stage tile SB -> PA (105..121), PB (121..137)
 constexpr int X1T = 137 * KB;   // [A~^T | R~^T] (64 rows j, K = 128) -> E arrays
 constexpr int X2T = 169 * KB;   // [B~^T | K~^T]
-constexpr int SMEM = 201 * KB + 1024;
+constexpr int S0T = 201 * KB;   // S0^T (64 rows j, K = i)
+constexpr int DST0 = 24 * KB;   // (dS D_L)^T atom 0 (keys i < 32), over raw v
+constexpr int DST1 = 48 * KB;   // atom 1 (i >= 32), over raw dY
+constexpr int SMEM = 217 * KB + 1024;
 }  // namespace kb
 
 // 256 threads (8 warps): warps w and w + 4 read the same TMEM lane quarter (rows 32 (w % 4) ..) and split the
@@ -457,14 +478,14 @@ wkv7_tc_bwd_grad_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_co
                                                            // in four parts, then each quarter's sum of g
   float* carry = reinterpret_cast<float*>(sm + kb::X2T);   // [256] Lambda carries (before X2T is built)
   uint8_t *DZY = sm + kb::DZY, *UV = sm + kb::UV, *X1T = sm + kb::X1T, *X2T = sm + kb::X2T;
-  uint8_t *S0T = sm, *DST = sm + 16 * KB;
+  uint8_t *S0T = sm + kb::S0T, *DST0 = sm + kb::DST0, *DST1 = sm + kb::DST1;
   uint8_t *SA = DZY, *SB = UV;  // stage tiles (32 KB each)
-  float* PA = reinterpret_cast<float*>(sm);            // dr r - dk k          (rows of the r~ / k~ half)
-  float* PB = PA + MAT;                                 // -db b                (rows of the a~ / b~ half)
-  float* QA = PB + MAT;                                 // da a
-  float* EA = reinterpret_cast<float*>(sm + kb::X1T);  // E b~
-  float* EB = EA + MAT;                                 // F k~
-  float* FW = reinterpret_cast<float*>(sm + kb::DZY);  // d log d / dw per element
+  float* PA = reinterpret_cast<float*>(sm + kb::UV);             // dr r - dk k   (rows of the r~ / k~ half)
+  float* PB = PA + MAT;                                           // -db b         (rows of the a~ / b~ half)
+  float* QA = reinterpret_cast<float*>(sm + kb::DZY + 16 * KB);  // da a
+  float* EA = reinterpret_cast<float*>(sm + kb::X1T);            // E b~
+  float* EB = EA + MAT;                                           // F k~
+  float* FW = reinterpret_cast<float*>(sm + kb::DZY);            // d log d / dw per element
   const long bh = (long)bb * H + h, ch = bh * chunks + c;
   const float* S0g = ckpt + (bh * (chunks + 1) + c) * MAT;
 
@@ -562,26 +583,33 @@ wkv7_tc_bwd_grad_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_co
         }
       }
     }
-    __syncthreads();  // raw tiles dead from here on
+    __syncthreads();  // raw v and dY dead from here on (r, w, k, a, b stay for the row epilogue)
     WKV_TRACE(34)
-    {  // S0^T (row j, K = i) and (dS D_L)^T (row j): column loads from global, 32 values per thread
+    {  // S0^T (row j, K = i) and (dS D_L)^T (row j; atom i / 32 in its own slot): column loads from global
       const int j = tid & 63, second = (tid >> 6) & 1, i0 = 32 * (tid >> 7);
       const float* src = second ? wk + WK_DS * MAT : S0g;
-      uint8_t* dst = second ? DST : S0T;
       const float sc = second ? DL[j] : 1.f;
       float col[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) col[i] = __ldg(src + (i0 + i) * N + j);
+      if (second) {
+        uint8_t* atom = i0 ? DST1 : DST0;
 #pragma unroll
-      for (int i = 0; i < 32; i += 4)
-        put4(dst, 64, j, i0 + i, col[i] * sc, col[i + 1] * sc, col[i + 2] * sc, col[i + 3] * sc);
+        for (int i = 0; i < 32; i += 4)
+          put4(atom, 64, j, i, col[i] * sc, col[i + 1] * sc, col[i + 2] * sc, col[i + 3] * sc);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) put4(S0T, 64, j, i0 + i, col[i], col[i + 1], col[i + 2], col[i + 3]);
+      }
     }
     tc_sync();
     if (tid == 0) {  // [dZ S0; dY S0] (cols 128..191) and [E; F] = [U; V] (dS D_L) (cols 256..319)
       mma_tf32_tiles(tmem + 128, sm100::smem_u32(DZY), 128, sm100::smem_u32(S0T), 64, 8, sm100::idesc_tf32(128, 64),
                      false);
-      mma_tf32_tiles(tmem + 256, sm100::smem_u32(UV), 128, sm100::smem_u32(DST), 64, 8, sm100::idesc_tf32(128, 64),
+      mma_tf32_tiles(tmem + 256, sm100::smem_u32(UV), 128, sm100::smem_u32(DST0), 64, 4, sm100::idesc_tf32(128, 64),
                      false);
+      mma_tf32_tiles(tmem + 256, sm100::smem_u32(UV) + 128 * 128, 128, sm100::smem_u32(DST1), 64, 4,
+                     sm100::idesc_tf32(128, 64), true);
       sm100::mma_commit(&bars[2]);  // own barrier: both commits may complete before either wait
     }
     second_issued = true;
@@ -648,14 +676,14 @@ wkv7_tc_bwd_grad_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_co
   if (ok) {
     WKV_TRACE(41)
     // ---- row epilogue: raw gradients and the dLambda terms (thread = row t of its half, 32 columns). The raw input
-    // rows come in as 16-byte loads, the gradient rows leave as 16-byte stores, and the decay-gradient factor of w
-    // is formed here (row-wise) for the column pass.
+    // rows are read from the tiles TMA brought at the start (zero past the sequence end), the gradient rows leave
+    // as 16-byte stores, and the decay-gradient factor of w is formed here (row-wise) for the column pass.
     const int tg = c * L + t;
     const bool lo = row < 64;  // rows of a~ / b~ (da, db) vs r~ / k~ (dr, dk)
     const bool valid = tg < T;
     const long go = (((long)bb * T + (valid ? tg : 0)) * H + h) * N;
-    const __nv_bfloat16* src1 = lo ? pa : pr;  // a / r
-    const __nv_bfloat16* src2 = lo ? pb : pk;  // b / k
+    const uint8_t* src1 = lo ? Ra : Rr;  // a / r
+    const uint8_t* src2 = lo ? Rb : Rk;  // b / k
     float* out1 = lo ? da : dr;
     float* out2 = lo ? db : dk;
     const int half = colh;
@@ -666,19 +694,14 @@ wkv7_tc_bwd_grad_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_co
       sm100::tmem_ld32(trow + 256 + 32 * half, d3);  // E / F
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        if (valid) {
-          rt::unpack8(__ldg(reinterpret_cast<const uint4*>(src1 + go + 32 * half + 8 * q)), x1 + 8 * q);
-          rt::unpack8(__ldg(reinterpret_cast<const uint4*>(src2 + go + 32 * half + 8 * q)), x2 + 8 * q);
-        } else {
-#pragma unroll
-          for (int u = 0; u < 8; ++u) x1[8 * q + u] = x2[8 * q + u] = 0.f;
-        }
+        raw8(src1, t, 32 * half + 8 * q, x1 + 8 * q);
+        raw8(src2, t, 32 * half + 8 * q, x2 + 8 * q);
       }
       if (lo && valid) {  // w factor of this row: -e^{-1/2} sigmoid(w) (1 - sigmoid(w))
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           float wv[8];
-          rt::unpack8(__ldg(reinterpret_cast<const uint4*>(pw + go + 32 * half + 8 * q)), wv);
+          raw8(Rw, t, 32 * half + 8 * q, wv);
 #pragma unroll
           for (int u = 0; u < 8; u += 4) {
             float f[4];
@@ -840,7 +863,7 @@ extern "C" cudaError_t rt_wkv7_tc_backward(int B, int T, int H, const void* r, c
       rec, (const __nv_bfloat16*)dy, dend, work, ds0, T, H, chunks);
   RT_CUDA_CHECK(cudaGetLastError());
   RT_CUDA_CHECK(cudaFuncSetAttribute(wkv7_tc_bwd_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ka::SMEM));
-  wkv7_tc_bwd_state_kernel<<<dim3(chunks, H, B), 128, ka::SMEM, stream>>>(mr, mw, mk, mv, ma, mb, mdy, ckpt, work, dv,
+  wkv7_tc_bwd_state_kernel<<<dim3(chunks, H, B), STATE_THREADS, ka::SMEM, stream>>>(mr, mw, mk, mv, ma, mb, mdy, ckpt, work, dv,
                                                                           T, H, chunks);
   RT_CUDA_CHECK(cudaGetLastError());
   RT_CUDA_CHECK(cudaFuncSetAttribute(wkv7_tc_bwd_grad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kb::SMEM));

@@ -77,7 +77,12 @@ RT_DEVICE bool wait_all(uint64_t* bar, uint32_t parity) {
   return __syncthreads_and(ok ? 1 : 0) != 0;
 }
 
-__global__ void __launch_bounds__(128, 1)
+// 256 threads: warps w and w + 4 share a TMEM lane quarter and split each 64-column block; tile phases split
+// their rows or columns the same way. The solves keep one right-hand-side column per thread on the first 128
+// threads (A~ columns on threads 64..127, Z columns on threads 0..63).
+constexpr int CHUNK_THREADS = 256;
+
+__global__ void __launch_bounds__(CHUNK_THREADS, 1)
 wkv7_tc_chunk_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_constant__ CUtensorMap m_w,
                      const __grid_constant__ CUtensorMap m_k, const __grid_constant__ CUtensorMap m_v,
                      const __grid_constant__ CUtensorMap m_a, const __grid_constant__ CUtensorMap m_b, int T,
@@ -86,6 +91,7 @@ wkv7_tc_chunk_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_const
   uint8_t* sm = align1024(smem_raw);
   const int c = blockIdx.x, h = blockIdx.y, bb = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5;
+  const int quarter = warp & 3, colh = warp >> 2;
   uint8_t* Rr = sm + OFF_RAW;
   uint8_t* Rw = Rr + 8 * KB;
   uint8_t* Rk = Rr + 16 * KB;
@@ -100,9 +106,12 @@ wkv7_tc_chunk_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_const
   uint8_t* MRB = sm + OFF_MRB;
   float* MPL = reinterpret_cast<float*>(sm + OFF_MPL);
   float* ZT = reinterpret_cast<float*>(sm + OFF_ZT);
+  float* carry = ZT;  // Lambda carries (before Z^T is written)
   uint8_t* MAK = X2;
   uint8_t* WUT = X1;
   float* rec = ws + (((long)bb * H + h) * chunks + c) * (REC_MATS * MAT);
+  const uint32_t trow = (uint32_t)(32 * quarter) << 16;  // this warp's TMEM lane quarter
+  const int row = 32 * quarter + (tid & 31);             // its TMEM lane (row of a 128-row result)
   WKV_TRACE_BEGIN
 
   if (tid == 0) {
@@ -135,17 +144,17 @@ wkv7_tc_chunk_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_const
   const int nvalid = min(L, T - c * L);
 
   if (ok) {
-    build_lambda(Rw, lam, DL, nvalid, tid);  // DL doubles as the carry scratch until it is written
+    build_lambda_nt<CHUNK_THREADS>(Rw, lam, carry, nvalid, tid);
     if (tid < 64) DL[tid] = expf(lam[poff(63, tid)]);
     WKV_TRACE(1)
-    // ---- phase-A tiles. X1 row tid: A~ (tid < 64) / R~; X2 row tid: B~ / K~ (thread = row).
+    // ---- phase-A tiles. X1 row r: A~ (r < 64) / R~; X2 row r: B~ / K~ (thread: row r = tid % 128, 32 keys).
     {
-      const int t = tid & 63;
-      const bool hi = tid >= 64;
+      const int r = tid & 127, t = r & 63, j1 = 32 * (tid >> 7);
+      const bool hi = r >= 64;
       const uint8_t* s1 = hi ? Rr : Ra;
       const uint8_t* s2 = hi ? Rk : Rb;
 #pragma unroll 1
-      for (int j0 = 0; j0 < 64; j0 += 8) {
+      for (int j0 = j1; j0 < j1 + 32; j0 += 8) {
         float x1[8], x2[8], lt[8], lp[8];
         raw8(s1, t, j0, x1);
         raw8(s2, t, j0, x2);
@@ -163,31 +172,31 @@ wkv7_tc_chunk_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_const
           x1[q] *= expf(hi ? lt[q] : lp[q]);
           x2[q] *= expf(-lt[q]);
         }
-        put4(X1, 128, tid, j0, x1[0], x1[1], x1[2], x1[3]);
-        put4(X1, 128, tid, j0 + 4, x1[4], x1[5], x1[6], x1[7]);
-        put4(X2, 128, tid, j0, x2[0], x2[1], x2[2], x2[3]);
-        put4(X2, 128, tid, j0 + 4, x2[4], x2[5], x2[6], x2[7]);
+        put4(X1, 128, r, j0, x1[0], x1[1], x1[2], x1[3]);
+        put4(X1, 128, r, j0 + 4, x1[4], x1[5], x1[6], x1[7]);
+        put4(X2, 128, r, j0, x2[0], x2[1], x2[2], x2[3]);
+        put4(X2, 128, r, j0 + 4, x2[4], x2[5], x2[6], x2[7]);
       }
     }
     WKV_TRACE(2)
-    // V^T (row i = tid < 64), B^T / K^T (row j; thread j < 64 and 64 + j): x[s][j] e^{Lambda_L - Lambda_s}
+    // V^T rows i (16 steps per thread); B^T / K^T rows j: x[s][j] e^{Lambda_L - Lambda_s} (32 steps per thread)
     {
       const int j = tid & 63;
-      if (tid < 64) {
-#pragma unroll 1
-        for (int s0 = 0; s0 < 64; s0 += 16) {
-          float x[16];
+      {
+        const int s0 = 16 * (tid >> 6);
+        float x[16];
 #pragma unroll
-          for (int q = 0; q < 16; ++q) x[q] = raw(Rv, s0 + q, j);
+        for (int q = 0; q < 16; ++q) x[q] = raw(Rv, s0 + q, j);
 #pragma unroll
-          for (int q = 0; q < 16; q += 4) put4(VT, 64, j, s0 + q, x[q], x[q + 1], x[q + 2], x[q + 3]);
-        }
+        for (int q = 0; q < 16; q += 4) put4(VT, 64, j, s0 + q, x[q], x[q + 1], x[q + 2], x[q + 3]);
       }
-      const uint8_t* src = tid < 64 ? Rb : Rk;
-      uint8_t* dst = tid < 64 ? BT : KT;
+      const bool kt = (tid & 64) != 0;
+      const uint8_t* src = kt ? Rk : Rb;
+      uint8_t* dst = kt ? KT : BT;
       const float lL = lam[poff(63, j)];
+      const int s1 = 32 * (tid >> 7);
 #pragma unroll 1
-      for (int s0 = 0; s0 < 64; s0 += 16) {  // loads first, then exponentials, then stores
+      for (int s0 = s1; s0 < s1 + 32; s0 += 16) {  // loads first, then exponentials, then stores
         float x[16], ls[16];
 #pragma unroll
         for (int q = 0; q < 16; ++q) {
@@ -215,29 +224,38 @@ wkv7_tc_chunk_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_const
   }
   if (ok) {
     WKV_TRACE(4)
-    // ---- epilogue 1: masks; M_ab -> MPL (plain), [M_ak; M_rk] -> MAK, M_rb -> MRB
+    // ---- epilogue 1 (32 columns of each block per thread): masks; M_ab -> MPL (plain), [M_ak; M_rk] -> MAK,
+    //      M_rb -> MRB
     {
-      float d[64];
-      const int t = tid & 63;
-      tmem_row64(tmem, warp, 0, d);
-      if (tid < 64) {
+      float d[32];
+      const int t = row & 63, s0 = 32 * colh;
+      sm100::tmem_ld32(tmem + trow + s0, d);
+      sm100::tmem_wait_ld();
+      if (row < 64) {
 #pragma unroll
-        for (int s = 0; s < 64; s += 4)
+        for (int u = 0; u < 32; u += 4) {
+          const int s = s0 + u;
           *reinterpret_cast<float4*>(&MPL[poff(t, s)]) =
-              make_float4(s < t ? d[s] : 0.f, s + 1 < t ? d[s + 1] : 0.f, s + 2 < t ? d[s + 2] : 0.f,
-                          s + 3 < t ? d[s + 3] : 0.f);
+              make_float4(s < t ? d[u] : 0.f, s + 1 < t ? d[u + 1] : 0.f, s + 2 < t ? d[u + 2] : 0.f,
+                          s + 3 < t ? d[u + 3] : 0.f);
+        }
       } else {
 #pragma unroll
-        for (int s = 0; s < 64; s += 4)
-          put4(MRB, 64, t, s, s <= t ? d[s] : 0.f, s + 1 <= t ? d[s + 1] : 0.f, s + 2 <= t ? d[s + 2] : 0.f,
-               s + 3 <= t ? d[s + 3] : 0.f);
+        for (int u = 0; u < 32; u += 4) {
+          const int s = s0 + u;
+          put4(MRB, 64, t, s, s <= t ? d[u] : 0.f, s + 1 <= t ? d[u + 1] : 0.f, s + 2 <= t ? d[u + 2] : 0.f,
+               s + 3 <= t ? d[u + 3] : 0.f);
+        }
       }
-      tmem_row64(tmem, warp, 64, d);
-      const int lim = tid < 64 ? t : t + 1;  // strict for M_ak, inclusive for M_rk
+      sm100::tmem_ld32(tmem + trow + 64 + s0, d);
+      sm100::tmem_wait_ld();
+      const int lim = row < 64 ? t : t + 1;  // strict for M_ak, inclusive for M_rk
 #pragma unroll
-      for (int s = 0; s < 64; s += 4)
-        put4(MAK, 128, tid, s, s < lim ? d[s] : 0.f, s + 1 < lim ? d[s + 1] : 0.f, s + 2 < lim ? d[s + 2] : 0.f,
-             s + 3 < lim ? d[s + 3] : 0.f);
+      for (int u = 0; u < 32; u += 4) {
+        const int s = s0 + u;
+        put4(MAK, 128, row, s, s < lim ? d[u] : 0.f, s + 1 < lim ? d[u + 1] : 0.f, s + 2 < lim ? d[u + 2] : 0.f,
+             s + 3 < lim ? d[u + 3] : 0.f);
+      }
     }
     tc_sync();
     // ---- MMA2: [Z; M_rk V] = [M_ak; M_rk] V  (cols 256..319)
@@ -251,7 +269,7 @@ wkv7_tc_chunk_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_const
   // Right-hand sides of the solves, one column per thread: A~ column j (threads 64 + j, built while MMA2 runs)
   // and Z column i (threads i < 64, from Z^T after MMA2).
   float x[64];
-  if (ok && tid >= 64) {
+  if (ok && tid >= 64 && tid < 128) {
     const int j = tid - 64;
 #pragma unroll
     for (int t = 0; t < 64; ++t) x[t] = raw(Ra, t, j);
@@ -266,16 +284,12 @@ wkv7_tc_chunk_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_const
   }
   if (ok) {
     WKV_TRACE(6)
-    if (tid < 64) {  // Z row t -> column t of Z^T
-      const uint32_t zrow = tmem + ((uint32_t)(32 * warp) << 16) + 256;
+    if (quarter < 2) {  // Z row t -> column t of Z^T (32 columns per thread)
+      float d[32];
+      sm100::tmem_ld32(tmem + trow + 256 + 32 * colh, d);
+      sm100::tmem_wait_ld();
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        float d[32];
-        sm100::tmem_ld32(zrow + 32 * half, d);
-        sm100::tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) ZT[poff(32 * half + i, tid)] = d[i];
-      }
+      for (int i = 0; i < 32; ++i) ZT[poff(32 * colh + i, row)] = d[i];
     }
     __syncthreads();
     if (tid < 64) {
@@ -291,11 +305,11 @@ wkv7_tc_chunk_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_const
     WKV_TRACE(7)
     // ---- W = T A~ (threads 64 + j: column j) and U0 = T Z (threads i: column i), T = (I - M_ab)^{-1}; the
     //      columns become the rows of [W^T; U0^T] (X1's [A~; R~] was last read by MMA1)
-    solve_lower(MPL, x);
-    {
-      const int row = tid < 64 ? 64 + tid : tid - 64;
+    if (tid < 128) {
+      solve_lower(MPL, x);
+      const int wrow = tid < 64 ? 64 + tid : tid - 64;
 #pragma unroll
-      for (int t = 0; t < 64; t += 4) put4(WUT, 128, row, t, x[t], x[t + 1], x[t + 2], x[t + 3]);
+      for (int t = 0; t < 64; t += 4) put4(WUT, 128, wrow, t, x[t], x[t + 1], x[t + 2], x[t + 3]);
     }
     tc_sync();
     WKV_TRACE(8)
@@ -317,57 +331,51 @@ wkv7_tc_chunk_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_const
   }
   if (ok) {
     WKV_TRACE(9)
-    const uint32_t row = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
-    if (tid < 64) {  // G = diag(D_L) + W^T B^ (row j = tid)
-      const int r = tid;
-#pragma unroll 1
-      for (int half = 0; half < 2; ++half) {
-        float d[32];
-        sm100::tmem_ld32(row + 128 + 32 * half, d);
-        sm100::tmem_wait_ld();
-        float* g = rec + REC_G * MAT + r * 64 + 32 * half;
+    const int half = colh;
+    if (row < 64) {  // G = diag(D_L) + W^T B^ (row j = row; 32 columns per thread)
+      const int r = row;
+      float d[32];
+      sm100::tmem_ld32(tmem + trow + 128 + 32 * half, d);
+      sm100::tmem_wait_ld();
+      float* g = rec + REC_G * MAT + r * 64 + 32 * half;
 #pragma unroll
-        for (int u = 0; u < 32; ++u) d[u] += 32 * half + u == r ? DL[r] : 0.f;
+      for (int u = 0; u < 32; ++u) d[u] += 32 * half + u == r ? DL[r] : 0.f;
 #pragma unroll
-        for (int u = 0; u < 32; u += 4) *reinterpret_cast<float4*>(g + u) = make_float4(d[u], d[u + 1], d[u + 2], d[u + 3]);
-      }
-    } else {  // row t = tid - 64: Q = R~ + M_rb W (tf32: an MMA operand later), Y0 = M_rk V + M_rb U0,
+      for (int u = 0; u < 32; u += 4) *reinterpret_cast<float4*>(g + u) = make_float4(d[u], d[u + 1], d[u + 2], d[u + 3]);
+    } else {  // row t = row - 64: Q = R~ + M_rb W (tf32: an MMA operand later), Y0 = M_rk V + M_rb U0,
               // H0 = U0^T B^ + V^T K^ (row i = t)
-      const int t = tid - 64;
-#pragma unroll 1
-      for (int half = 0; half < 2; ++half) {
-        float d[32], e[32];
-        sm100::tmem_ld32(row + 32 * half, d);
-        sm100::tmem_wait_ld();
-        float* gq = rec + REC_Q * MAT + t * 64 + 32 * half;
+      const int t = row - 64;
+      float d[32], e[32];
+      sm100::tmem_ld32(tmem + trow + 32 * half, d);
+      sm100::tmem_wait_ld();
+      float* gq = rec + REC_Q * MAT + t * 64 + 32 * half;
 #pragma unroll
-        for (int j8 = 0; j8 < 32; j8 += 8) {
-          float xr[8], lt[8], q[8];
-          raw8(Rr, t, 32 * half + j8, xr);
-          *reinterpret_cast<float4*>(lt) = *reinterpret_cast<const float4*>(&lam[poff(t, 32 * half + j8)]);
-          *reinterpret_cast<float4*>(lt + 4) = *reinterpret_cast<const float4*>(&lam[poff(t, 32 * half + j8 + 4)]);
+      for (int j8 = 0; j8 < 32; j8 += 8) {
+        float xr[8], lt[8], q[8];
+        raw8(Rr, t, 32 * half + j8, xr);
+        *reinterpret_cast<float4*>(lt) = *reinterpret_cast<const float4*>(&lam[poff(t, 32 * half + j8)]);
+        *reinterpret_cast<float4*>(lt + 4) = *reinterpret_cast<const float4*>(&lam[poff(t, 32 * half + j8 + 4)]);
 #pragma unroll
-          for (int u = 0; u < 8; ++u) q[u] = tf32r(xr[u] * expf(lt[u]) + d[j8 + u]);
-          *reinterpret_cast<float4*>(gq + j8) = make_float4(q[0], q[1], q[2], q[3]);
-          *reinterpret_cast<float4*>(gq + j8 + 4) = make_float4(q[4], q[5], q[6], q[7]);
-        }
-        sm100::tmem_ld32(row + 64 + 32 * half, d);
-        sm100::tmem_ld32(row + 256 + 32 * half, e);
-        sm100::tmem_wait_ld();
-        float* gy = rec + REC_Y0 * MAT + t * 64 + 32 * half;
-#pragma unroll
-        for (int u = 0; u < 32; u += 4)
-          *reinterpret_cast<float4*>(gy + u) = make_float4(d[u] + e[u], d[u + 1] + e[u + 1], d[u + 2] + e[u + 2],
-                                                           d[u + 3] + e[u + 3]);
-        sm100::tmem_ld32(row + 128 + 32 * half, d);
-        sm100::tmem_ld32(row + 192 + 32 * half, e);
-        sm100::tmem_wait_ld();
-        float* gh = rec + REC_H0 * MAT + t * 64 + 32 * half;
-#pragma unroll
-        for (int u = 0; u < 32; u += 4)
-          *reinterpret_cast<float4*>(gh + u) = make_float4(d[u] + e[u], d[u + 1] + e[u + 1], d[u + 2] + e[u + 2],
-                                                           d[u + 3] + e[u + 3]);
+        for (int u = 0; u < 8; ++u) q[u] = tf32r(xr[u] * expf(lt[u]) + d[j8 + u]);
+        *reinterpret_cast<float4*>(gq + j8) = make_float4(q[0], q[1], q[2], q[3]);
+        *reinterpret_cast<float4*>(gq + j8 + 4) = make_float4(q[4], q[5], q[6], q[7]);
       }
+      sm100::tmem_ld32(tmem + trow + 64 + 32 * half, d);
+      sm100::tmem_ld32(tmem + trow + 256 + 32 * half, e);
+      sm100::tmem_wait_ld();
+      float* gy = rec + REC_Y0 * MAT + t * 64 + 32 * half;
+#pragma unroll
+      for (int u = 0; u < 32; u += 4)
+        *reinterpret_cast<float4*>(gy + u) = make_float4(d[u] + e[u], d[u + 1] + e[u + 1], d[u + 2] + e[u + 2],
+                                                         d[u + 3] + e[u + 3]);
+      sm100::tmem_ld32(tmem + trow + 128 + 32 * half, d);
+      sm100::tmem_ld32(tmem + trow + 192 + 32 * half, e);
+      sm100::tmem_wait_ld();
+      float* gh = rec + REC_H0 * MAT + t * 64 + 32 * half;
+#pragma unroll
+      for (int u = 0; u < 32; u += 4)
+        *reinterpret_cast<float4*>(gh + u) = make_float4(d[u] + e[u], d[u + 1] + e[u + 1], d[u + 2] + e[u + 2],
+                                                         d[u + 3] + e[u + 3]);
     }
   }
   WKV_TRACE(10)
@@ -569,7 +577,7 @@ extern "C" cudaError_t rt_wkv7_tc_forward(int B, int T, int H, const void* r, co
        fp32_rows_map(&ms, ckpt, (long)B * H * (chunks + 1) * N);
   if (!ok) return cudaErrorInvalidValue;
   RT_CUDA_CHECK(cudaFuncSetAttribute(wkv7_tc_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, CHUNK_SMEM));
-  wkv7_tc_chunk_kernel<<<dim3(chunks, H, B), 128, CHUNK_SMEM, stream>>>(mr, mw, mk, mv, ma, mb, T, H, chunks, ws);
+  wkv7_tc_chunk_kernel<<<dim3(chunks, H, B), CHUNK_THREADS, CHUNK_SMEM, stream>>>(mr, mw, mk, mv, ma, mb, T, H, chunks, ws);
   RT_CUDA_CHECK(cudaGetLastError());
   wkv7_tc_scan_kernel<<<dim3(B * H, N / SCAN_ROWS), 128, 0, stream>>>(ws, s0, ckpt, s_end, chunks);
   RT_CUDA_CHECK(cudaGetLastError());
