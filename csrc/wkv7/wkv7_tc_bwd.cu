@@ -4,8 +4,8 @@
 // With dS the gradient of a chunk's end state and dY of its outputs, the chunk-start gradient is
 //     dS0 = dS G^T + dY^T Q                       (G, Q from the forward records),
 // a serial scan over chunks (kernel 1). Per chunk, from the chunk-start state S0 (forward checkpoint) and dS,
-// with T = (I - M_ab)^{-1} applied by fp32 triangular solves (never formed):
-//     U  = T (A~ S0^T + M_ak V)                    (the chunk's u_t = S_{t-1} a_t rows)
+// with T = (I - M_ab)^{-1} applied by an fp32 triangular solve (never formed):
+//     U  = T (A~ S0^T + M_ak V) = W S0^T + U0      (the chunk's u_t = S_{t-1} a_t rows; W, U0 from the forward)
 //     dU = M_rb^T dY + B^ dS^T,  dZ = T^T dU,  dV = M_rk^T dY + K^ dS^T + M_ak^T dZ          (kernel 2)
 //     dM_ab = (dZ U^T) strict, dM_ak = (dZ V^T) strict, dM_rb = (dY U^T) incl, dM_rk = (dY V^T) incl
 //     dA~ = dZ S0 + dM_ab B~ + dM_ak K~,   dR~ = dY S0 + dM_rb B~ + dM_rk K~
@@ -42,7 +42,7 @@ __device__ unsigned long long wkv7_trace_ns[64];
 
 constexpr int KB = 1024;
 constexpr int MAT = N * N;
-enum { REC_G = 0, REC_H0 = 1, REC_Q = 2, REC_Y0 = 3, REC_MATS = 4 };  // forward record (fwd file)
+enum { REC_G = 0, REC_H0 = 1, REC_Q = 2, REC_Y0 = 3, REC_W = 4, REC_U0 = 5, REC_MATS = 6 };  // forward record
 enum { WK_DS = 0, WK_U = 1, WK_DZ = 2, WK_MATS = 3 };                             // backward work record
 
 __device__ int wkv7_tc_bwd_fault_word = 0;
@@ -146,13 +146,14 @@ namespace ka {
 constexpr int RAW = 0;          // r, w, k, v, a, b, dY (8 KB each)
 constexpr int LAM = 56 * KB;
 constexpr int MISC = 72 * KB;
-constexpr int X1 = 73 * KB;     // [A~; R~]                     -> Zf^T (73..89), dU^T (89..105)
+constexpr int X1 = 73 * KB;     // [A~; R~]                     -> dU^T (89..105)
 constexpr int X2 = 105 * KB;    // [B~; K~] -> [M_rb^T; M_rk^T]  -> T^T (105..121)
-constexpr int VT = 137 * KB;    // V^T (64 rows)                 -> M_ak^T at 129..145 after MMA-Z
+// 137..153: free until M_ak^T (129..145) is written after MMA-dU
 constexpr int BKH = 153 * KB;   // [B^; K^] (128 rows)
 constexpr int DYT = 185 * KB;   // dY^T (64 rows)
-// after phase A (raw, Lambda dead): S0 (0..16), dS (16..32), M_ab plain (32..48), M_ak (48..64; read as 128 rows)
-constexpr int SMEM = 201 * KB + 1024;
+// after phase A (raw, Lambda dead): S0 (0..16), dS (16..32), M_ab plain (32..48)
+constexpr int WT = 201 * KB;    // W (64 rows t, K = j) by TMA; read as 128 rows (the 8 KB after it stay in bounds)
+constexpr int SMEM = 225 * KB + 1024;
 }  // namespace ka
 
 // 256 threads: the tile and epilogue phases split their rows or TMEM columns over two threads (warps w and w + 4
@@ -164,7 +165,8 @@ __global__ void __launch_bounds__(STATE_THREADS, 1)
 wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_constant__ CUtensorMap m_w,
                          const __grid_constant__ CUtensorMap m_k, const __grid_constant__ CUtensorMap m_v,
                          const __grid_constant__ CUtensorMap m_a, const __grid_constant__ CUtensorMap m_b,
-                         const __grid_constant__ CUtensorMap m_dy, const float* __restrict__ ckpt,
+                         const __grid_constant__ CUtensorMap m_dy, const __grid_constant__ CUtensorMap m_rec,
+                         const float* __restrict__ rec, const float* __restrict__ ckpt,
                          float* __restrict__ work, float* __restrict__ dv, int T, int H, int chunks) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
@@ -177,11 +179,11 @@ wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_c
   float* lam = reinterpret_cast<float*>(sm + ka::LAM);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + ka::MISC);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + ka::MISC + 32);
-  uint8_t *X1 = sm + ka::X1, *X2 = sm + ka::X2, *VT = sm + ka::VT, *BKH = sm + ka::BKH, *DYT = sm + ka::DYT;
-  uint8_t *S0t = sm, *DSt = sm + 16 * KB, *MAK = sm + 48 * KB;
+  uint8_t *X1 = sm + ka::X1, *X2 = sm + ka::X2, *BKH = sm + ka::BKH, *DYT = sm + ka::DYT;
+  uint8_t *S0t = sm, *DSt = sm + 16 * KB;
   float* MPL = reinterpret_cast<float*>(sm + 32 * KB);
-  float* ZP = reinterpret_cast<float*>(X1);             // Zf^T, plain (row i = column i of Zf)
-  float* DUP = reinterpret_cast<float*>(X1 + 16 * KB);  // dU^T, plain
+  float* DUP = reinterpret_cast<float*>(X1 + 16 * KB);  // dU^T, plain (row i = column i of dU)
+  uint8_t* WT = sm + ka::WT;
   float* carry = reinterpret_cast<float*>(BKH);         // Lambda carries (before BKH is built)
   uint8_t *MRT = X2, *MAKT = sm + 129 * KB, *DZT = sm;
   const long bh = (long)bb * H + h, ch = bh * chunks + c;
@@ -205,7 +207,7 @@ wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_c
   sm100::tc_fence_after();
   const uint32_t tmem = *tslot;
   if (tid == 0) {
-    sm100::mbar_expect_tx(&bars[0], 7 * 8192);
+    sm100::mbar_expect_tx(&bars[0], 7 * 8192 + 16 * KB);
     const int x = h * N, y = c * L;
     sm100::tma_load_3d(Rr, &m_r, &bars[0], x, y, bb);
     sm100::tma_load_3d(Rw, &m_w, &bars[0], x, y, bb);
@@ -214,6 +216,9 @@ wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_c
     sm100::tma_load_3d(Ra, &m_a, &bars[0], x, y, bb);
     sm100::tma_load_3d(Rb, &m_b, &bars[0], x, y, bb);
     sm100::tma_load_3d(Rdy, &m_dy, &bars[0], x, y, bb);
+    const int wrow = (int)((ch * REC_MATS + REC_W) * N);
+    sm100::tma_load_2d(WT, &m_rec, &bars[0], 0, wrow);
+    sm100::tma_load_2d(WT + 8 * KB, &m_rec, &bars[0], 32, wrow);
   }
   int stage = 1;
   bool ok = wait_all(&bars[0], 0);
@@ -259,18 +264,13 @@ wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_c
       }
     }
     WKV_TRACE(17)
-    {  // V^T (row i, threads with bit 6 clear), dY^T (row i, bit 6 set); 32 steps per thread
-      const int i = tid & 63, s1 = 32 * (tid >> 7);
-      uint8_t* dst = (tid & 64) ? DYT : VT;
-      const uint8_t* src = (tid & 64) ? Rdy : Rv;
-#pragma unroll 1
-      for (int s0 = s1; s0 < s1 + 32; s0 += 16) {
-        float x[16];
+    {  // dY^T (row i): 16 steps per thread
+      const int i = tid & 63, s1 = 16 * (tid >> 6);
+      float x[16];
 #pragma unroll
-        for (int q = 0; q < 16; ++q) x[q] = raw(src, s0 + q, i);
+      for (int q = 0; q < 16; ++q) x[q] = raw(Rdy, s1 + q, i);
 #pragma unroll
-        for (int q = 0; q < 16; q += 4) put4(dst, 64, i, s0 + q, x[q], x[q + 1], x[q + 2], x[q + 3]);
-      }
+      for (int q = 0; q < 16; q += 4) put4(DYT, 64, i, s1 + q, x[q], x[q + 1], x[q + 2], x[q + 3]);
     }
     tc_sync();
     WKV_TRACE(18)
@@ -298,8 +298,8 @@ wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_c
   }
   if (ok) {
     WKV_TRACE(19)
-    // ---- epilogue 1 (32 columns of each 64-column block per thread): M_ab (strict) -> MPL (plain), M_ak (strict)
-    //      -> MAK rows; [M_rb^T; M_rk^T] -> MRT (transposed, from rows t >= 64)
+    // ---- epilogue 1 (32 columns of each 64-column block per thread): M_ab (strict) -> MPL (plain);
+    //      [M_rb^T; M_rk^T] -> MRT (transposed, from rows t >= 64)
     const int row = 32 * quarter + (tid & 31), t = row & 63, s0 = 32 * colh;
     float d[32];
     sm100::tmem_ld32(tmem + trow_off + s0, d);  // M_ab / M_rb
@@ -316,27 +316,18 @@ wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_c
 #pragma unroll
       for (int u = 0; u < 32; ++u) put1(MRT, 128, s0 + u, t, s0 + u <= t ? d[u] : 0.f);
     }
-    sm100::tmem_ld32(tmem + trow_off + 64 + s0, d);  // M_ak / M_rk
-    sm100::tmem_wait_ld();
-    if (row < 64) {
-#pragma unroll
-      for (int u = 0; u < 32; u += 4) {
-        const int s = s0 + u;
-        put4(MAK, 64, t, s, s < t ? d[u] : 0.f, s + 1 < t ? d[u + 1] : 0.f, s + 2 < t ? d[u + 2] : 0.f,
-             s + 3 < t ? d[u + 3] : 0.f);
-      }
-    } else {
+    if (row >= 64) {  // warp-uniform: lane quarters 2 and 3
+      sm100::tmem_ld32(tmem + trow_off + 64 + s0, d);  // M_rk
+      sm100::tmem_wait_ld();
 #pragma unroll
       for (int u = 0; u < 32; ++u) put1(MRT, 128, 64 + s0 + u, t, s0 + u <= t ? d[u] : 0.f);
     }
     tc_sync();
-    // ---- MMA-Z (cols 128..191): [A~ S0^T + M_ak V; *];  MMA-dU (cols 192..255): [dU; dV'] =
+    // ---- MMA-U (cols 128..191): [W S0^T; *];  MMA-dU (cols 192..255): [dU; dV'] =
     //      [M_rb^T; M_rk^T] dY + [B^; K^] dS^T
     if (tid == 0) {
-      mma_tf32_tiles(tmem + 128, sm100::smem_u32(X1), 128, sm100::smem_u32(S0t), 64, 8, sm100::idesc_tf32(128, 64),
+      mma_tf32_tiles(tmem + 128, sm100::smem_u32(WT), 64, sm100::smem_u32(S0t), 64, 8, sm100::idesc_tf32(128, 64),
                      false);
-      mma_tf32_tiles(tmem + 128, sm100::smem_u32(MAK), 64, sm100::smem_u32(VT), 64, 8, sm100::idesc_tf32(128, 64),
-                     true);
       mma_tf32_tiles(tmem + 192, sm100::smem_u32(MRT), 128, sm100::smem_u32(DYT), 64, 8, sm100::idesc_tf32(128, 64),
                      false);
       mma_tf32_tiles(tmem + 192, sm100::smem_u32(BKH), 128, sm100::smem_u32(DSt), 64, 8, sm100::idesc_tf32(128, 64),
@@ -350,19 +341,25 @@ wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_c
   }
   if (ok) {
     WKV_TRACE(20)
-    // ---- epilogue 2: Zf and dU rows t (lanes 0..63; 32 columns per thread) -> columns t of the plain Zf^T, dU^T;
-    //      M_ak row t -> column t of M_ak^T
+    // ---- epilogue 2 (lanes 0..63, 32 columns per thread): U = W S0^T + U0 rows t (tf32) to the work record; dU
+    //      rows t -> columns t of the plain dU^T; M_ak row t -> column t of M_ak^T
     const int row = 32 * quarter + (tid & 31), s0 = 32 * colh;
     if (quarter < 2) {
       float e[32];
-#pragma unroll 1
-      for (int part = 0; part < 2; ++part) {  // Zf cols 128.., dU cols 192..
-        sm100::tmem_ld32(tmem + trow_off + 128 + 64 * part + s0, e);
-        sm100::tmem_wait_ld();
-        float* dst = part ? DUP : ZP;
+      sm100::tmem_ld32(tmem + trow_off + 128 + s0, e);  // (W S0^T) row t
+      sm100::tmem_wait_ld();
+      const float* u0 = rec + (ch * REC_MATS + REC_U0) * MAT + row * N + s0;
+      float* gu = wk + WK_U * MAT + row * N + s0;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) dst[poff(s0 + i, row)] = e[i];
+      for (int i = 0; i < 32; i += 4) {
+        const float4 b4 = __ldg(reinterpret_cast<const float4*>(u0 + i));
+        *reinterpret_cast<float4*>(gu + i) = make_float4(tf32r(e[i] + b4.x), tf32r(e[i + 1] + b4.y),
+                                                         tf32r(e[i + 2] + b4.z), tf32r(e[i + 3] + b4.w));
       }
+      sm100::tmem_ld32(tmem + trow_off + 192 + s0, e);  // dU row t
+      sm100::tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) DUP[poff(s0 + i, row)] = e[i];
       sm100::tmem_ld32(tmem + trow_off + 64 + s0, e);  // M_ak row t (still in TMEM)
       sm100::tmem_wait_ld();
 #pragma unroll
@@ -370,29 +367,26 @@ wkv7_tc_bwd_state_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_c
     }
     __syncthreads();
     WKV_TRACE(21)
-    // ---- U = T Zf (threads i < 64: column i, forward substitution), dZ = T^T dU (threads 64 + i: column i, back
-    //      substitution); U and dZ (tf32) to the work record, dZ columns as rows of dZ^T for dV
-    if (tid < 128) {
+    // ---- dZ = T^T dU (threads i < 64: column i, back substitution); dZ (tf32) to the work record and as the rows
+    //      of dZ^T for dV
+    if (tid < 64) {
       float d[64];
-      const int i = tid & 63;
-      const float* src = tid < 64 ? ZP : DUP;
+      const int i = tid;
 #pragma unroll
       for (int s = 0; s < 64; s += 4) {
-        const float4 z = *reinterpret_cast<const float4*>(&src[poff(i, s)]);
+        const float4 z = *reinterpret_cast<const float4*>(&DUP[poff(i, s)]);
         d[s] = z.x;
         d[s + 1] = z.y;
         d[s + 2] = z.z;
         d[s + 3] = z.w;
       }
-      if (tid < 64) solve_lower(MPL, d);
-      else solve_upper_t(MPL, d);
-      float* g = wk + (tid < 64 ? WK_U : WK_DZ) * MAT + i;
+      solve_upper_t(MPL, d);
+      WKV_TRACE(22)
+      float* g = wk + WK_DZ * MAT + i;
 #pragma unroll
       for (int s = 0; s < 64; ++s) g[s * N] = tf32r(d[s]);
-      if (tid >= 64) {
 #pragma unroll
-        for (int s = 0; s < 64; s += 4) put4(DZT, 64, i, s, d[s], d[s + 1], d[s + 2], d[s + 3]);
-      }
+      for (int s = 0; s < 64; s += 4) put4(DZT, 64, i, s, d[s], d[s + 1], d[s + 2], d[s + 3]);
     }
     tc_sync();
     WKV_TRACE(23)
@@ -856,14 +850,16 @@ extern "C" cudaError_t rt_wkv7_tc_backward(int B, int T, int H, const void* r, c
   bool ok = input_map(&mr, r, B, T, H) && input_map(&mw, w, B, T, H) && input_map(&mk, k, B, T, H) &&
             input_map(&mv, v, B, T, H) && input_map(&ma, a, B, T, H) && input_map(&mb, b, B, T, H) &&
             input_map(&mdy, dy, B, T, H);
-  ok = ok && fp32_rows_map(&mwk, work, (long)B * H * chunks * WK_MATS * N);
+  CUtensorMap mrec;
+  ok = ok && fp32_rows_map(&mwk, work, (long)B * H * chunks * WK_MATS * N) &&
+       fp32_rows_map(&mrec, rec, (long)B * H * chunks * REC_MATS * N);
   if (!ok) return cudaErrorInvalidValue;
   RT_CUDA_CHECK(cudaFuncSetAttribute(wkv7_tc_bscan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BSCAN_SMEM));
   wkv7_tc_bscan_kernel<<<dim3(B * H, N / BS_ROWS), 128, BSCAN_SMEM, stream>>>(
       rec, (const __nv_bfloat16*)dy, dend, work, ds0, T, H, chunks);
   RT_CUDA_CHECK(cudaGetLastError());
   RT_CUDA_CHECK(cudaFuncSetAttribute(wkv7_tc_bwd_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ka::SMEM));
-  wkv7_tc_bwd_state_kernel<<<dim3(chunks, H, B), STATE_THREADS, ka::SMEM, stream>>>(mr, mw, mk, mv, ma, mb, mdy, ckpt, work, dv,
+  wkv7_tc_bwd_state_kernel<<<dim3(chunks, H, B), STATE_THREADS, ka::SMEM, stream>>>(mr, mw, mk, mv, ma, mb, mdy, mrec, rec, ckpt, work, dv,
                                                                           T, H, chunks);
   RT_CUDA_CHECK(cudaGetLastError());
   RT_CUDA_CHECK(cudaFuncSetAttribute(wkv7_tc_bwd_grad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kb::SMEM));

@@ -47,8 +47,9 @@ __device__ unsigned long long wkv7_trace_ns[64];
 constexpr int KB = 1024;
 constexpr int MAT = N * N;  // floats of one 64 x 64 matrix
 
-// Workspace record per (batch, head, chunk): G, H0, Q, Y0 (row-major 64 x 64 fp32 each).
-enum { REC_G = 0, REC_H0 = 1, REC_Q = 2, REC_Y0 = 3, REC_MATS = 4 };
+// Workspace record per (batch, head, chunk): G, H0, Q, Y0, W, U0 (row-major 64 x 64 fp32 each; W and U0 rounded
+// to tf32). The backward forms the chunk's u rows as U = W S0^T + U0 from the last two.
+enum { REC_G = 0, REC_H0 = 1, REC_Q = 2, REC_Y0 = 3, REC_W = 4, REC_U0 = 5, REC_MATS = 6 };
 
 // Shared-memory map of the chunk kernel (offsets from a 1024-byte aligned base; tiles are K-major SW128).
 // Regions are reused once their last reader is done (noted per line).
@@ -307,6 +308,7 @@ wkv7_tc_chunk_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_const
     //      columns become the rows of [W^T; U0^T] (X1's [A~; R~] was last read by MMA1)
     if (tid < 128) {
       solve_lower(MPL, x);
+      WKV_TRACE(11)
       const int wrow = tid < 64 ? 64 + tid : tid - 64;
 #pragma unroll
       for (int t = 0; t < 64; t += 4) put4(WUT, 128, wrow, t, x[t], x[t + 1], x[t + 2], x[t + 3]);
@@ -323,6 +325,16 @@ wkv7_tc_chunk_kernel(const __grid_constant__ CUtensorMap m_r, const __grid_const
       mma_tf32_tiles(tmem + 192, sm100::smem_u32(VT) - 8192, 64, sm100::smem_u32(KT), 64, 8,
                      sm100::idesc_tf32(128, 64), false);
       sm100::mma_commit(&bars[1]);
+    }
+    {  // while MMA3 runs: W and U0 rows to the record, read out of [W^T; U0^T] (row t, 32 columns per thread)
+      const int t = tid & 63, part = tid >> 6;  // parts: W cols 0..31, 32..63, U0 cols 0..31, 32..63
+      const int base = part < 2 ? 0 : 64, c0 = 32 * (part & 1);
+      float* g = rec + (part < 2 ? REC_W : REC_U0) * MAT + t * 64 + c0;
+#pragma unroll
+      for (int u = 0; u < 32; u += 4)
+        *reinterpret_cast<float4*>(g + u) =
+            make_float4(get1(WUT, 128, base + c0 + u, t), get1(WUT, 128, base + c0 + u + 1, t),
+                        get1(WUT, 128, base + c0 + u + 2, t), get1(WUT, 128, base + c0 + u + 3, t));
     }
     stage = 4;
     ok = wait_all(&bars[1], mph);
@@ -536,7 +548,8 @@ bool fp32_rows_map(CUtensorMap* m, const float* base, long rows) {
 
 }  // namespace
 
-// Floats of the per-chunk record workspace (G, H0, Q, Y0 per chunk and head). The backward reads G and Q.
+// Floats of the per-chunk record workspace (G, H0, Q, Y0, W, U0 per chunk and head). The backward reads G, Q, W
+// and U0.
 #ifdef WKV7_TC_TRACE
 extern "C" void rt_wkv7_tc_fwd_trace(unsigned long long* out, int reset) {
   cudaMemcpyFromSymbol(out, wkv7_trace_ns, sizeof(unsigned long long) * 64);
