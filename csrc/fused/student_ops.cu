@@ -431,6 +431,125 @@ __global__ void pre_wkv_bwd_kernel(const float* __restrict__ g_r, const float* _
   }
 }
 
+// Head size 64, vectorised: a half-warp per (row, head), lane l of it takes n = 4l .. 4l + 3 with 16-byte fp32 loads
+// and 8-byte bf16 stores; a warp takes two rows at a time. Same arithmetic and the same per-block reductions as
+// pre_wkv_bwd_kernel.
+RT_DEVICE float half_warp_sum(float v) {
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+RT_DEVICE void load4_bf16(const bf16* p, float* f) {
+  const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
+  const __nv_bfloat162 lo = *reinterpret_cast<const __nv_bfloat162*>(&u.x);
+  const __nv_bfloat162 hi = *reinterpret_cast<const __nv_bfloat162*>(&u.y);
+  f[0] = __low2float(lo); f[1] = __high2float(lo); f[2] = __low2float(hi); f[3] = __high2float(hi);
+}
+RT_DEVICE void store4_bf16(bf16* p, float a, float b, float c, float d) {
+  const __nv_bfloat162 lo = __floats2bfloat162_rn(a, b), hi = __floats2bfloat162_rn(c, d);
+  uint2 u;
+  u.x = *reinterpret_cast<const unsigned*>(&lo);
+  u.y = *reinterpret_cast<const unsigned*>(&hi);
+  *reinterpret_cast<uint2*>(p) = u;
+}
+RT_DEVICE float4 ld4(const float* p) { return __ldcs(reinterpret_cast<const float4*>(p)); }
+
+__global__ void pre_wkv_bwd64_kernel(const float* __restrict__ g_r, const float* __restrict__ g_w,
+                                     const float* __restrict__ g_kp, const float* __restrict__ g_v,
+                                     const float* __restrict__ g_a, const float* __restrict__ g_b,
+                                     const float* __restrict__ b_r, const float* __restrict__ b_kp,
+                                     const float* __restrict__ b_v, const bf16* __restrict__ k,
+                                     const bf16* __restrict__ la, PreParams p, bf16* __restrict__ dr,
+                                     bf16* __restrict__ dk, bf16* __restrict__ dv, bf16* __restrict__ dlw,
+                                     bf16* __restrict__ dla, float* __restrict__ dw0, float* __restrict__ da0,
+                                     float* __restrict__ dk_k, float* __restrict__ dk_a, long rows, int H,
+                                     int rows_per_block) {
+  constexpr int N = 64;
+  const int h = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, sub = lane >> 4, n0 = 4 * (lane & 15);
+  const int C = H * N, c0 = h * N + n0;
+  const long r0 = (long)blockIdx.y * rows_per_block;
+  const long r1 = min(rows, r0 + rows_per_block);
+  float kkp[4], a0p[4], kap[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    kkp[j] = p.k_k[c0 + j];
+    a0p[j] = p.a0[c0 + j];
+    kap[j] = p.k_a[c0 + j];
+  }
+  float s_w0[4] = {0, 0, 0, 0}, s_a0[4] = {0, 0, 0, 0}, s_kk[4] = {0, 0, 0, 0}, s_ka[4] = {0, 0, 0, 0};
+  for (long base = r0 + 2 * warp; base < r1; base += 2 * PW_WARPS) {  // uniform per warp (shuffles below)
+    const long row = base + sub;
+    const bool valid = row < r1;
+    const long o = (valid ? row : r0) * C + c0;
+    float kv[4], lav[4], z[4], av[4];
+    load4_bf16(k + o, kv);
+    load4_bf16(la + o, lav);
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      z[j] = kv[j] * kkp[j];
+      ss += z[j] * z[j];
+      av[j] = rt::sigmoidf_(a0p[j] + lav[j]);
+    }
+    ss = half_warp_sum(ss);
+    const float norm = fmaxf(sqrtf(ss), 1e-12f);
+    const float inv = 1.f / norm;
+    const float4 gb = ld4(g_b + o), ga = ld4(g_a + o);
+    const float gbv[4] = {gb.x, gb.y, gb.z, gb.w}, gav[4] = {ga.x, ga.y, ga.z, ga.w};
+    float dkk[4], kk[4], dot = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      kk[j] = z[j] * inv;
+      dkk[j] = gbv[j] * av[j] - gav[j];  // b_in = kk * a, a_in = -kk
+      dot += dkk[j] * kk[j];
+    }
+    dot = half_warp_sum(dot);
+    const float4 gkp4 = ld4(g_kp + o), bkp4 = ld4(b_kp + o);
+    const float4 gr4 = ld4(g_r + o), br4 = ld4(b_r + o), gv4 = ld4(g_v + o), bv4 = ld4(b_v + o), gw4 = ld4(g_w + o);
+    const float gkp[4] = {gkp4.x + bkp4.x, gkp4.y + bkp4.y, gkp4.z + bkp4.z, gkp4.w + bkp4.w};
+    const float gwv[4] = {gw4.x, gw4.y, gw4.z, gw4.w};
+    float dkv[4], dpa[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float da = gbv[j] * kk[j] + gkp[j] * kv[j] * kap[j];  // a: from b_in (kk) and from k'
+      dpa[j] = da * av[j] * (1.f - av[j]);
+      const float dz = norm > 1e-12f ? (dkk[j] - kk[j] * dot) * inv : dkk[j] * inv;
+      dkv[j] = gkp[j] * (1.f + (av[j] - 1.f) * kap[j]) + dz * kkp[j];
+      if (valid) {
+        s_w0[j] += gwv[j];
+        s_a0[j] += dpa[j];
+        s_kk[j] += dz * kv[j];
+        s_ka[j] += gkp[j] * kv[j] * (av[j] - 1.f);
+      }
+    }
+    if (valid) {
+      store4_bf16(dr + o, gr4.x + br4.x, gr4.y + br4.y, gr4.z + br4.z, gr4.w + br4.w);
+      store4_bf16(dk + o, dkv[0], dkv[1], dkv[2], dkv[3]);
+      store4_bf16(dv + o, gv4.x + bv4.x, gv4.y + bv4.y, gv4.z + bv4.z, gv4.w + bv4.w);
+      store4_bf16(dlw + o, gwv[0], gwv[1], gwv[2], gwv[3]);
+      store4_bf16(dla + o, dpa[0], dpa[1], dpa[2], dpa[3]);
+    }
+  }
+  __shared__ float red[4][2 * PW_WARPS][N];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    red[0][2 * warp + sub][n0 + j] = s_w0[j];
+    red[1][2 * warp + sub][n0 + j] = s_a0[j];
+    red[2][2 * warp + sub][n0 + j] = s_kk[j];
+    red[3][2 * warp + sub][n0 + j] = s_ka[j];
+  }
+  __syncthreads();
+  for (int n = threadIdx.x; n < N; n += blockDim.x) {
+    float a = 0, b = 0, c2 = 0, d = 0;
+    for (int w = 0; w < 2 * PW_WARPS; ++w) { a += red[0][w][n]; b += red[1][w][n]; c2 += red[2][w][n]; d += red[3][w][n]; }
+    atomicAdd(&dw0[h * N + n], a);
+    atomicAdd(&da0[h * N + n], b);
+    atomicAdd(&dk_k[h * N + n], c2);
+    atomicAdd(&dk_a[h * N + n], d);
+  }
+}
+
 // ---------------------------------------------------------------- LoRA activations
 // mode 0: out = tanh(x); 1: out = sigmoid(x)  (forward, in place allowed)
 __global__ void act_kernel(bf16* __restrict__ x, long n, int mode) {
@@ -726,6 +845,21 @@ extern "C" cudaError_t rt_tm_pre_wkv_bwd(const float* g_r, const float* g_w, con
   PreParams p{w0, a0, k_k, k_a};
   const int rpb = 64;
   dim3 grid(H, (rows + rpb - 1) / rpb);
+  const uintptr_t align = reinterpret_cast<uintptr_t>(g_r) | reinterpret_cast<uintptr_t>(g_w) |
+                          reinterpret_cast<uintptr_t>(g_kp) | reinterpret_cast<uintptr_t>(g_v) |
+                          reinterpret_cast<uintptr_t>(g_a) | reinterpret_cast<uintptr_t>(g_b) |
+                          reinterpret_cast<uintptr_t>(b_r) | reinterpret_cast<uintptr_t>(b_kp) |
+                          reinterpret_cast<uintptr_t>(b_v) | reinterpret_cast<uintptr_t>(k) |
+                          reinterpret_cast<uintptr_t>(la) | reinterpret_cast<uintptr_t>(dr) |
+                          reinterpret_cast<uintptr_t>(dk) | reinterpret_cast<uintptr_t>(dv) |
+                          reinterpret_cast<uintptr_t>(dlw) | reinterpret_cast<uintptr_t>(dla);
+  if (N == 64 && (align & 15) == 0) {
+    pre_wkv_bwd64_kernel<<<grid, PW_WARPS * 32, 0, s>>>(g_r, g_w, g_kp, g_v, g_a, g_b, b_r, b_kp, b_v,
+                                                        (const bf16*)k, (const bf16*)la, p, (bf16*)dr, (bf16*)dk,
+                                                        (bf16*)dv, (bf16*)dlw, (bf16*)dla, dw0, da0, dk_k, dk_a,
+                                                        rows, H, rpb);
+    return cudaGetLastError();
+  }
   pre_wkv_bwd_kernel<<<grid, PW_WARPS * 32, 0, s>>>(g_r, g_w, g_kp, g_v, g_a, g_b, b_r, b_kp, b_v, (const bf16*)k,
                                                     (const bf16*)la,
                                                     p, (bf16*)dr, (bf16*)dk, (bf16*)dv, (bf16*)dlw, (bf16*)dla, dw0,
