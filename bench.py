@@ -13,8 +13,9 @@ A step is one optimizer update of all sixteen layers on one chunk: one
 teacher forward, sixteen student forward/backward passes, sixteen gradient
 reductions (world > 1) and sixteen clip+AdamW updates. The engine issues a
 step's updates at the start of the next step (they run under its teacher
-forward); the timed region starts after the warm-up's updates are issued and
-ends after the K-th step's updates, so it holds exactly K steps of work.
+forward); the timed region starts after the warm-up's updates completed and
+its end event waits for the K-th step's updates (side streams included), so
+it holds exactly K steps of work.
 
 Timing: W untimed warm-up steps, then K steps bracketed by a barrier and
 device synchronisation, timed with CUDA events; the reported number is the
@@ -232,7 +233,7 @@ def build_ours(args, topo, manifest, model_spec):
     def profiled(on):
         engine.profiler.on = on
     step.finish = finish
-    step.flush_updates = engine.flush  # issue the last step's deferred per-layer updates
+    step.flush_updates = engine.join_updates  # issue the last step's updates; the current stream waits for them
     step.phases = phases
     step.snapshot, step.restore = snapshot, restore
     step.set_overlap, step.profiled = set_overlap, profiled
@@ -532,7 +533,7 @@ def main():
     for _ in range(args.warmup):
         step(False)
     if hasattr(step, "flush_updates"):
-        step.flush_updates()  # the last warm-up step's updates stay outside the timed region
+        step.flush_updates()  # the last warm-up step's updates finish before the timed region
     snap = step.snapshot() if hasattr(step, "snapshot") else None
     barrier()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -542,7 +543,7 @@ def main():
     for _ in range(args.steps):
         tokens += step(False)
     if hasattr(step, "flush_updates"):
-        step.flush_updates()  # the K-th step's updates are inside the timed region
+        step.flush_updates()  # the K-th step's updates are inside the timed region (stop waits for them)
     stop.record()
     barrier()
     clocks = sampler.stop()

@@ -20,6 +20,8 @@
 
 #include "../common/common.cuh"
 #include "../common/sm100.cuh"
+#include "../common/tmap.cuh"
+#include "../wkv7/wkv7_tc.cuh"  // tile layouts, triangular solve, tf32 MMA issue
 
 namespace rt_gdn_wy {
 
@@ -875,6 +877,202 @@ __global__ void __launch_bounds__(128) gdn_norm_kernel(const bf16* __restrict__ 
   }
 }
 
+// ---------------------------------------------------------------- 1 on tcgen05 (head dim 128)
+// Per (chunk, value head, batch), 256 threads: TMA brings the chunk's normalised k rows (fp32, K-major 128-byte
+// swizzled) and raw v rows (bf16); K K^T is one tf32 MMA into TMEM; T = (I + A)^{-1} comes column by column from
+// an fp32 forward substitution (threads 0..63, one unit right-hand side each) while the other threads build the
+// B operand [V'^T; K'^T] with V' = beta v and K' = diag(beta e^Lambda) k; then [U0 | -W] = T [V' | K'] is a
+// second tf32 MMA (N = 256). Waits are bounded; a failure is recorded in the status word.
+namespace wyt {
+constexpr int KB = 1024;
+constexpr int KT = 0;          // k rows: 64 x 128 fp32, 4 atoms (read as 128 rows: the next 8 KB stay in bounds)
+constexpr int VR = 32 * KB;    // v rows: two bf16 64 x 64 swizzled boxes
+constexpr int MPL = 48 * KB;   // -A, plain swizzled 64 x 64 fp32
+constexpr int TA = 64 * KB;    // T (rows t, K = s), 2 atoms (read as 128 rows)
+constexpr int BT = 80 * KB;    // [V'^T; K'^T]: 256 rows, K = s, 2 atoms of 32 KB
+constexpr int MISC = 144 * KB; // barriers, TMEM slot, lam / beta / e^lam, scan scratch
+constexpr int BYTES = 145 * KB + 1024;
+}  // namespace wyt
+
+__global__ void __launch_bounds__(256, 1)
+gdn_wy_tc_kernel(const __grid_constant__ CUtensorMap m_k, const __grid_constant__ CUtensorMap m_v,
+                 const bf16* __restrict__ pa, const bf16* __restrict__ pb, long ab_stride,
+                 const float* __restrict__ A_log, const float* __restrict__ dt_bias, float* __restrict__ Wout,
+                 float* __restrict__ Uout, float* __restrict__ lam_out, int T, int Tp, int Hk, int Hv,
+                 int* __restrict__ status) {
+  constexpr int D = 128;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = sm100::align_smem_1024(smem_raw);
+  uint8_t *KTt = sm + wyt::KT, *VR = sm + wyt::VR, *TA = sm + wyt::TA, *BT = sm + wyt::BT;
+  float* MPL = reinterpret_cast<float*>(sm + wyt::MPL);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + wyt::MISC);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + wyt::MISC + 16);
+  float* lam = reinterpret_cast<float*>(sm + wyt::MISC + 64);
+  float* beta = lam + LC;
+  float* elam = beta + LC;
+  float* tmp = elam + LC;
+  const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5, quarter = warp & 3, colh = warp >> 2;
+  const int kh = h / (Hv / Hk);
+  const int t0 = c * LC;
+  if (tid == 0) {
+    sm100::mbar_init(&bars[0], 1);
+    sm100::mbar_init(&bars[1], 1);
+    sm100::fence_barrier_init();
+  }
+  if (warp == 0) {
+    sm100::tmem_alloc(tslot, 256);
+    sm100::tmem_relinquish();
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem = *tslot;
+  if (tid == 0) {
+    sm100::mbar_expect_tx(&bars[0], 48 * wyt::KB);
+#pragma unroll
+    for (int a = 0; a < 4; ++a) sm100::tma_load_3d(KTt + a * 8 * wyt::KB, &m_k, &bars[0], kh * D + 32 * a, t0, b);
+    const int vcol = 2 * Hk * D + h * D;
+#pragma unroll
+    for (int a = 0; a < 2; ++a) sm100::tma_load_3d(VR + a * 8 * wyt::KB, &m_v, &bars[0], vcol + 64 * a, t0, b);
+  }
+  // gates of the chunk's steps (padded steps: beta = 0, g = 0)
+  float g = 0.f, bt = 0.f;
+  if (tid < LC) {
+    const int t = t0 + tid;
+    if (t < T) {
+      g = gate_g(rt::to_f(pa[((long)b * T + t) * ab_stride + h]), dt_bias[h], -expf(A_log[h]));
+      bt = __bfloat162float(__float2bfloat16_rn(rt::sigmoidf_(rt::to_f(pb[((long)b * T + t) * ab_stride + h]))));
+    }
+  }
+  const float lt = scan64(tid < LC ? g : 0.f, tmp);
+  if (tid < LC) {
+    lam[tid] = lt;
+    beta[tid] = bt;
+    elam[tid] = expf(lt);
+    lam_out[((long)b * Hv + h) * Tp + t0 + tid] = lt;
+  }
+  int stage = 1;
+  bool ok = sm100::mbar_wait_bounded(&bars[0], 0);
+  ok = __syncthreads_and(ok ? 1 : 0) != 0;  // also publishes lam / beta
+  uint32_t mph = 0;
+  if (ok) {
+    if (tid == 0) {  // K K^T (cols 0..63): A = k rows (64, read as 128), B = k rows; K = 128
+      wtc::fence_async_smem();
+      sm100::tc_fence_after();
+      wtc::mma_tf32_tiles(tmem, sm100::smem_u32(KTt), 64, sm100::smem_u32(KTt), 64, 16, sm100::idesc_tf32(128, 64),
+                          false);
+      sm100::mma_commit(&bars[1]);
+    }
+    // B operand rows while the MMA runs: row r < 128: V'^T row i = r (beta_s v_s[i]); else K'^T row j = r - 128
+    // (beta_s e^{Lambda_s} k_s[j]); K = s, 64 steps.
+    {
+      const int r = tid;
+#pragma unroll 1
+      for (int s0 = 0; s0 < LC; s0 += 16) {
+        float x[16];
+        if (r < D) {
+          const uint8_t* box = VR + (r >> 6) * 8 * wyt::KB;
+#pragma unroll
+          for (int q = 0; q < 16; ++q) x[q] = wtc::raw(box, s0 + q, r & 63) * beta[s0 + q];
+        } else {
+          const int j = r - D;
+#pragma unroll
+          for (int q = 0; q < 16; ++q) x[q] = wtc::get1(KTt, 64, s0 + q, j) * (beta[s0 + q] * elam[s0 + q]);
+        }
+#pragma unroll
+        for (int q = 0; q < 16; q += 4) wtc::put4(BT, 256, r, s0 + q, x[q], x[q + 1], x[q + 2], x[q + 3]);
+      }
+    }
+    stage = 2;
+    ok = sm100::mbar_wait_bounded(&bars[1], mph);
+    ok = __syncthreads_and(ok ? 1 : 0) != 0;
+    mph ^= 1;
+    sm100::tc_fence_after();
+  }
+  if (ok) {
+    // -A[t][s] = -beta_t e^{Lambda_t - Lambda_s} (k_t . k_s) for s < t (lanes 0..63, 32 columns per thread)
+    if (quarter < 2) {
+      const int t = 32 * quarter + (tid & 31), s0 = 32 * colh;
+      float d[32];
+      sm100::tmem_ld32(tmem + ((uint32_t)(32 * quarter) << 16) + s0, d);
+      sm100::tmem_wait_ld();
+      const float bl = beta[t], lt = lam[t];
+#pragma unroll
+      for (int u = 0; u < 32; u += 4) {
+        float v[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int s = s0 + u + e;
+          v[e] = s < t ? -bl * expf(lt - lam[s]) * d[u + e] : 0.f;
+        }
+        *reinterpret_cast<float4*>(&MPL[wtc::poff(t, s0 + u)]) = make_float4(v[0], v[1], v[2], v[3]);
+      }
+    }
+    __syncthreads();
+    // T column c = (I - M)^{-1} e_c with M = -A (threads 0..63), into the A operand tile (rows t, K = s)
+    if (tid < LC) {
+      float x[64];
+#pragma unroll
+      for (int t = 0; t < 64; ++t) x[t] = t == tid ? 1.f : 0.f;
+      wtc::solve_lower(MPL, x);
+#pragma unroll
+      for (int t = 0; t < 64; ++t) wtc::put1(TA, 64, t, tid, x[t]);
+    }
+    wtc::tc_sync();
+    if (tid == 0) {  // [U0 | -W] = T [V' | K'] (cols 0..255)
+      wtc::mma_tf32_tiles(tmem, sm100::smem_u32(TA), 64, sm100::smem_u32(BT), 256, 8, sm100::idesc_tf32(128, 256),
+                          false);
+      sm100::mma_commit(&bars[1]);
+    }
+    stage = 3;
+    ok = sm100::mbar_wait_bounded(&bars[1], mph);
+    ok = __syncthreads_and(ok ? 1 : 0) != 0;
+    mph ^= 1;
+    sm100::tc_fence_after();
+  }
+  if (ok && quarter < 2) {  // rows t: U0 (warps with colh 0: cols 0..127), W = -(cols 128..255) (colh 1)
+    const int t = 32 * quarter + (tid & 31);
+    const long row = ((long)b * Hv + h) * Tp + t0 + t;
+    float* dst = (colh ? Wout : Uout) + row * D;
+    const float sign = colh ? -1.f : 1.f;
+    const uint32_t base = tmem + ((uint32_t)(32 * quarter) << 16) + 128 * colh;
+#pragma unroll 1
+    for (int part = 0; part < 4; ++part) {
+      float d[32];
+      sm100::tmem_ld32(base + 32 * part, d);
+      sm100::tmem_wait_ld();
+#pragma unroll
+      for (int u = 0; u < 32; u += 4)
+        *reinterpret_cast<float4*>(dst + 32 * part + u) =
+            make_float4(sign * d[u], sign * d[u + 1], sign * d[u + 2], sign * d[u + 3]);
+    }
+  }
+  if (!ok && tid == 0 && status) atomicCAS(status, 0, 0x500 | stage);
+  if (!ok && stage > 1) sm100::mbar_wait_bounded(&bars[1], mph);
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem, 256);
+  }
+}
+
+// TMA maps of the tcgen05 WY kernel; false if the layouts do not allow them (the SIMT kernel is used then).
+bool wy_tc_maps(CUtensorMap* mk, CUtensorMap* mv, const float* kn, const void* qkv, long row_stride, int B, int T,
+                int Hk) {
+  if ((row_stride % 8) || (reinterpret_cast<uintptr_t>(qkv) & 15) || (reinterpret_cast<uintptr_t>(kn) & 15))
+    return false;
+  const uint64_t kd[3] = {(uint64_t)Hk * 128, (uint64_t)T, (uint64_t)B};
+  const uint64_t ks[2] = {(uint64_t)Hk * 128 * 4, (uint64_t)T * Hk * 128 * 4};
+  const uint32_t kbox[3] = {32, 64, 1};
+  const uint64_t vd[3] = {(uint64_t)row_stride, (uint64_t)T, (uint64_t)B};
+  const uint64_t vs[2] = {(uint64_t)row_stride * 2, (uint64_t)T * row_stride * 2};
+  const uint32_t vbox[3] = {64, 64, 1};
+  return tmap::encode(mk, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, kn, kd, ks, kbox) &&
+         tmap::encode(mv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, qkv, vd, vs, vbox);
+}
+
 template <int D>
 long workspace(int B, int T, int Hk, int Hv) {
   const long Tp = (T + LC - 1) / LC * LC, chunks = Tp / LC;
@@ -901,9 +1099,22 @@ cudaError_t launch(const void* qkv, long row_stride, const void* a, const void* 
   RT_CUDA_CHECK(cudaFuncSetAttribute(gdn_wy_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, s1));
   RT_CUDA_CHECK(cudaFuncSetAttribute(gdn_state_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, s2));
   RT_CUDA_CHECK(cudaFuncSetAttribute(gdn_out_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, s3));
-  gdn_wy_kernel<D><<<dim3(chunks, Hv, B), NT, s1, stream>>>(kn, (const bf16*)qkv, row_stride, (const bf16*)a,
-                                                             (const bf16*)bb, ab_stride, A_log, dt_bias, W, U, lam, T,
-                                                             Tp, Hk, Hv);
+  // WY pass: tcgen05 form for head dim 128 (THESEUS_GDN_WY_TC=0 selects the SIMT kernel, which other sizes use)
+  static const bool wy_tc = [] {
+    const char* e = getenv("THESEUS_GDN_WY_TC");
+    return !(e && e[0] == '0');
+  }();
+  CUtensorMap mk, mv;
+  if (D == 128 && wy_tc && wy_tc_maps(&mk, &mv, kn, qkv, row_stride, B, T, Hk)) {
+    RT_CUDA_CHECK(cudaFuncSetAttribute(gdn_wy_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, wyt::BYTES));
+    gdn_wy_tc_kernel<<<dim3(chunks, Hv, B), 256, wyt::BYTES, stream>>>(mk, mv, (const bf16*)a, (const bf16*)bb,
+                                                                        ab_stride, A_log, dt_bias, W, U, lam, T, Tp,
+                                                                        Hk, Hv, nullptr);
+  } else {
+    gdn_wy_kernel<D><<<dim3(chunks, Hv, B), NT, s1, stream>>>(kn, (const bf16*)qkv, row_stride, (const bf16*)a,
+                                                               (const bf16*)bb, ab_stride, A_log, dt_bias, W, U, lam,
+                                                               T, Tp, Hk, Hv);
+  }
   RT_CUDA_CHECK(cudaGetLastError());
   // tcgen05 state pass for head dim 128 (THESEUS_GDN_STATE_TC=0 selects the SIMT pass, which other sizes use)
   static const bool state_tc = [] {

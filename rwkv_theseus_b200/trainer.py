@@ -173,6 +173,13 @@ class StepEngine:
                             student.update()
         return {layer: student.report for layer, student in self.students.items()}
 
+    def join_updates(self):
+        """Issue any deferred updates and make the current stream wait for every layer's update (local AdamW or
+        peer exchange): after this, work recorded on the current stream follows all of them."""
+        self.flush()
+        for student in self.students.values():
+            student.join_update()
+
     def flush(self):
         """Issue the updates deferred from the last step (in layer order, the same on every rank) and the metric
         reads waiting for them. Called at the start of every step; call it before anything that reads student
