@@ -38,7 +38,7 @@ constexpr uint32_t TMEM_O = 0, TMEM_S = 256;
 constexpr float RESCALE_THRESHOLD = 8.f;          // log2 units
 
 struct AttnArgs {
-  int T, Hq, Hkv, offset, cap;
+  int B, T, Hq, Hkv, offset, cap;
   float scale_log2;
   const bf16* gate;
   long gate_row, gate_head;
@@ -94,7 +94,11 @@ flash_attn_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_const
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int q0 = blockIdx.x * BQ, h = blockIdx.y, b = blockIdx.z;
+  // Longest first: the 1-D grid walks query tiles from the last (most keys under the causal mask) to the first,
+  // all heads and batches of one tile before the next, so the shortest tiles fill the tail of the launch.
+  const int tiles = (args.T + BQ - 1) / BQ, per = args.Hq * args.B;
+  const int tile = tiles - 1 - (int)blockIdx.x / per, rem = (int)blockIdx.x % per;
+  const int q0 = tile * BQ, h = rem % args.Hq, b = rem / args.Hq;
   const int g = h / (args.Hq / args.Hkv);
   const int t_last = min(q0 + BQ, args.T) - 1;
   const int nblk = (args.offset + t_last) / BKV + 1;
@@ -344,12 +348,12 @@ extern "C" cudaError_t rt_flash_attention_fwd(const void* q, const void* keys, c
       !make_map(&tv, values, Hkv, (uint64_t)B * cap, BKV))
     return cudaErrorInvalidValue;
   AttnArgs args;
-  args.T = T; args.Hq = Hq; args.Hkv = Hkv; args.offset = offset; args.cap = cap;
+  args.B = B; args.T = T; args.Hq = Hq; args.Hkv = Hkv; args.offset = offset; args.cap = cap;
   args.scale_log2 = 0.0625f * 1.4426950408889634f;
   args.gate = (const bf16*)gate; args.gate_row = gate_row; args.gate_head = gate_head;
   args.out = (bf16*)out; args.status = status;
   RT_CUDA_CHECK(cudaFuncSetAttribute(flash_attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-  dim3 grid((T + BQ - 1) / BQ, Hq, B);
-  flash_attn_fwd_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(tq, tk, tv, args);
+  const unsigned ctas = (unsigned)(((T + BQ - 1) / BQ) * Hq * B);
+  flash_attn_fwd_kernel<<<ctas, THREADS, SMEM_BYTES, stream>>>(tq, tk, tv, args);
   return cudaGetLastError();
 }
