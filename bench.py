@@ -331,7 +331,7 @@ def build_reference(args, topo_unused, manifest, model_spec):
 OWN_KERNELS = ("wkv7_", "gemm_kernel", "rmsnorm_", "conv1d_silu", "gdn_", "mix_kernel", "mix_bwd", "pre_wkv",
                "post_wkv", "nmse_loss", "adamw_kernel", "scale_norm", "act_kernel", "act_bwd", "norm_rope",
                "copy_rows", "to_bf16", "report_kernel", "gated_rmsnorm", "flash_attn", "exchange_", "loss_rows",
-               "norm2_kernel", "skinny_", "kl_", "zero_f32", "copy_bytes", "mix_vec")
+               "norm2_kernel", "skinny_", "kl_", "zero_f32", "copy_bytes", "mix_vec", "embed_rows")
 
 
 def count_launches(step_fn):

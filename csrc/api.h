@@ -68,6 +68,8 @@ cudaError_t rt_gated_rmsnorm(const void* x, const void* z, const float* w, void*
 cudaError_t rt_norm_rope(const void* src, long src_stride, long head_stride, const float* w, const float* inv_freq,
                          void* dst, int B, int T, int heads, long dst_batch_stride, int pos0, int D, int rot, float eps,
                          cudaStream_t stream);
+cudaError_t rt_embed_rows(const long* ids, const void* table, long vocab, void* out, int width, long rows,
+                          cudaStream_t stream);
 cudaError_t rt_copy_rows(const void* src, long src_stride, void* dst, int B, int T, long dst_batch_stride, int width,
                          cudaStream_t stream);
 long rt_gdn_workspace_floats(int B, int T, int Hk, int Hv, int D, long row_stride);

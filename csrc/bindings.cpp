@@ -303,6 +303,22 @@ void norm_rope_(at::Tensor src, int64_t heads, at::Tensor w, at::Tensor inv_freq
              "norm_rope");
 }
 
+// ids [..] int64 -> [.., width] bf16 rows of `table` [vocab, width] (bf16, contiguous).
+at::Tensor embed_rows(at::Tensor ids, at::Tensor table) {
+  TORCH_CHECK(ids.is_cuda() && ids.scalar_type() == at::kLong && table.is_cuda() &&
+                  table.scalar_type() == at::kBFloat16 && table.is_contiguous() && table.dim() == 2,
+              "embed_rows needs int64 ids and a contiguous bf16 [vocab, width] table on the GPU");
+  c10::cuda::CUDAGuard guard(ids.device());
+  auto flat = ids.contiguous();
+  auto sizes = ids.sizes().vec();
+  sizes.push_back(table.size(1));
+  auto out = at::empty(sizes, table.options());
+  check_cuda(rt_embed_rows(reinterpret_cast<const long*>(flat.data_ptr<int64_t>()), table.data_ptr(),
+                           table.size(0), out.data_ptr(), (int)table.size(1), flat.numel(), stream_of(table)),
+             "embed_rows");
+  return out;
+}
+
 void copy_rows_(at::Tensor src, at::Tensor dst, int64_t pos0) {
   TORCH_CHECK(src.is_cuda() && src.scalar_type() == at::kBFloat16 && src.dim() == 2 && src.stride(-1) == 1,
               "src must be 2-D bf16 rows");
@@ -731,6 +747,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gated_rmsnorm", &gated_rmsnorm);
   m.def("norm_rope_", &norm_rope_);
   m.def("copy_rows_", &copy_rows_);
+  m.def("embed_rows", &embed_rows, "embedding lookup (int64 ids, bf16 table) by this package's kernel");
   m.def("gdn_forward", &gdn_forward);
   m.def("tm_mix", &tm_mix);
   m.def("tm_mix_bwd", &tm_mix_bwd);

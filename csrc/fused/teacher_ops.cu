@@ -255,6 +255,21 @@ __global__ void copy_rows_kernel(const bf16* __restrict__ src, long src_stride, 
   for (int c = threadIdx.x; c < width / 8; c += blockDim.x) out[c] = in[c];
 }
 
+// out[row] = table[ids[row]] (bf16 rows of `width`, 16-byte moves); ids outside [0, vocab) give a zero row.
+__global__ void embed_rows_kernel(const long* __restrict__ ids, const bf16* __restrict__ table, long vocab,
+                                  bf16* __restrict__ out, int width, long rows) {
+  const long row = blockIdx.x;
+  if (row >= rows) return;
+  const long id = ids[row];
+  uint4* o = reinterpret_cast<uint4*>(out + row * (long)width);
+  if (id < 0 || id >= vocab) {
+    for (int c = threadIdx.x; c < width / 8; c += blockDim.x) o[c] = make_uint4(0, 0, 0, 0);
+    return;
+  }
+  const uint4* in = reinterpret_cast<const uint4*>(table + id * (long)width);
+  for (int c = threadIdx.x; c < width / 8; c += blockDim.x) o[c] = __ldg(in + c);
+}
+
 }  // namespace
 
 extern "C" cudaError_t rt_rmsnorm_1p(const void* x, const void* h, const float* w, void* sum_out, void* out, long rows,
@@ -329,6 +344,16 @@ extern "C" cudaError_t rt_norm_rope(const void* src, long src_stride, long head_
   norm_rope_kernel<<<(rows + warps - 1) / warps, warps * 32, warps * D * sizeof(float), stream>>>(
       (const bf16*)src, src_stride, head_stride, w, inv_freq, (bf16*)dst, heads, T, dst_batch_stride, pos0, D, rot, eps,
       rows);
+  return cudaGetLastError();
+}
+
+// Embedding lookup: out [rows, width] bf16 = table [vocab, width] rows at ids (int64).
+extern "C" cudaError_t rt_embed_rows(const long* ids, const void* table, long vocab, void* out, int width, long rows,
+                                     cudaStream_t stream) {
+  if (width % 8 || (reinterpret_cast<uintptr_t>(table) & 15) || (reinterpret_cast<uintptr_t>(out) & 15))
+    return cudaErrorInvalidValue;
+  if (rows <= 0) return cudaSuccess;
+  embed_rows_kernel<<<rows, 128, 0, stream>>>(ids, (const bf16*)table, vocab, (bf16*)out, width, rows);
   return cudaGetLastError();
 }
 

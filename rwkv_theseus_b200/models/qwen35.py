@@ -226,7 +226,7 @@ class TextModel(nn.Module):
         the pass ends inside block ``stop_at`` and returns its mixer (attention) output: the blocks before it and
         its own mixer update the cache; its residual and MLP, the later blocks and the final norm are not run."""
         start = int(positions[0]) if torch.is_tensor(positions) else int(positions)
-        x = self.embed_tokens(ids)
+        x = T.embed(ids, self.embed_tokens.weight)
         rope = T.rope_tables(self.inv_freq, start, ids.shape[1], x.device, x.dtype)
         # Each block's MLP residual is added by the next norm's fused add + RMSNorm kernel (x + mlp rounded to
         # x.dtype, then normalised), the same values as DecoderLayer.forward followed by the next input norm.

@@ -25,6 +25,13 @@ def linear(x, weight):
     return F.linear(x, weight.to(x.dtype))
 
 
+def embed(ids, weight):
+    """Embedding lookup; CUDA bf16 tables use this package's row-gather kernel."""
+    if ids.is_cuda and weight.dtype == torch.bfloat16 and weight.is_contiguous() and weight.shape[1] % 8 == 0:
+        return native().embed_rows(ids, weight)
+    return F.embedding(ids, weight)
+
+
 def rmsnorm(x, weight, eps):
     if _cuda(x):
         return native().rmsnorm_1p(x.contiguous(), f32(weight), float(eps))
