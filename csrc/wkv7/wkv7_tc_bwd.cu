@@ -57,7 +57,7 @@ RT_DEVICE bool wait_all(uint64_t* bar, uint32_t parity) {
 // grid (B*H, 8 row blocks of 8 value rows), 128 threads: thread = column j and rows r0..r0+3 of the block.
 constexpr int BS_ROWS = 8;
 constexpr int GP = 68;  // padded row of G (conflict-free float4 reads of G[j][j'..j'+3] across j)
-constexpr int BSCAN_SMEM = (2 * 64 * GP + 2 * MAT + BS_ROWS * 64 + BS_ROWS * 64) * 4;
+constexpr int BSCAN_SMEM = (2 * 64 * GP + 2 * MAT + BS_ROWS * 64) * 4 + 2 * 64 * BS_ROWS * 2;
 __global__ void __launch_bounds__(128)
 wkv7_tc_bscan_kernel(const float* __restrict__ rec, const __nv_bfloat16* __restrict__ dy,
                      const float* __restrict__ dend, float* __restrict__ work, float* __restrict__ ds0, int T, int H,
@@ -66,12 +66,12 @@ wkv7_tc_bscan_kernel(const float* __restrict__ rec, const __nv_bfloat16* __restr
   float* Gs = bsm;                     // [2][64][GP]
   float* Qs = Gs + 2 * 64 * GP;        // [2][64][64]
   float* dS = Qs + 2 * MAT;            // [8][64]
-  float* dYs = dS + BS_ROWS * 64;      // [64 t][8 rows]
+  __nv_bfloat16* dYs = reinterpret_cast<__nv_bfloat16*>(dS + BS_ROWS * 64);  // [2][64 t][8 rows] raw bf16
   const int bh = blockIdx.x, rb = blockIdx.y * BS_ROWS, tid = threadIdx.x;
   const int b = bh / H, h = bh % H;
   const int j = tid & 63, r0 = (tid >> 6) * 4;
   const float* rec0 = rec + (long)bh * chunks * REC_MATS * MAT;
-  auto prefetch = [&](int c) {
+  auto prefetch = [&](int c) {  // G_c, Q_c and the chunk's dY rows (this block's 8 value columns), one group
     const float* g = rec0 + (long)c * REC_MATS * MAT + REC_G * MAT;
     const float* q = rec0 + (long)c * REC_MATS * MAT + REC_Q * MAT;
     float* gd = Gs + (c & 1) * 64 * GP;
@@ -79,6 +79,12 @@ wkv7_tc_bscan_kernel(const float* __restrict__ rec, const __nv_bfloat16* __restr
     for (int e = tid; e < MAT / 4; e += 128) {
       rt::cp_async16(gd + (e >> 4) * GP + 4 * (e & 15), g + 4 * e, true);
       rt::cp_async16(qd + 4 * e, q + 4 * e, true);
+    }
+    if (tid < 64) {  // 16 bytes per step; past the sequence end the copy reads nothing and fills zeros
+      const int tg = c * L + tid;
+      const bool valid = tg < T;
+      rt::cp_async16(dYs + ((c & 1) * 64 + tid) * BS_ROWS,
+                     dy + (((long)b * T + (valid ? tg : 0)) * H + h) * N + rb, valid);
     }
     rt::cp_async_commit();
   };
@@ -94,23 +100,12 @@ wkv7_tc_bscan_kernel(const float* __restrict__ rec, const __nv_bfloat16* __restr
     float* wk = work + ((long)bh * chunks + c) * WK_MATS * MAT + WK_DS * MAT;
 #pragma unroll
     for (int q = 0; q < 4; ++q) wk[(rb + r0 + q) * N + j] = s[q];
-    if (tid < 64) {  // dY rows t of this block's 8 value columns (one 16-byte load per step)
-      const int t = tid, tg = c * L + t;
-      float v[8];
-      if (tg < T) {
-        rt::unpack8(__ldg(reinterpret_cast<const uint4*>(dy + (((long)b * T + tg) * H + h) * N + rb)), v);
-      } else {
-#pragma unroll
-        for (int u = 0; u < 8; ++u) v[u] = 0.f;
-      }
-#pragma unroll
-      for (int u = 0; u < 8; ++u) dYs[t * 8 + u] = v[u];
-    }
     rt::cp_async_wait<0>();
-    __syncthreads();  // G_c, Q_c landed; dS, dY visible; the other buffers are no longer read
+    __syncthreads();  // G_c, Q_c, dY_c landed; dS visible; the other buffers are no longer read
     if (c > 0) prefetch(c - 1);
     const float* g = Gs + (c & 1) * 64 * GP;
     const float* qm = Qs + (c & 1) * MAT;
+    const __nv_bfloat16* dyc = dYs + (c & 1) * 64 * BS_ROWS;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 4
     for (int jp = 0; jp < 64; jp += 4) {
@@ -121,14 +116,16 @@ wkv7_tc_bscan_kernel(const float* __restrict__ rec, const __nv_bfloat16* __restr
         acc[q] += sv.x * gv.x + sv.y * gv.y + sv.z * gv.z + sv.w * gv.w;
       }
     }
-#pragma unroll 4
+#pragma unroll 8
     for (int t = 0; t < 64; ++t) {
       const float qv = qm[t * 64 + j];
-      const float4 d4 = *reinterpret_cast<const float4*>(dYs + t * 8 + r0);
-      acc[0] += d4.x * qv;
-      acc[1] += d4.y * qv;
-      acc[2] += d4.z * qv;
-      acc[3] += d4.w * qv;
+      const uint2 raw4 = *reinterpret_cast<const uint2*>(dyc + t * BS_ROWS + r0);
+      const __nv_bfloat162 lo = *reinterpret_cast<const __nv_bfloat162*>(&raw4.x);
+      const __nv_bfloat162 hi = *reinterpret_cast<const __nv_bfloat162*>(&raw4.y);
+      acc[0] += __low2float(lo) * qv;
+      acc[1] += __high2float(lo) * qv;
+      acc[2] += __low2float(hi) * qv;
+      acc[3] += __high2float(hi) * qv;
     }
     __syncthreads();
 #pragma unroll

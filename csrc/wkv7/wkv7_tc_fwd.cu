@@ -407,14 +407,16 @@ __global__ void __launch_bounds__(128)
 wkv7_tc_scan_kernel(const float* __restrict__ ws, const float* __restrict__ s0, float* __restrict__ ckpt,
                     float* __restrict__ s_end, int chunks) {
   __shared__ __align__(16) float G[2][MAT];
+  __shared__ __align__(16) float H[2][SCAN_ROWS][N];
   __shared__ __align__(16) float S[SCAN_ROWS][N];
   const int bh = blockIdx.x, rb = blockIdx.y * SCAN_ROWS, tid = threadIdx.x;
   const int r = tid >> 4, j0 = 4 * (tid & 15);
   const float* rec0 = ws + (long)bh * chunks * REC_MATS * MAT;
-  auto prefetch = [&](int c) {
+  auto prefetch = [&](int c) {  // G_c and this block's rows of H0_c, one group
     const float* src = rec0 + (long)c * REC_MATS * MAT + REC_G * MAT;
     float* dst = G[c & 1];
     for (int e = tid; e < MAT / 4; e += 128) rt::cp_async16(dst + 4 * e, src + 4 * e, true);
+    rt::cp_async16(&H[c & 1][r][j0], rec0 + (long)c * REC_MATS * MAT + REC_H0 * MAT + (long)(rb + r) * N + j0, true);
     rt::cp_async_commit();
   };
   prefetch(0);
@@ -424,12 +426,10 @@ wkv7_tc_scan_kernel(const float* __restrict__ ws, const float* __restrict__ s0, 
 #pragma unroll 1
   for (int c = 0; c < chunks; ++c) {
     *reinterpret_cast<float4*>(ck + (long)c * MAT) = s;
-    const float4 hrow = __ldg(reinterpret_cast<const float4*>(rec0 + (long)c * REC_MATS * MAT + REC_H0 * MAT +
-                                                             (long)(rb + r) * N + j0));
     rt::cp_async_wait<0>();
-    __syncthreads();  // G_c landed, S visible, buffer (c + 1) & 1 no longer read
+    __syncthreads();  // G_c and H0_c landed, S visible, buffers (c + 1) & 1 no longer read
+    float4 acc = *reinterpret_cast<const float4*>(&H[c & 1][r][j0]);
     if (c + 1 < chunks) prefetch(c + 1);
-    float4 acc = hrow;
     const float* g = G[c & 1];
 #pragma unroll 8
     for (int j = 0; j < N; ++j) {
