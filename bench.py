@@ -285,8 +285,10 @@ def build_reference(args, topo_unused, manifest, model_spec):
         students[layer] = prepare_student(model, layer, cfg, topo, None, total_steps=10 ** 6, detached=True)
         captures[layer] = Capture(model.model.layers[layer].self_attn)
 
-    def step(read):
-        # The body of the reference train.py step loop (train.py:153-211) with grad_accum_steps = 1.
+    def step(read, mark=None):
+        # The body of the reference train.py step loop (train.py:153-211) with grad_accum_steps = 1. `mark(kind)`
+        # (phase split only) records a CUDA event at the start of each phase of that kind.
+        mark = mark or (lambda kind: None)
         accum = {layer: torch.zeros(3, device=topo.device) for layer in order}
         for _, _, optimizer, _ in students.values():
             optimizer.zero_grad(set_to_none=True)
@@ -295,8 +297,10 @@ def build_reference(args, topo_unused, manifest, model_spec):
             runner.reset()
             for adapter, *_ in students.values():
                 adapter.state = None
+        mark("teacher")
         runner.forward(batch["ids"].to(topo.device))
         for layer in order:
+            mark("students")
             adapter, ddp, optimizer, scheduler = students[layer]
             capture = captures[layer]
             x, target = capture.x, capture.y
@@ -308,6 +312,7 @@ def build_reference(args, topo_unused, manifest, model_spec):
             stats[0].backward()
             del prediction, state, stats, x, target
             capture.x = capture.y = None
+            mark("updates")
             topo.student_sum(accum[layer])
             count = accum[layer][2]
             if count.item() <= 0:
@@ -322,7 +327,27 @@ def build_reference(args, topo_unused, manifest, model_spec):
             optimizer.zero_grad(set_to_none=True)
             if read:
                 metrics(accum[layer]) | {"grad_norm": norm.item()}
+        mark("end")
         return int(batch["ids"].numel())
+
+    def phases():
+        """Device ms per phase kind of one extra, untimed step, between CUDA events recorded on the reference's
+        stream at each phase start: teacher forward, student forward + backward (with DDP's gradient all-reduce,
+        which runs inside backward), and the update (metric sum, gradient scale, clip, AdamW, scheduler). The same
+        keys as this package's split."""
+        marks = []
+
+        def mark(kind):
+            event = torch.cuda.Event(enable_timing=True)
+            event.record()
+            marks.append((kind, event))
+        step(False, mark)
+        torch.cuda.synchronize(topo.device)
+        out = {"step_ms": marks[0][1].elapsed_time(marks[-1][1])}
+        for kind in ("teacher", "students", "updates"):
+            out[f"{kind}_ms"] = sum(a.elapsed_time(b) for (k, a), (_, b) in zip(marks, marks[1:]) if k == kind)
+        return {k: round(v, 3) for k, v in out.items()}
+    step.phases = phases
     return step, topo
 
 
@@ -409,6 +434,26 @@ def print_breakdown(step_fn, rank):
         print(f"{total / 1000:9.3f} ms total kernel time")
         print_timeline(prof)
         print_phase_kernels(prof)
+        print_host_api(prof)
+
+
+def print_host_api(prof):
+    """Host time spent inside CUDA runtime/driver calls during the profiled step, by call name (how much of the
+    host's issue time the API calls themselves take, against the Python and C++ code around them)."""
+    import torch
+    cpu = torch.autograd.DeviceType.CPU
+    calls = {}
+    for e in prof.profiler.kineto_results.events():
+        name = e.name()
+        if e.device_type() != cpu or not name.startswith("cu"):
+            continue
+        entry = calls.setdefault(name, [0, 0])
+        entry[0] += e.duration_ns()
+        entry[1] += 1
+    total = sum(ns for ns, _ in calls.values())
+    print(f"host API calls: {total / 1e6:.3f} ms in {sum(n for _, n in calls.values())} calls")
+    for name, (ns, n) in sorted(calls.items(), key=lambda kv: -kv[1][0])[:12]:
+        print(f"    {ns / 1e6:8.3f} ms {n:6d}  {name[:70]}")
 
 
 def print_phase_kernels(prof):

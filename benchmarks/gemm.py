@@ -2,7 +2,9 @@
 """tcgen05 GEMM vs cuBLAS (torch.matmul) on the projection shapes of the 27B
 migration step (1024 tokens): teacher MLP/GDN/attention projections and the
 student C x C GEMMs in forward, input-gradient (MN-major B) and
-weight-gradient (MN-major A and B) form. Device time with CUDA events,
+weight-gradient (MN-major A and B) form. Rows with G = 3 are the student's
+r/k/v projections as one grouped launch (``gemm_group``) against one batched
+cuBLAS call (``torch.bmm``) on the same operands. Device time with CUDA events,
 median of --iters after --warmup; operands rotate over buffers larger than L2.
 """
 import argparse
@@ -15,7 +17,7 @@ import torch
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 from rwkv_theseus_b200.ops import native  # noqa: E402
 
-SHAPES = [  # (name, M, N, K, a_t, b_t)
+SHAPES = [  # (name, M, N, K, a_t, b_t[, G])
     ("mlp_gate_up", 1024, 17408, 5120, False, False),
     ("mlp_down", 1024, 5120, 17408, False, False),
     ("gdn_in_qkv", 1024, 10240, 5120, False, False),
@@ -24,6 +26,9 @@ SHAPES = [  # (name, M, N, K, a_t, b_t)
     ("student_fwd", 1024, 5120, 5120, False, False),
     ("student_dx", 1024, 5120, 5120, False, True),
     ("student_dw", 5120, 5120, 1024, True, True),
+    ("student_rkv_fwd", 1024, 5120, 5120, False, False, 3),
+    ("student_rkv_dx", 1024, 5120, 5120, False, True, 3),
+    ("student_rkv_dw", 5120, 5120, 1024, True, True, 3),
     ("lora_down", 1024, 192, 5120, False, False),
     ("gdn_ab", 1024, 96, 5120, False, False),
     ("big_square", 8192, 8192, 8192, False, False),
@@ -63,30 +68,39 @@ def main():
         else:
             tile = int(args.tile.rstrip("sk")) | ((1 << 16) if args.tile.endswith("sk") else 0)
     results = []
-    for name, M, N, K, a_t, b_t in SHAPES:
+    for name, M, N, K, a_t, b_t, *rest in SHAPES:
         if args.only and args.only not in name:
             continue
-        bytes_per_set = (M * K + N * K) * 2
+        G = rest[0] if rest else 1
+        bytes_per_set = G * (M * K + N * K) * 2
         sets = max(1, min(8, (256 << 20) // bytes_per_set + 1))
-        As = [torch.randn((K, M) if a_t else (M, K), device="cuda").to(torch.bfloat16) for _ in range(sets)]
-        Bs = [torch.randn((K, N) if b_t else (N, K), device="cuda").to(torch.bfloat16) for _ in range(sets)]
-        out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        As = [torch.randn((G, K, M) if a_t else (G, M, K), device="cuda").to(torch.bfloat16) for _ in range(sets)]
+        Bs = [torch.randn((G, K, N) if b_t else (G, N, K), device="cuda").to(torch.bfloat16) for _ in range(sets)]
+        out = torch.empty(G, M, N, device="cuda", dtype=torch.bfloat16)
+        outs = list(out.unbind(0))
 
         def ours(i):
-            native().gemm(As[i % sets], a_t, Bs[i % sets], b_t, 0, 1.0, out, tile)
+            if G == 1:
+                native().gemm(As[i % sets][0], a_t, Bs[i % sets][0], b_t, 0, 1.0, out[0], tile)
+            else:
+                native().gemm_group(list(As[i % sets].unbind(0)), a_t, list(Bs[i % sets].unbind(0)), b_t, 0, 1.0,
+                                    outs, tile)
 
         def cublas(i):
-            a = As[i % sets].t() if a_t else As[i % sets]
-            b = Bs[i % sets] if b_t else Bs[i % sets].t()
-            torch.matmul(a, b, out=out)
+            a = As[i % sets].transpose(1, 2) if a_t else As[i % sets]
+            b = Bs[i % sets] if b_t else Bs[i % sets].transpose(1, 2)
+            if G == 1:
+                torch.matmul(a[0], b[0], out=out[0])
+            else:
+                torch.bmm(a, b, out=out)
 
-        flops = 2.0 * M * N * K
+        flops = 2.0 * M * N * K * G
         t_ours = timed(ours, args.warmup, args.iters)
         t_cub = float("nan") if args.no_cublas else timed(cublas, args.warmup, args.iters)
-        ref = torch.matmul(As[0].t() if a_t else As[0], Bs[0] if b_t else Bs[0].t()).float()
-        native().gemm(As[0], a_t, Bs[0], b_t, 0, 1.0, out, tile)
+        ref = torch.matmul(As[0].transpose(1, 2) if a_t else As[0], Bs[0] if b_t else Bs[0].transpose(1, 2)).float()
+        ours(0)
         rel = ((out.float() - ref).abs().max() / ref.abs().max()).item()
-        row = {"shape": name, "M": M, "N": N, "K": K, "ours_ms": t_ours, "cublas_ms": t_cub,
+        row = {"shape": name, "M": M, "N": N, "K": K, "G": G, "ours_ms": t_ours, "cublas_ms": t_cub,
                "ours_tflops": flops / t_ours / 1e9, "cublas_tflops": flops / t_cub / 1e9,
                "ratio": t_cub / t_ours, "max_rel_err": rel}
         results.append(row)

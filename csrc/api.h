@@ -41,6 +41,11 @@ cudaError_t rt_wkv7_backward(int dtype, int B, int T, int H, int N, const void* 
 // epi: 0 bf16 store, 1 fp32 store, 2 fp32 accumulate (C += alpha * A.B^T).
 cudaError_t rt_gemm_bf16(const void* A, long lda, int a_mn, const void* B, long ldb, int b_mn, void* C, long ldc,
                          int M, int N, int K, int epi, float alpha, int* status, cudaStream_t stream);
+// G (1..3) GEMMs of one shape, layout and epilogue in one launch: C[g] = epi(A[g] . B[g]^T); choice < 0 picks the
+// measured tile schedule of the shape, else a fixed one (width | 1 << 16 for stream-K).
+cudaError_t rt_gemm_bf16_group(int G, const void* const* A, long lda, int a_mn, const void* const* B, long ldb,
+                               int b_mn, void* const* C, long ldc, int M, int N, int K, int epi, float alpha,
+                               int choice, int* status, cudaStream_t stream);
 int rt_gemm_fault();
 cudaError_t rt_gemm_fault_async(int* dst, cudaStream_t stream);
 int rt_kl_segments(long rows, long V);

@@ -194,6 +194,43 @@ at::Tensor gemm(at::Tensor A, bool a_t, at::Tensor B, bool b_t, int64_t epi, dou
   return C;
 }
 
+// outs[g] = a_op(A[g]) . b_op(B[g])^T for up to 3 problems of one shape, layout and epilogue, in one launch (see
+// `gemm`). `outs` empty: new outputs (epi 0 bf16, epi 1 fp32); epi 2 accumulates into the given fp32 `outs`.
+std::vector<at::Tensor> gemm_group(std::vector<at::Tensor> As, bool a_t, std::vector<at::Tensor> Bs, bool b_t,
+                                   int64_t epi, double alpha, std::vector<at::Tensor> outs, int64_t tile) {
+  const size_t G = As.size();
+  TORCH_CHECK(G >= 1 && G <= 3 && Bs.size() == G && (outs.empty() || outs.size() == G),
+              "gemm_group: 1 to 3 problems, one B (and out) per A");
+  c10::cuda::CUDAGuard guard(As[0].device());
+  const void* ap[3];
+  const void* bp[3];
+  void* cp[3];
+  const Operand a0 = operand(As[0], "A"), b0 = operand(Bs[0], "B");
+  const long M = a_t ? As[0].size(1) : As[0].size(0), K = a_t ? As[0].size(0) : As[0].size(1);
+  const long N = b_t ? Bs[0].size(1) : Bs[0].size(0), KB = b_t ? Bs[0].size(0) : Bs[0].size(1);
+  TORCH_CHECK(K == KB, "GEMM inner dimensions differ: ", K, " vs ", KB);
+  TORCH_CHECK(epi != 2 || !outs.empty(), "accumulate epilogue needs `outs`");
+  const auto ctype = epi == 0 ? at::kBFloat16 : at::kFloat;
+  for (size_t g = 0; g < G; ++g) {
+    const Operand a = operand(As[g], "A"), b = operand(Bs[g], "B");
+    TORCH_CHECK(As[g].sizes() == As[0].sizes() && Bs[g].sizes() == Bs[0].sizes() && a.ld == a0.ld && b.ld == b0.ld,
+                "gemm_group: every problem needs the same shapes and strides");
+    if (outs.size() < G) outs.push_back(at::empty({M, N}, As[0].options().dtype(ctype)));
+    const at::Tensor& C = outs[g];
+    TORCH_CHECK(C.is_cuda() && C.scalar_type() == ctype && C.dim() == 2 && C.size(0) == M && C.size(1) == N &&
+                    C.stride(1) == 1 && C.stride(0) == outs[0].stride(0),
+                "gemm_group: outputs must be [M, N] with unit inner stride and one row stride, ",
+                epi == 0 ? "bf16" : "fp32");
+    ap[g] = a.ptr;
+    bp[g] = b.ptr;
+    cp[g] = C.data_ptr();
+  }
+  check_cuda(rt_gemm_bf16_group((int)G, ap, a0.ld, a_t, bp, b0.ld, b_t, cp, outs[0].stride(0), M, N, K, (int)epi,
+                                (float)alpha, tile ? (int)tile : -1, nullptr, stream_of(As[0])),
+             "gemm_group");
+  return outs;
+}
+
 at::Tensor gemm_swiglu(at::Tensor A, at::Tensor Bg, at::Tensor Bu) {
   c10::cuda::CUDAGuard guard(A.device());
   auto a = operand(A, "A");
@@ -617,12 +654,19 @@ class StudentStep {
     bonus.clear();
     auto dmix = at::empty_like(s.mix);
     auto xm = [&](int i) { return s.mix.select(0, i); };  // xr, xw, xk, xv, xa, xg
-    // r, k, v projections
-    const std::pair<int, const char*> proj[3] = {{0, "receptance"}, {2, "key"}, {3, "value"}};
-    const at::Tensor* douts[3] = {&d5[0], &d5[1], &d5[2]};
-    for (int i = 0; i < 3; ++i) {
-      gemm(*douts[i], false, W_.at(proj[i].second), true, 0, 1.0, dmix.select(0, proj[i].first), 0);
-      grad(*douts[i], true, xm(proj[i].first), true, proj[i].second, first);
+    // r, k, v projections: input gradients as one grouped launch, weight gradients as another
+    if (grouped()) {
+      const std::vector<at::Tensor> drkv = {d5[0], d5[1], d5[2]};
+      gemm_group(drkv, false, {W_.at("receptance"), W_.at("key"), W_.at("value")}, true, 0, 1.0,
+                 {dmix.select(0, 0), dmix.select(0, 2), dmix.select(0, 3)}, 0);
+      gemm_group(drkv, true, {xm(0), xm(2), xm(3)}, true, first ? 1 : 2, 1.0,
+                 {G_.at("receptance"), G_.at("key"), G_.at("value")}, 0);
+    } else {
+      const std::pair<int, const char*> proj[3] = {{0, "receptance"}, {2, "key"}, {3, "value"}};
+      for (int i = 0; i < 3; ++i) {
+        gemm(d5[i], false, W_.at(proj[i].second), true, 0, 1.0, dmix.select(0, proj[i].first), 0);
+        grad(d5[i], true, xm(proj[i].first), true, proj[i].second, first);
+      }
     }
     // decay LoRA: lw = tanh(xw w1) w2
     acc(s.hw, d5[3], "w2");
@@ -662,6 +706,15 @@ class StudentStep {
     return out;
   }
 
+  // The r/k/v projections as grouped launches (THESEUS_GROUPED_GEMM=0: three launches each, for comparison).
+  static bool grouped() {
+    static const bool on = [] {
+      const char* e = getenv("THESEUS_GROUPED_GEMM");
+      return !(e && e[0] == '0');
+    }();
+    return on;
+  }
+
   static at::Tensor mm(const at::Tensor& a, const at::Tensor& b, bool b_t) {
     return gemm(a, false, b, b_t, 0, 1.0, c10::nullopt, 0);
   }
@@ -690,9 +743,17 @@ class StudentStep {
     s.mix = at::empty({6, M, C}, s.x.options());
     tm_mix(s.x, s.shift, P_.at("coef"), s.mix);
     auto xm = [&](int i) { return s.mix.select(0, i); };
-    s.r = mm(xm(0), W_.at("receptance"), false);
-    s.k = mm(xm(2), W_.at("key"), false);
-    s.v = mm(xm(3), W_.at("value"), false);
+    if (M > 32 && grouped()) {  // r, k, v as one grouped launch (three 5120-wide GEMMs alone leave most of a wave idle)
+      auto rkv = gemm_group({xm(0), xm(2), xm(3)}, false, {W_.at("receptance"), W_.at("key"), W_.at("value")},
+                            false, 0, 1.0, {}, 0);
+      s.r = rkv[0];
+      s.k = rkv[1];
+      s.v = rkv[2];
+    } else {  // decode-sized: split-K weight streaming per projection
+      s.r = mm(xm(0), W_.at("receptance"), false);
+      s.k = mm(xm(2), W_.at("key"), false);
+      s.v = mm(xm(3), W_.at("value"), false);
+    }
     s.hw = mm(xm(1), W_.at("w1"), true);
     act_(s.hw, 0);
     s.lw = mm(s.hw, W_.at("w2"), true);
@@ -734,6 +795,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm, "tcgen05 GEMM: a_op(A) . b_op(B)^T with bf16/fp32/accumulate epilogue",
         py::arg("A"), py::arg("a_t"), py::arg("B"), py::arg("b_t"), py::arg("epi") = 0, py::arg("alpha") = 1.0,
         py::arg("out") = py::none(), py::arg("tile") = 0);
+  m.def("gemm_group", &gemm_group, "up to 3 tcgen05 GEMMs of one shape in one launch (shared stream-K schedule)",
+        py::arg("A"), py::arg("a_t"), py::arg("B"), py::arg("b_t"), py::arg("epi") = 0, py::arg("alpha") = 1.0,
+        py::arg("outs") = std::vector<at::Tensor>(), py::arg("tile") = 0);
   m.def("gemm_fault", []() { return rt_gemm_fault(); },
         "1 if a GEMM gave up a bounded wait since the last call (then cleared); synchronizes the device");
   m.def("kl_rows", &kl_rows, "per-row KL(teacher || student) over the vocabulary in one pass", py::arg("student"),

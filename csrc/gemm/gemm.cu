@@ -37,6 +37,8 @@
 #include <map>
 #include <vector>
 #include <mutex>
+#include <atomic>
+#include <cstring>
 #include <tuple>
 #include "../common/common.cuh"
 #include "../common/sm100.cuh"
@@ -67,10 +69,20 @@ struct Cfg {
                 "TMEM columns must be a power of 2 (>= 32)");
 };
 
+// Operand tensor maps. A group of G <= MAX_GROUPS problems of one shape and layout (e.g. the r, k and v projections
+// of a TimeMix layer) runs as one launch: problem g reads a[g] and b[g] and writes C[g]. The SwiGLU epilogue (G = 1)
+// reads its two B operands from b[0] (gate) and b[1] (up).
+constexpr int MAX_GROUPS = 3;
+struct GemmMaps {
+  CUtensorMap a[MAX_GROUPS];
+  CUtensorMap b[MAX_GROUPS];
+};
+
 struct GemmArgs {
   int M, N, K;
-  void* C;
+  void* C[MAX_GROUPS];
   long ldc;
+  int groups;  // problems in the launch; tiles are numbered M-fastest, then N, then problem, then split
   int tiles_m, tiles_n;
   int splits, kchunk;  // split-K: tile t covers k-blocks [ks * kchunk, (ks + 1) * kchunk), ks = t / (tiles_m * tiles_n)
   float alpha;
@@ -96,7 +108,7 @@ struct WorkIter {
   int lo, cur;  // stream-K range still to walk: [lo, cur)
   __device__ WorkIter(const GemmArgs& a, int kblocks_) {
     kblocks = kblocks_;
-    per_split = a.tiles_m * a.tiles_n;
+    per_split = a.tiles_m * a.tiles_n * a.groups;
     total = per_split * a.splits;
     next_tile = blockIdx.x;
     stride = gridDim.x;
@@ -221,7 +233,7 @@ __device__ __forceinline__ void loss_row(const float (&v)[32], const GemmArgs& a
   const float tt = a.rowsum[4 * (long)row];
   const float k = 2.f / (a.N * fmaxf(tt / a.N, a.eps));
   const __nv_bfloat16* trow = a.target + (long)row * a.N + col;
-  __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.C) + (long)row * a.ldc + col;
+  __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.C[0]) + (long)row * a.ldc + col;
   if (col + 32 <= a.N && ((reinterpret_cast<uintptr_t>(trow) | reinterpret_cast<uintptr_t>(out)) & 15) == 0) {
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
@@ -251,13 +263,21 @@ __device__ __forceinline__ void loss_row(const float (&v)[32], const GemmArgs& a
   }
 }
 
+// Problem, row tile and column tile of a tile index (split index excluded).
+__device__ __forceinline__ void tile_coords(const GemmArgs& a, int tile, int& g, int& tm, int& tn) {
+  const int per_problem = a.tiles_m * a.tiles_n;
+  const int t = tile % (per_problem * a.groups);
+  g = t / per_problem;
+  tm = t % a.tiles_m;
+  tn = (t % per_problem) / a.tiles_m;
+}
+
 // Set by a launch without a status word whose bounded wait gave up (read and cleared by rt_gemm_fault).
 __device__ int gemm_fault_word = 0;
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(THREADS, 1)
-gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb0,
-            const __grid_constant__ CUtensorMap tb1, const GemmArgs args) {
+gemm_kernel(const __grid_constant__ GemmMaps maps, const GemmArgs args) {
   using C_ = Cfg<BN, A_MN, B_MN, EPI>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = sm100::align_smem_1024(smem_raw);
@@ -272,7 +292,6 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int per_split = args.tiles_m * args.tiles_n;
   const int kblocks = (args.K + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
@@ -289,9 +308,11 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
     sm100::fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
-    sm100::prefetch_tmap(&ta);
-    sm100::prefetch_tmap(&tb0);
-    if (C_::NB == 2) sm100::prefetch_tmap(&tb1);
+    for (int g = 0; g < args.groups; ++g) {
+      sm100::prefetch_tmap(&maps.a[g]);
+      sm100::prefetch_tmap(&maps.b[g]);
+    }
+    if (C_::NB == 2) sm100::prefetch_tmap(&maps.b[1]);
   }
   if (warp == 1) {
     sm100::tmem_alloc(tmem_slot, C_::TMEM_COLS);
@@ -311,21 +332,23 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
       WorkIter work(args, kblocks);
       int tile, k0, k1;
       while (!*abort && work.next(tile, k0, k1)) {
-        const int tm = tile % args.tiles_m, tn = (tile % per_split) / args.tiles_m;
+        int g, tm, tn;
+        tile_coords(args, tile, g, tm, tn);
+        const CUtensorMap* ta = &maps.a[g];
         for (int kb = k0; kb < k1; ++kb) {
           if (!sm100::mbar_wait(&empty[stage], phase ^ 1, abort)) break;
           uint8_t* a_dst = smem + stage * C_::STAGE_BYTES;
           sm100::mbar_expect_tx(&full[stage], C_::STAGE_BYTES);
           if (!A_MN) {
-            sm100::tma_load_2d(a_dst, &ta, &full[stage], kb * BK, tm * BM);
+            sm100::tma_load_2d(a_dst, ta, &full[stage], kb * BK, tm * BM);
           } else {
-            sm100::tma_load_2d(a_dst, &ta, &full[stage], tm * BM, kb * BK);
-            sm100::tma_load_2d(a_dst + MN_CHUNK_BYTES, &ta, &full[stage], tm * BM + 64, kb * BK);
+            sm100::tma_load_2d(a_dst, ta, &full[stage], tm * BM, kb * BK);
+            sm100::tma_load_2d(a_dst + MN_CHUNK_BYTES, ta, &full[stage], tm * BM + 64, kb * BK);
           }
 #pragma unroll
           for (int j = 0; j < C_::NB; ++j) {
             uint8_t* b_dst = a_dst + C_::A_BYTES + j * C_::B_BYTES;
-            const CUtensorMap* tb = j == 0 ? &tb0 : &tb1;
+            const CUtensorMap* tb = &maps.b[C_::NB == 2 ? j : g];
             if (!B_MN) {
               sm100::tma_load_2d(b_dst, tb, &full[stage], kb * BK, tn * BN);
             } else {
@@ -392,7 +415,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
     WorkIter work(args, kblocks);
     int tile, k0, k1;
     while (!*abort && work.next(tile, k0, k1)) {
-      const int tm = tile % args.tiles_m, tn = (tile % per_split) / args.tiles_m;
+      int g, tm, tn;
+      tile_coords(args, tile, g, tm, tn);
+      void* const Cg = args.C[g];
       if (!sm100::mbar_wait(&tfull[acc], acc_phase, abort)) break;
       sm100::tc_fence_after();
       const int row = tm * BM + row_in_tile;
@@ -445,7 +470,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
           if (grow >= args.M || gcol >= args.N) continue;
           const float vals[4] = {acc4.x, acc4.y, acc4.z, acc4.w};
           if (EPI == EPI_BF16) {
-            __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(args.C) + (long)grow * args.ldc + gcol;
+            __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(Cg) + (long)grow * args.ldc + gcol;
             if (gcol + 4 <= args.N && (reinterpret_cast<uintptr_t>(o) & 7) == 0) {
               __nv_bfloat162 a2 = __floats2bfloat162_rn(vals[0], vals[1]), b2 = __floats2bfloat162_rn(vals[2], vals[3]);
               uint2 pk;
@@ -456,7 +481,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
               for (int u = 0; u < 4 && gcol + u < args.N; ++u) o[u] = __float2bfloat16_rn(vals[u]);
             }
           } else {
-            float* o = reinterpret_cast<float*>(args.C) + (long)grow * args.ldc + gcol;
+            float* o = reinterpret_cast<float*>(Cg) + (long)grow * args.ldc + gcol;
             for (int u = 0; u < 4 && gcol + u < args.N; ++u) {
               if (EPI == EPI_F32) o[u] = vals[u];
               else o[u] += args.alpha * vals[u];
@@ -526,7 +551,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
           if (EPI == EPI_NMSE)
             loss_row(v, args, row, tn * BN + c * 32, se, pp, pt);
           else
-            store_row(v, EPI, args.C, args.ldc, row, tn * BN + c * 32, args.N, args.alpha);
+            store_row(v, EPI, Cg, args.ldc, row, tn * BN + c * 32, args.N, args.alpha);
         }
       }
       if (EPI == EPI_NMSE && !partial && row < args.M) {
@@ -635,33 +660,74 @@ struct LossArgs {
   float eps = 0.f;
 };
 
+// The problems of one launch: G of the same shape and layouts (A[g] . B[g]^T -> C[g]); B1 is the SwiGLU up operand.
+struct Prob {
+  int G = 1;
+  const void* A[MAX_GROUPS] = {};
+  const void* B[MAX_GROUPS] = {};
+  const void* B1 = nullptr;
+  void* C[MAX_GROUPS] = {};
+  long lda = 0, ldb = 0, ldc = 0;
+  int M = 0, N = 0, K = 0;
+};
+
+Prob single(const void* A, long lda, const void* B, long ldb, void* C, long ldc, int M, int N, int K) {
+  Prob p;
+  p.A[0] = A;
+  p.B[0] = B;
+  p.C[0] = C;
+  p.lda = lda; p.ldb = ldb; p.ldc = ldc;
+  p.M = M; p.N = N; p.K = K;
+  return p;
+}
+
+// cudaFuncSetAttribute once per device for the kernel instantiation that owns `done` (it is a per-device attribute;
+// the host cost of repeating it on every launch showed on the eagerly issued short-chunk student steps).
+template <typename Kern>
+cudaError_t set_smem_once(std::atomic<uint64_t>& done, Kern kern, int bytes) {
+  int dev = 0;
+  RT_CUDA_CHECK(cudaGetDevice(&dev));
+  const uint64_t bit = dev < 64 ? 1ull << dev : 0;
+  if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+  RT_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  done.fetch_or(bit, std::memory_order_acq_rel);
+  return cudaSuccess;
+}
+
 template <int BN, bool A_MN, bool B_MN, int EPI>
-cudaError_t launch(const void* A, long lda, const void* B0, const void* B1, long ldb, void* C, long ldc, int M,
-                   int N, int K, float alpha, int* status, cudaStream_t stream, int splits = 1, bool sk = false,
+cudaError_t launch(const Prob& p, float alpha, int* status, cudaStream_t stream, int splits = 1, bool sk = false,
                    LossArgs loss = LossArgs(), int splitp = 0) {
   using C_ = Cfg<BN, A_MN, B_MN, EPI>;
-  CUtensorMap ta, tb0, tb1;
-  bool ok = A_MN ? make_tmap(&ta, A, M, K, lda * 2, 64, BK) : make_tmap(&ta, A, K, M, lda * 2, BK, BM);
-  ok = ok && (B_MN ? make_tmap(&tb0, B0, N, K, ldb * 2, 64, BK) : make_tmap(&tb0, B0, K, N, ldb * 2, BK, BN));
+  if (p.G < 1 || p.G > MAX_GROUPS || (C_::NB == 2 && p.G != 1)) return cudaErrorInvalidValue;
+  const int M = p.M, N = p.N, K = p.K;
+  GemmMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  bool ok = true;
+  for (int g = 0; g < p.G && ok; ++g) {
+    ok = A_MN ? make_tmap(&maps.a[g], p.A[g], M, K, p.lda * 2, 64, BK) : make_tmap(&maps.a[g], p.A[g], K, M, p.lda * 2, BK, BM);
+    ok = ok && (B_MN ? make_tmap(&maps.b[g], p.B[g], N, K, p.ldb * 2, 64, BK)
+                     : make_tmap(&maps.b[g], p.B[g], K, N, p.ldb * 2, BK, BN));
+  }
   if (C_::NB == 2)
-    ok = ok && (B_MN ? make_tmap(&tb1, B1, N, K, ldb * 2, 64, BK) : make_tmap(&tb1, B1, K, N, ldb * 2, BK, BN));
-  else
-    tb1 = tb0;
+    ok = ok && (B_MN ? make_tmap(&maps.b[1], p.B1, N, K, p.ldb * 2, 64, BK)
+                     : make_tmap(&maps.b[1], p.B1, K, N, p.ldb * 2, BK, BN));
   if (!ok) return cudaErrorInvalidValue;
   GemmArgs args;
-  args.M = M; args.N = N; args.K = K; args.C = C; args.ldc = ldc; args.alpha = alpha; args.status = status;
+  args.M = M; args.N = N; args.K = K; args.ldc = p.ldc; args.alpha = alpha; args.status = status;
+  args.groups = p.G;
+  for (int g = 0; g < MAX_GROUPS; ++g) args.C[g] = g < p.G ? p.C[g] : p.C[0];
   args.tiles_m = (M + BM - 1) / BM;
   args.tiles_n = (N + BN - 1) / BN;
   args.splits = splits;
   args.kchunk = ((K + BK - 1) / BK + splits - 1) / splits;
-  const int total = args.tiles_m * args.tiles_n * splits;
+  const int tiles = args.tiles_m * args.tiles_n * p.G;
+  const int total = tiles * splits;
   args.sk = 0; args.q = 0; args.rem = 0; args.ws = nullptr; args.flags = nullptr; args.splitp = 0;
   args.target = static_cast<const __nv_bfloat16*>(loss.target);
   args.rowsum = loss.rowsum;
   args.eps = loss.eps;
   int grid = total < num_sms_cached() ? total : num_sms_cached();
   if (splitp > 1 && C_::NB == 1 && splits == 1 && EPI != EPI_ATOMIC_T && EPI != EPI_NMSE) {
-    const int tiles = args.tiles_m * args.tiles_n;
     const int kb = (K + BK - 1) / BK;
     int S = splitp;
     while (S > 1 && (tiles * S > num_sms_cached() || kb < 2 * S)) --S;  // co-resident CTAs, >= 2 k-blocks each
@@ -673,8 +739,8 @@ cudaError_t launch(const void* A, long lda, const void* B0, const void* B1, long
       args.flags = w->flags;
     }
   } else if (sk && C_::NB == 1 && splits == 1 && EPI != EPI_ATOMIC_T) {
-    const long iters = (long)args.tiles_m * args.tiles_n * ((K + BK - 1) / BK);
-    SkWorkspace* w = 4L * args.tiles_m * args.tiles_n <= SK_MAX_FLAGS && iters >= num_sms_cached() && iters < (1L << 30)
+    const long iters = (long)tiles * ((K + BK - 1) / BK);
+    SkWorkspace* w = 4L * tiles <= SK_MAX_FLAGS && iters >= num_sms_cached() && iters < (1L << 30)
                          ? sk_workspace(stream) : nullptr;
     if (w) {
       grid = num_sms_cached();
@@ -686,15 +752,16 @@ cudaError_t launch(const void* A, long lda, const void* B0, const void* B1, long
     }
   }
   auto kern = gemm_kernel<BN, A_MN, B_MN, EPI>;
-  RT_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C_::SMEM_BYTES));
-  kern<<<grid, THREADS, C_::SMEM_BYTES, stream>>>(ta, tb0, tb1, args);
+  static std::atomic<uint64_t> smem_set{0};  // one per instantiation of this launcher, i.e. per kernel
+  RT_CUDA_CHECK(set_smem_once(smem_set, kern, C_::SMEM_BYTES));
+  kern<<<grid, THREADS, C_::SMEM_BYTES, stream>>>(maps, args);
   return cudaGetLastError();
 }
 
 // Tile width: the one whose tile count fills the persistent grid best (fraction of the last wave that is
 // busy), preferring wider tiles (less L2 traffic per FLOP) when two are within 3%. Widths that are not a
 // multiple of 64 need a K-major B operand.
-int pick_bn(int M, int N, bool swiglu, bool b_mn) {
+int pick_bn(int M, int N, int G, bool swiglu, bool b_mn) {
   if (swiglu) return 128;
   const int sms = num_sms_cached();
   const long tm = (M + BM - 1) / BM;
@@ -703,7 +770,7 @@ int pick_bn(int M, int N, bool swiglu, bool b_mn) {
   for (int bn : {256, 224, 192, 160, 128, 64}) {
     if (b_mn && bn % 64) continue;
     if (N < bn / 2 && bn != 64) continue;
-    const long tiles = tm * ((N + bn - 1) / bn);
+    const long tiles = tm * ((N + bn - 1) / bn) * G;
     const long waves = (tiles + sms - 1) / sms;
     // useful fraction: filled slots, and the padding of the last (partial) column tile
     const double fill = (double)tiles / (double)(waves * sms);
@@ -722,13 +789,11 @@ constexpr int SK_FLAG = 1 << 16;
 constexpr int SP_SHIFT = 20;  // choice bits 20..27: parallel split-K factor S (0 = off)
 
 template <bool A_MN, bool B_MN, int EPI>
-cudaError_t dispatch_bn(int choice, const void* A, long lda, const void* B0, const void* B1, long ldb, void* C,
-                        long ldc, int M, int N, int K, float alpha, int* status, cudaStream_t s) {
+cudaError_t dispatch_bn(int choice, const Prob& p, float alpha, int* status, cudaStream_t s) {
   const int bn = choice & (SK_FLAG - 1);
   const bool sk = (choice & SK_FLAG) != 0;
   const int sp = (choice >> SP_SHIFT) & 255;
-#define RT_L(W) \
-  return launch<W, A_MN, B_MN, EPI>(A, lda, B0, B1, ldb, C, ldc, M, N, K, alpha, status, s, 1, sk, LossArgs(), sp)
+#define RT_L(W) return launch<W, A_MN, B_MN, EPI>(p, alpha, status, s, 1, sk, LossArgs(), sp)
   if (bn == 256) RT_L(256);
   if (bn == 192) RT_L(192);
   if (bn == 128) RT_L(128);
@@ -740,17 +805,17 @@ cudaError_t dispatch_bn(int choice, const void* A, long lda, const void* B0, con
 #undef RT_L
 }
 
-cudaError_t gemm_with_bn(int choice, const void* A, long lda, int a_mn, const void* B, long ldb, int b_mn, void* C,
-                         long ldc, int M, int N, int K, int epi, float alpha, int* status, cudaStream_t stream);
+cudaError_t gemm_with_bn(int choice, const Prob& p, int a_mn, int b_mn, int epi, float alpha, int* status,
+                         cudaStream_t stream);
 
 // Tile width per problem shape, measured once: the first call of a shape with a store epilogue (outside stream
 // capture) runs every candidate width on the real operands and keeps the fastest (every width computes each
 // output with the same MMA sequence over K, so the result does not depend on the choice). Accumulating calls
 // and calls under capture use the measured width of the shape when known, else the wave-fill estimate.
 struct TileKey {
-  int M, N, K, a_mn, b_mn;
+  int M, N, K, a_mn, b_mn, G;
   bool operator<(const TileKey& o) const {
-    return std::tie(M, N, K, a_mn, b_mn) < std::tie(o.M, o.N, o.K, o.a_mn, o.b_mn);
+    return std::tie(M, N, K, a_mn, b_mn, G) < std::tie(o.M, o.N, o.K, o.a_mn, o.b_mn, o.G);
   }
 };
 std::map<TileKey, int>& tile_cache() {
@@ -762,8 +827,7 @@ std::mutex& tile_mutex() {
   return m;
 }
 
-int measured_bn(const TileKey& key, int M, int K, const void* A, long lda, const void* B, long ldb, void* C, long ldc,
-                int epi, float alpha, int* status, cudaStream_t stream) {
+int measured_bn(const TileKey& key, const Prob& p, int epi, float alpha, int* status, cudaStream_t stream) {
   {
     std::lock_guard<std::mutex> lock(tile_mutex());
     auto it = tile_cache().find(key);
@@ -776,7 +840,7 @@ int measured_bn(const TileKey& key, int M, int K, const void* A, long lda, const
     long best_size = 0;
     bool larger_known = false;
     for (const auto& [k, choice] : tile_cache()) {
-      if (k.N != key.N || k.a_mn != key.a_mn || k.b_mn != key.b_mn) continue;
+      if (k.N != key.N || k.a_mn != key.a_mn || k.b_mn != key.b_mn || k.G != key.G) continue;
       const bool rows_any = !key.a_mn && k.K == key.K && k.M > key.M;
       const bool depth_any = key.a_mn && k.M == key.M && k.K > key.K;
       larger_known = larger_known || rows_any || depth_any;
@@ -788,13 +852,13 @@ int measured_bn(const TileKey& key, int M, int K, const void* A, long lda, const
         best_size = size;
       }
     }
-    if (best < 0 && larger_known) best = pick_bn(key.M, key.N, false, key.b_mn != 0);
+    if (best < 0 && larger_known) best = pick_bn(key.M, key.N, key.G, false, key.b_mn != 0);
     if (best >= 0) {
       tile_cache()[key] = best;
       return best;
     }
   }
-  const int guess = pick_bn(key.M, key.N, false, key.b_mn != 0);
+  const int guess = pick_bn(key.M, key.N, key.G, false, key.b_mn != 0);
   cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
   if (epi == EPI_F32_ACCUM || epi == EPI_NMSE || cudaStreamIsCapturing(stream, &cap) != cudaSuccess ||
       cap != cudaStreamCaptureStatusNone)
@@ -812,7 +876,7 @@ int measured_bn(const TileKey& key, int M, int K, const void* A, long lda, const
   {  // parallel split-K where the tiles fill under half of the SMs and K is deep
     const int sms = num_sms_cached();
     for (int bn : {64, 128, 192, 256}) {
-      const long tiles = (long)((key.M + BM - 1) / BM) * ((key.N + bn - 1) / bn);
+      const long tiles = (long)((key.M + BM - 1) / BM) * ((key.N + bn - 1) / bn) * key.G;
       if (tiles * 2 > sms || (key.N < bn / 2 && bn != 64) || (key.b_mn && bn % 64)) continue;
       const long smax = std::min<long>({sms / tiles, kblocks / 2, 255});
       for (long S : {smax, smax / 2})
@@ -824,20 +888,18 @@ int measured_bn(const TileKey& key, int M, int K, const void* A, long lda, const
     if (key.b_mn && bn % 64) continue;
     if (key.N < bn / 2 && bn != 64) continue;
     if (choice & SK_FLAG) {  // stream-K only where the whole-tile schedule leaves a wave partly idle
-      const long tiles = (long)((key.M + BM - 1) / BM) * ((key.N + bn - 1) / bn);
+      const long tiles = (long)((key.M + BM - 1) / BM) * ((key.N + bn - 1) / bn) * key.G;
       const int sms = num_sms_cached();
       if (tiles % sms == 0 || tiles * kblocks < 2L * sms || kblocks < 8) continue;
     }
     // one warm-up launch, then the best of two batches of four back-to-back launches (short kernels: the
     // batch amortises the event and launch jitter that dominates a single 10-20 us launch)
     float ms = 1e30f;
-    bool failed = gemm_with_bn(choice, A, lda, key.a_mn, B, ldb, key.b_mn, C, ldc, M, key.N, K, epi, alpha, status,
-                               stream) != cudaSuccess;
+    bool failed = gemm_with_bn(choice, p, key.a_mn, key.b_mn, epi, alpha, status, stream) != cudaSuccess;
     for (int rep = 0; rep < 2 && !failed; ++rep) {
       cudaEventRecord(e0, stream);
       for (int l = 0; l < 4 && !failed; ++l)
-        failed = gemm_with_bn(choice, A, lda, key.a_mn, B, ldb, key.b_mn, C, ldc, M, key.N, K, epi, alpha, status,
-                              stream) != cudaSuccess;
+        failed = gemm_with_bn(choice, p, key.a_mn, key.b_mn, epi, alpha, status, stream) != cudaSuccess;
       cudaEventRecord(e1, stream);
       if (failed || cudaEventSynchronize(e1) != cudaSuccess) break;
       float t = 0.f;
@@ -862,6 +924,31 @@ int measured_bn(const TileKey& key, int M, int K, const void* A, long lda, const
   return best;
 }
 
+bool bad_operands(const Prob& p) {
+  if ((p.lda & 7) || (p.ldb & 7)) return true;
+  for (int g = 0; g < p.G; ++g)
+    if (!p.A[g] || !p.B[g] || !p.C[g] || (reinterpret_cast<uintptr_t>(p.A[g]) & 15) ||
+        (reinterpret_cast<uintptr_t>(p.B[g]) & 15))
+      return true;
+  return false;
+}
+
+// Shapes share a measured tile choice per bucket: M by 128-row tiles and K by 512 (the token count of a partial
+// chunk varies from call to call; the choice affects speed only, never the result).
+cudaError_t gemm_measured(const Prob& p, int a_mn, int b_mn, int epi, float alpha, int* status, cudaStream_t stream) {
+  const TileKey key{(p.M + BM - 1) / BM * BM, p.N, (p.K + 511) / 512 * 512, a_mn != 0, b_mn != 0, p.G};
+  const int bn = measured_bn(key, p, epi, alpha, status, stream);
+  return gemm_with_bn(bn, p, a_mn, b_mn, epi, alpha, status, stream);
+}
+
+cudaError_t gemm_fixed(const Prob& p, int a_mn, int b_mn, int epi, float alpha, int choice, int* status,
+                       cudaStream_t stream) {
+  const int bn = choice & (SK_FLAG - 1);
+  if (bn != 64 && bn != 128 && bn != 160 && bn != 192 && bn != 224 && bn != 256) return cudaErrorInvalidValue;
+  if (b_mn && bn % 64) return cudaErrorInvalidValue;
+  return gemm_with_bn(choice, p, a_mn, b_mn, epi, alpha, status, stream);
+}
+
 }  // namespace
 
 // C[M,N] (ldc) = epi(A · B^T); A K-major [M,K] (lda) or MN-major [K,M] (lda); B K-major [N,K] (ldb) or
@@ -870,21 +957,37 @@ extern "C" cudaError_t rt_gemm_bf16(const void* A, long lda, int a_mn, const voi
                                     long ldc, int M, int N, int K, int epi, float alpha, int* status,
                                     cudaStream_t stream) {
   if (M <= 0 || N <= 0 || K <= 0) return cudaSuccess;
-  if ((lda & 7) || (ldb & 7) || (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15))
-    return cudaErrorInvalidValue;
-  // Shapes share a measured tile choice per bucket: M by 128-row tiles and K by 512 (the token count of a
-  // partial chunk varies from call to call; the choice affects speed only, never the result).
-  const TileKey key{(M + BM - 1) / BM * BM, N, (K + 511) / 512 * 512, a_mn != 0, b_mn != 0};
-  const int bn = measured_bn(key, M, K, A, lda, B, ldb, C, ldc, epi, alpha, status, stream);
-  return gemm_with_bn(bn, A, lda, a_mn, B, ldb, b_mn, C, ldc, M, N, K, epi, alpha, status, stream);
+  const Prob p = single(A, lda, B, ldb, C, ldc, M, N, K);
+  if (bad_operands(p)) return cudaErrorInvalidValue;
+  return gemm_measured(p, a_mn, b_mn, epi, alpha, status, stream);
+}
+
+// G (1..3) GEMMs of one shape and layout in one launch: C[g] = epi(A[g] · B[g]^T), with the layouts, strides and
+// epilogues of rt_gemm_bf16 (every problem uses the same lda / ldb / ldc). The tiles of all problems share one
+// persistent grid and one stream-K iteration space, so three 1024 x 5120 x 5120 projections fill the machine like
+// one 1024 x 15360 x 5120 GEMM. choice < 0: the measured tile choice of the shape; else a fixed one (tests).
+extern "C" cudaError_t rt_gemm_bf16_group(int G, const void* const* A, long lda, int a_mn, const void* const* B,
+                                          long ldb, int b_mn, void* const* C, long ldc, int M, int N, int K, int epi,
+                                          float alpha, int choice, int* status, cudaStream_t stream) {
+  if (G < 1 || G > MAX_GROUPS || !A || !B || !C) return cudaErrorInvalidValue;
+  if (M <= 0 || N <= 0 || K <= 0) return cudaSuccess;
+  Prob p = single(A[0], lda, B[0], ldb, C[0], ldc, M, N, K);
+  p.G = G;
+  for (int g = 1; g < G; ++g) {
+    p.A[g] = A[g];
+    p.B[g] = B[g];
+    p.C[g] = C[g];
+  }
+  if (bad_operands(p)) return cudaErrorInvalidValue;
+  return choice < 0 ? gemm_measured(p, a_mn, b_mn, epi, alpha, status, stream)
+                    : gemm_fixed(p, a_mn, b_mn, epi, alpha, choice, status, stream);
 }
 
 namespace {
-cudaError_t nmse_dispatch(int choice, const void* A, long lda, const void* B, long ldb, void* C, long ldc, int M, int N,
-                          int K, const LossArgs& loss, int* status, cudaStream_t s) {
+cudaError_t nmse_dispatch(int choice, const Prob& p, const LossArgs& loss, int* status, cudaStream_t s) {
   const int bn = choice & (SK_FLAG - 1);
   const bool sk = (choice & SK_FLAG) != 0;
-#define RT_L(W) return launch<W, false, false, EPI_NMSE>(A, lda, B, B, ldb, C, ldc, M, N, K, 1.f, status, s, 1, sk, loss)
+#define RT_L(W) return launch<W, false, false, EPI_NMSE>(p, 1.f, status, s, 1, sk, loss)
   if (bn == 256) RT_L(256);
   if (bn == 224) RT_L(224);
   if (bn == 192) RT_L(192);
@@ -903,16 +1006,16 @@ extern "C" cudaError_t rt_gemm_nmse_bf16(const void* A, long lda, const void* B,
                                          const void* target, float* rowsum, int M, int N, int K, float eps,
                                          int* status, cudaStream_t stream) {
   if (M <= 0 || N <= 0 || K <= 0) return cudaSuccess;
-  if ((lda & 7) || (ldb & 7) || (ldc & 7) || (reinterpret_cast<uintptr_t>(A) & 15) ||
-      (reinterpret_cast<uintptr_t>(B) & 15))
-    return cudaErrorInvalidValue;
-  const TileKey key{(M + BM - 1) / BM * BM, N, (K + 511) / 512 * 512, 0, 0};
-  const int choice = measured_bn(key, M, K, A, lda, B, ldb, dpred, ldc, EPI_NMSE, 1.f, status, stream);
+  if ((ldc & 7)) return cudaErrorInvalidValue;
+  const Prob p = single(A, lda, B, ldb, dpred, ldc, M, N, K);
+  if (bad_operands(p)) return cudaErrorInvalidValue;
+  const TileKey key{(M + BM - 1) / BM * BM, N, (K + 511) / 512 * 512, 0, 0, 1};
+  const int choice = measured_bn(key, p, EPI_NMSE, 1.f, status, stream);
   LossArgs loss;
   loss.target = target;
   loss.rowsum = rowsum;
   loss.eps = eps;
-  return nmse_dispatch(choice, A, lda, B, ldb, dpred, ldc, M, N, K, loss, status, stream);
+  return nmse_dispatch(choice, p, loss, status, stream);
 }
 
 // 1 if a GEMM launched without a status word gave up a wait since the last call (synchronizes the device).
@@ -950,26 +1053,23 @@ extern "C" cudaError_t rt_gemm_bf16_tile(const void* A, long lda, int a_mn, cons
                                          void* C, long ldc, int M, int N, int K, int epi, float alpha, int choice,
                                          int* status, cudaStream_t stream) {
   if (M <= 0 || N <= 0 || K <= 0) return cudaSuccess;
-  if ((lda & 7) || (ldb & 7) || (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15))
-    return cudaErrorInvalidValue;
-  const int bn = choice & (SK_FLAG - 1);
-  if (bn != 64 && bn != 128 && bn != 160 && bn != 192 && bn != 224 && bn != 256) return cudaErrorInvalidValue;
-  if (b_mn && bn % 64) return cudaErrorInvalidValue;
-  return gemm_with_bn(choice, A, lda, a_mn, B, ldb, b_mn, C, ldc, M, N, K, epi, alpha, status, stream);
+  const Prob p = single(A, lda, B, ldb, C, ldc, M, N, K);
+  if (bad_operands(p)) return cudaErrorInvalidValue;
+  return gemm_fixed(p, a_mn, b_mn, epi, alpha, choice, status, stream);
 }
 
 namespace {
 
-cudaError_t gemm_with_bn(int choice, const void* A, long lda, int a_mn, const void* B, long ldb, int b_mn, void* C,
-                         long ldc, int M, int N, int K, int epi, float alpha, int* status, cudaStream_t stream) {
-#define RT_G(AM, BMN)                                                                                                 \
-  switch (epi) {                                                                                                      \
-    case EPI_BF16:                                                                                                    \
-      return dispatch_bn<AM, BMN, EPI_BF16>(choice, A, lda, B, B, ldb, C, ldc, M, N, K, alpha, status, stream);       \
-    case EPI_F32:                                                                                                     \
-      return dispatch_bn<AM, BMN, EPI_F32>(choice, A, lda, B, B, ldb, C, ldc, M, N, K, alpha, status, stream);        \
-    default:                                                                                                          \
-      return dispatch_bn<AM, BMN, EPI_F32_ACCUM>(choice, A, lda, B, B, ldb, C, ldc, M, N, K, alpha, status, stream);  \
+cudaError_t gemm_with_bn(int choice, const Prob& p, int a_mn, int b_mn, int epi, float alpha, int* status,
+                         cudaStream_t stream) {
+#define RT_G(AM, BMN)                                                                       \
+  switch (epi) {                                                                            \
+    case EPI_BF16:                                                                          \
+      return dispatch_bn<AM, BMN, EPI_BF16>(choice, p, alpha, status, stream);              \
+    case EPI_F32:                                                                           \
+      return dispatch_bn<AM, BMN, EPI_F32>(choice, p, alpha, status, stream);               \
+    default:                                                                                \
+      return dispatch_bn<AM, BMN, EPI_F32_ACCUM>(choice, p, alpha, status, stream);         \
   }
   if (!a_mn && !b_mn) { RT_G(false, false) }
   if (!a_mn && b_mn) { RT_G(false, true) }
@@ -1020,8 +1120,9 @@ extern "C" cudaError_t rt_gemm_skinny_bf16(const void* X, long ldx, const void* 
   RT_CUDA_CHECK(cudaMemsetAsync(ws, 0, sizeof(float) * (size_t)parts * M * N, stream));
   const int splits = skinny_splits(N, K);
   for (int p = 0; p < parts; ++p)
-    RT_CUDA_CHECK((launch<32, false, false, EPI_ATOMIC_T>(p ? Wu : W, ldw, X, X, ldx, ws + (size_t)p * M * N, N, N,
-                                                          M, K, 1.f, status, stream, splits)));
+    RT_CUDA_CHECK((launch<32, false, false, EPI_ATOMIC_T>(single(p ? Wu : W, ldw, X, ldx, ws + (size_t)p * M * N, N,
+                                                                 N, M, K),
+                                                          1.f, status, stream, splits)));
   const long total = (long)M * N;
   const int grid = (int)((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
   skinny_finish_kernel<<<grid, 256, 0, stream>>>(ws, Wu ? ws + (size_t)M * N : nullptr,
@@ -1034,5 +1135,7 @@ extern "C" cudaError_t rt_gemm_swiglu_bf16(const void* A, long lda, const void* 
                                            long ldc, int M, int N, int K, int* status, cudaStream_t stream) {
   if (M <= 0 || N <= 0 || K <= 0) return cudaSuccess;
   if ((lda & 7) || (ldb & 7)) return cudaErrorInvalidValue;
-  return launch<128, false, false, EPI_SWIGLU>(A, lda, Bg, Bu, ldb, C, ldc, M, N, K, 1.f, status, stream);
+  Prob p = single(A, lda, Bg, ldb, C, ldc, M, N, K);
+  p.B1 = Bu;
+  return launch<128, false, false, EPI_SWIGLU>(p, 1.f, status, stream);
 }

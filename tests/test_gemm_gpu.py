@@ -156,3 +156,59 @@ def test_parallel_split_k_matches_fp32(M, N, K, tile):
     want = acc + 0.5 * (dy.float().t() @ x.float())
     native().gemm(dy, True, x, True, 2, 0.5, acc, 64 | 8 << SP)
     _check(acc, want, 1e-3)
+
+
+# Fixed schedules for the grouped launch: whole tiles of 256 / 128 / 64 columns, stream-K, parallel split-K (S = 4).
+# At 384 x 640 x 1216 every one of them runs as named for G = 2 and 3 (stream-K: at least one k-block per SM;
+# split-K: tiles x S within the SM count).
+_GROUP_SCHEDULES = [256, 128, 64, 256 | (1 << 16), 128 | (1 << 16), 256 | (4 << 20)]
+
+
+@cuda
+@pytest.mark.parametrize("G", [2, 3])
+@pytest.mark.parametrize("a_t,b_t", [(False, False), (False, True), (True, True)])
+@pytest.mark.parametrize("tile", [0] + _GROUP_SCHEDULES)
+def test_grouped_gemm_matches_fp32(G, a_t, b_t, tile):
+    """G problems of one shape in one launch (shared tile numbering and stream-K space) equal G fp32 matmuls."""
+    M, N, K = 384, 640, 1216
+    As = [_bf(K, M, seed=10 + g) if a_t else _bf(M, K, seed=10 + g) for g in range(G)]
+    Bs = [_bf(K, N, seed=20 + g) if b_t else _bf(N, K, seed=20 + g) for g in range(G)]
+    refs = [(A.float().t() if a_t else A.float()) @ (B.float() if b_t else B.float().t()) for A, B in zip(As, Bs)]
+    outs = native().gemm_group(As, a_t, Bs, b_t, 0, 1.0, [], tile)
+    for out, ref in zip(outs, refs):
+        _check(out, ref)
+    # fp32 store, then accumulate alpha * result into the given outputs (the weight-gradient epilogues)
+    f32 = native().gemm_group(As, a_t, Bs, b_t, 1, 1.0, [], tile)
+    for out, ref in zip(f32, refs):
+        _check(out, ref, 1e-3)
+    base = [torch.randn(M, N, device="cuda") for _ in range(G)]
+    acc = [b.clone() for b in base]
+    native().gemm_group(As, a_t, Bs, b_t, 2, 0.5, acc, tile)
+    for out, b, ref in zip(acc, base, refs):
+        _check(out, b + 0.5 * ref, 1e-3)
+
+
+@cuda
+def test_grouped_gemm_student_shape_and_strided_outputs():
+    """The r/k/v shape of the 27B student (1024 x 5120 x 5120, three problems) writing into slices of one buffer,
+    as the fused student writes its input gradients into the mix-gradient tensor."""
+    M, N, K = 1024, 5120, 5120
+    As = [_bf(M, K, seed=30 + g) for g in range(3)]
+    Bs = [_bf(N, K, seed=40 + g) for g in range(3)]
+    dst = torch.zeros(6, M, N, device="cuda", dtype=torch.bfloat16)
+    outs = [dst.select(0, i) for i in (0, 2, 3)]
+    native().gemm_group(As, False, Bs, False, 0, 1.0, outs, 0)
+    for i, (A, B) in zip((0, 2, 3), zip(As, Bs)):
+        _check(dst[i], A.float() @ B.float().t())
+    for i in (1, 4, 5):
+        assert dst[i].abs().max().item() == 0.0
+
+
+def test_grouped_gemm_rejects_mismatched_problems():
+    if not torch.cuda.is_available():
+        pytest.skip("CUDA unavailable")
+    A, B = _bf(128, 64, seed=1), _bf(64, 64, seed=2)
+    with pytest.raises(RuntimeError):
+        native().gemm_group([A, _bf(128, 128, seed=3)], False, [B, B], False, 0, 1.0, [], 0)
+    with pytest.raises(RuntimeError):
+        native().gemm_group([A] * 4, False, [B] * 4, False, 0, 1.0, [], 0)
