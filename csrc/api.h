@@ -61,7 +61,7 @@ cudaError_t rt_gemm_bf16_tile(const void* A, long lda, int a_mn, const void* B, 
 cudaError_t rt_gemm_skinny_bf16(const void* X, long ldx, const void* W, const void* Wu, long ldw, float* ws,
                                 void* out, long ldo, int M, int N, int K, int* status, cudaStream_t stream);
 cudaError_t rt_gemm_swiglu_bf16(const void* A, long lda, const void* Bg, const void* Bu, long ldb, void* C, long ldc,
-                                int M, int N, int K, int* status, cudaStream_t stream);
+                                int M, int N, int K, int choice, int* status, cudaStream_t stream);
 
 // Teacher-block kernels (bf16 activations, fp32 parameters).
 cudaError_t rt_rmsnorm_1p(const void* x, const void* h, const float* w, void* sum_out, void* out, long rows, int C,

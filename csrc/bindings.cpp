@@ -231,7 +231,7 @@ std::vector<at::Tensor> gemm_group(std::vector<at::Tensor> As, bool a_t, std::ve
   return outs;
 }
 
-at::Tensor gemm_swiglu(at::Tensor A, at::Tensor Bg, at::Tensor Bu) {
+at::Tensor gemm_swiglu(at::Tensor A, at::Tensor Bg, at::Tensor Bu, int64_t tile) {
   c10::cuda::CUDAGuard guard(A.device());
   auto a = operand(A, "A");
   auto g = operand(Bg, "Bg");
@@ -247,7 +247,8 @@ at::Tensor gemm_swiglu(at::Tensor A, at::Tensor Bg, at::Tensor Bu) {
                "gemm_swiglu (skinny)");
     return C;
   }
-  check_cuda(rt_gemm_swiglu_bf16(a.ptr, a.ld, g.ptr, u.ptr, g.ld, C.data_ptr(), N, M, N, K, nullptr, stream_of(A)),
+  check_cuda(rt_gemm_swiglu_bf16(a.ptr, a.ld, g.ptr, u.ptr, g.ld, C.data_ptr(), N, M, N, K, tile ? (int)tile : -1,
+                                 nullptr, stream_of(A)),
              "gemm_swiglu");
   return C;
 }
@@ -804,7 +805,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("teacher"));
   m.def("gemm_nmse", &gemm_nmse, "output GEMM with the NMSE/cosine loss in the epilogue: returns d loss / d p",
         py::arg("x"), py::arg("w"), py::arg("target"), py::arg("stats"), py::arg("eps"));
-  m.def("gemm_swiglu", &gemm_swiglu, "silu(A . Bg^T) * (A . Bu^T) in one tcgen05 GEMM");
+  m.def("gemm_swiglu", &gemm_swiglu, "silu(A . Bg^T) * (A . Bu^T) in one tcgen05 GEMM", py::arg("A"), py::arg("Bg"),
+        py::arg("Bu"), py::arg("tile") = 0);
   m.def("rmsnorm_1p", &rmsnorm_1p);
   m.def("add_rmsnorm_1p", &add_rmsnorm_1p);
   m.def("conv1d_silu", &conv1d_silu);

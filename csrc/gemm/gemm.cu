@@ -30,6 +30,15 @@
 // partials from the workspace and stores the tile, then clears the flag. Waits
 // only ever point at lower-index CTAs, which finished those pieces first.
 //
+// Grouped launches: up to three problems of one shape and layout (the TimeMix r, k and v projections) share
+// the persistent grid, the tile numbering and the stream-K iteration space, each with its own tensor maps and
+// output pointer.
+//
+// 256-row tiles (tuner candidates, store / accumulate / SwiGLU epilogues): the MMA warp issues two M = 128 MMAs
+// per k-step into two TMEM accumulators, both reading the same B tile, which halves the B traffic from L2 per
+// FLOP (what a CTA pair does with cta_group::2, without a cluster). With 512 accumulator columns the TMEM holds
+// one accumulator, so the epilogue of a tile does not overlap the next tile's main loop.
+//
 // All waits are bounded (sm100.cuh); on timeout the kernel records status 1
 // in *status and unwinds, freeing its TMEM.
 #include <cuda.h>
@@ -39,6 +48,7 @@
 #include <mutex>
 #include <atomic>
 #include <cstring>
+#include <cstdlib>
 #include <tuple>
 #include "../common/common.cuh"
 #include "../common/sm100.cuh"
@@ -50,18 +60,28 @@ enum Epi : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_F32_ACCUM = 2, EPI_SWIGLU = 3, E
 constexpr int BM = 128, BK = 64, STAGES = 4, THREADS = 192;
 constexpr int MN_CHUNK_BYTES = 64 * BK * 2;  // one 64-wide MN-major chunk: BK rows x 128 B
 
-template <int BN, bool A_MN, bool B_MN, int EPI>
+// MT = 2: a 256-row tile per CTA as two M = 128 MMAs per k-step that read the same B tile in shared memory, so each
+// B tile crosses L2 half as often per FLOP (the single-CTA counterpart of a CTA-pair tile; no cluster is needed).
+template <int BN, bool A_MN, bool B_MN, int EPI, int MT = 1>
 struct Cfg {
+  static_assert(MT == 1 || (MT == 2 && EPI != EPI_ATOMIC_T && EPI != EPI_NMSE),
+                "256-row tiles take the store, accumulate and SwiGLU epilogues");
   static constexpr int NB = EPI == EPI_SWIGLU ? 2 : 1;
-  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int ROWS = MT * BM;  // tile rows
+  static constexpr int A_HALF = BM * BK * 2;
+  static constexpr int A_BYTES = MT * A_HALF;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + NB * B_BYTES;
-  // Pipeline depth: 4 stages for the compute-bound tiles; the skinny split-K tiles (weight streaming for decode)
-  // are memory-bound and keep 8 stages of 20 KB in flight.
-  static constexpr int ST = EPI == EPI_ATOMIC_T ? 8 : STAGES;
-  static constexpr int ACC_COLS = NB * BN;
-  // two accumulators, rounded up to the power-of-two column count tcgen05.alloc takes
-  static constexpr int TMEM_COLS = 2 * ACC_COLS <= 64 ? 64 : 2 * ACC_COLS <= 128 ? 128 : 2 * ACC_COLS <= 256 ? 256 : 512;
+  // Pipeline depth: 4 stages for the compute-bound tiles (3 where a stage is over 50 KB: 256-row tiles of 192+
+  // columns and the 256-row SwiGLU tile);
+  // the skinny split-K tiles (weight streaming for decode) are memory-bound and keep 8 stages of 20 KB in flight.
+  static constexpr int ST = EPI == EPI_ATOMIC_T ? 8 : STAGES * STAGE_BYTES <= 200 * 1024 ? STAGES : 3;
+  static constexpr int ACC_COLS = NB * BN * MT;
+  // accumulators: two (the epilogue drains one while the next tile accumulates) when they fit in the 512 TMEM
+  // columns, else one; the column count is rounded up to the power of two tcgen05.alloc takes
+  static constexpr int NACC = 2 * ACC_COLS <= 512 ? 2 : 1;
+  static constexpr int TMEM_COLS = NACC * ACC_COLS <= 64 ? 64 : NACC * ACC_COLS <= 128 ? 128
+                                   : NACC * ACC_COLS <= 256 ? 256 : 512;
   static constexpr uint32_t IDESC = sm100::idesc_bf16(BM, BN, A_MN, B_MN);
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM_BYTES = ST * STAGE_BYTES + BAR_BYTES + 1024;
@@ -163,8 +183,8 @@ __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
 
 // Partial-tile slot layout: for 32-column chunk c and float4 q of a row, the 128 rows are contiguous, so a
 // warp's 32 rows move as one 512-byte run.
-__device__ __forceinline__ float4* sk_slot(float* ws, int slot, int bn, int c, int q, int row) {
-  return reinterpret_cast<float4*>(ws) + (long)slot * BM * (bn / 4) + ((long)(c * 8 + q) * BM + row);
+__device__ __forceinline__ float4* sk_slot(float* ws, int slot, int bn, int c, int q, int row, int rows = BM) {
+  return reinterpret_cast<float4*>(ws) + (long)slot * rows * (bn / 4) + ((long)(c * 8 + q) * rows + row);
 }
 
 __device__ __forceinline__ void store_row(float (&v)[32], int epi, void* C, long ldc, int row, int col, int N,
@@ -275,10 +295,10 @@ __device__ __forceinline__ void tile_coords(const GemmArgs& a, int tile, int& g,
 // Set by a launch without a status word whose bounded wait gave up (read and cleared by rt_gemm_fault).
 __device__ int gemm_fault_word = 0;
 
-template <int BN, bool A_MN, bool B_MN, int EPI>
+template <int BN, bool A_MN, bool B_MN, int EPI, int MT>
 __global__ void __launch_bounds__(THREADS, 1)
 gemm_kernel(const __grid_constant__ GemmMaps maps, const GemmArgs args) {
-  using C_ = Cfg<BN, A_MN, B_MN, EPI>;
+  using C_ = Cfg<BN, A_MN, B_MN, EPI, MT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = sm100::align_smem_1024(smem_raw);
   constexpr int ST = C_::ST;
@@ -288,6 +308,7 @@ gemm_kernel(const __grid_constant__ GemmMaps maps, const GemmArgs args) {
   uint64_t* tfull = bars + 2 * ST;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
+  constexpr int NACC = C_::NACC;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -299,7 +320,7 @@ gemm_kernel(const __grid_constant__ GemmMaps maps, const GemmArgs args) {
       sm100::mbar_init(&full[s], 1);
       sm100::mbar_init(&empty[s], 1);
     }
-    for (int a = 0; a < 2; ++a) {
+    for (int a = 0; a < NACC; ++a) {
       sm100::mbar_init(&tfull[a], 1);
       sm100::mbar_init(&tempty[a], 128);
     }
@@ -339,11 +360,16 @@ gemm_kernel(const __grid_constant__ GemmMaps maps, const GemmArgs args) {
           if (!sm100::mbar_wait(&empty[stage], phase ^ 1, abort)) break;
           uint8_t* a_dst = smem + stage * C_::STAGE_BYTES;
           sm100::mbar_expect_tx(&full[stage], C_::STAGE_BYTES);
-          if (!A_MN) {
-            sm100::tma_load_2d(a_dst, ta, &full[stage], kb * BK, tm * BM);
-          } else {
-            sm100::tma_load_2d(a_dst, ta, &full[stage], tm * BM, kb * BK);
-            sm100::tma_load_2d(a_dst + MN_CHUNK_BYTES, ta, &full[stage], tm * BM + 64, kb * BK);
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt) {
+            uint8_t* a_half = a_dst + mt * C_::A_HALF;
+            const int m0 = tm * C_::ROWS + mt * BM;
+            if (!A_MN) {
+              sm100::tma_load_2d(a_half, ta, &full[stage], kb * BK, m0);
+            } else {
+              sm100::tma_load_2d(a_half, ta, &full[stage], m0, kb * BK);
+              sm100::tma_load_2d(a_half + MN_CHUNK_BYTES, ta, &full[stage], m0 + 64, kb * BK);
+            }
           }
 #pragma unroll
           for (int j = 0; j < C_::NB; ++j) {
@@ -386,14 +412,18 @@ gemm_kernel(const __grid_constant__ GemmMaps maps, const GemmArgs args) {
           const uint32_t a_base = sm100::smem_u32(smem + stage * C_::STAGE_BYTES);
 #pragma unroll
           for (int ks = 0; ks < BK / 16; ++ks) {
-            const uint64_t adesc = A_MN ? sm100::smem_desc(a_base + ks * 2048, MN_CHUNK_BYTES, 1024)
-                                        : sm100::smem_desc(a_base + ks * 32, 16, 1024);
 #pragma unroll
-            for (int j = 0; j < C_::NB; ++j) {
-              const uint32_t b_base = a_base + C_::A_BYTES + j * C_::B_BYTES;
-              const uint64_t bdesc = B_MN ? sm100::smem_desc(b_base + ks * 2048, MN_CHUNK_BYTES, 1024)
-                                          : sm100::smem_desc(b_base + ks * 32, 16, 1024);
-              sm100::mma_bf16(d_tmem + j * BN, adesc, bdesc, C_::IDESC, (kb != k0) || (ks != 0));
+            for (int mt = 0; mt < MT; ++mt) {
+              const uint32_t a_half = a_base + mt * C_::A_HALF;
+              const uint64_t adesc = A_MN ? sm100::smem_desc(a_half + ks * 2048, MN_CHUNK_BYTES, 1024)
+                                          : sm100::smem_desc(a_half + ks * 32, 16, 1024);
+#pragma unroll
+              for (int j = 0; j < C_::NB; ++j) {
+                const uint32_t b_base = a_base + C_::A_BYTES + j * C_::B_BYTES;
+                const uint64_t bdesc = B_MN ? sm100::smem_desc(b_base + ks * 2048, MN_CHUNK_BYTES, 1024)
+                                            : sm100::smem_desc(b_base + ks * 32, 16, 1024);
+                sm100::mma_bf16(d_tmem + (mt * C_::NB + j) * BN, adesc, bdesc, C_::IDESC, (kb != k0) || (ks != 0));
+              }
             }
           }
           sm100::mma_commit(&empty[stage]);
@@ -401,7 +431,7 @@ gemm_kernel(const __grid_constant__ GemmMaps maps, const GemmArgs args) {
         }
         if (!ok) break;
         sm100::mma_commit(&tfull[acc]);
-        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+        if (++acc == NACC) { acc = 0; acc_phase ^= 1; }
       }
       sm100::mma_commit(drain);
       sm100::mbar_wait_bounded(drain, 0);
@@ -420,9 +450,9 @@ gemm_kernel(const __grid_constant__ GemmMaps maps, const GemmArgs args) {
       void* const Cg = args.C[g];
       if (!sm100::mbar_wait(&tfull[acc], acc_phase, abort)) break;
       sm100::tc_fence_after();
-      const int row = tm * BM + row_in_tile;
+      const int row = tm * C_::ROWS + row_in_tile;
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * C_::ACC_COLS;
-      if (C_::NB == 1 && EPI != EPI_NMSE && EPI != EPI_ATOMIC_T && args.splitp > 1) {
+      if (MT == 1 && C_::NB == 1 && EPI != EPI_NMSE && EPI != EPI_ATOMIC_T && args.splitp > 1) {
         // ---- parallel split-K: publish this part, wait for the tile's other parts, reduce this CTA's row band
         const int S = args.splitp, part = blockIdx.x % S;
 #pragma unroll 1
@@ -437,7 +467,7 @@ gemm_kernel(const __grid_constant__ GemmMaps maps, const GemmArgs args) {
         }
         sm100::tc_fence_before();
         sm100::mbar_arrive(&tempty[acc]);
-        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+        if (++acc == NACC) { acc = 0; acc_phase ^= 1; }
         int* arrive = args.flags + 4 * tile;
         int* depart = arrive + 1;
         __threadfence();
@@ -519,12 +549,15 @@ gemm_kernel(const __grid_constant__ GemmMaps maps, const GemmArgs args) {
         if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
       }
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int cc = 0; cc < MT * (BN / 32); ++cc) {  // MT = 2: rows 128..255 of the tile sit BN columns further
+        const int mt = cc / (BN / 32), c = cc % (BN / 32);
+        const int srow = mt * BM + row_in_tile, grow = row + mt * BM;
         float v[32];
-        sm100::tmem_ld32(t_row + c * 32, v);
+        const uint32_t t_half = t_row + mt * C_::NB * BN;  // this row half's accumulator (gate, then up for SwiGLU)
+        sm100::tmem_ld32(t_half + c * 32, v);
         if (EPI == EPI_SWIGLU) {
           float u[32];
-          sm100::tmem_ld32(t_row + BN + c * 32, u);
+          sm100::tmem_ld32(t_half + BN + c * 32, u);
           sm100::tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] = rt::siluf_(v[i]) * u[i];
@@ -534,7 +567,7 @@ gemm_kernel(const __grid_constant__ GemmMaps maps, const GemmArgs args) {
         if (partial) {
 #pragma unroll
           for (int q = 0; q < 8; ++q)
-            __stcg(sk_slot(args.ws, blockIdx.x, BN, c, q, row_in_tile),
+            __stcg(sk_slot(args.ws, blockIdx.x, BN, c, q, srow, C_::ROWS),
                    make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
           continue;
         }
@@ -542,16 +575,16 @@ gemm_kernel(const __grid_constant__ GemmMaps maps, const GemmArgs args) {
           for (int slot = first_slot; slot < (int)blockIdx.x; ++slot) {
 #pragma unroll
             for (int q = 0; q < 8; ++q) {
-              const float4 p = __ldcg(sk_slot(args.ws, slot, BN, c, q, row_in_tile));
+              const float4 p = __ldcg(sk_slot(args.ws, slot, BN, c, q, srow, C_::ROWS));
               v[4 * q] += p.x; v[4 * q + 1] += p.y; v[4 * q + 2] += p.z; v[4 * q + 3] += p.w;
             }
           }
         }
-        if (row < args.M) {
+        if (grow < args.M) {
           if (EPI == EPI_NMSE)
-            loss_row(v, args, row, tn * BN + c * 32, se, pp, pt);
+            loss_row(v, args, grow, tn * BN + c * 32, se, pp, pt);
           else
-            store_row(v, EPI, Cg, args.ldc, row, tn * BN + c * 32, args.N, args.alpha);
+            store_row(v, EPI, Cg, args.ldc, grow, tn * BN + c * 32, args.N, args.alpha);
         }
       }
       if (EPI == EPI_NMSE && !partial && row < args.M) {
@@ -561,8 +594,8 @@ gemm_kernel(const __grid_constant__ GemmMaps maps, const GemmArgs args) {
       }
       sm100::tc_fence_before();
       sm100::mbar_arrive(&tempty[acc]);
-      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
-      if (partial) {  // publish this warp's 32 rows
+      if (++acc == NACC) { acc = 0; acc_phase ^= 1; }
+      if (partial) {  // publish this warp's 32 rows (both halves of a 256-row tile)
         __threadfence();
         __syncwarp();
         if (lane == 0) atomicAdd(flag, 1);
@@ -622,7 +655,7 @@ int num_sms_cached() {
   return sms;
 }
 
-// Stream-K workspace of one device: a BM x 256 fp32 partial slot per SM and 4 counters per tile. Allocated on
+// Stream-K workspace of one device: a 256 x 256 fp32 partial slot per SM (the widest tile) and 4 counters per tile. Allocated on
 // the first stream-K launch outside stream capture and kept (graphs hold its address); the counters are zeroed
 // once and every launch leaves them zero again. Stream-K launches of one device therefore must not run
 // concurrently on two streams; the framework issues all GEMMs of a device on one stream at a time.
@@ -643,7 +676,7 @@ SkWorkspace* sk_workspace(cudaStream_t stream) {
   if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) return nullptr;
   float* ws = nullptr;
   int* flags = nullptr;
-  if (cudaMalloc(&ws, (size_t)num_sms_cached() * BM * 256 * sizeof(float)) != cudaSuccess) return nullptr;
+  if (cudaMalloc(&ws, (size_t)num_sms_cached() * 2 * BM * 256 * sizeof(float)) != cudaSuccess) return nullptr;
   if (cudaMalloc(&flags, SK_MAX_FLAGS * sizeof(int)) != cudaSuccess ||
       cudaMemsetAsync(flags, 0, SK_MAX_FLAGS * sizeof(int), stream) != cudaSuccess) {
     cudaFree(ws);
@@ -694,10 +727,10 @@ cudaError_t set_smem_once(std::atomic<uint64_t>& done, Kern kern, int bytes) {
   return cudaSuccess;
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI>
+template <int BN, bool A_MN, bool B_MN, int EPI, int MT = 1>
 cudaError_t launch(const Prob& p, float alpha, int* status, cudaStream_t stream, int splits = 1, bool sk = false,
                    LossArgs loss = LossArgs(), int splitp = 0) {
-  using C_ = Cfg<BN, A_MN, B_MN, EPI>;
+  using C_ = Cfg<BN, A_MN, B_MN, EPI, MT>;
   if (p.G < 1 || p.G > MAX_GROUPS || (C_::NB == 2 && p.G != 1)) return cudaErrorInvalidValue;
   const int M = p.M, N = p.N, K = p.K;
   GemmMaps maps;
@@ -716,7 +749,7 @@ cudaError_t launch(const Prob& p, float alpha, int* status, cudaStream_t stream,
   args.M = M; args.N = N; args.K = K; args.ldc = p.ldc; args.alpha = alpha; args.status = status;
   args.groups = p.G;
   for (int g = 0; g < MAX_GROUPS; ++g) args.C[g] = g < p.G ? p.C[g] : p.C[0];
-  args.tiles_m = (M + BM - 1) / BM;
+  args.tiles_m = (M + C_::ROWS - 1) / C_::ROWS;
   args.tiles_n = (N + BN - 1) / BN;
   args.splits = splits;
   args.kchunk = ((K + BK - 1) / BK + splits - 1) / splits;
@@ -727,7 +760,7 @@ cudaError_t launch(const Prob& p, float alpha, int* status, cudaStream_t stream,
   args.rowsum = loss.rowsum;
   args.eps = loss.eps;
   int grid = total < num_sms_cached() ? total : num_sms_cached();
-  if (splitp > 1 && C_::NB == 1 && splits == 1 && EPI != EPI_ATOMIC_T && EPI != EPI_NMSE) {
+  if (splitp > 1 && MT == 1 && C_::NB == 1 && splits == 1 && EPI != EPI_ATOMIC_T && EPI != EPI_NMSE) {
     const int kb = (K + BK - 1) / BK;
     int S = splitp;
     while (S > 1 && (tiles * S > num_sms_cached() || kb < 2 * S)) --S;  // co-resident CTAs, >= 2 k-blocks each
@@ -751,7 +784,7 @@ cudaError_t launch(const Prob& p, float alpha, int* status, cudaStream_t stream,
       args.flags = w->flags;
     }
   }
-  auto kern = gemm_kernel<BN, A_MN, B_MN, EPI>;
+  auto kern = gemm_kernel<BN, A_MN, B_MN, EPI, MT>;
   static std::atomic<uint64_t> smem_set{0};  // one per instantiation of this launcher, i.e. per kernel
   RT_CUDA_CHECK(set_smem_once(smem_set, kern, C_::SMEM_BYTES));
   kern<<<grid, THREADS, C_::SMEM_BYTES, stream>>>(maps, args);
@@ -784,8 +817,10 @@ int pick_bn(int M, int N, int G, bool swiglu, bool b_mn) {
   return best;
 }
 
-// Tile choice: width bn, plus SK_FLAG for the stream-K schedule.
+// Tile choice: width bn, plus SK_FLAG for the stream-K schedule and M2_FLAG for 256-row tiles (widths 256 and 128,
+// store and accumulate epilogues).
 constexpr int SK_FLAG = 1 << 16;
+constexpr int M2_FLAG = 1 << 17;
 constexpr int SP_SHIFT = 20;  // choice bits 20..27: parallel split-K factor S (0 = off)
 
 template <bool A_MN, bool B_MN, int EPI>
@@ -793,6 +828,11 @@ cudaError_t dispatch_bn(int choice, const Prob& p, float alpha, int* status, cud
   const int bn = choice & (SK_FLAG - 1);
   const bool sk = (choice & SK_FLAG) != 0;
   const int sp = (choice >> SP_SHIFT) & 255;
+  if (choice & M2_FLAG) {
+    if (bn == 256) return launch<256, A_MN, B_MN, EPI, 2>(p, alpha, status, s, 1, sk);
+    if (bn == 128) return launch<128, A_MN, B_MN, EPI, 2>(p, alpha, status, s, 1, sk);
+    return cudaErrorInvalidValue;
+  }
 #define RT_L(W) return launch<W, A_MN, B_MN, EPI>(p, alpha, status, s, 1, sk, LossArgs(), sp)
   if (bn == 256) RT_L(256);
   if (bn == 192) RT_L(192);
@@ -825,6 +865,15 @@ std::map<TileKey, int>& tile_cache() {
 std::mutex& tile_mutex() {
   static std::mutex m;
   return m;
+}
+
+// 256-row tiles among the measured candidates (THESEUS_GEMM_M2=0 leaves them out, for comparisons).
+bool m2_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("THESEUS_GEMM_M2");
+    return !(e && e[0] == '0');
+  }();
+  return on;
 }
 
 int measured_bn(const TileKey& key, const Prob& p, int epi, float alpha, int* status, cudaStream_t stream) {
@@ -873,6 +922,8 @@ int measured_bn(const TileKey& key, const Prob& p, int epi, float alpha, int* st
   float best_ms = 1e30f;
   const long kblocks = (key.K + BK - 1) / BK;
   std::vector<int> choices = {256, 224, 192, 160, 128, 64, 256 | SK_FLAG, 224 | SK_FLAG, 192 | SK_FLAG, 128 | SK_FLAG};
+  if (key.M >= 2 * BM && epi != EPI_NMSE && m2_enabled())
+    for (int c : {256 | M2_FLAG, 128 | M2_FLAG, 256 | M2_FLAG | SK_FLAG, 128 | M2_FLAG | SK_FLAG}) choices.push_back(c);
   {  // parallel split-K where the tiles fill under half of the SMs and K is deep
     const int sms = num_sms_cached();
     for (int bn : {64, 128, 192, 256}) {
@@ -888,7 +939,8 @@ int measured_bn(const TileKey& key, const Prob& p, int epi, float alpha, int* st
     if (key.b_mn && bn % 64) continue;
     if (key.N < bn / 2 && bn != 64) continue;
     if (choice & SK_FLAG) {  // stream-K only where the whole-tile schedule leaves a wave partly idle
-      const long tiles = (long)((key.M + BM - 1) / BM) * ((key.N + bn - 1) / bn) * key.G;
+      const int rows = (choice & M2_FLAG) ? 2 * BM : BM;
+      const long tiles = (long)((key.M + rows - 1) / rows) * ((key.N + bn - 1) / bn) * key.G;
       const int sms = num_sms_cached();
       if (tiles % sms == 0 || tiles * kblocks < 2L * sms || kblocks < 8) continue;
     }
@@ -946,6 +998,7 @@ cudaError_t gemm_fixed(const Prob& p, int a_mn, int b_mn, int epi, float alpha, 
   const int bn = choice & (SK_FLAG - 1);
   if (bn != 64 && bn != 128 && bn != 160 && bn != 192 && bn != 224 && bn != 256) return cudaErrorInvalidValue;
   if (b_mn && bn % 64) return cudaErrorInvalidValue;
+  if ((choice & M2_FLAG) && ((bn != 128 && bn != 256) || (choice >> SP_SHIFT))) return cudaErrorInvalidValue;
   return gemm_with_bn(choice, p, a_mn, b_mn, epi, alpha, status, stream);
 }
 
@@ -1130,12 +1183,74 @@ extern "C" cudaError_t rt_gemm_skinny_bf16(const void* X, long ldx, const void* 
   return cudaGetLastError();
 }
 
-// out[M,N] bf16 = silu(A · Bg^T) * (A · Bu^T); A, Bg, Bu K-major.
+namespace {
+cudaError_t swiglu_launch(int choice, const Prob& p, int* status, cudaStream_t stream) {
+  if (choice & M2_FLAG) return launch<128, false, false, EPI_SWIGLU, 2>(p, 1.f, status, stream);
+  return launch<128, false, false, EPI_SWIGLU>(p, 1.f, status, stream);
+}
+
+// SwiGLU tile rows per shape bucket (128, or 256 with M2_FLAG), measured once outside stream capture like the
+// single-B tile widths: one warm-up launch and the best of two batches of four per candidate; 128 rows unless the
+// 256-row tile is more than 3% faster. Both compute every output with the same MMA sequence over K.
+int swiglu_choice(const Prob& p, int* status, cudaStream_t stream) {
+  const TileKey key{(p.M + BM - 1) / BM * BM, p.N, (p.K + 511) / 512 * 512, 2, 2, 1};  // layouts 2: SwiGLU
+  {
+    std::lock_guard<std::mutex> lock(tile_mutex());
+    auto it = tile_cache().find(key);
+    if (it != tile_cache().end()) return it->second;
+  }
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (p.M < 2 * BM || !m2_enabled() || cudaStreamIsCapturing(stream, &cap) != cudaSuccess ||
+      cap != cudaStreamCaptureStatusNone)
+    return 128;
+  cudaEvent_t e0, e1;
+  if (cudaEventCreate(&e0) != cudaSuccess) return 128;
+  if (cudaEventCreate(&e1) != cudaSuccess) {
+    cudaEventDestroy(e0);
+    return 128;
+  }
+  int best = 128;
+  float best_ms = 1e30f;
+  for (int choice : {128, 128 | M2_FLAG}) {
+    float ms = 1e30f;
+    bool failed = swiglu_launch(choice, p, status, stream) != cudaSuccess;
+    for (int rep = 0; rep < 2 && !failed; ++rep) {
+      cudaEventRecord(e0, stream);
+      for (int l = 0; l < 4 && !failed; ++l) failed = swiglu_launch(choice, p, status, stream) != cudaSuccess;
+      cudaEventRecord(e1, stream);
+      if (failed || cudaEventSynchronize(e1) != cudaSuccess) break;
+      float t = 0.f;
+      cudaEventElapsedTime(&t, e0, e1);
+      ms = std::min(ms, t / 4);
+    }
+    if (failed) {
+      cudaGetLastError();
+      continue;
+    }
+    const float score = choice == 128 ? 0.97f * ms : ms;
+    if (score < best_ms) {
+      best_ms = score;
+      best = choice;
+    }
+  }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  std::lock_guard<std::mutex> lock(tile_mutex());
+  tile_cache()[key] = best;
+  return best;
+}
+}  // namespace
+
+// out[M,N] bf16 = silu(A · Bg^T) * (A · Bu^T); A, Bg, Bu K-major. choice < 0: measured tile rows; else 128
+// (choice 128) or 256 (128 | 1 << 17) rows per tile (tests).
 extern "C" cudaError_t rt_gemm_swiglu_bf16(const void* A, long lda, const void* Bg, const void* Bu, long ldb, void* C,
-                                           long ldc, int M, int N, int K, int* status, cudaStream_t stream) {
+                                           long ldc, int M, int N, int K, int choice, int* status,
+                                           cudaStream_t stream) {
   if (M <= 0 || N <= 0 || K <= 0) return cudaSuccess;
   if ((lda & 7) || (ldb & 7)) return cudaErrorInvalidValue;
   Prob p = single(A, lda, Bg, ldb, C, ldc, M, N, K);
   p.B1 = Bu;
-  return launch<128, false, false, EPI_SWIGLU>(p, 1.f, status, stream);
+  if (bad_operands(p) || !Bu || (reinterpret_cast<uintptr_t>(Bu) & 15)) return cudaErrorInvalidValue;
+  if (choice >= 0 && choice != 128 && choice != (128 | M2_FLAG)) return cudaErrorInvalidValue;
+  return swiglu_launch(choice < 0 ? swiglu_choice(p, status, stream) : choice, p, status, stream);
 }

@@ -161,7 +161,9 @@ def test_parallel_split_k_matches_fp32(M, N, K, tile):
 # Fixed schedules for the grouped launch: whole tiles of 256 / 128 / 64 columns, stream-K, parallel split-K (S = 4).
 # At 384 x 640 x 1216 every one of them runs as named for G = 2 and 3 (stream-K: at least one k-block per SM;
 # split-K: tiles x S within the SM count).
-_GROUP_SCHEDULES = [256, 128, 64, 256 | (1 << 16), 128 | (1 << 16), 256 | (4 << 20)]
+M2 = 1 << 17  # tile choice bit: 256-row tiles (two M = 128 MMAs per k-step on one B tile)
+_GROUP_SCHEDULES = [256, 128, 64, 256 | (1 << 16), 128 | (1 << 16), 256 | (4 << 20),
+                    256 | M2, 128 | M2, 256 | M2 | (1 << 16), 128 | M2 | (1 << 16)]
 
 
 @cuda
@@ -212,3 +214,34 @@ def test_grouped_gemm_rejects_mismatched_problems():
         native().gemm_group([A, _bf(128, 128, seed=3)], False, [B, B], False, 0, 1.0, [], 0)
     with pytest.raises(RuntimeError):
         native().gemm_group([A] * 4, False, [B] * 4, False, 0, 1.0, [], 0)
+
+
+@cuda
+@pytest.mark.parametrize("M,N,K", [(1024, 5120, 1024), (296, 384, 704), (1000, 200, 352), (256, 64, 64)])
+@pytest.mark.parametrize("a_t,b_t", [(False, False), (False, True), (True, False), (True, True)])
+@pytest.mark.parametrize("tile", [256 | M2, 128 | M2, 256 | M2 | (1 << 16), 128 | M2 | (1 << 16)])
+def test_256_row_tiles_match_fp32(M, N, K, a_t, b_t, tile):
+    """256-row tiles: partial row and column tiles, all operand layouts, store / fp32 / accumulate epilogues, whole
+    tiles and stream-K (run twice: the stream-K counters must be left at zero)."""
+    if (a_t and M % 8) or (b_t and N % 8):
+        pytest.skip("MN-major operands need a row stride that is a multiple of 8")
+    A = _bf(K, M, seed=51) if a_t else _bf(M, K, seed=51)
+    B = _bf(K, N, seed=52) if b_t else _bf(N, K, seed=52)
+    ref = (A.float().t() if a_t else A.float()) @ (B.float() if b_t else B.float().t())
+    for _ in range(2):
+        _check(native().gemm(A, a_t, B, b_t, 0, 1.0, None, tile), ref)
+    _check(native().gemm(A, a_t, B, b_t, 1, 1.0, None, tile), ref, 1e-3)
+    base = torch.randn(M, N, device="cuda")
+    acc = base.clone()
+    native().gemm(A, a_t, B, b_t, 2, -0.5, acc, tile)
+    _check(acc, base - 0.5 * ref, 1e-3)
+
+
+@cuda
+@pytest.mark.parametrize("M,N,K", [(1024, 1536, 1024), (300, 384, 512)])
+@pytest.mark.parametrize("tile", [0, 128, 128 | M2])
+def test_swiglu_tile_rows(M, N, K, tile):
+    """SwiGLU with 128- and 256-row tiles (and the measured choice) against fp32."""
+    x, wg, wu = _bf(M, K, seed=61), _bf(N, K, seed=62), _bf(N, K, seed=63)
+    ref = torch.nn.functional.silu(x.float() @ wg.float().t()) * (x.float() @ wu.float().t())
+    _check(native().gemm_swiglu(x, wg, wu, tile), ref)
