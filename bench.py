@@ -69,6 +69,8 @@ def parse():
     p.add_argument("--context", type=int, default=4096)
     p.add_argument("--micro-batch", type=int, default=1)
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--overlap-students", type=int, choices=(0, 1), default=1,
+                   help="ours: run the students' micro-steps on their own stream beside the teacher forward")
     p.add_argument("--profile", action="store_true", help="print a per-kernel breakdown of one step and exit")
     return p.parse_args()
 
@@ -87,7 +89,7 @@ def init_env(args):
 def write_dataset(root, vocab, tokens_needed, seed):
     """Synthetic manifest v1: documents with log-uniform lengths in [256, 16384]."""
     import numpy as np
-    from rwkv_theseus_b200.data import digest_file
+    from rwkv_theseus_b200.data import sha256_of_file
     rng = np.random.default_rng(seed)
     lengths, total = [], 0
     while total < tokens_needed:
@@ -99,7 +101,7 @@ def write_dataset(root, vocab, tokens_needed, seed):
     np.save(root / "offsets.npy", np.concatenate([[0], np.cumsum(lengths)]).astype(np.int64))
     manifest = {"format": 1, "vocab_size": vocab, "sources": [{
         "tokens": "tokens.bin", "offsets": "offsets.npy", "weight": 1.0,
-        "tokens_sha256": digest_file(root / "tokens.bin"), "offsets_sha256": digest_file(root / "offsets.npy")}]}
+        "tokens_sha256": sha256_of_file(root / "tokens.bin"), "offsets_sha256": sha256_of_file(root / "offsets.npy")}]}
     (root / "manifest.json").write_text(json.dumps(manifest))
     return root / "manifest.json"
 
@@ -164,7 +166,8 @@ def build_ours(args, topo, manifest, model_spec):
                        "output": str(Path(tempfile.gettempdir()) / "bench_out"), "model": str(ROOT),
                        "chunk_tokens": args.chunk, "context_tokens": args.context,
                        "micro_batch_size": args.micro_batch, "training_mode": "epoch", "head_size": 64,
-                       "backend": "cuda", "distributed_backend": "nccl"})
+                       "backend": "cuda", "distributed_backend": "nccl",
+                       "overlap_students": bool(args.overlap_students)})
     runner = Runner(model)
     students, captures = {}, {}
     for i, layer in enumerate(order):

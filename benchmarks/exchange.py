@@ -17,6 +17,7 @@ import argparse
 import json
 import os
 import sys
+import time
 import types
 
 import torch
@@ -110,9 +111,8 @@ def main():
                     rows.setdefault(evt.name[:48], []).append(evt.device_time)
             for name, ts in sorted(rows.items(), key=lambda kv: -sum(kv[1])):
                 print(json.dumps({"kernel": name, "calls": len(ts), "avg_us": sum(ts) / len(ts)}), flush=True)
-    from bench import ClockSampler  # nvidia-smi clocks and throttle reasons of this rank's GPU while timing
+    from bench import ClockSampler  # nvidia-smi clocks and throttle reasons of this rank's GPU under load
     uuid = str(torch.cuda.get_device_properties(dev).uuid)
-    sampler = ClockSampler(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
     base = timed(copy_only, a.iters, topo)
     frac = (N - 1) / N
     link_ms = 6 * n * frac / (LINK_GBS * 1e9) * 1e3
@@ -130,6 +130,17 @@ def main():
                             "nccl_ms": t_nccl, "nvlink_roofline_ms": link_ms,
                             "peer_fraction_of_roofline": link_ms / t_peer, "speedup_vs_nccl": t_nccl / t_peer,
                             "blocks": blocks, "mode": mode})
+    # The timed loops above last well under a second; the clock record comes from a separate 3-second loop of the
+    # last configuration under nvidia-smi (its start-up stalls CUDA calls briefly, so it is not timed).
+    sampler = ClockSampler(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+    start = time.perf_counter()
+    while True:
+        peer()
+        torch.cuda.synchronize()
+        done = torch.tensor([time.perf_counter() - start > 3.0], device=dev, dtype=torch.int32)
+        dist.all_reduce(done, op=dist.ReduceOp.MIN, group=topo.student_group)  # every rank leaves together
+        if done.item():
+            break
     clocks = sampler.stop()
     if topo.rank == 0:
         for line in results:

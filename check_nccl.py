@@ -73,14 +73,17 @@ def run(args):
                 raise RuntimeError("Student parameters diverged after the update")
             for group in (student.flat.param, student.flat.exp_avg, student.flat.exp_avg_sq):
                 assert group.dtype == torch.float32
-        snapshot = ({k: v.detach().cpu().to(torch.bfloat16) for k, v in student.weights().items()}
-                    if topo.rank == topo.leader else None)
-        weights = topo.broadcast_weights(snapshot)
-        assert weights and all(t.dtype == torch.bfloat16 and t.isfinite().all() for t in weights.values())
-        if topo.rank == topo.leader:
-            print(json.dumps({"stage": stage + 1, "backend": args.backend, "replicas": topo.world,
-                              "grad_sync": (args.grad_sync if cuda else "all_reduce") if topo.world > 1 else "local",
-                              "steps": args.steps, "status": "passed"}), flush=True)
+        leader = topo.rank == topo.leader
+        # the leader's bf16 weights reach every rank intact (the assembly path of validation and export)
+        received = topo.broadcast_weights(
+            {name: t.detach().cpu().to(torch.bfloat16) for name, t in student.weights().items()} if leader else None)
+        if not received or any(t.dtype != torch.bfloat16 or not bool(t.isfinite().all()) for t in received.values()):
+            raise RuntimeError("Broadcast weights arrived empty, in the wrong dtype or non-finite")
+        if leader:
+            sync = "local" if topo.world == 1 else (args.grad_sync if cuda else "all_reduce")
+            record = {"stage": stage + 1, "backend": args.backend, "replicas": topo.world, "grad_sync": sync,
+                      "steps": args.steps, "status": "passed"}
+            print(json.dumps(record), flush=True)
         del student
         topo.barrier()
     topo.close()

@@ -46,6 +46,8 @@ cudaError_t rt_gemm_bf16(const void* A, long lda, int a_mn, const void* B, long 
 cudaError_t rt_gemm_bf16_group(int G, const void* const* A, long lda, int a_mn, const void* const* B, long ldb,
                                int b_mn, void* const* C, long ldc, int M, int N, int K, int epi, float alpha,
                                int choice, int* status, cudaStream_t stream);
+cudaError_t rt_gemm_set_lane(int lane);
+void rt_gemm_set_concurrent(int on);
 int rt_gemm_fault();
 cudaError_t rt_gemm_fault_async(int* dst, cudaStream_t stream);
 int rt_kl_segments(long rows, long V);

@@ -799,6 +799,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_group", &gemm_group, "up to 3 tcgen05 GEMMs of one shape in one launch (shared stream-K schedule)",
         py::arg("A"), py::arg("a_t"), py::arg("B"), py::arg("b_t"), py::arg("epi") = 0, py::arg("alpha") = 1.0,
         py::arg("outs") = std::vector<at::Tensor>(), py::arg("tile") = 0);
+  m.def("gemm_set_lane", [](int64_t lane) { check_cuda(rt_gemm_set_lane((int)lane), "gemm_set_lane"); },
+        "issue lane (0 or 1) of this thread's next GEMMs: each lane has its own stream-K workspace");
+  m.def("gemm_set_concurrent", [](bool on) { rt_gemm_set_concurrent(on ? 1 : 0); },
+        "GEMMs of both lanes may overlap: parallel split-K tile choices run as stream-K");
   m.def("gemm_fault", []() { return rt_gemm_fault(); },
         "1 if a GEMM gave up a bounded wait since the last call (then cleared); synchronizes the device");
   m.def("kl_rows", &kl_rows, "per-row KL(teacher || student) over the vocabulary in one pass", py::arg("student"),

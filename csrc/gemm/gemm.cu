@@ -655,22 +655,30 @@ int num_sms_cached() {
   return sms;
 }
 
-// Stream-K workspace of one device: a 256 x 256 fp32 partial slot per SM (the widest tile) and 4 counters per tile. Allocated on
-// the first stream-K launch outside stream capture and kept (graphs hold its address); the counters are zeroed
-// once and every launch leaves them zero again. Stream-K launches of one device therefore must not run
-// concurrently on two streams; the framework issues all GEMMs of a device on one stream at a time.
+// Stream-K workspace of one device and issue lane: a 256 x 256 fp32 partial slot per SM (the widest tile) and 4
+// counters per tile. Allocated on the first stream-K launch of the lane outside stream capture and kept (graphs
+// hold its address); the counters are zeroed once and every launch leaves them zero again. Launches that use one
+// workspace therefore must not run concurrently: a lane is a sequence of GEMMs issued in order on one stream (the
+// teacher's forward is lane 0, the students' micro-steps lane 1 when they run beside it), and the host thread
+// selects the lane of its next launches with rt_gemm_set_lane.
 constexpr int SK_MAX_FLAGS = 4 * 32768;
+constexpr int SK_LANES = 2;
 struct SkWorkspace {
   float* ws = nullptr;
   int* flags = nullptr;
 };
-std::map<int, SkWorkspace> g_sk_spaces;
+std::map<std::pair<int, int>, SkWorkspace> g_sk_spaces;  // (device, lane)
 std::mutex g_sk_mutex;
+thread_local int g_lane = 0;
+// Set while GEMMs of two lanes may run at the same time. Parallel split-K (whose S parts wait for each other and
+// so need all of them resident at once) then runs as stream-K, whose waits only point at lower-index CTAs that
+// were dispatched earlier: two concurrent GEMMs can delay each other's CTAs but never wait on each other.
+std::atomic<bool> g_concurrent{false};
 SkWorkspace* sk_workspace(cudaStream_t stream) {
   int dev = 0;
   cudaGetDevice(&dev);
   std::lock_guard<std::mutex> lock(g_sk_mutex);
-  SkWorkspace& w = g_sk_spaces[dev];
+  SkWorkspace& w = g_sk_spaces[{dev, g_lane}];
   if (w.ws) return &w;
   cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
   if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) return nullptr;
@@ -760,6 +768,10 @@ cudaError_t launch(const Prob& p, float alpha, int* status, cudaStream_t stream,
   args.rowsum = loss.rowsum;
   args.eps = loss.eps;
   int grid = total < num_sms_cached() ? total : num_sms_cached();
+  if (splitp > 1 && g_concurrent.load(std::memory_order_relaxed)) {  // see g_concurrent
+    splitp = 0;
+    sk = true;
+  }
   if (splitp > 1 && MT == 1 && C_::NB == 1 && splits == 1 && EPI != EPI_ATOMIC_T && EPI != EPI_NMSE) {
     const int kb = (K + BK - 1) / BK;
     int S = splitp;
@@ -1083,13 +1095,26 @@ extern "C" int rt_gemm_fault() {
     int dev = 0;
     cudaGetDevice(&dev);
     std::lock_guard<std::mutex> lock(g_sk_mutex);
-    auto it = g_sk_spaces.find(dev);
-    if (it != g_sk_spaces.end() && it->second.flags && (cudaDeviceSynchronize() != cudaSuccess ||
-                                                        cudaMemset(it->second.flags, 0, SK_MAX_FLAGS * sizeof(int)) != cudaSuccess))
-      return -1;
+    if (cudaDeviceSynchronize() != cudaSuccess) return -1;
+    for (int lane = 0; lane < SK_LANES; ++lane) {
+      auto it = g_sk_spaces.find({dev, lane});
+      if (it != g_sk_spaces.end() && it->second.flags &&
+          cudaMemset(it->second.flags, 0, SK_MAX_FLAGS * sizeof(int)) != cudaSuccess)
+        return -1;
+    }
   }
   return v;
 }
+
+// Issue lane of this host thread's next GEMM launches (0 or 1; each lane has its own stream-K workspace).
+extern "C" cudaError_t rt_gemm_set_lane(int lane) {
+  if (lane < 0 || lane >= SK_LANES) return cudaErrorInvalidValue;
+  g_lane = lane;
+  return cudaSuccess;
+}
+
+// 1 while GEMMs of both lanes may overlap on the device (parallel split-K choices then run as stream-K).
+extern "C" void rt_gemm_set_concurrent(int on) { g_concurrent.store(on != 0); }
 
 // Asynchronous form of rt_gemm_fault for a per-step metrics snapshot: on `stream`, copy the fault word to `dst`
 // (pinned host or device memory) and clear it. A nonzero copy means a launch before it gave up a wait; the
@@ -1198,6 +1223,19 @@ int swiglu_choice(const Prob& p, int* status, cudaStream_t stream) {
     std::lock_guard<std::mutex> lock(tile_mutex());
     auto it = tile_cache().find(key);
     if (it != tile_cache().end()) return it->second;
+    // A shorter chunk of a measured shape (same N and K, fewer rows) reuses the nearest larger bucket's choice
+    // (256-row tiles only while it keeps at least two row tiles) instead of timing in the middle of training.
+    int reuse = -1, reuse_m = 0;
+    for (const auto& [k, choice] : tile_cache())
+      if (k.a_mn == 2 && k.N == key.N && k.K == key.K && k.M > key.M && (reuse < 0 || k.M < reuse_m)) {
+        reuse = choice;
+        reuse_m = k.M;
+      }
+    if (reuse >= 0) {
+      if (key.M < 2 * 2 * BM) reuse = 128;
+      tile_cache()[key] = reuse;
+      return reuse;
+    }
   }
   cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
   if (p.M < 2 * BM || !m2_enabled() || cudaStreamIsCapturing(stream, &cap) != cudaSuccess ||

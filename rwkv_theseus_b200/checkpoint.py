@@ -30,12 +30,13 @@ import torch
 from safetensors.torch import load_file, save_file
 from torch.utils._pytree import tree_map
 
-from .data import digest_file
+from .data import sha256_of_file
 
 # Config keys that may change between a checkpoint and its resume (plus every ``wandb_*`` key).
 MUTABLE_KEYS = frozenset({"output", "log_interval", "checkpoint_interval", "validation_interval",
                           "timeout_minutes", "lr", "warmup_steps", "constant_steps", "min_lr",
-                          "fused_optimizer", "grad_sync", "student_graphs"})
+                          "fused_optimizer", "grad_sync", "student_graphs",
+                          "overlap_students"})
 # Values assumed for keys that older manifests do not carry.
 _OLD_MANIFEST_DEFAULTS = {"training_mode": "sampled", "micro_batch_size": 1}
 
@@ -45,18 +46,27 @@ def cpu_tree(obj):
     return tree_map(lambda leaf: leaf.detach().cpu().clone() if torch.is_tensor(leaf) else leaf, obj)
 
 
+# Host generators saved with a checkpoint: key in the saved dict (the checkpoint layout), getter, setter.
+_HOST_RNGS = (
+    ("python", random.getstate, random.setstate),
+    ("numpy", np.random.get_state, np.random.set_state),
+    ("torch", torch.get_rng_state, lambda saved: torch.set_rng_state(saved.cpu())),
+)
+
+
 def rng_state():
     """Generator states of Python, NumPy, torch CPU and (when initialised) the current CUDA device."""
-    return {"python": random.getstate(), "numpy": np.random.get_state(), "torch": torch.get_rng_state(),
-            "cuda": torch.cuda.get_rng_state() if torch.cuda.is_initialized() else None}
+    saved = {key: get() for key, get, _ in _HOST_RNGS}
+    saved["cuda"] = torch.cuda.get_rng_state() if torch.cuda.is_initialized() else None
+    return saved
 
 
-def restore_rng(state):
-    random.setstate(state["python"])
-    np.random.set_state(state["numpy"])
-    torch.set_rng_state(state["torch"].cpu())
-    if state.get("cuda") is not None and torch.cuda.is_available():
-        torch.cuda.set_rng_state(state["cuda"].cpu())
+def restore_rng(saved):
+    for key, _, put in _HOST_RNGS:
+        put(saved[key])
+    device_state = saved.get("cuda")
+    if device_state is not None and torch.cuda.is_available():
+        torch.cuda.set_rng_state(device_state.cpu())
 
 
 def model_fingerprint(path):
@@ -70,7 +80,7 @@ def model_fingerprint(path):
         record[shard.name] = [info.st_size, info.st_mtime_ns]
     for meta_file in ("config.json", "model.safetensors.index.json"):
         if (root / meta_file).exists():
-            record[meta_file] = digest_file(root / meta_file)
+            record[meta_file] = sha256_of_file(root / meta_file)
     return hashlib.sha256(json.dumps(record, sort_keys=True).encode()).hexdigest()
 
 
@@ -133,8 +143,8 @@ def _manifest(cfg, topo, step, complete, order, base_id):
     import transformers
     return {"format": 2, "training_topology": "parallel_layers_v1", "stage": 0, "step": step,
             "complete": complete, "order": order, "config": cfg, "world": topo.world,
-            "base_fingerprint": base_id, "train_fingerprint": digest_file(cfg["train_manifest"]),
-            "validation_fingerprint": digest_file(cfg["validation_manifest"]),
+            "base_fingerprint": base_id, "train_fingerprint": sha256_of_file(cfg["train_manifest"]),
+            "validation_fingerprint": sha256_of_file(cfg["validation_manifest"]),
             "torch": torch.__version__, "transformers": transformers.__version__}
 
 
@@ -188,7 +198,7 @@ def validate_resume(meta, cfg, topo, base_id, order):
     if meta["order"] != order:
         raise ValueError("Migration layer order changed; start a new run.")
     for split in ("train", "validation"):
-        if meta[f"{split}_fingerprint"] != digest_file(cfg[f"{split}_manifest"]):
+        if meta[f"{split}_fingerprint"] != sha256_of_file(cfg[f"{split}_manifest"]):
             raise ValueError(f"{split} manifest changed")
     changed = _changed_config_keys(meta["config"], cfg, meta["complete"])
     if changed:

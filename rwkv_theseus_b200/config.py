@@ -22,6 +22,9 @@ so a reference ``configs/train.json`` loads unchanged):
   (NVLink peer-memory exchange with sharded AdamW) or ``"nccl"`` (all-reduce,
   then the full update on every rank, as the reference does).
 * ``student_graphs``: replay each fused student micro-step as a CUDA graph.
+* ``overlap_students``: run the students' micro-steps on a CUDA stream of their
+  own, each starting once the teacher forward has produced its layer's capture
+  (beside the rest of the teacher forward).
 """
 import json
 from dataclasses import dataclass
@@ -84,6 +87,7 @@ SCHEMA = {
     "fused_optimizer": Field(True, "bool"),
     "grad_sync": Field("peer", choices=("peer", "nccl")),
     "student_graphs": Field(True, "bool"),
+    "overlap_students": Field(True, "bool"),
 }
 
 DEFAULTS = {name: field.default for name, field in SCHEMA.items()}

@@ -19,18 +19,18 @@ compressed), optionally re-read every tensor bitwise, write the sidecars atomica
 rename the PTH into place. The tensor names, sidecar keys and contract strings are the file format the
 engine reads; they are kept identical to the reference's.
 """
-from collections import Counter, defaultdict
-from dataclasses import dataclass
-from datetime import datetime, timezone
 import hashlib
 import json
 import math
 import os
-from pathlib import Path
 import re
 import shutil
 import tempfile
 import zipfile
+from collections import Counter, defaultdict
+from dataclasses import dataclass
+from datetime import datetime, timezone
+from pathlib import Path
 
 import torch
 from safetensors import safe_open
@@ -52,57 +52,71 @@ def sidecar(path, kind):
 
 
 def atomic_json(path, value):
+    """Write `value` as indented JSON next to `path`, flush it to disk, then rename it over `path`."""
     path = Path(path)
-    fd, tmp = tempfile.mkstemp(prefix=path.name + ".", suffix=".partial", dir=path.parent)
+    text = json.dumps(value, indent=2, ensure_ascii=False) + "\n"
+    fd, partial = tempfile.mkstemp(prefix=path.name + ".", suffix=".partial", dir=path.parent)
     try:
-        with os.fdopen(fd, "w", encoding="utf-8") as f:
-            json.dump(value, f, indent=2, ensure_ascii=False)
-            f.write("\n")
-            f.flush()
-            os.fsync(f.fileno())
-        os.replace(tmp, path)
+        os.write(fd, text.encode("utf-8"))
+        os.fsync(fd)
     finally:
-        if os.path.exists(tmp):
-            os.unlink(tmp)
+        os.close(fd)
+    try:
+        os.replace(partial, path)
+    except BaseException:
+        Path(partial).unlink(missing_ok=True)
+        raise
 
 
 # ---------------------------------------------------------------- HF checkpoint -> PTH
+_GEOMETRY_KEYS = ("hidden_size", "intermediate_size", "num_hidden_layers", "vocab_size", "linear_num_key_heads",
+                  "linear_num_value_heads", "linear_key_head_dim", "linear_value_head_dim", "linear_conv_kernel_dim",
+                  "num_attention_heads", "num_key_value_heads", "head_dim")
+_LAYER_KINDS = {"linear_attention", "full_attention"}
+
+
+def _layer_kinds(text, layers):
+    """``layer_types``, or the pattern ``full_attention_interval`` implies (every n-th block full attention)."""
+    if text.get("layer_types") is not None:
+        return list(text["layer_types"])
+    interval = int(text["full_attention_interval"])
+    if interval < 1:
+        raise ValueError(f"full_attention_interval must be at least 1, got {interval}")
+    return ["full_attention" if index % interval == interval - 1 else "linear_attention" for index in range(layers)]
+
+
 def geometry(config):
     """Validated text-model geometry of a Qwen3.5-family hybrid config.json."""
-    tc = config.get("text_config", config)
-    if config.get("quantization_config") or tc.get("quantization_config"):
-        raise ValueError("Use original BF16/FP16/FP32 weights, not FP8/INT4/quantized weights.")
-    if tc.get("model_type") not in ("qwen3_5_text", "qwen3_5"):
-        raise ValueError(f"Unsupported text architecture: {tc.get('model_type')!r}")
-    keys = ("hidden_size", "intermediate_size", "num_hidden_layers", "vocab_size", "linear_num_key_heads",
-            "linear_num_value_heads", "linear_key_head_dim", "linear_value_head_dim", "linear_conv_kernel_dim",
-            "num_attention_heads", "num_key_value_heads", "head_dim")
-    g = {k: int(tc[k]) for k in keys}
-    if min(g.values()) <= 0:
-        raise ValueError("All model dimensions must be positive.")
-    kinds = tc.get("layer_types")
-    if kinds is None:
-        every = int(tc["full_attention_interval"])
-        if every <= 0:
-            raise ValueError("full_attention_interval must be positive.")
-        kinds = ["full_attention" if (i + 1) % every == 0 else "linear_attention"
-                 for i in range(g["num_hidden_layers"])]
-    if len(kinds) != g["num_hidden_layers"] or not set(kinds) <= {"linear_attention", "full_attention"}:
-        raise ValueError("Invalid layer_types; only GDN + full attention is supported.")
-    if tc.get("hidden_act", "silu") not in ("silu", "swish"):
-        raise ValueError("This schema requires the source SiLU/SwiGLU activations.")
-    if g["linear_num_value_heads"] % g["linear_num_key_heads"]:
-        raise ValueError("GDN value-head count must be divisible by key-head count.")
-    if g["num_attention_heads"] % g["num_key_value_heads"]:
-        raise ValueError("Attention head count must be divisible by KV-head count.")
-    if g["linear_key_head_dim"] != g["linear_value_head_dim"]:
-        raise ValueError("This version targets square RWKV states: Dk must equal Dv.")
-    if tc.get("attn_output_gate", True) is not True:
-        raise ValueError("This version targets Qwen3.5-family gated full attention.")
-    g.update(layer_types=list(kinds), key_dim=g["linear_num_key_heads"] * g["linear_key_head_dim"],
-             value_dim=g["linear_num_value_heads"] * g["linear_value_head_dim"],
-             attention_bias=bool(tc.get("attention_bias", False)),
-             tie_word_embeddings=bool(tc.get("tie_word_embeddings", config.get("tie_word_embeddings", False))))
+    text = config.get("text_config", config)
+    if text.get("quantization_config") or config.get("quantization_config"):
+        raise ValueError("quantized checkpoints (FP8, INT4, ...) are not accepted; convert the BF16/FP16/FP32 release")
+    if text.get("model_type") not in ("qwen3_5", "qwen3_5_text"):
+        raise ValueError(f"model_type {text.get('model_type')!r} is not a Qwen3.5 text model")
+    g = {key: int(text[key]) for key in _GEOMETRY_KEYS}
+    bad = [key for key, value in g.items() if value < 1]
+    if bad:
+        raise ValueError(f"non-positive model dimensions: {bad}")
+    kinds = _layer_kinds(text, g["num_hidden_layers"])
+    rules = (
+        (len(kinds) == g["num_hidden_layers"] and set(kinds) <= _LAYER_KINDS,
+         "layer_types must name one block per layer, each linear_attention (GDN) or full_attention"),
+        (text.get("hidden_act", "silu") in ("silu", "swish"), "the MLP must be SiLU-gated (SwiGLU)"),
+        (g["linear_num_value_heads"] % g["linear_num_key_heads"] == 0,
+         "GDN value heads must be a multiple of its key heads"),
+        (g["num_attention_heads"] % g["num_key_value_heads"] == 0,
+         "attention heads must be a multiple of the KV heads"),
+        (g["linear_key_head_dim"] == g["linear_value_head_dim"],
+         "GDN key and value head sizes must be equal (square recurrent state)"),
+        (text.get("attn_output_gate", True) is True, "full attention must carry the sigmoid output gate"),
+    )
+    for holds, message in rules:
+        if not holds:
+            raise ValueError(message)
+    g["layer_types"] = kinds
+    g["key_dim"] = g["linear_num_key_heads"] * g["linear_key_head_dim"]
+    g["value_dim"] = g["linear_num_value_heads"] * g["linear_value_head_dim"]
+    g["attention_bias"] = bool(text.get("attention_bias", False))
+    g["tie_word_embeddings"] = bool(text.get("tie_word_embeddings", config.get("tie_word_embeddings", False)))
     return g
 
 
@@ -422,11 +436,12 @@ def scan_snapshots(weights, layers, width, depth, head_size=None):
                 shape_of[layer, name] = tuple(part.get_shape())
     sizes, schemas = {}, {}
     for layer in layers:
-        rk = shape_of.get((layer, "r_k"))
+        rk = shape_of.get((layer, "r_k"))  # [heads, head size]: the only tensor that states the head size
         if rk is None:
-            raise ValueError(f"Layer {layer} is incomplete; missing: r_k (needed to infer head size)")
-        if len(rk) != 2 or rk[0] * rk[1] != width or rk[1] not in (64, 128):
-            raise ValueError(f"Invalid layer {layer} r_k shape {rk}; shared WKV supports D64/D128")
+            raise ValueError(f"Layer {layer} is incomplete: it has no r_k, so its head size is unknown")
+        heads_ok = len(rk) == 2 and rk[0] * rk[1] == width
+        if not heads_ok or rk[1] not in (64, 128):
+            raise ValueError(f"Layer {layer}: r_k of shape {tuple(rk)} is not [width / D, D] with D 64 or 128")
         if head_size is not None and rk[1] != head_size:
             raise ValueError(f"Layer {layer} was trained with head_size={rk[1]}, but --head-size={head_size}; "
                              "this option validates, it does not reshape heads")

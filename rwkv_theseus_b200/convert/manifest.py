@@ -13,12 +13,12 @@ Tokenisation runs on a thread pool with a bounded window of in-flight lines; res
 written strictly in input order, so the corpus is byte-identical for any worker count.
 """
 import collections
-import concurrent.futures
 import hashlib
 import json
 import math
 import os
 import shutil
+from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
 import numpy as np
@@ -112,7 +112,7 @@ def tokenize_in_order(lines, tokenizer, vocab_size, workers):
             yield tokenize_line(number, line, tokenizer, vocab_size)
         return
     window = collections.deque()
-    with concurrent.futures.ThreadPoolExecutor(workers, thread_name_prefix="tokenize") as pool:
+    with ThreadPoolExecutor(workers, thread_name_prefix="tokenize") as pool:
         try:
             for number, line in numbered:
                 window.append(pool.submit(tokenize_line, number, line, tokenizer, vocab_size))
@@ -158,13 +158,14 @@ def convert(input_path, tokenizer_path, output_path, *, weight=1.0, name=None, p
         if path.exists():
             raise FileExistsError(f"{what} already exists: {path}")
     weight = float(weight)
-    if not (math.isfinite(weight) and weight > 0):
-        raise ValueError("weight must be positive and finite")
-    workers = int(workers if workers is not None else (os.cpu_count() or 1))
-    if workers < 1:
-        raise ValueError("workers must be >= 1")
-    if progress_interval < 0:
-        raise ValueError("progress_interval must be >= 0")
+    workers = int(os.cpu_count() or 1) if workers is None else int(workers)
+    problems = [text for bad, text in ((not math.isfinite(weight) or weight <= 0, f"source weight {weight} is not a "
+                                        "positive finite number"),
+                                       (workers < 1, f"need at least one tokenizer worker, got {workers}"),
+                                       (progress_interval < 0, f"negative progress_interval {progress_interval}"))
+                if bad]
+    if problems:
+        raise ValueError("; ".join(problems))
     if tokenizer is None:
         from transformers import AutoTokenizer
         tokenizer = AutoTokenizer.from_pretrained(tok_dir, local_files_only=True)

@@ -33,16 +33,17 @@ from pathlib import Path
 import numpy as np
 import torch
 
-SAMPLER_VERSION = 2
-
-
-def digest_file(path):
+def sha256_of_file(path):
     """SHA-256 of a file's bytes, read in 8 MiB blocks."""
     hasher = hashlib.sha256()
     with open(path, "rb") as handle:
         for block in iter(lambda: handle.read(8 << 20), b""):
             hasher.update(block)
     return hasher.hexdigest()
+
+
+# Version of the window-sampling steps, stored in every reader cursor (a cursor of another version is refused).
+SAMPLER_VERSION = 2
 
 
 class Corpus:
@@ -55,7 +56,7 @@ class Corpus:
             raise ValueError("Unsupported token manifest")
         if not self.spec["sources"]:
             raise ValueError("Manifest must contain at least one source")
-        self.fingerprint = digest_file(self.path)
+        self.fingerprint = sha256_of_file(self.path)
         self.tokens, self.offsets, weights = [], [], []
         for entry in self.spec["sources"]:
             tokens = np.memmap(self.path.parent / entry["tokens"], dtype="<u4", mode="r")
@@ -181,9 +182,11 @@ class EpochTokenStream(TokenStream):
         self.windows = table[self.pair_id::self.pairs].copy()
         self.consumed_tokens = 0
 
+    MODE = "epoch_v1"  # reader_mode recorded in (and required of) a checkpoint cursor
+
     @property
     def exhausted(self):
-        return self.window >= len(self.windows)
+        return not self.window < len(self.windows)
 
     def _draw_window(self):
         if self.exhausted:
@@ -191,18 +194,21 @@ class EpochTokenStream(TokenStream):
         return self.corpus.span(*self.windows[self.window])
 
     def next(self):
-        if self.exhausted:
-            return None
-        batch = super().next()
-        self.consumed_tokens += batch["ids"].numel()
+        """The next chunk of this rank's share, or None once every window was read."""
+        batch = None if self.exhausted else super().next()
+        if batch is not None:
+            self.consumed_tokens += batch["ids"].numel()
         return batch
 
     def state_dict(self):
-        return super().state_dict() | {"reader_mode": "epoch_v1", "consumed_tokens": self.consumed_tokens}
+        cursor = super().state_dict()
+        cursor.update(reader_mode=self.MODE, consumed_tokens=self.consumed_tokens)
+        return cursor
 
     def load_state_dict(self, state):
-        if state.get("reader_mode") != "epoch_v1":
-            raise ValueError("A sampled reader checkpoint cannot resume an exhaustive epoch")
+        mode = state.get("reader_mode")
+        if mode != self.MODE:
+            raise ValueError(f"Reader mode {mode!r} cannot resume an exhaustive epoch ({self.MODE})")
         super().load_state_dict(state)
         self.consumed_tokens = state["consumed_tokens"]
 
@@ -225,9 +231,9 @@ class BatchedEpochTokenStream(EpochTokenStream):
     and ends at the same positions, so caches and recurrent states reset per group)."""
 
     def __init__(self, *args, micro_batch_size, **kwargs):
-        if micro_batch_size < 2:
-            raise ValueError("Batched reader requires micro_batch_size >= 2")
-        self.micro_batch_size = micro_batch_size
+        self.micro_batch_size = int(micro_batch_size)
+        if self.micro_batch_size <= 1:
+            raise ValueError(f"lane packing needs micro_batch_size >= 2, got {micro_batch_size}")
         super().__init__(*args, **kwargs)
         self.groups = pack_lanes(self.windows, micro_batch_size)
         self.rank_chunks = [self._packed_chunks(self._table[rank::self.pairs]) for rank in range(self.pairs)]
@@ -241,9 +247,10 @@ class BatchedEpochTokenStream(EpochTokenStream):
 
     @property
     def exhausted(self):
-        return self.group >= len(self.groups)
+        return not self.group < len(self.groups)
 
     def next(self):
+        """The next chunk of the current lane group ([lanes, tokens]), or None once every group was read."""
         if self.exhausted:
             return None
         rows = self.groups[self.group]

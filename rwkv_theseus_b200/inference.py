@@ -22,7 +22,7 @@ import torch
 from safetensors.torch import load_file
 
 from .checkpoint import model_fingerprint, split_delta
-from .data import digest_file
+from .data import sha256_of_file
 from .models.hf_io import build_empty, finalize, load_model, save_model, shard_files
 from .models.qwen35 import HybridConfig
 from .models.runner import Runner, install
@@ -46,42 +46,57 @@ def save_export(model, path, cfg, order, base_id, checkpoint=None):
             "lora_rank": cfg.get("lora_rank"), "gate_lora_rank": cfg.get("gate_lora_rank"),
             "base_fingerprint": base_id, "loader": "rwkv_theseus_b200.inference.load_export",
             "state_layout": "B,H,value,key",
-            "migration_fingerprint": digest_file(Path(checkpoint) / "migrated.safetensors") if checkpoint else None}
+            "migration_fingerprint": sha256_of_file(Path(checkpoint) / "migrated.safetensors") if checkpoint else None}
     (temp / "theseus.json").write_text(json.dumps(meta, indent=2))
     os.replace(temp, path)
 
 
-def load_export(path, device="cuda", base_model=None):
-    path = Path(path)
-    meta = json.loads((path / "theseus.json").read_text())
-    if meta["format"] == 2:
-        cfg = HybridConfig.from_pretrained(path)
-        model = build_empty(cfg, "meta", torch.bfloat16)
-        for layer in meta["layers"]:
-            install(model, layer, meta)
-        expected = set(model.state_dict())
-        seen = set()
-        for shard in shard_files(path):
-            state = load_file(str(path / shard), device=str(device))
-            if seen.intersection(state) or set(state) - expected:
-                raise ValueError("Invalid converted checkpoint keys")
-            model.load_state_dict(state, strict=False, assign=True)
-            seen.update(state)
-        if cfg.tie_word_embeddings and "lm_head.weight" not in seen:
-            model.lm_head.weight = model.model.embed_tokens.weight
-            seen.add("lm_head.weight")
-        if expected != seen:
-            raise ValueError(f"Missing converted weights: {sorted(expected - seen)[:8]}")
-        finalize(model, device)
-        return Runner(model)
-    base = base_model or meta["base_model"]
-    if model_fingerprint(base) != meta["base_fingerprint"]:
+def _load_full_export(root, meta, device):
+    """Format 2: a complete converted model directory (config + bf16 shards, migrated layers named
+    ``model.layers.<i>.self_attn.core.*``). Every expected tensor must come from exactly one shard."""
+    cfg = HybridConfig.from_pretrained(root)
+    model = build_empty(cfg, "meta", torch.bfloat16)
+    for layer in meta["layers"]:
+        install(model, layer, meta)
+    wanted = set(model.state_dict())
+    loaded = set()
+    for shard in shard_files(root):
+        tensors = load_file(str(root / shard), device=str(device))
+        names = set(tensors)
+        if names - wanted or names & loaded:
+            raise ValueError(f"Invalid converted checkpoint keys in {shard}")
+        model.load_state_dict(tensors, strict=False, assign=True)
+        loaded |= names
+    if cfg.tie_word_embeddings and "lm_head.weight" not in loaded:
+        model.lm_head.weight = model.model.embed_tokens.weight
+        loaded.add("lm_head.weight")
+    missing = sorted(wanted - loaded)
+    if missing:
+        raise ValueError(f"Missing converted weights: {missing[:8]}")
+    finalize(model, device)
+    return model
+
+
+def _load_delta_export(root, meta, device, base_model):
+    """Format 1: the migrated TimeMix tensors only, installed into the original base model, whose fingerprint
+    must match the one recorded at export."""
+    base = base_model if base_model else meta["base_model"]
+    if meta["base_fingerprint"] != model_fingerprint(base):
         raise ValueError("Export base fingerprint mismatch")
     model = load_model(base, device)
-    delta = split_delta(load_file(str(path / "migrated.safetensors")))
+    per_layer = split_delta(load_file(str(root / "migrated.safetensors")))
     for layer in meta["layers"]:
-        install(model, layer, meta, delta[layer])
-    return Runner(model)
+        install(model, layer, meta, per_layer[layer])
+    return model
+
+
+def load_export(path, device="cuda", base_model=None):
+    """A ``Runner`` over the assembled model of an export directory (format 2, or the delta-only format 1)."""
+    root = Path(path)
+    meta = json.loads((root / "theseus.json").read_text())
+    if meta["format"] == 2:
+        return Runner(_load_full_export(root, meta, device))
+    return Runner(_load_delta_export(root, meta, device, base_model))
 
 
 @torch.no_grad()

@@ -6,6 +6,8 @@ the fused loss kernel computes the same three sums in one pass (and the NMSE
 gradient in the same kernel, see ``ops.loss``); this module is the
 device-agnostic definition used on CPU and as the test oracle.
 """
+import math
+
 import torch
 from torch.nn import functional as F
 
@@ -19,15 +21,19 @@ def statistics(prediction, target, epsilon=1e-6, mask=None):
 
 
 def loss_sum(stats, cosine_weight):
-    return stats[0] + cosine_weight * (stats[2] - stats[1])
+    """Training objective of summed statistics: sum NMSE + w * (token count - sum cosine)."""
+    nmse_total, cos_total, count = stats[0], stats[1], stats[2]
+    return nmse_total + cosine_weight * (count - cos_total)
 
 
 def metrics(stats):
-    nmse, cosine, count = stats.double().cpu().tolist()
-    if count <= 0:
+    """Per-token means of summed statistics: NMSE, its root (RRMS), cosine, and the token count."""
+    totals = [float(v) for v in stats.detach().double().cpu()]
+    tokens = totals[2]
+    if not tokens > 0:
         raise ValueError("No valid validation tokens")
-    mean = nmse / count
-    return {"nmse": mean, "rrms": mean ** .5, "cosine": cosine / count, "tokens": int(count)}
+    per_token = totals[0] / tokens
+    return {"nmse": per_token, "rrms": math.sqrt(per_token), "cosine": totals[1] / tokens, "tokens": int(tokens)}
 
 
 def kl_sum(student_logits, teacher_logits):

@@ -107,10 +107,15 @@ def install(model, layer, options, weights=None, trainable=False, retain_teacher
 
 
 class Capture:
-    """Records, detached, what one attention module receives (``x``) and returns (``y``) on each forward."""
+    """Records, detached, what one attention module receives (``x``) and returns (``y``) on each forward.
+
+    With ``record_events`` set, a CUDA event is recorded on the forward's stream right after the module's work
+    (``ready``): work on another stream that reads ``x`` and ``y`` waits on it instead of on the whole forward."""
 
     def __init__(self, attention):
         self.x = self.y = None
+        self.ready = None
+        self.record_events = False
         self._handles = [attention.register_forward_pre_hook(self._take_input, with_kwargs=True),
                          attention.register_forward_hook(self._take_output)]
 
@@ -119,6 +124,9 @@ class Capture:
 
     def _take_output(self, module, args, output):
         self.y = (output[0] if isinstance(output, tuple) else output).detach()
+        if self.record_events and self.y.is_cuda:
+            self.ready = torch.cuda.Event()
+            self.ready.record()
 
     def close(self):
         for handle in self._handles:

@@ -127,17 +127,22 @@ class Topology:
         return group
 
     def synchronize(self):
-        if self.device.type == "cuda":
-            torch.cuda.synchronize(self.device)
+        """Wait for this rank's device work (nothing to wait for on CPU ranks)."""
+        if self.device.type != "cuda":
+            return
+        torch.cuda.synchronize(self.device)
 
     def barrier(self):
+        """Device work finished here, then every rank of the Gloo world meets."""
         self.synchronize()
         dist.barrier()
 
     def close(self):
+        """Collective shutdown: the peer exchange's mappings are released before the process groups."""
         self.barrier()
-        exchange, self._grad_sync = self._grad_sync, None
-        if exchange is not None:
+        exchange = self._grad_sync
+        self._grad_sync = None
+        if exchange:
             exchange.close()
         dist.destroy_process_group()
 
@@ -149,10 +154,12 @@ class Topology:
             raise ValueError(f"Ranks disagree on {label}: {digests}")
 
     def broadcast_object(self, value, source=None):
+        """`source`'s (default: the leader's) picklable `value` on every rank."""
         self.synchronize()
-        box = [value]
-        dist.broadcast_object_list(box, src=self.leader if source is None else source)
-        return box[0]
+        holder = [value if self.rank == (self.leader if source is None else source) else None]
+        dist.broadcast_object_list(holder, src=self.leader if source is None else source)
+        (received,) = holder
+        return received
 
     def broadcast_weights(self, state):
         """The leader's tensors on every rank (CPU), as one packed byte buffer, followed by a digest check."""

@@ -55,12 +55,14 @@ class RunIdentity:
 
 
 class Tracker:
-    def __init__(self):
-        self.run = None
-        self.cfg = None
+    """W&B run of the leader rank; every other rank (and ``wandb_mode: disabled``) logs nothing."""
+
+    run = None
+    cfg = None
 
     def start(self, cfg, topo, resume=False):
-        if topo.rank != topo.leader or cfg["wandb_mode"] == "disabled":
+        logging_rank = topo.rank == topo.leader and cfg["wandb_mode"] != "disabled"
+        if not logging_rank:
             return
         import wandb
         self.cfg = cfg

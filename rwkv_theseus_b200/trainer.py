@@ -28,6 +28,7 @@ import gc
 import json
 import os
 import random
+from contextlib import nullcontext
 from pathlib import Path
 
 import numpy as np
@@ -35,7 +36,7 @@ import torch
 
 from .checkpoint import cpu_tree, model_fingerprint, read_checkpoint, restore_rng, save_checkpoint, validate_resume
 from .config import steps_for
-from .data import digest_file, reader_for
+from .data import sha256_of_file, reader_for
 from .losses import metrics
 from .models.hf_io import load_model
 from .models.runner import Capture, Runner, install, migration_order, state_to_device
@@ -116,6 +117,17 @@ class StepEngine:
         if self.device.type == "cuda":
             for student in students.values():
                 student.overlap_update = True
+        # On CUDA (config ``overlap_students``) the micro-steps run on a stream of their own: student L waits only
+        # for the event its capture records after layer L's attention, so it runs beside the rest of the teacher
+        # forward and fills the SMs that the teacher's latency-bound kernels (GDN state pass, attention tail) leave
+        # idle. Its GEMMs use the second stream-K workspace (lane 1); parallel split-K runs as stream-K while two
+        # lanes can overlap. The step ends with the compute stream waiting for the student stream.
+        self.student_stream = None
+        if self.device.type == "cuda" and cfg.get("overlap_students", True):
+            self.student_stream = torch.cuda.Stream(self.device)
+            native().gemm_set_concurrent(True)
+            for capture in captures.values():
+                capture.record_events = True
 
     def _to_device(self, ids):
         """Token ids to the device through two alternating pinned buffers (asynchronous copy). A buffer is
@@ -161,17 +173,41 @@ class StepEngine:
             for layer in self.order:
                 student, capture = self.students[layer], self.captures[layer]
                 if batch is not None:
-                    with profiler.phase(f"student_{layer:02d}"):
-                        student.micro_step(capture.x, capture.y)
+                    self._micro_step(student, capture, f"student_{layer:02d}")
                     capture.x = capture.y = None
                 if updating:
                     if self.defer_updates:
                         self._deferred.append(student)
-                    else:
-                        with profiler.phase(f"update_{layer:02d}"):
+                    else:  # right after the micro-step, on the stream it ran on
+                        with self._on_student_stream(), profiler.phase(f"update_{layer:02d}"):
                             student.reduce()
                             student.update()
+            if self.student_stream is not None and batch is not None:
+                torch.cuda.current_stream(self.device).wait_stream(self.student_stream)
         return {layer: student.report for layer, student in self.students.items()}
+
+    def _on_student_stream(self):
+        return torch.cuda.stream(self.student_stream) if self.student_stream is not None else nullcontext()
+
+    def _micro_step(self, student, capture, phase):
+        stream = self.student_stream
+        if stream is None or capture.ready is None:
+            with self.profiler.phase(phase):
+                student.micro_step(capture.x, capture.y)
+            return
+        x, y = capture.x, capture.y
+        stream.wait_event(capture.ready)
+        carried = () if student.state is None else tuple(student.state.values())
+        for tensor in (x, y, *carried):  # allocated on other streams: not reused before the student stream is done
+            tensor.record_stream(stream)
+        ext = native()
+        with torch.cuda.stream(stream), self.profiler.phase(phase):
+            ext.gemm_set_lane(1)
+            try:
+                student.micro_step(x, y)
+            finally:
+                ext.gemm_set_lane(0)
+        capture.ready = None
 
     def join_updates(self):
         """Issue any deferred updates and make the current stream wait for every layer's update (local AdamW or
@@ -328,7 +364,7 @@ class MigrationJob:
         for manifest, spec in self._manifests():
             for source in spec["sources"]:
                 for field in ("tokens", "offsets"):
-                    if digest_file(Path(manifest).parent / source[field]) != source[f"{field}_sha256"]:
+                    if sha256_of_file(Path(manifest).parent / source[field]) != source[f"{field}_sha256"]:
                         raise ValueError(f"Data content changed: {source[field]}")
 
     def _check_data_fits_model(self):
@@ -337,7 +373,7 @@ class MigrationJob:
                 raise ValueError("Dataset vocabulary exceeds model embedding size")
             for name, expected in spec.get("tokenizer_files", {}).items():
                 found = Path(self.cfg["model"]) / name
-                if not found.exists() or digest_file(found) != expected:
+                if not found.exists() or sha256_of_file(found) != expected:
                     raise ValueError(f"Dataset/model tokenizer differs: {name}")
 
     def _open(self):
@@ -373,7 +409,7 @@ class MigrationJob:
         if not (self.meta["complete"] and exported.exists()):
             return False
         record = json.loads(exported.read_text())
-        if (record.get("migration_fingerprint") != digest_file(self.checkpoint / "migrated.safetensors")
+        if (record.get("migration_fingerprint") != sha256_of_file(self.checkpoint / "migrated.safetensors")
                 or record.get("base_fingerprint") != self.base_id):
             raise ValueError("Existing converted model differs from resumed checkpoint; choose a new output")
         return True

@@ -6,7 +6,7 @@ import numpy as np
 import torch
 
 from rwkv_theseus_b200.config import DEFAULTS
-from rwkv_theseus_b200.data import digest_file
+from rwkv_theseus_b200.data import sha256_of_file
 from rwkv_theseus_b200.models.hf_io import save_model
 from rwkv_theseus_b200.models.qwen35 import HybridConfig, HybridForCausalLM
 
@@ -44,22 +44,27 @@ def write_dataset(path, vocab=64):
     np.save(path / "offsets.npy", np.array([0, 11, 28, 37], dtype=np.int64))
     manifest = {"format": 1, "vocab_size": vocab, "sources": [{
         "tokens": "tokens.bin", "offsets": "offsets.npy", "weight": 1,
-        "tokens_sha256": digest_file(path / "tokens.bin"), "offsets_sha256": digest_file(path / "offsets.npy")}]}
+        "tokens_sha256": sha256_of_file(path / "tokens.bin"), "offsets_sha256": sha256_of_file(path / "offsets.npy")}]}
     (path / "manifest.json").write_text(json.dumps(manifest))
     return path / "manifest.json"
 
 
+# Run shape of the end-to-end CPU runs: 3-token chunks in 9-token windows, 3 steps per stage with 2 warm-up
+# steps, two micro-steps per update, 2 validation chunks; logging every step, no periodic validation or checkpoints.
+_RUN_SHAPE = {"chunk_tokens": 3, "context_tokens": 9, "stage_steps": 3, "warmup_steps": 2, "grad_accum_steps": 2,
+              "validation_chunks": 2}
+_CADENCE = {"log_interval": 1, "validation_interval": 0, "checkpoint_interval": 0}
+_STUDENT = {"head_size": 8, "backend": "reference", "distributed_backend": "gloo", "training_mode": "sampled",
+            "original_teacher_kl": True, "debug_input": True}
+
+
 def make_config(tmp_path, stages):
+    """A training config over a saved tiny teacher with `stages` attention blocks and two tiny token datasets."""
     save_tiny(tmp_path / "base", depth=stages * 2)
-    cfg = DEFAULTS | {"training_mode": "sampled", "model": str(tmp_path / "base"),
-                      "train_manifest": str(write_dataset(tmp_path / "train")),
-                      "validation_manifest": str(write_dataset(tmp_path / "val")),
-                      "output": str(tmp_path / "full"), "expected_attention_layers": stages,
-                      "head_size": 8, "backend": "reference", "distributed_backend": "gloo",
-                      "chunk_tokens": 3, "context_tokens": 9, "stage_steps": 3,
-                      "warmup_steps": 2, "grad_accum_steps": 2, "validation_chunks": 2,
-                      "validation_interval": 0, "checkpoint_interval": 0, "log_interval": 1,
-                      "original_teacher_kl": True, "debug_input": True}
+    paths = {"model": str(tmp_path / "base"), "output": str(tmp_path / "full"),
+             "train_manifest": str(write_dataset(tmp_path / "train")),
+             "validation_manifest": str(write_dataset(tmp_path / "val"))}
+    cfg = {**DEFAULTS, **paths, **_STUDENT, **_RUN_SHAPE, **_CADENCE, "expected_attention_layers": stages}
     path = tmp_path / "config.json"
     path.write_text(json.dumps(cfg))
     return cfg, path

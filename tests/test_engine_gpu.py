@@ -45,11 +45,12 @@ class Reader:
         return batch
 
 
-def engine(defer, chunk, steps):
+def engine(defer, chunk, steps, overlap=True):
     cfg_model = smoke_config()
     model = random_model(cfg_model, torch.device("cuda"), seed=3)
     order = migration_order(model, 2)
-    cfg = DEFAULTS | {"head_size": 64, "backend": "cuda", "lr": 1e-3, "warmup_steps": 0, "chunk_tokens": chunk}
+    cfg = DEFAULTS | {"head_size": 64, "backend": "cuda", "lr": 1e-3, "warmup_steps": 0, "chunk_tokens": chunk,
+                      "overlap_students": overlap}
     students, captures = {}, {}
     for i, layer in enumerate(order):
         torch.manual_seed(cfg["seed"] + i)
@@ -93,3 +94,46 @@ def test_deferred_updates_match_immediate(chunk):
     for eng in (deferred, immediate):
         for capture in eng.captures.values():
             capture.close()
+    from rwkv_theseus_b200.ops import native
+    native().gemm_set_concurrent(False)  # process-wide switch the overlapping engine turned on
+
+
+def _train(eng, reader, steps):
+    pending, logged = None, []
+    for _ in range(steps):
+        reports = eng.step(reader)
+        if pending is not None:
+            logged.append(pending.result())
+        pending = eng.read_metrics_async(reports)
+    logged.append(pending.result())
+    eng.join_updates()
+    torch.cuda.synchronize()
+    return logged
+
+
+@cuda
+@pytest.mark.parametrize("chunk", [128, 96])
+def test_students_beside_teacher_match_serial_schedule(chunk):
+    """Students on their own stream (each waiting only for its layer's capture event) train exactly like students
+    issued after the whole teacher forward on the compute stream."""
+    from rwkv_theseus_b200.ops import native
+    steps = 4
+    try:
+        runs = {}
+        for overlap in (True, False):
+            eng, reader = engine(True, chunk, steps, overlap=overlap)
+            assert (eng.student_stream is not None) == overlap
+            runs[overlap] = (eng, _train(eng, reader, steps))
+        (side, log_s), (serial, log_c) = runs[True], runs[False]
+        for layer in side.order:
+            a, b = side.students[layer], serial.students[layer]
+            torch.testing.assert_close(a.flat.param, b.flat.param, rtol=1e-5, atol=1e-6)
+        for ms, mc in zip(log_s, log_c):
+            for key in ms:
+                assert ms[key]["tokens"] == mc[key]["tokens"]
+                assert abs(ms[key]["nmse"] - mc[key]["nmse"]) <= 1e-3 * abs(mc[key]["nmse"]) + 1e-6
+        for eng, _ in runs.values():
+            for capture in eng.captures.values():
+                capture.close()
+    finally:
+        native().gemm_set_concurrent(False)  # process-wide switch the overlapping engine turned on

@@ -38,7 +38,8 @@ def _launch(mode, nproc=None):
     cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            f"--nproc-per-node={nproc}", "--master-addr=127.0.0.1", f"--master-port={_port()}", __file__, mode]
     out = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=300)
-    assert out.returncode == 0, out.stdout[-4000:] + out.stderr[-4000:]
+    failed = "\n".join(line for line in out.stdout.splitlines() if line.startswith("RANK_FAILED"))
+    assert out.returncode == 0, failed + "\n" + out.stdout[-3000:] + out.stderr[-3000:]
     return out.stdout
 
 
@@ -66,6 +67,20 @@ def _student(topo, grad_sync, weights=None):
     torch.manual_seed(0)
     return Student(types.SimpleNamespace(hidden_size=256, num_hidden_layers=8), 3, cfg, topo, weights=weights,
                    total_steps=10)
+
+
+def _close_params(peer, nccl, steps, label, lr=1e-3):
+    """Peer exchange against the NCCL all-reduce path. The two sum the ranks' gradients in different orders, so
+    with more than two ranks an element whose gradients nearly cancel can take a different Adam step (its
+    normalised moment m / sqrt(v) depends on the rounding of a tiny sum). Every element is within the largest
+    possible drift (2 lr per update: each Adam step is below lr in size) and almost all (99.9%) within fp32
+    rounding of each other; with two ranks the sums are identical and so is every element."""
+    diff = (peer - nccl).abs()
+    tight = diff <= 1e-7 + 1e-5 * nccl.abs()
+    assert diff.max().item() <= 2 * lr * steps, (label, diff.max().item())
+    assert tight.float().mean().item() >= 0.999, (label, 1 - tight.float().mean().item())
+    if torch.distributed.get_world_size() <= 2:
+        assert bool(tight.all()), (label, diff.max().item())
 
 
 def _match(topo):
@@ -97,21 +112,25 @@ def _match(topo):
         assert torch.equal(peer.fused.shadow, nccl.fused.shadow) or \
             (peer.fused.shadow.float() - nccl.fused.shadow.float()).abs().max() <= 1e-2 * nccl.flat.param.abs().max()
         tail = slice(peer.decay_numel, None)  # fp32 non-decay parameters are gathered every update
-        assert torch.allclose(peer.flat.param[tail], nccl.flat.param[tail], rtol=1e-5, atol=1e-7), step
+        _close_params(peer.flat.param[tail], nccl.flat.param[tail], step + 1, f"non-decay step {step}")
         if step == 1:
             peer.sync_state()  # gather the sharded fp32 masters and moments mid-run; training continues
             torch.cuda.synchronize()
-        assert torch.allclose(peer.flat.param, nccl.flat.param, rtol=1e-5, atol=1e-7) or step != 1, step
+            _close_params(peer.flat.param, nccl.flat.param, step + 1, f"all parameters step {step}")
         assert torch.equal(peer.fused.shadow, peer.flat.param.to(torch.bfloat16)) or step != 1, step
         assert torch.allclose(peer.report, nccl.report, rtol=1e-5), (step, peer.report, nccl.report)
         assert not peer.stats.any(), step
     topo.check_grad_sync()
     peer.sync_state()
     torch.cuda.synchronize()
-    assert torch.allclose(peer.flat.param, nccl.flat.param, rtol=1e-5, atol=1e-7)
+    _close_params(peer.flat.param, nccl.flat.param, 4, "all parameters, end")
     assert torch.equal(peer.fused.shadow, peer.flat.param.to(torch.bfloat16))
-    assert torch.allclose(peer.flat.exp_avg, nccl.flat.exp_avg, rtol=1e-5, atol=1e-9)
-    assert torch.allclose(peer.flat.exp_avg_sq, nccl.flat.exp_avg_sq, rtol=1e-5, atol=1e-12)
+    for name, atol in (("exp_avg", 1e-9), ("exp_avg_sq", 1e-12)):  # moments: same rule as the parameters
+        mine, theirs = getattr(peer.flat, name), getattr(nccl.flat, name)
+        diff = (mine - theirs).abs()
+        tight = diff <= atol + 1e-5 * theirs.abs()
+        assert diff.max().item() <= 1e-3 * theirs.abs().max().item(), (name, diff.max().item())
+        assert tight.float().mean().item() >= 0.999 and (topo.world > 2 or bool(tight.all())), name
     everyone = [torch.empty_like(peer.flat.param) for _ in range(topo.world)]
     torch.distributed.all_gather(everyone, peer.flat.param, group=topo.student_group)
     assert all(torch.equal(everyone[0], e) for e in everyone)
@@ -196,6 +215,9 @@ def main(mode):
     topo = Topology("nccl", timeout_minutes=2)
     try:
         {"match": _match, "odd": _odd, "timeout": _timeout}[mode](topo)
+    except BaseException as err:  # one line per failing rank, which the launcher puts first in its report
+        print(f"RANK_FAILED rank {topo.rank}: {type(err).__name__}: {err!r}"[:600], flush=True)
+        raise
     finally:
         topo.close()
 

@@ -8,7 +8,7 @@ import numpy as np
 import pytest
 
 from jsonl_to_manifest import convert, validate_messages
-from rwkv_theseus_b200.data import EpochTokenStream, digest_file
+from rwkv_theseus_b200.data import EpochTokenStream, sha256_of_file
 
 
 class LengthTokenizer:
@@ -70,8 +70,8 @@ def test_corpus_offsets_and_manifest_fields(tmp_path):
     source = spec["sources"][0]
     assert spec["format"] == 1 and spec["vocab_size"] == 300
     assert source["name"] == "mix" and source["documents"] == 3 and source["token_count"] == sum(lengths)
-    assert spec["tokenizer_files"] == {"tokenizer_config.json": digest_file(model / "tokenizer_config.json")}
-    assert source["tokens_sha256"] == digest_file(manifest.parent / source["tokens"])
+    assert spec["tokenizer_files"] == {"tokenizer_config.json": sha256_of_file(model / "tokenizer_config.json")}
+    assert source["tokens_sha256"] == sha256_of_file(manifest.parent / source["tokens"])
     np.testing.assert_array_equal(np.load(manifest.parent / source["offsets"]), np.cumsum([0] + lengths))
     np.testing.assert_array_equal(np.fromfile(manifest.parent / source["tokens"], dtype="<u4"),
                                   np.concatenate(expected))

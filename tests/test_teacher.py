@@ -54,77 +54,106 @@ def test_hf_layout_roundtrip_and_strict_loader(tmp_path):
         torch.testing.assert_close(a, b)
 
 
-def test_cached_chunks_and_all_replaced():
-    model = tiny_model()
-    runner = Runner(model)
-    ids = torch.randint(0, 64, (1, 11))
-    full = runner.forward(ids)
+def _split_forward(runner, ids, cuts):
     runner.reset()
-    parts = [runner.forward(ids[:, :4]), runner.forward(ids[:, 4:7]), runner.forward(ids[:, 7:])]
-    torch.testing.assert_close(torch.cat(parts, 1), full, atol=.03, rtol=.03)
-    for layer in [3, 1]:
+    outs, start = [], 0
+    for stop in (*cuts, ids.shape[1]):
+        outs.append(runner.forward(ids[:, start:stop]))
+        start = stop
+    return torch.cat(outs, 1)
+
+
+@pytest.mark.parametrize("cuts", [(3,), (2, 9), (1, 5, 6)])
+def test_runner_chunks_match_one_pass_before_and_after_replacement(cuts):
+    """The runner's cache carries attention KV, GDN conv windows and delta-rule states (and, once installed,
+    TimeMix states) so that any split of a sequence gives the one-pass hidden states."""
+    torch.manual_seed(len(cuts))
+    model = tiny_model(seed=len(cuts))
+    runner = Runner(model)
+    ids = torch.randint(0, 64, (2, 12))
+    runner.reset()
+    one_pass = runner.forward(ids)
+    torch.testing.assert_close(_split_forward(runner, ids, cuts), one_pass, atol=.03, rtol=.03)
+    for layer in migration_order(model, expected=2):
         install(model, layer, {"head_size": 8, "backend": "reference"})
     runner.reset()
-    full = runner.forward(ids)
-    runner.reset()
-    pieces = [runner.forward(ids[:, :4]), runner.forward(ids[:, 4:])]
-    torch.testing.assert_close(torch.cat(pieces, 1), full, atol=.03, rtol=.03)
-    assert runner.cache.cursor == 11
+    replaced = runner.forward(ids)
+    torch.testing.assert_close(_split_forward(runner, ids, cuts), replaced, atol=.03, rtol=.03)
+    assert runner.cache.cursor == ids.shape[1]
 
 
-def test_truncated_teacher_matches_full_boundary_across_chunks():
-    full_model, short_model = tiny_model(), tiny_model()
-    full_runner, short_runner = Runner(full_model), Runner(short_model)
-    full_capture = Capture(full_model.model.layers[1].self_attn)
-    short_capture = Capture(short_model.model.layers[1].self_attn)
+def test_forward_through_layer_captures_the_same_boundary():
+    """A forward that stops after the last migrated block captures what a full forward captures at that block,
+    chunk after chunk, and advances the cache cursor the same way."""
+    reference_model, short_model = tiny_model(seed=3), tiny_model(seed=3)
+    runners = Runner(reference_model), Runner(short_model)
+    captures = [Capture(m.model.layers[1].self_attn) for m in (reference_model, short_model)]
     try:
-        for ids in (torch.randint(0, 64, (1, 6)), torch.randint(0, 64, (1, 3))):
-            full_runner.forward(ids)
-            short_runner.forward(ids, through_layer=1)
-            torch.testing.assert_close(short_capture.x, full_capture.x, atol=.001, rtol=.001)
-            torch.testing.assert_close(short_capture.y, full_capture.y, atol=.001, rtol=.001)
-        assert full_runner.cache.cursor == short_runner.cache.cursor == 9
+        for length in (5, 1, 4):
+            ids = torch.randint(0, 64, (1, length))
+            runners[0].forward(ids)
+            runners[1].forward(ids, through_layer=1)
+            for attr in ("x", "y"):
+                torch.testing.assert_close(getattr(captures[1], attr), getattr(captures[0], attr),
+                                           atol=.001, rtol=.001)
+        assert runners[0].cache.cursor == runners[1].cache.cursor == 10
     finally:
-        full_capture.close()
-        short_capture.close()
+        for capture in captures:
+            capture.close()
 
 
-def test_adapter_only_current_layer_has_grad_and_runner_restore():
-    teacher, student = tiny_model(), tiny_model()
-    tr, sr = Runner(teacher), Runner(student)
-    adapter = install(student, 3, {"head_size": 8, "backend": "reference"}, trainable=True)
+def test_trainable_adapter_keeps_gradients_in_its_layer():
+    """Only the installed TimeMix of the trained layer receives gradients from its distillation loss; the rest
+    of the (frozen) model stays gradient-free."""
+    teacher, student = tiny_model(seed=4), tiny_model(seed=4)
+    teacher_runner, student_runner = Runner(teacher), Runner(student)
+    adapter = install(student, 1, {"head_size": 8, "backend": "reference"}, trainable=True)
     adapter.__dict__["train_call"] = adapter.core
-    capture = Capture(teacher.model.layers[3].self_attn)
-    ids = torch.randint(0, 64, (1, 6))
-    tr.forward(ids)
-    adapter.teacher_input = capture.x
-    adapter.debug_input = True
-    sr.forward(ids)
-    (adapter.prediction.float() - capture.y.float()).square().mean().backward()
-    grads = [n for n, p in student.named_parameters() if p.grad is not None]
-    assert grads and all(n.startswith("model.layers.3.self_attn.core.") for n in grads)
-    adapter.teacher_input = adapter.prediction = None
-    state = cpu_tree(sr.state_dict())
-    more = torch.randint(0, 64, (1, 3))
-    expected = sr.forward(more)
-    sr.load_state_dict(state)
-    torch.testing.assert_close(sr.forward(more), expected, atol=.001, rtol=.001)
-    capture.close()
+    capture = Capture(teacher.model.layers[1].self_attn)
+    try:
+        ids = torch.randint(0, 64, (1, 7))
+        teacher_runner.forward(ids)
+        adapter.teacher_input, adapter.debug_input = capture.x, True
+        student_runner.forward(ids)
+        loss = (adapter.prediction.float() - capture.y.float()).abs().mean()
+        loss.backward()
+        with_grad = {name for name, p in student.named_parameters() if p.grad is not None}
+        assert with_grad
+        assert all(name.startswith("model.layers.1.self_attn.core.") for name in with_grad)
+    finally:
+        capture.close()
 
 
-def test_isolated_validation_does_not_change_training():
-    model = tiny_model()
+def test_runner_state_dict_replays_the_same_continuation():
+    """Saving the runner state after a prefix and loading it back reproduces the continuation exactly."""
+    model = tiny_model(seed=5)
     install(model, 3, {"head_size": 8, "backend": "reference"})
     runner = Runner(model)
-    ids = torch.randint(0, 64, (1, 5))
-    runner.forward(ids)
-    state = cpu_tree(runner.state_dict())
+    runner.forward(torch.randint(0, 64, (1, 6)))
+    saved = cpu_tree(runner.state_dict())
+    tail = torch.randint(0, 64, (1, 4))
+    first = runner.forward(tail)
+    runner.forward(torch.randint(0, 64, (1, 2)))  # moves the cache on
+    runner.load_state_dict(saved)
+    torch.testing.assert_close(runner.forward(tail), first)
+
+
+def test_isolated_state_is_invisible_to_the_training_stream():
+    """Validation forwards inside ``isolated_state`` (other tokens, other lengths) leave the training cache where
+    it was."""
+    model = tiny_model(seed=6)
+    install(model, 1, {"head_size": 8, "backend": "reference"})
+    runner = Runner(model)
+    prefix, nxt = torch.randint(0, 64, (1, 4)), torch.randint(0, 64, (1, 3))
+    runner.forward(prefix)
+    saved = cpu_tree(runner.state_dict())
     with isolated_state(runner):
-        runner.forward(ids)
-        runner.forward(ids)
-    actual = runner.forward(ids)
-    runner.load_state_dict(state)
-    torch.testing.assert_close(actual, runner.forward(ids))
+        for length in (2, 5):
+            runner.forward(torch.randint(0, 64, (1, length)))
+    assert runner.cache.cursor == 4
+    after = runner.forward(nxt)
+    runner.load_state_dict(saved)
+    torch.testing.assert_close(after, runner.forward(nxt))
 
 
 def test_migration_order():
