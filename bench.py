@@ -203,6 +203,7 @@ def build_ours(args, topo, manifest, model_spec):
         try:  # a steady-state step: the previous step's updates are issued under its teacher forward
             start.record()
             reports = engine.step(reader)
+            engine.join_students()  # stop after the step's last micro-steps (the step itself does not wait for them)
             stop.record()
             dev, host = engine.profiler.summary(), engine.profiler.host_summary()
             stop.synchronize()

@@ -121,8 +121,11 @@ class StepEngine:
         # for the event its capture records after layer L's attention, so it runs beside the rest of the teacher
         # forward and fills the SMs that the teacher's latency-bound kernels (GDN state pass, attention tail) leave
         # idle. Its GEMMs use the second stream-K workspace (lane 1); parallel split-K runs as stream-K while two
-        # lanes can overlap. The step ends with the compute stream waiting for the student stream.
+        # lanes can overlap. Nothing joins the streams at the end of a step: the next step's teacher forward starts
+        # beside the last students; the deferred updates and the metric copies are issued on the student stream,
+        # and ``join_students`` / ``join_updates`` order later reads after the students.
         self.student_stream = None
+        self._compute = None
         if self.device.type == "cuda" and cfg.get("overlap_students", True):
             self.student_stream = torch.cuda.Stream(self.device)
             native().gemm_set_concurrent(True)
@@ -163,6 +166,8 @@ class StepEngine:
         ``read_metrics_async`` can read a step while the next one already runs."""
         profiler = self.profiler
         profiler.reset()
+        if self.device.type == "cuda":
+            self._compute = torch.cuda.current_stream(self.device)  # the teacher's stream
         self.flush()  # the previous step's updates, under this step's teacher forward
         micro_steps = self.cfg["grad_accum_steps"]
         for micro in range(micro_steps):
@@ -182,9 +187,13 @@ class StepEngine:
                         with self._on_student_stream(), profiler.phase(f"update_{layer:02d}"):
                             student.reduce()
                             student.update()
-            if self.student_stream is not None and batch is not None:
-                torch.cuda.current_stream(self.device).wait_stream(self.student_stream)
         return {layer: student.report for layer, student in self.students.items()}
+
+    def join_students(self):
+        """Make the current stream wait for every student micro-step issued so far (the step itself does not: the
+        next step's teacher forward starts while the last students of this one still run)."""
+        if self.student_stream is not None:
+            torch.cuda.current_stream(self.device).wait_stream(self.student_stream)
 
     def _on_student_stream(self):
         return torch.cuda.stream(self.student_stream) if self.student_stream is not None else nullcontext()
@@ -213,6 +222,7 @@ class StepEngine:
         """Issue any deferred updates and make the current stream wait for every layer's update (local AdamW or
         peer exchange): after this, work recorded on the current stream follows all of them."""
         self.flush()
+        self.join_students()
         for student in self.students.values():
             student.join_update()
 
@@ -221,13 +231,14 @@ class StepEngine:
         reads waiting for them. Called at the start of every step; call it before anything that reads student
         parameters outside a step (validation, checkpoints, export) or before a step-exact device timing ends."""
         deferred, self._deferred = self._deferred, []
-        for student in deferred:
-            with self.profiler.phase(f"update_{student.layer:02d}"):
-                student.reduce()
-                student.update()
         waiting, self._waiting_reads = self._waiting_reads, []
-        for pending in waiting:
-            self._issue_read(pending)
+        with self._on_student_stream():  # the updates and metric copies follow the students' last micro-steps
+            for student in deferred:
+                with self.profiler.phase(f"update_{student.layer:02d}"):
+                    student.reduce()
+                    student.update()
+            for pending in waiting:
+                self._issue_read(pending)
 
     # ---------------------------------------------------------------- metrics
 
@@ -274,7 +285,11 @@ class StepEngine:
                 self._pinned_status[slot].copy_(exchange.status_words(), non_blocking=True)
             reports_copied = torch.cuda.Event()
             reports_copied.record(side)
-        native().fault_words_async(self._pinned_faults[slot])
+        if self.student_stream is not None:  # after the students' kernels and the teacher's (which precede them)
+            self.student_stream.wait_stream(self._compute or main)
+            main = self.student_stream
+        with torch.cuda.stream(main):
+            native().fault_words_async(self._pinned_faults[slot])
         faults_copied = torch.cuda.Event()
         faults_copied.record(main)
         self._pending_events[slot] = (reports_copied, faults_copied)
