@@ -127,7 +127,10 @@ class StepEngine:
         self.student_stream = None
         self._compute = None
         if self.device.type == "cuda" and cfg.get("overlap_students", True):
-            self.student_stream = torch.cuda.Stream(self.device)
+            # THESEUS_STUDENT_PRIORITY: CUDA priority of the student stream (0, the default, is the lowest and the
+            # compute stream's; -1 makes the block scheduler prefer student kernels when both streams have work).
+            priority = int(os.environ.get("THESEUS_STUDENT_PRIORITY", "0"))
+            self.student_stream = torch.cuda.Stream(self.device, priority=priority)
             native().gemm_set_concurrent(True)
             for capture in captures.values():
                 capture.record_events = True
