@@ -212,12 +212,24 @@ flash_attn_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_const
         for (int i = 0; i < 32; ++i) { s[i] = a[i]; s[32 + i] = c2[i]; }
       }
       const int k0 = j * BKV;
-      float mb = -INFINITY;
+      // Blocks that end at or before the warp's first query position need no causal mask (a warp-uniform test).
+      // The block maximum is taken over four independent chains (max is exact, so the order does not matter).
+      const bool unmasked = k0 + BKV - 1 <= args.offset + q0 + quarter * 32;
+      float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      if (unmasked) {
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        s[i] = (k0 + i <= qpos) ? s[i] * args.scale_log2 : -INFINITY;
-        mb = fmaxf(mb, s[i]);
+        for (int i = 0; i < 64; ++i) {
+          s[i] *= args.scale_log2;
+          m4[i & 3] = fmaxf(m4[i & 3], s[i]);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          s[i] = (k0 + i <= qpos) ? s[i] * args.scale_log2 : -INFINITY;
+          m4[i & 3] = fmaxf(m4[i & 3], s[i]);
+        }
       }
+      const float mb = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
       const float m_new = fmaxf(m_run, mb);
       if (j == 0) {
         m_run = m_new;
@@ -244,16 +256,16 @@ flash_attn_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_const
           }
         }
       }
-      float psum = 0.f;
+      float ps[4] = {0.f, 0.f, 0.f, 0.f};  // four independent partial sums of the block's probabilities
       uint32_t packed[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
         const float p0 = exp2f(s[2 * i] - m_run), p1 = exp2f(s[2 * i + 1] - m_run);
-        psum += p0 + p1;
+        ps[i & 3] += p0 + p1;
         __nv_bfloat162 pk = __floats2bfloat162_rn(p0, p1);
         packed[i] = *reinterpret_cast<uint32_t*>(&pk);
       }
-      l_run += psum;
+      l_run += (ps[0] + ps[1]) + (ps[2] + ps[3]);
       // P buffer st was last read by the MMA of block j-2.
       if (j >= 2 && !sm100::mbar_wait(&o_done[st], ((j - 2) >> 1) & 1, abort)) { ok = false; break; }
       uint8_t* prow = sP + st * P_BYTES + r * 128;
