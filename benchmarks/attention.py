@@ -1,7 +1,8 @@
 #!/usr/bin/env python3
 """tcgen05 flash attention vs PyTorch SDPA on the 27B layer shape: 1024 queries of 24 heads (head_dim 256,
-4 KV heads) at cache offsets 0/1024/2048/3072 (the four chunks of a 4096-token window). CUDA-event timing,
-median of 20 after 5 warm-ups; FLOPs count the causal work only."""
+4 KV heads) at cache offsets 0/1024/2048/3072 (the four chunks of a 4096-token window). CUDA-event timing of
+10 back-to-back launches per sample (so the host's launch preparation overlaps the previous launch instead of
+being timed), median of 20 samples after 5 warm-ups; FLOPs count the causal work only."""
 import json
 import os
 import sys
@@ -13,6 +14,9 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 from rwkv_theseus_b200.ops import native  # noqa: E402
 
 
+REPEAT = 10
+
+
 def timed(fn, warmup=5, iters=20):
     for _ in range(warmup):
         fn()
@@ -21,10 +25,11 @@ def timed(fn, warmup=5, iters=20):
     for _ in range(iters):
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
-        fn()
+        for _ in range(REPEAT):
+            fn()
         e.record()
         torch.cuda.synchronize()
-        out.append(s.elapsed_time(e))
+        out.append(s.elapsed_time(e) / REPEAT)
     return sorted(out)[len(out) // 2]
 
 
