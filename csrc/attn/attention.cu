@@ -72,6 +72,13 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
       : "memory");
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+// 2^x by the hardware approximation (flush-to-zero): the softmax probabilities it feeds are rounded to bf16
+// right after, far coarser than its error; arguments are <= 0 (x - running max) or -inf (masked keys, giving 0).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 __global__ void __launch_bounds__(THREADS, 1)
@@ -260,7 +267,7 @@ flash_attn_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_const
       uint32_t packed[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        const float p0 = exp2f(s[2 * i] - m_run), p1 = exp2f(s[2 * i + 1] - m_run);
+        const float p0 = ex2_approx(s[2 * i] - m_run), p1 = ex2_approx(s[2 * i + 1] - m_run);
         ps[i & 3] += p0 + p1;
         __nv_bfloat162 pk = __floats2bfloat162_rn(p0, p1);
         packed[i] = *reinterpret_cast<uint32_t*>(&pk);
